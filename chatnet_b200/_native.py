@@ -1,0 +1,125 @@
+"""ctypes binding of libchatnet_cuda (include/chatnet_cuda.h).
+
+The library is the product: there is no Python or CPU fallback.  Loading
+fails loudly when the shared object is missing, and every call checks the
+returned status and raises the exception the reference would have thrown:
+
+    CN_ERR_UNSUPPORTED -> NotSupportedError   (NotSupportedException)
+    CN_ERR_NOT_FOUND   -> KeyError            (KeyNotFoundException)
+    CN_ERR_INVALID_ARG -> ValueError          (ArgumentException)
+    CN_ERR_TIMEOUT     -> TimeoutError
+    others             -> CudaError
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = Path(os.environ.get("CHATNET_CUDA_LIB", _PKG / "_build" / "libchatnet_cuda.so"))
+
+CN_OK = 0
+CN_ERR_INVALID_ARG = -1
+CN_ERR_UNSUPPORTED = -2
+CN_ERR_CUDA = -3
+CN_ERR_OOM = -4
+CN_ERR_TIMEOUT = -5
+CN_ERR_NOT_FOUND = -6
+CN_ERR_NCCL = -7
+
+TYPE_F32 = 0
+TYPE_F16 = 1
+TYPE_Q4_0 = 2
+TYPE_Q4_K = 12
+TYPE_Q6_K = 14
+
+DIST_CFG0_Q4_0 = 1
+DIST_CFG2_Q4_K = 2
+DIST_CFG2_Q6_K = 3
+DIST_NORMAL = 4
+DIST_NORM_W = 5
+
+
+class NotSupportedError(NotImplementedError):
+    """The reference's NotSupportedException (LlamaModel.cs:564-565)."""
+
+
+class CudaError(RuntimeError):
+    pass
+
+
+_vp = C.c_void_p
+_i = C.c_int
+_i64 = C.c_int64
+_u64 = C.c_uint64
+_f = C.c_float
+_fp = C.POINTER(C.c_float)
+
+# name -> (restype, argtypes); mirrors include/chatnet_cuda.h
+SIGNATURES: dict[str, tuple] = {
+    "cn_abi_version": (_i, []),
+    "cn_last_error": (C.c_char_p, []),
+    "cn_byte_size": (_u64, [_i, _u64]),
+    "cn_device_count": (_i, [C.POINTER(_i)]),
+    "cn_create": (_i, [_i, C.POINTER(_vp)]),
+    "cn_destroy": (_i, [_vp]),
+    "cn_ctx_stream": (_vp, [_vp]),
+    "cn_synchronize": (_i, [_vp]),
+    "cn_tensor_upload": (_i, [_vp, _vp, _u64, _i, _i64, _i64, C.POINTER(_vp)]),
+    "cn_tensor_synth": (_i, [_vp, _i, _i64, _i64, _u64, _i, C.POINTER(_vp)]),
+    "cn_tensor_download": (_i, [_vp, _vp, _u64]),
+    "cn_tensor_free": (_i, [_vp]),
+    "cn_tensor_device_ptr": (_vp, [_vp]),
+    "cn_tensor_bytes": (_u64, [_vp]),
+    "cn_synth_fill": (_i, [_i, _i64, _i64, _u64, _i, _vp, _u64]),
+    "cn_synth_seed": (_u64, [_i, C.c_char_p]),
+    "cn_dequantize": (_i, [_vp, _vp, _i64, _i64, _fp]),
+    "cn_matvec": (_i, [_vp, _vp, _fp, _fp, _i]),
+    "cn_dequantize_dev": (_i, [_i, _vp, _vp, _i64, _vp]),
+    "cn_matvec_dev": (_i, [_vp, _i, _vp, _i, _i, _vp, _vp, _i]),
+}
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Loads libchatnet_cuda once; raises if it is missing (no fallback)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"libchatnet_cuda not built: {LIB_PATH} is missing "
+                "(run `python -m chatnet_b200.build`)")
+        h = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(h, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = h
+    return _lib
+
+
+def last_error() -> str:
+    return lib().cn_last_error().decode(errors="replace")
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc == CN_OK:
+        return
+    msg = f"{what}: {last_error()} (status {rc})" if what else f"{last_error()} (status {rc})"
+    if rc == CN_ERR_UNSUPPORTED:
+        raise NotSupportedError(msg)
+    if rc == CN_ERR_NOT_FOUND:
+        raise KeyError(msg)
+    if rc == CN_ERR_INVALID_ARG:
+        raise ValueError(msg)
+    if rc == CN_ERR_TIMEOUT:
+        raise TimeoutError(msg)
+    if rc == CN_ERR_OOM:
+        raise MemoryError(msg)
+    raise CudaError(msg)
+
+
+def byte_size(type_: int, elements: int) -> int:
+    return int(lib().cn_byte_size(type_, elements))

@@ -1,0 +1,79 @@
+// cn_internal.h -- context / tensor structs and internal launchers.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "chatnet_cuda.h"
+
+struct cn_ctx {
+    int device = 0;
+    int sms = 0;
+    cudaStream_t stream = nullptr;
+    uint32_t* dev_err = nullptr;  // device error word (cn::kErr* bits)
+
+    // GEMV scratch: activation fragments, per-chunk sums, split-K partials
+    // and the per-tile arrival counters (self-resetting, zeroed at alloc).
+    void* xfrag = nullptr;
+    size_t xfrag_bytes = 0;
+    float* xsum = nullptr;
+    size_t xsum_bytes = 0;
+    float* partials = nullptr;
+    size_t partial_bytes = 0;
+    int* counters = nullptr;
+    size_t counter_count = 0;
+
+    // staging for the host-pointer entry points
+    void* dstage = nullptr;
+    size_t dstage_bytes = 0;
+    void* hstage = nullptr;  // pinned
+    size_t hstage_bytes = 0;
+};
+
+struct cn_tensor {
+    cn_ctx* ctx = nullptr;
+    int type = 0;
+    int64_t rows = 0, cols = 0;
+    uint64_t bytes = 0, row_bytes = 0;
+    void* d = nullptr;
+    bool owns = true;
+    bool has_map = false;
+    CUtensorMap map;
+};
+
+namespace cn {
+
+uint64_t row_bytes(int type, int64_t cols);
+bool type_supported(int type);
+
+int ensure(void** p, size_t* have, size_t need, bool zero);
+
+// Encodes the TMA descriptor a GEMV uses for a [rows][row_bytes] weight
+// matrix, or returns CN_ERR_UNSUPPORTED if the layout cannot be tiled
+// (row_bytes not a multiple of 16, or unaligned base).
+int encode_weight_map(int type, const void* d_w, int64_t rows, uint64_t row_bytes,
+                      CUtensorMap* out);
+
+// Scratch requirements of one GEMV call.
+struct GemvPlan {
+    int nt = 1;       // n-tiles of 4 batch columns
+    int tiles = 0;    // 16-row tiles
+    int units = 0;    // 256-position k units
+    int ctas = 0;
+    bool tma = false;
+    size_t xfrag_bytes = 0, xsum_bytes = 0, partial_bytes = 0, counters = 0;
+};
+int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool tma,
+              GemvPlan* plan);
+
+// Enqueues x-prep + GEMV on ctx->stream.  `map` may be null (encoded on the
+// fly when possible, else the generic kernel runs).
+int gemv_launch(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols,
+                const CUtensorMap* map, const float* d_x, float* d_y, int batch);
+
+int dequant_launch(int type, const void* d_blocks, float* d_out, int64_t n, cudaStream_t s);
+int synth_launch(int type, int64_t rows, int64_t cols, uint64_t seed, int dist, void* d_out,
+                 cudaStream_t s);
+
+}  // namespace cn

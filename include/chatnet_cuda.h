@@ -1,0 +1,156 @@
+/*
+ * chatnet_cuda.h -- C ABI of libchatnet_cuda, the B200 (sm_100a) engine for
+ * ChatNet's quantized-weight hot path.
+ *
+ * The reference is a C# engine; its host code (InferenceEngine, IModel,
+ * IWeightLoader) stays unchanged and reaches this library through
+ * P/Invoke.  Every entry point below names the reference routine it
+ * replaces (paths relative to the ChatNet source tree).
+ *
+ * Conventions
+ *  - Every function returns int status: CN_OK (0) or a negative CN_ERR_*.
+ *    Nothing throws or aborts.  cn_last_error() returns a message for the
+ *    last failing call on the calling thread.
+ *  - Status codes stand for the reference's exceptions:
+ *    CN_ERR_UNSUPPORTED = NotSupportedException (LlamaModel.cs:564-565),
+ *    CN_ERR_NOT_FOUND   = KeyNotFoundException (MemoryMappedWeights.cs:52),
+ *    CN_ERR_INVALID_ARG = ArgumentException / IndexOutOfRangeException.
+ *  - "_dev" entry points take DEVICE pointers and a cudaStream_t passed as
+ *    void* (NULL = legacy default stream); they only enqueue work.
+ *  - Entry points without "_dev" take HOST pointers, borrowed for the call,
+ *    and return when the results are in host memory (the drop-in shape of
+ *    the reference's synchronous Span-based methods).
+ *  - Weight tensors hold the GGUF block bytes exactly as they are in the
+ *    file (uploaded once, untouched), row-major [rows][row_bytes].
+ */
+#ifndef CHATNET_CUDA_H
+#define CHATNET_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CN_ABI_VERSION 1
+
+/* status codes */
+#define CN_OK 0
+#define CN_ERR_INVALID_ARG (-1)
+#define CN_ERR_UNSUPPORTED (-2)
+#define CN_ERR_CUDA (-3)
+#define CN_ERR_OOM (-4)
+#define CN_ERR_TIMEOUT (-5)
+#define CN_ERR_NOT_FOUND (-6)
+#define CN_ERR_NCCL (-7)
+
+/* GgmlType values (Gguf/GgufConstants.cs:41-71) of the supported types. */
+#define CN_TYPE_F32 0
+#define CN_TYPE_F16 1
+#define CN_TYPE_Q4_0 2
+#define CN_TYPE_Q4_K 12
+#define CN_TYPE_Q6_K 14
+
+typedef struct cn_ctx cn_ctx;
+typedef struct cn_tensor cn_tensor;
+
+/* ---- library ------------------------------------------------------------ */
+
+/* Returns CN_ABI_VERSION.  (no reference counterpart: ABI handshake) */
+int cn_abi_version(void);
+
+/* Message for the last failing call on this thread ("" if none).  The
+ * pointer stays valid until the next failing call on the same thread.
+ * (stands for Exception.Message) */
+const char* cn_last_error(void);
+
+/* Bytes of `elements` values stored as `type`; 0 for unsupported types.
+ * Replaces GgufTensorInfo.ByteSize (Gguf/GgufTensorInfo.cs:30-114). */
+uint64_t cn_byte_size(int type, uint64_t elements);
+
+/* Number of visible CUDA devices. */
+int cn_device_count(int* out_count);
+
+/* ---- context ------------------------------------------------------------ */
+
+/* Creates a context on `device` with one stream and the scratch space the
+ * kernels need.  Replaces the per-model state LlamaModel allocates in its
+ * constructor (LlamaModel.cs:48-73). */
+int cn_create(int device, cn_ctx** out);
+int cn_destroy(cn_ctx* ctx);
+/* The context's cudaStream_t (as void*). */
+void* cn_ctx_stream(cn_ctx* ctx);
+/* Waits for the context's stream; also reports a device-side timeout
+ * (CN_ERR_TIMEOUT) if a kernel gave up waiting. */
+int cn_synchronize(cn_ctx* ctx);
+
+/* ---- weight tensors -------------------------------------------------- */
+
+/* Uploads `bytes` of GGUF blocks for a [rows, cols] tensor of `type` to
+ * HBM, byte for byte.  bytes must equal rows * cn_byte_size(type, cols).
+ * Replaces MemoryMappedWeights.GetTensorPointer/GetTensorData
+ * (Memory/MemoryMappedWeights.cs:48-83) as the source of weight bytes. */
+int cn_tensor_upload(cn_ctx* ctx, const void* host_blocks, uint64_t bytes, int type,
+                     int64_t rows, int64_t cols, cn_tensor** out);
+
+/* Allocates a tensor and fills it on the device with the seeded synthetic
+ * generator (cn_synth_fill); no host copy.  (no reference counterpart:
+ * synthetic inputs for the benchmark configs) */
+int cn_tensor_synth(cn_ctx* ctx, int type, int64_t rows, int64_t cols, uint64_t seed,
+                    int dist, cn_tensor** out);
+
+/* Copies a tensor's bytes back to host memory (bytes must match). */
+int cn_tensor_download(const cn_tensor* t, void* host, uint64_t bytes);
+int cn_tensor_free(cn_tensor* t);
+const void* cn_tensor_device_ptr(const cn_tensor* t);
+uint64_t cn_tensor_bytes(const cn_tensor* t);
+
+/* ---- synthetic inputs (host side; identical bytes on the device) -------- */
+
+/* Distributions for cn_synth_fill / cn_tensor_synth. */
+#define CN_DIST_CFG0_Q4_0 1  /* Q4_0, d = |N|*0.02/8, nibbles U[0,15]          */
+#define CN_DIST_CFG2_Q4_K 2  /* Q4_K, d,dmin = |N|*0.01, 6-bit sc/m U[0,63]    */
+#define CN_DIST_CFG2_Q6_K 3  /* Q6_K, d = |N|*0.01, int8 scales U[0,63]        */
+#define CN_DIST_NORMAL 4     /* F32 or F16: N(0,1)                              */
+#define CN_DIST_NORM_W 5     /* F32: 1 + 0.01*N(0,1) (RMSNorm weights)          */
+
+/* Fills `host` with the generator's bytes for a [rows, cols] tensor.
+ * N(0,1) is the sum of twelve 16-bit uniforms minus 6, exact in fp32.
+ * (no reference counterpart) */
+int cn_synth_fill(int type, int64_t rows, int64_t cols, uint64_t seed, int dist, void* host,
+                  uint64_t bytes);
+/* 64-bit seed of a named tensor in a benchmark config (FNV-1a of the name
+ * mixed with the config id). */
+uint64_t cn_synth_seed(int config_id, const char* tensor_name);
+
+/* ---- op level: host buffers, synchronous -------------------------------- */
+
+/* Dequantizes rows [row0, row0+nrows) of W to fp32, bit-exact with
+ * DequantQ4_0/Q4K/Q6K.Dequantize (Tensors/Quantization/DequantQ4_0.cs:28-58,
+ * DequantQ4K.cs:37-77, DequantQ6K.cs:37-88). */
+int cn_dequantize(cn_ctx* ctx, const cn_tensor* W, int64_t row0, int64_t nrows, float* host_out);
+
+/* y[b][r] = dot(W[r], x[b]) for b < batch: x is [batch][cols] fp32, y is
+ * [batch][rows] fp32.  Replaces MatVecMulByType (Models/Llama/
+ * LlamaModel.cs:470-567) -> TensorMath.MatVecMulQ4_0 / MatVecMulQ6K /
+ * MatVecMulGeneric(Q4_K) (Tensors/TensorMath.cs:548-656). */
+int cn_matvec(cn_ctx* ctx, const cn_tensor* W, const float* host_x, float* host_y, int batch);
+
+/* ---- device level: device pointers, asynchronous ------------------------ */
+
+/* Bit-exact dequantization of n_elements values (same semantics as the
+ * reference Dequantize, including Q4_0's partial last block and the K
+ * types' whole-super-block rule). */
+int cn_dequantize_dev(int type, const void* d_blocks, float* d_out, int64_t n_elements,
+                      void* stream);
+
+/* Fused dequant-GEMV on raw device pointers, using ctx's scratch and
+ * stream: y[b][r] = dot(W[r], x[b]).  Same math as cn_matvec. */
+int cn_matvec_dev(cn_ctx* ctx, int type, const void* d_w, int out_dim, int in_dim,
+                  const float* d_x, float* d_y, int batch);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

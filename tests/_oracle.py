@@ -1,0 +1,93 @@
+"""ctypes binding of the CPU oracle (oracle/liboracle.so) -- test infrastructure.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU legs use this module.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent.parent
+ORACLE_DIR = ROOT / "oracle"
+LIB = ORACLE_DIR / "_build" / "liboracle.so"
+
+_f = C.c_float
+_fp = C.POINTER(C.c_float)
+_vp = C.c_void_p
+_i = C.c_int
+
+
+class LlamaConfig(C.Structure):
+    _fields_ = [("dim", _i), ("hidden_dim", _i), ("n_layers", _i), ("n_heads", _i),
+                ("n_kv_heads", _i), ("head_dim", _i), ("vocab", _i), ("ctx_len", _i),
+                ("rope_base", _f), ("eps", _f), ("kv_f16", _i)]
+
+
+_SIG = {
+    "or_half_to_float": (_f, [C.c_uint16]),
+    "or_float_to_half": (C.c_uint16, [_f]),
+    "or_byte_size": (C.c_uint64, [_i, C.c_uint64]),
+    "or_dequantize": (_i, [_i, _vp, _fp, C.c_int64]),
+    "or_dot": (_f, [_i, _vp, _fp, _i]),
+    "or_matvec": (_i, [_i, _vp, _fp, _fp, _i, _i, _i]),
+    "or_matvec_batch": (_i, [_i, _vp, _fp, _fp, _i, _i, _i, _i]),
+    "or_rmsnorm": (None, [_fp, _fp, _fp, _i, _f]),
+    "or_softmax": (None, [_fp, _i]),
+    "or_silu_mul": (None, [_fp, _fp, _i]),
+    "or_rope": (None, [_fp, _fp, _i, _i, _i, _i, _f]),
+    "or_add": (None, [_fp, _fp, _i]),
+    "or_argmax": (_i, [_fp, _i]),
+    "or_llama_forward": (_i, [C.POINTER(LlamaConfig), C.POINTER(_vp), C.POINTER(_i), _vp, _vp,
+                              C.POINTER(_i), _i, _i, _fp, _i]),
+    "or_llama_layers": (_i, [C.POINTER(LlamaConfig), C.POINTER(_vp), C.POINTER(_i), _vp, _vp,
+                             _fp, _i, _i, _i, _i]),
+    "or_llama_head": (_i, [C.POINTER(LlamaConfig), C.POINTER(_vp), C.POINTER(_i), _fp, _fp, _i]),
+}
+
+
+def fp(a: np.ndarray):
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_fp)
+
+
+class Oracle:
+    def __init__(self, lib: C.CDLL):
+        self.lib = lib
+
+    def dequantize(self, type_: int, blocks: np.ndarray, n: int) -> np.ndarray:
+        out = np.zeros(n, dtype=np.float32)
+        rc = self.lib.or_dequantize(type_, blocks.ctypes.data, fp(out), n)
+        assert rc == 0, rc
+        return out
+
+    def dot(self, type_: int, row: np.ndarray, x: np.ndarray) -> float:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        return float(self.lib.or_dot(type_, row.ctypes.data, fp(x), x.size))
+
+    def matvec(self, type_: int, W: np.ndarray, x: np.ndarray, rows: int, nthreads: int = 0):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        x2 = x.reshape(-1, x.shape[-1])
+        y = np.empty((x2.shape[0], rows), dtype=np.float32)
+        rc = self.lib.or_matvec_batch(type_, W.ctypes.data, fp(x2), fp(y), rows, x2.shape[1],
+                                      x2.shape[0], nthreads)
+        assert rc == 0, rc
+        return y[0] if x.ndim == 1 else y
+
+
+def build() -> Path:
+    if not LIB.exists() or LIB.stat().st_mtime < max(
+            p.stat().st_mtime for p in ORACLE_DIR.glob("oracle.*")):
+        subprocess.run(["make", "-s", "-C", str(ORACLE_DIR)], check=True)
+    return LIB
+
+
+def load() -> Oracle:
+    lib = C.CDLL(str(build()))
+    for name, (res, args) in _SIG.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return Oracle(lib)

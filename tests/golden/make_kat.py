@@ -1,0 +1,114 @@
+"""Writes kat_quant.json: the reference's own known-answer tests for the hot path.
+
+The cases restate the fixtures of ChatNet's tests/ChatNet.Tests/
+QuantizationTests.cs (block bytes built exactly as each test builds them,
+WriteHalf = IEEE round-to-nearest fp16) together with the values the test
+asserts and its tolerance.  Where the test compares DotProduct against the
+sum of Dequantize, the expected sum is derived here from the block formula
+(exact in fp32 for these fixtures), so the check does not depend on the
+oracle it pins.
+
+Run: python tests/golden/make_kat.py   (rewrites tests/golden/kat_quant.json)
+"""
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+T = "tests/ChatNet.Tests/QuantizationTests.cs"
+
+
+def half_bytes(v: float) -> list[int]:
+    h = np.array([v], dtype=np.float16).view(np.uint16)[0]
+    return [int(h & 0xFF), int(h >> 8)]
+
+
+def f16(v: float) -> float:
+    return float(np.float16(v))
+
+
+def cases() -> list[dict]:
+    out = []
+
+    # Q4_0_Dequantize_ProducesCorrectValues (:23-41): d=1, qs=0 -> all -8
+    blk = half_bytes(1.0) + [0] * 16
+    out.append(dict(name="Q4_0_Dequantize_ProducesCorrectValues", ref=f"{T}:23-41", type=2, n=32,
+                    blocks=blk, dequant=[-8.0] * 32, tol=0.01))
+
+    # Q4_0_Dequantize_MidpointValues (:43-60): d=0.5, 0x88 -> 0
+    blk = half_bytes(0.5) + [0x88] * 16
+    out.append(dict(name="Q4_0_Dequantize_MidpointValues", ref=f"{T}:43-60", type=2, n=32,
+                    blocks=blk, dequant=[0.0] * 32, tol=0.01))
+
+    # Q4_0_DotProduct_MatchesScalar (:62-87): d=2, 0x37 (lo 7, hi 3), x=1
+    blk = half_bytes(2.0) + [0x37] * 16
+    deq = [(7 - 8) * 2.0] * 16 + [(3 - 8) * 2.0] * 16
+    out.append(dict(name="Q4_0_DotProduct_MatchesScalar", ref=f"{T}:62-87", type=2, n=32,
+                    blocks=blk, dequant=deq, x=[1.0] * 32, dot=float(sum(deq)), tol=0.01))
+
+    # Q6K_Dequantize_ProducesFiniteValues (:302-319): d=1 at byte 208, scales=1
+    blk = [0] * 210
+    blk[192:208] = [1] * 16
+    blk[208:210] = half_bytes(1.0)
+    out.append(dict(name="Q6K_Dequantize_ProducesFiniteValues", ref=f"{T}:302-319", type=14,
+                    n=256, blocks=blk, dequant=[-32.0] * 256, finite=True, tol=0.01))
+
+    # Q6K_DotProduct_MatchesDequantize (:321-345): d=0.1, scales=2, ql=0x22, x=1
+    blk = [0x22] * 128 + [0] * 64 + [2] * 16 + half_bytes(0.1)
+    v = np.float32(np.float32(f16(0.1)) * np.float32(2)) * np.float32(-30)
+    out.append(dict(name="Q6K_DotProduct_MatchesDequantize", ref=f"{T}:321-345", type=14, n=256,
+                    blocks=blk, dequant=[float(v)] * 256, x=[1.0] * 256,
+                    dot=float(np.float32(v) * 256), tol=0.1))
+
+    # Q4K_Dequantize_ProducesFiniteValues (:445-462): d=1, dmin=0.5, scales 0x11
+    blk = half_bytes(1.0) + half_bytes(0.5) + [0x11] * 12 + [0] * 128
+    # sc = m = 17 for sub-blocks 0..3, 1 for 4..7 (DecodeScales); q = 0
+    deq = [(-8.5 if (i // 32) < 4 else -0.5) for i in range(256)]
+    out.append(dict(name="Q4K_Dequantize_ProducesFiniteValues", ref=f"{T}:445-462", type=12,
+                    n=256, blocks=blk, dequant=deq, finite=True, tol=0.01))
+
+    # Q4K_DotProduct_MatchesDequantize (:464-489): d=.5, dmin=.25, 0x11, qs 0x33, x=1
+    blk = half_bytes(0.5) + half_bytes(0.25) + [0x11] * 12 + [0x33] * 128
+    deq = [(0.5 * 17 * 3 - 0.25 * 17) if (i // 32) < 4 else (0.5 * 1 * 3 - 0.25 * 1)
+           for i in range(256)]
+    out.append(dict(name="Q4K_DotProduct_MatchesDequantize", ref=f"{T}:464-489", type=12, n=256,
+                    blocks=blk, dequant=deq, x=[1.0] * 256, dot=float(sum(deq)), tol=0.1))
+
+    # Q4_0_MultiBlock_Dequantize (:704-726): two blocks d=1 and d=2, 0x88 -> 0
+    blk = half_bytes(1.0) + [0x88] * 16 + half_bytes(2.0) + [0x88] * 16
+    out.append(dict(name="Q4_0_MultiBlock_Dequantize", ref=f"{T}:704-726", type=2, n=64,
+                    blocks=blk, dequant=[0.0] * 64, tol=0.01))
+
+    # Q4K_MultiBlock_DotProduct (:728-759): 2 super-blocks, qs 0x55, x=0.5
+    one = half_bytes(0.5) + half_bytes(0.25) + [0x11] * 12 + [0x55] * 128
+    blk = one + one
+    deq1 = [(0.5 * 17 * 5 - 0.25 * 17) if (i // 32) < 4 else (0.5 * 1 * 5 - 0.25 * 1)
+            for i in range(256)]
+    deq = deq1 + deq1
+    out.append(dict(name="Q4K_MultiBlock_DotProduct", ref=f"{T}:728-759", type=12, n=512,
+                    blocks=blk, dequant=deq, x=[0.5] * 512,
+                    dot=float(sum(d * 0.5 for d in deq)), tol=0.1))
+    return out
+
+
+# GgufTensorInfo_ByteSize_AllTypes (:642-698), the rows for the hot path's types
+# plus F32/F16: (type, block size, bytes per block)
+BYTESIZE = [(0, 1, 4), (1, 1, 2), (2, 32, 18), (12, 256, 144), (14, 256, 210)]
+
+
+def main() -> None:
+    doc = {
+        "source": T,
+        "note": "fixtures restated from the reference's MSTest known-answer tests",
+        "cases": cases(),
+        "byte_size": [dict(type=t, block=b, bytes_per_block=p, ref=f"{T}:642-698")
+                      for (t, b, p) in BYTESIZE],
+    }
+    (HERE / "kat_quant.json").write_text(json.dumps(doc, indent=1) + "\n")
+
+
+if __name__ == "__main__":
+    main()

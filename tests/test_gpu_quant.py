@@ -1,0 +1,140 @@
+"""GPU parity of the block dequantizers (bit-exact) and the fused dequant-GEMVs
+(max relative error 1e-3) against the CPU oracle, through the C ABI."""
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import chatnet_b200 as cn
+from tests.parity import REL_TOL, bits_equal, rel_err
+
+pytestmark = pytest.mark.gpu
+
+KAT = json.loads((Path(__file__).parent / "golden" / "kat_quant.json").read_text())
+Q = {"q4_0": cn.TYPE_Q4_0, "q4_k": cn.TYPE_Q4_K, "q6_k": cn.TYPE_Q6_K}
+
+
+@pytest.mark.parametrize("case", KAT["cases"], ids=lambda c: c["name"])
+def test_kat_on_gpu(ctx, oracle, case):
+    blocks = np.array(case["blocks"], dtype=np.uint8)
+    n = case["n"]
+    W = ctx.upload(blocks, case["type"], 1, n)
+    got = ctx.dequantize(W).ravel()
+    assert bits_equal(got, oracle.dequantize(case["type"], blocks, n))
+    np.testing.assert_allclose(got, case["dequant"], rtol=0, atol=case["tol"])
+    if "x" in case:
+        y = ctx.matvec(W, np.array(case["x"], np.float32))
+        assert abs(float(y[0]) - case["dot"]) <= case["tol"]
+
+
+@pytest.mark.parametrize("name,rows,cols", [
+    ("q4_0", 5632, 2048), ("q4_0", 7, 96), ("q4_k", 4096, 4096), ("q4_k", 3, 512),
+    ("q6_k", 512, 4096), ("q6_k", 5, 768)])
+def test_dequantize_bit_exact(ctx, oracle, name, rows, cols):
+    t = Q[name]
+    blocks = cn.synth_fill(t, rows, cols, seed=cn.synth_seed(2, f"deq.{name}.{rows}x{cols}"))
+    W = ctx.upload(blocks, t, rows, cols)
+    got = ctx.dequantize(W)
+    ref = oracle.dequantize(t, blocks, rows * cols).reshape(rows, cols)
+    assert bits_equal(got, ref)
+    # a row window
+    part = ctx.dequantize(W, 1, rows - 2) if rows > 2 else got
+    assert bits_equal(part, ref[1:rows - 1] if rows > 2 else ref)
+
+
+def test_dequantize_q4_0_partial_block(ctx, oracle):
+    """Dequantize handles a partial last block (DequantQ4_0.cs:39-53)."""
+    rows, cols = 3, 45  # 2 blocks per row, the second holds 13 values
+    blocks = np.random.default_rng(0).integers(0, 256, size=rows * 36, dtype=np.uint8)
+    blocks.reshape(rows, 2, 18)[:, :, 1] = 0x1C  # finite fp16 scales
+    W = ctx.upload(blocks, cn.TYPE_Q4_0, rows, cols)
+    got = ctx.dequantize(W)
+    for r in range(rows):
+        ref = oracle.dequantize(cn.TYPE_Q4_0, blocks[r * 36:(r + 1) * 36], cols)
+        assert bits_equal(got[r], ref)
+
+
+def test_device_synth_matches_host(ctx):
+    for t, rows, cols in [(cn.TYPE_Q4_0, 33, 2048), (cn.TYPE_Q4_K, 17, 4096),
+                          (cn.TYPE_Q6_K, 9, 4096), (cn.TYPE_F32, 3, 999), (cn.TYPE_F16, 5, 128)]:
+        seed = cn.synth_seed(9, f"synth.{t}")
+        host = cn.synth_fill(t, rows, cols, seed).view(np.uint8).ravel()
+        dev = ctx.synth(t, rows, cols, seed).download()
+        assert np.array_equal(host, dev), t
+    w = ctx.synth(cn.TYPE_F32, 1, 4096, 11, dist=cn.DIST_NORM_W).download()
+    assert np.array_equal(w, cn.synth_fill(cn.TYPE_F32, 1, 4096, 11, cn.DIST_NORM_W).view(np.uint8).ravel())
+
+
+def _x(batch, cols, key):
+    return cn.synth_fill(cn.TYPE_F32, batch, cols, cn.synth_seed(2, key))
+
+
+MATVEC_CASES = [
+    # (type, rows, cols, batches) -- configs 0 and 2 of the benchmark
+    ("q4_0", 5632, 2048, (1,)),
+    ("q4_k", 4096, 4096, (1, 4, 16, 32)),
+    ("q4_k", 11008, 4096, (1, 4)),
+    ("q4_k", 4096, 11008, (1, 16)),
+    ("q6_k", 32000, 4096, (1, 4, 32)),
+]
+
+
+@pytest.mark.parametrize("name,rows,cols,batches", MATVEC_CASES,
+                         ids=[f"{c[0]}-{c[1]}x{c[2]}" for c in MATVEC_CASES])
+def test_matvec_parity(ctx, oracle, name, rows, cols, batches):
+    t = Q[name]
+    blocks = cn.synth_fill(t, rows, cols, seed=cn.synth_seed(2, f"mv.{name}.{rows}x{cols}"))
+    W = ctx.upload(blocks, t, rows, cols)
+    rng = np.random.default_rng(rows + cols)
+    sample = np.sort(rng.choice(rows, size=min(rows, 384), replace=False))
+    Ws = blocks.reshape(rows, -1)[sample].copy()
+    for b in batches:
+        x = _x(b, cols, f"mv.x.{name}.{rows}.{b}")
+        y = ctx.matvec(W, x)
+        ref = oracle.matvec(t, Ws, x, len(sample))
+        err = rel_err(y[:, sample], ref)
+        assert err <= REL_TOL, (b, err)
+        assert np.isfinite(y).all()
+
+
+@pytest.mark.parametrize("name,rows,cols", [
+    ("q4_0", 37, 96),      # rows not 16-aligned; row bytes not 16-aligned -> generic path
+    ("q4_0", 16, 256),
+    ("q4_0", 100, 2304),   # row bytes 1296 = 81*16 -> tiled path, ragged tile
+    ("q4_k", 21, 256),
+    ("q6_k", 19, 768),     # 630-byte rows -> generic path
+    ("q6_k", 40, 2048)])
+@pytest.mark.parametrize("batch", [1, 3, 5, 13])
+def test_matvec_edge_shapes(ctx, oracle, name, rows, cols, batch):
+    t = Q[name]
+    blocks = cn.synth_fill(t, rows, cols, seed=cn.synth_seed(2, f"edge.{name}.{rows}x{cols}"))
+    W = ctx.upload(blocks, t, rows, cols)
+    x = _x(batch, cols, f"edge.x.{rows}.{cols}.{batch}")
+    y = ctx.matvec(W, x)
+    ref = oracle.matvec(t, blocks, x, rows)
+    assert rel_err(y, ref) <= REL_TOL
+
+
+def test_matvec_repeatable(ctx):
+    """Stream-K partials are combined in a fixed order: results are bitwise stable."""
+    rows, cols = 4096, 11008
+    blocks = cn.synth_fill(cn.TYPE_Q4_K, rows, cols, seed=5)
+    W = ctx.upload(blocks, cn.TYPE_Q4_K, rows, cols)
+    x = _x(4, cols, "rep")
+    y0 = ctx.matvec(W, x)
+    for _ in range(3):
+        assert bits_equal(ctx.matvec(W, x), y0)
+
+
+def test_matvec_errors(ctx):
+    blocks = cn.synth_fill(cn.TYPE_Q4_0, 16, 64, seed=1)
+    W = ctx.upload(blocks, cn.TYPE_Q4_0, 16, 64)
+    with pytest.raises(ValueError):
+        ctx.matvec(W, np.zeros((33, 64), np.float32))
+    with pytest.raises(cn.NotSupportedError):
+        ctx.upload(np.zeros(20, np.uint8), 3, 1, 32)   # Q4_1: not on this path
+    with pytest.raises(ValueError):
+        ctx.upload(np.zeros(17, np.uint8), cn.TYPE_Q4_0, 1, 32)  # wrong byte count
