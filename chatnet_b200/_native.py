@@ -78,7 +78,24 @@ SIGNATURES: dict[str, tuple] = {
     "cn_matvec": (_i, [_vp, _vp, _fp, _fp, _i]),
     "cn_dequantize_dev": (_i, [_i, _vp, _vp, _i64, _vp]),
     "cn_matvec_dev": (_i, [_vp, _i, _vp, _i, _i, _vp, _vp, _i]),
+    "cn_llama_create": (_i, [_vp, _vp, C.POINTER(_vp), _i, C.POINTER(_vp)]),
+    "cn_llama_destroy": (_i, [_vp]),
+    "cn_llama_forward": (_i, [_vp, C.POINTER(_i), _i, _i, _fp]),
+    "cn_llama_decode": (_i, [_vp, C.POINTER(_i), C.POINTER(_i), _i, _fp, C.POINTER(_i)]),
+    "cn_llama_kv_write": (_i, [_vp, _i, _i, _i, _i, _vp, _vp]),
+    "cn_llama_kv_read": (_i, [_vp, _i, _i, _i, _i, _vp, _vp]),
+    "cn_llama_kv_synth": (_i, [_vp, _i, _i, _u64, _u64]),
 }
+
+KV_F32 = 0
+KV_F16 = 1
+
+
+class LlamaConfigC(C.Structure):
+    """cn_llama_config (include/chatnet_cuda.h)."""
+    _fields_ = [("dim", _i), ("hidden_dim", _i), ("n_layers", _i), ("n_heads", _i),
+                ("n_kv_heads", _i), ("head_dim", _i), ("vocab", _i), ("ctx_len", _i),
+                ("rope_base", _f), ("rms_eps", _f), ("kv_dtype", _i), ("max_batch", _i)]
 
 _lib = None
 

@@ -152,6 +152,7 @@ int cn_destroy(cn_ctx* ctx) {
     cudaFree(ctx->xsum);
     cudaFree(ctx->partials);
     cudaFree(ctx->counters);
+    cudaFree(ctx->xinv);
     cudaFree(ctx->dstage);
     cudaFreeHost(ctx->hstage);
     cudaFree(ctx->dev_err);

@@ -135,9 +135,10 @@ __device__ __forceinline__ float half_bits_to_float(uint16_t h) {
 
 // Loads a 32-bit word from shared memory at a 2-byte aligned address.
 __device__ __forceinline__ uint32_t lds_u32_a2(const uint8_t* p) {
-    uintptr_t a = reinterpret_cast<uintptr_t>(p);
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
-    if ((a & 3) == 0) return w[0];
+    const int mis = (int)(reinterpret_cast<uintptr_t>(p) & 3);
+    // pointer arithmetic (not an integer round trip) keeps the address space
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(p - mis);
+    if (mis == 0) return w[0];
     return __byte_perm(w[0], w[1], 0x5432);
 }
 

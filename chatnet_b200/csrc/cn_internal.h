@@ -23,6 +23,7 @@ struct cn_ctx {
     size_t partial_bytes = 0;
     int* counters = nullptr;
     size_t counter_count = 0;
+    float* xinv = nullptr;
 
     // staging for the host-pointer entry points
     void* dstage = nullptr;
@@ -67,8 +68,44 @@ struct GemvPlan {
 int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool tma,
               GemvPlan* plan);
 
-// Enqueues x-prep + GEMV on ctx->stream.  `map` may be null (encoded on the
-// fly when possible, else the generic kernel runs).
+// A GEMV bound to one weight matrix and batch size.
+struct GemvOp {
+    int type = 0;
+    const void* w = nullptr;
+    int64_t rows = 0, cols = 0;
+    uint64_t rb = 0;
+    int batch = 1;
+    bool tma = false;
+    CUtensorMap map;
+    GemvPlan plan;
+};
+
+// Scratch a GEMV reads and writes (owned by the caller; one GEMV at a time
+// per set of buffers; the counters must start zeroed and are left zeroed).
+struct GemvBufs {
+    uint4* xfrag;
+    float* xsum;
+    float* partials;
+    int* counters;
+    float* xinv;  // [32] per-batch 2^-e written by the prep
+};
+
+struct GemvNeeds {
+    size_t xfrag_bytes = 0, xsum_bytes = 0, partial_bytes = 0, counters = 0;
+};
+
+int gemv_make(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols,
+              const CUtensorMap* map, int batch, GemvOp* op);
+// Converts x [batch][cols] into the GEMV's activation fragments (TMA path).
+int gemv_prep(cudaStream_t st, int sms, const GemvOp& op, const float* d_x, const GemvBufs& b);
+// Runs the GEMV on prepped fragments (TMA path) or on x directly (generic).
+int gemv_run(cn_ctx* ctx, cudaStream_t st, const GemvOp& op, const float* d_x, const GemvBufs& b,
+             float* d_y);
+int gemv_reserve(const GemvPlan& p, GemvNeeds* n);
+float gemv_step1_scale(int type);
+
+// Enqueues x-prep + GEMV on ctx->stream using the ctx's scratch.  `map` may
+// be null (encoded on the fly when possible, else the generic kernel runs).
 int gemv_launch(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols,
                 const CUtensorMap* map, const float* d_x, float* d_y, int batch);
 

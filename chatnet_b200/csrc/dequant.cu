@@ -152,19 +152,15 @@ __global__ void synth_blocks_kernel(int type, uint64_t seed, int64_t nblocks, ui
     for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < nblocks;
          b += (int64_t)gridDim.x * blockDim.x) {
         if (type == CN_TYPE_Q4_0) {
-            uint8_t tmp[18];
-            synth::q4_0_block(seed, b, tmp);
-            for (int i = 0; i < 18; i++) out[b * 18 + i] = tmp[i];
+            synth::q4_0_block(seed, b, out + b * 18);
         } else if (type == CN_TYPE_Q4_K) {
-            uint8_t tmp[144];
+            __align__(16) uint8_t tmp[144];
             synth::q4_k_block(seed, b, tmp);
             uint4* o = reinterpret_cast<uint4*>(out + b * 144);  // 144 = 9 x 16
             const uint4* s = reinterpret_cast<const uint4*>(tmp);
             for (int i = 0; i < 9; i++) o[i] = s[i];
         } else {
-            uint8_t tmp[210];
-            synth::q6_k_block(seed, b, tmp);
-            for (int i = 0; i < 210; i++) out[b * 210 + i] = tmp[i];
+            synth::q6_k_block(seed, b, out + b * 210);
         }
     }
 }

@@ -31,21 +31,23 @@
 
 namespace cn {
 
-constexpr int kWarps = 4;  // warps per CTA, each an independent pipeline
+// CTA shape: 8 consumer warps (16 rows each, one mma m-tile) and 1 producer
+// warp that streams 128-row x 256-position units into a ring of stages.
+constexpr int kCons = 8;
+constexpr int kThreads = (kCons + 1) * 32;
+constexpr int kTileRows = 16 * kCons;
 
 template <int TYPE>
 struct Fmt;
 template <>
 struct Fmt<CN_TYPE_Q4_0> {
-    static constexpr int kBox = 144;  // bytes per row per unit (8 blocks)
-    static constexpr int kStages = 8;
+    static constexpr int kBox = 144;  // bytes per row per unit (8 blocks of 18)
     __device__ static int box_x(int u) { return 18 * u; }  // uint64 elements
     __device__ static int offset(int) { return 0; }
 };
 template <>
 struct Fmt<CN_TYPE_Q4_K> {
-    static constexpr int kBox = 144;  // one super-block
-    static constexpr int kStages = 8;
+    static constexpr int kBox = 144;  // one 144-byte super-block
     __device__ static int box_x(int u) { return 18 * u; }
     __device__ static int offset(int) { return 0; }
 };
@@ -54,34 +56,41 @@ struct Fmt<CN_TYPE_Q6_K> {
     // 210-byte super-blocks are only 2-byte aligned: load the 16-byte
     // aligned 240-byte window that covers super-block u and index into it.
     static constexpr int kBox = 240;
-    static constexpr int kStages = 6;
     __device__ static int box_x(int u) { return ((210 * u) >> 4) * 2; }
     __device__ static int offset(int u) { return (210 * u) & 15; }
 };
 
-template <int TYPE>
-constexpr int stage_bytes() {
-    return Fmt<TYPE>::kBox * 16;
-}
-template <int TYPE>
-constexpr int warp_smem() {
-    return stage_bytes<TYPE>() * Fmt<TYPE>::kStages;
-}
-template <int TYPE>
-constexpr int cta_smem() {
-    return kWarps * warp_smem<TYPE>() + kWarps * Fmt<TYPE>::kStages * 8 + 1024;
-}
+// Shared-memory geometry of one (format, n-tiles) instantiation.
+template <int TYPE, int NT>
+struct Geo {
+    static constexpr int kW = Fmt<TYPE>::kBox * kTileRows;             // raw blocks
+    static constexpr int kXF = 8 * NT * 32 * 16;                        // B fragments
+    static constexpr int kXS = TYPE == CN_TYPE_Q4_K ? 8 * NT * 4 * 4 : 0;  // chunk sums
+    static constexpr int kStage = kW + kXF + kXS;                       // multiple of 128
+    static constexpr int kTable = TYPE == CN_TYPE_Q4_K ? kCons * 16 * 8 * 8 : 0;
+    static constexpr int kFixed = kTable + 64 * 16;                     // table + barriers
+    // Two CTAs per SM when three or more stages fit in half the SM's shared
+    // memory; otherwise one CTA with up to six stages.
+    static constexpr int kHalf = 113 * 1024;
+    static constexpr int kFull = 225 * 1024;
+    static constexpr int kS2 = (kHalf - kFixed) / kStage;
+    static constexpr int kStages = kS2 >= 3 ? (kS2 > 4 ? 4 : kS2)
+                                            : ((kFull - kFixed) / kStage > 6 ? 6 : (kFull - kFixed) / kStage);
+    static constexpr int kMinCtas = kS2 >= 3 ? 2 : 1;
+    static constexpr int kSmem = kFixed + kStages * kStage;
+};
 
 struct GemvArgs {
     int64_t rows;
     int units;  // 256-position units per row
-    int tiles;  // 16-row tiles
+    int tiles;  // 128-row tiles
     int batch;
-    const uint4* xfrag;  // [nt][chunks][32 lanes]
-    const float* xsum;   // [batch][chunks]
+    const uint4* xfrag;  // [chunk][nt][32 lanes]
+    const float* xsum;   // [chunk][nt*4]
+    const float* xinv;   // [nt*4] 2^-e of each batch column's prep scaling
     float* y;            // [batch][rows]
-    float* partials;     // [2 * warps][16][nt*4] stream-K partial slots
-    int* counters;       // [tiles]
+    float* partials;     // [2 * ctas][128 rows][nt*4] stream-K partial slots
+    int* counters;       // [tiles * kCons]
     uint32_t* err;
 };
 
@@ -94,19 +103,47 @@ __device__ __forceinline__ uint32_t word_at(const uint8_t* row, int off) {
     else return __byte_perm(w[0], w[1], 0x5432);
 }
 
+// 32-bit word at a 2-byte aligned address whose misalignment (0 or 2) is a
+// compile-time constant.
+template <int MIS>
 __device__ __forceinline__ uint32_t word2(const uint8_t* p) {
-    // p is 2-byte aligned; alignment known only at run time
-    return lds_u32_a2(p);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(p - MIS);
+    if constexpr (MIS == 0) return w[0];
+    else return __byte_perm(w[0], w[1], 0x5432);
 }
 
-// ---- per-unit consumers --------------------------------------------------
+// Exact float of an unsigned byte via the 2^23 magic (no I2F).
+__device__ __forceinline__ float ubyte_f(uint32_t w, int k) {
+    return __int_as_float(0x4B000000 | ((w >> (8 * k)) & 0xFF)) - 8388608.0f;
+}
+__device__ __forceinline__ float sbyte_f(uint32_t w, int k) {
+    return (float)(int8_t)((w >> (8 * k)) & 0xFF);
+}
+
+__device__ __forceinline__ void fma2(float& a0, float& a1, float t0, float t1, float s) {
+    // (a0, a1) += (t0, t1) * s with the packed fp32x2 FMA of sm_100
+    uint64_t acc, tv, sv;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(acc) : "f"(a0), "f"(a1));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(tv) : "f"(t0), "f"(t1));
+    asm("mov.b64 %0, {%1, %1};" : "=l"(sv) : "f"(s));
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(tv), "l"(sv));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(acc));
+}
+
+// Padding columns of the fragments are zero in shared memory, so every lane
+// loads unconditionally (no divergence).
+template <int NT>
+__device__ __forceinline__ uint4 bfrag(const uint4* xf, int c, int nt, int lane, bool) {
+    return xf[(c * NT + nt) * 32 + lane];
+}
+
+// ---- per-unit consumers (one warp, 16 rows) ----------------------------------
 
 template <int NT>
-__device__ __forceinline__ void unit_q4_0(const uint8_t* st, int u, int g, int t, int lane,
-                                          const GemvArgs& a, int chunks, bool live[NT],
-                                          float (&acc)[NT][4]) {
-    const uint8_t* rg = st + g * 144;
-    const uint8_t* rh = st + (g + 8) * 144;
+__device__ __forceinline__ void unit_q4_0(const uint8_t* stw, const uint4* xf, int row0, int g,
+                                          int t, int lane, const bool* live, float (&acc)[NT][4]) {
+    const uint8_t* rg = stw + (row0 + g) * 144;
+    const uint8_t* rh = rg + 8 * 144;
     const uint32_t k1032 = 0x64086408u;  // half2(1032, 1032)
     const uint32_t k1_16 = 0x2C002C00u;  // half2(1/16, 1/16)
     const uint32_t km72 = 0xD480D480u;   // half2(-72, -72)
@@ -122,6 +159,7 @@ __device__ __forceinline__ void unit_q4_0(const uint8_t* st, int u, int g, int t
             wg = word_at<2>(rg, 18 * b + 2 + 4 * t);
             wh = word_at<2>(rh, 18 * b + 2 + 4 * t);
         }
+        // (1024 + q) - 1032 = q - 8 and (1024 + 16q)/16 - 72 = q - 8, exact
         uint32_t a0[4], a1[4], p, q;
         nib_lo(wg, p, q);
         a0[0] = h2_sub(p, k1032);
@@ -135,124 +173,121 @@ __device__ __forceinline__ void unit_q4_0(const uint8_t* st, int u, int g, int t
         nib_hi(wh, p, q);
         a1[1] = h2_fma(p, k1_16, km72);
         a1[3] = h2_fma(q, k1_16, km72);
-        int c = u * 8 + b;
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
-            uint4 bx = live[nt] ? __ldg(a.xfrag + ((size_t)nt * chunks + c) * 32 + lane)
-                                : make_uint4(0, 0, 0, 0);
+            uint4 bx = bfrag<NT>(xf, b, nt, lane, live[nt]);
             float tmp[4];
             const float z[4] = {0.f, 0.f, 0.f, 0.f};
             uint32_t b0[2] = {bx.x, bx.y}, b1[2] = {bx.z, bx.w};
             mma_16816(tmp, a0, b0, z);
             mma_16816(tmp, a1, b1, tmp);
-            acc[nt][0] = fmaf(tmp[0], dg, acc[nt][0]);
-            acc[nt][1] = fmaf(tmp[1], dg, acc[nt][1]);
-            acc[nt][2] = fmaf(tmp[2], dh, acc[nt][2]);
-            acc[nt][3] = fmaf(tmp[3], dh, acc[nt][3]);
+            fma2(acc[nt][0], acc[nt][1], tmp[0], tmp[1], dg);
+            fma2(acc[nt][2], acc[nt][3], tmp[2], tmp[3], dh);
         }
     }
 }
 
-__device__ __forceinline__ float byte_f(uint32_t w, int k) { return (float)((w >> (8 * k)) & 0xFF); }
-
+// Q4_K.  Nibbles go into the A fragments as fp16 subnormals (bit pattern q,
+// value q * 2^-24, exact), so decode is a mask per half2; 2^24 is folded
+// into d*sc.  The per-(row, sub-block) scales d*sc*2^24 and dmin*m are
+// decoded once per unit by the whole warp into a shared table.
 template <int NT>
-__device__ __forceinline__ void unit_q4_k(const uint8_t* st, int u, int g, int t, int lane,
-                                          const GemvArgs& a, int chunks, bool live[NT],
-                                          float (&acc)[NT][4]) {
-    const uint8_t* rg = st + g * 144;
-    const uint8_t* rh = st + (g + 8) * 144;
+__device__ __forceinline__ void unit_q4_k(const uint8_t* stw, const uint4* xf, const float* xs,
+                                          float2* table, int row0, int g, int t, int lane,
+                                          const bool* live, float (&acc)[NT][4]) {
+    {
+        // DecodeScales (DequantQ4K.cs:218-241) for row lane/2, sub-blocks
+        // 4*(lane&1) .. +3, four 6-bit fields at a time
+        const int r = lane >> 1, jh = lane & 1;
+        const uint8_t* rp = stw + (row0 + r) * 144;
+        const uint32_t* W = reinterpret_cast<const uint32_t*>(rp);
+        float d = half_bits_to_float(lds_u16(rp)) * 16777216.0f;
+        float dmin = half_bits_to_float(lds_u16(rp + 2));
+        uint32_t w1 = W[1], w2 = W[2], w3 = W[3];
+        const uint32_t sc_lo = w1 & 0x3F3F3F3Fu, m_lo = w2 & 0x3F3F3F3Fu;
+        const uint32_t sc_hi = (w3 & 0x0F0F0F0Fu) | ((w1 >> 2) & 0x30303030u);
+        const uint32_t m_hi = ((w3 >> 4) & 0x0F0F0F0Fu) | ((w2 >> 2) & 0x30303030u);
+        const uint32_t sc = jh ? sc_hi : sc_lo, m = jh ? m_hi : m_lo;
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            table[r * 8 + 4 * jh + k] = make_float2(d * ubyte_f(sc, k), dmin * ubyte_f(m, k));
+    }
+    __syncwarp();
+    const uint8_t* rg = stw + (row0 + g) * 144;
+    const uint8_t* rh = rg + 8 * 144;
     const uint32_t* Wg = reinterpret_cast<const uint32_t*>(rg);
     const uint32_t* Wh = reinterpret_cast<const uint32_t*>(rh);
-    const uint32_t k1024 = 0x64006400u;
-    const uint32_t k1_16 = 0x2C002C00u;
-    const uint32_t km64 = 0xD400D400u;  // half2(-64, -64)
-    float dg = half_bits_to_float(lds_u16(rg)), mg = half_bits_to_float(lds_u16(rg + 2));
-    float dh = half_bits_to_float(lds_u16(rh)), mh = half_bits_to_float(lds_u16(rh + 2));
-    // DecodeScales (DequantQ4K.cs:218-241), four bytes at a time
-    uint32_t g0 = Wg[1], g1 = Wg[2], g2 = Wg[3];
-    uint32_t h0 = Wh[1], h1 = Wh[2], h2 = Wh[3];
-    uint32_t gsc[2] = {g0 & 0x3F3F3F3Fu, (g2 & 0x0F0F0F0Fu) | ((g0 >> 2) & 0x30303030u)};
-    uint32_t gm[2] = {g1 & 0x3F3F3F3Fu, ((g2 >> 4) & 0x0F0F0F0Fu) | ((g1 >> 2) & 0x30303030u)};
-    uint32_t hsc[2] = {h0 & 0x3F3F3F3Fu, (h2 & 0x0F0F0F0Fu) | ((h0 >> 2) & 0x30303030u)};
-    uint32_t hm[2] = {h1 & 0x3F3F3F3Fu, ((h2 >> 4) & 0x0F0F0F0Fu) | ((h1 >> 2) & 0x30303030u)};
+    const uint32_t M = 0x000F000Fu, MH = 0x00F000F0u;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
         uint32_t wg = Wg[4 + 4 * j + t], wh = Wh[4 + 4 * j + t];
-        uint32_t a0[4], a1[4], p, q;
-        nib_lo(wg, p, q);
-        a0[0] = h2_sub(p, k1024);
-        a0[2] = h2_sub(q, k1024);
-        nib_lo(wh, p, q);
-        a0[1] = h2_sub(p, k1024);
-        a0[3] = h2_sub(q, k1024);
-        nib_hi(wg, p, q);
-        a1[0] = h2_fma(p, k1_16, km64);
-        a1[2] = h2_fma(q, k1_16, km64);
-        nib_hi(wh, p, q);
-        a1[1] = h2_fma(p, k1_16, km64);
-        a1[3] = h2_fma(q, k1_16, km64);
-        float dscg = dg * byte_f(gsc[j >> 2], j & 3), dmg = mg * byte_f(gm[j >> 2], j & 3);
-        float dsch = dh * byte_f(hsc[j >> 2], j & 3), dmh = mh * byte_f(hm[j >> 2], j & 3);
-        int c = u * 8 + j;
+        // low nibbles at bits 0-3 (value q * 2^-24), high nibbles left at
+        // bits 4-7 (value 16 q * 2^-24); the high k-step's x fragments are
+        // pre-scaled by 1/16, so both k-steps accumulate q * x * 2^-24.
+        const uint32_t wg8 = wg >> 8, wh8 = wh >> 8;
+        uint32_t a0[4], a1[4];
+        a0[0] = wg & M;
+        a0[1] = wh & M;
+        a0[2] = wg8 & M;
+        a0[3] = wh8 & M;
+        a1[0] = wg & MH;
+        a1[1] = wh & MH;
+        a1[2] = wg8 & MH;
+        a1[3] = wh8 & MH;
+        const float2 sg = table[g * 8 + j], sh = table[(g + 8) * 8 + j];
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
-            uint4 bx = live[nt] ? __ldg(a.xfrag + ((size_t)nt * chunks + c) * 32 + lane)
-                                : make_uint4(0, 0, 0, 0);
-            int bidx = nt * 4 + t;
-            float xs = bidx < a.batch ? __ldg(a.xsum + (size_t)bidx * chunks + c) : 0.f;
+            uint4 bx = bfrag<NT>(xf, j, nt, lane, live[nt]);
+            float X = xs[j * NT * 4 + nt * 4 + t];
             float tmp[4];
             const float z[4] = {0.f, 0.f, 0.f, 0.f};
             uint32_t b0[2] = {bx.x, bx.y}, b1[2] = {bx.z, bx.w};
             mma_16816(tmp, a0, b0, z);
             mma_16816(tmp, a1, b1, tmp);
-            acc[nt][0] = fmaf(tmp[0], dscg, fmaf(-dmg, xs, acc[nt][0]));
-            acc[nt][1] = fmaf(tmp[1], dscg, acc[nt][1]);
-            acc[nt][2] = fmaf(tmp[2], dsch, fmaf(-dmh, xs, acc[nt][2]));
-            acc[nt][3] = fmaf(tmp[3], dsch, acc[nt][3]);
+            acc[nt][0] = fmaf(-sg.y, X, acc[nt][0]);
+            acc[nt][2] = fmaf(-sh.y, X, acc[nt][2]);
+            fma2(acc[nt][0], acc[nt][1], tmp[0], tmp[1], sg.x);
+            fma2(acc[nt][2], acc[nt][3], tmp[2], tmp[3], sh.x);
         }
     }
+    __syncwarp();  // the table is rebuilt by the next unit
 }
 
-__device__ __forceinline__ float sbyte_f(uint32_t w, int k) {
-    return (float)(int8_t)((w >> (8 * k)) & 0xFF);
-}
-
-template <int NT>
-__device__ __forceinline__ void unit_q6_k(const uint8_t* st, int u, int g, int t, int lane,
-                                          const GemvArgs& a, int chunks, bool live[NT],
+// MIS = (210 u) mod 4: super-blocks of odd units start 2 bytes off a word.
+template <int NT, int MIS>
+__device__ __forceinline__ void unit_q6_k(const uint8_t* stw, const uint4* xf, int u, int row0,
+                                          int g, int t, int lane, const bool* live,
                                           float (&acc)[NT][4]) {
     const int o = Fmt<CN_TYPE_Q6_K>::offset(u);
-    const uint8_t* rg = st + g * 240 + o;
-    const uint8_t* rh = st + (g + 8) * 240 + o;
-    const uint32_t k1056 = 0x64206420u;  // half2(1056, 1056)
+    const uint8_t* rg = stw + (row0 + g) * 240 + o;
+    const uint8_t* rh = rg + 8 * 240;
+    const uint32_t k1056 = 0x64206420u;  // half2(1056, 1056): (1024 + q) - 1056 = q - 32
     float dg = half_bits_to_float(lds_u16(rg + 208));
     float dh = half_bits_to_float(lds_u16(rh + 208));
     uint32_t scg[4], sch[4];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        scg[i] = word2(rg + 192 + 4 * i);
-        sch[i] = word2(rh + 192 + 4 * i);
+        scg[i] = word2<MIS>(rg + 192 + 4 * i);
+        sch[i] = word2<MIS>(rh + 192 + 4 * i);
     }
 #pragma unroll
     for (int h = 0; h < 2; h++) {
         uint32_t Ag[2], Bg[2], Hg[2], Ah[2], Bh[2], Hh[2];
 #pragma unroll
         for (int j = 0; j < 2; j++) {
-            Ag[j] = word2(rg + 64 * h + 16 * j + 4 * t);
-            Bg[j] = word2(rg + 64 * h + 32 + 16 * j + 4 * t);
-            Hg[j] = word2(rg + 128 + 32 * h + 16 * j + 4 * t);
-            Ah[j] = word2(rh + 64 * h + 16 * j + 4 * t);
-            Bh[j] = word2(rh + 64 * h + 32 + 16 * j + 4 * t);
-            Hh[j] = word2(rh + 128 + 32 * h + 16 * j + 4 * t);
+            Ag[j] = word2<MIS>(rg + 64 * h + 16 * j + 4 * t);
+            Bg[j] = word2<MIS>(rg + 64 * h + 32 + 16 * j + 4 * t);
+            Hg[j] = word2<MIS>(rg + 128 + 32 * h + 16 * j + 4 * t);
+            Ah[j] = word2<MIS>(rh + 64 * h + 16 * j + 4 * t);
+            Bh[j] = word2<MIS>(rh + 64 * h + 32 + 16 * j + 4 * t);
+            Hh[j] = word2<MIS>(rh + 128 + 32 * h + 16 * j + 4 * t);
         }
 #pragma unroll
         for (int s = 0; s < 4; s++) {
-            int c = u * 8 + 4 * h + s;
+            const int c = 4 * h + s;
             uint4 bxs[NT];
 #pragma unroll
-            for (int nt = 0; nt < NT; nt++)
-                bxs[nt] = live[nt] ? __ldg(a.xfrag + ((size_t)nt * chunks + c) * 32 + lane)
-                                   : make_uint4(0, 0, 0, 0);
+            for (int nt = 0; nt < NT; nt++) bxs[nt] = bfrag<NT>(xf, c, nt, lane, live[nt]);
 #pragma unroll
             for (int j = 0; j < 2; j++) {
                 // 6-bit quants of positions 4t..4t+3 of k-step (h, s, j)
@@ -275,9 +310,9 @@ __device__ __forceinline__ void unit_q6_k(const uint8_t* st, int u, int g, int t
                 av[2] = h2_sub(__byte_perm(qg, 0x64646464u, 0x4341), k1056);
                 av[1] = h2_sub(__byte_perm(qh, 0x64646464u, 0x4240), k1056);
                 av[3] = h2_sub(__byte_perm(qh, 0x64646464u, 0x4341), k1056);
-                int si = 8 * h + j + 2 * s;  // scale index (DequantQ6K.cs:61,73-76)
-                float sg = dg * sbyte_f(scg[si >> 2], si & 3);
-                float sh = dh * sbyte_f(sch[si >> 2], si & 3);
+                const int si = 8 * h + j + 2 * s;  // scale index (DequantQ6K.cs:61,73-76)
+                const float sg = dg * sbyte_f(scg[si >> 2], si & 3);
+                const float sh = dh * sbyte_f(sch[si >> 2], si & 3);
 #pragma unroll
                 for (int nt = 0; nt < NT; nt++) {
                     uint32_t bb[2];
@@ -291,10 +326,8 @@ __device__ __forceinline__ void unit_q6_k(const uint8_t* st, int u, int g, int t
                     float tmp[4];
                     const float z[4] = {0.f, 0.f, 0.f, 0.f};
                     mma_16816(tmp, av, bb, z);
-                    acc[nt][0] = fmaf(tmp[0], sg, acc[nt][0]);
-                    acc[nt][1] = fmaf(tmp[1], sg, acc[nt][1]);
-                    acc[nt][2] = fmaf(tmp[2], sh, acc[nt][2]);
-                    acc[nt][3] = fmaf(tmp[3], sh, acc[nt][3]);
+                    fma2(acc[nt][0], acc[nt][1], tmp[0], tmp[1], sg);
+                    fma2(acc[nt][2], acc[nt][3], tmp[2], tmp[3], sh);
                 }
             }
         }
@@ -303,47 +336,50 @@ __device__ __forceinline__ void unit_q6_k(const uint8_t* st, int u, int g, int t
 
 // ---- stream-K bookkeeping ---------------------------------------------------
 //
-// The (tile, unit) space is linearised tile-major and cut into W equal
-// contiguous ranges, one per warp.  A tile whose units all belong to one
-// warp is written directly; otherwise every contributing warp stores its
-// partial in slot 2*w + (tile is w's first tile ? 0 : 1), and the last of
-// them to arrive sums the slots in warp order (deterministic) and resets
-// the tile's counter for the next launch.
+// The (128-row tile, unit) space is linearised tile-major and cut into C
+// equal contiguous ranges, one per CTA, with C = min(CTAs, total units) so
+// every range is non-empty (idle CTAs, if any, come last).  A tile whose
+// units all belong to one CTA is written directly; otherwise every
+// contributing CTA stores its partial in slot 2*c + (tile is c's first tile
+// ? 0 : 1), and for each 16-row sub-tile the last warp to arrive sums the
+// slots in CTA order (deterministic) and resets that sub-tile's counter.
 
-__device__ __forceinline__ int64_t range_start(int64_t total, int w, int W) {
-    return total * w / W;
+__device__ __forceinline__ int64_t range_start(int64_t total, int c, int C) {
+    return total * c / C;
 }
 
-__device__ __forceinline__ int owner_of(int64_t v, int64_t total, int W) {
-    int w = (int)((v * W) / total);
-    while (w + 1 < W && range_start(total, w + 1, W) <= v) w++;
-    while (w > 0 && range_start(total, w, W) > v) w--;
-    return w;
+__device__ __forceinline__ int owner_of(int64_t v, int64_t total, int C) {
+    int c = (int)((v * C) / total);
+    while (c + 1 < C && range_start(total, c + 1, C) <= v) c++;
+    while (c > 0 && range_start(total, c, C) > v) c--;
+    return c;
 }
 
 template <int NT>
-__device__ void finish_tile(const GemvArgs& a, int tile, int gw, int W, int64_t total, int g, int t,
-                            int lane, float (&acc)[NT][4]) {
-    const int64_t r0 = (int64_t)tile * 16 + g, r1 = r0 + 8;
-    const int w_first = owner_of((int64_t)tile * a.units, total, W);
-    const int w_last = owner_of((int64_t)(tile + 1) * a.units - 1, total, W);
-    if (w_first == w_last) {
+__device__ void finish_subtile(const GemvArgs& a, int tile, int warp, int cta, int C,
+                               int64_t total, int g, int t, int lane, float (&acc)[NT][4]) {
+    const int64_t r0 = (int64_t)tile * kTileRows + warp * 16 + g, r1 = r0 + 8;
+    const int c_first = owner_of((int64_t)tile * a.units, total, C);
+    const int c_last = owner_of((int64_t)(tile + 1) * a.units - 1, total, C);
+    if (c_first == c_last) {
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
             int b = nt * 4 + t;
             if (b < a.batch) {
-                if (r0 < a.rows) a.y[(size_t)b * a.rows + r0] = acc[nt][0] + acc[nt][1];
-                if (r1 < a.rows) a.y[(size_t)b * a.rows + r1] = acc[nt][2] + acc[nt][3];
+                const float inv = a.xinv[b];
+                if (r0 < a.rows) a.y[(size_t)b * a.rows + r0] = (acc[nt][0] + acc[nt][1]) * inv;
+                if (r1 < a.rows) a.y[(size_t)b * a.rows + r1] = (acc[nt][2] + acc[nt][3]) * inv;
             }
         }
         return;
     }
     constexpr int BW = NT * 4;
-    auto slot = [&](int w) {
-        int first_tile = (int)(range_start(total, w, W) / a.units);
-        return 2 * w + (tile == first_tile ? 0 : 1);
+    auto slot_base = [&](int c) {
+        int first_tile = (int)(range_start(total, c, C) / a.units);
+        int slot = 2 * c + (tile == first_tile ? 0 : 1);
+        return a.partials + ((size_t)slot * kTileRows + warp * 16) * BW;
     };
-    float* p = a.partials + (size_t)slot(gw) * 16 * BW;
+    float* p = slot_base(cta);
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
         p[g * BW + nt * 4 + t] = acc[nt][0] + acc[nt][1];
@@ -352,143 +388,224 @@ __device__ void finish_tile(const GemvArgs& a, int tile, int gw, int W, int64_t 
     __threadfence();
     __syncwarp();
     int prev = 0;
-    if (lane == 0) prev = atomicAdd(&a.counters[tile], 1);
+    int* ctr = &a.counters[tile * kCons + warp];
+    if (lane == 0) prev = atomicAdd(ctr, 1);
     prev = __shfl_sync(0xffffffffu, prev, 0);
-    if (prev != w_last - w_first) return;
-    // last arrival: reduce the contributors in warp order
+    if (prev != c_last - c_first) return;
     __threadfence();
     for (int e = lane; e < 16 * BW; e += 32) {
         float s = 0.f;
-        for (int w = w_first; w <= w_last; w++)
-            s += __ldcg(a.partials + (size_t)slot(w) * 16 * BW + e);
+        for (int c = c_first; c <= c_last; c++) s += __ldcg(slot_base(c) + e);
         int row = e / BW, b = e % BW;
-        int64_t r = (int64_t)tile * 16 + row;
-        if (b < a.batch && r < a.rows) a.y[(size_t)b * a.rows + r] = s;
+        int64_t r = (int64_t)tile * kTileRows + warp * 16 + row;
+        if (b < a.batch && r < a.rows) a.y[(size_t)b * a.rows + r] = s * a.xinv[b];
     }
-    if (lane == 0) atomicExch(&a.counters[tile], 0);
+    if (lane == 0) atomicExch(ctr, 0);
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
 }
 
 // ---- the kernel ---------------------------------------------------------------
 
 template <int TYPE, int NT>
-__global__ void __launch_bounds__(kWarps * 32)
-    gemv_tma_kernel(const __grid_constant__ CUtensorMap map, const GemvArgs a) {
-    using F = Fmt<TYPE>;
-    constexpr int S = F::kStages;
-    constexpr int SB = stage_bytes<TYPE>();
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                               ~uintptr_t(1023));
+__global__ void __launch_bounds__(kThreads, Geo<TYPE, NT>::kMinCtas)
+    gemv_kernel(const __grid_constant__ CUtensorMap map, const GemvArgs a) {
+    using G = Geo<TYPE, NT>;
+    constexpr int S = G::kStages;
+    // Dynamic shared memory starts at the CTA's shared window (no static
+    // shared variables here), which is 1 KB aligned; every region below is
+    // a multiple of 128 bytes, as TMA destinations need.
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t* stages = smem;
+    float2* table = reinterpret_cast<float2*>(smem + S * G::kStage);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * G::kStage + G::kTable);
+    uint64_t* empty = full + S;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g = lane >> 2, t = lane & 3;
-    uint8_t* wsm = smem + warp * warp_smem<TYPE>();
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * warp_smem<TYPE>()) + warp * S;
 
-    if (lane == 0) {
-        for (int s = 0; s < S; s++) mbar_init(&bars[s], 1);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kCons);
+        }
         fence_mbar_init();
     }
-    __syncwarp();
+    __syncthreads();
 
-    const int chunks = a.units * 8;
     const int64_t total = (int64_t)a.tiles * a.units;
-    const int W = gridDim.x * kWarps;
-    const int gw = blockIdx.x * kWarps + warp;
-    const int64_t v0 = range_start(total, gw, W), v1 = range_start(total, gw + 1, W);
+    const int C = (int)(total < (int64_t)gridDim.x ? total : (int64_t)gridDim.x);
+    const int cta = blockIdx.x;
+    if (cta >= C) return;
+    const int64_t v0 = range_start(total, cta, C), v1 = range_start(total, cta + 1, C);
+
+    if (warp == kCons) {
+        // producer: one lane streams raw blocks + activation fragments
+        if (lane != 0) return;
+        const int nunits = (int)(v1 - v0);
+        int tile = (int)(v0 / a.units), u = (int)(v0 % a.units);
+        int s = 0;
+        uint32_t n = 0, phase = 0;
+        for (; n < (uint32_t)nunits; n++) {
+            if (n >= (uint32_t)S && !mbar_wait(&empty[s], phase ^ 1)) {
+                atomicOr(a.err, kErrTimeout);
+                for (uint32_t k = n - S; k < n; k++) mbar_wait(&full[k % S], (k / S) & 1);
+                return;
+            }
+            uint8_t* st = stages + s * G::kStage;
+            mbar_expect_tx(&full[s], G::kStage);
+            tma_load_2d(st, &map, Fmt<TYPE>::box_x(u), tile * kTileRows, &full[s]);
+            bulk_g2s(st + G::kW, a.xfrag + (size_t)u * 8 * NT * 32, G::kXF, &full[s]);
+            if constexpr (G::kXS > 0)
+                bulk_g2s(st + G::kW + G::kXF, a.xsum + (size_t)u * 8 * NT * 4, G::kXS, &full[s]);
+            if (++u == a.units) {
+                u = 0;
+                tile++;
+            }
+            if (++s == S) {
+                s = 0;
+                phase ^= 1;
+            }
+        }
+        // let the last copies land before the CTA can retire
+        for (uint32_t k = (n > (uint32_t)S ? n - S : 0); k < n; k++) mbar_wait(&full[k % S], (k / S) & 1);
+        return;
+    }
+
+    const int g = lane >> 2, t = lane & 3;
     bool live[NT];
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) live[nt] = (nt * 4 + (g >> 1)) < a.batch;
-
-    // lane 0 streams units v0..v1-1 into the stage ring
-    int64_t pv = v0;
-    auto issue = [&](int stage) {
-        if (pv >= v1) return;
-        int tile = (int)(pv / a.units), u = (int)(pv % a.units);
-        mbar_expect_tx(&bars[stage], SB);
-        tma_load_2d(wsm + stage * SB, &map, F::box_x(u), tile * 16, &bars[stage]);
-        pv++;
-    };
-    if (lane == 0)
-        for (int s = 0; s < S; s++) issue(s);
-
     float acc[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
 
-    uint32_t n = 0;  // units consumed
-    for (int64_t v = v0; v < v1; v++, n++) {
-        const int stage = n % S;
-        if (!mbar_wait(&bars[stage], (n / S) & 1)) {
+    const int nunits = (int)(v1 - v0);
+    int tile = (int)(v0 / a.units), u = (int)(v0 % a.units);
+    int s = 0;
+    uint32_t phase = 0;
+    for (int n = 0; n < nunits; n++) {
+        if (!mbar_wait(&full[s], phase)) {
             if (lane == 0) atomicOr(a.err, kErrTimeout);
-            // let the copies already issued land (bounded) before leaving
-            int64_t inflight = (v1 - v < S) ? (v1 - v) : S;
-            for (int k = 1; k < inflight; k++) mbar_wait(&bars[(n + k) % S], ((n + k) / S) & 1);
             return;
         }
-        const int tile = (int)(v / a.units), u = (int)(v % a.units);
-        const uint8_t* st = wsm + stage * SB;
-        if constexpr (TYPE == CN_TYPE_Q4_0) unit_q4_0<NT>(st, u, g, t, lane, a, chunks, live, acc);
-        else if constexpr (TYPE == CN_TYPE_Q4_K) unit_q4_k<NT>(st, u, g, t, lane, a, chunks, live, acc);
-        else unit_q6_k<NT>(st, u, g, t, lane, a, chunks, live, acc);
-        __syncwarp();
-        if (lane == 0) {
-            fence_proxy_async();
-            issue(stage);
+        const uint8_t* st = stages + s * G::kStage;
+        const uint4* xf = reinterpret_cast<const uint4*>(st + G::kW);
+        if constexpr (TYPE == CN_TYPE_Q4_0) {
+            unit_q4_0<NT>(st, xf, warp * 16, g, t, lane, live, acc);
+        } else if constexpr (TYPE == CN_TYPE_Q4_K) {
+            const float* xs = reinterpret_cast<const float*>(st + G::kW + G::kXF);
+            unit_q4_k<NT>(st, xf, xs, table + warp * 128, warp * 16, g, t, lane, live, acc);
+        } else {
+            if (u & 1) unit_q6_k<NT, 2>(st, xf, u, warp * 16, g, t, lane, live, acc);
+            else unit_q6_k<NT, 0>(st, xf, u, warp * 16, g, t, lane, live, acc);
         }
-        if (u == a.units - 1 || v == v1 - 1) {
-            finish_tile<NT>(a, tile, gw, W, total, g, t, lane, acc);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (u == a.units - 1 || n == nunits - 1) {
+            finish_subtile<NT>(a, tile, warp, cta, C, total, g, t, lane, acc);
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+        }
+        if (++u == a.units) {
+            u = 0;
+            tile++;
+        }
+        if (++s == S) {
+            s = 0;
+            phase ^= 1;
         }
     }
 }
 
 // ---- activation prep ----------------------------------------------------------
 //
-// xfrag[nt][c][lane] = the four B-fragment registers lane (g, t) feeds to
-// the two k-steps of 32-position chunk c: column g = hi (g even) or lo
-// (g odd) part of batch row 4*nt + g/2, positions 4t+{0,2}, 4t+{1,3} of
-// each 16-position half.  xsum[b][c] = fp32 sum of x[b] over chunk c.
-__global__ void xprep_kernel(const float* __restrict__ x, int K, int batch, int nt_count,
-                             uint4* __restrict__ xfrag, float* __restrict__ xsum) {
+// One CTA per batch column b of the n-tiles (4 * nt_count CTAs):
+//  * picks a power of two 2^e so that max|x[b]| * 2^e lies in [2^14, 2^15)
+//    (exact scaling; keeps the fp16 hi/lo split far from overflow and from
+//    subnormals whatever the activation range) and stores 2^-e in xinv[b];
+//  * writes its lanes of xfrag[c][nt][lane]: the four B-fragment registers
+//    lane (g, t) feeds the two k-steps of chunk c, where column g = hi (g
+//    even) or lo (g odd) part of batch b = 4*nt + g/2, positions 4t+{0,2},
+//    4t+{1,3} of each 16-position half (the second half multiplied by
+//    step1_scale: 1/16 for Q4_K, else 1);
+//  * writes xsum[c][b] = fp32 sum of the scaled x[b] over chunk c.
+// Columns b >= batch are written as zeros.
+constexpr int kPrepThreads = 1024;
+
+__global__ void __launch_bounds__(kPrepThreads)
+    xprep_kernel(const float* __restrict__ x, int K, int batch, int nt_count, float step1_scale,
+                 uint4* __restrict__ xfrag, float* __restrict__ xsum, float* __restrict__ xinv) {
+    __shared__ float red[32];
+    const int b = blockIdx.x;
     const int chunks = K / 32;
-    const int64_t total = (int64_t)nt_count * chunks * 32;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        int lane = (int)(i & 31);
-        int64_t rest = i >> 5;
-        int c = (int)(rest % chunks);
-        int nt = (int)(rest / chunks);
-        int g = lane >> 2, t = lane & 3;
-        int b = nt * 4 + (g >> 1);
-        uint4 out = make_uint4(0, 0, 0, 0);
-        if (b < batch) {
-            const float* xr = x + (size_t)b * K + (size_t)c * 32 + 4 * t;
-            float4 v0 = *reinterpret_cast<const float4*>(xr);
-            float4 v1 = *reinterpret_cast<const float4*>(xr + 16);
-            float e[8] = {v0.x, v0.z, v0.y, v0.w, v1.x, v1.z, v1.y, v1.w};
-            uint32_t r[4];
+    const int nt = b >> 2, gh = 2 * (b & 3);  // hi lane group gh, lo lane group gh + 1
+    if (b >= batch) {
+        for (int i = threadIdx.x; i < chunks * 4; i += blockDim.x) {
+            int c = i >> 2, t = i & 3;
+            xfrag[((size_t)c * nt_count + nt) * 32 + 4 * gh + t] = make_uint4(0, 0, 0, 0);
+            xfrag[((size_t)c * nt_count + nt) * 32 + 4 * (gh + 1) + t] = make_uint4(0, 0, 0, 0);
+        }
+        if (xsum)
+            for (int c = threadIdx.x; c < chunks; c += blockDim.x) xsum[(size_t)c * nt_count * 4 + b] = 0.f;
+        return;
+    }
+    const float* xr = x + (size_t)b * K;
+    float amax = 0.f;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) amax = fmaxf(amax, fabsf(xr[i]));
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                float e0 = e[2 * k], e1 = e[2 * k + 1];
-                __half2 h = __floats2half2_rn(e0, e1);
-                if (g & 1) {  // lo part: the rounding residual of the hi part
-                    float2 back = __half22float2(h);
-                    h = __floats2half2_rn(e0 - back.x, e1 - back.y);
-                }
-                r[k] = *reinterpret_cast<uint32_t*>(&h);
-            }
-            out = make_uint4(r[0], r[1], r[2], r[3]);
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) amax = fmaxf(amax, red[i]);
+    int e = 0;
+    if (amax > 0.f && amax < INFINITY) e = 14 - ilogbf(amax);
+    e = e < -120 ? -120 : (e > 120 ? 120 : e);
+    const float sc = ldexpf(1.0f, e);
+    if (threadIdx.x == 0) xinv[b] = ldexpf(1.0f, -e);
+    // chunks*4 is a multiple of 4 and blockDim a multiple of 32, so the four
+    // items of a chunk sit in adjacent lanes of one warp (for the xsum shuffle)
+    const int items = chunks * 4;
+    for (int i0 = 0; i0 < items; i0 += blockDim.x) {
+        const int i = i0 + threadIdx.x;
+        const bool on = i < items;
+        const int c = i >> 2, t = i & 3;
+        const float* p = xr + (size_t)(on ? c : 0) * 32 + 4 * t;
+        float4 v0 = *reinterpret_cast<const float4*>(p);
+        float4 v1 = *reinterpret_cast<const float4*>(p + 16);
+        if (xsum) {
+            // fp32 sum of the scaled chunk: 8 values here, 32 across the 4 lanes
+            float ps = (((v0.x * sc + v0.y * sc) + (v0.z * sc + v0.w * sc)) +
+                        ((v1.x * sc + v1.y * sc) + (v1.z * sc + v1.w * sc)));
+            ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+            if (on && t == 0) xsum[(size_t)c * nt_count * 4 + b] = ps;
         }
-        xfrag[i] = out;
-        if (xsum != nullptr && lane == 0 && nt == 0) {
-            for (int bb = 0; bb < batch; bb++) {
-                const float* xr = x + (size_t)bb * K + (size_t)c * 32;
-                float s = 0.f;
-                for (int k = 0; k < 32; k++) s += xr[k];
-                xsum[(size_t)bb * chunks + c] = s;
-            }
+        if (!on) continue;
+        const float s1 = sc * step1_scale;
+        float e8[8] = {v0.x * sc, v0.z * sc, v0.y * sc, v0.w * sc,
+                       v1.x * s1, v1.z * s1, v1.y * s1, v1.w * s1};
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            __half2 h = __floats2half2_rn(e8[2 * k], e8[2 * k + 1]);
+            float2 back = __half22float2(h);
+            __half2 l = __floats2half2_rn(e8[2 * k] - back.x, e8[2 * k + 1] - back.y);
+            hi[k] = *reinterpret_cast<uint32_t*>(&h);
+            lo[k] = *reinterpret_cast<uint32_t*>(&l);
         }
+        uint4* dst = xfrag + ((size_t)c * nt_count + nt) * 32;
+        dst[4 * gh + t] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        dst[4 * (gh + 1) + t] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
 }
 
@@ -611,7 +728,7 @@ int encode_weight_map(int type, const void* d_w, int64_t rows, uint64_t rb, CUte
     if (!enc) return set_error(CN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
     cuuint64_t dims[2] = {rb / 8, (cuuint64_t)rows};
     cuuint64_t strides[1] = {rb};
-    cuuint32_t box[2] = {(cuuint32_t)(bx / 8), 16};
+    cuuint32_t box[2] = {(cuuint32_t)(bx / 8), (cuuint32_t)kTileRows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(d_w), dims, strides,
                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -622,16 +739,17 @@ int encode_weight_map(int type, const void* d_w, int64_t rows, uint64_t rb, CUte
 
 template <int TYPE, int NT>
 static int occupancy_ctas(cn_ctx* ctx) {
-    static int cached = -1;  // per instantiation (all B200s alike)
-    if (cached < 0) {
-        auto k = gemv_tma_kernel<TYPE, NT>;
+    static int cached[64] = {0};  // per device
+    int dev = ctx->device & 63;
+    if (cached[dev] <= 0) {
+        auto k = gemv_kernel<TYPE, NT>;
         CN_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     cta_smem<TYPE>()));
+                                     Geo<TYPE, NT>::kSmem));
         int n = 0;
-        CN_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kWarps * 32, cta_smem<TYPE>()));
-        cached = n > 0 ? n : 1;
+        CN_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kThreads, Geo<TYPE, NT>::kSmem));
+        cached[dev] = n > 0 ? n : 1;
     }
-    return cached;
+    return cached[dev];
 }
 
 static int pick_nt(int batch) { return batch <= 4 ? 1 : batch <= 8 ? 2 : batch <= 16 ? 4 : 8; }
@@ -644,7 +762,7 @@ int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool
               GemvPlan* p) {
     p->nt = pick_nt(batch);
     p->tma = tma;
-    p->tiles = (int)((rows + 15) / 16);
+    p->tiles = (int)((rows + kTileRows - 1) / kTileRows);
     p->units = (int)(cols / 256);
     if (!tma) return CN_OK;
     int occ = 1;
@@ -660,112 +778,149 @@ int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool
     else { CN_OCC(CN_TYPE_Q6_K) }
 #undef CN_OCC
     if (occ < 0) return occ;  // error code from the occupancy query
-    // Stream-K grid: every resident warp gets an equal share of the
-    // (tile, unit) space, but at least 2 units each so short matrices do
-    // not spread over warps that would only fill their pipelines.
+    // Stream-K grid: every resident CTA gets an equal share of the
+    // (tile, unit) space, but at least 2 units each.
     const int64_t total = (int64_t)p->tiles * p->units;
-    int64_t want = (total / 2 + kWarps - 1) / kWarps;
-    if (want < 1) want = 1;
+    int64_t want = total / 2 > 0 ? total / 2 : 1;
     int ctas = ctx->sms * occ;
     if (want < ctas) ctas = (int)want;
     p->ctas = ctas;
-    const int W = ctas * kWarps;
     const int chunks = p->units * 8;
-    p->xfrag_bytes = (size_t)p->nt * chunks * 32 * sizeof(uint4);
-    p->xsum_bytes = type == CN_TYPE_Q4_K ? (size_t)batch * chunks * sizeof(float) : 0;
-    p->partial_bytes = (size_t)2 * W * 16 * p->nt * 4 * sizeof(float);
-    p->counters = (size_t)p->tiles;
+    p->xfrag_bytes = (size_t)chunks * p->nt * 32 * sizeof(uint4);
+    p->xsum_bytes = type == CN_TYPE_Q4_K ? (size_t)chunks * p->nt * 4 * sizeof(float) : 0;
+    p->partial_bytes = (size_t)2 * ctas * kTileRows * p->nt * 4 * sizeof(float);
+    p->counters = (size_t)p->tiles * kCons;
     return CN_OK;
 }
 
 template <int TYPE, int NT>
 static int launch_tma(cn_ctx* ctx, const CUtensorMap* map, const GemvPlan& p, const GemvArgs& a) {
-    auto k = gemv_tma_kernel<TYPE, NT>;
-    k<<<p.ctas, kWarps * 32, cta_smem<TYPE>(), ctx->stream>>>(*map, a);
+    gemv_kernel<TYPE, NT><<<p.ctas, kThreads, Geo<TYPE, NT>::kSmem, ctx->stream>>>(*map, a);
     CN_CUDA(cudaGetLastError());
+    return CN_OK;
+}
+
+int gemv_make(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols,
+              const CUtensorMap* map, int batch, GemvOp* op) {
+    CN_CHECK(type_supported(type), CN_ERR_UNSUPPORTED, "Unsupported weight quantization type: %d",
+             type);
+    CN_CHECK(d_w, CN_ERR_INVALID_ARG, "null weight pointer");
+    CN_CHECK(rows > 0 && cols > 0 && batch > 0 && batch <= 32, CN_ERR_INVALID_ARG,
+             "bad matvec shape rows=%lld cols=%lld batch=%d", (long long)rows, (long long)cols,
+             batch);
+    CN_CHECK(rows < (1ll << 31) && cols < (1ll << 31), CN_ERR_INVALID_ARG, "matvec too large");
+    op->type = type;
+    op->w = d_w;
+    op->rows = rows;
+    op->cols = cols;
+    op->batch = batch;
+    op->rb = row_bytes(type, cols);
+    op->tma = tileable(type, cols, op->rb) && ((reinterpret_cast<uintptr_t>(d_w) & 15) == 0);
+    if (op->tma) {
+        if (map) op->map = *map;
+        else if (encode_weight_map(type, d_w, rows, op->rb, &op->map) != CN_OK) op->tma = false;
+    }
+    if (!op->tma) {
+        int blk = type == CN_TYPE_Q4_0 ? 32 : (type == CN_TYPE_Q4_K || type == CN_TYPE_Q6_K) ? 256 : 1;
+        CN_CHECK(cols % blk == 0, CN_ERR_INVALID_ARG, "inDim %lld not a multiple of %d",
+                 (long long)cols, blk);
+    }
+    set_error(CN_OK, "");
+    return gemv_plan(ctx, type, rows, cols, batch, op->tma, &op->plan);
+}
+
+float gemv_step1_scale(int type) { return type == CN_TYPE_Q4_K ? 0.0625f : 1.0f; }
+
+int gemv_prep(cudaStream_t st, int sms, const GemvOp& op, const float* d_x, const GemvBufs& b) {
+    if (!op.tma) return CN_OK;
+    CN_CHECK((reinterpret_cast<uintptr_t>(d_x) & 15) == 0, CN_ERR_INVALID_ARG,
+             "x must be 16-byte aligned");
+    xprep_kernel<<<op.plan.nt * 4, kPrepThreads, 0, st>>>(
+        d_x, (int)op.cols, op.batch, op.plan.nt, gemv_step1_scale(op.type), b.xfrag,
+        op.type == CN_TYPE_Q4_K ? b.xsum : nullptr, b.xinv);
+    CN_CUDA(cudaGetLastError());
+    return CN_OK;
+}
+
+int gemv_run(cn_ctx* ctx, cudaStream_t st, const GemvOp& op, const float* d_x, const GemvBufs& b,
+             float* d_y) {
+    CN_CHECK((reinterpret_cast<uintptr_t>(d_y) & 3) == 0, CN_ERR_INVALID_ARG, "y must be aligned");
+    if (!op.tma) {
+        int blk = op.type == CN_TYPE_Q4_0 ? 32 : (op.type == CN_TYPE_Q4_K || op.type == CN_TYPE_Q6_K) ? 256 : 1;
+        int threads = 256;
+        int64_t warps = op.rows * op.batch;
+        int64_t blocks = (warps * 32 + threads - 1) / threads;
+        if (blocks > ctx->sms * 16) blocks = ctx->sms * 16;
+        gemv_generic_kernel<<<(unsigned)blocks, threads, 0, st>>>(
+            op.type, (const uint8_t*)op.w, op.rows, (int)op.cols, op.rb, blk, d_x, d_y, op.batch);
+        CN_CUDA(cudaGetLastError());
+        return CN_OK;
+    }
+    GemvArgs a;
+    a.rows = op.rows;
+    a.units = op.plan.units;
+    a.tiles = op.plan.tiles;
+    a.batch = op.batch;
+    a.xfrag = b.xfrag;
+    a.xsum = b.xsum;
+    a.xinv = b.xinv;
+    a.y = d_y;
+    a.partials = b.partials;
+    a.counters = b.counters;
+    a.err = ctx->dev_err;
+    const GemvPlan& p = op.plan;
+    const CUtensorMap* map = &op.map;
+    cn_ctx tmp = *ctx;
+    tmp.stream = st;
+#define CN_DISPATCH(T)                                               \
+    switch (p.nt) {                                                  \
+        case 1: return launch_tma<T, 1>(&tmp, map, p, a);            \
+        case 2: return launch_tma<T, 2>(&tmp, map, p, a);            \
+        case 4: return launch_tma<T, 4>(&tmp, map, p, a);            \
+        default: return launch_tma<T, 8>(&tmp, map, p, a);           \
+    }
+    if (op.type == CN_TYPE_Q4_0) { CN_DISPATCH(CN_TYPE_Q4_0) }
+    if (op.type == CN_TYPE_Q4_K) { CN_DISPATCH(CN_TYPE_Q4_K) }
+    CN_DISPATCH(CN_TYPE_Q6_K)
+#undef CN_DISPATCH
+}
+
+int gemv_reserve(const GemvPlan& p, GemvNeeds* n) {
+    size_t x = p.xfrag_bytes, s = p.xsum_bytes, pa = p.partial_bytes, c = p.counters;
+    if (x > n->xfrag_bytes) n->xfrag_bytes = x;
+    if (s > n->xsum_bytes) n->xsum_bytes = s;
+    if (pa > n->partial_bytes) n->partial_bytes = pa;
+    if (c > n->counters) n->counters = c;
     return CN_OK;
 }
 
 int gemv_launch(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols,
                 const CUtensorMap* map, const float* d_x, float* d_y, int batch) {
-    CN_CHECK(type_supported(type), CN_ERR_UNSUPPORTED, "Unsupported weight quantization type: %d",
-             type);
-    CN_CHECK(rows > 0 && cols > 0 && batch > 0 && batch <= 32, CN_ERR_INVALID_ARG,
-             "bad matvec shape rows=%lld cols=%lld batch=%d", (long long)rows, (long long)cols,
-             batch);
-    CN_CHECK(rows < (1ll << 31) && cols < (1ll << 31), CN_ERR_INVALID_ARG, "matvec too large");
     CN_CHECK((reinterpret_cast<uintptr_t>(d_x) & 15) == 0 && (reinterpret_cast<uintptr_t>(d_y) & 3) == 0,
              CN_ERR_INVALID_ARG, "x must be 16-byte aligned and y 4-byte aligned");
-    const uint64_t rb = row_bytes(type, cols);
-    CUtensorMap local;
-    bool tma = tileable(type, cols, rb) && ((reinterpret_cast<uintptr_t>(d_w) & 15) == 0);
-    if (tma && map == nullptr) {
-        if (encode_weight_map(type, d_w, rows, rb, &local) != CN_OK) tma = false;
-        else map = &local;
-    }
-    if (!tma) {
-        int blk = type == CN_TYPE_Q4_0 ? 32 : (type == CN_TYPE_Q4_K || type == CN_TYPE_Q6_K) ? 256 : 1;
-        CN_CHECK(cols % blk == 0, CN_ERR_INVALID_ARG, "inDim %lld not a multiple of %d",
-                 (long long)cols, blk);
-        int threads = 256;
-        int64_t warps = rows * batch;
-        int64_t blocks = (warps * 32 + threads - 1) / threads;
-        if (blocks > ctx->sms * 16) blocks = ctx->sms * 16;
-        gemv_generic_kernel<<<(unsigned)blocks, threads, 0, ctx->stream>>>(
-            type, (const uint8_t*)d_w, rows, (int)cols, rb, blk, d_x, d_y, batch);
-        CN_CUDA(cudaGetLastError());
-        return CN_OK;
-    }
-    GemvPlan p;
-    int rc = gemv_plan(ctx, type, rows, cols, batch, true, &p);
+    GemvOp op;
+    int rc = gemv_make(ctx, type, d_w, rows, cols, map, batch, &op);
     if (rc) return rc;
-    rc = ensure(&ctx->xfrag, &ctx->xfrag_bytes, p.xfrag_bytes, false);
+    if (op.tma) {
+        const GemvPlan& p = op.plan;
+        rc = ensure(&ctx->xfrag, &ctx->xfrag_bytes, p.xfrag_bytes, false);
+        if (!rc && p.xsum_bytes) rc = ensure((void**)&ctx->xsum, &ctx->xsum_bytes, p.xsum_bytes, false);
+        if (!rc) rc = ensure((void**)&ctx->partials, &ctx->partial_bytes, p.partial_bytes, false);
+        if (!rc && !ctx->xinv) {
+            size_t have = 0;
+            rc = ensure((void**)&ctx->xinv, &have, 256, true);
+        }
+        if (!rc) {
+            size_t cb = ctx->counter_count * sizeof(int);
+            rc = ensure((void**)&ctx->counters, &cb, p.counters * sizeof(int), true);
+            ctx->counter_count = cb / sizeof(int);
+        }
+        if (rc) return rc;
+    }
+    GemvBufs b{(uint4*)ctx->xfrag, ctx->xsum, ctx->partials, ctx->counters, ctx->xinv};
+    rc = gemv_prep(ctx->stream, ctx->sms, op, d_x, b);
     if (rc) return rc;
-    if (p.xsum_bytes) {
-        rc = ensure((void**)&ctx->xsum, &ctx->xsum_bytes, p.xsum_bytes, false);
-        if (rc) return rc;
-    }
-    if (p.partial_bytes) {
-        rc = ensure((void**)&ctx->partials, &ctx->partial_bytes, p.partial_bytes, false);
-        if (rc) return rc;
-        size_t cb = ctx->counter_count * sizeof(int);
-        rc = ensure((void**)&ctx->counters, &cb, p.counters * sizeof(int), true);
-        if (rc) return rc;
-        ctx->counter_count = cb / sizeof(int);
-    }
-    {
-        const int chunks = p.units * 8;
-        int64_t total = (int64_t)p.nt * chunks * 32;
-        int threads = 256;
-        int blocks = (int)((total + threads - 1) / threads);
-        if (blocks > ctx->sms * 8) blocks = ctx->sms * 8;
-        xprep_kernel<<<blocks, threads, 0, ctx->stream>>>(
-            d_x, (int)cols, batch, p.nt, (uint4*)ctx->xfrag,
-            type == CN_TYPE_Q4_K ? ctx->xsum : nullptr);
-        CN_CUDA(cudaGetLastError());
-    }
-    GemvArgs a;
-    a.rows = rows;
-    a.units = p.units;
-    a.tiles = p.tiles;
-    a.batch = batch;
-    a.xfrag = (const uint4*)ctx->xfrag;
-    a.xsum = ctx->xsum;
-    a.y = d_y;
-    a.partials = ctx->partials;
-    a.counters = ctx->counters;
-    a.err = ctx->dev_err;
-#define CN_DISPATCH(T)                                              \
-    switch (p.nt) {                                                 \
-        case 1: return launch_tma<T, 1>(ctx, map, p, a);            \
-        case 2: return launch_tma<T, 2>(ctx, map, p, a);            \
-        case 4: return launch_tma<T, 4>(ctx, map, p, a);            \
-        default: return launch_tma<T, 8>(ctx, map, p, a);           \
-    }
-    if (type == CN_TYPE_Q4_0) { CN_DISPATCH(CN_TYPE_Q4_0) }
-    if (type == CN_TYPE_Q4_K) { CN_DISPATCH(CN_TYPE_Q4_K) }
-    CN_DISPATCH(CN_TYPE_Q6_K)
-#undef CN_DISPATCH
+    return gemv_run(ctx, ctx->stream, op, d_x, b, d_y);
 }
 
 }  // namespace cn

@@ -1,0 +1,532 @@
+// llama.cu -- the Llama decoder on the device (cn_llama_*).
+//
+// Replaces LlamaModel (Models/Llama/LlamaModel.cs): the constructor's KV
+// cache and scratch (:48-88) become device buffers, and Forward (:93-238)
+// becomes one decode step enqueued on the context's stream:
+//
+//   embed -> per layer [RMSNorm, Q/K/V GEMVs, RoPE + KV store, GQA
+//   attention, O GEMV, residual add, RMSNorm, gate/up GEMVs, SiLU*up,
+//   down GEMV, residual add] -> final RMSNorm -> lm_head GEMV -> argmax
+//
+// The step reads token ids and positions from device memory, so one CUDA
+// graph per batch size replays every step; the host only copies ids and
+// positions in and logits / argmax out.
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <new>
+#include <vector>
+
+#include "cn_common.cuh"
+#include "cn_internal.h"
+#include "ops.h"
+#include "synth.cuh"
+
+namespace cn {
+
+enum { T_EMB = 0, T_OUT = 1, T_ONORM = 2 };
+enum { L_ANORM = 0, L_Q, L_K, L_V, L_O, L_FNORM, L_GATE, L_UP, L_DOWN };
+constexpr int kMaxBatch = 32;
+
+struct Step {
+    bool built = false;
+    std::vector<GemvOp> ops;  // [layer * 7 + {q,k,v,o,gate,up,down}], then lm_head
+    AttnPlan ap;
+    cudaGraphExec_t graph = nullptr;
+};
+
+}  // namespace cn
+
+struct cn_llama {
+    cn_ctx* ctx = nullptr;
+    cn_llama_config cfg;
+    std::vector<const cn_tensor*> t;
+    int kvdim = 0;
+    size_t kv_elem = 4;
+    int64_t seq_stride = 0;  // KV elements per sequence slot
+    void* kc = nullptr;
+    void* vc = nullptr;
+    float2* rope = nullptr;
+    float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr,
+          *tmp = nullptr, *gate = nullptr, *up = nullptr, *logits = nullptr, *part = nullptr;
+    int *tokens = nullptr, *pos = nullptr, *amax = nullptr;
+    int *h_tokens = nullptr, *h_pos = nullptr, *h_amax = nullptr;
+    cn::GemvBufs gb{nullptr, nullptr, nullptr, nullptr, nullptr};
+    size_t counter_bytes = 0;
+    cn::Step steps[cn::kMaxBatch + 1];
+    bool use_graph = true;
+};
+
+namespace cn {
+
+static const cn_tensor* LT(const cn_llama* m, int l, int j) { return m->t[3 + 9 * l + j]; }
+
+static int check_shape(const cn_tensor* t, const char* name, int64_t rows, int64_t cols,
+                       bool f32_vector) {
+    CN_CHECK(t != nullptr, CN_ERR_NOT_FOUND, "Tensor not found: %s", name);
+    if (f32_vector) {
+        CN_CHECK(t->type == CN_TYPE_F32 && t->rows * t->cols == cols, CN_ERR_INVALID_ARG,
+                 "%s must be F32 with %lld values", name, (long long)cols);
+        return CN_OK;
+    }
+    CN_CHECK(t->rows == rows && t->cols == cols, CN_ERR_INVALID_ARG,
+             "%s is [%lld, %lld], expected [%lld, %lld]", name, (long long)t->rows,
+             (long long)t->cols, (long long)rows, (long long)cols);
+    return CN_OK;
+}
+
+static int dmalloc(void** p, size_t bytes, bool zero = true) {
+    CN_CUDA(cudaMalloc(p, bytes < 256 ? 256 : bytes));
+    if (zero) CN_CUDA(cudaMemset(*p, 0, bytes < 256 ? 256 : bytes));
+    return CN_OK;
+}
+
+// Builds the per-batch GEMV ops and attention plan.
+static int build_step(cn_llama* m, int B) {
+    Step& st = m->steps[B];
+    if (st.built) return CN_OK;
+    const cn_llama_config& c = m->cfg;
+    st.ops.clear();
+    static const int wj[7] = {L_Q, L_K, L_V, L_O, L_GATE, L_UP, L_DOWN};
+    for (int l = 0; l < c.n_layers; l++)
+        for (int j = 0; j < 7; j++) {
+            const cn_tensor* w = LT(m, l, wj[j]);
+            GemvOp op;
+            int rc = gemv_make(m->ctx, w->type, w->d, w->rows, w->cols, w->has_map ? &w->map : nullptr,
+                               B, &op);
+            if (rc) return rc;
+            st.ops.push_back(op);
+        }
+    {
+        const cn_tensor* w = m->t[T_OUT];
+        GemvOp op;
+        int rc = gemv_make(m->ctx, w->type, w->d, w->rows, w->cols, w->has_map ? &w->map : nullptr,
+                           B, &op);
+        if (rc) return rc;
+        st.ops.push_back(op);
+    }
+    int rc = attention_plan(c.n_heads, c.n_kv_heads, c.head_dim, c.ctx_len, B, m->ctx->sms, &st.ap);
+    if (rc) return rc;
+    if ((rc = attention_prepare(st.ap))) return rc;
+    st.built = true;
+    return CN_OK;
+}
+
+// Tracks which activation vector the shared fragment buffer holds.
+struct PrepCache {
+    const float* x = nullptr;
+    float scale = 0.f;
+    int nt = 0;
+    int64_t cols = 0;
+};
+
+static int gemv(cn_llama* m, cudaStream_t s, const GemvOp& op, const float* x, float* y,
+                PrepCache& pc) {
+    if (op.tma) {
+        float sc = gemv_step1_scale(op.type);
+        if (pc.x != x || pc.scale != sc || pc.nt != op.plan.nt || pc.cols != op.cols ||
+            op.type == CN_TYPE_Q4_K) {
+            // Q4_K also needs the chunk sums of x, written by the same prep
+            int rc = gemv_prep(s, m->ctx->sms, op, x, m->gb);
+            if (rc) return rc;
+            pc.x = x;
+            pc.scale = sc;
+            pc.nt = op.plan.nt;
+            pc.cols = op.cols;
+        }
+    }
+    return gemv_run(m->ctx, s, op, x, m->gb, y);
+}
+
+// Enqueues one decode step for B sequences (tokens/positions already in
+// m->tokens / m->pos).
+static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
+    const cn_llama_config& c = m->cfg;
+    Step& st = m->steps[B];
+    const int dim = c.dim, hid = c.hidden_dim, kvd = m->kvdim;
+    const cn_tensor* emb = m->t[T_EMB];
+    int rc = launch_embed(emb->type, emb->d, emb->row_bytes, m->tokens, c.vocab, dim, B, m->x,
+                          m->ctx->dev_err, s);
+    if (rc) return rc;
+    PrepCache pc;
+    for (int l = 0; l < c.n_layers; l++) {
+        const GemvOp* ops = &st.ops[(size_t)l * 7];
+        rc = launch_rmsnorm(m->x, (const float*)LT(m, l, L_ANORM)->d, m->xn, dim, B, c.rms_eps, s);
+        if (rc) return rc;
+        pc = PrepCache();
+        if ((rc = gemv(m, s, ops[0], m->xn, m->q, pc))) return rc;
+        if ((rc = gemv(m, s, ops[1], m->xn, m->k, pc))) return rc;
+        if ((rc = gemv(m, s, ops[2], m->xn, m->v, pc))) return rc;
+        RopeKvArgs ra;
+        ra.q = m->q;
+        ra.k = m->k;
+        ra.v = m->v;
+        ra.rope = m->rope;
+        ra.pos_dev = m->pos;
+        ra.pos_host = 0;
+        ra.batch = B;
+        ra.n_heads = c.n_heads;
+        ra.n_kv = c.n_kv_heads;
+        ra.hd = c.head_dim;
+        ra.q_stride = dim;
+        ra.kv_stride = kvd;
+        ra.kcache = m->kc;
+        ra.vcache = m->vc;
+        ra.cache_seq_stride = m->seq_stride;
+        ra.cache_layer_off = (int64_t)l * c.ctx_len * kvd;
+        ra.kv_f16 = c.kv_dtype == CN_KV_F16;
+        ra.ctx_len = c.ctx_len;
+        ra.err = m->ctx->dev_err;
+        if ((rc = launch_rope_kv(ra, s))) return rc;
+        AttnArgs aa;
+        aa.q = m->q;
+        aa.kcache = m->kc;
+        aa.vcache = m->vc;
+        aa.pos_dev = m->pos;
+        aa.pos_host = 0;
+        aa.batch = B;
+        aa.n_heads = c.n_heads;
+        aa.n_kv = c.n_kv_heads;
+        aa.hd = c.head_dim;
+        aa.q_stride = dim;
+        aa.cache_seq_stride = m->seq_stride;
+        aa.cache_layer_off = ra.cache_layer_off;
+        aa.kv_f16 = ra.kv_f16;
+        aa.ctx_len = c.ctx_len;
+        aa.part = m->part;
+        aa.out = m->att;
+        aa.out_stride = dim;
+        if ((rc = launch_attention(aa, st.ap, s))) return rc;
+        if ((rc = gemv(m, s, ops[3], m->att, m->tmp, pc))) return rc;
+        if ((rc = launch_add(m->x, m->tmp, (int64_t)B * dim, s))) return rc;
+        rc = launch_rmsnorm(m->x, (const float*)LT(m, l, L_FNORM)->d, m->xn, dim, B, c.rms_eps, s);
+        if (rc) return rc;
+        if ((rc = gemv(m, s, ops[4], m->xn, m->gate, pc))) return rc;
+        if ((rc = gemv(m, s, ops[5], m->xn, m->up, pc))) return rc;
+        if ((rc = launch_silu_mul(m->gate, m->up, (int64_t)B * hid, s))) return rc;
+        if ((rc = gemv(m, s, ops[6], m->gate, m->tmp, pc))) return rc;
+        if ((rc = launch_add(m->x, m->tmp, (int64_t)B * dim, s))) return rc;
+    }
+    rc = launch_rmsnorm(m->x, (const float*)m->t[T_ONORM]->d, m->xn, dim, B, c.rms_eps, s);
+    if (rc) return rc;
+    pc = PrepCache();
+    if ((rc = gemv(m, s, st.ops[(size_t)c.n_layers * 7], m->xn, m->logits, pc))) return rc;
+    return launch_argmax(m->logits, c.vocab, B, m->amax, s);
+}
+
+static int run_step(cn_llama* m, int B) {
+    cudaStream_t s = m->ctx->stream;
+    int rc = build_step(m, B);
+    if (rc) return rc;
+    Step& st = m->steps[B];
+    if (!m->use_graph) return enqueue_step(m, B, s);
+    if (!st.graph) {
+        cudaGraph_t g = nullptr;
+        CN_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        rc = enqueue_step(m, B, s);
+        cudaError_t e = cudaStreamEndCapture(s, &g);
+        if (rc) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        if (e != cudaSuccess) return cuda_error(e, "cudaStreamEndCapture");
+        e = cudaGraphInstantiate(&st.graph, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) {
+            st.graph = nullptr;
+            return cuda_error(e, "cudaGraphInstantiate");
+        }
+    }
+    CN_CUDA(cudaGraphLaunch(st.graph, s));
+    return CN_OK;
+}
+
+static int check_dev_err_reset(cn_llama* m) {
+    uint32_t e = 0;
+    CN_CUDA(cudaMemcpy(&e, m->ctx->dev_err, 4, cudaMemcpyDeviceToHost));
+    if (!e) return CN_OK;
+    CN_CUDA(cudaMemset(m->ctx->dev_err, 0, 4));
+    CN_CUDA(cudaMemset(m->gb.counters, 0, m->counter_bytes));
+    if (e & kErrTimeout) return set_error(CN_ERR_TIMEOUT, "a kernel gave up waiting (0x%x)", e);
+    return set_error(CN_ERR_INVALID_ARG, "token id or position out of range (0x%x)", e);
+}
+
+__global__ void kv_synth_kernel(uint64_t seed, int layers, int npos, int ctx, int kvd, int f16,
+                                void* out) {
+    const int64_t n = (int64_t)layers * npos * kvd;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t l = i / ((int64_t)npos * kvd);
+        int64_t r = i % ((int64_t)npos * kvd);
+        int64_t idx = (l * ctx + r / kvd) * kvd + r % kvd;
+        float v = synth::normal_elem(seed, (uint64_t)idx);
+        if (f16) reinterpret_cast<__half*>(out)[idx] = __float2half_rn(v);
+        else reinterpret_cast<float*>(out)[idx] = v;
+    }
+}
+
+static void free_model(cn_llama* m) {
+    for (int b = 0; b <= kMaxBatch; b++)
+        if (m->steps[b].graph) cudaGraphExecDestroy(m->steps[b].graph);
+    void* bufs[] = {m->kc, m->vc, m->rope, m->x, m->xn, m->q, m->k, m->v, m->att, m->tmp,
+                    m->gate, m->up, m->logits, m->part, m->tokens, m->pos, m->amax,
+                    m->gb.xfrag, m->gb.xsum, m->gb.partials, m->gb.counters, m->gb.xinv};
+    for (void* p : bufs) cudaFree(p);
+    cudaFreeHost(m->h_tokens);
+    cudaFreeHost(m->h_pos);
+    cudaFreeHost(m->h_amax);
+    delete m;
+}
+
+}  // namespace cn
+
+using namespace cn;
+
+extern "C" {
+
+int cn_llama_create(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* const* tensors,
+                    int n_tensors, cn_llama** out) {
+    CN_CHECK(ctx && cfg && tensors && out, CN_ERR_INVALID_ARG, "null argument");
+    *out = nullptr;
+    const cn_llama_config c = *cfg;
+    CN_CHECK(c.n_layers > 0 && c.dim > 0 && c.hidden_dim > 0 && c.n_heads > 0 && c.n_kv_heads > 0 &&
+                 c.head_dim > 0 && c.vocab > 0 && c.ctx_len > 0,
+             CN_ERR_INVALID_ARG, "non-positive hyper-parameter");
+    CN_CHECK(c.n_heads * c.head_dim == c.dim, CN_ERR_INVALID_ARG,
+             "n_heads * head_dim (%d) != dim (%d)", c.n_heads * c.head_dim, c.dim);
+    CN_CHECK(c.n_heads % c.n_kv_heads == 0, CN_ERR_INVALID_ARG, "n_heads %% n_kv_heads != 0");
+    CN_CHECK(c.max_batch >= 1 && c.max_batch <= kMaxBatch, CN_ERR_INVALID_ARG,
+             "max_batch %d outside [1, %d]", c.max_batch, kMaxBatch);
+    CN_CHECK(c.kv_dtype == CN_KV_F32 || c.kv_dtype == CN_KV_F16, CN_ERR_INVALID_ARG,
+             "bad kv_dtype %d", c.kv_dtype);
+    CN_CHECK(n_tensors == CN_LLAMA_TENSORS(c.n_layers), CN_ERR_INVALID_ARG,
+             "expected %d tensors, got %d", CN_LLAMA_TENSORS(c.n_layers), n_tensors);
+    const int kvd = c.n_kv_heads * c.head_dim;
+    int rc;
+    if ((rc = check_shape(tensors[T_EMB], "token_embd.weight", c.vocab, c.dim, false))) return rc;
+    if ((rc = check_shape(tensors[T_OUT], "output.weight", c.vocab, c.dim, false))) return rc;
+    if ((rc = check_shape(tensors[T_ONORM], "output_norm.weight", 1, c.dim, true))) return rc;
+    for (int l = 0; l < c.n_layers; l++) {
+        const cn_tensor* const* L = tensors + 3 + 9 * l;
+        if ((rc = check_shape(L[L_ANORM], "attn_norm.weight", 1, c.dim, true))) return rc;
+        if ((rc = check_shape(L[L_Q], "attn_q.weight", c.dim, c.dim, false))) return rc;
+        if ((rc = check_shape(L[L_K], "attn_k.weight", kvd, c.dim, false))) return rc;
+        if ((rc = check_shape(L[L_V], "attn_v.weight", kvd, c.dim, false))) return rc;
+        if ((rc = check_shape(L[L_O], "attn_output.weight", c.dim, c.dim, false))) return rc;
+        if ((rc = check_shape(L[L_FNORM], "ffn_norm.weight", 1, c.dim, true))) return rc;
+        if ((rc = check_shape(L[L_GATE], "ffn_gate.weight", c.hidden_dim, c.dim, false))) return rc;
+        if ((rc = check_shape(L[L_UP], "ffn_up.weight", c.hidden_dim, c.dim, false))) return rc;
+        if ((rc = check_shape(L[L_DOWN], "ffn_down.weight", c.dim, c.hidden_dim, false))) return rc;
+    }
+    for (int i = 0; i < n_tensors; i++)
+        CN_CHECK(tensors[i]->ctx == ctx, CN_ERR_INVALID_ARG, "tensor %d belongs to another context", i);
+    {
+        AttnPlan ap;
+        if ((rc = attention_plan(c.n_heads, c.n_kv_heads, c.head_dim, c.ctx_len, c.max_batch,
+                                 ctx->sms, &ap)))
+            return rc;
+    }
+
+    cudaSetDevice(ctx->device);
+    cn_llama* m = new (std::nothrow) cn_llama();
+    CN_CHECK(m, CN_ERR_OOM, "host allocation failed");
+    m->ctx = ctx;
+    m->cfg = c;
+    m->t.assign(tensors, tensors + n_tensors);
+    m->kvdim = kvd;
+    m->kv_elem = c.kv_dtype == CN_KV_F16 ? 2 : 4;
+    m->seq_stride = (int64_t)c.n_layers * c.ctx_len * kvd;
+    m->use_graph = getenv("CN_NO_GRAPH") == nullptr;
+    const int B = c.max_batch;
+    const size_t kvbytes = (size_t)B * m->seq_stride * m->kv_elem;
+    auto fail = [&](int code) {
+        free_model(m);
+        return code;
+    };
+    if ((rc = dmalloc(&m->kc, kvbytes)) || (rc = dmalloc(&m->vc, kvbytes))) return fail(rc);
+    // RoPE table, computed with the reference's formula and the host libm
+    // (TensorMath.ApplyRoPE, TensorMath.cs:418-432).
+    {
+        const int half = c.head_dim / 2;
+        std::vector<float2> tab((size_t)c.ctx_len * half);
+        const float neg_log_base = -logf(c.rope_base);
+        const float dim_inv = 1.0f / (float)c.head_dim;
+        for (int p = 0; p < c.ctx_len; p++)
+            for (int i = 0; i < c.head_dim; i += 2) {
+                float theta = (float)p * expf((float)i * dim_inv * neg_log_base);
+                tab[(size_t)p * half + i / 2] = make_float2(cosf(theta), sinf(theta));
+            }
+        if ((rc = dmalloc((void**)&m->rope, tab.size() * sizeof(float2), false))) return fail(rc);
+        cudaError_t e = cudaMemcpy(m->rope, tab.data(), tab.size() * sizeof(float2),
+                                   cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return fail(cuda_error(e, "rope upload"));
+    }
+    const size_t fd = (size_t)B * c.dim * 4, fk = (size_t)B * kvd * 4, fh = (size_t)B * c.hidden_dim * 4;
+    if ((rc = dmalloc((void**)&m->x, fd)) || (rc = dmalloc((void**)&m->xn, fd)) ||
+        (rc = dmalloc((void**)&m->q, fd)) || (rc = dmalloc((void**)&m->k, fk)) ||
+        (rc = dmalloc((void**)&m->v, fk)) || (rc = dmalloc((void**)&m->att, fd)) ||
+        (rc = dmalloc((void**)&m->tmp, fd)) || (rc = dmalloc((void**)&m->gate, fh)) ||
+        (rc = dmalloc((void**)&m->up, fh)) ||
+        (rc = dmalloc((void**)&m->logits, (size_t)B * c.vocab * 4)) ||
+        (rc = dmalloc((void**)&m->tokens, B * 4)) || (rc = dmalloc((void**)&m->pos, B * 4)) ||
+        (rc = dmalloc((void**)&m->amax, B * 4)))
+        return fail(rc);
+    {
+        // split counts depend on the batch size: size for the largest need
+        size_t part = 0;
+        for (int b = 1; b <= B; b++) {
+            AttnPlan ap;
+            attention_plan(c.n_heads, c.n_kv_heads, c.head_dim, c.ctx_len, b, ctx->sms, &ap);
+            if (ap.part_floats > part) part = ap.part_floats;
+        }
+        if ((rc = dmalloc((void**)&m->part, part * 4))) return fail(rc);
+    }
+    // GEMV scratch for the largest plan of any batch size up to max_batch
+    {
+        GemvNeeds need;
+        const int reps[4] = {4, 8, 16, 32};
+        for (int r = 0; r < 4; r++) {
+            int b = reps[r] < B ? reps[r] : B;
+            for (int i = 0; i < n_tensors; i++) {
+                const cn_tensor* w = tensors[i];
+                if (w->type == CN_TYPE_F32 && (i == T_ONORM || (i >= 3 && (i - 3) % 9 == L_ANORM) ||
+                                               (i >= 3 && (i - 3) % 9 == L_FNORM)))
+                    continue;
+                GemvOp op;
+                if ((rc = gemv_make(ctx, w->type, w->d, w->rows, w->cols, w->has_map ? &w->map : nullptr,
+                                    b, &op)))
+                    return fail(rc);
+                gemv_reserve(op.plan, &need);
+            }
+            if (reps[r] >= B) break;
+        }
+        if ((rc = dmalloc((void**)&m->gb.xfrag, need.xfrag_bytes, true)) ||
+            (rc = dmalloc((void**)&m->gb.xsum, need.xsum_bytes, true)) ||
+            (rc = dmalloc((void**)&m->gb.partials, need.partial_bytes, false)) ||
+            (rc = dmalloc((void**)&m->gb.counters, need.counters * 4 + 256, true)) ||
+            (rc = dmalloc((void**)&m->gb.xinv, 256, true)))
+            return fail(rc);
+        m->counter_bytes = need.counters * 4 + 256;
+    }
+    cudaError_t e = cudaMallocHost((void**)&m->h_tokens, B * 4);
+    if (e == cudaSuccess) e = cudaMallocHost((void**)&m->h_pos, B * 4);
+    if (e == cudaSuccess) e = cudaMallocHost((void**)&m->h_amax, B * 4);
+    if (e != cudaSuccess) return fail(cuda_error(e, "cudaMallocHost"));
+    set_error(CN_OK, "");
+    *out = m;
+    return CN_OK;
+}
+
+int cn_llama_destroy(cn_llama* m) {
+    if (!m) return CN_OK;
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    free_model(m);
+    return CN_OK;
+}
+
+int cn_llama_decode(cn_llama* m, const int* tokens, const int* pos, int batch, float* logits_host,
+                    int* argmax_host) {
+    CN_CHECK(m && tokens && pos, CN_ERR_INVALID_ARG, "null argument");
+    CN_CHECK(batch >= 1 && batch <= m->cfg.max_batch, CN_ERR_INVALID_ARG,
+             "batch %d outside [1, %d]", batch, m->cfg.max_batch);
+    for (int b = 0; b < batch; b++) {
+        CN_CHECK(tokens[b] >= 0 && tokens[b] < m->cfg.vocab, CN_ERR_INVALID_ARG,
+                 "token id %d outside [0, %d)", tokens[b], m->cfg.vocab);
+        CN_CHECK(pos[b] >= 0 && pos[b] < m->cfg.ctx_len, CN_ERR_INVALID_ARG,
+                 "position %d outside [0, %d)", pos[b], m->cfg.ctx_len);
+    }
+    cudaSetDevice(m->ctx->device);
+    cudaStream_t s = m->ctx->stream;
+    memcpy(m->h_tokens, tokens, batch * 4);
+    memcpy(m->h_pos, pos, batch * 4);
+    CN_CUDA(cudaMemcpyAsync(m->tokens, m->h_tokens, batch * 4, cudaMemcpyHostToDevice, s));
+    CN_CUDA(cudaMemcpyAsync(m->pos, m->h_pos, batch * 4, cudaMemcpyHostToDevice, s));
+    int rc = run_step(m, batch);
+    if (rc) return rc;
+    if (logits_host)
+        CN_CUDA(cudaMemcpyAsync(logits_host, m->logits, (size_t)batch * m->cfg.vocab * 4,
+                                cudaMemcpyDeviceToHost, s));
+    if (argmax_host) CN_CUDA(cudaMemcpyAsync(m->h_amax, m->amax, batch * 4, cudaMemcpyDeviceToHost, s));
+    CN_CUDA(cudaStreamSynchronize(s));
+    if ((rc = check_dev_err_reset(m))) return rc;
+    if (argmax_host) memcpy(argmax_host, m->h_amax, batch * 4);
+    return CN_OK;
+}
+
+int cn_llama_forward(cn_llama* m, const int* tokens, int n, int pos, float* logits_host) {
+    CN_CHECK(m && tokens && logits_host, CN_ERR_INVALID_ARG, "null argument");
+    CN_CHECK(n >= 1, CN_ERR_INVALID_ARG, "no tokens");
+    CN_CHECK(pos >= 0 && pos + n <= m->cfg.ctx_len, CN_ERR_INVALID_ARG,
+             "positions [%d, %d) outside the context of %d", pos, pos + n, m->cfg.ctx_len);
+    for (int t = 0; t < n; t++) {
+        int p = pos + t;
+        int rc = cn_llama_decode(m, tokens + t, &p, 1, t == n - 1 ? logits_host : nullptr, nullptr);
+        if (rc) return rc;
+    }
+    return CN_OK;
+}
+
+static int kv_check(cn_llama* m, int seq, int layer, int pos0, int npos) {
+    CN_CHECK(m, CN_ERR_INVALID_ARG, "null model");
+    CN_CHECK(seq >= 0 && seq < m->cfg.max_batch, CN_ERR_INVALID_ARG, "seq %d out of range", seq);
+    CN_CHECK(layer >= 0 && layer < m->cfg.n_layers, CN_ERR_INVALID_ARG, "layer %d out of range", layer);
+    CN_CHECK(pos0 >= 0 && npos >= 0 && pos0 + npos <= m->cfg.ctx_len, CN_ERR_INVALID_ARG,
+             "positions out of range");
+    return CN_OK;
+}
+
+int cn_llama_kv_write(cn_llama* m, int seq, int layer, int pos0, int npos, const void* k_host,
+                      const void* v_host) {
+    int rc = kv_check(m, seq, layer, pos0, npos);
+    if (rc) return rc;
+    cudaSetDevice(m->ctx->device);
+    size_t off = ((size_t)seq * m->seq_stride + ((size_t)layer * m->cfg.ctx_len + pos0) * m->kvdim) *
+                 m->kv_elem;
+    size_t bytes = (size_t)npos * m->kvdim * m->kv_elem;
+    CN_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    if (k_host) CN_CUDA(cudaMemcpy((uint8_t*)m->kc + off, k_host, bytes, cudaMemcpyHostToDevice));
+    if (v_host) CN_CUDA(cudaMemcpy((uint8_t*)m->vc + off, v_host, bytes, cudaMemcpyHostToDevice));
+    return CN_OK;
+}
+
+int cn_llama_kv_read(cn_llama* m, int seq, int layer, int pos0, int npos, void* k_host,
+                     void* v_host) {
+    int rc = kv_check(m, seq, layer, pos0, npos);
+    if (rc) return rc;
+    cudaSetDevice(m->ctx->device);
+    size_t off = ((size_t)seq * m->seq_stride + ((size_t)layer * m->cfg.ctx_len + pos0) * m->kvdim) *
+                 m->kv_elem;
+    size_t bytes = (size_t)npos * m->kvdim * m->kv_elem;
+    CN_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    if (k_host) CN_CUDA(cudaMemcpy(k_host, (uint8_t*)m->kc + off, bytes, cudaMemcpyDeviceToHost));
+    if (v_host) CN_CUDA(cudaMemcpy(v_host, (uint8_t*)m->vc + off, bytes, cudaMemcpyDeviceToHost));
+    return CN_OK;
+}
+
+int cn_llama_kv_synth(cn_llama* m, int seq, int npos, uint64_t seed_k, uint64_t seed_v) {
+    int rc = kv_check(m, seq, 0, 0, npos);
+    if (rc) return rc;
+    cudaSetDevice(m->ctx->device);
+    cudaStream_t s = m->ctx->stream;
+    const size_t seq_bytes = (size_t)m->seq_stride * m->kv_elem;
+    uint8_t* kb = (uint8_t*)m->kc + (size_t)seq * seq_bytes;
+    uint8_t* vb = (uint8_t*)m->vc + (size_t)seq * seq_bytes;
+    CN_CUDA(cudaMemsetAsync(kb, 0, seq_bytes, s));
+    CN_CUDA(cudaMemsetAsync(vb, 0, seq_bytes, s));
+    if (npos > 0) {
+        int64_t n = (int64_t)m->cfg.n_layers * npos * m->kvdim;
+        int blocks = (int)((n + 255) / 256 > 148 * 64 ? 148 * 64 : (n + 255) / 256);
+        int f16 = m->cfg.kv_dtype == CN_KV_F16;
+        kv_synth_kernel<<<blocks, 256, 0, s>>>(seed_k, m->cfg.n_layers, npos, m->cfg.ctx_len, m->kvdim,
+                                               f16, kb);
+        kv_synth_kernel<<<blocks, 256, 0, s>>>(seed_v, m->cfg.n_layers, npos, m->cfg.ctx_len, m->kvdim,
+                                               f16, vb);
+        CN_CUDA(cudaGetLastError());
+    }
+    CN_CUDA(cudaStreamSynchronize(s));
+    return CN_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,449 @@
+// ops.cu -- the decode-step kernels around the GEMVs.
+//
+//   rmsnorm_kernel     TensorMath.RmsNorm            (Tensors/TensorMath.cs:97-165)
+//   rope_kv_kernel     TensorMath.ApplyRoPE + the KV-cache store
+//                      (TensorMath.cs:408-458, Models/Llama/LlamaModel.cs:146-153)
+//   attn_split_kernel  LlamaModel.ComputeAttention + TensorMath.Softmax
+//   attn_combine_kernel   (LlamaModel.cs:241-346, TensorMath.cs:177-241), split over
+//                      the context (flash-decoding) and merged exactly once
+//   silu_mul_kernel    TensorMath.SiluElementwiseMul (TensorMath.cs:253-286)
+//   add_kernel         TensorMath.Add                (TensorMath.cs:712-733)
+//   embed_kernel       LlamaModel.LoadEmbedding      (LlamaModel.cs:365-394)
+//   argmax_kernel      GreedySampler.Sample          (Samplers/GreedySampler.cs:13-26)
+//
+// Elementwise arithmetic uses the reference's operation order with explicit
+// round-to-nearest intrinsics; reductions (sums of squares, dot products,
+// softmax sums) run in a different order than the C# loops, which changes
+// results only at the level of fp32 rounding.
+#include <float.h>
+
+#include "cn_common.cuh"
+#include "cn_internal.h"
+#include "formats.cuh"
+#include "ops.h"
+
+namespace cn {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Block-wide sum; `red` holds one float per warp.  All threads get the sum.
+__device__ float block_sum(float v, float* red) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    float s = 0.f;
+    for (int i = 0; i < nw; i++) s += red[i];
+    return s;
+}
+__device__ float block_max(float v, float* red) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_max(v);
+    __syncthreads();
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    float m = -FLT_MAX;
+    for (int i = 0; i < nw; i++) m = fmaxf(m, red[i]);
+    return m;
+}
+
+// ---- RMSNorm: y = x * (1 / sqrt(sum(x^2)/n + eps)) * w, one CTA per row ----
+
+__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                               float* __restrict__ y, int n, float eps) {
+    __shared__ float red[32];
+    const float* xr = x + (size_t)blockIdx.x * n;
+    float* yr = y + (size_t)blockIdx.x * n;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+    ss = block_sum(ss, red);
+    const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+        yr[i] = __fmul_rn(__fmul_rn(xr[i], rms), w[i]);
+}
+
+// ---- RoPE (interleaved pairs) on q and k, then k and v into the cache ---------
+//
+// cos/sin come from a host-built table [ctx][head_dim/2] computed exactly as
+// ApplyRoPE does (theta = pos * exp(i * (1/hd) * -ln(base)), libm cos/sin),
+// so the rotation factors are bit-identical to the reference's.
+
+__global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ k,
+                               const float* __restrict__ v, const float2* __restrict__ rope,
+                               const int* __restrict__ pos_dev, int pos_host, int n_heads,
+                               int n_kv, int hd, int q_stride, int kv_stride, void* kcache,
+                               void* vcache, int64_t cache_seq_stride, int64_t cache_layer_off,
+                               int kv_f16, int ctx_len, uint32_t* err) {
+    const int b = blockIdx.y;
+    const int pos = pos_dev ? pos_dev[b] : pos_host;
+    if (pos < 0 || pos >= ctx_len) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(err, kErrBadArg);
+        return;
+    }
+    const int half = hd / 2;
+    const float2* tab = rope + (size_t)pos * half;
+    const int total = (n_heads + n_kv) * half + n_kv * hd;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const int64_t base = (int64_t)b * cache_seq_stride + cache_layer_off + (int64_t)pos * n_kv * hd;
+        if (i < n_heads * half) {
+            int h = i / half, p = i % half;
+            float* vec = q + (size_t)b * q_stride + h * hd + 2 * p;
+            float2 cs = tab[p];
+            float x0 = vec[0], x1 = vec[1];
+            vec[0] = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+            vec[1] = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+        } else if (i < (n_heads + n_kv) * half) {
+            int j = i - n_heads * half;
+            int h = j / half, p = j % half;
+            const float* vec = k + (size_t)b * kv_stride + h * hd + 2 * p;
+            float2 cs = tab[p];
+            float x0 = vec[0], x1 = vec[1];
+            float r0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+            float r1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+            int64_t off = base + h * hd + 2 * p;
+            if (kv_f16) {
+                reinterpret_cast<__half*>(kcache)[off] = __float2half_rn(r0);
+                reinterpret_cast<__half*>(kcache)[off + 1] = __float2half_rn(r1);
+            } else {
+                reinterpret_cast<float*>(kcache)[off] = r0;
+                reinterpret_cast<float*>(kcache)[off + 1] = r1;
+            }
+        } else {
+            int d = i - (n_heads + n_kv) * half;
+            float val = v[(size_t)b * kv_stride + d];
+            if (kv_f16) reinterpret_cast<__half*>(vcache)[base + d] = __float2half_rn(val);
+            else reinterpret_cast<float*>(vcache)[base + d] = val;
+        }
+    }
+}
+
+// ---- attention: split-K over positions, then combine ----------------------------
+//
+// CTA (split s, kv head kh, sequence b) handles positions [p0, p1) of
+// 0..pos for the kv_mul query heads that share kv head kh (GQA: head h uses
+// kv head h / kv_mul, LlamaModel.cs:265).  It writes, per query head, the
+// local max m, sum l = sum exp(score - m) and o = sum exp(score - m) v to
+// scratch; the combine kernel merges the splits:
+//   out = sum_s exp(m_s - M) o_s / sum_s exp(m_s - M) l_s.
+// This equals Softmax followed by the weighted V sum up to fp32 rounding.
+
+template <typename KV>
+__device__ __forceinline__ float kv_load(const KV* p);
+template <>
+__device__ __forceinline__ float kv_load<float>(const float* p) { return *p; }
+template <>
+__device__ __forceinline__ float kv_load<__half>(const __half* p) { return __half2float(*p); }
+
+constexpr int kAttnThreads = 256;
+constexpr int kMaxKvMul = 16;
+constexpr int kMaxHd = 256;
+
+template <typename KV>
+__global__ void __launch_bounds__(kAttnThreads)
+    attn_split_kernel(const float* __restrict__ q, const KV* __restrict__ kcache,
+                      const KV* __restrict__ vcache, const int* __restrict__ pos_dev, int pos_host,
+                      int n_heads, int n_kv, int hd, int q_stride, int64_t cache_seq_stride,
+                      int64_t cache_layer_off, int ctx_len, int splits, int chunk, float scale,
+                      float* __restrict__ part /* [b][head][split][hd + 2] */) {
+    extern __shared__ float sm[];
+    const int s = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
+    const int kv_mul = n_heads / n_kv;
+    int pos = pos_dev ? pos_dev[b] : pos_host;
+    if (pos < 0 || pos >= ctx_len) pos = -1;  // rejected upstream; read nothing
+    const int seq = pos + 1;
+    const int p0 = s * chunk;
+    const int p1 = min(seq, p0 + chunk);
+    const int L = max(0, p1 - p0);
+    float* qs = sm;                          // [kv_mul][hd]
+    float* sc = qs + kv_mul * hd;            // [kv_mul][chunk]
+    float* red = sc + kv_mul * chunk;        // [32]
+    const int kvdim = n_kv * hd;
+    for (int i = threadIdx.x; i < kv_mul * hd; i += blockDim.x)
+        qs[i] = q[(size_t)b * q_stride + (kh * kv_mul) * hd + i];
+    __syncthreads();
+    const KV* kbase = kcache + (int64_t)b * cache_seq_stride + cache_layer_off + kh * hd;
+    const KV* vbase = vcache + (int64_t)b * cache_seq_stride + cache_layer_off + kh * hd;
+    // scores: thread per position, all kv_mul heads
+    for (int i = threadIdx.x; i < L; i += blockDim.x) {
+        const KV* kr = kbase + (int64_t)(p0 + i) * kvdim;
+        float acc[kMaxKvMul];
+#pragma unroll
+        for (int g = 0; g < kMaxKvMul; g++) acc[g] = 0.f;
+        for (int d = 0; d < hd; d++) {
+            float kv = kv_load<KV>(kr + d);
+#pragma unroll
+            for (int g = 0; g < kMaxKvMul; g++)
+                if (g < kv_mul) acc[g] = fmaf(qs[g * hd + d], kv, acc[g]);
+        }
+#pragma unroll
+        for (int g = 0; g < kMaxKvMul; g++)
+            if (g < kv_mul) sc[g * chunk + i] = __fmul_rn(acc[g], scale);
+    }
+    __syncthreads();
+    // local softmax statistics per head
+    for (int g = 0; g < kv_mul; g++) {
+        float m = -FLT_MAX;
+        for (int i = threadIdx.x; i < L; i += blockDim.x) m = fmaxf(m, sc[g * chunk + i]);
+        m = block_max(m, red);
+        float l = 0.f;
+        for (int i = threadIdx.x; i < L; i += blockDim.x) {
+            float e = expf(sc[g * chunk + i] - m);
+            sc[g * chunk + i] = e;
+            l += e;
+        }
+        l = block_sum(l, red);
+        if (threadIdx.x == 0) {
+            float* pr = part + (((size_t)b * n_heads + kh * kv_mul + g) * splits + s) * (hd + 2);
+            pr[hd] = L > 0 ? m : -FLT_MAX;
+            pr[hd + 1] = l;
+        }
+    }
+    __syncthreads();
+    // o[g][d] = sum_i e[g][i] * v[i][d]
+    for (int e = threadIdx.x; e < kv_mul * hd; e += blockDim.x) {
+        const int g = e / hd, d = e % hd;
+        float o = 0.f;
+        for (int i = 0; i < L; i++) o = fmaf(sc[g * chunk + i], kv_load<KV>(vbase + (int64_t)(p0 + i) * kvdim + d), o);
+        part[(((size_t)b * n_heads + kh * kv_mul + g) * splits + s) * (hd + 2) + d] = o;
+    }
+}
+
+__global__ void attn_combine_kernel(const float* __restrict__ part, int n_heads, int hd, int splits,
+                                    float* __restrict__ out, int out_stride) {
+    const int h = blockIdx.x, b = blockIdx.y;
+    const float* pr = part + ((size_t)b * n_heads + h) * splits * (hd + 2);
+    float M = -FLT_MAX;
+    for (int s = 0; s < splits; s++) M = fmaxf(M, pr[s * (hd + 2) + hd]);
+    float Lsum = 0.f;
+    for (int s = 0; s < splits; s++) {
+        float m = pr[s * (hd + 2) + hd];
+        if (m > -FLT_MAX) Lsum += expf(m - M) * pr[s * (hd + 2) + hd + 1];
+    }
+    const float inv = 1.0f / Lsum;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float o = 0.f;
+        for (int s = 0; s < splits; s++) {
+            float m = pr[s * (hd + 2) + hd];
+            if (m > -FLT_MAX) o += expf(m - M) * pr[s * (hd + 2) + d];
+        }
+        out[(size_t)b * out_stride + h * hd + d] = o * inv;
+    }
+}
+
+// ---- elementwise -----------------------------------------------------------------
+
+__global__ void silu_mul_kernel(float* __restrict__ gate, const float* __restrict__ up, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        float x = gate[i];
+        float s = __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
+        gate[i] = __fmul_rn(s, up[i]);
+    }
+}
+
+__global__ void add_kernel(float* __restrict__ a, const float* __restrict__ b, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        a[i] = __fadd_rn(a[i], b[i]);
+}
+
+// ---- embedding: dequantize row tokens[b] of token_embd (bit-exact) -----------------
+
+__global__ void embed_kernel(int type, const uint8_t* __restrict__ emb, uint64_t row_bytes,
+                             const int* __restrict__ tokens, int vocab, int dim,
+                             float* __restrict__ x, uint32_t* err) {
+    const int b = blockIdx.y;
+    const int tok = tokens[b];
+    if (tok < 0 || tok >= vocab) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(err, kErrBadArg);
+        return;
+    }
+    const uint8_t* row = emb + (size_t)tok * row_bytes;
+    float* out = x + (size_t)b * dim;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x) {
+        float v;
+        if (type == CN_TYPE_Q4_0) {
+            const uint8_t* p = row + (i / 32) * 18;
+            int j = i % 32;
+            int q = j < 16 ? (p[2 + j] & 0x0F) : ((p[2 + j - 16] >> 4) & 0x0F);
+            v = __fmul_rn((float)(q - 8), ld_half(p));
+        } else if (type == CN_TYPE_Q4_K) {
+            const uint8_t* p = row + (i / 256) * 144;
+            int w = i % 256, sub = w / 32, j = w % 32;
+            int sc, m;
+            q4k_scale_min(p + 4, sub, sc, m);
+            float dsc = __fmul_rn(ld_half(p), (float)sc), dm = __fmul_rn(ld_half(p + 2), (float)m);
+            uint8_t byte = p[16 + sub * 16 + (j & 15)];
+            int q = j < 16 ? (byte & 0x0F) : ((byte >> 4) & 0x0F);
+            v = __fsub_rn(__fmul_rn(dsc, (float)q), dm);
+        } else if (type == CN_TYPE_Q6_K) {
+            const uint8_t* p = row + (i / 256) * 210;
+            int w = i % 256, half = w / 128, r = w % 128, s = r / 32, l = r % 32;
+            const uint8_t* ql = p + half * 64;
+            const uint8_t* qh = p + 128 + half * 32;
+            int lo = (s & 1) ? ql[l + 32] : ql[l];
+            lo = (s >> 1) ? (lo >> 4) : (lo & 0x0F);
+            int q = (lo | (((qh[l] >> (2 * s)) & 3) << 4)) - 32;
+            int si = half * 8 + l / 16 + 2 * s;
+            v = __fmul_rn(__fmul_rn(ld_half(p + 208), (float)(int8_t)p[192 + si]), (float)q);
+        } else if (type == CN_TYPE_F16) {
+            v = ld_half(row + 2 * i);
+        } else {
+            v = reinterpret_cast<const float*>(row)[i];
+        }
+        out[i] = v;
+    }
+}
+
+// ---- argmax: first index of the maximum (strict > in the scan) ---------------------
+
+__global__ void argmax_kernel(const float* __restrict__ logits, int n, int* __restrict__ out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const float* l = logits + (size_t)blockIdx.x * n;
+    float bv = -FLT_MAX;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float v = l[i];
+        if (v > bv || (v == bv && i < bi)) {
+            bv = v;
+            bi = i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (lane == 0) {
+        sv[w] = bv;
+        si[w] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < (int)(blockDim.x >> 5); k++)
+            if (sv[k] > bv || (sv[k] == bv && si[k] < bi)) {
+                bv = sv[k];
+                bi = si[k];
+            }
+        out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+    }
+}
+
+// ---- launchers -----------------------------------------------------------------------
+
+static int grid_1d(int64_t n, int threads, int cap) {
+    int64_t g = (n + threads - 1) / threads;
+    if (g < 1) g = 1;
+    if (g > cap) g = cap;
+    return (int)g;
+}
+
+int launch_rmsnorm(const float* x, const float* w, float* y, int n, int rows, float eps,
+                   cudaStream_t s) {
+    rmsnorm_kernel<<<rows, 256, 0, s>>>(x, w, y, n, eps);
+    CN_CUDA(cudaGetLastError());
+    return CN_OK;
+}
+
+int launch_rope_kv(const RopeKvArgs& a, cudaStream_t s) {
+    const int total = (a.n_heads + a.n_kv) * (a.hd / 2) + a.n_kv * a.hd;
+    dim3 grid(grid_1d(total, 256, 64), a.batch);
+    rope_kv_kernel<<<grid, 256, 0, s>>>(a.q, a.k, a.v, a.rope, a.pos_dev, a.pos_host, a.n_heads,
+                                        a.n_kv, a.hd, a.q_stride, a.kv_stride, a.kcache, a.vcache,
+                                        a.cache_seq_stride, a.cache_layer_off, a.kv_f16, a.ctx_len,
+                                        a.err);
+    CN_CUDA(cudaGetLastError());
+    return CN_OK;
+}
+
+int attention_plan(int n_heads, int n_kv, int hd, int max_seq, int batch, int sms, AttnPlan* p) {
+    CN_CHECK(n_kv > 0 && n_heads % n_kv == 0, CN_ERR_INVALID_ARG, "n_heads %% n_kv_heads != 0");
+    CN_CHECK(n_heads / n_kv <= kMaxKvMul, CN_ERR_UNSUPPORTED, "kv_mul > %d", kMaxKvMul);
+    CN_CHECK(hd <= kMaxHd && hd % 2 == 0, CN_ERR_UNSUPPORTED, "head_dim %d", hd);
+    // enough CTAs for ~2 waves, chunks of at least 32 positions
+    int want = (2 * sms + batch * n_kv - 1) / (batch * n_kv);
+    int chunk = (max_seq + want - 1) / want;
+    if (chunk < 32) chunk = 32;
+    if (chunk > 256) chunk = 256;
+    chunk = (chunk + 31) / 32 * 32;
+    p->chunk = chunk;
+    p->splits = (max_seq + chunk - 1) / chunk;
+    p->part_floats = (size_t)batch * n_heads * p->splits * (hd + 2);
+    p->smem = (size_t)((n_heads / n_kv) * (hd + chunk) + 32) * sizeof(float);
+    return CN_OK;
+}
+
+int attention_prepare(const AttnPlan& p) {
+    CN_CUDA(cudaFuncSetAttribute(attn_split_kernel<__half>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+    CN_CUDA(cudaFuncSetAttribute(attn_split_kernel<float>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+    return CN_OK;
+}
+
+int launch_attention(const AttnArgs& a, const AttnPlan& p, cudaStream_t s) {
+    dim3 grid(p.splits, a.n_kv, a.batch);
+    const float scale = 1.0f / sqrtf((float)a.hd);
+    if (a.kv_f16) {
+        auto k = attn_split_kernel<__half>;
+        k<<<grid, kAttnThreads, p.smem, s>>>(a.q, (const __half*)a.kcache, (const __half*)a.vcache,
+                                             a.pos_dev, a.pos_host, a.n_heads, a.n_kv, a.hd, a.q_stride,
+                                             a.cache_seq_stride, a.cache_layer_off, a.ctx_len, p.splits, p.chunk,
+                                             scale, a.part);
+    } else {
+        auto k = attn_split_kernel<float>;
+        k<<<grid, kAttnThreads, p.smem, s>>>(a.q, (const float*)a.kcache, (const float*)a.vcache,
+                                             a.pos_dev, a.pos_host, a.n_heads, a.n_kv, a.hd, a.q_stride,
+                                             a.cache_seq_stride, a.cache_layer_off, a.ctx_len, p.splits, p.chunk,
+                                             scale, a.part);
+    }
+    CN_CUDA(cudaGetLastError());
+    attn_combine_kernel<<<dim3(a.n_heads, a.batch), 128, 0, s>>>(a.part, a.n_heads, a.hd, p.splits,
+                                                                 a.out, a.out_stride);
+    CN_CUDA(cudaGetLastError());
+    return CN_OK;
+}
+
+int launch_silu_mul(float* gate, const float* up, int64_t n, cudaStream_t s) {
+    silu_mul_kernel<<<grid_1d(n, 256, 148 * 8), 256, 0, s>>>(gate, up, n);
+    CN_CUDA(cudaGetLastError());
+    return CN_OK;
+}
+
+int launch_add(float* a, const float* b, int64_t n, cudaStream_t s) {
+    add_kernel<<<grid_1d(n, 256, 148 * 8), 256, 0, s>>>(a, b, n);
+    CN_CUDA(cudaGetLastError());
+    return CN_OK;
+}
+
+int launch_embed(int type, const void* emb, uint64_t row_bytes, const int* tokens, int vocab,
+                 int dim, int batch, float* x, uint32_t* err, cudaStream_t s) {
+    embed_kernel<<<dim3(grid_1d(dim, 256, 32), batch), 256, 0, s>>>(
+        type, (const uint8_t*)emb, row_bytes, tokens, vocab, dim, x, err);
+    CN_CUDA(cudaGetLastError());
+    return CN_OK;
+}
+
+int launch_argmax(const float* logits, int n, int batch, int* out, cudaStream_t s) {
+    argmax_kernel<<<batch, 1024, 0, s>>>(logits, n, out);
+    CN_CUDA(cudaGetLastError());
+    return CN_OK;
+}
+
+}  // namespace cn

@@ -1,0 +1,57 @@
+// ops.h -- launchers of the decode-step kernels (ops.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace cn {
+
+struct RopeKvArgs {
+    float* q;             // [batch][q_stride], rotated in place
+    const float* k;       // [batch][kv_stride]
+    const float* v;       // [batch][kv_stride]
+    const float2* rope;   // [ctx][hd/2] (cos, sin)
+    const int* pos_dev;   // [batch] positions on the device, or null
+    int pos_host;         // used when pos_dev is null
+    int batch, n_heads, n_kv, hd, q_stride, kv_stride;
+    void* kcache;         // [batch][layers][ctx][n_kv*hd], fp32 or fp16
+    void* vcache;
+    int64_t cache_seq_stride;  // elements between sequences
+    int64_t cache_layer_off;   // elements to this layer
+    int kv_f16, ctx_len;
+    uint32_t* err;
+};
+
+struct AttnPlan {
+    int splits = 0, chunk = 0;
+    size_t part_floats = 0, smem = 0;
+};
+
+struct AttnArgs {
+    const float* q;  // [batch][q_stride] (rotated)
+    const void* kcache;
+    const void* vcache;
+    const int* pos_dev;
+    int pos_host;
+    int batch, n_heads, n_kv, hd, q_stride;
+    int64_t cache_seq_stride, cache_layer_off;
+    int kv_f16, ctx_len;
+    float* part;     // scratch: AttnPlan::part_floats
+    float* out;      // [batch][out_stride]
+    int out_stride;
+};
+
+int launch_rmsnorm(const float* x, const float* w, float* y, int n, int rows, float eps,
+                   cudaStream_t s);
+int launch_rope_kv(const RopeKvArgs& a, cudaStream_t s);
+int attention_plan(int n_heads, int n_kv, int hd, int max_seq, int batch, int sms, AttnPlan* p);
+// Sets the kernels' shared-memory limit for plan p (call before any capture).
+int attention_prepare(const AttnPlan& p);
+int launch_attention(const AttnArgs& a, const AttnPlan& p, cudaStream_t s);
+int launch_silu_mul(float* gate, const float* up, int64_t n, cudaStream_t s);
+int launch_add(float* a, const float* b, int64_t n, cudaStream_t s);
+int launch_embed(int type, const void* emb, uint64_t row_bytes, const int* tokens, int vocab,
+                 int dim, int batch, float* x, uint32_t* err, cudaStream_t s);
+int launch_argmax(const float* logits, int n, int batch, int* out, cudaStream_t s);
+
+}  // namespace cn

@@ -95,15 +95,17 @@ CN_HD void put64(uint8_t* p, uint64_t v) {
     for (int i = 0; i < 8; i++) p[i] = (uint8_t)(v >> (8 * i));
 }
 
-// Q4_0 block b (18 bytes): d = fp16(|N| * 0.02/8), nibbles U[0,15].
-// Draws 5b..5b+4.
+// Little-endian fp16 bits at a 2-byte aligned address, written as one
+// 16-bit store.
+CN_HD void put16(uint8_t* p, uint16_t v) { *reinterpret_cast<uint16_t*>(p) = v; }
+
+// Q4_0 block b (18 bytes, `out` 2-byte aligned): d = fp16(|N| * 0.02/8),
+// nibbles U[0,15].  Draws 5b..5b+4.
 CN_HD void q4_0_block(uint64_t seed, uint64_t b, uint8_t* out) {
     uint64_t base = 5 * b;
     float n = normal(seed, base);
     float d = fmul(n < 0.f ? -n : n, 0.0025f);
-    uint16_t h = f2h(d);
-    out[0] = (uint8_t)h;
-    out[1] = (uint8_t)(h >> 8);
+    put16(out, f2h(d));
     put64(out + 2, draw(seed, base + 3));
     put64(out + 10, draw(seed, base + 4));
 }
@@ -117,10 +119,8 @@ CN_HD void q4_k_block(uint64_t seed, uint64_t b, uint8_t* out) {
     float n0 = normal(seed, base), n1 = normal(seed, base + 3);
     uint16_t d = f2h(fmul(n0 < 0.f ? -n0 : n0, 0.01f));
     uint16_t dmin = f2h(fmul(n1 < 0.f ? -n1 : n1, 0.01f));
-    out[0] = (uint8_t)d;
-    out[1] = (uint8_t)(d >> 8);
-    out[2] = (uint8_t)dmin;
-    out[3] = (uint8_t)(dmin >> 8);
+    put16(out, d);
+    put16(out + 2, dmin);
     uint64_t rs = draw(seed, base + 6), rm = draw(seed, base + 7);
     uint8_t sc[8], m[8];
     for (int j = 0; j < 8; j++) {
@@ -147,9 +147,7 @@ CN_HD void q6_k_block(uint64_t seed, uint64_t b, uint8_t* out) {
         out[200 + j] = (uint8_t)((s1 >> (8 * j)) & 63);
     }
     float n = normal(seed, base + 26);
-    uint16_t d = f2h(fmul(n < 0.f ? -n : n, 0.01f));
-    out[208] = (uint8_t)d;
-    out[209] = (uint8_t)(d >> 8);
+    put16(out + 208, f2h(fmul(n < 0.f ? -n : n, 0.01f)));
 }
 
 // Element i of an F32 / F16 tensor.

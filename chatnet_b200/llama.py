@@ -1,0 +1,147 @@
+"""Model-level host side: CudaLlamaModel mirrors ChatNet's IModel for Llama.
+
+    IModel.Forward(ReadOnlySpan<int> tokenIds, int position, Span<float> logits)
+        (Abstractions/IModel.cs:18, Models/Llama/LlamaModel.cs:93-238)
+    -> CudaLlamaModel.forward(token_ids, position, logits)
+
+Weights are uploaded once (byte-identical GGUF blocks) and the KV cache and
+scratch live on the device; each call crosses the host/device boundary only
+for the token ids in and the logits out.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import _native as N
+from ._native import check
+
+LAYER_TENSORS = ("attn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "ffn_norm",
+                 "ffn_gate", "ffn_up", "ffn_down")
+
+
+@dataclass
+class LlamaConfig:
+    """Hyper-parameters, as LlamaConfig (Models/Llama/LlamaConfig.cs:23-39)."""
+    dim: int
+    hidden_dim: int
+    n_layers: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    vocab: int
+    ctx_len: int
+    rope_base: float = 10000.0
+    rms_eps: float = 1e-5
+    kv_f16: bool = False
+    max_batch: int = 1
+
+    @property
+    def kv_dim(self) -> int:
+        return self.n_kv_heads * self.head_dim
+
+    @property
+    def kv_mul(self) -> int:
+        return self.n_heads // self.n_kv_heads
+
+    def to_c(self) -> N.LlamaConfigC:
+        return N.LlamaConfigC(self.dim, self.hidden_dim, self.n_layers, self.n_heads,
+                              self.n_kv_heads, self.head_dim, self.vocab, self.ctx_len,
+                              self.rope_base, self.rms_eps, N.KV_F16 if self.kv_f16 else N.KV_F32,
+                              self.max_batch)
+
+
+def tensor_names(n_layers: int) -> list[str]:
+    """GGUF tensor names in cn_llama_create order (LlamaWeights.cs:78-145)."""
+    names = ["token_embd.weight", "output.weight", "output_norm.weight"]
+    for l in range(n_layers):
+        names += [f"blk.{l}.{t}.weight" for t in LAYER_TENSORS]
+    return names
+
+
+def tensor_shape(cfg: LlamaConfig, name: str) -> tuple[int, int]:
+    """[rows, cols] of a tensor (rows = output dim)."""
+    if name in ("token_embd.weight", "output.weight"):
+        return cfg.vocab, cfg.dim
+    if name.endswith("norm.weight"):
+        return 1, cfg.dim
+    kind = name.split(".")[2]
+    return {"attn_q": (cfg.dim, cfg.dim), "attn_k": (cfg.kv_dim, cfg.dim),
+            "attn_v": (cfg.kv_dim, cfg.dim), "attn_output": (cfg.dim, cfg.dim),
+            "ffn_gate": (cfg.hidden_dim, cfg.dim), "ffn_up": (cfg.hidden_dim, cfg.dim),
+            "ffn_down": (cfg.dim, cfg.hidden_dim)}[kind]
+
+
+class CudaLlamaModel:
+    """IModel for Llama on one B200 (cn_llama_*)."""
+
+    def __init__(self, ctx, cfg: LlamaConfig, tensors: list):
+        self.ctx, self.cfg = ctx, cfg
+        self._tensors = list(tensors)  # keep the borrowed weights alive
+        arr = (C.c_void_p * len(tensors))(*[t.handle for t in tensors])
+        h = C.c_void_p()
+        c = cfg.to_c()
+        check(N.lib().cn_llama_create(ctx.handle, C.byref(c), arr, len(tensors), C.byref(h)),
+              "cn_llama_create")
+        self.handle = h.value
+
+    # IModel.Forward
+    def forward(self, token_ids, position: int, logits: np.ndarray | None = None) -> np.ndarray:
+        ids = np.ascontiguousarray(token_ids, dtype=np.int32)
+        if logits is None:
+            logits = np.empty(self.cfg.vocab, dtype=np.float32)
+        assert logits.dtype == np.float32 and logits.size >= self.cfg.vocab
+        check(N.lib().cn_llama_forward(self.handle, ids.ctypes.data_as(C.POINTER(C.c_int)), ids.size,
+                                       position, logits.ctypes.data_as(C.POINTER(C.c_float))),
+              "cn_llama_forward")
+        return logits
+
+    def decode(self, tokens, positions, logits: bool = True, argmax: bool = True):
+        """One batched decode step: sequence b (KV slot b) at positions[b]."""
+        tok = np.ascontiguousarray(tokens, dtype=np.int32)
+        pos = np.ascontiguousarray(positions, dtype=np.int32)
+        B = tok.size
+        lg = np.empty((B, self.cfg.vocab), dtype=np.float32) if logits else None
+        am = np.empty(B, dtype=np.int32) if argmax else None
+        check(N.lib().cn_llama_decode(
+            self.handle, tok.ctypes.data_as(C.POINTER(C.c_int)), pos.ctypes.data_as(C.POINTER(C.c_int)),
+            B, lg.ctypes.data_as(C.POINTER(C.c_float)) if lg is not None else None,
+            am.ctypes.data_as(C.POINTER(C.c_int)) if am is not None else None), "cn_llama_decode")
+        return lg, am
+
+    def kv_synth(self, seq: int, npos: int, seed_k: int, seed_v: int) -> None:
+        check(N.lib().cn_llama_kv_synth(self.handle, seq, npos, seed_k, seed_v), "cn_llama_kv_synth")
+
+    def kv_read(self, seq: int, layer: int, pos0: int, npos: int):
+        dt = np.float16 if self.cfg.kv_f16 else np.float32
+        k = np.empty((npos, self.cfg.kv_dim), dt)
+        v = np.empty((npos, self.cfg.kv_dim), dt)
+        check(N.lib().cn_llama_kv_read(self.handle, seq, layer, pos0, npos, k.ctypes.data,
+                                       v.ctypes.data), "cn_llama_kv_read")
+        return k, v
+
+    def kv_write(self, seq: int, layer: int, pos0: int, k: np.ndarray, v: np.ndarray) -> None:
+        dt = np.float16 if self.cfg.kv_f16 else np.float32
+        k = np.ascontiguousarray(k, dt)
+        v = np.ascontiguousarray(v, dt)
+        check(N.lib().cn_llama_kv_write(self.handle, seq, layer, pos0, k.shape[0], k.ctypes.data,
+                                        v.ctypes.data), "cn_llama_kv_write")
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            N.lib().cn_llama_destroy(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -150,6 +150,68 @@ int cn_dequantize_dev(int type, const void* d_blocks, float* d_out, int64_t n_el
 int cn_matvec_dev(cn_ctx* ctx, int type, const void* d_w, int out_dim, int in_dim,
                   const float* d_x, float* d_y, int batch);
 
+/* ---- model level: one Llama decoder resident on the device ------------- */
+
+typedef struct cn_llama cn_llama;
+
+#define CN_KV_F32 0 /* fp32 KV cache, as LlamaModel allocates (LlamaModel.cs:60-61) */
+#define CN_KV_F16 1 /* fp16 KV cache (rounded to nearest on store)                  */
+
+/* Hyper-parameters; mirrors LlamaConfig (Models/Llama/LlamaConfig.cs:23-39). */
+typedef struct {
+    int dim, hidden_dim, n_layers, n_heads, n_kv_heads, head_dim, vocab, ctx_len;
+    float rope_base, rms_eps;
+    int kv_dtype;  /* CN_KV_F32 or CN_KV_F16 */
+    int max_batch; /* sequences decoded together, 1..32; each owns a KV slot */
+} cn_llama_config;
+
+/* Number of tensors cn_llama_create takes for n_layers layers. */
+#define CN_LLAMA_TENSORS(n_layers) (3 + 9 * (n_layers))
+
+/* Builds the model from uploaded tensors (borrowed: they must outlive the
+ * model), in the order LlamaWeights.ResolveAll resolves them
+ * (Models/Llama/LlamaWeights.cs:78-145):
+ *   [0] token_embd [rows=vocab, cols=dim]
+ *   [1] output     [vocab, dim]  (pass token_embd again when the file has no
+ *                                 output.weight, LlamaWeights.cs:89-98)
+ *   [2] output_norm F32 [1, dim]
+ *   then for each layer l, at 3 + 9*l:
+ *   attn_norm F32 [1, dim], attn_q [dim, dim], attn_k [kv, dim],
+ *   attn_v [kv, dim], attn_output [dim, dim], ffn_norm F32 [1, dim],
+ *   ffn_gate [hidden, dim], ffn_up [hidden, dim], ffn_down [dim, hidden]
+ * Allocates the KV cache ([max_batch][layers][ctx][kv] zero-filled, like
+ * LlamaModel.cs:60-61) and all scratch.  Replaces the LlamaModel
+ * constructor (LlamaModel.cs:48-88). */
+int cn_llama_create(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* const* tensors,
+                    int n_tensors, cn_llama** out);
+int cn_llama_destroy(cn_llama* m);
+
+/* IModel.Forward (Abstractions/IModel.cs:18, LlamaModel.cs:93-238): runs the
+ * n tokens of KV slot 0 at positions pos..pos+n-1, one at a time, and writes
+ * the logits of the last one to logits_host [vocab]. */
+int cn_llama_forward(cn_llama* m, const int* tokens, int n, int pos, float* logits_host);
+
+/* One decode step for `batch` sequences: sequence b (KV slot b) reads token
+ * tokens[b] at position pos[b].  logits_host [batch][vocab] and argmax_host
+ * [batch] (GreedySampler.Sample, Samplers/GreedySampler.cs:13-26) may each
+ * be NULL.  The step runs as a CUDA graph captured on the first call for
+ * each batch size, so that first call must not happen during a stream
+ * capture. */
+int cn_llama_decode(cn_llama* m, const int* tokens, const int* pos, int batch, float* logits_host,
+                    int* argmax_host);
+
+/* KV cache access for seeding and checking (no reference counterpart; the
+ * reference fills its cache only through Forward).  Element type follows
+ * cfg.kv_dtype (float or uint16 fp16 bits), layout [npos][n_kv*head_dim]. */
+int cn_llama_kv_write(cn_llama* m, int seq, int layer, int pos0, int npos, const void* k_host,
+                      const void* v_host);
+int cn_llama_kv_read(cn_llama* m, int seq, int layer, int pos0, int npos, void* k_host,
+                     void* v_host);
+/* Fills positions [0, npos) of every layer of KV slot `seq` with the seeded
+ * N(0,1) generator (element index (layer*ctx + pos)*kv + d, as
+ * cn_synth_fill lays out a [layers*ctx, kv] tensor) and zeroes the rest. */
+int cn_llama_kv_synth(cn_llama* m, int seq, int npos, uint64_t seed_k, uint64_t seed_v);
+
 #ifdef __cplusplus
 }
 #endif

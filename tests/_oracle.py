@@ -91,3 +91,34 @@ def load() -> Oracle:
         fn.restype = res
         fn.argtypes = args
     return Oracle(lib)
+
+
+def llama_config(cfg) -> LlamaConfig:
+    """Oracle config struct from chatnet_b200.llama.LlamaConfig."""
+    return LlamaConfig(cfg.dim, cfg.hidden_dim, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads,
+                       cfg.head_dim, cfg.vocab, cfg.ctx_len, cfg.rope_base, cfg.rms_eps,
+                       1 if cfg.kv_f16 else 0)
+
+
+class OracleLlama:
+    """One sequence of the oracle Llama: weights (host bytes) + its own KV cache."""
+
+    def __init__(self, oracle: Oracle, cfg, host: dict, types: list[int], names: list[str],
+                 kcache: np.ndarray, vcache: np.ndarray):
+        self.o, self.cfg = oracle, llama_config(cfg)
+        self.arrays = [np.ascontiguousarray(host[n]) for n in names]
+        self.ptrs = (C.c_void_p * len(names))(*[a.ctypes.data for a in self.arrays])
+        self.types = (C.c_int * len(names))(*types)
+        self.k = np.ascontiguousarray(kcache)
+        self.v = np.ascontiguousarray(vcache)
+        self.vocab = cfg.vocab
+
+    def forward(self, tokens, pos: int, nthreads: int = 0) -> np.ndarray:
+        tok = np.ascontiguousarray(tokens, dtype=np.int32)
+        logits = np.empty(self.vocab, dtype=np.float32)
+        rc = self.o.lib.or_llama_forward(C.byref(self.cfg), self.ptrs, self.types,
+                                         self.k.ctypes.data, self.v.ctypes.data,
+                                         tok.ctypes.data_as(C.POINTER(C.c_int)), tok.size, pos,
+                                         fp(logits), nthreads)
+        assert rc == 0, rc
+        return logits

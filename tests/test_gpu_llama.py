@@ -1,0 +1,195 @@
+"""Model-level parity: the CUDA decode step (cn_llama_*) against the oracle's
+restatement of LlamaModel.Forward on the same seeded weights, KV cache and
+tokens.  Logits: max relative error 1e-3 (normalised by max |logit|);
+greedy argmax must match."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import chatnet_b200 as cn
+from chatnet_b200 import configs as cf
+from chatnet_b200.llama import CudaLlamaModel, tensor_names
+from tests import _oracle
+from tests.parity import REL_TOL, rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def small_dc(weight_type=cn.TYPE_Q4_0, kv_f16=False, n_layers=2, max_batch=1, ctx_len=64):
+    dc = cf.with_layers(cf.CONFIGS[1], n_layers, max_batch)
+    m = cf.replace(dc.model, dim=256, hidden_dim=512, n_heads=4, n_kv_heads=2, head_dim=64,
+                   vocab=500, ctx_len=ctx_len, kv_f16=kv_f16)
+    return cf.replace(dc, model=m, weight_type=weight_type, kv_filled=10, decode_pos=12)
+
+
+class Pair:
+    """A GPU model and per-sequence oracles built from the same host bytes."""
+
+    def __init__(self, ctx, oracle, dc, host=None, seqs=1, tie_output=False):
+        self.dc = dc
+        self.host = host if host is not None else cf.host_tensors(dc)
+        if tie_output:
+            self.host["output.weight"] = self.host["token_embd.weight"]
+        self.names = tensor_names(dc.model.n_layers)
+        self.types = [cf.tensor_type(dc, n) for n in self.names]
+        self.tensors = cf.device_tensors(ctx, dc, self.host)
+        if tie_output:
+            self.tensors[1] = self.tensors[0]
+        self.gpu = CudaLlamaModel(ctx, dc.model, self.tensors)
+        self.oracles = []
+        for s in range(seqs):
+            k, v = cf.host_kv(dc, s)
+            self.gpu.kv_synth(s, dc.kv_filled, *cf.kv_seeds(dc, s))
+            self.oracles.append(_oracle.OracleLlama(oracle, dc.model, self.host, self.types,
+                                                    self.names, k.copy(), v.copy()))
+
+    def close(self):
+        self.gpu.close()
+        for t in self.tensors:
+            t.free()
+
+
+def test_kv_synth_matches_host(ctx, oracle):
+    for f16 in (False, True):
+        dc = small_dc(kv_f16=f16)
+        p = Pair(ctx, oracle, dc)
+        k, v = p.gpu.kv_read(0, 1, 0, dc.model.ctx_len)
+        hk, hv = cf.host_kv(dc, 0)
+        L, C = dc.model.n_layers, dc.model.ctx_len
+        np.testing.assert_array_equal(k, hk.reshape(L, C, -1)[1])
+        np.testing.assert_array_equal(v, hv.reshape(L, C, -1)[1])
+        p.close()
+
+
+@pytest.mark.parametrize("wtype", [cn.TYPE_Q4_0, cn.TYPE_Q4_K])
+@pytest.mark.parametrize("kv_f16", [False, True])
+def test_small_model_decode_parity(ctx, oracle, wtype, kv_f16):
+    dc = small_dc(wtype, kv_f16)
+    p = Pair(ctx, oracle, dc)
+    tok = cf.token(dc, 0)
+    got = p.gpu.forward([tok], dc.decode_pos)
+    ref = p.oracles[0].forward([tok], dc.decode_pos)
+    assert rel_err(got, ref) <= REL_TOL
+    assert int(np.argmax(got)) == int(np.argmax(ref))
+    # the new K/V rows landed in the cache like the oracle's
+    kd = dc.model.kv_dim
+    for layer in range(dc.model.n_layers):
+        k, v = p.gpu.kv_read(0, layer, dc.decode_pos, 1)
+        ok = p.oracles[0].k.reshape(dc.model.n_layers, dc.model.ctx_len, kd)[layer, dc.decode_pos]
+        ov = p.oracles[0].v.reshape(dc.model.n_layers, dc.model.ctx_len, kd)[layer, dc.decode_pos]
+        assert rel_err(k.astype(np.float32)[0], ok.astype(np.float32)) <= REL_TOL
+        assert rel_err(v.astype(np.float32)[0], ov.astype(np.float32)) <= REL_TOL
+    p.close()
+
+
+def test_multi_token_forward_from_zero(ctx, oracle):
+    """IModel.Forward with several tokens from position 0 (the engine's prompt path)."""
+    dc = cf.replace(small_dc(), kv_filled=0)
+    p = Pair(ctx, oracle, dc)
+    toks = [cf.token(dc, 0, s) for s in range(6)]
+    got = p.gpu.forward(toks, 0)
+    ref = p.oracles[0].forward(toks, 0)
+    assert rel_err(got, ref) <= REL_TOL
+    p.close()
+
+
+def test_tied_output_and_last_position(ctx, oracle):
+    """lm_head tied to token_embd (LlamaWeights.cs:89-98); decode at ctx_len-1."""
+    dc = cf.replace(small_dc(), kv_filled=63, decode_pos=63)
+    p = Pair(ctx, oracle, dc, tie_output=True)
+    tok = cf.token(dc, 0)
+    got = p.gpu.forward([tok], 63)
+    ref = p.oracles[0].forward([tok], 63)
+    assert rel_err(got, ref) <= REL_TOL
+    p.close()
+
+
+def test_batched_decode_matches_sequences(ctx, oracle):
+    B = 5
+    dc = small_dc(cn.TYPE_Q4_K, True, max_batch=B)
+    p = Pair(ctx, oracle, dc, seqs=B)
+    toks = [cf.token(dc, s) for s in range(B)]
+    pos = [12, 13, 14, 12, 40]
+    lg, am = p.gpu.decode(toks, pos)
+    for s in range(B):
+        ref = p.oracles[s].forward([toks[s]], pos[s])
+        assert rel_err(lg[s], ref) <= REL_TOL, s
+        assert am[s] == int(np.argmax(lg[s]))
+    p.close()
+
+
+def test_decode_rejects_bad_input(ctx, oracle):
+    dc = small_dc()
+    p = Pair(ctx, oracle, dc)
+    with pytest.raises(ValueError):
+        p.gpu.decode([dc.model.vocab], [0])
+    with pytest.raises(ValueError):
+        p.gpu.decode([0], [dc.model.ctx_len])
+    with pytest.raises(ValueError):
+        p.gpu.decode([0, 1], [0, 0])  # batch above max_batch
+    p.gpu.forward([1], 0)  # still usable afterwards
+    p.close()
+
+
+def test_create_validates_tensors(ctx):
+    dc = small_dc()
+    host = cf.host_tensors(dc)
+    ts = cf.device_tensors(ctx, dc, host)
+    with pytest.raises(ValueError):
+        CudaLlamaModel(ctx, dc.model, ts[:-1])  # wrong count
+    bad = list(ts)
+    bad[4], bad[5] = bad[5], bad[4]  # attn_q <-> attn_k: shape mismatch
+    with pytest.raises(ValueError):
+        CudaLlamaModel(ctx, dc.model, bad)
+    for t in ts:
+        t.free()
+
+
+@pytest.fixture(scope="module")
+def tiny_full(ctx, oracle):
+    """Config 1 at full size: 22 layers, TinyLlama shapes, Q4_0, fp32 KV."""
+    dc = cf.CONFIGS[1]
+    p = Pair(ctx, oracle, dc)
+    yield p
+    p.close()
+
+
+def test_config1_decode_step(tiny_full):
+    p, dc = tiny_full, tiny_full.dc
+    tok = cf.token(dc, 0)
+    got = p.gpu.forward([tok], dc.decode_pos)
+    ref = p.oracles[0].forward([tok], dc.decode_pos)
+    err = rel_err(got, ref)
+    top2 = np.sort(ref)[-2:]
+    print(f"config1 logits rel err {err:.2e}, top-1/top-2 margin {top2[1] - top2[0]:.4f}")
+    assert err <= REL_TOL
+    assert int(np.argmax(got)) == int(np.argmax(ref))
+
+
+def test_config1_greedy_32_steps(tiny_full):
+    """The greedy token matches the oracle for 32 decode steps."""
+    p, dc = tiny_full, tiny_full.dc
+    o = p.oracles[0]
+    tok_g = tok_o = cf.token(dc, 0, 1)
+    pos = dc.decode_pos + 1  # after test_config1_decode_step wrote position 512
+    for step in range(32):
+        lg, am = p.gpu.decode([tok_g], [pos + step])
+        ref = o.forward([tok_o], pos + step)
+        assert rel_err(lg[0], ref) <= REL_TOL, step
+        tok_g, tok_o = int(am[0]), int(np.argmax(ref))
+        assert tok_g == tok_o, (step, tok_g, tok_o)
+
+
+def test_config4_two_layers_batched(ctx, oracle):
+    """Config 4 shapes (70B: d 8192, FFN 28672, 64/8 heads, Q4_K, fp16 KV at
+    2047) with 2 of its 80 layers, 2 sequences decoded together."""
+    dc = cf.with_layers(cf.CONFIGS[4], 2, max_batch=2)
+    p = Pair(ctx, oracle, dc, seqs=2)
+    toks = [cf.token(dc, s) for s in range(2)]
+    lg, am = p.gpu.decode(toks, [dc.decode_pos] * 2)
+    for s in range(2):
+        ref = p.oracles[s].forward([toks[s]], dc.decode_pos)
+        assert rel_err(lg[s], ref) <= REL_TOL
+        assert am[s] == int(np.argmax(ref))
+    p.close()

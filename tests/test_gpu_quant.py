@@ -138,3 +138,20 @@ def test_matvec_errors(ctx):
         ctx.upload(np.zeros(20, np.uint8), 3, 1, 32)   # Q4_1: not on this path
     with pytest.raises(ValueError):
         ctx.upload(np.zeros(17, np.uint8), cn.TYPE_Q4_0, 1, 32)  # wrong byte count
+
+
+@pytest.mark.parametrize("name", ["q4_0", "q4_k", "q6_k"])
+@pytest.mark.parametrize("magnitude", [1e-6, 1.0, 3e5])
+def test_matvec_activation_range(ctx, oracle, name, magnitude):
+    """Activations far outside fp16 range (either way) keep fp32-level accuracy:
+    the prep rescales each sequence by an exact power of two."""
+    t = Q[name]
+    rows, cols = 256, 2048
+    blocks = cn.synth_fill(t, rows, cols, seed=cn.synth_seed(2, f"range.{name}"))
+    W = ctx.upload(blocks, t, rows, cols)
+    x = _x(3, cols, f"range.x.{name}") * np.float32(magnitude)
+    x[1] *= np.float32(1e-3)   # sequences with very different scales in one batch
+    y = ctx.matvec(W, x)
+    ref = oracle.matvec(t, blocks, x, rows)
+    assert np.isfinite(y).all()
+    assert rel_err(y, ref) <= REL_TOL
