@@ -1,0 +1,342 @@
+#!/usr/bin/env python
+"""Decode benchmark: tokens/s of the Llama-2-70B-shaped Q4_K model (BASELINE.json
+config 4) on B200, through libchatnet_cuda.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--config 4|1]
+    python bench.py --impl reference ...     # the reference's CPU algorithm (oracle port)
+
+A step is one decode step of `batch` sequences (each at position 2047 of a
+2048-token fp16 KV cache filled with seeded N(0,1) values), all 80 layers
+plus lm_head and argmax.  Weights (38.5 GB of Q4_K blocks) and the KV cache
+are generated on the device from the seeded generator (synthetic data of
+the config's shapes and distributions).  Inputs are far larger than L2.
+
+Printed JSON line (rank 0):
+  value      tokens/s of the whole job with inputs resident in HBM
+             (CUDA-graph steps timed with CUDA events, max over ranks)
+  e2e        the same through cn_llama_decode with host buffers: token ids
+             and positions copied in, logits and argmax copied out per step
+  roofline   the dominant kernel (the fused Q4_K dequant-GEMV of the FFN
+             gate/up projections, 28672 x 8192) timed alone on the context
+             stream: algorithmic bytes per launch / mean launch time
+  cpu_baseline  the oracle port of the reference's C# CPU path timed on the
+             host's cores on a 2-layer sample, extrapolated to 80 layers
+With --gpus N > 1 every rank decodes its own replica (data-parallel
+replicas; tensor parallelism is not built), so `scaling` is weak.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tok/s"
+CPU_SAMPLE_LAYERS = 2
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--config", type=int, default=4, choices=(1, 4))
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# clocks: nvidia-smi sampled during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peak_gbs() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return 6650.0, "fallback"
+
+
+def committed_traffic(kernel_key: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get(kernel_key)
+        except ValueError:
+            return None
+    return None
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle port of the reference's C# path
+# ---------------------------------------------------------------------------
+class CpuSample:
+    """The oracle port of the reference's CPU path on a CPU_SAMPLE_LAYERS-layer
+    sample of the model (same seeded tensors as the device copy), timed per
+    token and extrapolated to the full depth (every layer costs the same)."""
+
+    def __init__(self, dc_full, batch: int):
+        import ctypes as C
+        from chatnet_b200 import configs as cf
+        from chatnet_b200.llama import tensor_names
+        from tests import _oracle
+        self.C, self._o = C, _oracle
+        self.full, self.batch = dc_full, batch
+        self.orc = _oracle.load()
+        dc = cf.with_layers(dc_full, CPU_SAMPLE_LAYERS)
+        self.dc = dc
+        host = cf.host_tensors(dc)
+        names = tensor_names(CPU_SAMPLE_LAYERS)
+        types = [cf.tensor_type(dc, n) for n in names]
+        k, v = cf.host_kv(dc, 0)
+        self.ol = _oracle.OracleLlama(self.orc, dc.model, host, types, names, k, v)
+        self.x0 = self.orc.dequantize(types[0], host["token_embd.weight"][cf.token(dc, 0)],
+                                      dc.model.dim)
+        self.logits = np.empty(dc.model.vocab, np.float32)
+
+    def run_once(self) -> float:
+        """Seconds for one step of `batch` sequences (extrapolated)."""
+        C, fp, ol, orc = self.C, self._o.fp, self.ol, self.orc
+        x = self.x0.copy()
+        t0 = time.perf_counter()
+        rc = orc.lib.or_llama_layers(C.byref(ol.cfg), ol.ptrs, ol.types, ol.k.ctypes.data,
+                                     ol.v.ctypes.data, fp(x), self.dc.decode_pos, 0,
+                                     CPU_SAMPLE_LAYERS, 0)
+        t1 = time.perf_counter()
+        rc |= orc.lib.or_llama_head(C.byref(ol.cfg), ol.ptrs, ol.types, fp(x), fp(self.logits), 0)
+        t2 = time.perf_counter()
+        assert rc == 0
+        per_token = (t1 - t0) * self.full.model.n_layers / CPU_SAMPLE_LAYERS + (t2 - t1)
+        return self.batch * per_token  # B independent forwards on the CPU path
+
+    def describe(self, reps: int) -> str:
+        return (f"{CPU_SAMPLE_LAYERS} of {self.full.model.n_layers} layers + lm_head per token "
+                f"({self.dc.model.dim}-dim, position {self.dc.decode_pos}), x{self.batch} "
+                f"sequences, median of {reps} runs, extrapolated linearly in layers")
+
+
+# ---------------------------------------------------------------------------
+def main():
+    a = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    from chatnet_b200 import configs as cf
+    dc = cf.with_batch(cf.CONFIGS[a.config], a.batch)
+    workload = {"workload": dc.name, "config_id": a.config, "batch": a.batch,
+                "n_layers": dc.model.n_layers, "dim": dc.model.dim, "ffn": dc.model.hidden_dim,
+                "heads": f"{dc.model.n_heads}/{dc.model.n_kv_heads}", "head_dim": dc.model.head_dim,
+                "vocab": dc.model.vocab, "ctx": dc.model.ctx_len, "position": dc.decode_pos,
+                "weights": "Q4_K" if a.config == 4 else "Q4_0",
+                "kv_cache": "fp16" if dc.model.kv_f16 else "fp32",
+                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "l2": "inputs larger than L2 (weights 38.5 GB)" if a.config == 4 else
+                      "inputs larger than L2 (weights 0.58 GB)"}
+
+    if a.impl == "reference":
+        if rank != 0:
+            return 0
+        cs = CpuSample(dc, a.batch)
+        times = []
+        for i in range(a.warmup + a.steps):
+            t = cs.run_once()
+            if i >= a.warmup:
+                times.append(t)
+        sample = cs.describe(a.steps)
+        per_step = statistics.median(times)
+        val = a.batch / per_step
+        line = {"metric": METRIC, "value": val, "unit": "tok/s", "n_gpus": 0, "steps": a.steps,
+                "warmup": a.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "impl": "reference", "config": workload,
+                "cpu_baseline": {"value": val, "unit": "tok/s", "cores": os.cpu_count(),
+                                 "kind": "port", "sample": sample},
+                "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    import torch
+    import chatnet_b200 as cn
+    from chatnet_b200.llama import CudaLlamaModel
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+
+    ctx = cn.Context(local)
+    ext = torch.cuda.ExternalStream(ctx.stream)
+    t0 = time.time()
+    tensors = cf.device_tensors(ctx, dc)  # seeded generator, on the device
+    model = CudaLlamaModel(ctx, dc.model, tensors)
+    B = a.batch
+    for b in range(B):
+        model.kv_synth(b, dc.kv_filled, *cf.kv_seeds(dc, b))
+    toks = [cf.token(dc, b) for b in range(B)]
+    pos = [dc.decode_pos] * B
+    model.set_inputs(toks, pos)
+    setup_s = time.time() - t0
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ctx.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # warm-up (captures the graph on the first step)
+    for _ in range(max(a.warmup, 3)):
+        model.step(B)
+    ctx.synchronize()
+
+    # timed region: device-resident steps
+    barrier()
+    clk = ClockSampler(local)
+    clk.start()
+    time.sleep(0.3)  # let the sampler start before the timed region
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ext)
+    for _ in range(a.steps):
+        model.step(B)
+    e1.record(ext)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / a.steps
+    clocks = clk.stop()
+    ctx.synchronize()
+    ms = max_over_ranks(ms)
+    value = world * B * 1000.0 / ms
+
+    # end to end through cn_llama_decode (host buffers)
+    barrier()
+    e0.record(ext)
+    for _ in range(a.steps):
+        lg, am = model.decode(toks, pos, logits=True, argmax=True)
+    e1.record(ext)
+    e1.synchronize()
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1) / a.steps)
+    e2e = world * B * 1000.0 / ms_e2e
+    assert np.isfinite(lg).all()
+
+    # roofline: the dominant kernel timed alone (FFN gate projection)
+    us, nbytes = model.time_gemv(4, B, iters=2 * dc.model.n_layers)
+    peak, peak_kind = measured_peak_gbs()
+    achieved = nbytes / (us * 1e-6) / 1e9
+    shape = f"{dc.model.hidden_dim}x{dc.model.dim}"
+    traffic = committed_traffic(f"gemv_{'q4_k' if a.config == 4 else 'q4_0'}_{shape}_b{B}")
+    kernels = model.step_kernels(B)
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cs = CpuSample(dc, B)
+        per_step_s = statistics.median([cs.run_once() for _ in range(3)])
+        cpu = {"value": B / per_step_s, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": cs.describe(3)}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": ("q4_k" if a.config == 4 else "q4_0") + " x fp16(hi+lo) -> f32",
+            "data": "synthetic (seeded generator, config shapes and distributions)",
+            "config": workload,
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": B * 8,
+                    "d2h_bytes_per_step": B * (dc.model.vocab * 4 + 4)},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "kernel": f"gemv_kernel<Q4_K> {shape} batch {B}",
+                         "us_per_launch": us, "bytes_per_launch": nbytes,
+                         "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
+            "cpu_baseline": cpu,
+            "gpu_launches": kernels * a.steps,
+            "clocks": clocks,
+            "setup_s": setup_s,
+        }
+        print(json.dumps(line), flush=True)
+
+    model.close()
+    for t in tensors:
+        t.free()
+    ctx.close()
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

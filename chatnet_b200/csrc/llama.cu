@@ -455,6 +455,101 @@ int cn_llama_decode(cn_llama* m, const int* tokens, const int* pos, int batch, f
     return CN_OK;
 }
 
+int cn_llama_set_inputs(cn_llama* m, const int* tokens, const int* pos, int batch) {
+    CN_CHECK(m && tokens && pos, CN_ERR_INVALID_ARG, "null argument");
+    CN_CHECK(batch >= 1 && batch <= m->cfg.max_batch, CN_ERR_INVALID_ARG,
+             "batch %d outside [1, %d]", batch, m->cfg.max_batch);
+    for (int b = 0; b < batch; b++) {
+        CN_CHECK(tokens[b] >= 0 && tokens[b] < m->cfg.vocab, CN_ERR_INVALID_ARG,
+                 "token id %d outside [0, %d)", tokens[b], m->cfg.vocab);
+        CN_CHECK(pos[b] >= 0 && pos[b] < m->cfg.ctx_len, CN_ERR_INVALID_ARG,
+                 "position %d outside [0, %d)", pos[b], m->cfg.ctx_len);
+    }
+    cudaSetDevice(m->ctx->device);
+    CN_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    CN_CUDA(cudaMemcpy(m->tokens, tokens, batch * 4, cudaMemcpyHostToDevice));
+    CN_CUDA(cudaMemcpy(m->pos, pos, batch * 4, cudaMemcpyHostToDevice));
+    return CN_OK;
+}
+
+int cn_llama_step(cn_llama* m, int batch) {
+    CN_CHECK(m, CN_ERR_INVALID_ARG, "null model");
+    CN_CHECK(batch >= 1 && batch <= m->cfg.max_batch, CN_ERR_INVALID_ARG,
+             "batch %d outside [1, %d]", batch, m->cfg.max_batch);
+    cudaSetDevice(m->ctx->device);
+    return run_step(m, batch);
+}
+
+int cn_llama_step_kernels(cn_llama* m, int batch, int* out_count) {
+    CN_CHECK(m && out_count, CN_ERR_INVALID_ARG, "null argument");
+    CN_CHECK(batch >= 1 && batch <= m->cfg.max_batch, CN_ERR_INVALID_ARG, "bad batch");
+    cudaSetDevice(m->ctx->device);
+    int rc = build_step(m, batch);
+    if (rc) return rc;
+    cudaStream_t s = m->ctx->stream;
+    cudaGraph_t g = nullptr;
+    CN_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    rc = enqueue_step(m, batch, s);
+    cudaError_t e = cudaStreamEndCapture(s, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return cuda_error(e, "cudaStreamEndCapture");
+    size_t n = 0;
+    e = cudaGraphGetNodes(g, nullptr, &n);
+    std::vector<cudaGraphNode_t> nodes(n);
+    if (e == cudaSuccess && n) e = cudaGraphGetNodes(g, nodes.data(), &n);
+    int kernels = 0;
+    for (size_t i = 0; e == cudaSuccess && i < n; i++) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(nodes[i], &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) kernels++;
+    }
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return cuda_error(e, "cudaGraphGetNodes");
+    *out_count = kernels;
+    return CN_OK;
+}
+
+int cn_llama_time_gemv(cn_llama* m, int proj, int batch, int iters, float* us_per_launch,
+                       double* bytes_per_launch) {
+    CN_CHECK(m && us_per_launch && bytes_per_launch, CN_ERR_INVALID_ARG, "null argument");
+    CN_CHECK(proj >= 0 && proj <= 7 && iters >= 1, CN_ERR_INVALID_ARG, "bad proj/iters");
+    CN_CHECK(batch >= 1 && batch <= m->cfg.max_batch, CN_ERR_INVALID_ARG, "bad batch");
+    cudaSetDevice(m->ctx->device);
+    int rc = build_step(m, batch);
+    if (rc) return rc;
+    Step& st = m->steps[batch];
+    const int L = m->cfg.n_layers;
+    auto op_of = [&](int i) -> const GemvOp& {
+        return proj == 7 ? st.ops[(size_t)L * 7] : st.ops[(size_t)(i % L) * 7 + proj];
+    };
+    const GemvOp& op0 = op_of(0);
+    const float* x = (proj == 3) ? m->att : (proj == 6) ? m->gate : m->xn;
+    float* y = (proj == 0 || proj == 3 || proj == 6) ? m->tmp
+               : (proj == 1) ? m->k : (proj == 2) ? m->v : (proj == 7) ? m->logits : m->up;
+    cudaStream_t s = m->ctx->stream;
+    if ((rc = gemv_prep(s, m->ctx->sms, op0, x, m->gb))) return rc;
+    // warm-up, then timed launches cycling through the layers (cold L2)
+    for (int i = 0; i < 3; i++)
+        if ((rc = gemv_run(m->ctx, s, op_of(i), x, m->gb, y))) return rc;
+    cudaEvent_t e0, e1;
+    CN_CUDA(cudaEventCreate(&e0));
+    CN_CUDA(cudaEventCreate(&e1));
+    CN_CUDA(cudaEventRecord(e0, s));
+    for (int i = 0; i < iters; i++)
+        if ((rc = gemv_run(m->ctx, s, op_of(i + 3), x, m->gb, y))) return rc;
+    CN_CUDA(cudaEventRecord(e1, s));
+    CN_CUDA(cudaEventSynchronize(e1));
+    float ms = 0.f;
+    CN_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    *us_per_launch = ms * 1000.f / iters;
+    *bytes_per_launch = (double)op0.rb * op0.rows + 4.0 * batch * (op0.rows + op0.cols);
+    return check_dev_err_reset(m);
+}
+
 int cn_llama_forward(cn_llama* m, const int* tokens, int n, int pos, float* logits_host) {
     CN_CHECK(m && tokens && logits_host, CN_ERR_INVALID_ARG, "null argument");
     CN_CHECK(n >= 1, CN_ERR_INVALID_ARG, "no tokens");

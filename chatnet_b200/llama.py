@@ -111,6 +111,28 @@ class CudaLlamaModel:
             am.ctypes.data_as(C.POINTER(C.c_int)) if am is not None else None), "cn_llama_decode")
         return lg, am
 
+    def set_inputs(self, tokens, positions) -> None:
+        tok = np.ascontiguousarray(tokens, dtype=np.int32)
+        pos = np.ascontiguousarray(positions, dtype=np.int32)
+        check(N.lib().cn_llama_set_inputs(self.handle, tok.ctypes.data_as(C.POINTER(C.c_int)),
+                                          pos.ctypes.data_as(C.POINTER(C.c_int)), tok.size),
+              "cn_llama_set_inputs")
+
+    def step(self, batch: int) -> None:
+        """Enqueue one decode step on the device inputs (no host copies, no wait)."""
+        check(N.lib().cn_llama_step(self.handle, batch), "cn_llama_step")
+
+    def step_kernels(self, batch: int) -> int:
+        n = C.c_int(0)
+        check(N.lib().cn_llama_step_kernels(self.handle, batch, C.byref(n)), "cn_llama_step_kernels")
+        return n.value
+
+    def time_gemv(self, proj: int, batch: int, iters: int) -> tuple[float, float]:
+        us, nb = C.c_float(0), C.c_double(0)
+        check(N.lib().cn_llama_time_gemv(self.handle, proj, batch, iters, C.byref(us), C.byref(nb)),
+              "cn_llama_time_gemv")
+        return us.value, nb.value
+
     def kv_synth(self, seq: int, npos: int, seed_k: int, seed_v: int) -> None:
         check(N.lib().cn_llama_kv_synth(self.handle, seq, npos, seed_k, seed_v), "cn_llama_kv_synth")
 

@@ -200,6 +200,25 @@ int cn_llama_forward(cn_llama* m, const int* tokens, int n, int pos, float* logi
 int cn_llama_decode(cn_llama* m, const int* tokens, const int* pos, int batch, float* logits_host,
                     int* argmax_host);
 
+/* Sets the step inputs (token ids and positions of `batch` sequences) in
+ * device memory, then cn_llama_step enqueues one decode step on the
+ * context's stream without any host copy or wait; the logits and argmax stay
+ * on the device.  Together they split cn_llama_decode for callers that keep
+ * the loop on the device (benchmarks, device-side sampling).  The first
+ * cn_llama_step of each batch size captures the CUDA graph. */
+int cn_llama_set_inputs(cn_llama* m, const int* tokens, const int* pos, int batch);
+int cn_llama_step(cn_llama* m, int batch);
+/* Kernel launches one decode step makes for `batch` (nodes of its graph). */
+int cn_llama_step_kernels(cn_llama* m, int batch, int* out_count);
+/* Times one projection's fused dequant-GEMV as the step runs it (activation
+ * prep excluded): `iters` launches cycling through the layers' matrices of
+ * projection `proj` (0..6 = q,k,v,o,gate,up,down; 7 = lm_head), with CUDA
+ * events on the context's stream.  Reports the mean time per launch and
+ * the launch's algorithmic bytes (weights + x + y).  (no reference
+ * counterpart: roofline measurement) */
+int cn_llama_time_gemv(cn_llama* m, int proj, int batch, int iters, float* us_per_launch,
+                       double* bytes_per_launch);
+
 /* KV cache access for seeding and checking (no reference counterpart; the
  * reference fills its cache only through Forward).  Element type follows
  * cfg.kv_dtype (float or uint16 fp16 bits), layout [npos][n_kv*head_dim]. */
