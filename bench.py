@@ -54,6 +54,9 @@ def parse():
     ap.add_argument("--config", type=int, default=4, choices=(1, 4))
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--nvtx-step", action="store_true",
+                    help="after warm-up run one step inside the NVTX range 'timed_step' and exit "
+                         "(for ncu --nvtx --nvtx-include timed_step/ launch lists)")
     return ap.parse_args()
 
 
@@ -263,6 +266,15 @@ def main():
     for _ in range(max(a.warmup, 3)):
         model.step(B)
     ctx.synchronize()
+
+    if a.nvtx_step:
+        ctx.synchronize()
+        torch.cuda.nvtx.range_push("timed_step")
+        model.step(B)
+        ctx.synchronize()
+        torch.cuda.nvtx.range_pop()
+        print(json.dumps({"nvtx_step": True, "kernels": model.step_kernels(B)}), flush=True)
+        return 0
 
     # timed region: device-resident steps
     barrier()

@@ -24,6 +24,7 @@ struct cn_ctx {
     int* counters = nullptr;
     size_t counter_count = 0;
     float* xinv = nullptr;
+    size_t xinv_bytes = 0;
 
     // staging for the host-pointer entry points
     void* dstage = nullptr;
@@ -63,7 +64,7 @@ struct GemvPlan {
     int units = 0;    // 256-position k units
     int ctas = 0;
     bool tma = false;
-    size_t xfrag_bytes = 0, xsum_bytes = 0, partial_bytes = 0, counters = 0;
+    size_t xfrag_bytes = 0, xsum_bytes = 0, xinv_bytes = 0, partial_bytes = 0, counters = 0;
 };
 int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool tma,
               GemvPlan* plan);
@@ -87,11 +88,11 @@ struct GemvBufs {
     float* xsum;
     float* partials;
     int* counters;
-    float* xinv;  // [32] per-batch 2^-e written by the prep
+    float* xinv;  // [units][nt*4] per-unit 2^-e written by the prep
 };
 
 struct GemvNeeds {
-    size_t xfrag_bytes = 0, xsum_bytes = 0, partial_bytes = 0, counters = 0;
+    size_t xfrag_bytes = 0, xsum_bytes = 0, xinv_bytes = 0, partial_bytes = 0, counters = 0;
 };
 
 int gemv_make(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols,
@@ -102,6 +103,10 @@ int gemv_prep(cudaStream_t st, int sms, const GemvOp& op, const float* d_x, cons
 int gemv_run(cn_ctx* ctx, cudaStream_t st, const GemvOp& op, const float* d_x, const GemvBufs& b,
              float* d_y);
 int gemv_reserve(const GemvPlan& p, GemvNeeds* n);
+// RMSNorm of `rows` rows of n values into y, and, when op is a tiled GEMV,
+// its activation fragments for op in b (one kernel).
+int norm_prep(cudaStream_t st, const float* x, const float* w, float* y, int n, int rows,
+              float eps, const GemvOp* op, const GemvBufs& b);
 float gemv_step1_scale(int type);
 
 // Enqueues x-prep + GEMV on ctx->stream using the ctx's scratch.  `map` may

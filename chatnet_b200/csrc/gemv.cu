@@ -66,7 +66,10 @@ struct Geo {
     static constexpr int kW = Fmt<TYPE>::kBox * kTileRows;             // raw blocks
     static constexpr int kXF = 8 * NT * 32 * 16;                        // B fragments
     static constexpr int kXS = TYPE == CN_TYPE_Q4_K ? 8 * NT * 4 * 4 : 0;  // chunk sums
-    static constexpr int kStage = kW + kXF + kXS;                       // multiple of 128
+    static constexpr int kXI = NT * 4 * 4;                              // unit 2^-e per column
+    static constexpr int kXIpad = (kXI + 127) / 128 * 128;
+    static constexpr int kBytes = kW + kXF + kXS + kXI;                 // bytes landing per stage
+    static constexpr int kStage = kW + kXF + kXS + kXIpad;              // multiple of 128
     static constexpr int kTable = TYPE == CN_TYPE_Q4_K ? kCons * 16 * 8 * 8 : 0;
     static constexpr int kFixed = kTable + 64 * 16;                     // table + barriers
     // Two CTAs per SM when three or more stages fit in half the SM's shared
@@ -87,7 +90,7 @@ struct GemvArgs {
     int batch;
     const uint4* xfrag;  // [chunk][nt][32 lanes]
     const float* xsum;   // [chunk][nt*4]
-    const float* xinv;   // [nt*4] 2^-e of each batch column's prep scaling
+    const float* xinv;   // [unit][nt*4] 2^-e of each unit's activation scaling
     float* y;            // [batch][rows]
     float* partials;     // [2 * ctas][128 rows][nt*4] stream-K partial slots
     int* counters;       // [tiles * kCons]
@@ -366,9 +369,8 @@ __device__ void finish_subtile(const GemvArgs& a, int tile, int warp, int cta, i
         for (int nt = 0; nt < NT; nt++) {
             int b = nt * 4 + t;
             if (b < a.batch) {
-                const float inv = a.xinv[b];
-                if (r0 < a.rows) a.y[(size_t)b * a.rows + r0] = (acc[nt][0] + acc[nt][1]) * inv;
-                if (r1 < a.rows) a.y[(size_t)b * a.rows + r1] = (acc[nt][2] + acc[nt][3]) * inv;
+                if (r0 < a.rows) a.y[(size_t)b * a.rows + r0] = acc[nt][0] + acc[nt][1];
+                if (r1 < a.rows) a.y[(size_t)b * a.rows + r1] = acc[nt][2] + acc[nt][3];
             }
         }
         return;
@@ -398,7 +400,7 @@ __device__ void finish_subtile(const GemvArgs& a, int tile, int warp, int cta, i
         for (int c = c_first; c <= c_last; c++) s += __ldcg(slot_base(c) + e);
         int row = e / BW, b = e % BW;
         int64_t r = (int64_t)tile * kTileRows + warp * 16 + row;
-        if (b < a.batch && r < a.rows) a.y[(size_t)b * a.rows + r] = s * a.xinv[b];
+        if (b < a.batch && r < a.rows) a.y[(size_t)b * a.rows + r] = s;
     }
     if (lane == 0) atomicExch(ctr, 0);
 }
@@ -461,11 +463,12 @@ __global__ void __launch_bounds__(kThreads, Geo<TYPE, NT>::kMinCtas)
                 return;
             }
             uint8_t* st = stages + s * G::kStage;
-            mbar_expect_tx(&full[s], G::kStage);
+            mbar_expect_tx(&full[s], G::kBytes);
             tma_load_2d(st, &map, Fmt<TYPE>::box_x(u), tile * kTileRows, &full[s]);
             bulk_g2s(st + G::kW, a.xfrag + (size_t)u * 8 * NT * 32, G::kXF, &full[s]);
             if constexpr (G::kXS > 0)
                 bulk_g2s(st + G::kW + G::kXF, a.xsum + (size_t)u * 8 * NT * 4, G::kXS, &full[s]);
+            bulk_g2s(st + G::kW + G::kXF + G::kXS, a.xinv + (size_t)u * NT * 4, G::kXI, &full[s]);
             if (++u == a.units) {
                 u = 0;
                 tile++;
@@ -499,14 +502,25 @@ __global__ void __launch_bounds__(kThreads, Geo<TYPE, NT>::kMinCtas)
         }
         const uint8_t* st = stages + s * G::kStage;
         const uint4* xf = reinterpret_cast<const uint4*>(st + G::kW);
+        float au[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) au[nt][0] = au[nt][1] = au[nt][2] = au[nt][3] = 0.f;
         if constexpr (TYPE == CN_TYPE_Q4_0) {
-            unit_q4_0<NT>(st, xf, warp * 16, g, t, lane, live, acc);
+            unit_q4_0<NT>(st, xf, warp * 16, g, t, lane, live, au);
         } else if constexpr (TYPE == CN_TYPE_Q4_K) {
             const float* xs = reinterpret_cast<const float*>(st + G::kW + G::kXF);
-            unit_q4_k<NT>(st, xf, xs, table + warp * 128, warp * 16, g, t, lane, live, acc);
+            unit_q4_k<NT>(st, xf, xs, table + warp * 128, warp * 16, g, t, lane, live, au);
         } else {
-            if (u & 1) unit_q6_k<NT, 2>(st, xf, u, warp * 16, g, t, lane, live, acc);
-            else unit_q6_k<NT, 0>(st, xf, u, warp * 16, g, t, lane, live, acc);
+            if (u & 1) unit_q6_k<NT, 2>(st, xf, u, warp * 16, g, t, lane, live, au);
+            else unit_q6_k<NT, 0>(st, xf, u, warp * 16, g, t, lane, live, au);
+        }
+        // undo the unit's activation scaling (exact power of two per column)
+        const float* xi = reinterpret_cast<const float*>(st + G::kW + G::kXF + G::kXS);
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            const float inv = xi[nt * 4 + t];
+            fma2(acc[nt][0], acc[nt][1], au[nt][0], au[nt][1], inv);
+            fma2(acc[nt][2], acc[nt][3], au[nt][2], au[nt][3], inv);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
@@ -528,84 +542,130 @@ __global__ void __launch_bounds__(kThreads, Geo<TYPE, NT>::kMinCtas)
 
 // ---- activation prep ----------------------------------------------------------
 //
-// One CTA per batch column b of the n-tiles (4 * nt_count CTAs):
-//  * picks a power of two 2^e so that max|x[b]| * 2^e lies in [2^14, 2^15)
-//    (exact scaling; keeps the fp16 hi/lo split far from overflow and from
-//    subnormals whatever the activation range) and stores 2^-e in xinv[b];
-//  * writes its lanes of xfrag[c][nt][lane]: the four B-fragment registers
-//    lane (g, t) feeds the two k-steps of chunk c, where column g = hi (g
-//    even) or lo (g odd) part of batch b = 4*nt + g/2, positions 4t+{0,2},
-//    4t+{1,3} of each 16-position half (the second half multiplied by
-//    step1_scale: 1/16 for Q4_K, else 1);
-//  * writes xsum[c][b] = fp32 sum of the scaled x[b] over chunk c.
-// Columns b >= batch are written as zeros.
-constexpr int kPrepThreads = 1024;
+// The GEMVs read x as fp16 fragments.  Each 256-position unit u of each batch
+// row b is scaled by its own power of two 2^e (max |x| over the unit lands in
+// [2^14, 2^15)), which is exact and keeps the fp16 hi + lo split far from
+// overflow and from subnormals whatever the activation range; the GEMV
+// multiplies the unit's partial sums by xinv[u][b] = 2^-e.  Being unit-local,
+// the conversion needs no reduction over the whole vector, so any kernel
+// holding whole units can emit it (the standalone prep and the fused
+// RMSNorm below).
+//
+// Layouts (nt_count n-tiles of 4 batch columns):
+//   xfrag[c][nt][lane]: the four B-fragment registers lane (g, t) feeds the
+//     two k-steps of chunk c; column g = hi (g even) or lo (g odd) part of
+//     batch b = 4*nt + g/2; positions 4t+{0,2}, 4t+{1,3} of each 16-position
+//     half, the second half multiplied by step1 (1/16 for Q4_K, else 1);
+//   xsum[c][b]: fp32 sum of the scaled x over chunk c (Q4_K's dmin term);
+//   xinv[u][b]: 2^-e.
+// Columns of batch rows >= batch are never read back, so they are not written.
 
-__global__ void __launch_bounds__(kPrepThreads)
-    xprep_kernel(const float* __restrict__ x, int K, int batch, int nt_count, float step1_scale,
-                 uint4* __restrict__ xfrag, float* __restrict__ xsum, float* __restrict__ xinv) {
+// One warp emits unit u of row b.  Lane (c = lane/4, t = lane%4) holds in
+// v[0..3] positions 32c + 4t + 0..3 and in v[4..7] positions 32c + 16 + 4t + 0..3.
+__device__ __forceinline__ void emit_unit(const float (&v)[8], int u, int b, int nt_count,
+                                          float step1, uint4* __restrict__ xfrag,
+                                          float* __restrict__ xsum, float* __restrict__ xinv,
+                                          int lane) {
+    float am = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) am = fmaxf(am, fabsf(v[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    int e = 0;
+    if (am > 0.f && am < INFINITY) e = 14 - ilogbf(am);
+    e = e < -120 ? -120 : (e > 120 ? 120 : e);
+    const float sc = ldexpf(1.0f, e), s1 = sc * step1;
+    const int c = lane >> 2, t = lane & 3;
+    const int nt = b >> 2, gh = 2 * (b & 3);
+    float e8[8] = {v[0] * sc, v[2] * sc, v[1] * sc, v[3] * sc,
+                   v[4] * s1, v[6] * s1, v[5] * s1, v[7] * s1};
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        __half2 h = __floats2half2_rn(e8[2 * k], e8[2 * k + 1]);
+        float2 back = __half22float2(h);
+        __half2 l = __floats2half2_rn(e8[2 * k] - back.x, e8[2 * k + 1] - back.y);
+        hi[k] = *reinterpret_cast<uint32_t*>(&h);
+        lo[k] = *reinterpret_cast<uint32_t*>(&l);
+    }
+    uint4* dst = xfrag + ((size_t)(8 * u + c) * nt_count + nt) * 32;
+    dst[4 * gh + t] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    dst[4 * (gh + 1) + t] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    if (xsum) {
+        float ps = ((v[0] * sc + v[1] * sc) + (v[2] * sc + v[3] * sc)) +
+                   ((v[4] * sc + v[5] * sc) + (v[6] * sc + v[7] * sc));
+        ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+        if (t == 0) xsum[(size_t)(8 * u + c) * nt_count * 4 + b] = ps;
+    }
+    if (lane == 0) xinv[(size_t)u * nt_count * 4 + b] = ldexpf(1.0f, -e);
+}
+
+// Standalone prep: one warp per (unit, batch row).
+__global__ void xprep_kernel(const float* __restrict__ x, int K, int batch, int nt_count,
+                             float step1, uint4* __restrict__ xfrag, float* __restrict__ xsum,
+                             float* __restrict__ xinv) {
+    const int lane = threadIdx.x & 31;
+    const int units = K / 256;
+    const int64_t items = (int64_t)units * batch;
+    const int64_t w0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t it = w0; it < items; it += nw) {
+        const int u = (int)(it % units), b = (int)(it / units);
+        const float* p = x + (size_t)b * K + (size_t)u * 256 + (lane >> 2) * 32 + 4 * (lane & 3);
+        float4 a0 = *reinterpret_cast<const float4*>(p);
+        float4 a1 = *reinterpret_cast<const float4*>(p + 16);
+        const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        emit_unit(v, u, b, nt_count, step1, xfrag, xsum, xinv, lane);
+    }
+}
+
+// RMSNorm (TensorMath.RmsNorm, Tensors/TensorMath.cs:97-165) fused with the
+// prep of its output: one CTA per batch row.  y = x * (1 / sqrt(sum(x^2)/n +
+// eps)) * w, elementwise in the reference's order; y is also stored in fp32.
+constexpr int kNormThreads = 1024;
+
+__global__ void __launch_bounds__(kNormThreads)
+    norm_prep_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ y,
+                     int n, float eps, int emit, int nt_count, float step1,
+                     uint4* __restrict__ xfrag, float* __restrict__ xsum, float* __restrict__ xinv) {
     __shared__ float red[32];
     const int b = blockIdx.x;
-    const int chunks = K / 32;
-    const int nt = b >> 2, gh = 2 * (b & 3);  // hi lane group gh, lo lane group gh + 1
-    if (b >= batch) {
-        for (int i = threadIdx.x; i < chunks * 4; i += blockDim.x) {
-            int c = i >> 2, t = i & 3;
-            xfrag[((size_t)c * nt_count + nt) * 32 + 4 * gh + t] = make_uint4(0, 0, 0, 0);
-            xfrag[((size_t)c * nt_count + nt) * 32 + 4 * (gh + 1) + t] = make_uint4(0, 0, 0, 0);
-        }
-        if (xsum)
-            for (int c = threadIdx.x; c < chunks; c += blockDim.x) xsum[(size_t)c * nt_count * 4 + b] = 0.f;
+    const float* xr = x + (size_t)b * n;
+    float* yr = y + (size_t)b * n;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    ss = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) ss += red[i];
+    const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+    if (!emit) {
+        for (int i = threadIdx.x; i < n; i += blockDim.x)
+            yr[i] = __fmul_rn(__fmul_rn(xr[i], rms), w[i]);
         return;
     }
-    const float* xr = x + (size_t)b * K;
-    float amax = 0.f;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) amax = fmaxf(amax, fabsf(xr[i]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
-    __syncthreads();
-    amax = 0.f;
-    for (int i = 0; i < (int)(blockDim.x >> 5); i++) amax = fmaxf(amax, red[i]);
-    int e = 0;
-    if (amax > 0.f && amax < INFINITY) e = 14 - ilogbf(amax);
-    e = e < -120 ? -120 : (e > 120 ? 120 : e);
-    const float sc = ldexpf(1.0f, e);
-    if (threadIdx.x == 0) xinv[b] = ldexpf(1.0f, -e);
-    // chunks*4 is a multiple of 4 and blockDim a multiple of 32, so the four
-    // items of a chunk sit in adjacent lanes of one warp (for the xsum shuffle)
-    const int items = chunks * 4;
-    for (int i0 = 0; i0 < items; i0 += blockDim.x) {
-        const int i = i0 + threadIdx.x;
-        const bool on = i < items;
-        const int c = i >> 2, t = i & 3;
-        const float* p = xr + (size_t)(on ? c : 0) * 32 + 4 * t;
-        float4 v0 = *reinterpret_cast<const float4*>(p);
-        float4 v1 = *reinterpret_cast<const float4*>(p + 16);
-        if (xsum) {
-            // fp32 sum of the scaled chunk: 8 values here, 32 across the 4 lanes
-            float ps = (((v0.x * sc + v0.y * sc) + (v0.z * sc + v0.w * sc)) +
-                        ((v1.x * sc + v1.y * sc) + (v1.z * sc + v1.w * sc)));
-            ps += __shfl_xor_sync(0xffffffffu, ps, 1);
-            ps += __shfl_xor_sync(0xffffffffu, ps, 2);
-            if (on && t == 0) xsum[(size_t)c * nt_count * 4 + b] = ps;
-        }
-        if (!on) continue;
-        const float s1 = sc * step1_scale;
-        float e8[8] = {v0.x * sc, v0.z * sc, v0.y * sc, v0.w * sc,
-                       v1.x * s1, v1.z * s1, v1.y * s1, v1.w * s1};
-        uint32_t hi[4], lo[4];
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            __half2 h = __floats2half2_rn(e8[2 * k], e8[2 * k + 1]);
-            float2 back = __half22float2(h);
-            __half2 l = __floats2half2_rn(e8[2 * k] - back.x, e8[2 * k + 1] - back.y);
-            hi[k] = *reinterpret_cast<uint32_t*>(&h);
-            lo[k] = *reinterpret_cast<uint32_t*>(&l);
-        }
-        uint4* dst = xfrag + ((size_t)c * nt_count + nt) * 32;
-        dst[4 * gh + t] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        dst[4 * (gh + 1) + t] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
+    for (int u = warp; u < n / 256; u += nwarp) {
+        const int off = u * 256 + (lane >> 2) * 32 + 4 * (lane & 3);
+        float4 a0 = *reinterpret_cast<const float4*>(xr + off);
+        float4 a1 = *reinterpret_cast<const float4*>(xr + off + 16);
+        float4 w0 = *reinterpret_cast<const float4*>(w + off);
+        float4 w1 = *reinterpret_cast<const float4*>(w + off + 16);
+        float v[8];
+        v[0] = __fmul_rn(__fmul_rn(a0.x, rms), w0.x);
+        v[1] = __fmul_rn(__fmul_rn(a0.y, rms), w0.y);
+        v[2] = __fmul_rn(__fmul_rn(a0.z, rms), w0.z);
+        v[3] = __fmul_rn(__fmul_rn(a0.w, rms), w0.w);
+        v[4] = __fmul_rn(__fmul_rn(a1.x, rms), w1.x);
+        v[5] = __fmul_rn(__fmul_rn(a1.y, rms), w1.y);
+        v[6] = __fmul_rn(__fmul_rn(a1.z, rms), w1.z);
+        v[7] = __fmul_rn(__fmul_rn(a1.w, rms), w1.w);
+        *reinterpret_cast<float4*>(yr + off) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4*>(yr + off + 16) = make_float4(v[4], v[5], v[6], v[7]);
+        emit_unit(v, u, b, nt_count, step1, xfrag, xsum, xinv, lane);
     }
 }
 
@@ -788,6 +848,7 @@ int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool
     const int chunks = p->units * 8;
     p->xfrag_bytes = (size_t)chunks * p->nt * 32 * sizeof(uint4);
     p->xsum_bytes = type == CN_TYPE_Q4_K ? (size_t)chunks * p->nt * 4 * sizeof(float) : 0;
+    p->xinv_bytes = (size_t)p->units * p->nt * 4 * sizeof(float);
     p->partial_bytes = (size_t)2 * ctas * kTileRows * p->nt * 4 * sizeof(float);
     p->counters = (size_t)p->tiles * kCons;
     return CN_OK;
@@ -835,9 +896,23 @@ int gemv_prep(cudaStream_t st, int sms, const GemvOp& op, const float* d_x, cons
     if (!op.tma) return CN_OK;
     CN_CHECK((reinterpret_cast<uintptr_t>(d_x) & 15) == 0, CN_ERR_INVALID_ARG,
              "x must be 16-byte aligned");
-    xprep_kernel<<<op.plan.nt * 4, kPrepThreads, 0, st>>>(
-        d_x, (int)op.cols, op.batch, op.plan.nt, gemv_step1_scale(op.type), b.xfrag,
-        op.type == CN_TYPE_Q4_K ? b.xsum : nullptr, b.xinv);
+    const int64_t items = (int64_t)op.plan.units * op.batch;
+    int blocks = (int)((items + 7) / 8);
+    if (blocks > sms * 8) blocks = sms * 8;
+    xprep_kernel<<<blocks, 256, 0, st>>>(d_x, (int)op.cols, op.batch, op.plan.nt,
+                                         gemv_step1_scale(op.type), b.xfrag,
+                                         op.type == CN_TYPE_Q4_K ? b.xsum : nullptr, b.xinv);
+    CN_CUDA(cudaGetLastError());
+    return CN_OK;
+}
+
+int norm_prep(cudaStream_t st, const float* x, const float* w, float* y, int n, int rows,
+              float eps, const GemvOp* op, const GemvBufs& b) {
+    const bool emit = op && op->tma;
+    norm_prep_kernel<<<rows, kNormThreads, 0, st>>>(
+        x, w, y, n, eps, emit ? 1 : 0, emit ? op->plan.nt : 1,
+        emit ? gemv_step1_scale(op->type) : 1.0f, emit ? b.xfrag : nullptr,
+        emit && op->type == CN_TYPE_Q4_K ? b.xsum : nullptr, emit ? b.xinv : nullptr);
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }
@@ -887,6 +962,7 @@ int gemv_run(cn_ctx* ctx, cudaStream_t st, const GemvOp& op, const float* d_x, c
 
 int gemv_reserve(const GemvPlan& p, GemvNeeds* n) {
     size_t x = p.xfrag_bytes, s = p.xsum_bytes, pa = p.partial_bytes, c = p.counters;
+    if (p.xinv_bytes > n->xinv_bytes) n->xinv_bytes = p.xinv_bytes;
     if (x > n->xfrag_bytes) n->xfrag_bytes = x;
     if (s > n->xsum_bytes) n->xsum_bytes = s;
     if (pa > n->partial_bytes) n->partial_bytes = pa;
@@ -906,10 +982,7 @@ int gemv_launch(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t co
         rc = ensure(&ctx->xfrag, &ctx->xfrag_bytes, p.xfrag_bytes, false);
         if (!rc && p.xsum_bytes) rc = ensure((void**)&ctx->xsum, &ctx->xsum_bytes, p.xsum_bytes, false);
         if (!rc) rc = ensure((void**)&ctx->partials, &ctx->partial_bytes, p.partial_bytes, false);
-        if (!rc && !ctx->xinv) {
-            size_t have = 0;
-            rc = ensure((void**)&ctx->xinv, &have, 256, true);
-        }
+        if (!rc) rc = ensure((void**)&ctx->xinv, &ctx->xinv_bytes, p.xinv_bytes, false);
         if (!rc) {
             size_t cb = ctx->counter_count * sizeof(int);
             rc = ensure((void**)&ctx->counters, &cb, p.counters * sizeof(int), true);

@@ -113,30 +113,42 @@ static int build_step(cn_llama* m, int B) {
     return CN_OK;
 }
 
-// Tracks which activation vector the shared fragment buffer holds.
+// Tracks which activation vector (and in which form: Q4_K's pre-scaled
+// second k-step and chunk sums, or the plain one) the fragment buffer holds.
 struct PrepCache {
     const float* x = nullptr;
-    float scale = 0.f;
+    int kind = -1;
     int nt = 0;
     int64_t cols = 0;
+    void set(const float* x_, const GemvOp& op) {
+        x = x_;
+        kind = op.type == CN_TYPE_Q4_K;
+        nt = op.plan.nt;
+        cols = op.cols;
+    }
+    bool holds(const float* x_, const GemvOp& op) const {
+        return x == x_ && kind == (op.type == CN_TYPE_Q4_K) && nt == op.plan.nt && cols == op.cols;
+    }
 };
 
 static int gemv(cn_llama* m, cudaStream_t s, const GemvOp& op, const float* x, float* y,
                 PrepCache& pc) {
-    if (op.tma) {
-        float sc = gemv_step1_scale(op.type);
-        if (pc.x != x || pc.scale != sc || pc.nt != op.plan.nt || pc.cols != op.cols ||
-            op.type == CN_TYPE_Q4_K) {
-            // Q4_K also needs the chunk sums of x, written by the same prep
-            int rc = gemv_prep(s, m->ctx->sms, op, x, m->gb);
-            if (rc) return rc;
-            pc.x = x;
-            pc.scale = sc;
-            pc.nt = op.plan.nt;
-            pc.cols = op.cols;
-        }
+    if (op.tma && !pc.holds(x, op)) {
+        int rc = gemv_prep(s, m->ctx->sms, op, x, m->gb);
+        if (rc) return rc;
+        pc.set(x, op);
     }
     return gemv_run(m->ctx, s, op, x, m->gb, y);
+}
+
+// RMSNorm of x into xn, emitting the fragments of the GEMV that reads xn next.
+static int norm(cn_llama* m, cudaStream_t s, const cn_tensor* w, int B, const GemvOp& next,
+                PrepCache& pc) {
+    int rc = norm_prep(s, m->x, (const float*)w->d, m->xn, m->cfg.dim, B, m->cfg.rms_eps, &next, m->gb);
+    if (rc) return rc;
+    pc = PrepCache();
+    if (next.tma) pc.set(m->xn, next);
+    return CN_OK;
 }
 
 // Enqueues one decode step for B sequences (tokens/positions already in
@@ -152,9 +164,7 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
     PrepCache pc;
     for (int l = 0; l < c.n_layers; l++) {
         const GemvOp* ops = &st.ops[(size_t)l * 7];
-        rc = launch_rmsnorm(m->x, (const float*)LT(m, l, L_ANORM)->d, m->xn, dim, B, c.rms_eps, s);
-        if (rc) return rc;
-        pc = PrepCache();
+        if ((rc = norm(m, s, LT(m, l, L_ANORM), B, ops[0], pc))) return rc;
         if ((rc = gemv(m, s, ops[0], m->xn, m->q, pc))) return rc;
         if ((rc = gemv(m, s, ops[1], m->xn, m->k, pc))) return rc;
         if ((rc = gemv(m, s, ops[2], m->xn, m->v, pc))) return rc;
@@ -200,18 +210,16 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
         if ((rc = launch_attention(aa, st.ap, s))) return rc;
         if ((rc = gemv(m, s, ops[3], m->att, m->tmp, pc))) return rc;
         if ((rc = launch_add(m->x, m->tmp, (int64_t)B * dim, s))) return rc;
-        rc = launch_rmsnorm(m->x, (const float*)LT(m, l, L_FNORM)->d, m->xn, dim, B, c.rms_eps, s);
-        if (rc) return rc;
+        if ((rc = norm(m, s, LT(m, l, L_FNORM), B, ops[4], pc))) return rc;
         if ((rc = gemv(m, s, ops[4], m->xn, m->gate, pc))) return rc;
         if ((rc = gemv(m, s, ops[5], m->xn, m->up, pc))) return rc;
         if ((rc = launch_silu_mul(m->gate, m->up, (int64_t)B * hid, s))) return rc;
         if ((rc = gemv(m, s, ops[6], m->gate, m->tmp, pc))) return rc;
         if ((rc = launch_add(m->x, m->tmp, (int64_t)B * dim, s))) return rc;
     }
-    rc = launch_rmsnorm(m->x, (const float*)m->t[T_ONORM]->d, m->xn, dim, B, c.rms_eps, s);
-    if (rc) return rc;
-    pc = PrepCache();
-    if ((rc = gemv(m, s, st.ops[(size_t)c.n_layers * 7], m->xn, m->logits, pc))) return rc;
+    const GemvOp& head = st.ops[(size_t)c.n_layers * 7];
+    if ((rc = norm(m, s, m->t[T_ONORM], B, head, pc))) return rc;
+    if ((rc = gemv(m, s, head, m->xn, m->logits, pc))) return rc;
     return launch_argmax(m->logits, c.vocab, B, m->amax, s);
 }
 
@@ -405,7 +413,7 @@ int cn_llama_create(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* const* t
             (rc = dmalloc((void**)&m->gb.xsum, need.xsum_bytes, true)) ||
             (rc = dmalloc((void**)&m->gb.partials, need.partial_bytes, false)) ||
             (rc = dmalloc((void**)&m->gb.counters, need.counters * 4 + 256, true)) ||
-            (rc = dmalloc((void**)&m->gb.xinv, 256, true)))
+            (rc = dmalloc((void**)&m->gb.xinv, need.xinv_bytes, true)))
             return fail(rc);
         m->counter_bytes = need.counters * 4 + 256;
     }

@@ -137,16 +137,47 @@ __global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ 
 //   out = sum_s exp(m_s - M) o_s / sum_s exp(m_s - M) l_s.
 // This equals Softmax followed by the weighted V sum up to fp32 rounding.
 
-template <typename KV>
-__device__ __forceinline__ float kv_load(const KV* p);
-template <>
-__device__ __forceinline__ float kv_load<float>(const float* p) { return *p; }
-template <>
-__device__ __forceinline__ float kv_load<__half>(const __half* p) { return __half2float(*p); }
-
 constexpr int kAttnThreads = 256;
 constexpr int kMaxKvMul = 16;
 constexpr int kMaxHd = 256;
+
+// K/V element widths, loaded 16 bytes at a time.
+template <typename KV>
+struct KvVec;
+template <>
+struct KvVec<float> {
+    static constexpr int kPer16 = 4;
+    __device__ static void to_float(const uint4& v, float* out) {
+        out[0] = __uint_as_float(v.x);
+        out[1] = __uint_as_float(v.y);
+        out[2] = __uint_as_float(v.z);
+        out[3] = __uint_as_float(v.w);
+    }
+};
+template <>
+struct KvVec<__half> {
+    static constexpr int kPer16 = 8;
+    __device__ static void to_float(const uint4& v, float* out) {
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+            out[2 * i] = f.x;
+            out[2 * i + 1] = f.y;
+        }
+    }
+};
+
+// Shared-memory layout of one attention CTA (floats unless noted):
+//   qs   [kv_mul][hd + 4]        the kv_mul query heads (fp32), padded rows
+//   ks   [chunk][hd + pad] (KV)  K rows of the chunk, padded by 16 bytes
+//   vs   [chunk][hd] (KV)        V rows of the chunk
+//   sc   [kv_mul][chunk]         scores, then exp(score - max)
+//   red  [64]
+template <typename KV>
+__host__ __device__ constexpr int attn_krow(int hd) {
+    return hd + 16 / (int)sizeof(KV);  // elements per padded K row
+}
 
 template <typename KV>
 __global__ void __launch_bounds__(kAttnThreads)
@@ -155,87 +186,134 @@ __global__ void __launch_bounds__(kAttnThreads)
                       int n_heads, int n_kv, int hd, int q_stride, int64_t cache_seq_stride,
                       int64_t cache_layer_off, int ctx_len, int splits, int chunk, float scale,
                       float* __restrict__ part /* [b][head][split][hd + 2] */) {
-    extern __shared__ float sm[];
+    extern __shared__ __align__(16) float sm[];
     const int s = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
     const int kv_mul = n_heads / n_kv;
     int pos = pos_dev ? pos_dev[b] : pos_host;
     if (pos < 0 || pos >= ctx_len) pos = -1;  // rejected upstream; read nothing
     const int seq = pos + 1;
     const int p0 = s * chunk;
-    const int p1 = min(seq, p0 + chunk);
-    const int L = max(0, p1 - p0);
-    float* qs = sm;                          // [kv_mul][hd]
-    float* sc = qs + kv_mul * hd;            // [kv_mul][chunk]
-    float* red = sc + kv_mul * chunk;        // [32]
+    const int L = max(0, min(seq, p0 + chunk) - p0);
+    const int qrow = hd + 4;
+    const int krow = attn_krow<KV>(hd);
+    float* qs = sm;
+    KV* ks = reinterpret_cast<KV*>(qs + kv_mul * qrow);
+    KV* vs = ks + chunk * krow;
+    float* sc = reinterpret_cast<float*>(vs + chunk * hd);
+    float* red = sc + kv_mul * chunk;
+    const int tid = threadIdx.x;
     const int kvdim = n_kv * hd;
-    for (int i = threadIdx.x; i < kv_mul * hd; i += blockDim.x)
-        qs[i] = q[(size_t)b * q_stride + (kh * kv_mul) * hd + i];
-    __syncthreads();
+    const int lane = tid & 31, warp = tid >> 5, nwarp = blockDim.x >> 5;
+    float* pr_base = part + ((size_t)b * n_heads + kh * kv_mul) * splits * (hd + 2);
+
+    if (L == 0) {  // nothing of this split is inside 0..pos
+        for (int e = tid; e < kv_mul * (hd + 2); e += blockDim.x) {
+            const int g = e / (hd + 2), d = e % (hd + 2);
+            pr_base[((size_t)g * splits + s) * (hd + 2) + d] = d == hd ? -FLT_MAX : 0.f;
+        }
+        return;
+    }
+    // stage q (fp32) and the K / V rows of the chunk (16-byte loads)
+    for (int i = tid; i < kv_mul * hd; i += blockDim.x)
+        qs[(i / hd) * qrow + i % hd] = q[(size_t)b * q_stride + (kh * kv_mul) * hd + i];
+    constexpr int P16 = KvVec<KV>::kPer16;
+    const int vec_per_row = hd / P16;
     const KV* kbase = kcache + (int64_t)b * cache_seq_stride + cache_layer_off + kh * hd;
     const KV* vbase = vcache + (int64_t)b * cache_seq_stride + cache_layer_off + kh * hd;
-    // scores: thread per position, all kv_mul heads
-    for (int i = threadIdx.x; i < L; i += blockDim.x) {
-        const KV* kr = kbase + (int64_t)(p0 + i) * kvdim;
-        float acc[kMaxKvMul];
-#pragma unroll
-        for (int g = 0; g < kMaxKvMul; g++) acc[g] = 0.f;
-        for (int d = 0; d < hd; d++) {
-            float kv = kv_load<KV>(kr + d);
-#pragma unroll
-            for (int g = 0; g < kMaxKvMul; g++)
-                if (g < kv_mul) acc[g] = fmaf(qs[g * hd + d], kv, acc[g]);
-        }
-#pragma unroll
-        for (int g = 0; g < kMaxKvMul; g++)
-            if (g < kv_mul) sc[g * chunk + i] = __fmul_rn(acc[g], scale);
+    for (int i = tid; i < L * vec_per_row; i += blockDim.x) {
+        const int r = i / vec_per_row, c = i % vec_per_row;
+        const int64_t g = (int64_t)(p0 + r) * kvdim + c * P16;
+        *reinterpret_cast<uint4*>(ks + r * krow + c * P16) = __ldg(reinterpret_cast<const uint4*>(kbase + g));
+        *reinterpret_cast<uint4*>(vs + r * hd + c * P16) = __ldg(reinterpret_cast<const uint4*>(vbase + g));
     }
     __syncthreads();
-    // local softmax statistics per head
-    for (int g = 0; g < kv_mul; g++) {
-        float m = -FLT_MAX;
-        for (int i = threadIdx.x; i < L; i += blockDim.x) m = fmaxf(m, sc[g * chunk + i]);
-        m = block_max(m, red);
-        float l = 0.f;
-        for (int i = threadIdx.x; i < L; i += blockDim.x) {
-            float e = expf(sc[g * chunk + i] - m);
-            sc[g * chunk + i] = e;
-            l += e;
+    // scores: one (position, head) dot product per thread-iteration
+    for (int e = tid; e < L * kv_mul; e += blockDim.x) {
+        const int p = e / kv_mul, g = e % kv_mul;
+        const KV* kr = ks + p * krow;
+        const float* qr = qs + g * qrow;
+        float acc = 0.f;
+        for (int d = 0; d < hd; d += P16) {
+            float kf[P16];
+            KvVec<KV>::to_float(*reinterpret_cast<const uint4*>(kr + d), kf);
+#pragma unroll
+            for (int j = 0; j < P16; j++) acc = fmaf(qr[d + j], kf[j], acc);
         }
-        l = block_sum(l, red);
-        if (threadIdx.x == 0) {
-            float* pr = part + (((size_t)b * n_heads + kh * kv_mul + g) * splits + s) * (hd + 2);
-            pr[hd] = L > 0 ? m : -FLT_MAX;
+        sc[g * chunk + p] = __fmul_rn(acc, scale);
+    }
+    __syncthreads();
+    // softmax statistics per head: warp w handles heads w, w + nwarp, ...
+    for (int g = warp; g < kv_mul; g += nwarp) {
+        float m = -FLT_MAX;
+        for (int p = lane; p < L; p += 32) m = fmaxf(m, sc[g * chunk + p]);
+        m = warp_max(m);
+        float l = 0.f;
+        for (int p = lane; p < L; p += 32) {
+            float ev = expf(sc[g * chunk + p] - m);
+            sc[g * chunk + p] = ev;
+            l += ev;
+        }
+        l = warp_sum(l);
+        if (lane == 0) {
+            float* pr = pr_base + ((size_t)g * splits + s) * (hd + 2);
+            pr[hd] = m;
             pr[hd + 1] = l;
         }
     }
     __syncthreads();
-    // o[g][d] = sum_i e[g][i] * v[i][d]
-    for (int e = threadIdx.x; e < kv_mul * hd; e += blockDim.x) {
-        const int g = e / hd, d = e % hd;
-        float o = 0.f;
-        for (int i = 0; i < L; i++) o = fmaf(sc[g * chunk + i], kv_load<KV>(vbase + (int64_t)(p0 + i) * kvdim + d), o);
-        part[(((size_t)b * n_heads + kh * kv_mul + g) * splits + s) * (hd + 2) + d] = o;
+    // o[g][d] = sum_p e[g][p] v[p][d], four consecutive d per thread
+    for (int e = tid; e < kv_mul * (hd / 4); e += blockDim.x) {
+        const int g = e / (hd / 4), d = (e % (hd / 4)) * 4;
+        const float* er = sc + g * chunk;
+        float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+        for (int p = 0; p < L; p++) {
+            const float w = er[p];
+            const KV* vr = vs + p * hd + d;
+            float v4[4];
+            if constexpr (sizeof(KV) == 2) {
+                float2 a = __half22float2(*reinterpret_cast<const __half2*>(vr));
+                float2 c = __half22float2(*reinterpret_cast<const __half2*>(vr + 2));
+                v4[0] = a.x; v4[1] = a.y; v4[2] = c.x; v4[3] = c.y;
+            } else {
+                float4 f = *reinterpret_cast<const float4*>(vr);
+                v4[0] = f.x; v4[1] = f.y; v4[2] = f.z; v4[3] = f.w;
+            }
+            o0 = fmaf(w, v4[0], o0);
+            o1 = fmaf(w, v4[1], o1);
+            o2 = fmaf(w, v4[2], o2);
+            o3 = fmaf(w, v4[3], o3);
+        }
+        float* pr = pr_base + ((size_t)g * splits + s) * (hd + 2) + d;
+        pr[0] = o0;
+        pr[1] = o1;
+        pr[2] = o2;
+        pr[3] = o3;
     }
 }
 
+// Merge of the splits of (sequence b, head h): weights w_s = exp(m_s - M)
+// computed once, then out[d] = sum_s w_s o_s[d] / sum_s w_s l_s.
 __global__ void attn_combine_kernel(const float* __restrict__ part, int n_heads, int hd, int splits,
                                     float* __restrict__ out, int out_stride) {
+    extern __shared__ float wsm[];  // [splits + 1]
     const int h = blockIdx.x, b = blockIdx.y;
     const float* pr = part + ((size_t)b * n_heads + h) * splits * (hd + 2);
+    __shared__ float red[32];
     float M = -FLT_MAX;
-    for (int s = 0; s < splits; s++) M = fmaxf(M, pr[s * (hd + 2) + hd]);
-    float Lsum = 0.f;
-    for (int s = 0; s < splits; s++) {
+    for (int s = threadIdx.x; s < splits; s += blockDim.x) M = fmaxf(M, pr[s * (hd + 2) + hd]);
+    M = block_max(M, red);
+    float lsum = 0.f;
+    for (int s = threadIdx.x; s < splits; s += blockDim.x) {
         float m = pr[s * (hd + 2) + hd];
-        if (m > -FLT_MAX) Lsum += expf(m - M) * pr[s * (hd + 2) + hd + 1];
+        float w = m > -FLT_MAX ? expf(m - M) : 0.f;
+        wsm[s] = w;
+        lsum += w * pr[s * (hd + 2) + hd + 1];
     }
-    const float inv = 1.0f / Lsum;
+    lsum = block_sum(lsum, red);
+    const float inv = 1.0f / lsum;
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
         float o = 0.f;
-        for (int s = 0; s < splits; s++) {
-            float m = pr[s * (hd + 2) + hd];
-            if (m > -FLT_MAX) o += expf(m - M) * pr[s * (hd + 2) + d];
-        }
+        for (int s = 0; s < splits; s++) o = fmaf(wsm[s], pr[s * (hd + 2) + d], o);
         out[(size_t)b * out_stride + h * hd + d] = o * inv;
     }
 }
@@ -375,17 +453,21 @@ int launch_rope_kv(const RopeKvArgs& a, cudaStream_t s) {
 int attention_plan(int n_heads, int n_kv, int hd, int max_seq, int batch, int sms, AttnPlan* p) {
     CN_CHECK(n_kv > 0 && n_heads % n_kv == 0, CN_ERR_INVALID_ARG, "n_heads %% n_kv_heads != 0");
     CN_CHECK(n_heads / n_kv <= kMaxKvMul, CN_ERR_UNSUPPORTED, "kv_mul > %d", kMaxKvMul);
-    CN_CHECK(hd <= kMaxHd && hd % 2 == 0, CN_ERR_UNSUPPORTED, "head_dim %d", hd);
-    // enough CTAs for ~2 waves, chunks of at least 32 positions
-    int want = (2 * sms + batch * n_kv - 1) / (batch * n_kv);
+    CN_CHECK(hd <= kMaxHd && hd % 8 == 0, CN_ERR_UNSUPPORTED, "head_dim %d (needs a multiple of 8)", hd);
+    // about four CTAs per SM in total, chunks of 32..128 positions
+    int want = (4 * sms + batch * n_kv - 1) / (batch * n_kv);
     int chunk = (max_seq + want - 1) / want;
-    if (chunk < 32) chunk = 32;
-    if (chunk > 256) chunk = 256;
     chunk = (chunk + 31) / 32 * 32;
+    if (chunk < 32) chunk = 32;
+    if (chunk > 128) chunk = 128;
     p->chunk = chunk;
     p->splits = (max_seq + chunk - 1) / chunk;
     p->part_floats = (size_t)batch * n_heads * p->splits * (hd + 2);
-    p->smem = (size_t)((n_heads / n_kv) * (hd + chunk) + 32) * sizeof(float);
+    const int kv_mul = n_heads / n_kv;
+    // worst case over both cache types (fp32 rows are the wider ones)
+    const size_t q_bytes = (size_t)kv_mul * (hd + 4) * 4;
+    const size_t kv_bytes = (size_t)chunk * (attn_krow<float>(hd) + hd) * 4;
+    p->smem = q_bytes + kv_bytes + (size_t)kv_mul * chunk * 4 + 64 * 4;
     return CN_OK;
 }
 
@@ -401,21 +483,19 @@ int launch_attention(const AttnArgs& a, const AttnPlan& p, cudaStream_t s) {
     dim3 grid(p.splits, a.n_kv, a.batch);
     const float scale = 1.0f / sqrtf((float)a.hd);
     if (a.kv_f16) {
-        auto k = attn_split_kernel<__half>;
-        k<<<grid, kAttnThreads, p.smem, s>>>(a.q, (const __half*)a.kcache, (const __half*)a.vcache,
-                                             a.pos_dev, a.pos_host, a.n_heads, a.n_kv, a.hd, a.q_stride,
-                                             a.cache_seq_stride, a.cache_layer_off, a.ctx_len, p.splits, p.chunk,
-                                             scale, a.part);
+        attn_split_kernel<__half><<<grid, kAttnThreads, p.smem, s>>>(
+            a.q, (const __half*)a.kcache, (const __half*)a.vcache, a.pos_dev, a.pos_host, a.n_heads,
+            a.n_kv, a.hd, a.q_stride, a.cache_seq_stride, a.cache_layer_off, a.ctx_len, p.splits,
+            p.chunk, scale, a.part);
     } else {
-        auto k = attn_split_kernel<float>;
-        k<<<grid, kAttnThreads, p.smem, s>>>(a.q, (const float*)a.kcache, (const float*)a.vcache,
-                                             a.pos_dev, a.pos_host, a.n_heads, a.n_kv, a.hd, a.q_stride,
-                                             a.cache_seq_stride, a.cache_layer_off, a.ctx_len, p.splits, p.chunk,
-                                             scale, a.part);
+        attn_split_kernel<float><<<grid, kAttnThreads, p.smem, s>>>(
+            a.q, (const float*)a.kcache, (const float*)a.vcache, a.pos_dev, a.pos_host, a.n_heads,
+            a.n_kv, a.hd, a.q_stride, a.cache_seq_stride, a.cache_layer_off, a.ctx_len, p.splits,
+            p.chunk, scale, a.part);
     }
     CN_CUDA(cudaGetLastError());
-    attn_combine_kernel<<<dim3(a.n_heads, a.batch), 128, 0, s>>>(a.part, a.n_heads, a.hd, p.splits,
-                                                                 a.out, a.out_stride);
+    attn_combine_kernel<<<dim3(a.n_heads, a.batch), 128, (p.splits + 1) * sizeof(float), s>>>(
+        a.part, a.n_heads, a.hd, p.splits, a.out, a.out_stride);
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }
