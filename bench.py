@@ -54,6 +54,9 @@ def parse():
     ap.add_argument("--config", type=int, default=4, choices=(1, 4))
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gemv", default=None, metavar="TYPE:ROWSxCOLS:BATCH",
+                    help="kernel mode: run one fused dequant-GEMV (e.g. q4_k:28672x8192:1) "
+                         "--steps times on one GPU and print its mean time (ncu captures)")
     ap.add_argument("--nvtx-step", action="store_true",
                     help="after warm-up run one step inside the NVTX range 'timed_step' and exit "
                          "(for ncu --nvtx --nvtx-include timed_step/ launch lists)")
@@ -184,6 +187,41 @@ class CpuSample:
                 f"sequences, median of {reps} runs, extrapolated linearly in layers")
 
 
+def gemv_mode(a) -> int:
+    """One GEMV, seeded synthetic weights, launched --steps times after --warmup."""
+    import torch
+    import chatnet_b200 as cn
+    from chatnet_b200 import _native as N
+    name, shape, batch = a.gemv.split(":")
+    rows, cols = (int(v) for v in shape.split("x"))
+    batch = int(batch)
+    t = {"q4_0": cn.TYPE_Q4_0, "q4_k": cn.TYPE_Q4_K, "q6_k": cn.TYPE_Q6_K}[name]
+    ctx = cn.Context(0)
+    W = ctx.synth(t, rows, cols, cn.synth_seed(2, f"gemv.{name}.{rows}x{cols}"))
+    x = torch.from_numpy(cn.synth_fill(cn.TYPE_F32, batch, cols, cn.synth_seed(2, "gemv.x"))).cuda()
+    y = torch.empty(batch, rows, device="cuda")
+    ext = torch.cuda.ExternalStream(ctx.stream)
+
+    def run():
+        N.check(N.lib().cn_matvec_dev(ctx.handle, t, W.device_ptr, rows, cols, x.data_ptr(),
+                                      y.data_ptr(), batch), "cn_matvec_dev")
+    for _ in range(a.warmup):
+        run()
+    ctx.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ext)
+    for _ in range(a.steps):
+        run()
+    e1.record(ext)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / a.steps
+    nbytes = cn.byte_size(t, cols) * rows + 4 * batch * (rows + cols)
+    print(json.dumps({"gemv": a.gemv, "us_per_call": us, "GBps_incl_prep": nbytes / us / 1e3,
+                      "note": "warm L2 when the matrix fits in it; prep + GEMV launches"}))
+    ctx.close()
+    return 0
+
+
 # ---------------------------------------------------------------------------
 def main():
     a = parse()
@@ -201,6 +239,9 @@ def main():
                 "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                 "l2": "inputs larger than L2 (weights 38.5 GB)" if a.config == 4 else
                       "inputs larger than L2 (weights 0.58 GB)"}
+
+    if a.gemv:
+        return gemv_mode(a)
 
     if a.impl == "reference":
         if rank != 0:

@@ -358,30 +358,31 @@ __device__ __forceinline__ int owner_of(int64_t v, int64_t total, int C) {
     return c;
 }
 
+// Writes the tile's rows directly (the CTA computed all of its units).
 template <int NT>
-__device__ void finish_subtile(const GemvArgs& a, int tile, int warp, int cta, int C,
-                               int64_t total, int g, int t, int lane, float (&acc)[NT][4]) {
+__device__ __forceinline__ void store_rows(const GemvArgs& a, int tile, int warp, int g, int t,
+                                           float (&acc)[NT][4]) {
     const int64_t r0 = (int64_t)tile * kTileRows + warp * 16 + g, r1 = r0 + 8;
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+        int b = nt * 4 + t;
+        if (b < a.batch) {
+            if (r0 < a.rows) a.y[(size_t)b * a.rows + r0] = acc[nt][0] + acc[nt][1];
+            if (r1 < a.rows) a.y[(size_t)b * a.rows + r1] = acc[nt][2] + acc[nt][3];
+        }
+    }
+}
+
+// A tile shared by CTAs c_first..c_last: store this CTA's partial in its
+// slot (0 for its first tile, 1 for its last), and let the last warp to
+// arrive (per 16-row sub-tile) sum the slots in CTA order.
+template <int NT>
+__device__ void finish_shared(const GemvArgs& a, int tile, int warp, int cta, int my_slot,
+                              int64_t total, int C, int g, int t, int lane, float (&acc)[NT][4]) {
+    constexpr int BW = NT * 4;
     const int c_first = owner_of((int64_t)tile * a.units, total, C);
     const int c_last = owner_of((int64_t)(tile + 1) * a.units - 1, total, C);
-    if (c_first == c_last) {
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++) {
-            int b = nt * 4 + t;
-            if (b < a.batch) {
-                if (r0 < a.rows) a.y[(size_t)b * a.rows + r0] = acc[nt][0] + acc[nt][1];
-                if (r1 < a.rows) a.y[(size_t)b * a.rows + r1] = acc[nt][2] + acc[nt][3];
-            }
-        }
-        return;
-    }
-    constexpr int BW = NT * 4;
-    auto slot_base = [&](int c) {
-        int first_tile = (int)(range_start(total, c, C) / a.units);
-        int slot = 2 * c + (tile == first_tile ? 0 : 1);
-        return a.partials + ((size_t)slot * kTileRows + warp * 16) * BW;
-    };
-    float* p = slot_base(cta);
+    float* p = a.partials + ((size_t)(2 * cta + my_slot) * kTileRows + warp * 16) * BW;
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
         p[g * BW + nt * 4 + t] = acc[nt][0] + acc[nt][1];
@@ -395,11 +396,21 @@ __device__ void finish_subtile(const GemvArgs& a, int tile, int warp, int cta, i
     prev = __shfl_sync(0xffffffffu, prev, 0);
     if (prev != c_last - c_first) return;
     __threadfence();
+    // contributors: c_first's last tile (slot 1, unless the tile is also its
+    // first), the middle CTAs (whole range inside the tile: slot 0), c_last's
+    // first tile (slot 0)
+    const float* src[8];
+    int ns = 0;
+    for (int c = c_first; c <= c_last && ns < 8; c++) {
+        const int first_tile = (int)(range_start(total, c, C) / a.units);
+        const int slot = 2 * c + (tile == first_tile ? 0 : 1);
+        src[ns++] = a.partials + ((size_t)slot * kTileRows + warp * 16) * BW;
+    }
     for (int e = lane; e < 16 * BW; e += 32) {
         float s = 0.f;
-        for (int c = c_first; c <= c_last; c++) s += __ldcg(slot_base(c) + e);
-        int row = e / BW, b = e % BW;
-        int64_t r = (int64_t)tile * kTileRows + warp * 16 + row;
+        for (int k = 0; k < ns; k++) s += __ldcg(src[k] + e);
+        const int row = e / BW, b = e % BW;
+        const int64_t r = (int64_t)tile * kTileRows + warp * 16 + row;
         if (b < a.batch && r < a.rows) a.y[(size_t)b * a.rows + r] = s;
     }
     if (lane == 0) atomicExch(ctr, 0);
@@ -493,6 +504,7 @@ __global__ void __launch_bounds__(kThreads, Geo<TYPE, NT>::kMinCtas)
 
     const int nunits = (int)(v1 - v0);
     int tile = (int)(v0 / a.units), u = (int)(v0 % a.units);
+    const int tile0 = tile, u0 = u;
     int s = 0;
     uint32_t phase = 0;
     for (int n = 0; n < nunits; n++) {
@@ -525,7 +537,13 @@ __global__ void __launch_bounds__(kThreads, Geo<TYPE, NT>::kMinCtas)
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
         if (u == a.units - 1 || n == nunits - 1) {
-            finish_subtile<NT>(a, tile, warp, cta, C, total, g, t, lane, acc);
+            // only the first and the last tile of the range can be shared
+            const bool head_cut = (tile == tile0) && (u0 != 0);
+            const bool tail_cut = (n == nunits - 1) && (u != a.units - 1);
+            if (head_cut || tail_cut)
+                finish_shared<NT>(a, tile, warp, cta, tile == tile0 ? 0 : 1, total, C, g, t, lane, acc);
+            else
+                store_rows<NT>(a, tile, warp, g, t, acc);
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
         }
@@ -842,6 +860,10 @@ int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool
     // (tile, unit) space, but at least 2 units each.
     const int64_t total = (int64_t)p->tiles * p->units;
     int64_t want = total / 2 > 0 ? total / 2 : 1;
+    // at most 8 CTAs may share a tile (the fix-up sums up to 8 partials):
+    // ranges of at least units/7 units guarantee that
+    const int64_t cap = (int64_t)p->tiles * 7 > 0 ? (int64_t)p->tiles * 7 : 1;
+    if (want > cap) want = cap;
     int ctas = ctx->sms * occ;
     if (want < ctas) ctas = (int)want;
     p->ctas = ctas;
