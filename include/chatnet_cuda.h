@@ -150,6 +150,20 @@ int cn_dequantize_dev(int type, const void* d_blocks, float* d_out, int64_t n_el
 int cn_matvec_dev(cn_ctx* ctx, int type, const void* d_w, int out_dim, int in_dim,
                   const float* d_x, float* d_y, int batch);
 
+/* The fused dequant-GEMV of cn_matvec_dev for callers that cannot allocate
+ * device memory (hosts that own every buffer, or forbid cudaMalloc/cudaFree
+ * once running): no context, no allocation.  Its scratch is one fixed 4 MiB
+ * array inside the library, present on every GPU that loads it; calls needing
+ * more are rejected with CN_ERR_INVALID_ARG (batch 1..4 fits inner dimensions
+ * beyond 100k).  Calls share that array, so calls whose GPU work overlaps
+ * race: serialise them.  The first call on each device looks up the array's
+ * address and must not happen during a stream capture.  `stream` is a
+ * cudaStream_t (NULL = legacy default stream); the call only enqueues work.
+ * (no counterpart in the reference: an allocation-free variant of
+ * cn_matvec_dev) */
+int cn_matvec_noalloc_dev(int type, const void* d_w, int out_dim, int in_dim, const float* d_x,
+                          float* d_y, int batch, void* stream);
+
 /* ---- model level: one Llama decoder resident on the device ------------- */
 
 typedef struct cn_llama cn_llama;

@@ -1,0 +1,91 @@
+"""cn_matvec_noalloc_dev: the fused dequant-GEMV for hosts that cannot allocate
+device memory (they own every buffer, or forbid cudaMalloc/cudaFree while
+running).  Its scratch is a fixed array inside the library, so the check here
+is that it computes what cn_matvec_dev computes, call after call on the same
+reused array, and that it turns away work that does not fit that array.
+
+This file is collected last on purpose: if it fails, a run that stops at the
+first failure has already run every other test."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import chatnet_b200 as cn
+from chatnet_b200 import _native as N
+from tests.parity import REL_TOL, rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def _matvec_dev(ctx, t, W, rows, cols, x, batch):
+    import torch
+    y = torch.empty(batch, rows, device="cuda")
+    ctx.synchronize()
+    torch.cuda.synchronize()
+    N.check(N.lib().cn_matvec_dev(ctx.handle, t, W.device_ptr, rows, cols, x.data_ptr(),
+                                  y.data_ptr(), batch), "cn_matvec_dev")
+    ctx.synchronize()
+    return y.cpu().numpy()
+
+
+def _noalloc(t, W, rows, cols, x, batch):
+    import torch
+    y = torch.full((batch, rows), float("nan"), device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    N.check(N.lib().cn_matvec_noalloc_dev(t, W.device_ptr, rows, cols, x.data_ptr(), y.data_ptr(),
+                                          batch, stream), "cn_matvec_noalloc_dev")
+    torch.cuda.synchronize()
+    return y.cpu().numpy()
+
+
+CASES = [(cn.TYPE_Q4_K, 11008, 4096, 1), (cn.TYPE_Q4_0, 5632, 2048, 3),
+         (cn.TYPE_Q6_K, 4096, 4096, 4), (cn.TYPE_Q4_K, 37, 512, 2)]
+
+
+def test_noalloc_matches_matvec_dev(ctx):
+    import torch
+    for i, (t, rows, cols, batch) in enumerate(CASES):
+        W = ctx.synth(t, rows, cols, cn.synth_seed(7, f"noalloc.w.{i}"))
+        x = torch.from_numpy(
+            cn.synth_fill(cn.TYPE_F32, batch, cols, cn.synth_seed(7, f"noalloc.x.{i}"))).cuda()
+        ref = _matvec_dev(ctx, t, W, rows, cols, x, batch)
+        # two calls in a row on the shared array (the second sees the first's leftovers)
+        y1 = _noalloc(t, W, rows, cols, x, batch)
+        y2 = _noalloc(t, W, rows, cols, x, batch)
+        assert np.isfinite(y1).all() and np.isfinite(y2).all()
+        assert rel_err(y1, ref) <= REL_TOL, (i, rel_err(y1, ref))
+        assert rel_err(y2, ref) <= REL_TOL, (i, rel_err(y2, ref))
+        W.free()
+
+
+def test_noalloc_allocates_nothing(ctx):
+    import torch
+    t, rows, cols, batch = cn.TYPE_Q4_K, 4096, 8192, 1
+    W = ctx.synth(t, rows, cols, cn.synth_seed(7, "noalloc.mem.w"))
+    x = torch.from_numpy(cn.synth_fill(cn.TYPE_F32, batch, cols, cn.synth_seed(7, "noalloc.mem.x"))).cuda()
+    y = torch.empty(batch, rows, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def call():
+        N.check(N.lib().cn_matvec_noalloc_dev(t, W.device_ptr, rows, cols, x.data_ptr(),
+                                              y.data_ptr(), batch, stream))
+        torch.cuda.synchronize()
+    call()  # the first call on the device loads the array's address
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(3):
+        call()
+    assert torch.cuda.mem_get_info()[0] == free0
+    W.free()
+
+
+def test_noalloc_rejects_oversized_work(ctx):
+    import torch
+    t, rows, cols, batch = cn.TYPE_Q4_K, 1024, 28672, 32
+    W = ctx.synth(t, rows, cols, cn.synth_seed(7, "noalloc.big.w"))
+    x = torch.zeros(batch, cols, device="cuda")
+    y = torch.zeros(batch, rows, device="cuda")
+    with pytest.raises(ValueError, match="scratch"):
+        N.check(N.lib().cn_matvec_noalloc_dev(t, W.device_ptr, rows, cols, x.data_ptr(),
+                                              y.data_ptr(), batch, None))
+    W.free()
