@@ -64,8 +64,15 @@ struct GemvPlan {
     int units = 0;    // 256-position k units
     int ctas = 0;
     bool tma = false;
+    // Kernel family: kPathMma (fp16 mma.sync, gemv.cu), kPathI8 (integer
+    // mma.sync, gemv_i8.cu: Q4_K at batch 1..8), kPathTc (tcgen05,
+    // gemv_tc.cu: Q4_K at batch 1..5, opt-in).  The integer and tcgen05
+    // paths use 128-row tiles and keep activation records in the xfrag
+    // buffer (no xsum / xinv).
+    int path = 0;
     size_t xfrag_bytes = 0, xsum_bytes = 0, xinv_bytes = 0, partial_bytes = 0, counters = 0;
 };
+enum { kPathMma = 0, kPathTc = 1, kPathI8 = 2 };
 int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool tma,
               GemvPlan* plan);
 
@@ -108,6 +115,32 @@ int gemv_reserve(const GemvPlan& p, GemvNeeds* n);
 int norm_prep(cudaStream_t st, const float* x, const float* w, float* y, int n, int rows,
               float eps, const GemvOp* op, const GemvBufs& b);
 float gemv_step1_scale(int type);
+// Which activation form a GEMV reads: 0 plain fragments, 1 Q4_K fragments
+// (pre-scaled second k-step + chunk sums), 2 tensor-core digit records,
+// 3 integer-GEMV records.
+int gemv_prep_kind(const GemvOp& op);
+
+// Kernel family the environment selects for Q4_K decode GEMVs:
+// CHATNET_GEMV=i8 (default), tc or mma.
+int gemv_q4k_path();
+
+// integer mma.sync Q4_K GEMV (gemv_i8.cu)
+int gemv_i8_ctas(int sms, int tiles, int units);
+size_t gemv_i8_xbytes(int64_t cols, int batch);
+size_t gemv_i8_partial_bytes(int ctas);
+int gemv_i8_prepare();
+int gemv_i8_prep(cudaStream_t st, int sms, const float* d_x, int64_t cols, int batch, uint8_t* xrec);
+int gemv_i8_run(cudaStream_t st, uint32_t* err, const CUtensorMap* map, int64_t rows, int64_t cols,
+                int batch, int ctas, const uint8_t* xrec, float* partials, int* counters, float* y);
+
+// tensor-core Q4_K GEMV (gemv_tc.cu)
+int gemv_tc_ctas(int sms, int tiles, int units);
+size_t gemv_tc_xbytes(int64_t cols);
+size_t gemv_tc_partial_bytes(int ctas);
+int gemv_tc_prepare();
+int gemv_tc_prep(cudaStream_t st, int sms, const float* d_x, int64_t cols, int batch, uint8_t* xdig);
+int gemv_tc_run(cudaStream_t st, uint32_t* err, const CUtensorMap* map, int64_t rows, int64_t cols,
+                int batch, int ctas, const uint8_t* xdig, float* partials, int* counters, float* y);
 
 // Enqueues x-prep + GEMV on ctx->stream using the ctx's scratch.  `map` may
 // be null (encoded on the fly when possible, else the generic kernel runs).

@@ -24,10 +24,14 @@
 //    Tiles shared by several warps are combined through scratch partials
 //    by the last warp to arrive, in warp order (deterministic).
 #include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include "cn_common.cuh"
 #include "cn_internal.h"
 #include "formats.cuh"
+#include "gemv_i8.cuh"
+#include "gemv_tc.cuh"
 
 namespace cn {
 
@@ -416,9 +420,6 @@ __device__ void finish_shared(const GemvArgs& a, int tile, int warp, int cta, in
     if (lane == 0) atomicExch(ctr, 0);
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile(
@@ -647,6 +648,8 @@ __global__ void __launch_bounds__(kNormThreads)
     norm_prep_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ y,
                      int n, float eps, int emit, int nt_count, float step1,
                      uint4* __restrict__ xfrag, float* __restrict__ xsum, float* __restrict__ xinv) {
+    // emit: 0 = y only, 1 = y + mma.sync fragments, 2 = y + tensor-core digit
+    // records, 3 = y + integer-GEMV records
     __shared__ float red[32];
     const int b = blockIdx.x;
     const float* xr = x + (size_t)b * n;
@@ -683,7 +686,12 @@ __global__ void __launch_bounds__(kNormThreads)
         v[7] = __fmul_rn(__fmul_rn(a1.w, rms), w1.w);
         *reinterpret_cast<float4*>(yr + off) = make_float4(v[0], v[1], v[2], v[3]);
         *reinterpret_cast<float4*>(yr + off + 16) = make_float4(v[4], v[5], v[6], v[7]);
-        emit_unit(v, u, b, nt_count, step1, xfrag, xsum, xinv, lane);
+        if (emit == 3)
+            i8::emit_i8(v, u, b, (int)gridDim.x, reinterpret_cast<uint8_t*>(xfrag), lane);
+        else if (emit == 2)
+            tc::emit_digits(v, u, b, (int)gridDim.x, reinterpret_cast<uint8_t*>(xfrag), lane);
+        else
+            emit_unit(v, u, b, nt_count, step1, xfrag, xsum, xinv, lane);
     }
 }
 
@@ -842,7 +850,31 @@ int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool
     p->tma = tma;
     p->tiles = (int)((rows + kTileRows - 1) / kTileRows);
     p->units = (int)(cols / 256);
+    p->path = kPathMma;
     if (!tma) return CN_OK;
+    const int q4k_path = type == CN_TYPE_Q4_K ? gemv_q4k_path() : kPathMma;
+    if (q4k_path == kPathI8 && batch <= i8::kMaxNB) {
+        p->path = kPathI8;
+        p->tiles = (int)((rows + 127) / 128);
+        p->ctas = gemv_i8_ctas(ctx->sms, p->tiles, p->units);
+        p->xfrag_bytes = gemv_i8_xbytes(cols, batch);
+        p->xsum_bytes = 0;
+        p->xinv_bytes = 0;
+        p->partial_bytes = gemv_i8_partial_bytes(p->ctas);
+        p->counters = (size_t)p->tiles;
+        return gemv_i8_prepare();
+    }
+    if (q4k_path == kPathTc && batch <= tc::kMaxNB) {
+        p->path = kPathTc;
+        p->tiles = (int)((rows + tc::kRows - 1) / tc::kRows);
+        p->ctas = gemv_tc_ctas(ctx->sms, p->tiles, p->units);
+        p->xfrag_bytes = gemv_tc_xbytes(cols);
+        p->xsum_bytes = 0;
+        p->xinv_bytes = 0;
+        p->partial_bytes = gemv_tc_partial_bytes(p->ctas);
+        p->counters = (size_t)p->tiles;
+        return gemv_tc_prepare();
+    }
     int occ = 1;
 #define CN_OCC(T)                                                  \
     switch (p->nt) {                                               \
@@ -914,8 +946,29 @@ int gemv_make(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols
 
 float gemv_step1_scale(int type) { return type == CN_TYPE_Q4_K ? 0.0625f : 1.0f; }
 
+int gemv_prep_kind(const GemvOp& op) {
+    if (op.plan.path == kPathI8) return 3;
+    if (op.plan.path == kPathTc) return 2;
+    return op.type == CN_TYPE_Q4_K ? 1 : 0;
+}
+
+// Q4_K decode GEMVs run on the integer path unless CHATNET_GEMV names
+// another family ("tc" or "mma"); read once per process.
+int gemv_q4k_path() {
+    static int path = -1;
+    if (path < 0) {
+        const char* e = getenv("CHATNET_GEMV");
+        path = (e && strcmp(e, "tc") == 0) ? kPathTc : (e && strcmp(e, "mma") == 0) ? kPathMma : kPathI8;
+    }
+    return path;
+}
+
 int gemv_prep(cudaStream_t st, int sms, const GemvOp& op, const float* d_x, const GemvBufs& b) {
     if (!op.tma) return CN_OK;
+    if (op.plan.path == kPathI8)
+        return gemv_i8_prep(st, sms, d_x, op.cols, op.batch, reinterpret_cast<uint8_t*>(b.xfrag));
+    if (op.plan.path == kPathTc)
+        return gemv_tc_prep(st, sms, d_x, op.cols, op.batch, reinterpret_cast<uint8_t*>(b.xfrag));
     CN_CHECK((reinterpret_cast<uintptr_t>(d_x) & 15) == 0, CN_ERR_INVALID_ARG,
              "x must be 16-byte aligned");
     const int64_t items = (int64_t)op.plan.units * op.batch;
@@ -932,7 +985,8 @@ int norm_prep(cudaStream_t st, const float* x, const float* w, float* y, int n, 
               float eps, const GemvOp* op, const GemvBufs& b) {
     const bool emit = op && op->tma;
     norm_prep_kernel<<<rows, kNormThreads, 0, st>>>(
-        x, w, y, n, eps, emit ? 1 : 0, emit ? op->plan.nt : 1,
+        x, w, y, n, eps, emit ? (op->plan.path == kPathI8 ? 3 : op->plan.path == kPathTc ? 2 : 1) : 0,
+        emit ? op->plan.nt : 1,
         emit ? gemv_step1_scale(op->type) : 1.0f, emit ? b.xfrag : nullptr,
         emit && op->type == CN_TYPE_Q4_K ? b.xsum : nullptr, emit ? b.xinv : nullptr);
     CN_CUDA(cudaGetLastError());
@@ -953,6 +1007,12 @@ int gemv_run(cn_ctx* ctx, cudaStream_t st, const GemvOp& op, const float* d_x, c
         CN_CUDA(cudaGetLastError());
         return CN_OK;
     }
+    if (op.plan.path == kPathI8)
+        return gemv_i8_run(st, ctx->dev_err, &op.map, op.rows, op.cols, op.batch, op.plan.ctas,
+                           reinterpret_cast<const uint8_t*>(b.xfrag), b.partials, b.counters, d_y);
+    if (op.plan.path == kPathTc)
+        return gemv_tc_run(st, ctx->dev_err, &op.map, op.rows, op.cols, op.batch, op.plan.ctas,
+                           reinterpret_cast<const uint8_t*>(b.xfrag), b.partials, b.counters, d_y);
     GemvArgs a;
     a.rows = op.rows;
     a.units = op.plan.units;

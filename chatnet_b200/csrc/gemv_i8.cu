@@ -1,0 +1,428 @@
+// gemv_i8.cu -- Q4_K dequant-GEMV on integer mma.sync (m16n8k32, u8 x s8 ->
+// s32), decode batch 1..8.
+//
+// Same contract as the other GEMVs (TensorMath.MatVecMulGeneric with
+// DequantQ4K.DotProduct, Tensors/TensorMath.cs:624-656, DequantQ4K.cs:89-163).
+// A decode GEMV streams every weight byte once and reuses it only for the
+// batch's few columns, so the limit is instructions issued per weight, not
+// math.  Here a weight costs about one instruction:
+//
+//  * A producer warp streams [128 rows x one 144-byte super-block] of raw
+//    blocks per unit (2-D TMA) plus the unit's activation record (bulk copy,
+//    gemv_i8.cuh) into a ring of shared-memory stages; two CTAs per SM.
+//  * Eight consumer warps own 16 rows each.  One ldmatrix.x4 hands a warp the
+//    quant words of two sub-blocks for its 16 rows, already in the A-fragment
+//    layout of m16n8k32 (row g, bytes 4t..4t+3 of the sub-block's 16 bytes:
+//    low nibbles = positions 4t+0..3, high nibbles = 16+4t+0..3).  One AND
+//    (low nibbles) and one AND (batch 1: 16 * high nibble) or shift+AND
+//    (high nibbles) per register give the u8 operand.
+//  * Activations are exact integer digits (gemv_i8.cuh), so each MMA gives
+//    the exact integer sum_i q_i X_i of a sub-block; its 6-bit scale is
+//    applied with one integer multiply-add per accumulator.  Once per unit
+//    and row the digits are recombined (fp32), and
+//    d * sum - dmin * sum_j m_j XS_j, times 2^-e, joins the row's fp32 sum.
+//  * Stream-K over (128-row tile, unit) as in gemv.cu, deterministic fix-up.
+// Every mbarrier wait is bounded (error word, then uniform fall-through).
+#include "cn_common.cuh"
+#include "cn_internal.h"
+#include "gemv_i8.cuh"
+
+namespace cn {
+
+namespace i8 {
+
+constexpr int kRows = 128;
+constexpr int kRaw = 144 * kRows;  // raw Q4_K bytes per unit per tile
+constexpr int kCons = 8;           // consumer warps, 16 rows each
+constexpr int kThreads = (kCons + 1) * 32;
+
+template <int NB>
+struct Geo {
+    static constexpr int NT = n_tiles(NB);
+    static constexpr int kRec = (rec_bytes(NT) + 127) / 128 * 128;
+    static constexpr int kStage = kRaw + kRec;
+    static constexpr int kStages = (110 * 1024) / kStage;  // two CTAs per SM
+    static constexpr int kSmem = kStages * kStage + 256;
+};
+static_assert(Geo<1>::kStages >= 4 && Geo<8>::kStages >= 4, "pipeline depth");
+
+struct Args {
+    int64_t rows;
+    int units, tiles, batch;
+    const uint8_t* xrec;  // [unit][rec_bytes(NT)]
+    float* y;             // [batch][rows]
+    float* partials;      // [2 * ctas][128][8]
+    int* counters;        // [tiles], zero on entry, left zero
+    uint32_t* err;
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void imma(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                     uint2 b) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%10, %10, %10, %10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b.x), "r"(b.y), "r"(0));
+}
+
+__device__ __forceinline__ int64_t range_start(int64_t total, int c, int C) { return total * c / C; }
+__device__ __forceinline__ int owner_of(int64_t v, int64_t total, int C) {
+    int c = (int)((v * C) / total);
+    while (c + 1 < C && range_start(total, c + 1, C) <= v) c++;
+    while (c > 0 && range_start(total, c, C) > v) c--;
+    return c;
+}
+
+__device__ __forceinline__ void bar_consumers() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kCons * 32) : "memory");
+}
+
+// Which (row, sequence) pairs a consumer thread owns after the per-unit
+// recombination: row (t & 1 ? g + 8 : g) of its warp's 16 and, per n-tile nt,
+// sequence 2 nt + t / 2 (batch > 1) or sequence 0 for t < 2 (batch 1).
+template <int NB>
+__device__ __forceinline__ int owned_seq(int nt, int t) {
+    return NB == 1 ? (t < 2 ? 0 : -1) : (2 * nt + (t >> 1) < NB ? 2 * nt + (t >> 1) : -1);
+}
+
+// Stores a finished tile's owned values, or combines a tile several CTAs
+// share (partials parked per CTA, summed in CTA order by the last arrival).
+// All consumer threads call it together.
+template <int NB>
+__device__ void finish_tile(const Args& a, int r, int t, int tile, int cta, int C, int64_t total,
+                            bool shared_tile, int my_slot, const float (&acc)[Geo<NB>::NT], int* bcast) {
+    constexpr int NT = Geo<NB>::NT;
+    const int64_t row = (int64_t)tile * kRows + r;
+    if (!shared_tile) {
+        if (row < a.rows) {
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+                const int b = owned_seq<NB>(nt, t);
+                if (b >= 0) a.y[(size_t)b * a.rows + row] = acc[nt];
+            }
+        }
+        return;
+    }
+    float* p = a.partials + ((size_t)(2 * cta + my_slot) * kRows + r) * 8;
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+        const int b = owned_seq<NB>(nt, t);
+        if (b >= 0) p[b] = acc[nt];
+    }
+    __threadfence();
+    bar_consumers();
+    const int c_first = owner_of((int64_t)tile * a.units, total, C);
+    const int c_last = owner_of((int64_t)(tile + 1) * a.units - 1, total, C);
+    if (threadIdx.x == 0) *bcast = atomicAdd(&a.counters[tile], 1);
+    bar_consumers();
+    if (*bcast != c_last - c_first) return;
+    __threadfence();
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+        const int b = owned_seq<NB>(nt, t);
+        if (b < 0) continue;
+        float s = 0.f;
+        for (int c = c_first; c <= c_last; c++) {
+            const int first_tile = (int)(range_start(total, c, C) / a.units);
+            const int slot = 2 * c + (tile == first_tile ? 0 : 1);
+            s += __ldcg(a.partials + ((size_t)slot * kRows + r) * 8 + b);
+        }
+        if (row < a.rows) a.y[(size_t)b * a.rows + row] = s;
+    }
+    if (threadIdx.x == 0) atomicExch(&a.counters[tile], 0);
+}
+
+}  // namespace i8
+
+template <int NB>
+__global__ void __launch_bounds__(i8::kThreads, 2)
+    gemv_i8_q4k_kernel(const __grid_constant__ CUtensorMap map, const i8::Args a) {
+    using namespace i8;
+    using G = Geo<NB>;
+    constexpr int NT = G::NT;
+    constexpr int kStages = G::kStages, kStage = G::kStage;
+    constexpr int kRecB = rec_bytes(NT);
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStage);
+    uint64_t* empty = full + kStages;
+    int* bcast = reinterpret_cast<int*>(empty + kStages);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kCons);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    const int64_t total = (int64_t)a.tiles * a.units;
+    const int C = (int)(total < (int64_t)gridDim.x ? total : (int64_t)gridDim.x);
+    const int cta = blockIdx.x;
+    const int64_t v0 = cta < C ? range_start(total, cta, C) : 0;
+    const int64_t v1 = cta < C ? range_start(total, cta + 1, C) : 0;
+    const int nunits = (int)(v1 - v0);
+    const int tile0 = cta < C ? (int)(v0 / a.units) : 0;
+    const int u0 = cta < C ? (int)(v0 % a.units) : 0;
+
+    if (warp == kCons) {
+        // ---- producer ----
+        if (lane == 0) {
+            int tile = tile0, u = u0, s = 0, issued = 0;
+            uint32_t ph = 0;
+            for (int n = 0; n < nunits; n++) {
+                if (n >= kStages && !mbar_wait(&empty[s], ph ^ 1)) {
+                    atomicOr(a.err, kErrTimeout);
+                    break;
+                }
+                uint8_t* st = smem + s * kStage;
+                mbar_expect_tx(&full[s], kRaw + kRecB);
+                tma_load_2d(st, &map, 18 * u, tile * kRows, &full[s]);
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+                    "[%3];" ::"r"(smem_u32(st + kRaw)),
+                    "l"(reinterpret_cast<uint64_t>(a.xrec + (size_t)u * kRecB)), "r"(kRecB),
+                    "r"(smem_u32(&full[s]))
+                    : "memory");
+                issued = n + 1;
+                if (++u == a.units) {
+                    u = 0;
+                    tile++;
+                }
+                if (++s == kStages) {
+                    s = 0;
+                    ph ^= 1;
+                }
+            }
+            // no copy may still be landing when the CTA exits
+            for (int n = issued - kStages < 0 ? 0 : issued - kStages; n < issued; n++)
+                mbar_wait(&full[n % kStages], (uint32_t)(n / kStages) & 1);
+        }
+        return;
+    }
+
+    // ---- consumers ----
+    const int g = lane >> 2, t = lane & 3;
+    const int row0 = 16 * warp + g, row1 = row0 + 8;
+    const int r_own = (t & 1) ? row1 : row0;
+    // ldmatrix: lanes 8i..8i+7 address the 8 rows of matrix i = (row half
+    // i & 1, sub-block i >> 1 of the pair)
+    const uint32_t lds_off =
+        (uint32_t)((16 * warp + (lane & 7) + 8 * ((lane >> 3) & 1)) * 144 + 16 + 16 * (lane >> 4));
+    // weights of this thread's two accumulator columns in the recombination
+    const float w_lo = NB == 1 ? ldexpf(1.0f, 8 * t) : ldexpf(1.0f, 16 * (t & 1));
+    const float w_hi = NB == 1 ? ldexpf(1.0f, 8 * t + 4) : ldexpf(1.0f, 16 * (t & 1) + 8);
+
+    float acc[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) acc[nt] = 0.f;
+    int s = 0, et = tile0, eu = u0;
+    uint32_t ph = 0;
+    bool ok = true;
+    for (int n = 0; n < nunits; n++) {
+        if (ok && !mbar_wait(&full[s], ph)) {
+            atomicOr(a.err, kErrTimeout);
+            ok = false;
+        }
+        __syncwarp();
+        const uint8_t* st = smem + s * kStage;
+        const uint8_t* rec = st + kRaw;
+        const uint4 h0 = *reinterpret_cast<const uint4*>(st + row0 * 144);
+        const uint4 h1 = *reinterpret_cast<const uint4*>(st + row1 * 144);
+        // DecodeScales (DequantQ4K.cs:218-241), four 6-bit scales per word
+        const uint32_t sc0_lo = h0.y & 0x3F3F3F3Fu;
+        const uint32_t sc0_hi = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
+        const uint32_t sc1_lo = h1.y & 0x3F3F3F3Fu;
+        const uint32_t sc1_hi = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
+        int S[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) S[nt][0] = S[nt][1] = S[nt][2] = S[nt][3] = 0;
+        const uint32_t base = smem_u32(st) + lds_off;
+#pragma unroll
+        for (int jp = 0; jp < 4; jp++) {
+            uint32_t r[4];
+            ldsm_x4(base + 32 * jp, r);
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {
+                const int j = 2 * jp + hh;
+                const uint32_t q0 = r[2 * hh], q1 = r[2 * hh + 1];
+                const uint32_t a0 = q0 & 0x0F0F0F0Fu, a1 = q1 & 0x0F0F0F0Fu;
+                const uint32_t a2 = NB == 1 ? (q0 & 0xF0F0F0F0u) : ((q0 >> 4) & 0x0F0F0F0Fu);
+                const uint32_t a3 = NB == 1 ? (q1 & 0xF0F0F0F0u) : ((q1 >> 4) & 0x0F0F0F0Fu);
+                const int s0 = (int)(((j < 4 ? sc0_lo : sc0_hi) >> (8 * (j & 3))) & 0xFF);
+                const int s1 = (int)(((j < 4 ? sc1_lo : sc1_hi) >> (8 * (j & 3))) & 0xFF);
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++) {
+                    const uint2 bf = *reinterpret_cast<const uint2*>(rec + ((j * NT + nt) * 32 + lane) * 8);
+                    int d[4];
+                    imma(d, a0, a1, a2, a3, bf);
+                    S[nt][0] += s0 * d[0];
+                    S[nt][1] += s0 * d[1];
+                    S[nt][2] += s1 * d[2];
+                    S[nt][3] += s1 * d[3];
+                }
+            }
+        }
+        // the owned row's block header and the owned sequences' sums
+        const uint4 ho = (t & 1) ? h1 : h0;
+        const float dd = half_bits_to_float((uint16_t)(ho.x & 0xFFFF));
+        const float dmin = half_bits_to_float((uint16_t)(ho.x >> 16));
+        const uint32_t m_lo = ho.z & 0x3F3F3F3Fu;
+        const uint32_t m_hi = ((ho.w >> 4) & 0x0F0F0F0Fu) | ((ho.z >> 2) & 0x30303030u);
+        const int* xs = reinterpret_cast<const int*>(rec + xs_off(NT));
+        const float* inv = reinterpret_cast<const float*>(rec + inv_off(NT));
+        float mt[NT], iv[NT];
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            const int b = NB == 1 ? 0 : 2 * nt + (t >> 1);
+            mt[nt] = 0.f;
+            iv[nt] = 0.f;
+            if (b < NB) {
+                const int4 xa = *reinterpret_cast<const int4*>(xs + 8 * b);
+                const int4 xb = *reinterpret_cast<const int4*>(xs + 8 * b + 4);
+                long long m = 0;
+                m += (long long)(int)((m_lo >> 0) & 0xFF) * xa.x;
+                m += (long long)(int)((m_lo >> 8) & 0xFF) * xa.y;
+                m += (long long)(int)((m_lo >> 16) & 0xFF) * xa.z;
+                m += (long long)(int)((m_lo >> 24) & 0xFF) * xa.w;
+                m += (long long)(int)((m_hi >> 0) & 0xFF) * xb.x;
+                m += (long long)(int)((m_hi >> 8) & 0xFF) * xb.y;
+                m += (long long)(int)((m_hi >> 16) & 0xFF) * xb.z;
+                m += (long long)(int)((m_hi >> 24) & 0xFF) * xb.w;
+                mt[nt] = (float)m;
+                iv[nt] = inv[b];
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == kStages) {
+            s = 0;
+            ph ^= 1;
+        }
+        // recombine the digits: this thread's two columns, then across the
+        // threads that hold the same sequence
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            float f0 = fmaf((float)S[nt][1], w_hi, (float)S[nt][0] * w_lo);
+            float f1 = fmaf((float)S[nt][3], w_hi, (float)S[nt][2] * w_lo);
+            f0 += __shfl_xor_sync(0xffffffffu, f0, 1);
+            f1 += __shfl_xor_sync(0xffffffffu, f1, 1);
+            if (NB == 1) {
+                f0 += __shfl_xor_sync(0xffffffffu, f0, 2);
+                f1 += __shfl_xor_sync(0xffffffffu, f1, 2);
+            }
+            const float v = (t & 1) ? f1 : f0;
+            // batch 1 digits carry a factor 16 (see gemv_i8.cuh)
+            const float tsum = NB == 1 ? fmaf(dd, v, -16.0f * dmin * mt[nt]) : fmaf(dd, v, -dmin * mt[nt]);
+            acc[nt] = fmaf(tsum, NB == 1 ? iv[nt] * 0.0625f : iv[nt], acc[nt]);
+        }
+        // unit n ends a tile, or this CTA's range
+        if (eu == a.units - 1 || n == nunits - 1) {
+            const bool head_cut = (et == tile0) && (u0 != 0);
+            const bool tail_cut = (n == nunits - 1) && (eu != a.units - 1);
+            finish_tile<NB>(a, r_own, t, et, cta, C, total, head_cut || tail_cut, et == tile0 ? 0 : 1, acc,
+                            bcast);
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) acc[nt] = 0.f;
+        }
+        if (++eu == a.units) {
+            eu = 0;
+            et++;
+        }
+    }
+}
+
+// Standalone activation prep: one warp per (unit, sequence).
+__global__ void xrec_i8_kernel(const float* __restrict__ x, int K, int batch, uint8_t* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int units = K / 256;
+    const int64_t items = (int64_t)units * batch;
+    const int64_t w0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t it = w0; it < items; it += nw) {
+        const int u = (int)(it % units), b = (int)(it / units);
+        const float* p = x + (size_t)b * K + (size_t)u * 256 + (lane >> 2) * 32 + 4 * (lane & 3);
+        const float4 a0 = *reinterpret_cast<const float4*>(p);
+        const float4 a1 = *reinterpret_cast<const float4*>(p + 16);
+        const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        i8::emit_i8(v, u, b, batch, out, lane);
+    }
+}
+
+// ---- host ---------------------------------------------------------------------------
+
+int gemv_i8_ctas(int sms, int tiles, int units) {
+    // two CTAs per SM, each at least 2 units; at most 8 CTAs share a tile
+    const int64_t total = (int64_t)tiles * units;
+    int64_t want = total / 2 > 0 ? total / 2 : 1;
+    const int64_t cap = (int64_t)tiles * 7;
+    if (want > cap) want = cap;
+    return 2 * sms < want ? 2 * sms : (int)want;
+}
+
+size_t gemv_i8_xbytes(int64_t cols, int batch) {
+    return (size_t)(cols / 256) * i8::rec_bytes(i8::n_tiles(batch));
+}
+size_t gemv_i8_partial_bytes(int ctas) { return (size_t)2 * ctas * i8::kRows * 8 * sizeof(float); }
+
+int gemv_i8_prepare() {
+    static bool done[64] = {false};
+    int dev = 0;
+    CN_CUDA(cudaGetDevice(&dev));
+    if (done[dev & 63]) return CN_OK;
+#define CN_ATTR(NB)                                                                               \
+    CN_CUDA(cudaFuncSetAttribute(gemv_i8_q4k_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                 i8::Geo<NB>::kSmem));
+    CN_ATTR(1) CN_ATTR(2) CN_ATTR(3) CN_ATTR(4) CN_ATTR(5) CN_ATTR(6) CN_ATTR(7) CN_ATTR(8)
+#undef CN_ATTR
+    done[dev & 63] = true;
+    return CN_OK;
+}
+
+int gemv_i8_prep(cudaStream_t st, int sms, const float* d_x, int64_t cols, int batch, uint8_t* xrec) {
+    CN_CHECK((reinterpret_cast<uintptr_t>(d_x) & 15) == 0, CN_ERR_INVALID_ARG, "x must be 16-byte aligned");
+    CN_CHECK((reinterpret_cast<uintptr_t>(xrec) & 15) == 0, CN_ERR_INVALID_ARG, "scratch misaligned");
+    const int64_t items = (cols / 256) * batch;
+    int blocks = (int)((items + 7) / 8);
+    if (blocks > sms * 8) blocks = sms * 8;
+    xrec_i8_kernel<<<blocks, 256, 0, st>>>(d_x, (int)cols, batch, xrec);
+    CN_CUDA(cudaGetLastError());
+    return CN_OK;
+}
+
+int gemv_i8_run(cudaStream_t st, uint32_t* err, const CUtensorMap* map, int64_t rows, int64_t cols,
+                int batch, int ctas, const uint8_t* xrec, float* partials, int* counters, float* y) {
+    CN_CHECK(batch >= 1 && batch <= i8::kMaxNB && cols % 256 == 0 && ctas > 0, CN_ERR_INVALID_ARG,
+             "integer GEMV: bad shape");
+    int rc = gemv_i8_prepare();
+    if (rc) return rc;
+    i8::Args a;
+    a.rows = rows;
+    a.units = (int)(cols / 256);
+    a.tiles = (int)((rows + i8::kRows - 1) / i8::kRows);
+    a.batch = batch;
+    a.xrec = xrec;
+    a.y = y;
+    a.partials = partials;
+    a.counters = counters;
+    a.err = err;
+    switch (batch) {
+#define CN_I8(NB)                                                                                  \
+    case NB:                                                                                       \
+        gemv_i8_q4k_kernel<NB><<<ctas, i8::kThreads, i8::Geo<NB>::kSmem, st>>>(*map, a);           \
+        break;
+        CN_I8(1) CN_I8(2) CN_I8(3) CN_I8(4) CN_I8(5) CN_I8(6) CN_I8(7) CN_I8(8)
+#undef CN_I8
+    }
+    CN_CUDA(cudaGetLastError());
+    return CN_OK;
+}
+
+}  // namespace cn

@@ -1,0 +1,101 @@
+// gemv_i8.cuh -- activation records of the integer mma.sync GEMV (gemv_i8.cu)
+// and the warp routine that writes them (standalone prep and fused RMSNorm).
+#pragma once
+
+#include <stdint.h>
+
+namespace cn {
+namespace i8 {
+
+constexpr int kMaxNB = 8;  // sequences per call
+
+// Activations enter the integer GEMV as exact integers: per 256-position
+// unit u and sequence b, X = rint(x * 2^e) with e chosen so |X| <= 2^22, and
+// X is split into balanced digits, each an int8 column of the MMA's B
+// operand:
+//   batch 1:  6 base-16 digits d_i in [-8, 7], X = sum d_i 16^i, column i
+//             (columns 6, 7 zero).  The low-nibble positions carry 16 d_i, so
+//             the MMA can take the weights' high nibbles as 16 * q without a
+//             shift: every product is 16 * q * d_i.
+//   batch >1: 3 base-256 digits, X = sum d_i 256^i, column 4b + i (column
+//             4b + 3 zero).
+// Record of unit u (kRecBytes(NT) bytes, NT = n-tiles of 8 columns):
+//   [0, 2048 NT)      B fragments of m16n8k32: (8 j + ...) sub-block j, n-tile
+//                     nt, lane L at ((j * NT + nt) * 32 + L) * 8: {b0, b1} =
+//                     column nt*8 + L/4 at positions 32j + 4(L%4) + 0..3 and
+//                     32j + 16 + 4(L%4) + 0..3;
+//   [2048 NT, +256)   xs: int32 [8 sequences][8 sub-blocks], sum of X;
+//   [2048 NT+256, +32) inv: fp32 [8 sequences], 2^-e.
+__host__ __device__ constexpr int n_tiles(int batch) { return batch == 1 ? 1 : (4 * batch + 7) / 8; }
+__host__ __device__ constexpr int rec_bytes(int nt) { return 2048 * nt + 288; }
+__host__ __device__ constexpr int xs_off(int nt) { return 2048 * nt; }
+__host__ __device__ constexpr int inv_off(int nt) { return 2048 * nt + 256; }
+
+// One warp writes unit u of sequence b.  Lane (c = lane/4, t = lane%4) holds
+// in v[0..3] positions 32c + 4t + 0..3 and in v[4..7] positions
+// 32c + 16 + 4t + 0..3.  The warp with b == 0 also writes the zero columns.
+__device__ __forceinline__ void emit_i8(const float (&v)[8], int u, int b, int batch,
+                                        uint8_t* __restrict__ out, int lane) {
+    float am = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) am = fmaxf(am, fabsf(v[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    int e = 0;
+    if (am > 0.f && am < INFINITY) e = 21 - ilogbf(am);
+    e = e < -120 ? -120 : (e > 120 ? 120 : e);
+    const float sc = ldexpf(1.0f, e);
+    const int c = lane >> 2, t = lane & 3;
+    const int NT = n_tiles(batch);
+    uint8_t* reg = out + (size_t)u * rec_bytes(NT);
+    int X[8], xsum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        X[i] = __float2int_rn(v[i] * sc);
+        xsum += X[i];
+    }
+    // column n of this lane's sub-block c: word b0 (low-nibble positions) and b1
+    auto put = [&](int n, uint32_t b0, uint32_t b1) {
+        const int nt = n >> 3, L = (n & 7) * 4 + t;
+        *reinterpret_cast<uint2*>(reg + ((size_t)(c * NT + nt) * 32 + L) * 8) = make_uint2(b0, b1);
+    };
+    if (batch == 1) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            // digit i of X: balanced base 16
+            uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const int d = ((X[k] + 8) & 15) - 8;
+                X[k] = (X[k] - d) >> 4;
+                if (k < 4) w0 |= (uint32_t)((16 * d) & 255) << (8 * k);
+                else w1 |= (uint32_t)(d & 255) << (8 * (k - 4));
+            }
+            if (i < 6) put(i, w0, w1);
+            else put(i, 0u, 0u);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 3; i++) {
+            uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const int d = i < 2 ? ((X[k] + 128) & 255) - 128 : X[k];
+                X[k] = (X[k] - d) >> 8;
+                if (k < 4) w0 |= (uint32_t)(d & 255) << (8 * k);
+                else w1 |= (uint32_t)(d & 255) << (8 * (k - 4));
+            }
+            put(4 * b + i, w0, w1);
+        }
+        put(4 * b + 3, 0u, 0u);
+        if (b == 0)
+            for (int n = 4 * batch; n < 8 * NT; n++) put(n, 0u, 0u);
+    }
+    xsum += __shfl_xor_sync(0xffffffffu, xsum, 1);
+    xsum += __shfl_xor_sync(0xffffffffu, xsum, 2);
+    if (t == 0) reinterpret_cast<int*>(reg + xs_off(NT))[b * 8 + c] = xsum;
+    if (lane == 0) reinterpret_cast<float*>(reg + inv_off(NT))[b] = ldexpf(1.0f, -e);
+}
+
+}  // namespace i8
+}  // namespace cn

@@ -114,7 +114,8 @@ static int build_step(cn_llama* m, int B) {
 }
 
 // Tracks which activation vector (and in which form: Q4_K's pre-scaled
-// second k-step and chunk sums, or the plain one) the fragment buffer holds.
+// second k-step and chunk sums, the plain one, or the tensor-core digit
+// records) the fragment buffer holds.
 struct PrepCache {
     const float* x = nullptr;
     int kind = -1;
@@ -122,12 +123,12 @@ struct PrepCache {
     int64_t cols = 0;
     void set(const float* x_, const GemvOp& op) {
         x = x_;
-        kind = op.type == CN_TYPE_Q4_K;
+        kind = gemv_prep_kind(op);
         nt = op.plan.nt;
         cols = op.cols;
     }
     bool holds(const float* x_, const GemvOp& op) const {
-        return x == x_ && kind == (op.type == CN_TYPE_Q4_K) && nt == op.plan.nt && cols == op.cols;
+        return x == x_ && kind == gemv_prep_kind(op) && nt == op.plan.nt && cols == op.cols;
     }
 };
 
@@ -393,8 +394,10 @@ int cn_llama_create(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* const* t
     // GEMV scratch for the largest plan of any batch size up to max_batch
     {
         GemvNeeds need;
-        const int reps[4] = {4, 8, 16, 32};
-        for (int r = 0; r < 4; r++) {
+        // one batch size per plan class: the Q4_K decode families (1..5,
+        // 1..8), then the n-tiles of 4 of the fp16 kernel
+        const int reps[5] = {4, 5, 8, 16, 32};
+        for (int r = 0; r < 5; r++) {
             int b = reps[r] < B ? reps[r] : B;
             for (int i = 0; i < n_tensors; i++) {
                 const cn_tensor* w = tensors[i];

@@ -118,6 +118,29 @@ def test_matvec_edge_shapes(ctx, oracle, name, rows, cols, batch):
     assert rel_err(y, ref) <= REL_TOL
 
 
+TC_CASES = [
+    # Q4_K decode at batch 1..8: integer mma.sync path (128-row tiles, stream-K)
+    (300, 768),     # ragged last tile
+    (1, 256),       # one row, one unit
+    (7, 4096),      # one tile shared by 7 CTAs
+    (1024, 8192),   # Llama-2-70B k/v projection: 56 CTAs, up to 7 per tile
+    (2048, 5632),   # inner dimension not a power of two
+]
+
+
+@pytest.mark.parametrize("rows,cols", TC_CASES, ids=[f"{r}x{c}" for r, c in TC_CASES])
+@pytest.mark.parametrize("batch", [1, 2, 3, 4, 5, 8])
+def test_matvec_q4_k_decode(ctx, oracle, rows, cols, batch):
+    t = cn.TYPE_Q4_K
+    blocks = cn.synth_fill(t, rows, cols, seed=cn.synth_seed(2, f"tc.{rows}x{cols}"))
+    W = ctx.upload(blocks, t, rows, cols)
+    x = _x(batch, cols, f"tc.x.{rows}.{cols}.{batch}")
+    y = ctx.matvec(W, x)
+    ref = oracle.matvec(t, blocks, x, rows)
+    assert np.isfinite(y).all()
+    assert rel_err(y, ref) <= REL_TOL
+
+
 def test_matvec_repeatable(ctx):
     """Stream-K partials are combined in a fixed order: results are bitwise stable."""
     rows, cols = 4096, 11008
