@@ -125,7 +125,7 @@ int gemv_prep_kind(const GemvOp& op);
 int gemv_q4k_path();
 
 // integer mma.sync Q4_K GEMV (gemv_i8.cu)
-int gemv_i8_ctas(int sms, int tiles, int units);
+int gemv_i8_ctas(int sms, int tiles, int units, int batch);
 size_t gemv_i8_xbytes(int64_t cols, int batch);
 size_t gemv_i8_partial_bytes(int ctas);
 int gemv_i8_prepare();

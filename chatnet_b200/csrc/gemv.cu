@@ -856,7 +856,7 @@ int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool
     if (q4k_path == kPathI8 && batch <= i8::kMaxNB) {
         p->path = kPathI8;
         p->tiles = (int)((rows + 127) / 128);
-        p->ctas = gemv_i8_ctas(ctx->sms, p->tiles, p->units);
+        p->ctas = gemv_i8_ctas(ctx->sms, p->tiles, p->units, batch);
         p->xfrag_bytes = gemv_i8_xbytes(cols, batch);
         p->xsum_bytes = 0;
         p->xinv_bytes = 0;

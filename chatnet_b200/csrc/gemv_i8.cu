@@ -36,15 +36,18 @@ constexpr int kRaw = 144 * kRows;  // raw Q4_K bytes per unit per tile
 constexpr int kCons = 8;           // consumer warps, 16 rows each
 constexpr int kThreads = (kCons + 1) * 32;
 
+// Three CTAs per SM with three stages each when one n-tile of activation
+// digits suffices (batch 1, 2), else two CTAs with four stages.
 template <int NB>
 struct Geo {
     static constexpr int NT = n_tiles(NB);
     static constexpr int kRec = (rec_bytes(NT) + 127) / 128 * 128;
     static constexpr int kStage = kRaw + kRec;
-    static constexpr int kStages = (110 * 1024) / kStage;  // two CTAs per SM
+    static constexpr int kCtasPerSm = NT == 1 ? 3 : 2;
+    static constexpr int kStages = (NT == 1 ? 72 * 1024 : 110 * 1024) / kStage;
     static constexpr int kSmem = kStages * kStage + 256;
 };
-static_assert(Geo<1>::kStages >= 4 && Geo<8>::kStages >= 4, "pipeline depth");
+static_assert(Geo<1>::kStages >= 3 && Geo<3>::kStages >= 4 && Geo<8>::kStages >= 4, "pipeline depth");
 
 struct Args {
     int64_t rows;
@@ -69,6 +72,30 @@ __device__ __forceinline__ void imma(int (&d)[4], uint32_t a0, uint32_t a1, uint
         "{%8, %9}, {%10, %10, %10, %10};"
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b.x), "r"(b.y), "r"(0));
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+    return v;
+}
+// byte k of w, zero-extended
+__device__ __forceinline__ int byte_of(uint32_t w, int k) { return (int)__byte_perm(w, 0u, 0x4440u | k); }
+// dot product of four u8 lanes of a with four s8 lanes of b, plus c
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
 }
 
 __device__ __forceinline__ int64_t range_start(int64_t total, int c, int C) { return total * c / C; }
@@ -115,14 +142,22 @@ __device__ void finish_tile(const Args& a, int r, int t, int tile, int cta, int 
         const int b = owned_seq<NB>(nt, t);
         if (b >= 0) p[b] = acc[nt];
     }
-    __threadfence();
+    // the barrier orders every thread's partials before thread 0's
+    // release-acquire increment; the last arrival's acquire (then the
+    // barrier) orders all contributors' partials before its reads
     bar_consumers();
     const int c_first = owner_of((int64_t)tile * a.units, total, C);
     const int c_last = owner_of((int64_t)(tile + 1) * a.units - 1, total, C);
-    if (threadIdx.x == 0) *bcast = atomicAdd(&a.counters[tile], 1);
+    if (threadIdx.x == 0) {
+        int old;
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                     : "=r"(old)
+                     : "l"(a.counters + tile)
+                     : "memory");
+        *bcast = old;
+    }
     bar_consumers();
     if (*bcast != c_last - c_first) return;
-    __threadfence();
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
         const int b = owned_seq<NB>(nt, t);
@@ -141,7 +176,7 @@ __device__ void finish_tile(const Args& a, int r, int t, int tile, int cta, int 
 }  // namespace i8
 
 template <int NB>
-__global__ void __launch_bounds__(i8::kThreads, 2)
+__global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB>::kCtasPerSm)
     gemv_i8_q4k_kernel(const __grid_constant__ CUtensorMap map, const i8::Args a) {
     using namespace i8;
     using G = Geo<NB>;
@@ -219,6 +254,9 @@ __global__ void __launch_bounds__(i8::kThreads, 2)
     // weights of this thread's two accumulator columns in the recombination
     const float w_lo = NB == 1 ? ldexpf(1.0f, 8 * t) : ldexpf(1.0f, 16 * (t & 1));
     const float w_hi = NB == 1 ? ldexpf(1.0f, 8 * t + 4) : ldexpf(1.0f, 16 * (t & 1) + 8);
+    // weight of the min term (batch 1 sums carry the digits' factor 16)
+    const float kMin = NB == 1 ? -16.0f : -1.0f;
+    const uint32_t smem0 = smem_u32(smem);
 
     float acc[NT];
 #pragma unroll
@@ -232,23 +270,30 @@ __global__ void __launch_bounds__(i8::kThreads, 2)
             ok = false;
         }
         __syncwarp();
-        const uint8_t* st = smem + s * kStage;
-        const uint8_t* rec = st + kRaw;
-        const uint4 h0 = *reinterpret_cast<const uint4*>(st + row0 * 144);
-        const uint4 h1 = *reinterpret_cast<const uint4*>(st + row1 * 144);
-        // DecodeScales (DequantQ4K.cs:218-241), four 6-bit scales per word
-        const uint32_t sc0_lo = h0.y & 0x3F3F3F3Fu;
-        const uint32_t sc0_hi = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
-        const uint32_t sc1_lo = h1.y & 0x3F3F3F3Fu;
-        const uint32_t sc1_hi = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
+        const uint32_t st = smem0 + s * kStage;
+        const uint32_t rec = st + kRaw;
+        const uint4 h0 = lds128(st + row0 * 144);
+        const uint4 h1 = lds128(st + row1 * 144);
+        // DecodeScales (DequantQ4K.cs:218-241): the 8 six-bit scales of each row
+        int sc0[8], sc1[8];
+        {
+            const uint32_t lo0 = h0.y & 0x3F3F3F3Fu, hi0 = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
+            const uint32_t lo1 = h1.y & 0x3F3F3F3Fu, hi1 = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                sc0[k] = byte_of(lo0, k);
+                sc0[4 + k] = byte_of(hi0, k);
+                sc1[k] = byte_of(lo1, k);
+                sc1[4 + k] = byte_of(hi1, k);
+            }
+        }
         int S[NT][4];
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) S[nt][0] = S[nt][1] = S[nt][2] = S[nt][3] = 0;
-        const uint32_t base = smem_u32(st) + lds_off;
 #pragma unroll
         for (int jp = 0; jp < 4; jp++) {
             uint32_t r[4];
-            ldsm_x4(base + 32 * jp, r);
+            ldsm_x4(st + lds_off + 32 * jp, r);
 #pragma unroll
             for (int hh = 0; hh < 2; hh++) {
                 const int j = 2 * jp + hh;
@@ -256,28 +301,24 @@ __global__ void __launch_bounds__(i8::kThreads, 2)
                 const uint32_t a0 = q0 & 0x0F0F0F0Fu, a1 = q1 & 0x0F0F0F0Fu;
                 const uint32_t a2 = NB == 1 ? (q0 & 0xF0F0F0F0u) : ((q0 >> 4) & 0x0F0F0F0Fu);
                 const uint32_t a3 = NB == 1 ? (q1 & 0xF0F0F0F0u) : ((q1 >> 4) & 0x0F0F0F0Fu);
-                const int s0 = (int)(((j < 4 ? sc0_lo : sc0_hi) >> (8 * (j & 3))) & 0xFF);
-                const int s1 = (int)(((j < 4 ? sc1_lo : sc1_hi) >> (8 * (j & 3))) & 0xFF);
 #pragma unroll
                 for (int nt = 0; nt < NT; nt++) {
-                    const uint2 bf = *reinterpret_cast<const uint2*>(rec + ((j * NT + nt) * 32 + lane) * 8);
+                    const uint2 bf = lds64(rec + ((j * NT + nt) * 32 + lane) * 8);
                     int d[4];
                     imma(d, a0, a1, a2, a3, bf);
-                    S[nt][0] += s0 * d[0];
-                    S[nt][1] += s0 * d[1];
-                    S[nt][2] += s1 * d[2];
-                    S[nt][3] += s1 * d[3];
+                    S[nt][0] += sc0[j] * d[0];
+                    S[nt][1] += sc0[j] * d[1];
+                    S[nt][2] += sc1[j] * d[2];
+                    S[nt][3] += sc1[j] * d[3];
                 }
             }
         }
-        // the owned row's block header and the owned sequences' sums
-        const uint4 ho = (t & 1) ? h1 : h0;
+        // the owned row: d, dmin and its packed mins (DecodeScales)
+        const uint4 ho = lds128(st + r_own * 144);
         const float dd = half_bits_to_float((uint16_t)(ho.x & 0xFFFF));
         const float dmin = half_bits_to_float((uint16_t)(ho.x >> 16));
         const uint32_t m_lo = ho.z & 0x3F3F3F3Fu;
         const uint32_t m_hi = ((ho.w >> 4) & 0x0F0F0F0Fu) | ((ho.z >> 2) & 0x30303030u);
-        const int* xs = reinterpret_cast<const int*>(rec + xs_off(NT));
-        const float* inv = reinterpret_cast<const float*>(rec + inv_off(NT));
         float mt[NT], iv[NT];
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
@@ -285,19 +326,15 @@ __global__ void __launch_bounds__(i8::kThreads, 2)
             mt[nt] = 0.f;
             iv[nt] = 0.f;
             if (b < NB) {
-                const int4 xa = *reinterpret_cast<const int4*>(xs + 8 * b);
-                const int4 xb = *reinterpret_cast<const int4*>(xs + 8 * b + 4);
-                long long m = 0;
-                m += (long long)(int)((m_lo >> 0) & 0xFF) * xa.x;
-                m += (long long)(int)((m_lo >> 8) & 0xFF) * xa.y;
-                m += (long long)(int)((m_lo >> 16) & 0xFF) * xa.z;
-                m += (long long)(int)((m_lo >> 24) & 0xFF) * xa.w;
-                m += (long long)(int)((m_hi >> 0) & 0xFF) * xb.x;
-                m += (long long)(int)((m_hi >> 8) & 0xFF) * xb.y;
-                m += (long long)(int)((m_hi >> 16) & 0xFF) * xb.z;
-                m += (long long)(int)((m_hi >> 24) & 0xFF) * xb.w;
-                mt[nt] = (float)m;
-                iv[nt] = inv[b];
+                // sum_j m_j XS_j, one base-256 digit of XS at a time
+                const uint4 xa = lds128(rec + xs_off(NT) + b * 32);
+                const uint4 xb = lds128(rec + xs_off(NT) + b * 32 + 16);
+                const int t0 = dp4a_us(m_hi, xa.y, dp4a_us(m_lo, xa.x, 0));
+                const int t1 = dp4a_us(m_hi, xa.w, dp4a_us(m_lo, xa.z, 0));
+                const int t2 = dp4a_us(m_hi, xb.y, dp4a_us(m_lo, xb.x, 0));
+                const int t3 = dp4a_us(m_hi, xb.w, dp4a_us(m_lo, xb.z, 0));
+                mt[nt] = fmaf((float)t3, 16777216.0f, fmaf((float)t2, 65536.0f, fmaf((float)t1, 256.0f, (float)t0)));
+                iv[nt] = lds_f32(rec + inv_off(NT) + 4 * b);
             }
         }
         __syncwarp();
@@ -307,21 +344,14 @@ __global__ void __launch_bounds__(i8::kThreads, 2)
             ph ^= 1;
         }
         // recombine the digits: this thread's two columns, then across the
-        // threads that hold the same sequence
+        // threads that hold the same sequence (butterfly: keep the owned row)
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
-            float f0 = fmaf((float)S[nt][1], w_hi, (float)S[nt][0] * w_lo);
-            float f1 = fmaf((float)S[nt][3], w_hi, (float)S[nt][2] * w_lo);
-            f0 += __shfl_xor_sync(0xffffffffu, f0, 1);
-            f1 += __shfl_xor_sync(0xffffffffu, f1, 1);
-            if (NB == 1) {
-                f0 += __shfl_xor_sync(0xffffffffu, f0, 2);
-                f1 += __shfl_xor_sync(0xffffffffu, f1, 2);
-            }
-            const float v = (t & 1) ? f1 : f0;
-            // batch 1 digits carry a factor 16 (see gemv_i8.cuh)
-            const float tsum = NB == 1 ? fmaf(dd, v, -16.0f * dmin * mt[nt]) : fmaf(dd, v, -dmin * mt[nt]);
-            acc[nt] = fmaf(tsum, NB == 1 ? iv[nt] * 0.0625f : iv[nt], acc[nt]);
+            const float f0 = fmaf((float)S[nt][1], w_hi, (float)S[nt][0] * w_lo);
+            const float f1 = fmaf((float)S[nt][3], w_hi, (float)S[nt][2] * w_lo);
+            float v = ((t & 1) ? f1 : f0) + __shfl_xor_sync(0xffffffffu, (t & 1) ? f0 : f1, 1);
+            if (NB == 1) v += __shfl_xor_sync(0xffffffffu, v, 2);
+            acc[nt] = fmaf(fmaf(dd, v, kMin * dmin * mt[nt]), iv[nt], acc[nt]);
         }
         // unit n ends a tile, or this CTA's range
         if (eu == a.units - 1 || n == nunits - 1) {
@@ -358,13 +388,14 @@ __global__ void xrec_i8_kernel(const float* __restrict__ x, int K, int batch, ui
 
 // ---- host ---------------------------------------------------------------------------
 
-int gemv_i8_ctas(int sms, int tiles, int units) {
-    // two CTAs per SM, each at least 2 units; at most 8 CTAs share a tile
+int gemv_i8_ctas(int sms, int tiles, int units, int batch) {
+    // every resident CTA, each at least 2 units; at most 8 CTAs share a tile
+    const int per_sm = i8::n_tiles(batch) == 1 ? i8::Geo<1>::kCtasPerSm : i8::Geo<8>::kCtasPerSm;
     const int64_t total = (int64_t)tiles * units;
     int64_t want = total / 2 > 0 ? total / 2 : 1;
     const int64_t cap = (int64_t)tiles * 7;
     if (want > cap) want = cap;
-    return 2 * sms < want ? 2 * sms : (int)want;
+    return per_sm * sms < want ? per_sm * sms : (int)want;
 }
 
 size_t gemv_i8_xbytes(int64_t cols, int batch) {

@@ -19,13 +19,17 @@ constexpr int kMaxNB = 8;  // sequences per call
 //             shift: every product is 16 * q * d_i.
 //   batch >1: 3 base-256 digits, X = sum d_i 256^i, column 4b + i (column
 //             4b + 3 zero).
-// Record of unit u (kRecBytes(NT) bytes, NT = n-tiles of 8 columns):
-//   [0, 2048 NT)      B fragments of m16n8k32: (8 j + ...) sub-block j, n-tile
-//                     nt, lane L at ((j * NT + nt) * 32 + L) * 8: {b0, b1} =
-//                     column nt*8 + L/4 at positions 32j + 4(L%4) + 0..3 and
+// Record of unit u (rec_bytes(NT) bytes, NT = n-tiles of 8 columns):
+//   [0, 2048 NT)      B fragments of m16n8k32: sub-block j, n-tile nt, lane L
+//                     at ((j * NT + nt) * 32 + L) * 8: {b0, b1} = column
+//                     nt*8 + L/4 at positions 32j + 4(L%4) + 0..3 and
 //                     32j + 16 + 4(L%4) + 0..3;
-//   [2048 NT, +256)   xs: int32 [8 sequences][8 sub-blocks], sum of X;
-//   [2048 NT+256, +32) inv: fp32 [8 sequences], 2^-e.
+//   [2048 NT, +256)   xsd: int8 [8 sequences][4 digits k][8 sub-blocks j]:
+//                     XS_j = sum of X over sub-block j = sum_k 256^k xsd[k][j]
+//                     (balanced digits, so a dp4a against the row's packed
+//                     6-bit mins gives sum_j m_j XS_j digit by digit);
+//   [2048 NT+256, +32) inv: fp32 [8 sequences], 2^-e (batch 1: 2^-e / 16,
+//                     which undoes the digits' factor 16).
 __host__ __device__ constexpr int n_tiles(int batch) { return batch == 1 ? 1 : (4 * batch + 7) / 8; }
 __host__ __device__ constexpr int rec_bytes(int nt) { return 2048 * nt + 288; }
 __host__ __device__ constexpr int xs_off(int nt) { return 2048 * nt; }
@@ -93,8 +97,17 @@ __device__ __forceinline__ void emit_i8(const float (&v)[8], int u, int b, int b
     }
     xsum += __shfl_xor_sync(0xffffffffu, xsum, 1);
     xsum += __shfl_xor_sync(0xffffffffu, xsum, 2);
-    if (t == 0) reinterpret_cast<int*>(reg + xs_off(NT))[b * 8 + c] = xsum;
-    if (lane == 0) reinterpret_cast<float*>(reg + inv_off(NT))[b] = ldexpf(1.0f, -e);
+    if (t == 0) {
+        int8_t* xd = reinterpret_cast<int8_t*>(reg + xs_off(NT)) + b * 32 + c;
+#pragma unroll
+        for (int k = 0; k < 3; k++) {
+            const int d = ((xsum + 128) & 255) - 128;
+            xd[8 * k] = (int8_t)d;
+            xsum = (xsum - d) >> 8;
+        }
+        xd[24] = (int8_t)xsum;  // |sum| <= 2^27: the top digit is at most 8
+    }
+    if (lane == 0) reinterpret_cast<float*>(reg + inv_off(NT))[b] = ldexpf(1.0f, batch == 1 ? -e - 4 : -e);
 }
 
 }  // namespace i8
