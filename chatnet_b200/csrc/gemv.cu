@@ -861,7 +861,7 @@ int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool
         p->xsum_bytes = 0;
         p->xinv_bytes = 0;
         p->partial_bytes = gemv_i8_partial_bytes(p->ctas);
-        p->counters = (size_t)p->tiles;
+        p->counters = (size_t)p->tiles * 8;  // one per 16-row sub-tile
         return gemv_i8_prepare();
     }
     if (q4k_path == kPathTc && batch <= tc::kMaxNB) {

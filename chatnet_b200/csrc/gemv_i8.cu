@@ -55,14 +55,12 @@ struct Args {
     const uint8_t* xrec;  // [unit][rec_bytes(NT)]
     float* y;             // [batch][rows]
     float* partials;      // [2 * ctas][128][8]
-    int* counters;        // [tiles], zero on entry, left zero
+    int* counters;        // [tiles][kCons], zero on entry, left zero
     uint32_t* err;
 };
 
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(addr));
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
 }
 
 __device__ __forceinline__ void imma(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -106,10 +104,6 @@ __device__ __forceinline__ int owner_of(int64_t v, int64_t total, int C) {
     return c;
 }
 
-__device__ __forceinline__ void bar_consumers() {
-    asm volatile("bar.sync 1, %0;" ::"n"(kCons * 32) : "memory");
-}
-
 // Which (row, sequence) pairs a consumer thread owns after the per-unit
 // recombination: row (t & 1 ? g + 8 : g) of its warp's 16 and, per n-tile nt,
 // sequence 2 nt + t / 2 (batch > 1) or sequence 0 for t < 2 (batch 1).
@@ -118,12 +112,15 @@ __device__ __forceinline__ int owned_seq(int nt, int t) {
     return NB == 1 ? (t < 2 ? 0 : -1) : (2 * nt + (t >> 1) < NB ? 2 * nt + (t >> 1) : -1);
 }
 
-// Stores a finished tile's owned values, or combines a tile several CTAs
-// share (partials parked per CTA, summed in CTA order by the last arrival).
-// All consumer threads call it together.
+// Stores the owned values of a finished 16-row sub-tile, or, for a tile
+// several CTAs share, parks this warp's partials and lets the last warp to
+// arrive (per 16-row sub-tile, so warps never wait for each other) add all
+// contributors' partials in CTA order: deterministic.  r = the thread's row
+// in the 128-row tile.
 template <int NB>
-__device__ void finish_tile(const Args& a, int r, int t, int tile, int cta, int C, int64_t total,
-                            bool shared_tile, int my_slot, const float (&acc)[Geo<NB>::NT], int* bcast) {
+__device__ void finish_subtile(const Args& a, int r, int t, int warp, int tile, int cta, int C,
+                               int64_t total, bool shared_tile, int my_slot,
+                               const float (&acc)[Geo<NB>::NT]) {
     constexpr int NT = Geo<NB>::NT;
     const int64_t row = (int64_t)tile * kRows + r;
     if (!shared_tile) {
@@ -142,22 +139,18 @@ __device__ void finish_tile(const Args& a, int r, int t, int tile, int cta, int 
         const int b = owned_seq<NB>(nt, t);
         if (b >= 0) p[b] = acc[nt];
     }
-    // the barrier orders every thread's partials before thread 0's
-    // release-acquire increment; the last arrival's acquire (then the
-    // barrier) orders all contributors' partials before its reads
-    bar_consumers();
+    // __syncwarp orders the lanes' partials before lane 0's release-acquire
+    // increment; the last arrival's acquire orders every contributor's
+    // partials before its reads
+    __syncwarp();
     const int c_first = owner_of((int64_t)tile * a.units, total, C);
     const int c_last = owner_of((int64_t)(tile + 1) * a.units - 1, total, C);
-    if (threadIdx.x == 0) {
-        int old;
-        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
-                     : "=r"(old)
-                     : "l"(a.counters + tile)
-                     : "memory");
-        *bcast = old;
-    }
-    bar_consumers();
-    if (*bcast != c_last - c_first) return;
+    int* ctr = a.counters + tile * kCons + warp;
+    int old = 0;
+    if ((threadIdx.x & 31) == 0)
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(ctr) : "memory");
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old != c_last - c_first) return;
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
         const int b = owned_seq<NB>(nt, t);
@@ -170,7 +163,8 @@ __device__ void finish_tile(const Args& a, int r, int t, int tile, int cta, int 
         }
         if (row < a.rows) a.y[(size_t)b * a.rows + row] = s;
     }
-    if (threadIdx.x == 0) atomicExch(&a.counters[tile], 0);
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) atomicExch(ctr, 0);
 }
 
 }  // namespace i8
@@ -213,7 +207,7 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB>::kCtasPerSm)
             int tile = tile0, u = u0, s = 0, issued = 0;
             uint32_t ph = 0;
             for (int n = 0; n < nunits; n++) {
-                if (n >= kStages && !mbar_wait(&empty[s], ph ^ 1)) {
+                if (n >= kStages && !mbar_wait_sleep(&empty[s], ph ^ 1)) {
                     atomicOr(a.err, kErrTimeout);
                     break;
                 }
@@ -247,60 +241,65 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB>::kCtasPerSm)
     const int g = lane >> 2, t = lane & 3;
     const int row0 = 16 * warp + g, row1 = row0 + 8;
     const int r_own = (t & 1) ? row1 : row0;
-    // ldmatrix: lanes 8i..8i+7 address the 8 rows of matrix i = (row half
-    // i & 1, sub-block i >> 1 of the pair)
-    const uint32_t lds_off =
-        (uint32_t)((16 * warp + (lane & 7) + 8 * ((lane >> 3) & 1)) * 144 + 16 + 16 * (lane >> 4));
+    // ldmatrix.x2: lanes 0-7 address rows 0-7 of the warp's 16, lanes 8-15
+    // rows 8-15 (lanes 16-31 repeat them), at the sub-block's quant bytes
+    const uint32_t lds_off = (uint32_t)((16 * warp + (lane & 15)) * 144 + 16);
     // weights of this thread's two accumulator columns in the recombination
-    const float w_lo = NB == 1 ? ldexpf(1.0f, 8 * t) : ldexpf(1.0f, 16 * (t & 1));
-    const float w_hi = NB == 1 ? ldexpf(1.0f, 8 * t + 4) : ldexpf(1.0f, 16 * (t & 1) + 8);
+    // (batch 1: base 15, columns 2t and 2t+1 weigh 15^2t and 15^(2t+1))
+    const float w_lo = NB == 1 ? (t == 0 ? 1.0f : t == 1 ? 225.0f : t == 2 ? 50625.0f : 11390625.0f)
+                               : ldexpf(1.0f, 16 * (t & 1));
+    const float w_hi = NB == 1 ? 15.0f * w_lo : ldexpf(1.0f, 16 * (t & 1) + 8);
     // weight of the min term (batch 1 sums carry the digits' factor 16)
     const float kMin = NB == 1 ? -16.0f : -1.0f;
     const uint32_t smem0 = smem_u32(smem);
 
-    float acc[NT];
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++) acc[nt] = 0.f;
-    int s = 0, et = tile0, eu = u0;
+    int s = 0, n = 0, et = tile0, eu = u0;
     uint32_t ph = 0;
     bool ok = true;
-    for (int n = 0; n < nunits; n++) {
-        if (ok && !mbar_wait(&full[s], ph)) {
-            atomicOr(a.err, kErrTimeout);
-            ok = false;
-        }
-        __syncwarp();
-        const uint32_t st = smem0 + s * kStage;
-        const uint32_t rec = st + kRaw;
-        const uint4 h0 = lds128(st + row0 * 144);
-        const uint4 h1 = lds128(st + row1 * 144);
-        // DecodeScales (DequantQ4K.cs:218-241): the 8 six-bit scales of each row
-        int sc0[8], sc1[8];
-        {
-            const uint32_t lo0 = h0.y & 0x3F3F3F3Fu, hi0 = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
-            const uint32_t lo1 = h1.y & 0x3F3F3F3Fu, hi1 = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
+    while (n < nunits) {
+        // one tile segment of this CTA's range
+        const int seg = min(nunits - n, a.units - eu);
+        float acc[NT];
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                sc0[k] = byte_of(lo0, k);
-                sc0[4 + k] = byte_of(hi0, k);
-                sc1[k] = byte_of(lo1, k);
-                sc1[4 + k] = byte_of(hi1, k);
+        for (int nt = 0; nt < NT; nt++) acc[nt] = 0.f;
+        for (int k = 0; k < seg; k++) {
+            if (ok && !mbar_wait_sleep(&full[s], ph)) {
+                atomicOr(a.err, kErrTimeout);
+                ok = false;
             }
-        }
-        int S[NT][4];
+            __syncwarp();
+            const uint32_t st = smem0 + s * kStage;
+            const uint32_t rec = st + kRaw;
+            const uint4 h0 = lds128(st + row0 * 144);
+            const uint4 h1 = lds128(st + row1 * 144);
+            // DecodeScales (DequantQ4K.cs:218-241): the 8 six-bit scales of each row
+            int sc0[8], sc1[8];
+            {
+                const uint32_t lo0 = h0.y & 0x3F3F3F3Fu, hi0 = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
+                const uint32_t lo1 = h1.y & 0x3F3F3F3Fu, hi1 = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
 #pragma unroll
-        for (int nt = 0; nt < NT; nt++) S[nt][0] = S[nt][1] = S[nt][2] = S[nt][3] = 0;
+                for (int q = 0; q < 4; q++) {
+                    sc0[q] = byte_of(lo0, q);
+                    sc0[4 + q] = byte_of(hi0, q);
+                    sc1[q] = byte_of(lo1, q);
+                    sc1[4 + q] = byte_of(hi1, q);
+                }
+            }
+            int S[NT][4];
 #pragma unroll
-        for (int jp = 0; jp < 4; jp++) {
-            uint32_t r[4];
-            ldsm_x4(st + lds_off + 32 * jp, r);
+            for (int nt = 0; nt < NT; nt++) S[nt][0] = S[nt][1] = S[nt][2] = S[nt][3] = 0;
 #pragma unroll
-            for (int hh = 0; hh < 2; hh++) {
-                const int j = 2 * jp + hh;
-                const uint32_t q0 = r[2 * hh], q1 = r[2 * hh + 1];
-                const uint32_t a0 = q0 & 0x0F0F0F0Fu, a1 = q1 & 0x0F0F0F0Fu;
-                const uint32_t a2 = NB == 1 ? (q0 & 0xF0F0F0F0u) : ((q0 >> 4) & 0x0F0F0F0Fu);
-                const uint32_t a3 = NB == 1 ? (q1 & 0xF0F0F0F0u) : ((q1 >> 4) & 0x0F0F0F0Fu);
+            for (int j = 0; j < 8; j++) {
+                // quant words of sub-block j, rows g and g+8: byte 4t+i holds
+                // positions 4t+i (low nibble) and 16+4t+i (high nibble)
+                uint32_t q0, q1;
+                ldsm_x2(st + lds_off + 16 * j, q0, q1);
+                // batch 1: k-slots 0-15 take the raw bytes, 16-31 the low
+                // nibbles (gemv_i8.cuh); otherwise low, then high nibbles
+                const uint32_t a0 = NB == 1 ? q0 : (q0 & 0x0F0F0F0Fu);
+                const uint32_t a1 = NB == 1 ? q1 : (q1 & 0x0F0F0F0Fu);
+                const uint32_t a2 = NB == 1 ? (q0 & 0x0F0F0F0Fu) : ((q0 >> 4) & 0x0F0F0F0Fu);
+                const uint32_t a3 = NB == 1 ? (q1 & 0x0F0F0F0Fu) : ((q1 >> 4) & 0x0F0F0F0Fu);
 #pragma unroll
                 for (int nt = 0; nt < NT; nt++) {
                     const uint2 bf = lds64(rec + ((j * NT + nt) * 32 + lane) * 8);
@@ -312,60 +311,55 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB>::kCtasPerSm)
                     S[nt][3] += sc1[j] * d[3];
                 }
             }
-        }
-        // the owned row: d, dmin and its packed mins (DecodeScales)
-        const uint4 ho = lds128(st + r_own * 144);
-        const float dd = half_bits_to_float((uint16_t)(ho.x & 0xFFFF));
-        const float dmin = half_bits_to_float((uint16_t)(ho.x >> 16));
-        const uint32_t m_lo = ho.z & 0x3F3F3F3Fu;
-        const uint32_t m_hi = ((ho.w >> 4) & 0x0F0F0F0Fu) | ((ho.z >> 2) & 0x30303030u);
-        float mt[NT], iv[NT];
+            // the owned row: d, dmin and its packed mins (DecodeScales)
+            const uint4 ho = lds128(st + r_own * 144);
+            const float dd = half_bits_to_float((uint16_t)(ho.x & 0xFFFF));
+            const float dmin = half_bits_to_float((uint16_t)(ho.x >> 16));
+            const uint32_t m_lo = ho.z & 0x3F3F3F3Fu;
+            const uint32_t m_hi = ((ho.w >> 4) & 0x0F0F0F0Fu) | ((ho.z >> 2) & 0x30303030u);
+            float mt[NT], iv[NT];
 #pragma unroll
-        for (int nt = 0; nt < NT; nt++) {
-            const int b = NB == 1 ? 0 : 2 * nt + (t >> 1);
-            mt[nt] = 0.f;
-            iv[nt] = 0.f;
-            if (b < NB) {
-                // sum_j m_j XS_j, one base-256 digit of XS at a time
-                const uint4 xa = lds128(rec + xs_off(NT) + b * 32);
-                const uint4 xb = lds128(rec + xs_off(NT) + b * 32 + 16);
-                const int t0 = dp4a_us(m_hi, xa.y, dp4a_us(m_lo, xa.x, 0));
-                const int t1 = dp4a_us(m_hi, xa.w, dp4a_us(m_lo, xa.z, 0));
-                const int t2 = dp4a_us(m_hi, xb.y, dp4a_us(m_lo, xb.x, 0));
-                const int t3 = dp4a_us(m_hi, xb.w, dp4a_us(m_lo, xb.z, 0));
-                mt[nt] = fmaf((float)t3, 16777216.0f, fmaf((float)t2, 65536.0f, fmaf((float)t1, 256.0f, (float)t0)));
-                iv[nt] = lds_f32(rec + inv_off(NT) + 4 * b);
+            for (int nt = 0; nt < NT; nt++) {
+                const int b = NB == 1 ? 0 : 2 * nt + (t >> 1);
+                mt[nt] = 0.f;
+                iv[nt] = 0.f;
+                if (b < NB) {
+                    // sum_j m_j XS_j, one base-256 digit of XS at a time
+                    const uint4 xa = lds128(rec + xs_off(NT) + b * 32);
+                    const uint4 xb = lds128(rec + xs_off(NT) + b * 32 + 16);
+                    const int t0 = dp4a_us(m_hi, xa.y, dp4a_us(m_lo, xa.x, 0));
+                    const int t1 = dp4a_us(m_hi, xa.w, dp4a_us(m_lo, xa.z, 0));
+                    const int t2 = dp4a_us(m_hi, xb.y, dp4a_us(m_lo, xb.x, 0));
+                    const int t3 = dp4a_us(m_hi, xb.w, dp4a_us(m_lo, xb.z, 0));
+                    mt[nt] = fmaf((float)t3, 16777216.0f,
+                                  fmaf((float)t2, 65536.0f, fmaf((float)t1, 256.0f, (float)t0)));
+                    iv[nt] = lds_f32(rec + inv_off(NT) + 4 * b);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (++s == kStages) {
+                s = 0;
+                ph ^= 1;
+            }
+            // recombine the digits: this thread's two columns, then across the
+            // threads that hold the same sequence (butterfly: keep the owned row)
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+                const float f0 = fmaf((float)S[nt][1], w_hi, (float)S[nt][0] * w_lo);
+                const float f1 = fmaf((float)S[nt][3], w_hi, (float)S[nt][2] * w_lo);
+                float v = ((t & 1) ? f1 : f0) + __shfl_xor_sync(0xffffffffu, (t & 1) ? f0 : f1, 1);
+                if (NB == 1) v += __shfl_xor_sync(0xffffffffu, v, 2);
+                acc[nt] = fmaf(fmaf(dd, v, kMin * dmin * mt[nt]), iv[nt], acc[nt]);
             }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        if (++s == kStages) {
-            s = 0;
-            ph ^= 1;
-        }
-        // recombine the digits: this thread's two columns, then across the
-        // threads that hold the same sequence (butterfly: keep the owned row)
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++) {
-            const float f0 = fmaf((float)S[nt][1], w_hi, (float)S[nt][0] * w_lo);
-            const float f1 = fmaf((float)S[nt][3], w_hi, (float)S[nt][2] * w_lo);
-            float v = ((t & 1) ? f1 : f0) + __shfl_xor_sync(0xffffffffu, (t & 1) ? f0 : f1, 1);
-            if (NB == 1) v += __shfl_xor_sync(0xffffffffu, v, 2);
-            acc[nt] = fmaf(fmaf(dd, v, kMin * dmin * mt[nt]), iv[nt], acc[nt]);
-        }
-        // unit n ends a tile, or this CTA's range
-        if (eu == a.units - 1 || n == nunits - 1) {
-            const bool head_cut = (et == tile0) && (u0 != 0);
-            const bool tail_cut = (n == nunits - 1) && (eu != a.units - 1);
-            finish_tile<NB>(a, r_own, t, et, cta, C, total, head_cut || tail_cut, et == tile0 ? 0 : 1, acc,
-                            bcast);
-#pragma unroll
-            for (int nt = 0; nt < NT; nt++) acc[nt] = 0.f;
-        }
-        if (++eu == a.units) {
-            eu = 0;
-            et++;
-        }
+        n += seg;
+        const bool head_cut = (et == tile0) && (u0 != 0);
+        const bool tail_cut = eu + seg != a.units;
+        finish_subtile<NB>(a, r_own, t, warp, et, cta, C, total, head_cut || tail_cut, et == tile0 ? 0 : 1,
+                           acc);
+        et++;
+        eu = 0;
     }
 }
 

@@ -13,10 +13,14 @@ constexpr int kMaxNB = 8;  // sequences per call
 // unit u and sequence b, X = rint(x * 2^e) with e chosen so |X| <= 2^22, and
 // X is split into balanced digits, each an int8 column of the MMA's B
 // operand:
-//   batch 1:  6 base-16 digits d_i in [-8, 7], X = sum d_i 16^i, column i
-//             (columns 6, 7 zero).  The low-nibble positions carry 16 d_i, so
-//             the MMA can take the weights' high nibbles as 16 * q without a
-//             shift: every product is 16 * q * d_i.
+//   batch 1:  6 balanced base-15 digits d_i in [-7, 7], X = sum d_i 15^i,
+//             column i (columns 6, 7 zero).  Quant byte 4t+i of a sub-block
+//             holds the nibbles of positions p = 4t+i (low) and p' = 16+4t+i
+//             (high).  The MMA's A operand takes the raw byte lo + 16 hi in
+//             k-slot 4t+i (no unpacking) and lo in k-slot 16+4t+i; B holds
+//             d(p') in k-slot 4t+i and 16 d(p) - d(p') (|.| <= 119) in k-slot
+//             16+4t+i, so the lo * d(p') terms cancel and each column sums to
+//             16 * sum_p q_p d_i(p).
 //   batch >1: 3 base-256 digits, X = sum d_i 256^i, column 4b + i (column
 //             4b + 3 zero).
 // Record of unit u (rec_bytes(NT) bytes, NT = n-tiles of 8 columns):
@@ -59,25 +63,33 @@ __device__ __forceinline__ void emit_i8(const float (&v)[8], int u, int b, int b
         xsum += X[i];
     }
     // column n of this lane's sub-block c: word b0 (low-nibble positions) and b1
+    // b0: k-slots 4t+0..3, b1: k-slots 16+4t+0..3 of column n
     auto put = [&](int n, uint32_t b0, uint32_t b1) {
         const int nt = n >> 3, L = (n & 7) * 4 + t;
         *reinterpret_cast<uint2*>(reg + ((size_t)(c * NT + nt) * 32 + L) * 8) = make_uint2(b0, b1);
     };
     if (batch == 1) {
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            // digit i of X: balanced base 16
-            uint32_t w0 = 0, w1 = 0;
+        for (int i = 0; i < 6; i++) {
+            // digit i of X: balanced base 15
+            int d[8];
 #pragma unroll
             for (int k = 0; k < 8; k++) {
-                const int d = ((X[k] + 8) & 15) - 8;
-                X[k] = (X[k] - d) >> 4;
-                if (k < 4) w0 |= (uint32_t)((16 * d) & 255) << (8 * k);
-                else w1 |= (uint32_t)(d & 255) << (8 * (k - 4));
+                int r = X[k] % 15;
+                r += r < 0 ? 15 : 0;
+                d[k] = r > 7 ? r - 15 : r;
+                X[k] = (X[k] - d[k]) / 15;
             }
-            if (i < 6) put(i, w0, w1);
-            else put(i, 0u, 0u);
+            uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                w0 |= (uint32_t)(d[4 + k] & 255) << (8 * k);
+                w1 |= (uint32_t)((16 * d[k] - d[4 + k]) & 255) << (8 * k);
+            }
+            put(i, w0, w1);
         }
+        put(6, 0u, 0u);
+        put(7, 0u, 0u);
     } else {
 #pragma unroll
         for (int i = 0; i < 3; i++) {
