@@ -98,6 +98,19 @@ struct GemvBufs {
     float* xinv;  // [units][nt*4] per-unit 2^-e written by the prep
 };
 
+// Where and in which form a kernel that produces a GEMV's input also
+// writes that input's activation record: kind -1 none, 0 fp16 fragments,
+// 1 fp16 fragments + chunk sums (Q4_K), 2 tcgen05 digit records, 3 integer
+// records (gemv_prep_kind).
+struct PrepTarget {
+    int kind = -1;
+    int nt_count = 1;
+    float step1 = 1.0f;
+    void* xfrag = nullptr;
+    float* xsum = nullptr;
+    float* xinv = nullptr;
+};
+
 struct GemvNeeds {
     size_t xfrag_bytes = 0, xsum_bytes = 0, xinv_bytes = 0, partial_bytes = 0, counters = 0;
 };
@@ -111,9 +124,15 @@ int gemv_run(cn_ctx* ctx, cudaStream_t st, const GemvOp& op, const float* d_x, c
              float* d_y);
 int gemv_reserve(const GemvPlan& p, GemvNeeds* n);
 // RMSNorm of `rows` rows of n values into y, and, when op is a tiled GEMV,
-// its activation fragments for op in b (one kernel).
+// its activation records for op in b (one kernel).
 int norm_prep(cudaStream_t st, const float* x, const float* w, float* y, int n, int rows,
               float eps, const GemvOp* op, const GemvBufs& b);
+// Same after a residual add: x_out = x_in + delta (x_out must not alias
+// x_in), then y = RMSNorm(x_out) * w and op's records.
+int add_norm_prep(cudaStream_t st, const float* x_in, const float* delta, float* x_out, const float* w,
+                  float* y, int n, int rows, float eps, const GemvOp* op, const GemvBufs& b);
+// The record target of op in b (kind -1 when op reads plain fp32).
+PrepTarget prep_target(const GemvOp* op, const GemvBufs& b);
 float gemv_step1_scale(int type);
 // Which activation form a GEMV reads: 0 plain fragments, 1 Q4_K fragments
 // (pre-scaled second k-step + chunk sums), 2 tensor-core digit records,
@@ -129,7 +148,6 @@ int gemv_i8_ctas(int sms, int tiles, int units, int batch);
 size_t gemv_i8_xbytes(int64_t cols, int batch);
 size_t gemv_i8_partial_bytes(int ctas);
 int gemv_i8_prepare();
-int gemv_i8_prep(cudaStream_t st, int sms, const float* d_x, int64_t cols, int batch, uint8_t* xrec);
 int gemv_i8_run(cudaStream_t st, uint32_t* err, const CUtensorMap* map, int64_t rows, int64_t cols,
                 int batch, int ctas, const uint8_t* xrec, float* partials, int* counters, float* y);
 
@@ -138,7 +156,6 @@ int gemv_tc_ctas(int sms, int tiles, int units);
 size_t gemv_tc_xbytes(int64_t cols);
 size_t gemv_tc_partial_bytes(int ctas);
 int gemv_tc_prepare();
-int gemv_tc_prep(cudaStream_t st, int sms, const float* d_x, int64_t cols, int batch, uint8_t* xdig);
 int gemv_tc_run(cudaStream_t st, uint32_t* err, const CUtensorMap* map, int64_t rows, int64_t cols,
                 int batch, int ctas, const uint8_t* xdig, float* partials, int* counters, float* y);
 

@@ -32,6 +32,7 @@
 #include "formats.cuh"
 #include "gemv_i8.cuh"
 #include "gemv_tc.cuh"
+#include "prep.cuh"
 
 namespace cn {
 
@@ -559,71 +560,8 @@ __global__ void __launch_bounds__(kThreads, Geo<TYPE, NT>::kMinCtas)
     }
 }
 
-// ---- activation prep ----------------------------------------------------------
-//
-// The GEMVs read x as fp16 fragments.  Each 256-position unit u of each batch
-// row b is scaled by its own power of two 2^e (max |x| over the unit lands in
-// [2^14, 2^15)), which is exact and keeps the fp16 hi + lo split far from
-// overflow and from subnormals whatever the activation range; the GEMV
-// multiplies the unit's partial sums by xinv[u][b] = 2^-e.  Being unit-local,
-// the conversion needs no reduction over the whole vector, so any kernel
-// holding whole units can emit it (the standalone prep and the fused
-// RMSNorm below).
-//
-// Layouts (nt_count n-tiles of 4 batch columns):
-//   xfrag[c][nt][lane]: the four B-fragment registers lane (g, t) feeds the
-//     two k-steps of chunk c; column g = hi (g even) or lo (g odd) part of
-//     batch b = 4*nt + g/2; positions 4t+{0,2}, 4t+{1,3} of each 16-position
-//     half, the second half multiplied by step1 (1/16 for Q4_K, else 1);
-//   xsum[c][b]: fp32 sum of the scaled x over chunk c (Q4_K's dmin term);
-//   xinv[u][b]: 2^-e.
-// Columns of batch rows >= batch are never read back, so they are not written.
-
-// One warp emits unit u of row b.  Lane (c = lane/4, t = lane%4) holds in
-// v[0..3] positions 32c + 4t + 0..3 and in v[4..7] positions 32c + 16 + 4t + 0..3.
-__device__ __forceinline__ void emit_unit(const float (&v)[8], int u, int b, int nt_count,
-                                          float step1, uint4* __restrict__ xfrag,
-                                          float* __restrict__ xsum, float* __restrict__ xinv,
-                                          int lane) {
-    float am = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; i++) am = fmaxf(am, fabsf(v[i]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-    int e = 0;
-    if (am > 0.f && am < INFINITY) e = 14 - ilogbf(am);
-    e = e < -120 ? -120 : (e > 120 ? 120 : e);
-    const float sc = ldexpf(1.0f, e), s1 = sc * step1;
-    const int c = lane >> 2, t = lane & 3;
-    const int nt = b >> 2, gh = 2 * (b & 3);
-    float e8[8] = {v[0] * sc, v[2] * sc, v[1] * sc, v[3] * sc,
-                   v[4] * s1, v[6] * s1, v[5] * s1, v[7] * s1};
-    uint32_t hi[4], lo[4];
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-        __half2 h = __floats2half2_rn(e8[2 * k], e8[2 * k + 1]);
-        float2 back = __half22float2(h);
-        __half2 l = __floats2half2_rn(e8[2 * k] - back.x, e8[2 * k + 1] - back.y);
-        hi[k] = *reinterpret_cast<uint32_t*>(&h);
-        lo[k] = *reinterpret_cast<uint32_t*>(&l);
-    }
-    uint4* dst = xfrag + ((size_t)(8 * u + c) * nt_count + nt) * 32;
-    dst[4 * gh + t] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    dst[4 * (gh + 1) + t] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-    if (xsum) {
-        float ps = ((v[0] * sc + v[1] * sc) + (v[2] * sc + v[3] * sc)) +
-                   ((v[4] * sc + v[5] * sc) + (v[6] * sc + v[7] * sc));
-        ps += __shfl_xor_sync(0xffffffffu, ps, 1);
-        ps += __shfl_xor_sync(0xffffffffu, ps, 2);
-        if (t == 0) xsum[(size_t)(8 * u + c) * nt_count * 4 + b] = ps;
-    }
-    if (lane == 0) xinv[(size_t)u * nt_count * 4 + b] = ldexpf(1.0f, -e);
-}
-
-// Standalone prep: one warp per (unit, batch row).
-__global__ void xprep_kernel(const float* __restrict__ x, int K, int batch, int nt_count,
-                             float step1, uint4* __restrict__ xfrag, float* __restrict__ xsum,
-                             float* __restrict__ xinv) {
+// Standalone prep of any record form: one warp per (unit, batch row).
+__global__ void xprep_kernel(const float* __restrict__ x, int K, int batch, PrepTarget pt) {
     const int lane = threadIdx.x & 31;
     const int units = K / 256;
     const int64_t items = (int64_t)units * batch;
@@ -635,63 +573,71 @@ __global__ void xprep_kernel(const float* __restrict__ x, int K, int batch, int 
         float4 a0 = *reinterpret_cast<const float4*>(p);
         float4 a1 = *reinterpret_cast<const float4*>(p + 16);
         const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-        emit_unit(v, u, b, nt_count, step1, xfrag, xsum, xinv, lane);
+        emit_any(pt, v, u, b, batch, lane);
     }
 }
 
-// RMSNorm (TensorMath.RmsNorm, Tensors/TensorMath.cs:97-165) fused with the
-// prep of its output: one CTA per batch row.  y = x * (1 / sqrt(sum(x^2)/n +
-// eps)) * w, elementwise in the reference's order; y is also stored in fp32.
-constexpr int kNormThreads = 1024;
+// Residual add fused with RMSNorm (TensorMath.Add, Tensors/TensorMath.cs:712-733;
+// TensorMath.RmsNorm, Tensors/TensorMath.cs:97-165) and with the prep of the
+// normalised row for the GEMV that reads it next.  Grid (units, rows): every
+// CTA sums the squares of its whole row (x_in + delta, read from L2), then
+// writes its own 256-value slice of x_out = x_in + delta (when delta is
+// given) and of y = x * (1 / sqrt(sum(x^2)/n + eps)) * w, elementwise in the
+// reference's order, and emits the slice's record.  x_out must not alias
+// x_in (other CTAs still read x_in).
+constexpr int kNormThreads = 256;
 
 __global__ void __launch_bounds__(kNormThreads)
-    norm_prep_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ y,
-                     int n, float eps, int emit, int nt_count, float step1,
-                     uint4* __restrict__ xfrag, float* __restrict__ xsum, float* __restrict__ xinv) {
-    // emit: 0 = y only, 1 = y + mma.sync fragments, 2 = y + tensor-core digit
-    // records, 3 = y + integer-GEMV records
-    __shared__ float red[32];
-    const int b = blockIdx.x;
-    const float* xr = x + (size_t)b * n;
-    float* yr = y + (size_t)b * n;
+    add_norm_prep_kernel(const float* __restrict__ x_in, const float* __restrict__ delta,
+                         float* __restrict__ x_out, const float* __restrict__ w, float* __restrict__ y,
+                         int n, float eps, PrepTarget pt) {
+    __shared__ float red[kNormThreads / 32];
+    __shared__ __align__(16) float vals[256];
+    const int u = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const float* xr = x_in + (size_t)b * n;
+    const float* dr = delta ? delta + (size_t)b * n : nullptr;
     float ss = 0.f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+    for (int i = 4 * tid; i < n; i += 4 * kNormThreads) {
+        float4 v = *reinterpret_cast<const float4*>(xr + i);
+        if (dr) {
+            const float4 d = *reinterpret_cast<const float4*>(dr + i);
+            v.x = __fadd_rn(v.x, d.x);
+            v.y = __fadd_rn(v.y, d.y);
+            v.z = __fadd_rn(v.z, d.z);
+            v.w = __fadd_rn(v.w, d.w);
+        }
+        ss = fmaf(v.x, v.x, ss);
+        ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss);
+        ss = fmaf(v.w, v.w, ss);
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
     __syncthreads();
     ss = 0.f;
-    for (int i = 0; i < (int)(blockDim.x >> 5); i++) ss += red[i];
+#pragma unroll
+    for (int i = 0; i < kNormThreads / 32; i++) ss += red[i];
     const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
-    if (!emit) {
-        for (int i = threadIdx.x; i < n; i += blockDim.x)
-            yr[i] = __fmul_rn(__fmul_rn(xr[i], rms), w[i]);
-        return;
+    const int i = u * 256 + tid;
+    if (i < n) {
+        float v = xr[i];
+        if (dr) {
+            v = __fadd_rn(v, dr[i]);
+            x_out[(size_t)b * n + i] = v;
+        }
+        const float o = __fmul_rn(__fmul_rn(v, rms), w[i]);
+        y[(size_t)b * n + i] = o;
+        vals[tid] = o;
     }
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
-    for (int u = warp; u < n / 256; u += nwarp) {
-        const int off = u * 256 + (lane >> 2) * 32 + 4 * (lane & 3);
-        float4 a0 = *reinterpret_cast<const float4*>(xr + off);
-        float4 a1 = *reinterpret_cast<const float4*>(xr + off + 16);
-        float4 w0 = *reinterpret_cast<const float4*>(w + off);
-        float4 w1 = *reinterpret_cast<const float4*>(w + off + 16);
-        float v[8];
-        v[0] = __fmul_rn(__fmul_rn(a0.x, rms), w0.x);
-        v[1] = __fmul_rn(__fmul_rn(a0.y, rms), w0.y);
-        v[2] = __fmul_rn(__fmul_rn(a0.z, rms), w0.z);
-        v[3] = __fmul_rn(__fmul_rn(a0.w, rms), w0.w);
-        v[4] = __fmul_rn(__fmul_rn(a1.x, rms), w1.x);
-        v[5] = __fmul_rn(__fmul_rn(a1.y, rms), w1.y);
-        v[6] = __fmul_rn(__fmul_rn(a1.z, rms), w1.z);
-        v[7] = __fmul_rn(__fmul_rn(a1.w, rms), w1.w);
-        *reinterpret_cast<float4*>(yr + off) = make_float4(v[0], v[1], v[2], v[3]);
-        *reinterpret_cast<float4*>(yr + off + 16) = make_float4(v[4], v[5], v[6], v[7]);
-        if (emit == 3)
-            i8::emit_i8(v, u, b, (int)gridDim.x, reinterpret_cast<uint8_t*>(xfrag), lane);
-        else if (emit == 2)
-            tc::emit_digits(v, u, b, (int)gridDim.x, reinterpret_cast<uint8_t*>(xfrag), lane);
-        else
-            emit_unit(v, u, b, nt_count, step1, xfrag, xsum, xinv, lane);
+    if (pt.kind < 0) return;
+    __syncthreads();
+    if (tid < 32) {
+        const int c = tid >> 2, t = tid & 3;
+        const float4 a0 = *reinterpret_cast<const float4*>(vals + 32 * c + 4 * t);
+        const float4 a1 = *reinterpret_cast<const float4*>(vals + 32 * c + 16 + 4 * t);
+        const float v8[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        emit_any(pt, v8, u, b, (int)gridDim.y, tid);
     }
 }
 
@@ -963,34 +909,47 @@ int gemv_q4k_path() {
     return path;
 }
 
+PrepTarget prep_target(const GemvOp* op, const GemvBufs& b) {
+    PrepTarget pt;
+    if (!op || !op->tma) return pt;
+    pt.kind = gemv_prep_kind(*op);
+    pt.nt_count = op->plan.nt;
+    pt.step1 = gemv_step1_scale(op->type);
+    pt.xfrag = b.xfrag;
+    pt.xsum = op->type == CN_TYPE_Q4_K ? b.xsum : nullptr;
+    pt.xinv = b.xinv;
+    return pt;
+}
+
 int gemv_prep(cudaStream_t st, int sms, const GemvOp& op, const float* d_x, const GemvBufs& b) {
     if (!op.tma) return CN_OK;
-    if (op.plan.path == kPathI8)
-        return gemv_i8_prep(st, sms, d_x, op.cols, op.batch, reinterpret_cast<uint8_t*>(b.xfrag));
-    if (op.plan.path == kPathTc)
-        return gemv_tc_prep(st, sms, d_x, op.cols, op.batch, reinterpret_cast<uint8_t*>(b.xfrag));
     CN_CHECK((reinterpret_cast<uintptr_t>(d_x) & 15) == 0, CN_ERR_INVALID_ARG,
              "x must be 16-byte aligned");
     const int64_t items = (int64_t)op.plan.units * op.batch;
     int blocks = (int)((items + 7) / 8);
     if (blocks > sms * 8) blocks = sms * 8;
-    xprep_kernel<<<blocks, 256, 0, st>>>(d_x, (int)op.cols, op.batch, op.plan.nt,
-                                         gemv_step1_scale(op.type), b.xfrag,
-                                         op.type == CN_TYPE_Q4_K ? b.xsum : nullptr, b.xinv);
+    xprep_kernel<<<blocks, 256, 0, st>>>(d_x, (int)op.cols, op.batch, prep_target(&op, b));
+    CN_CUDA(cudaGetLastError());
+    return CN_OK;
+}
+
+int add_norm_prep(cudaStream_t st, const float* x_in, const float* delta, float* x_out, const float* w,
+                  float* y, int n, int rows, float eps, const GemvOp* op, const GemvBufs& b) {
+    CN_CHECK(n % 4 == 0 && (reinterpret_cast<uintptr_t>(x_in) & 15) == 0 &&
+                 (!delta || (reinterpret_cast<uintptr_t>(delta) & 15) == 0),
+             CN_ERR_INVALID_ARG, "norm: dim must be a multiple of 4 and rows 16-byte aligned");
+    CN_CHECK(!delta || (x_out && x_out != x_in), CN_ERR_INVALID_ARG, "norm: x_out must not alias x_in");
+    PrepTarget pt = prep_target(op, b);
+    if (pt.kind >= 0 && n % 256 != 0) pt.kind = -1;  // the GEMV preps for itself
+    add_norm_prep_kernel<<<dim3((n + 255) / 256, rows), kNormThreads, 0, st>>>(x_in, delta, x_out, w, y, n,
+                                                                              eps, pt);
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }
 
 int norm_prep(cudaStream_t st, const float* x, const float* w, float* y, int n, int rows,
               float eps, const GemvOp* op, const GemvBufs& b) {
-    const bool emit = op && op->tma;
-    norm_prep_kernel<<<rows, kNormThreads, 0, st>>>(
-        x, w, y, n, eps, emit ? (op->plan.path == kPathI8 ? 3 : op->plan.path == kPathTc ? 2 : 1) : 0,
-        emit ? op->plan.nt : 1,
-        emit ? gemv_step1_scale(op->type) : 1.0f, emit ? b.xfrag : nullptr,
-        emit && op->type == CN_TYPE_Q4_K ? b.xsum : nullptr, emit ? b.xinv : nullptr);
-    CN_CUDA(cudaGetLastError());
-    return CN_OK;
+    return add_norm_prep(st, x, nullptr, nullptr, w, y, n, rows, eps, op, b);
 }
 
 int gemv_run(cn_ctx* ctx, cudaStream_t st, const GemvOp& op, const float* d_x, const GemvBufs& b,

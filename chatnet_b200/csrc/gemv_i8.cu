@@ -363,23 +363,6 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB>::kCtasPerSm)
     }
 }
 
-// Standalone activation prep: one warp per (unit, sequence).
-__global__ void xrec_i8_kernel(const float* __restrict__ x, int K, int batch, uint8_t* __restrict__ out) {
-    const int lane = threadIdx.x & 31;
-    const int units = K / 256;
-    const int64_t items = (int64_t)units * batch;
-    const int64_t w0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    for (int64_t it = w0; it < items; it += nw) {
-        const int u = (int)(it % units), b = (int)(it / units);
-        const float* p = x + (size_t)b * K + (size_t)u * 256 + (lane >> 2) * 32 + 4 * (lane & 3);
-        const float4 a0 = *reinterpret_cast<const float4*>(p);
-        const float4 a1 = *reinterpret_cast<const float4*>(p + 16);
-        const float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-        i8::emit_i8(v, u, b, batch, out, lane);
-    }
-}
-
 // ---- host ---------------------------------------------------------------------------
 
 int gemv_i8_ctas(int sms, int tiles, int units, int batch) {
@@ -408,17 +391,6 @@ int gemv_i8_prepare() {
     CN_ATTR(1) CN_ATTR(2) CN_ATTR(3) CN_ATTR(4) CN_ATTR(5) CN_ATTR(6) CN_ATTR(7) CN_ATTR(8)
 #undef CN_ATTR
     done[dev & 63] = true;
-    return CN_OK;
-}
-
-int gemv_i8_prep(cudaStream_t st, int sms, const float* d_x, int64_t cols, int batch, uint8_t* xrec) {
-    CN_CHECK((reinterpret_cast<uintptr_t>(d_x) & 15) == 0, CN_ERR_INVALID_ARG, "x must be 16-byte aligned");
-    CN_CHECK((reinterpret_cast<uintptr_t>(xrec) & 15) == 0, CN_ERR_INVALID_ARG, "scratch misaligned");
-    const int64_t items = (cols / 256) * batch;
-    int blocks = (int)((items + 7) / 8);
-    if (blocks > sms * 8) blocks = sms * 8;
-    xrec_i8_kernel<<<blocks, 256, 0, st>>>(d_x, (int)cols, batch, xrec);
-    CN_CUDA(cudaGetLastError());
     return CN_OK;
 }
 

@@ -48,8 +48,10 @@ struct cn_llama {
     void* kc = nullptr;
     void* vc = nullptr;
     float2* rope = nullptr;
-    float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr,
-          *tmp = nullptr, *gate = nullptr, *up = nullptr, *logits = nullptr, *part = nullptr;
+    // x / x2: the residual stream, ping-ponged by the fused add + norm
+    float *x = nullptr, *x2 = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr,
+          *att = nullptr, *tmp = nullptr, *gate = nullptr, *up = nullptr, *logits = nullptr, *part = nullptr;
+    int* attn_ctr = nullptr;  // [max_batch][n_kv] attention merge counters
     int *tokens = nullptr, *pos = nullptr, *amax = nullptr;
     int *h_tokens = nullptr, *h_pos = nullptr, *h_amax = nullptr;
     cn::GemvBufs gb{nullptr, nullptr, nullptr, nullptr, nullptr};
@@ -142,13 +144,19 @@ static int gemv(cn_llama* m, cudaStream_t s, const GemvOp& op, const float* x, f
     return gemv_run(m->ctx, s, op, x, m->gb, y);
 }
 
-// RMSNorm of x into xn, emitting the fragments of the GEMV that reads xn next.
-static int norm(cn_llama* m, cudaStream_t s, const cn_tensor* w, int B, const GemvOp& next,
-                PrepCache& pc) {
-    int rc = norm_prep(s, m->x, (const float*)w->d, m->xn, m->cfg.dim, B, m->cfg.rms_eps, &next, m->gb);
+// Residual add of the pending delta (if any) into the stream, RMSNorm into
+// xn, and the records of the GEMV that reads xn next, in one kernel.  *x is
+// the current stream; with a delta it moves to the other buffer.
+static int norm(cn_llama* m, cudaStream_t s, const cn_tensor* w, int B, const GemvOp& next, float** x,
+                const float** delta, PrepCache& pc) {
+    float* out = *delta ? (*x == m->x ? m->x2 : m->x) : nullptr;
+    int rc = add_norm_prep(s, *x, *delta, out, (const float*)w->d, m->xn, m->cfg.dim, B, m->cfg.rms_eps,
+                           &next, m->gb);
     if (rc) return rc;
+    if (*delta) *x = out;
+    *delta = nullptr;
     pc = PrepCache();
-    if (next.tma) pc.set(m->xn, next);
+    if (next.tma && m->cfg.dim % 256 == 0) pc.set(m->xn, next);
     return CN_OK;
 }
 
@@ -163,9 +171,11 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
                           m->ctx->dev_err, s);
     if (rc) return rc;
     PrepCache pc;
+    float* x = m->x;
+    const float* delta = nullptr;  // output of the last projection, not yet added to x
     for (int l = 0; l < c.n_layers; l++) {
         const GemvOp* ops = &st.ops[(size_t)l * 7];
-        if ((rc = norm(m, s, LT(m, l, L_ANORM), B, ops[0], pc))) return rc;
+        if ((rc = norm(m, s, LT(m, l, L_ANORM), B, ops[0], &x, &delta, pc))) return rc;
         if ((rc = gemv(m, s, ops[0], m->xn, m->q, pc))) return rc;
         if ((rc = gemv(m, s, ops[1], m->xn, m->k, pc))) return rc;
         if ((rc = gemv(m, s, ops[2], m->xn, m->v, pc))) return rc;
@@ -206,20 +216,28 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
         aa.kv_f16 = ra.kv_f16;
         aa.ctx_len = c.ctx_len;
         aa.part = m->part;
+        aa.counters = m->attn_ctr;
         aa.out = m->att;
         aa.out_stride = dim;
+        aa.prep = prep_target(&ops[3], m->gb);
+        if ((c.n_heads / c.n_kv_heads) * c.head_dim % 256 != 0) aa.prep.kind = -1;
         if ((rc = launch_attention(aa, st.ap, s))) return rc;
+        pc = PrepCache();
+        if (aa.prep.kind >= 0) pc.set(m->att, ops[3]);
         if ((rc = gemv(m, s, ops[3], m->att, m->tmp, pc))) return rc;
-        if ((rc = launch_add(m->x, m->tmp, (int64_t)B * dim, s))) return rc;
-        if ((rc = norm(m, s, LT(m, l, L_FNORM), B, ops[4], pc))) return rc;
+        delta = m->tmp;
+        if ((rc = norm(m, s, LT(m, l, L_FNORM), B, ops[4], &x, &delta, pc))) return rc;
         if ((rc = gemv(m, s, ops[4], m->xn, m->gate, pc))) return rc;
         if ((rc = gemv(m, s, ops[5], m->xn, m->up, pc))) return rc;
-        if ((rc = launch_silu_mul(m->gate, m->up, (int64_t)B * hid, s))) return rc;
+        const PrepTarget spt = prep_target(&ops[6], m->gb);
+        if ((rc = launch_silu_prep(m->gate, m->up, hid, B, spt, s))) return rc;
+        pc = PrepCache();
+        if (spt.kind >= 0 && hid % 256 == 0) pc.set(m->gate, ops[6]);
         if ((rc = gemv(m, s, ops[6], m->gate, m->tmp, pc))) return rc;
-        if ((rc = launch_add(m->x, m->tmp, (int64_t)B * dim, s))) return rc;
+        delta = m->tmp;
     }
     const GemvOp& head = st.ops[(size_t)c.n_layers * 7];
-    if ((rc = norm(m, s, m->t[T_ONORM], B, head, pc))) return rc;
+    if ((rc = norm(m, s, m->t[T_ONORM], B, head, &x, &delta, pc))) return rc;
     if ((rc = gemv(m, s, head, m->xn, m->logits, pc))) return rc;
     return launch_argmax(m->logits, c.vocab, B, m->amax, s);
 }
@@ -278,7 +296,7 @@ __global__ void kv_synth_kernel(uint64_t seed, int layers, int npos, int ctx, in
 static void free_model(cn_llama* m) {
     for (int b = 0; b <= kMaxBatch; b++)
         if (m->steps[b].graph) cudaGraphExecDestroy(m->steps[b].graph);
-    void* bufs[] = {m->kc, m->vc, m->rope, m->x, m->xn, m->q, m->k, m->v, m->att, m->tmp,
+    void* bufs[] = {m->kc, m->vc, m->rope, m->x, m->x2, m->attn_ctr, m->xn, m->q, m->k, m->v, m->att, m->tmp,
                     m->gate, m->up, m->logits, m->part, m->tokens, m->pos, m->amax,
                     m->gb.xfrag, m->gb.xsum, m->gb.partials, m->gb.counters, m->gb.xinv};
     for (void* p : bufs) cudaFree(p);
@@ -372,7 +390,9 @@ int cn_llama_create(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* const* t
         if (e != cudaSuccess) return fail(cuda_error(e, "rope upload"));
     }
     const size_t fd = (size_t)B * c.dim * 4, fk = (size_t)B * kvd * 4, fh = (size_t)B * c.hidden_dim * 4;
-    if ((rc = dmalloc((void**)&m->x, fd)) || (rc = dmalloc((void**)&m->xn, fd)) ||
+    if ((rc = dmalloc((void**)&m->x, fd)) || (rc = dmalloc((void**)&m->x2, fd)) ||
+        (rc = dmalloc((void**)&m->xn, fd)) ||
+        (rc = dmalloc((void**)&m->attn_ctr, (size_t)B * c.n_kv_heads * sizeof(int))) ||
         (rc = dmalloc((void**)&m->q, fd)) || (rc = dmalloc((void**)&m->k, fk)) ||
         (rc = dmalloc((void**)&m->v, fk)) || (rc = dmalloc((void**)&m->att, fd)) ||
         (rc = dmalloc((void**)&m->tmp, fd)) || (rc = dmalloc((void**)&m->gate, fh)) ||

@@ -4,8 +4,9 @@
 //   rope_kv_kernel     TensorMath.ApplyRoPE + the KV-cache store
 //                      (TensorMath.cs:408-458, Models/Llama/LlamaModel.cs:146-153)
 //   attn_split_kernel  LlamaModel.ComputeAttention + TensorMath.Softmax
-//   attn_combine_kernel   (LlamaModel.cs:241-346, TensorMath.cs:177-241), split over
-//                      the context (flash-decoding) and merged exactly once
+//                      (LlamaModel.cs:241-346, TensorMath.cs:177-241), split over
+//                      the context (flash-decoding); the last split CTA of each
+//                      (sequence, kv head) merges the splits
 //   silu_mul_kernel    TensorMath.SiluElementwiseMul (TensorMath.cs:253-286)
 //   add_kernel         TensorMath.Add                (TensorMath.cs:712-733)
 //   embed_kernel       LlamaModel.LoadEmbedding      (LlamaModel.cs:365-394)
@@ -21,6 +22,7 @@
 #include "cn_internal.h"
 #include "formats.cuh"
 #include "ops.h"
+#include "prep.cuh"
 
 namespace cn {
 
@@ -185,10 +187,13 @@ __global__ void __launch_bounds__(kAttnThreads)
                       const KV* __restrict__ vcache, const int* __restrict__ pos_dev, int pos_host,
                       int n_heads, int n_kv, int hd, int q_stride, int64_t cache_seq_stride,
                       int64_t cache_layer_off, int ctx_len, int splits, int chunk, float scale,
-                      float* __restrict__ part /* [b][head][split][hd + 2] */) {
+                      float* __restrict__ part /* [b][head][split][hd + 4] */, int* __restrict__ counters,
+                      float* __restrict__ out, int out_stride, PrepTarget pt) {
     extern __shared__ __align__(16) float sm[];
+    __shared__ int s_last;
     const int s = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
     const int kv_mul = n_heads / n_kv;
+    const int prow = hd + 4;  // floats per partial row: o[hd], m, l, pad
     int pos = pos_dev ? pos_dev[b] : pos_host;
     if (pos < 0 || pos >= ctx_len) pos = -1;  // rejected upstream; read nothing
     const int seq = pos + 1;
@@ -200,121 +205,173 @@ __global__ void __launch_bounds__(kAttnThreads)
     KV* ks = reinterpret_cast<KV*>(qs + kv_mul * qrow);
     KV* vs = ks + chunk * krow;
     float* sc = reinterpret_cast<float*>(vs + chunk * hd);
-    float* red = sc + kv_mul * chunk;
     const int tid = threadIdx.x;
     const int kvdim = n_kv * hd;
     const int lane = tid & 31, warp = tid >> 5, nwarp = blockDim.x >> 5;
-    float* pr_base = part + ((size_t)b * n_heads + kh * kv_mul) * splits * (hd + 2);
+    float* pr_base = part + ((size_t)b * n_heads + kh * kv_mul) * splits * prow;
 
-    if (L == 0) {  // nothing of this split is inside 0..pos
-        for (int e = tid; e < kv_mul * (hd + 2); e += blockDim.x) {
-            const int g = e / (hd + 2), d = e % (hd + 2);
-            pr_base[((size_t)g * splits + s) * (hd + 2) + d] = d == hd ? -FLT_MAX : 0.f;
+    if (L == 0) {  // nothing of this split is inside 0..pos: an empty partial
+        for (int e = tid; e < kv_mul * prow; e += blockDim.x) {
+            const int g = e / prow, d = e % prow;
+            pr_base[((size_t)g * splits + s) * prow + d] = d == hd ? -FLT_MAX : 0.f;
         }
-        return;
-    }
-    // stage q (fp32) and the K / V rows of the chunk (16-byte loads)
-    for (int i = tid; i < kv_mul * hd; i += blockDim.x)
-        qs[(i / hd) * qrow + i % hd] = q[(size_t)b * q_stride + (kh * kv_mul) * hd + i];
-    constexpr int P16 = KvVec<KV>::kPer16;
-    const int vec_per_row = hd / P16;
-    const KV* kbase = kcache + (int64_t)b * cache_seq_stride + cache_layer_off + kh * hd;
-    const KV* vbase = vcache + (int64_t)b * cache_seq_stride + cache_layer_off + kh * hd;
-    for (int i = tid; i < L * vec_per_row; i += blockDim.x) {
-        const int r = i / vec_per_row, c = i % vec_per_row;
-        const int64_t g = (int64_t)(p0 + r) * kvdim + c * P16;
-        *reinterpret_cast<uint4*>(ks + r * krow + c * P16) = __ldg(reinterpret_cast<const uint4*>(kbase + g));
-        *reinterpret_cast<uint4*>(vs + r * hd + c * P16) = __ldg(reinterpret_cast<const uint4*>(vbase + g));
-    }
-    __syncthreads();
-    // scores: one (position, head) dot product per thread-iteration
-    for (int e = tid; e < L * kv_mul; e += blockDim.x) {
-        const int p = e / kv_mul, g = e % kv_mul;
-        const KV* kr = ks + p * krow;
-        const float* qr = qs + g * qrow;
-        float acc = 0.f;
-        for (int d = 0; d < hd; d += P16) {
-            float kf[P16];
-            KvVec<KV>::to_float(*reinterpret_cast<const uint4*>(kr + d), kf);
+    } else {
+        // stage q (fp32) and the K / V rows of the chunk (16-byte loads)
+        for (int i = tid; i < kv_mul * hd; i += blockDim.x)
+            qs[(i / hd) * qrow + i % hd] = q[(size_t)b * q_stride + (kh * kv_mul) * hd + i];
+        constexpr int P16 = KvVec<KV>::kPer16;
+        const int vec_per_row = hd / P16;
+        const KV* kbase = kcache + (int64_t)b * cache_seq_stride + cache_layer_off + kh * hd;
+        const KV* vbase = vcache + (int64_t)b * cache_seq_stride + cache_layer_off + kh * hd;
+        for (int i = tid; i < L * vec_per_row; i += blockDim.x) {
+            const int r = i / vec_per_row, c = i % vec_per_row;
+            const int64_t g = (int64_t)(p0 + r) * kvdim + c * P16;
+            *reinterpret_cast<uint4*>(ks + r * krow + c * P16) = __ldg(reinterpret_cast<const uint4*>(kbase + g));
+            *reinterpret_cast<uint4*>(vs + r * hd + c * P16) = __ldg(reinterpret_cast<const uint4*>(vbase + g));
+        }
+        __syncthreads();
+        // scores: one (position, head) dot product per thread-iteration
+        for (int e = tid; e < L * kv_mul; e += blockDim.x) {
+            const int p = e / kv_mul, g = e % kv_mul;
+            const KV* kr = ks + p * krow;
+            const float* qr = qs + g * qrow;
+            float acc = 0.f;
+            for (int d = 0; d < hd; d += P16) {
+                float kf[P16];
+                KvVec<KV>::to_float(*reinterpret_cast<const uint4*>(kr + d), kf);
 #pragma unroll
-            for (int j = 0; j < P16; j++) acc = fmaf(qr[d + j], kf[j], acc);
+                for (int j = 0; j < P16; j++) acc = fmaf(qr[d + j], kf[j], acc);
+            }
+            sc[g * chunk + p] = __fmul_rn(acc, scale);
         }
-        sc[g * chunk + p] = __fmul_rn(acc, scale);
+        __syncthreads();
+        // softmax statistics per head: warp w handles heads w, w + nwarp, ...
+        for (int g = warp; g < kv_mul; g += nwarp) {
+            float m = -FLT_MAX;
+            for (int p = lane; p < L; p += 32) m = fmaxf(m, sc[g * chunk + p]);
+            m = warp_max(m);
+            float l = 0.f;
+            for (int p = lane; p < L; p += 32) {
+                float ev = expf(sc[g * chunk + p] - m);
+                sc[g * chunk + p] = ev;
+                l += ev;
+            }
+            l = warp_sum(l);
+            if (lane == 0) {
+                float* pr = pr_base + ((size_t)g * splits + s) * prow;
+                pr[hd] = m;
+                pr[hd + 1] = l;
+            }
+        }
+        __syncthreads();
+        // o[g][d] = sum_p e[g][p] v[p][d], four consecutive d per thread
+        for (int e = tid; e < kv_mul * (hd / 4); e += blockDim.x) {
+            const int g = e / (hd / 4), d = (e % (hd / 4)) * 4;
+            const float* er = sc + g * chunk;
+            float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+            for (int p = 0; p < L; p++) {
+                const float w = er[p];
+                const KV* vr = vs + p * hd + d;
+                float v4[4];
+                if constexpr (sizeof(KV) == 2) {
+                    float2 a = __half22float2(*reinterpret_cast<const __half2*>(vr));
+                    float2 c = __half22float2(*reinterpret_cast<const __half2*>(vr + 2));
+                    v4[0] = a.x; v4[1] = a.y; v4[2] = c.x; v4[3] = c.y;
+                } else {
+                    float4 f = *reinterpret_cast<const float4*>(vr);
+                    v4[0] = f.x; v4[1] = f.y; v4[2] = f.z; v4[3] = f.w;
+                }
+                o0 = fmaf(w, v4[0], o0);
+                o1 = fmaf(w, v4[1], o1);
+                o2 = fmaf(w, v4[2], o2);
+                o3 = fmaf(w, v4[3], o3);
+            }
+            *reinterpret_cast<float4*>(pr_base + ((size_t)g * splits + s) * prow + d) = make_float4(o0, o1, o2, o3);
+        }
+    }
+
+    // The last split of (b, kv head) to finish merges all splits (the
+    // barrier orders the CTA's partials before thread 0's release; the last
+    // arrival's acquire, then the barrier, orders everyone's partials before
+    // the merge reads them).
+    __syncthreads();
+    if (tid == 0) {
+        int old;
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                     : "=r"(old)
+                     : "l"(counters + b * n_kv + kh)
+                     : "memory");
+        s_last = old == splits - 1;
     }
     __syncthreads();
-    // softmax statistics per head: warp w handles heads w, w + nwarp, ...
+    if (!s_last) return;
+
+    // Merge (LlamaModel.cs:241-346, TensorMath.cs:177-241, split form):
+    // w_s = exp(m_s - M), out[d] = sum_s w_s o_s[d] * (1 / sum_s w_s l_s).
+    float* wsm = sm;                                    // [kv_mul][splits]
+    float* linv = wsm + ((kv_mul * splits + 3) & ~3);  // [kv_mul]
+    float* obuf = linv + ((kv_mul + 3) & ~3);           // [kv_mul * hd], 16-byte aligned
     for (int g = warp; g < kv_mul; g += nwarp) {
-        float m = -FLT_MAX;
-        for (int p = lane; p < L; p += 32) m = fmaxf(m, sc[g * chunk + p]);
-        m = warp_max(m);
-        float l = 0.f;
-        for (int p = lane; p < L; p += 32) {
-            float ev = expf(sc[g * chunk + p] - m);
-            sc[g * chunk + p] = ev;
-            l += ev;
+        const float* pr = pr_base + (size_t)g * splits * prow;
+        float M = -FLT_MAX;
+        for (int t = lane; t < splits; t += 32) M = fmaxf(M, __ldcg(pr + (size_t)t * prow + hd));
+        M = warp_max(M);
+        float lsum = 0.f;
+        for (int t = lane; t < splits; t += 32) {
+            const float m = __ldcg(pr + (size_t)t * prow + hd);
+            const float w = m > -FLT_MAX ? expf(m - M) : 0.f;
+            wsm[g * splits + t] = w;
+            lsum += w * __ldcg(pr + (size_t)t * prow + hd + 1);
         }
-        l = warp_sum(l);
-        if (lane == 0) {
-            float* pr = pr_base + ((size_t)g * splits + s) * (hd + 2);
-            pr[hd] = m;
-            pr[hd + 1] = l;
-        }
+        lsum = warp_sum(lsum);
+        if (lane == 0) linv[g] = 1.0f / lsum;
     }
     __syncthreads();
-    // o[g][d] = sum_p e[g][p] v[p][d], four consecutive d per thread
     for (int e = tid; e < kv_mul * (hd / 4); e += blockDim.x) {
         const int g = e / (hd / 4), d = (e % (hd / 4)) * 4;
-        const float* er = sc + g * chunk;
-        float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
-        for (int p = 0; p < L; p++) {
-            const float w = er[p];
-            const KV* vr = vs + p * hd + d;
-            float v4[4];
-            if constexpr (sizeof(KV) == 2) {
-                float2 a = __half22float2(*reinterpret_cast<const __half2*>(vr));
-                float2 c = __half22float2(*reinterpret_cast<const __half2*>(vr + 2));
-                v4[0] = a.x; v4[1] = a.y; v4[2] = c.x; v4[3] = c.y;
-            } else {
-                float4 f = *reinterpret_cast<const float4*>(vr);
-                v4[0] = f.x; v4[1] = f.y; v4[2] = f.z; v4[3] = f.w;
+        const float* pr = pr_base + (size_t)g * splits * prow + d;
+        const float* wr = wsm + g * splits;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        int t = 0;
+        for (; t + 4 <= splits; t += 4) {  // four independent loads in flight
+            float4 v[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) v[k] = __ldcg(reinterpret_cast<const float4*>(pr + (size_t)(t + k) * prow));
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float w = wr[t + k];
+                o.x = fmaf(w, v[k].x, o.x);
+                o.y = fmaf(w, v[k].y, o.y);
+                o.z = fmaf(w, v[k].z, o.z);
+                o.w = fmaf(w, v[k].w, o.w);
             }
-            o0 = fmaf(w, v4[0], o0);
-            o1 = fmaf(w, v4[1], o1);
-            o2 = fmaf(w, v4[2], o2);
-            o3 = fmaf(w, v4[3], o3);
         }
-        float* pr = pr_base + ((size_t)g * splits + s) * (hd + 2) + d;
-        pr[0] = o0;
-        pr[1] = o1;
-        pr[2] = o2;
-        pr[3] = o3;
+        for (; t < splits; t++) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(pr + (size_t)t * prow));
+            const float w = wr[t];
+            o.x = fmaf(w, v.x, o.x);
+            o.y = fmaf(w, v.y, o.y);
+            o.z = fmaf(w, v.z, o.z);
+            o.w = fmaf(w, v.w, o.w);
+        }
+        const float li = linv[g];
+        o = make_float4(o.x * li, o.y * li, o.z * li, o.w * li);
+        *reinterpret_cast<float4*>(out + (size_t)b * out_stride + (kh * kv_mul + g) * hd + d) = o;
+        *reinterpret_cast<float4*>(obuf + g * hd + d) = o;
     }
-}
-
-// Merge of the splits of (sequence b, head h): weights w_s = exp(m_s - M)
-// computed once, then out[d] = sum_s w_s o_s[d] / sum_s w_s l_s.
-__global__ void attn_combine_kernel(const float* __restrict__ part, int n_heads, int hd, int splits,
-                                    float* __restrict__ out, int out_stride) {
-    extern __shared__ float wsm[];  // [splits + 1]
-    const int h = blockIdx.x, b = blockIdx.y;
-    const float* pr = part + ((size_t)b * n_heads + h) * splits * (hd + 2);
-    __shared__ float red[32];
-    float M = -FLT_MAX;
-    for (int s = threadIdx.x; s < splits; s += blockDim.x) M = fmaxf(M, pr[s * (hd + 2) + hd]);
-    M = block_max(M, red);
-    float lsum = 0.f;
-    for (int s = threadIdx.x; s < splits; s += blockDim.x) {
-        float m = pr[s * (hd + 2) + hd];
-        float w = m > -FLT_MAX ? expf(m - M) : 0.f;
-        wsm[s] = w;
-        lsum += w * pr[s * (hd + 2) + hd + 1];
-    }
-    lsum = block_sum(lsum, red);
-    const float inv = 1.0f / lsum;
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-        float o = 0.f;
-        for (int s = 0; s < splits; s++) o = fmaf(wsm[s], pr[s * (hd + 2) + d], o);
-        out[(size_t)b * out_stride + h * hd + d] = o * inv;
+    if (tid == 0) counters[b * n_kv + kh] = 0;
+    // the O projection's records: this group's kv_mul * hd outputs are whole
+    // 256-position units (the host passes a record target only then)
+    if (pt.kind < 0) return;
+    __syncthreads();
+    const int units = kv_mul * hd / 256;
+    for (int w = warp; w < units; w += nwarp) {
+        const int c = lane >> 2, t4 = lane & 3;
+        const float* src = obuf + w * 256 + 32 * c + 4 * t4;
+        const float4 a0 = *reinterpret_cast<const float4*>(src);
+        const float4 a1 = *reinterpret_cast<const float4*>(src + 16);
+        const float v8[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        emit_any(pt, v8, kh * units + w, b, (int)gridDim.z, lane);
     }
 }
 
@@ -326,6 +383,38 @@ __global__ void silu_mul_kernel(float* __restrict__ gate, const float* __restric
         float x = gate[i];
         float s = __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
         gate[i] = __fmul_rn(s, up[i]);
+    }
+}
+
+// SiluElementwiseMul fused with the prep of its output: one warp per
+// (256-position unit, row); the lanes hold the values in the record layout.
+__global__ void silu_prep_kernel(float* __restrict__ gate, const float* __restrict__ up, int n, int batch,
+                                 PrepTarget pt) {
+    const int lane = threadIdx.x & 31;
+    const int units = n / 256;
+    const int64_t items = (int64_t)units * batch;
+    const int64_t w0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t it = w0; it < items; it += nw) {
+        const int u = (int)(it % units), b = (int)(it / units);
+        const size_t off = (size_t)b * n + (size_t)u * 256 + (lane >> 2) * 32 + 4 * (lane & 3);
+        float v[8];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            float4 g4 = *reinterpret_cast<const float4*>(gate + off + 16 * h);
+            const float4 u4 = *reinterpret_cast<const float4*>(up + off + 16 * h);
+            float* gv = reinterpret_cast<float*>(&g4);
+            const float* uv = reinterpret_cast<const float*>(&u4);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float x = gv[k];
+                const float s = __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
+                gv[k] = __fmul_rn(s, uv[k]);
+                v[4 * h + k] = gv[k];
+            }
+            *reinterpret_cast<float4*>(gate + off + 16 * h) = g4;
+        }
+        emit_any(pt, v, u, b, batch, lane);
     }
 }
 
@@ -454,20 +543,24 @@ int attention_plan(int n_heads, int n_kv, int hd, int max_seq, int batch, int sm
     CN_CHECK(n_kv > 0 && n_heads % n_kv == 0, CN_ERR_INVALID_ARG, "n_heads %% n_kv_heads != 0");
     CN_CHECK(n_heads / n_kv <= kMaxKvMul, CN_ERR_UNSUPPORTED, "kv_mul > %d", kMaxKvMul);
     CN_CHECK(hd <= kMaxHd && hd % 8 == 0, CN_ERR_UNSUPPORTED, "head_dim %d (needs a multiple of 8)", hd);
-    // about four CTAs per SM in total, chunks of 32..128 positions
-    int want = (4 * sms + batch * n_kv - 1) / (batch * n_kv);
+    // about one CTA per SM in total, chunks of 32..128 positions (the merge
+    // then reads few partials per (sequence, kv head))
+    int want = (sms + batch * n_kv - 1) / (batch * n_kv);
     int chunk = (max_seq + want - 1) / want;
     chunk = (chunk + 31) / 32 * 32;
     if (chunk < 32) chunk = 32;
     if (chunk > 128) chunk = 128;
     p->chunk = chunk;
     p->splits = (max_seq + chunk - 1) / chunk;
-    p->part_floats = (size_t)batch * n_heads * p->splits * (hd + 2);
+    p->part_floats = (size_t)batch * n_heads * p->splits * (hd + 4);
     const int kv_mul = n_heads / n_kv;
     // worst case over both cache types (fp32 rows are the wider ones)
     const size_t q_bytes = (size_t)kv_mul * (hd + 4) * 4;
     const size_t kv_bytes = (size_t)chunk * (attn_krow<float>(hd) + hd) * 4;
-    p->smem = q_bytes + kv_bytes + (size_t)kv_mul * chunk * 4 + 64 * 4;
+    const size_t split_smem = q_bytes + kv_bytes + (size_t)kv_mul * chunk * 4;
+    const size_t merge_smem =
+        (((size_t)kv_mul * p->splits + 3) / 4 * 4 + ((kv_mul + 3) & ~3) + (size_t)kv_mul * hd) * 4;
+    p->smem = split_smem > merge_smem ? split_smem : merge_smem;
     return CN_OK;
 }
 
@@ -482,26 +575,36 @@ int attention_prepare(const AttnPlan& p) {
 int launch_attention(const AttnArgs& a, const AttnPlan& p, cudaStream_t s) {
     dim3 grid(p.splits, a.n_kv, a.batch);
     const float scale = 1.0f / sqrtf((float)a.hd);
+    CN_CHECK(a.out_stride % 4 == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 &&
+                 (reinterpret_cast<uintptr_t>(a.part) & 15) == 0,
+             CN_ERR_INVALID_ARG, "attention: output rows and scratch must be 16-byte aligned");
+    PrepTarget pt = a.prep;
+    if ((a.n_heads / a.n_kv) * a.hd % 256 != 0 || a.out_stride % 4 != 0) pt.kind = -1;
     if (a.kv_f16) {
         attn_split_kernel<__half><<<grid, kAttnThreads, p.smem, s>>>(
             a.q, (const __half*)a.kcache, (const __half*)a.vcache, a.pos_dev, a.pos_host, a.n_heads,
             a.n_kv, a.hd, a.q_stride, a.cache_seq_stride, a.cache_layer_off, a.ctx_len, p.splits,
-            p.chunk, scale, a.part);
+            p.chunk, scale, a.part, a.counters, a.out, a.out_stride, pt);
     } else {
         attn_split_kernel<float><<<grid, kAttnThreads, p.smem, s>>>(
             a.q, (const float*)a.kcache, (const float*)a.vcache, a.pos_dev, a.pos_host, a.n_heads,
             a.n_kv, a.hd, a.q_stride, a.cache_seq_stride, a.cache_layer_off, a.ctx_len, p.splits,
-            p.chunk, scale, a.part);
+            p.chunk, scale, a.part, a.counters, a.out, a.out_stride, pt);
     }
-    CN_CUDA(cudaGetLastError());
-    attn_combine_kernel<<<dim3(a.n_heads, a.batch), 128, (p.splits + 1) * sizeof(float), s>>>(
-        a.part, a.n_heads, a.hd, p.splits, a.out, a.out_stride);
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }
 
 int launch_silu_mul(float* gate, const float* up, int64_t n, cudaStream_t s) {
     silu_mul_kernel<<<grid_1d(n, 256, 148 * 8), 256, 0, s>>>(gate, up, n);
+    CN_CUDA(cudaGetLastError());
+    return CN_OK;
+}
+
+int launch_silu_prep(float* gate, const float* up, int n, int batch, const PrepTarget& pt, cudaStream_t s) {
+    if (pt.kind < 0 || n % 256 != 0) return launch_silu_mul(gate, up, (int64_t)n * batch, s);
+    const int64_t items = (int64_t)(n / 256) * batch;
+    silu_prep_kernel<<<(unsigned)((items + 7) / 8), 256, 0, s>>>(gate, up, n, batch, pt);
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "cn_internal.h"
+
 namespace cn {
 
 struct RopeKvArgs {
@@ -37,8 +39,10 @@ struct AttnArgs {
     int64_t cache_seq_stride, cache_layer_off;
     int kv_f16, ctx_len;
     float* part;     // scratch: AttnPlan::part_floats
+    int* counters;   // [batch][n_kv], zero on entry, left zero
     float* out;      // [batch][out_stride]
     int out_stride;
+    PrepTarget prep;  // the O projection's records (kind -1: none)
 };
 
 int launch_rmsnorm(const float* x, const float* w, float* y, int n, int rows, float eps,
@@ -49,6 +53,10 @@ int attention_plan(int n_heads, int n_kv, int hd, int max_seq, int batch, int sm
 int attention_prepare(const AttnPlan& p);
 int launch_attention(const AttnArgs& a, const AttnPlan& p, cudaStream_t s);
 int launch_silu_mul(float* gate, const float* up, int64_t n, cudaStream_t s);
+// gate = silu(gate) * up for `batch` rows of n values, plus the records of
+// the GEMV that reads the result (falls back to launch_silu_mul when pt has
+// no record form or n is not a multiple of 256).
+int launch_silu_prep(float* gate, const float* up, int n, int batch, const PrepTarget& pt, cudaStream_t s);
 int launch_add(float* a, const float* b, int64_t n, cudaStream_t s);
 int launch_embed(int type, const void* emb, uint64_t row_bytes, const int* tokens, int vocab,
                  int dim, int batch, float* x, uint32_t* err, cudaStream_t s);
