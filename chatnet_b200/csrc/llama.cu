@@ -108,7 +108,8 @@ static int build_step(cn_llama* m, int B) {
         if (rc) return rc;
         st.ops.push_back(op);
     }
-    int rc = attention_plan(c.n_heads, c.n_kv_heads, c.head_dim, c.ctx_len, B, m->ctx->sms, &st.ap);
+    int rc = attention_plan(c.n_heads, c.n_kv_heads, c.head_dim, c.ctx_len, B, m->ctx->sms,
+                            c.kv_dtype == CN_KV_F16, &st.ap);
     if (rc) return rc;
     if ((rc = attention_prepare(st.ap))) return rc;
     st.built = true;
@@ -351,7 +352,7 @@ int cn_llama_create(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* const* t
     {
         AttnPlan ap;
         if ((rc = attention_plan(c.n_heads, c.n_kv_heads, c.head_dim, c.ctx_len, c.max_batch,
-                                 ctx->sms, &ap)))
+                                 ctx->sms, c.kv_dtype == CN_KV_F16, &ap)))
             return rc;
     }
 
@@ -406,7 +407,7 @@ int cn_llama_create(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* const* t
         size_t part = 0;
         for (int b = 1; b <= B; b++) {
             AttnPlan ap;
-            attention_plan(c.n_heads, c.n_kv_heads, c.head_dim, c.ctx_len, b, ctx->sms, &ap);
+            attention_plan(c.n_heads, c.n_kv_heads, c.head_dim, c.ctx_len, b, ctx->sms, c.kv_dtype == CN_KV_F16, &ap);
             if (ap.part_floats > part) part = ap.part_floats;
         }
         if ((rc = dmalloc((void**)&m->part, part * 4))) return fail(rc);

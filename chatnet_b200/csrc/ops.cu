@@ -181,6 +181,100 @@ __host__ __device__ constexpr int attn_krow(int hd) {
     return hd + 16 / (int)sizeof(KV);  // elements per padded K row
 }
 
+// Tail of both attention kernels: counts this split in for (b, kv head) and,
+// in the last split to arrive, merges all splits of the group's heads, writes
+// the attention output and, when pt names a record form, the O projection's
+// records.  `sm` is the CTA's dynamic shared memory (reused), s_last a shared
+// int.  Called by every thread of the CTA.
+__device__ __forceinline__ void attn_finish(float* __restrict__ pr_base, int splits, int prow, int hd, int kv_mul, int n_kv,
+                            int b, int kh, int* __restrict__ counters, float* __restrict__ out,
+                            int out_stride, const PrepTarget& pt, float* sm, int* s_last) {
+    // The last split of (b, kv head) to finish merges all splits (the
+    // barrier orders the CTA's partials before thread 0's release; the last
+    // arrival's acquire, then the barrier, orders everyone's partials before
+    // the merge reads them).
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = blockDim.x >> 5;
+    __syncthreads();
+    if (tid == 0) {
+        int old;
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                     : "=r"(old)
+                     : "l"(counters + b * n_kv + kh)
+                     : "memory");
+        *s_last = old == splits - 1;
+    }
+    __syncthreads();
+    if (!*s_last) return;
+
+    // Merge (LlamaModel.cs:241-346, TensorMath.cs:177-241, split form):
+    // w_s = exp(m_s - M), out[d] = sum_s w_s o_s[d] * (1 / sum_s w_s l_s).
+    float* wsm = sm;                                    // [kv_mul][splits]
+    float* linv = wsm + ((kv_mul * splits + 3) & ~3);  // [kv_mul]
+    float* obuf = linv + ((kv_mul + 3) & ~3);           // [kv_mul * hd], 16-byte aligned
+    for (int g = warp; g < kv_mul; g += nwarp) {
+        const float* pr = pr_base + (size_t)g * splits * prow;
+        float M = -FLT_MAX;
+        for (int t = lane; t < splits; t += 32) M = fmaxf(M, __ldcg(pr + (size_t)t * prow + hd));
+        M = warp_max(M);
+        float lsum = 0.f;
+        for (int t = lane; t < splits; t += 32) {
+            const float m = __ldcg(pr + (size_t)t * prow + hd);
+            const float w = m > -FLT_MAX ? expf(m - M) : 0.f;
+            wsm[g * splits + t] = w;
+            lsum += w * __ldcg(pr + (size_t)t * prow + hd + 1);
+        }
+        lsum = warp_sum(lsum);
+        if (lane == 0) linv[g] = 1.0f / lsum;
+    }
+    __syncthreads();
+    for (int e = tid; e < kv_mul * (hd / 4); e += blockDim.x) {
+        const int g = e / (hd / 4), d = (e % (hd / 4)) * 4;
+        const float* pr = pr_base + (size_t)g * splits * prow + d;
+        const float* wr = wsm + g * splits;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        int t = 0;
+        for (; t + 4 <= splits; t += 4) {  // four independent loads in flight
+            float4 v[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) v[k] = __ldcg(reinterpret_cast<const float4*>(pr + (size_t)(t + k) * prow));
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float w = wr[t + k];
+                o.x = fmaf(w, v[k].x, o.x);
+                o.y = fmaf(w, v[k].y, o.y);
+                o.z = fmaf(w, v[k].z, o.z);
+                o.w = fmaf(w, v[k].w, o.w);
+            }
+        }
+        for (; t < splits; t++) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(pr + (size_t)t * prow));
+            const float w = wr[t];
+            o.x = fmaf(w, v.x, o.x);
+            o.y = fmaf(w, v.y, o.y);
+            o.z = fmaf(w, v.z, o.z);
+            o.w = fmaf(w, v.w, o.w);
+        }
+        const float li = linv[g];
+        o = make_float4(o.x * li, o.y * li, o.z * li, o.w * li);
+        *reinterpret_cast<float4*>(out + (size_t)b * out_stride + (kh * kv_mul + g) * hd + d) = o;
+        *reinterpret_cast<float4*>(obuf + g * hd + d) = o;
+    }
+    if (tid == 0) counters[b * n_kv + kh] = 0;
+    // the O projection's records: this group's kv_mul * hd outputs are whole
+    // 256-position units (the host passes a record target only then)
+    if (pt.kind < 0) return;
+    __syncthreads();
+    const int units = kv_mul * hd / 256;
+    for (int w = warp; w < units; w += nwarp) {
+        const int c = lane >> 2, t4 = lane & 3;
+        const float* src = obuf + w * 256 + 32 * c + 4 * t4;
+        const float4 a0 = *reinterpret_cast<const float4*>(src);
+        const float4 a1 = *reinterpret_cast<const float4*>(src + 16);
+        const float v8[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        emit_any(pt, v8, kh * units + w, b, (int)gridDim.z, lane);
+    }
+}
+
 template <typename KV>
 __global__ void __launch_bounds__(kAttnThreads)
     attn_split_kernel(const float* __restrict__ q, const KV* __restrict__ kcache,
@@ -290,89 +384,194 @@ __global__ void __launch_bounds__(kAttnThreads)
         }
     }
 
-    // The last split of (b, kv head) to finish merges all splits (the
-    // barrier orders the CTA's partials before thread 0's release; the last
-    // arrival's acquire, then the barrier, orders everyone's partials before
-    // the merge reads them).
-    __syncthreads();
-    if (tid == 0) {
-        int old;
-        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
-                     : "=r"(old)
-                     : "l"(counters + b * n_kv + kh)
-                     : "memory");
-        s_last = old == splits - 1;
-    }
-    __syncthreads();
-    if (!s_last) return;
+    attn_finish(pr_base, splits, prow, hd, kv_mul, n_kv, b, kh, counters, out, out_stride, pt, sm, &s_last);
+}
 
-    // Merge (LlamaModel.cs:241-346, TensorMath.cs:177-241, split form):
-    // w_s = exp(m_s - M), out[d] = sum_s w_s o_s[d] * (1 / sum_s w_s l_s).
-    float* wsm = sm;                                    // [kv_mul][splits]
-    float* linv = wsm + ((kv_mul * splits + 3) & ~3);  // [kv_mul]
-    float* obuf = linv + ((kv_mul + 3) & ~3);           // [kv_mul * hd], 16-byte aligned
-    for (int g = warp; g < kv_mul; g += nwarp) {
-        const float* pr = pr_base + (size_t)g * splits * prow;
-        float M = -FLT_MAX;
-        for (int t = lane; t < splits; t += 32) M = fmaxf(M, __ldcg(pr + (size_t)t * prow + hd));
-        M = warp_max(M);
-        float lsum = 0.f;
-        for (int t = lane; t < splits; t += 32) {
-            const float m = __ldcg(pr + (size_t)t * prow + hd);
-            const float w = m > -FLT_MAX ? expf(m - M) : 0.f;
-            wsm[g * splits + t] = w;
-            lsum += w * __ldcg(pr + (size_t)t * prow + hd + 1);
+// ---- attention on the tensor cores (fp16 KV cache) -----------------------------
+//
+// Same math as attn_split_kernel for an fp16 cache with kv_mul <= 8 query heads
+// per kv head and head_dim 64 or 128, but the two contractions run on
+// mma.sync m16n8k16 (fp16 in, fp32 accumulate).  A CTA takes 128 positions
+// (16 per warp) of one (sequence, kv head):
+//   * K / V rows arrive by cp.async into padded shared rows (zero-filled past
+//     the current position);
+//   * the A operand of Q K^T stacks the kv_mul query heads twice: rows 0-7
+//     hold fp16(q), rows 8-15 fp16(q - fp16(q)), so D row g + D row g + 8 is
+//     the score at fp32-level accuracy (K is exact in fp16);
+//   * the score fragments become, in registers, the A operand of P V, again
+//     split into hi and lo halves; V comes in through ldmatrix.trans;
+//   * the warps' partial outputs and exp-sums are added in shared memory and
+//     the split is merged by attn_finish.
+constexpr int kMmaChunk = 128;
+
+__device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm4_trans(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+// 16 bytes global -> shared; src_bytes 0 writes zeros
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ uint32_t half2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads)
+    attn_mma_kernel(const float* __restrict__ q, const __half* __restrict__ kcache,
+                    const __half* __restrict__ vcache, const int* __restrict__ pos_dev, int pos_host,
+                    int n_heads, int n_kv, int q_stride, int64_t cache_seq_stride, int64_t cache_layer_off,
+                    int ctx_len, int splits, float scale, float* __restrict__ part, int* __restrict__ counters,
+                    float* __restrict__ out, int out_stride, PrepTarget pt) {
+    static_assert(kAttnThreads == 256 && kMmaChunk == 16 * (kAttnThreads / 32), "16 positions per warp");
+    constexpr int RS = HD + 8;  // halves per shared row (16-byte pad against bank conflicts)
+    extern __shared__ __align__(16) float sm[];
+    __shared__ int s_last;
+    __shared__ float mx[8][8], ls[8][8];
+    const int s = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
+    const int kv_mul = n_heads / n_kv;
+    const int prow = HD + 4;
+    int pos = pos_dev ? pos_dev[b] : pos_host;
+    if (pos < 0 || pos >= ctx_len) pos = -1;  // rejected upstream; read nothing
+    const int seq = pos + 1;
+    const int p0 = s * kMmaChunk;
+    const int L = max(0, min(seq, p0 + kMmaChunk) - p0);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    float* pr_base = part + ((size_t)b * n_heads + kh * kv_mul) * splits * prow;
+    __half* Ks = reinterpret_cast<__half*>(sm);
+    __half* Vs = Ks + kMmaChunk * RS;
+    __half* Qs = Vs + kMmaChunk * RS;  // [16][RS]
+
+    if (L == 0) {  // nothing of this split is inside 0..pos: an empty partial
+        for (int e = tid; e < kv_mul * prow; e += blockDim.x) {
+            const int gi = e / prow, d = e % prow;
+            pr_base[((size_t)gi * splits + s) * prow + d] = d == HD ? -FLT_MAX : 0.f;
         }
-        lsum = warp_sum(lsum);
-        if (lane == 0) linv[g] = 1.0f / lsum;
-    }
-    __syncthreads();
-    for (int e = tid; e < kv_mul * (hd / 4); e += blockDim.x) {
-        const int g = e / (hd / 4), d = (e % (hd / 4)) * 4;
-        const float* pr = pr_base + (size_t)g * splits * prow + d;
-        const float* wr = wsm + g * splits;
-        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-        int t = 0;
-        for (; t + 4 <= splits; t += 4) {  // four independent loads in flight
-            float4 v[4];
+    } else {
+        const int kvdim = n_kv * HD;
+        const __half* kbase = kcache + (int64_t)b * cache_seq_stride + cache_layer_off + kh * HD;
+        const __half* vbase = vcache + (int64_t)b * cache_seq_stride + cache_layer_off + kh * HD;
+        constexpr int CPR = HD / 8;  // 16-byte chunks per row
+        for (int i = tid; i < kMmaChunk * CPR; i += kAttnThreads) {
+            const int r = i / CPR, c = i % CPR;
+            const bool in = r < L;
+            const int64_t go = (int64_t)(p0 + (in ? r : 0)) * kvdim + c * 8;
+            cp_async16(smem_u32(Ks + r * RS + c * 8), kbase + go, in ? 16 : 0);
+            cp_async16(smem_u32(Vs + r * RS + c * 8), vbase + go, in ? 16 : 0);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        // query heads: fp16 hi in rows 0-7, the fp16 remainder in rows 8-15
+        for (int i = tid; i < 8 * HD; i += kAttnThreads) {
+            const int gi = i / HD, d = i % HD;
+            const float v = gi < kv_mul ? q[(size_t)b * q_stride + (kh * kv_mul + gi) * HD + d] : 0.f;
+            const __half hi = __float2half_rn(v);
+            Qs[gi * RS + d] = hi;
+            Qs[(8 + gi) * RS + d] = __float2half_rn(v - __half2float(hi));
+        }
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncthreads();
+
+        // S = Q K^T for this warp's 16 positions (two n-tiles of 8)
+        const uint32_t qaddr = smem_u32(Qs) + (uint32_t)(((lane & 7) + 8 * ((lane >> 3) & 1)) * RS + 8 * (lane >> 4)) * 2;
+        const uint32_t kaddr =
+            smem_u32(Ks) + (uint32_t)((16 * warp + (lane & 7) + 8 * (lane >> 4)) * RS + 8 * ((lane >> 3) & 1)) * 2;
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-            for (int k = 0; k < 4; k++) v[k] = __ldcg(reinterpret_cast<const float4*>(pr + (size_t)(t + k) * prow));
+        for (int ks = 0; ks < HD / 16; ks++) {
+            uint32_t a[4], kb[4];
+            ldsm4(qaddr + ks * 32, a);
+            ldsm4(kaddr + ks * 32, kb);
+            mma_16816(acc[0], a, kb, acc[0]);
+            mma_16816(acc[1], a, kb + 2, acc[1]);
+        }
+        // scores of head g at positions 16 warp + 8 nt + 2t + e; softmax
+        // statistics over the CTA's positions
+        float sc[2][2];
+        float m = -FLT_MAX;
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const float w = wr[t + k];
-                o.x = fmaf(w, v[k].x, o.x);
-                o.y = fmaf(w, v[k].y, o.y);
-                o.z = fmaf(w, v[k].z, o.z);
-                o.w = fmaf(w, v[k].w, o.w);
+        for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int pl = 16 * warp + 8 * nt + 2 * t + e;
+                const float v = pl < L ? __fmul_rn(acc[nt][e] + acc[nt][2 + e], scale) : -FLT_MAX;
+                sc[nt][e] = v;
+                m = fmaxf(m, v);
             }
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        if (t == 0) mx[warp][g] = m;
+        __syncthreads();
+        float M = mx[0][g];
+#pragma unroll
+        for (int w = 1; w < 8; w++) M = fmaxf(M, mx[w][g]);
+        float pe[2][2], l = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                pe[nt][e] = sc[nt][e] > -FLT_MAX ? expf(sc[nt][e] - M) : 0.f;
+                l += pe[nt][e];
+            }
+        l += __shfl_xor_sync(0xffffffffu, l, 1);
+        l += __shfl_xor_sync(0xffffffffu, l, 2);
+        if (t == 0) ls[warp][g] = l;
+
+        // O = P V: A = P (rows 0-7 fp16(p), rows 8-15 the remainder), k =
+        // this warp's 16 positions, n = head dims in tiles of 8
+        uint32_t pa[4];
+        {
+            const __half2 h0 = __floats2half2_rn(pe[0][0], pe[0][1]);
+            const __half2 h1 = __floats2half2_rn(pe[1][0], pe[1][1]);
+            const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+            pa[0] = half2_bits(h0);
+            pa[1] = half2_bits(__floats2half2_rn(pe[0][0] - f0.x, pe[0][1] - f0.y));
+            pa[2] = half2_bits(h1);
+            pa[3] = half2_bits(__floats2half2_rn(pe[1][0] - f1.x, pe[1][1] - f1.y));
         }
-        for (; t < splits; t++) {
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(pr + (size_t)t * prow));
-            const float w = wr[t];
-            o.x = fmaf(w, v.x, o.x);
-            o.y = fmaf(w, v.y, o.y);
-            o.z = fmaf(w, v.z, o.z);
-            o.w = fmaf(w, v.w, o.w);
+        const uint32_t vaddr =
+            smem_u32(Vs) + (uint32_t)((16 * warp + (lane & 7) + 8 * ((lane >> 3) & 1)) * RS + 8 * (lane >> 4)) * 2;
+        float o[HD / 8][4];
+#pragma unroll
+        for (int n = 0; n < HD / 8; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+#pragma unroll
+        for (int n = 0; n < HD / 8; n += 2) {
+            uint32_t vb[4];
+            ldsm4_trans(vaddr + n * 16, vb);
+            mma_16816(o[n], pa, vb, o[n]);
+            mma_16816(o[n + 1], pa, vb + 2, o[n + 1]);
         }
-        const float li = linv[g];
-        o = make_float4(o.x * li, o.y * li, o.z * li, o.w * li);
-        *reinterpret_cast<float4*>(out + (size_t)b * out_stride + (kh * kv_mul + g) * hd + d) = o;
-        *reinterpret_cast<float4*>(obuf + g * hd + d) = o;
+        // sum the warps' outputs (the K rows are no longer read: every warp
+        // passed the barrier after its scores)
+        float* ob = reinterpret_cast<float*>(Ks);  // [8 warps][8 heads][HD]
+#pragma unroll
+        for (int n = 0; n < HD / 8; n++)
+            *reinterpret_cast<float2*>(ob + (warp * 8 + g) * HD + 8 * n + 2 * t) =
+                make_float2(o[n][0] + o[n][2], o[n][1] + o[n][3]);
+        __syncthreads();
+        for (int i = tid; i < kv_mul * HD; i += kAttnThreads) {
+            const int gi = i / HD, d = i % HD;
+            float sum = 0.f;
+#pragma unroll
+            for (int w = 0; w < 8; w++) sum += ob[(w * 8 + gi) * HD + d];
+            pr_base[((size_t)gi * splits + s) * prow + d] = sum;
+        }
+        if (tid < kv_mul) {
+            float Mh = mx[0][tid], lh = 0.f;
+#pragma unroll
+            for (int w = 1; w < 8; w++) Mh = fmaxf(Mh, mx[w][tid]);
+#pragma unroll
+            for (int w = 0; w < 8; w++) lh += ls[w][tid];
+            pr_base[((size_t)tid * splits + s) * prow + HD] = Mh;
+            pr_base[((size_t)tid * splits + s) * prow + HD + 1] = lh;
+        }
     }
-    if (tid == 0) counters[b * n_kv + kh] = 0;
-    // the O projection's records: this group's kv_mul * hd outputs are whole
-    // 256-position units (the host passes a record target only then)
-    if (pt.kind < 0) return;
-    __syncthreads();
-    const int units = kv_mul * hd / 256;
-    for (int w = warp; w < units; w += nwarp) {
-        const int c = lane >> 2, t4 = lane & 3;
-        const float* src = obuf + w * 256 + 32 * c + 4 * t4;
-        const float4 a0 = *reinterpret_cast<const float4*>(src);
-        const float4 a1 = *reinterpret_cast<const float4*>(src + 16);
-        const float v8[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-        emit_any(pt, v8, kh * units + w, b, (int)gridDim.z, lane);
-    }
+    attn_finish(pr_base, splits, prow, HD, kv_mul, n_kv, b, kh, counters, out, out_stride, pt, sm, &s_last);
 }
 
 // ---- elementwise -----------------------------------------------------------------
@@ -539,28 +738,40 @@ int launch_rope_kv(const RopeKvArgs& a, cudaStream_t s) {
     return CN_OK;
 }
 
-int attention_plan(int n_heads, int n_kv, int hd, int max_seq, int batch, int sms, AttnPlan* p) {
+static bool attn_use_mma(int n_heads, int n_kv, int hd, bool kv_f16) {
+    return kv_f16 && n_heads / n_kv <= 8 && (hd == 64 || hd == 128);
+}
+
+int attention_plan(int n_heads, int n_kv, int hd, int max_seq, int batch, int sms, bool kv_f16, AttnPlan* p) {
     CN_CHECK(n_kv > 0 && n_heads % n_kv == 0, CN_ERR_INVALID_ARG, "n_heads %% n_kv_heads != 0");
     CN_CHECK(n_heads / n_kv <= kMaxKvMul, CN_ERR_UNSUPPORTED, "kv_mul > %d", kMaxKvMul);
     CN_CHECK(hd <= kMaxHd && hd % 8 == 0, CN_ERR_UNSUPPORTED, "head_dim %d (needs a multiple of 8)", hd);
-    // about one CTA per SM in total, chunks of 32..128 positions (the merge
-    // then reads few partials per (sequence, kv head))
-    int want = (sms + batch * n_kv - 1) / (batch * n_kv);
-    int chunk = (max_seq + want - 1) / want;
-    chunk = (chunk + 31) / 32 * 32;
-    if (chunk < 32) chunk = 32;
-    if (chunk > 128) chunk = 128;
+    const int kv_mul = n_heads / n_kv;
+    p->mma = attn_use_mma(n_heads, n_kv, hd, kv_f16);
+    int chunk;
+    if (p->mma) {
+        chunk = kMmaChunk;
+    } else {
+        // about one CTA per SM in total, chunks of 32..128 positions (the
+        // merge then reads few partials per (sequence, kv head))
+        const int want = (sms + batch * n_kv - 1) / (batch * n_kv);
+        chunk = (max_seq + want - 1) / want;
+        chunk = (chunk + 31) / 32 * 32;
+        if (chunk < 32) chunk = 32;
+        if (chunk > 128) chunk = 128;
+    }
     p->chunk = chunk;
     p->splits = (max_seq + chunk - 1) / chunk;
     p->part_floats = (size_t)batch * n_heads * p->splits * (hd + 4);
-    const int kv_mul = n_heads / n_kv;
     // worst case over both cache types (fp32 rows are the wider ones)
     const size_t q_bytes = (size_t)kv_mul * (hd + 4) * 4;
     const size_t kv_bytes = (size_t)chunk * (attn_krow<float>(hd) + hd) * 4;
-    const size_t split_smem = q_bytes + kv_bytes + (size_t)kv_mul * chunk * 4;
+    size_t smem = q_bytes + kv_bytes + (size_t)kv_mul * chunk * 4;
+    const size_t mma_smem = (size_t)(2 * kMmaChunk + 16) * (hd + 8) * 2;
     const size_t merge_smem =
         (((size_t)kv_mul * p->splits + 3) / 4 * 4 + ((kv_mul + 3) & ~3) + (size_t)kv_mul * hd) * 4;
-    p->smem = split_smem > merge_smem ? split_smem : merge_smem;
+    if (p->mma) smem = mma_smem;
+    p->smem = smem > merge_smem ? smem : merge_smem;
     return CN_OK;
 }
 
@@ -569,6 +780,8 @@ int attention_prepare(const AttnPlan& p) {
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
     CN_CUDA(cudaFuncSetAttribute(attn_split_kernel<float>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+    CN_CUDA(cudaFuncSetAttribute(attn_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+    CN_CUDA(cudaFuncSetAttribute(attn_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
     return CN_OK;
 }
 
@@ -580,7 +793,15 @@ int launch_attention(const AttnArgs& a, const AttnPlan& p, cudaStream_t s) {
              CN_ERR_INVALID_ARG, "attention: output rows and scratch must be 16-byte aligned");
     PrepTarget pt = a.prep;
     if ((a.n_heads / a.n_kv) * a.hd % 256 != 0 || a.out_stride % 4 != 0) pt.kind = -1;
-    if (a.kv_f16) {
+    if (p.mma) {
+        CN_CHECK(a.kv_f16 && attn_use_mma(a.n_heads, a.n_kv, a.hd, true) && p.chunk == kMmaChunk,
+                 CN_ERR_INVALID_ARG, "attention plan does not match the call");
+        auto k = a.hd == 64 ? attn_mma_kernel<64> : attn_mma_kernel<128>;
+        k<<<grid, kAttnThreads, p.smem, s>>>(a.q, (const __half*)a.kcache, (const __half*)a.vcache, a.pos_dev,
+                                             a.pos_host, a.n_heads, a.n_kv, a.q_stride, a.cache_seq_stride,
+                                             a.cache_layer_off, a.ctx_len, p.splits, scale, a.part, a.counters,
+                                             a.out, a.out_stride, pt);
+    } else if (a.kv_f16) {
         attn_split_kernel<__half><<<grid, kAttnThreads, p.smem, s>>>(
             a.q, (const __half*)a.kcache, (const __half*)a.vcache, a.pos_dev, a.pos_host, a.n_heads,
             a.n_kv, a.hd, a.q_stride, a.cache_seq_stride, a.cache_layer_off, a.ctx_len, p.splits,

@@ -26,6 +26,7 @@ struct RopeKvArgs {
 
 struct AttnPlan {
     int splits = 0, chunk = 0;
+    bool mma = false;  // tensor-core kernel (fp16 cache, kv_mul <= 8, head_dim 64 or 128)
     size_t part_floats = 0, smem = 0;
 };
 
@@ -48,7 +49,7 @@ struct AttnArgs {
 int launch_rmsnorm(const float* x, const float* w, float* y, int n, int rows, float eps,
                    cudaStream_t s);
 int launch_rope_kv(const RopeKvArgs& a, cudaStream_t s);
-int attention_plan(int n_heads, int n_kv, int hd, int max_seq, int batch, int sms, AttnPlan* p);
+int attention_plan(int n_heads, int n_kv, int hd, int max_seq, int batch, int sms, bool kv_f16, AttnPlan* p);
 // Sets the kernels' shared-memory limit for plan p (call before any capture).
 int attention_prepare(const AttnPlan& p);
 int launch_attention(const AttnArgs& a, const AttnPlan& p, cudaStream_t s);
