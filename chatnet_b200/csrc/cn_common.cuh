@@ -66,6 +66,15 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                  : "memory");
 }
 
+// Programmatic dependent launch.  A kernel launched with launch_k(pdl = true)
+// may start while the previous kernel in the stream is still running: it
+// calls pdl_trigger() early (letting its own successor start) and pdl_wait()
+// before it touches anything the previous kernel writes or reads; pdl_wait
+// returns once that kernel has completed and its memory is visible.  Both
+// are no-ops in a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -183,6 +192,29 @@ __device__ __forceinline__ uint32_t lds_u32_a2(const uint8_t* p) {
 
 __device__ __forceinline__ uint16_t lds_u16(const uint8_t* p) {
     return *reinterpret_cast<const uint16_t*>(p);
+}
+
+// Whether step kernels use programmatic dependent launch (on unless the
+// environment sets CHATNET_PDL=0; read once).
+bool pdl_enabled();
+
+// Launches kernel<<<grid, block, smem, st>>>(args...), with programmatic
+// stream serialization when pdl is set (the kernel must then follow the
+// pdl_wait contract above).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                            cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
 }  // namespace cn

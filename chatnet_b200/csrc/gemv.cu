@@ -455,6 +455,8 @@ __global__ void __launch_bounds__(kThreads, Geo<TYPE, NT>::kMinCtas)
         fence_mbar_init();
     }
     __syncthreads();
+    pdl_trigger();
+    pdl_wait();
 
     const int64_t total = (int64_t)a.tiles * a.units;
     const int C = (int)(total < (int64_t)gridDim.x ? total : (int64_t)gridDim.x);
@@ -562,6 +564,8 @@ __global__ void __launch_bounds__(kThreads, Geo<TYPE, NT>::kMinCtas)
 
 // Standalone prep of any record form: one warp per (unit, batch row).
 __global__ void xprep_kernel(const float* __restrict__ x, int K, int batch, PrepTarget pt) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int units = K / 256;
     const int64_t items = (int64_t)units * batch;
@@ -591,6 +595,8 @@ __global__ void __launch_bounds__(kNormThreads)
     add_norm_prep_kernel(const float* __restrict__ x_in, const float* __restrict__ delta,
                          float* __restrict__ x_out, const float* __restrict__ w, float* __restrict__ y,
                          int n, float eps, PrepTarget pt) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float red[kNormThreads / 32];
     __shared__ __align__(16) float vals[256];
     const int u = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
@@ -704,6 +710,8 @@ __device__ float block_dot(int type, const uint8_t* row, int blk, const float* x
 __global__ void gemv_generic_kernel(int type, const uint8_t* __restrict__ w, int64_t rows, int cols,
                                     uint64_t rbytes, int blk_elems, const float* __restrict__ x,
                                     float* __restrict__ y, int batch) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -856,7 +864,8 @@ int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool
 
 template <int TYPE, int NT>
 static int launch_tma(cn_ctx* ctx, const CUtensorMap* map, const GemvPlan& p, const GemvArgs& a) {
-    gemv_kernel<TYPE, NT><<<p.ctas, kThreads, Geo<TYPE, NT>::kSmem, ctx->stream>>>(*map, a);
+    CN_CUDA(launch_k(true, gemv_kernel<TYPE, NT>, dim3(p.ctas), dim3(kThreads), (size_t)Geo<TYPE, NT>::kSmem,
+                     ctx->stream, *map, a));
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }
@@ -898,6 +907,15 @@ int gemv_prep_kind(const GemvOp& op) {
     return op.type == CN_TYPE_Q4_K ? 1 : 0;
 }
 
+bool pdl_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char* e = getenv("CHATNET_PDL");
+        on = (e && e[0] == '0') ? 0 : 1;
+    }
+    return on == 1;
+}
+
 // Q4_K decode GEMVs run on the integer path unless CHATNET_GEMV names
 // another family ("tc" or "mma"); read once per process.
 int gemv_q4k_path() {
@@ -928,7 +946,8 @@ int gemv_prep(cudaStream_t st, int sms, const GemvOp& op, const float* d_x, cons
     const int64_t items = (int64_t)op.plan.units * op.batch;
     int blocks = (int)((items + 7) / 8);
     if (blocks > sms * 8) blocks = sms * 8;
-    xprep_kernel<<<blocks, 256, 0, st>>>(d_x, (int)op.cols, op.batch, prep_target(&op, b));
+    CN_CUDA(launch_k(true, xprep_kernel, dim3(blocks), dim3(256), 0, st, d_x, (int)op.cols, op.batch,
+                     prep_target(&op, b)));
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }
@@ -941,8 +960,8 @@ int add_norm_prep(cudaStream_t st, const float* x_in, const float* delta, float*
     CN_CHECK(!delta || (x_out && x_out != x_in), CN_ERR_INVALID_ARG, "norm: x_out must not alias x_in");
     PrepTarget pt = prep_target(op, b);
     if (pt.kind >= 0 && n % 256 != 0) pt.kind = -1;  // the GEMV preps for itself
-    add_norm_prep_kernel<<<dim3((n + 255) / 256, rows), kNormThreads, 0, st>>>(x_in, delta, x_out, w, y, n,
-                                                                              eps, pt);
+    CN_CUDA(launch_k(true, add_norm_prep_kernel, dim3((n + 255) / 256, rows), dim3(kNormThreads), 0, st, x_in,
+                     delta, x_out, w, y, n, eps, pt));
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }
@@ -961,8 +980,8 @@ int gemv_run(cn_ctx* ctx, cudaStream_t st, const GemvOp& op, const float* d_x, c
         int64_t warps = op.rows * op.batch;
         int64_t blocks = (warps * 32 + threads - 1) / threads;
         if (blocks > ctx->sms * 16) blocks = ctx->sms * 16;
-        gemv_generic_kernel<<<(unsigned)blocks, threads, 0, st>>>(
-            op.type, (const uint8_t*)op.w, op.rows, (int)op.cols, op.rb, blk, d_x, d_y, op.batch);
+        CN_CUDA(launch_k(true, gemv_generic_kernel, dim3((unsigned)blocks), dim3(threads), 0, st,
+            op.type, (const uint8_t*)op.w, op.rows, (int)op.cols, op.rb, blk, d_x, d_y, op.batch));
         CN_CUDA(cudaGetLastError());
         return CN_OK;
     }

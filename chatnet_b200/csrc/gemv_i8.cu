@@ -191,6 +191,7 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB>::kCtasPerSm)
         fence_mbar_init();
     }
     __syncthreads();
+    pdl_trigger();
 
     const int64_t total = (int64_t)a.tiles * a.units;
     const int C = (int)(total < (int64_t)gridDim.x ? total : (int64_t)gridDim.x);
@@ -204,16 +205,34 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB>::kCtasPerSm)
     if (warp == kCons) {
         // ---- producer ----
         if (lane == 0) {
+            // the weights depend on no earlier kernel: start the first
+            // stages' loads, then wait for the kernel that writes the
+            // activation records
+            const int pre = nunits < kStages ? nunits : kStages;
+            {
+                int tile = tile0, u = u0;
+                for (int n = 0; n < pre; n++) {
+                    mbar_expect_tx(&full[n], kRaw + kRecB);
+                    tma_load_2d(smem + n * kStage, &map, 18 * u, tile * kRows, &full[n]);
+                    if (++u == a.units) {
+                        u = 0;
+                        tile++;
+                    }
+                }
+            }
+            pdl_wait();
             int tile = tile0, u = u0, s = 0, issued = 0;
             uint32_t ph = 0;
             for (int n = 0; n < nunits; n++) {
-                if (n >= kStages && !mbar_wait_sleep(&empty[s], ph ^ 1)) {
-                    atomicOr(a.err, kErrTimeout);
-                    break;
-                }
                 uint8_t* st = smem + s * kStage;
-                mbar_expect_tx(&full[s], kRaw + kRecB);
-                tma_load_2d(st, &map, 18 * u, tile * kRows, &full[s]);
+                if (n >= kStages) {
+                    if (!mbar_wait_sleep(&empty[s], ph ^ 1)) {
+                        atomicOr(a.err, kErrTimeout);
+                        break;
+                    }
+                    mbar_expect_tx(&full[s], kRaw + kRecB);
+                    tma_load_2d(st, &map, 18 * u, tile * kRows, &full[s]);
+                }
                 asm volatile(
                     "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
                     "[%3];" ::"r"(smem_u32(st + kRaw)),
@@ -230,7 +249,9 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB>::kCtasPerSm)
                     ph ^= 1;
                 }
             }
-            // no copy may still be landing when the CTA exits
+            // no copy may still be landing when the CTA exits (the first
+            // stages' weight loads were issued even if the loop stopped early)
+            if (issued < pre) issued = pre;
             for (int n = issued - kStages < 0 ? 0 : issued - kStages; n < issued; n++)
                 mbar_wait(&full[n % kStages], (uint32_t)(n / kStages) & 1);
         }
@@ -238,6 +259,7 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB>::kCtasPerSm)
     }
 
     // ---- consumers ----
+    pdl_wait();
     const int g = lane >> 2, t = lane & 3;
     const int row0 = 16 * warp + g, row1 = row0 + 8;
     const int r_own = (t & 1) ? row1 : row0;
@@ -413,7 +435,8 @@ int gemv_i8_run(cudaStream_t st, uint32_t* err, const CUtensorMap* map, int64_t 
     switch (batch) {
 #define CN_I8(NB)                                                                                  \
     case NB:                                                                                       \
-        gemv_i8_q4k_kernel<NB><<<ctas, i8::kThreads, i8::Geo<NB>::kSmem, st>>>(*map, a);           \
+        CN_CUDA(launch_k(true, gemv_i8_q4k_kernel<NB>, dim3(ctas), dim3(i8::kThreads),             \
+                         (size_t)i8::Geo<NB>::kSmem, st, *map, a));                                \
         break;
         CN_I8(1) CN_I8(2) CN_I8(3) CN_I8(4) CN_I8(5) CN_I8(6) CN_I8(7) CN_I8(8)
 #undef CN_I8

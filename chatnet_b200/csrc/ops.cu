@@ -86,6 +86,8 @@ __global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ 
                                int n_kv, int hd, int q_stride, int kv_stride, void* kcache,
                                void* vcache, int64_t cache_seq_stride, int64_t cache_layer_off,
                                int kv_f16, int ctx_len, uint32_t* err) {
+    pdl_trigger();
+    pdl_wait();
     const int b = blockIdx.y;
     const int pos = pos_dev ? pos_dev[b] : pos_host;
     if (pos < 0 || pos >= ctx_len) {
@@ -283,6 +285,8 @@ __global__ void __launch_bounds__(kAttnThreads)
                       int64_t cache_layer_off, int ctx_len, int splits, int chunk, float scale,
                       float* __restrict__ part /* [b][head][split][hd + 4] */, int* __restrict__ counters,
                       float* __restrict__ out, int out_stride, PrepTarget pt) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(16) float sm[];
     __shared__ int s_last;
     const int s = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
@@ -428,6 +432,8 @@ __global__ void __launch_bounds__(kAttnThreads)
                     int n_heads, int n_kv, int q_stride, int64_t cache_seq_stride, int64_t cache_layer_off,
                     int ctx_len, int splits, float scale, float* __restrict__ part, int* __restrict__ counters,
                     float* __restrict__ out, int out_stride, PrepTarget pt) {
+    pdl_trigger();
+    pdl_wait();
     static_assert(kAttnThreads == 256 && kMmaChunk == 16 * (kAttnThreads / 32), "16 positions per warp");
     constexpr int RS = HD + 8;  // halves per shared row (16-byte pad against bank conflicts)
     extern __shared__ __align__(16) float sm[];
@@ -577,6 +583,8 @@ __global__ void __launch_bounds__(kAttnThreads)
 // ---- elementwise -----------------------------------------------------------------
 
 __global__ void silu_mul_kernel(float* __restrict__ gate, const float* __restrict__ up, int64_t n) {
+    pdl_trigger();
+    pdl_wait();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         float x = gate[i];
@@ -589,6 +597,8 @@ __global__ void silu_mul_kernel(float* __restrict__ gate, const float* __restric
 // (256-position unit, row); the lanes hold the values in the record layout.
 __global__ void silu_prep_kernel(float* __restrict__ gate, const float* __restrict__ up, int n, int batch,
                                  PrepTarget pt) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int units = n / 256;
     const int64_t items = (int64_t)units * batch;
@@ -628,6 +638,8 @@ __global__ void add_kernel(float* __restrict__ a, const float* __restrict__ b, i
 __global__ void embed_kernel(int type, const uint8_t* __restrict__ emb, uint64_t row_bytes,
                              const int* __restrict__ tokens, int vocab, int dim,
                              float* __restrict__ x, uint32_t* err) {
+    pdl_trigger();
+    pdl_wait();
     const int b = blockIdx.y;
     const int tok = tokens[b];
     if (tok < 0 || tok >= vocab) {
@@ -674,6 +686,8 @@ __global__ void embed_kernel(int type, const uint8_t* __restrict__ emb, uint64_t
 // ---- argmax: first index of the maximum (strict > in the scan) ---------------------
 
 __global__ void argmax_kernel(const float* __restrict__ logits, int n, int* __restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float sv[32];
     __shared__ int si[32];
     const float* l = logits + (size_t)blockIdx.x * n;
@@ -730,10 +744,9 @@ int launch_rmsnorm(const float* x, const float* w, float* y, int n, int rows, fl
 int launch_rope_kv(const RopeKvArgs& a, cudaStream_t s) {
     const int total = (a.n_heads + a.n_kv) * (a.hd / 2) + a.n_kv * a.hd;
     dim3 grid(grid_1d(total, 256, 64), a.batch);
-    rope_kv_kernel<<<grid, 256, 0, s>>>(a.q, a.k, a.v, a.rope, a.pos_dev, a.pos_host, a.n_heads,
-                                        a.n_kv, a.hd, a.q_stride, a.kv_stride, a.kcache, a.vcache,
-                                        a.cache_seq_stride, a.cache_layer_off, a.kv_f16, a.ctx_len,
-                                        a.err);
+    CN_CUDA(launch_k(true, rope_kv_kernel, grid, dim3(256), 0, s, a.q, a.k, a.v, a.rope, a.pos_dev, a.pos_host,
+                     a.n_heads, a.n_kv, a.hd, a.q_stride, a.kv_stride, a.kcache, a.vcache, a.cache_seq_stride,
+                     a.cache_layer_off, a.kv_f16, a.ctx_len, a.err));
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }
@@ -797,27 +810,27 @@ int launch_attention(const AttnArgs& a, const AttnPlan& p, cudaStream_t s) {
         CN_CHECK(a.kv_f16 && attn_use_mma(a.n_heads, a.n_kv, a.hd, true) && p.chunk == kMmaChunk,
                  CN_ERR_INVALID_ARG, "attention plan does not match the call");
         auto k = a.hd == 64 ? attn_mma_kernel<64> : attn_mma_kernel<128>;
-        k<<<grid, kAttnThreads, p.smem, s>>>(a.q, (const __half*)a.kcache, (const __half*)a.vcache, a.pos_dev,
-                                             a.pos_host, a.n_heads, a.n_kv, a.q_stride, a.cache_seq_stride,
-                                             a.cache_layer_off, a.ctx_len, p.splits, scale, a.part, a.counters,
-                                             a.out, a.out_stride, pt);
+        CN_CUDA(launch_k(true, k, grid, dim3(kAttnThreads), p.smem, s, a.q, (const __half*)a.kcache,
+                         (const __half*)a.vcache, a.pos_dev, a.pos_host, a.n_heads, a.n_kv, a.q_stride,
+                         a.cache_seq_stride, a.cache_layer_off, a.ctx_len, p.splits, scale, a.part,
+                         a.counters, a.out, a.out_stride, pt));
     } else if (a.kv_f16) {
-        attn_split_kernel<__half><<<grid, kAttnThreads, p.smem, s>>>(
+        CN_CUDA(launch_k(true, attn_split_kernel<__half>, grid, dim3(kAttnThreads), p.smem, s,
             a.q, (const __half*)a.kcache, (const __half*)a.vcache, a.pos_dev, a.pos_host, a.n_heads,
             a.n_kv, a.hd, a.q_stride, a.cache_seq_stride, a.cache_layer_off, a.ctx_len, p.splits,
-            p.chunk, scale, a.part, a.counters, a.out, a.out_stride, pt);
+            p.chunk, scale, a.part, a.counters, a.out, a.out_stride, pt));
     } else {
-        attn_split_kernel<float><<<grid, kAttnThreads, p.smem, s>>>(
+        CN_CUDA(launch_k(true, attn_split_kernel<float>, grid, dim3(kAttnThreads), p.smem, s,
             a.q, (const float*)a.kcache, (const float*)a.vcache, a.pos_dev, a.pos_host, a.n_heads,
             a.n_kv, a.hd, a.q_stride, a.cache_seq_stride, a.cache_layer_off, a.ctx_len, p.splits,
-            p.chunk, scale, a.part, a.counters, a.out, a.out_stride, pt);
+            p.chunk, scale, a.part, a.counters, a.out, a.out_stride, pt));
     }
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }
 
 int launch_silu_mul(float* gate, const float* up, int64_t n, cudaStream_t s) {
-    silu_mul_kernel<<<grid_1d(n, 256, 148 * 8), 256, 0, s>>>(gate, up, n);
+    CN_CUDA(launch_k(true, silu_mul_kernel, dim3(grid_1d(n, 256, 148 * 8)), dim3(256), 0, s, gate, up, n));
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }
@@ -825,7 +838,8 @@ int launch_silu_mul(float* gate, const float* up, int64_t n, cudaStream_t s) {
 int launch_silu_prep(float* gate, const float* up, int n, int batch, const PrepTarget& pt, cudaStream_t s) {
     if (pt.kind < 0 || n % 256 != 0) return launch_silu_mul(gate, up, (int64_t)n * batch, s);
     const int64_t items = (int64_t)(n / 256) * batch;
-    silu_prep_kernel<<<(unsigned)((items + 7) / 8), 256, 0, s>>>(gate, up, n, batch, pt);
+    CN_CUDA(launch_k(true, silu_prep_kernel, dim3((unsigned)((items + 7) / 8)), dim3(256), 0, s, gate, up, n,
+                     batch, pt));
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }
@@ -838,14 +852,14 @@ int launch_add(float* a, const float* b, int64_t n, cudaStream_t s) {
 
 int launch_embed(int type, const void* emb, uint64_t row_bytes, const int* tokens, int vocab,
                  int dim, int batch, float* x, uint32_t* err, cudaStream_t s) {
-    embed_kernel<<<dim3(grid_1d(dim, 256, 32), batch), 256, 0, s>>>(
-        type, (const uint8_t*)emb, row_bytes, tokens, vocab, dim, x, err);
+    CN_CUDA(launch_k(true, embed_kernel, dim3(grid_1d(dim, 256, 32), batch), dim3(256), 0, s, type,
+                     (const uint8_t*)emb, row_bytes, tokens, vocab, dim, x, err));
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }
 
 int launch_argmax(const float* logits, int n, int batch, int* out, cudaStream_t s) {
-    argmax_kernel<<<batch, 1024, 0, s>>>(logits, n, out);
+    CN_CUDA(launch_k(true, argmax_kernel, dim3(batch), dim3(1024), 0, s, logits, n, out));
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }
