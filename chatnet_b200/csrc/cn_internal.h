@@ -150,6 +150,20 @@ size_t gemv_i8_partial_bytes(int ctas);
 int gemv_i8_prepare();
 int gemv_i8_run(cudaStream_t st, uint32_t* err, const CUtensorMap* map, int64_t rows, int64_t cols,
                 int batch, int ctas, const uint8_t* xrec, float* partials, int* counters, float* y);
+int gemv_i8_run_group(cudaStream_t st, uint32_t* err, int nmat, const CUtensorMap* const* maps,
+                      const int64_t* rows, int64_t cols, int batch, int ctas, const uint8_t* xrec,
+                      float* partials, int* counters, float* const* y);
+
+// Several GEMVs that read the same activations (same inner dimension and
+// batch, all on the integer path) run as one launch: q/k/v, gate/up.
+struct GemvGroup {
+    int n = 0;
+    GemvOp ops[3];
+    GemvPlan plan;  // of the concatenated rows
+};
+// Fails with CN_ERR_UNSUPPORTED when the ops cannot share a launch.
+int gemv_group_make(cn_ctx* ctx, const GemvOp* ops, int n, GemvGroup* g);
+int gemv_group_run(cn_ctx* ctx, cudaStream_t st, const GemvGroup& g, const GemvBufs& b, float* const* y);
 
 // tensor-core Q4_K GEMV (gemv_tc.cu)
 int gemv_tc_ctas(int sms, int tiles, int units);

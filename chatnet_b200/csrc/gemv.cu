@@ -1020,6 +1020,38 @@ int gemv_run(cn_ctx* ctx, cudaStream_t st, const GemvOp& op, const float* d_x, c
 #undef CN_DISPATCH
 }
 
+int gemv_group_make(cn_ctx* ctx, const GemvOp* ops, int n, GemvGroup* g) {
+    CN_CHECK(n >= 1 && n <= 3, CN_ERR_INVALID_ARG, "a GEMV group has 1..3 members");
+    int64_t rows = 0;
+    for (int i = 0; i < n; i++) {
+        const GemvOp& o = ops[i];
+        if (o.plan.path != kPathI8 || o.cols != ops[0].cols || o.batch != ops[0].batch || o.type != ops[0].type)
+            return set_error(CN_ERR_UNSUPPORTED, "GEMVs cannot share a launch");
+        g->ops[i] = o;
+        rows += (o.rows + 127) / 128 * 128;
+    }
+    g->n = n;
+    GemvPlan p = ops[0].plan;
+    p.tiles = (int)(rows / 128);
+    p.ctas = gemv_i8_ctas(ctx->sms, p.tiles, p.units, ops[0].batch);
+    p.partial_bytes = gemv_i8_partial_bytes(p.ctas);
+    p.counters = (size_t)p.tiles * 8;
+    g->plan = p;
+    return CN_OK;
+}
+
+int gemv_group_run(cn_ctx* ctx, cudaStream_t st, const GemvGroup& g, const GemvBufs& b, float* const* y) {
+    const CUtensorMap* maps[3];
+    int64_t rows[3];
+    for (int i = 0; i < g.n; i++) {
+        CN_CHECK((reinterpret_cast<uintptr_t>(y[i]) & 3) == 0, CN_ERR_INVALID_ARG, "y must be aligned");
+        maps[i] = &g.ops[i].map;
+        rows[i] = g.ops[i].rows;
+    }
+    return gemv_i8_run_group(st, ctx->dev_err, g.n, maps, rows, g.ops[0].cols, g.ops[0].batch, g.plan.ctas,
+                             reinterpret_cast<const uint8_t*>(b.xfrag), b.partials, b.counters, y);
+}
+
 int gemv_reserve(const GemvPlan& p, GemvNeeds* n) {
     size_t x = p.xfrag_bytes, s = p.xsum_bytes, pa = p.partial_bytes, c = p.counters;
     if (p.xinv_bytes > n->xinv_bytes) n->xinv_bytes = p.xinv_bytes;

@@ -49,15 +49,35 @@ struct Geo {
 };
 static_assert(Geo<1>::kStages >= 3 && Geo<3>::kStages >= 4 && Geo<8>::kStages >= 4, "pipeline depth");
 
+// Up to kMaxMats weight matrices with the same inner dimension share one
+// launch (and one activation record): their 128-row tiles are numbered one
+// after another, matrix m owning tiles [toff[m], toff[m + 1]).
+constexpr int kMaxMats = 3;
+struct Maps {
+    CUtensorMap m[kMaxMats];
+};
+
 struct Args {
-    int64_t rows;
-    int units, tiles, batch;
+    int units, tiles, batch, nmat;
+    int toff[kMaxMats + 1];
+    int64_t rows[kMaxMats];
+    float* y[kMaxMats];   // [batch][rows[m]]
     const uint8_t* xrec;  // [unit][rec_bytes(NT)]
-    float* y;             // [batch][rows]
     float* partials;      // [2 * ctas][128][8]
     int* counters;        // [tiles][kCons], zero on entry, left zero
     uint32_t* err;
 };
+
+// matrix of a tile, its first row in that matrix, its row count and output
+__device__ __forceinline__ int mat_of(const Args& a, int tile) {
+    return (a.nmat > 2 && tile >= a.toff[2]) ? 2 : (a.nmat > 1 && tile >= a.toff[1]) ? 1 : 0;
+}
+__device__ __forceinline__ int64_t pick64(const int64_t (&v)[kMaxMats], int m) {
+    return m == 2 ? v[2] : m == 1 ? v[1] : v[0];
+}
+__device__ __forceinline__ float* pickp(float* const (&v)[kMaxMats], int m) {
+    return m == 2 ? v[2] : m == 1 ? v[1] : v[0];
+}
 
 __device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
@@ -122,13 +142,16 @@ __device__ void finish_subtile(const Args& a, int r, int t, int warp, int tile, 
                                int64_t total, bool shared_tile, int my_slot,
                                const float (&acc)[Geo<NB>::NT]) {
     constexpr int NT = Geo<NB>::NT;
-    const int64_t row = (int64_t)tile * kRows + r;
+    const int m = mat_of(a, tile);
+    const int64_t rows = pick64(a.rows, m);
+    float* const y = pickp(a.y, m);
+    const int64_t row = (int64_t)(tile - (m == 2 ? a.toff[2] : m == 1 ? a.toff[1] : 0)) * kRows + r;
     if (!shared_tile) {
-        if (row < a.rows) {
+        if (row < rows) {
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
                 const int b = owned_seq<NB>(nt, t);
-                if (b >= 0) a.y[(size_t)b * a.rows + row] = acc[nt];
+                if (b >= 0) y[(size_t)b * rows + row] = acc[nt];
             }
         }
         return;
@@ -161,7 +184,7 @@ __device__ void finish_subtile(const Args& a, int r, int t, int warp, int tile, 
             const int slot = 2 * c + (tile == first_tile ? 0 : 1);
             s += __ldcg(a.partials + ((size_t)slot * kRows + r) * 8 + b);
         }
-        if (row < a.rows) a.y[(size_t)b * a.rows + row] = s;
+        if (row < rows) y[(size_t)b * rows + row] = s;
     }
     __syncwarp();
     if ((threadIdx.x & 31) == 0) atomicExch(ctr, 0);
@@ -171,7 +194,7 @@ __device__ void finish_subtile(const Args& a, int r, int t, int warp, int tile, 
 
 template <int NB>
 __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB>::kCtasPerSm)
-    gemv_i8_q4k_kernel(const __grid_constant__ CUtensorMap map, const i8::Args a) {
+    gemv_i8_q4k_kernel(const __grid_constant__ i8::Maps maps, const i8::Args a) {
     using namespace i8;
     using G = Geo<NB>;
     constexpr int NT = G::NT;
@@ -208,12 +231,19 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB>::kCtasPerSm)
             // the weights depend on no earlier kernel: start the first
             // stages' loads, then wait for the kernel that writes the
             // activation records
+            // raw blocks of unit u of global tile `tile` (its matrix's map, the
+            // tile's rows within that matrix)
+            auto load_raw = [&](uint8_t* dst, int tile, int u, uint64_t* bar) {
+                const int m = mat_of(a, tile);
+                const int lt = tile - (m == 2 ? a.toff[2] : m == 1 ? a.toff[1] : 0);
+                tma_load_2d(dst, &maps.m[m], 18 * u, lt * kRows, bar);
+            };
             const int pre = nunits < kStages ? nunits : kStages;
             {
                 int tile = tile0, u = u0;
                 for (int n = 0; n < pre; n++) {
                     mbar_expect_tx(&full[n], kRaw + kRecB);
-                    tma_load_2d(smem + n * kStage, &map, 18 * u, tile * kRows, &full[n]);
+                    load_raw(smem + n * kStage, tile, u, &full[n]);
                     if (++u == a.units) {
                         u = 0;
                         tile++;
@@ -231,7 +261,7 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB>::kCtasPerSm)
                         break;
                     }
                     mbar_expect_tx(&full[s], kRaw + kRecB);
-                    tma_load_2d(st, &map, 18 * u, tile * kRows, &full[s]);
+                    load_raw(st, tile, u, &full[s]);
                 }
                 asm volatile(
                     "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
@@ -416,19 +446,31 @@ int gemv_i8_prepare() {
     return CN_OK;
 }
 
-int gemv_i8_run(cudaStream_t st, uint32_t* err, const CUtensorMap* map, int64_t rows, int64_t cols,
-                int batch, int ctas, const uint8_t* xrec, float* partials, int* counters, float* y) {
-    CN_CHECK(batch >= 1 && batch <= i8::kMaxNB && cols % 256 == 0 && ctas > 0, CN_ERR_INVALID_ARG,
-             "integer GEMV: bad shape");
+int gemv_i8_run_group(cudaStream_t st, uint32_t* err, int nmat, const CUtensorMap* const* maps,
+                      const int64_t* rows, int64_t cols, int batch, int ctas, const uint8_t* xrec,
+                      float* partials, int* counters, float* const* y) {
+    CN_CHECK(batch >= 1 && batch <= i8::kMaxNB && cols % 256 == 0 && ctas > 0 && nmat >= 1 &&
+                 nmat <= i8::kMaxMats,
+             CN_ERR_INVALID_ARG, "integer GEMV: bad shape");
     int rc = gemv_i8_prepare();
     if (rc) return rc;
+    i8::Maps mp;
     i8::Args a;
-    a.rows = rows;
     a.units = (int)(cols / 256);
-    a.tiles = (int)((rows + i8::kRows - 1) / i8::kRows);
     a.batch = batch;
+    a.nmat = nmat;
+    int tiles = 0;
+    for (int m = 0; m < i8::kMaxMats; m++) {
+        const int mm = m < nmat ? m : nmat - 1;
+        mp.m[m] = *maps[mm];
+        a.rows[m] = rows[mm];
+        a.y[m] = y[mm];
+        a.toff[m] = tiles;
+        if (m < nmat) tiles += (int)((rows[m] + i8::kRows - 1) / i8::kRows);
+    }
+    a.toff[i8::kMaxMats] = tiles;
+    a.tiles = tiles;
     a.xrec = xrec;
-    a.y = y;
     a.partials = partials;
     a.counters = counters;
     a.err = err;
@@ -436,13 +478,18 @@ int gemv_i8_run(cudaStream_t st, uint32_t* err, const CUtensorMap* map, int64_t 
 #define CN_I8(NB)                                                                                  \
     case NB:                                                                                       \
         CN_CUDA(launch_k(true, gemv_i8_q4k_kernel<NB>, dim3(ctas), dim3(i8::kThreads),             \
-                         (size_t)i8::Geo<NB>::kSmem, st, *map, a));                                \
+                         (size_t)i8::Geo<NB>::kSmem, st, mp, a));                                  \
         break;
         CN_I8(1) CN_I8(2) CN_I8(3) CN_I8(4) CN_I8(5) CN_I8(6) CN_I8(7) CN_I8(8)
 #undef CN_I8
     }
     CN_CUDA(cudaGetLastError());
     return CN_OK;
+}
+
+int gemv_i8_run(cudaStream_t st, uint32_t* err, const CUtensorMap* map, int64_t rows, int64_t cols,
+                int batch, int ctas, const uint8_t* xrec, float* partials, int* counters, float* y) {
+    return gemv_i8_run_group(st, err, 1, &map, &rows, cols, batch, ctas, xrec, partials, counters, &y);
 }
 
 }  // namespace cn

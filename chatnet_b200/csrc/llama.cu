@@ -32,6 +32,8 @@ constexpr int kMaxBatch = 32;
 struct Step {
     bool built = false;
     std::vector<GemvOp> ops;  // [layer * 7 + {q,k,v,o,gate,up,down}], then lm_head
+    // per layer: q/k/v and gate/up as single launches (n == 0: run apart)
+    std::vector<GemvGroup> qkv, gu;
     AttnPlan ap;
     cudaGraphExec_t graph = nullptr;
 };
@@ -108,6 +110,14 @@ static int build_step(cn_llama* m, int B) {
         if (rc) return rc;
         st.ops.push_back(op);
     }
+    st.qkv.assign(c.n_layers, GemvGroup());
+    st.gu.assign(c.n_layers, GemvGroup());
+    for (int l = 0; l < c.n_layers; l++) {
+        const GemvOp* o = &st.ops[(size_t)l * 7];
+        if (gemv_group_make(m->ctx, o, 3, &st.qkv[l]) != CN_OK) st.qkv[l].n = 0;
+        if (gemv_group_make(m->ctx, o + 4, 2, &st.gu[l]) != CN_OK) st.gu[l].n = 0;
+    }
+    set_error(CN_OK, "");
     int rc = attention_plan(c.n_heads, c.n_kv_heads, c.head_dim, c.ctx_len, B, m->ctx->sms,
                             c.kv_dtype == CN_KV_F16, &st.ap);
     if (rc) return rc;
@@ -134,6 +144,17 @@ struct PrepCache {
         return x == x_ && kind == gemv_prep_kind(op) && nt == op.plan.nt && cols == op.cols;
     }
 };
+
+// A GEMV group (prep shared by its members, which read the same x).
+static int gemv_g(cn_llama* m, cudaStream_t s, const GemvGroup& g, const float* x, float* const* y,
+                  PrepCache& pc) {
+    if (!pc.holds(x, g.ops[0])) {
+        int rc = gemv_prep(s, m->ctx->sms, g.ops[0], x, m->gb);
+        if (rc) return rc;
+        pc.set(x, g.ops[0]);
+    }
+    return gemv_group_run(m->ctx, s, g, m->gb, y);
+}
 
 static int gemv(cn_llama* m, cudaStream_t s, const GemvOp& op, const float* x, float* y,
                 PrepCache& pc) {
@@ -177,9 +198,14 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
     for (int l = 0; l < c.n_layers; l++) {
         const GemvOp* ops = &st.ops[(size_t)l * 7];
         if ((rc = norm(m, s, LT(m, l, L_ANORM), B, ops[0], &x, &delta, pc))) return rc;
-        if ((rc = gemv(m, s, ops[0], m->xn, m->q, pc))) return rc;
-        if ((rc = gemv(m, s, ops[1], m->xn, m->k, pc))) return rc;
-        if ((rc = gemv(m, s, ops[2], m->xn, m->v, pc))) return rc;
+        if (st.qkv[l].n) {
+            float* ys[3] = {m->q, m->k, m->v};
+            if ((rc = gemv_g(m, s, st.qkv[l], m->xn, ys, pc))) return rc;
+        } else {
+            if ((rc = gemv(m, s, ops[0], m->xn, m->q, pc))) return rc;
+            if ((rc = gemv(m, s, ops[1], m->xn, m->k, pc))) return rc;
+            if ((rc = gemv(m, s, ops[2], m->xn, m->v, pc))) return rc;
+        }
         RopeKvArgs ra;
         ra.q = m->q;
         ra.k = m->k;
@@ -228,8 +254,13 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
         if ((rc = gemv(m, s, ops[3], m->att, m->tmp, pc))) return rc;
         delta = m->tmp;
         if ((rc = norm(m, s, LT(m, l, L_FNORM), B, ops[4], &x, &delta, pc))) return rc;
-        if ((rc = gemv(m, s, ops[4], m->xn, m->gate, pc))) return rc;
-        if ((rc = gemv(m, s, ops[5], m->xn, m->up, pc))) return rc;
+        if (st.gu[l].n) {
+            float* ys[2] = {m->gate, m->up};
+            if ((rc = gemv_g(m, s, st.gu[l], m->xn, ys, pc))) return rc;
+        } else {
+            if ((rc = gemv(m, s, ops[4], m->xn, m->gate, pc))) return rc;
+            if ((rc = gemv(m, s, ops[5], m->xn, m->up, pc))) return rc;
+        }
         const PrepTarget spt = prep_target(&ops[6], m->gb);
         if ((rc = launch_silu_prep(m->gate, m->up, hid, B, spt, s))) return rc;
         pc = PrepCache();
@@ -430,6 +461,21 @@ int cn_llama_create(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* const* t
                                     b, &op)))
                     return fail(rc);
                 gemv_reserve(op.plan, &need);
+            }
+            // the grouped launches (q/k/v, gate/up) of any layer: same shapes
+            if (c.n_layers > 0) {
+                static const int wj[5] = {L_Q, L_K, L_V, L_GATE, L_UP};
+                GemvOp o[5];
+                for (int j = 0; j < 5; j++) {
+                    const cn_tensor* w = tensors[3 + wj[j]];
+                    if ((rc = gemv_make(ctx, w->type, w->d, w->rows, w->cols, w->has_map ? &w->map : nullptr,
+                                        b, &o[j])))
+                        return fail(rc);
+                }
+                GemvGroup g;
+                if (gemv_group_make(ctx, o, 3, &g) == CN_OK) gemv_reserve(g.plan, &need);
+                if (gemv_group_make(ctx, o + 3, 2, &g) == CN_OK) gemv_reserve(g.plan, &need);
+                set_error(CN_OK, "");
             }
             if (reps[r] >= B) break;
         }
