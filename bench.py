@@ -128,6 +128,25 @@ def measured_peak_gbs() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
+def gemv_kernel_name(config: int, batch: int) -> str:
+    """The GEMV kernel family the library runs for the config's projections
+    (Q4_K decode at batch 1..8: the integer mma.sync kernel unless the
+    environment selects another; Q4_0 and larger batches: the fp16 one)."""
+    choice = os.environ.get("CHATNET_GEMV", "i8")
+    if config == 4 and batch <= 8 and choice not in ("tc", "mma"):
+        return "gemv_i8_q4k"
+    if config == 4 and batch <= 5 and choice == "tc":
+        return "gemv_tc_q4k"
+    return "gemv_q4_k" if config == 4 else "gemv_q4_0"
+
+
+def gemv_dtype(config: int, batch: int) -> str:
+    name = gemv_kernel_name(config, batch)
+    if name in ("gemv_i8_q4k", "gemv_tc_q4k"):
+        return "q4_k x int22 activation digits (int8 mma, exact) -> s32 -> f32"
+    return ("q4_k" if config == 4 else "q4_0") + " x fp16(hi+lo) -> f32"
+
+
 def committed_traffic(kernel_key: str):
     """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
     p = ROOT / "profiles" / "traffic.json"
@@ -350,7 +369,8 @@ def main():
     peak, peak_kind = measured_peak_gbs()
     achieved = nbytes / (us * 1e-6) / 1e9
     shape = f"{dc.model.hidden_dim}x{dc.model.dim}"
-    traffic = committed_traffic(f"gemv_{'q4_k' if a.config == 4 else 'q4_0'}_{shape}_b{B}")
+    gemv_name = gemv_kernel_name(a.config, B)
+    traffic = committed_traffic(f"{gemv_name}_{shape}_b{B}")
     kernels = model.step_kernels(B)
 
     cpu = None
@@ -365,14 +385,14 @@ def main():
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None,
-            "dtype": ("q4_k" if a.config == 4 else "q4_0") + " x fp16(hi+lo) -> f32",
+            "dtype": gemv_dtype(a.config, B),
             "data": "synthetic (seeded generator, config shapes and distributions)",
             "config": workload,
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": B * 8,
                     "d2h_bytes_per_step": B * (dc.model.vocab * 4 + 4)},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": f"gemv_kernel<Q4_K> {shape} batch {B}",
+                         "kernel": f"{gemv_name} {shape} batch {B}",
                          "us_per_launch": us, "bytes_per_launch": nbytes,
                          "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
             "cpu_baseline": cpu,
