@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--config", type=int, default=4, choices=(1, 4))
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--parallel", default="tp", choices=("tp", "replicas"),
+                    help="N > 1: tensor parallelism over the N GPUs (default), or N independent replicas")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--gemv", default=None, metavar="TYPE:ROWSxCOLS:BATCH",
                     help="kernel mode: run one fused dequant-GEMV (e.g. q4_k:28672x8192:1) "
@@ -255,7 +257,9 @@ def main():
                 "vocab": dc.model.vocab, "ctx": dc.model.ctx_len, "position": dc.decode_pos,
                 "weights": "Q4_K" if a.config == 4 else "Q4_0",
                 "kv_cache": "fp16" if dc.model.kv_f16 else "fp32",
-                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "parallelism": ("single GPU" if world == 1 else
+                                f"tp{world} (row/column-sharded projections, exchange fused into the "
+                                f"GEMV epilogue over NVLink)" if a.parallel == "tp" else f"replicas x{world}"),
                 "l2": "inputs larger than L2 (weights 38.5 GB)" if a.config == 4 else
                       "inputs larger than L2 (weights 0.58 GB)"}
 
@@ -299,14 +303,27 @@ def main():
     ctx = cn.Context(local)
     ext = torch.cuda.ExternalStream(ctx.stream)
     t0 = time.time()
-    tensors = cf.device_tensors(ctx, dc)  # seeded generator, on the device
-    model = CudaLlamaModel(ctx, dc.model, tensors)
+    tp_mode = world > 1 and a.parallel == "tp"
+    tp = None
     B = a.batch
+    if tp_mode:
+        # one rank per GPU: join the group through the exchange buffers' IPC handles
+        tp = cn.TensorParallel(ctx, rank, world, B, dc.model.dim, dc.model.vocab)
+        handles = [None] * world
+        dist.all_gather_object(handles, tp.ipc_handle())
+        tp.connect(handles)
+        tensors = cf.device_tensors(ctx, dc, rank=rank, size=world)  # this rank's shards
+    else:
+        tensors = cf.device_tensors(ctx, dc)  # seeded generator, on the device
+    model = CudaLlamaModel(ctx, dc.model, tensors, tp=tp)
     for b in range(B):
         model.kv_synth(b, dc.kv_filled, *cf.kv_seeds(dc, b))
     toks = [cf.token(dc, b) for b in range(B)]
     pos = [dc.decode_pos] * B
     model.set_inputs(toks, pos)
+    model.prepare(B)  # capture the step graph before any rank starts a step
+    if dist is not None:
+        dist.barrier()
     setup_s = time.time() - t0
 
     def barrier():
@@ -351,7 +368,8 @@ def main():
     clocks = clk.stop()
     ctx.synchronize()
     ms = max_over_ranks(ms)
-    value = world * B * 1000.0 / ms
+    tokens_per_step = B if tp_mode else world * B  # tp: all ranks decode the same B sequences
+    value = tokens_per_step * 1000.0 / ms
 
     # end to end through cn_llama_decode (host buffers)
     barrier()
@@ -361,14 +379,14 @@ def main():
     e1.record(ext)
     e1.synchronize()
     ms_e2e = max_over_ranks(e0.elapsed_time(e1) / a.steps)
-    e2e = world * B * 1000.0 / ms_e2e
+    e2e = tokens_per_step * 1000.0 / ms_e2e
     assert np.isfinite(lg).all()
 
     # roofline: the dominant kernel timed alone (FFN gate projection)
     us, nbytes = model.time_gemv(4, B, iters=2 * dc.model.n_layers)
     peak, peak_kind = measured_peak_gbs()
     achieved = nbytes / (us * 1e-6) / 1e9
-    shape = f"{dc.model.hidden_dim}x{dc.model.dim}"
+    shape = f"{dc.model.hidden_dim // (world if tp_mode else 1)}x{dc.model.dim}"  # this rank's gate shard
     gemv_name = gemv_kernel_name(a.config, B)
     traffic = committed_traffic(f"{gemv_name}_{shape}_b{B}")
     kernels = model.step_kernels(B)
@@ -383,7 +401,8 @@ def main():
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong" if tp_mode else "weak",
             "vs_baseline": None,
             "dtype": gemv_dtype(a.config, B),
             "data": "synthetic (seeded generator, config shapes and distributions)",
@@ -405,6 +424,10 @@ def main():
     model.close()
     for t in tensors:
         t.free()
+    if tp is not None:
+        if dist is not None:
+            dist.barrier()  # no rank unmaps its buffer while another may still store into it
+        tp.close()
     ctx.close()
     if dist is not None:
         dist.destroy_process_group()

@@ -123,6 +123,17 @@ class Context:
               "cn_tensor_synth")
         return self._own(Tensor(self, h.value, type_, rows, cols))
 
+    def synth_slice(self, type_: int, rows: int, cols: int, row0: int, nrows: int, col0: int, ncols: int,
+                    seed: int, dist: int | None = None) -> Tensor:
+        """Region [row0, row0+nrows) x [col0, col0+ncols) of what synth(type_, rows, cols, seed)
+        would generate (a tensor-parallel shard), generated in place."""
+        if dist is None:
+            dist = _DEFAULT_DIST.get(type_, DIST_NORMAL)
+        h = C.c_void_p()
+        check(N.lib().cn_tensor_synth_slice(self.handle, type_, rows, cols, row0, nrows, col0, ncols, seed,
+                                            dist, C.byref(h)), "cn_tensor_synth_slice")
+        return self._own(Tensor(self, h.value, type_, nrows, ncols))
+
     def dequantize(self, W: Tensor, row0: int = 0, nrows: int | None = None) -> np.ndarray:
         if nrows is None:
             nrows = W.rows - row0
@@ -158,3 +169,30 @@ class Context:
             self.close()
         except Exception:
             pass
+
+
+class TensorParallel:
+    """This process's rank of a tensor-parallel group (cn_tp_*): one process
+    per GPU; the exchange buffers are shared between GPUs with CUDA IPC."""
+
+    def __init__(self, ctx: Context, rank: int, size: int, max_batch: int, dim: int, vocab: int):
+        h = C.c_void_p()
+        check(N.lib().cn_tp_create(ctx.handle, rank, size, max_batch, dim, vocab, C.byref(h)), "cn_tp_create")
+        self.handle, self.rank, self.size = h.value, rank, size
+
+    def ipc_handle(self) -> bytes:
+        buf = (C.c_uint8 * N.TP_HANDLE_BYTES)()
+        check(N.lib().cn_tp_handle(self.handle, buf), "cn_tp_handle")
+        return bytes(buf)
+
+    def connect(self, handles: list[bytes]) -> None:
+        """handles: every rank's ipc_handle(), in rank order."""
+        assert len(handles) == self.size and all(len(h) == N.TP_HANDLE_BYTES for h in handles)
+        blob = b"".join(handles)
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        check(N.lib().cn_tp_connect(self.handle, buf), "cn_tp_connect")
+
+    def close(self) -> None:
+        if self.handle:
+            N.lib().cn_tp_destroy(self.handle)
+            self.handle = None

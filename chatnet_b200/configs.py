@@ -19,9 +19,9 @@ from dataclasses import dataclass, replace
 
 import numpy as np
 
-from . import (DIST_NORM_W, DIST_NORMAL, TYPE_F16, TYPE_F32, TYPE_Q4_0, TYPE_Q4_K, synth_fill,
+from . import (DIST_NORM_W, DIST_NORMAL, TYPE_F16, TYPE_F32, TYPE_Q4_0, TYPE_Q4_K, byte_size, synth_fill,
                synth_seed)
-from .llama import LlamaConfig, tensor_names, tensor_shape
+from .llama import LlamaConfig, shard_region, tensor_names, tensor_shape
 
 
 @dataclass(frozen=True)
@@ -75,17 +75,33 @@ def host_tensors(dc: DecodeConfig) -> dict[str, np.ndarray]:
     return out
 
 
-def device_tensors(ctx, dc: DecodeConfig, host: dict[str, np.ndarray] | None = None) -> list:
-    """The model's tensors in HBM: uploaded from `host`, or generated on the device."""
+def device_tensors(ctx, dc: DecodeConfig, host: dict[str, np.ndarray] | None = None, rank: int = 0,
+                   size: int = 1) -> list:
+    """The model's tensors in HBM: uploaded from `host`, or generated on the device.
+    With size > 1, tensor-parallel rank `rank`'s shards (shard_region)."""
     ts = []
     for name in tensor_names(dc.model.n_layers):
         rows, cols = tensor_shape(dc.model, name)
         t = tensor_type(dc, name)
+        r0, nr, c0, nc = shard_region(dc.model, name, rank, size)
         if host is not None:
-            ts.append(ctx.upload(host[name], t, rows, cols))
-        else:
+            ts.append(ctx.upload(host_slice(host[name], t, cols, r0, nr, c0, nc), t, nr, nc))
+        elif size == 1:
             ts.append(ctx.synth(t, rows, cols, synth_seed(dc.config_id, name), tensor_dist(dc, name)))
+        else:
+            ts.append(ctx.synth_slice(t, rows, cols, r0, nr, c0, nc, synth_seed(dc.config_id, name),
+                                      tensor_dist(dc, name)))
     return ts
+
+
+def host_slice(a: np.ndarray, type_: int, cols: int, r0: int, nr: int, c0: int, nc: int) -> np.ndarray:
+    """Rows [r0, r0+nr) and columns [c0, c0+nc) (whole blocks) of a host tensor's bytes."""
+    raw = np.ascontiguousarray(a).view(np.uint8).reshape(a.shape[0], -1)
+    if c0 == 0 and nc == cols:
+        return raw[r0:r0 + nr].copy()
+    blk = {TYPE_F32: 1, TYPE_F16: 1}.get(type_, 32 if type_ == TYPE_Q4_0 else 256)
+    bpb = byte_size(type_, blk)
+    return raw[r0:r0 + nr, (c0 // blk) * bpb:((c0 + nc) // blk) * bpb].copy()
 
 
 def token(dc: DecodeConfig, seq: int, step: int = 0) -> int:

@@ -241,6 +241,27 @@ int cn_tensor_synth(cn_ctx* ctx, int type, int64_t rows, int64_t cols, uint64_t 
     return CN_OK;
 }
 
+int cn_tensor_synth_slice(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int64_t row0, int64_t nrows,
+                          int64_t col0, int64_t ncols, uint64_t seed, int dist, cn_tensor** out) {
+    CN_CHECK(ctx && out, CN_ERR_INVALID_ARG, "null argument");
+    DeviceGuard dg(ctx->device);
+    cn_tensor* t = nullptr;
+    int rc = tensor_alloc(ctx, type, nrows, ncols, &t);
+    if (rc) return rc;
+    rc = synth_slice_launch(type, rows, cols, row0, nrows, col0, ncols, seed, dist, t->d, ctx->stream);
+    if (rc == CN_OK) {
+        cudaError_t e = cudaStreamSynchronize(ctx->stream);
+        if (e != cudaSuccess) rc = cuda_error(e, "synth");
+    }
+    if (rc) {
+        cudaFree(t->d);
+        delete t;
+        return rc;
+    }
+    *out = t;
+    return CN_OK;
+}
+
 int cn_tensor_download(const cn_tensor* t, void* host, uint64_t bytes) {
     CN_CHECK(t && host, CN_ERR_INVALID_ARG, "null argument");
     CN_CHECK(bytes == t->bytes, CN_ERR_INVALID_ARG, "download size %llu != tensor size %llu",

@@ -33,6 +33,22 @@ struct cn_ctx {
     size_t hstage_bytes = 0;
 };
 
+// A tensor-parallel rank's exchange state (tp.cu).  `buf` (IPC-exported)
+// holds [flags: kMaxTp uint32, padded to 256 B][slots: 2 parities x size ranks
+// x max_batch x dim fp32][logits: max_batch x vocab fp32]; peer[p] is rank
+// p's buf mapped into this process (peer[rank] == buf).
+struct cn_tp {
+    cn_ctx* ctx = nullptr;
+    int rank = 0, size = 1, max_batch = 1;
+    int64_t dim = 0, vocab = 0;
+    uint8_t* buf = nullptr;
+    size_t bytes = 0, slots_off = 256, logits_off = 0;
+    void* peer[8] = {};
+    bool connected = false;
+    uint32_t* step = nullptr;  // step counter (bumped once per decode step)
+    int* done = nullptr;       // GEMV completion counters [16]
+};
+
 struct cn_tensor {
     cn_ctx* ctx = nullptr;
     int type = 0;
@@ -111,6 +127,34 @@ struct PrepTarget {
     float* xinv = nullptr;
 };
 
+// Tensor-parallel exchange, producer side: a GEMV whose output is a partial
+// sum (O and down split along their input) or a slice (lm_head rows) stores
+// every output value into each rank's buffer over NVLink and, when all of
+// its CTAs are done, raises its flag on every rank.  Destination of value
+// (b, row) on rank p: dst[p] + parity * parity_stride + b * dst_ld + dst_row0
+// + row, parity = seq & 1, seq = *seq_base * uses + seq_add.
+constexpr int kMaxTp = 8;
+struct XchgOut {
+    int size = 1, rank = 0;
+    float* dst[kMaxTp] = {};
+    int64_t parity_stride = 0, dst_ld = 0, dst_row0 = 0;
+    uint32_t* flag[kMaxTp] = {};  // &flags[rank] on each rank
+    const uint32_t* seq_base = nullptr;
+    uint32_t uses = 1, seq_add = 0;
+    int* done = nullptr;  // completion counter, zero on entry, left zero
+};
+// Consumer side: wait until flags[p] >= seq for every rank p, then the
+// summed input is sum_p src[parity * parity_stride + p * rank_stride + ...].
+struct XchgIn {
+    int size = 1;
+    const float* src = nullptr;
+    int64_t parity_stride = 0, rank_stride = 0;
+    const uint32_t* flags = nullptr;
+    const uint32_t* seq_base = nullptr;
+    uint32_t uses = 1, seq_add = 0;
+    uint32_t* err = nullptr;
+};
+
 struct GemvNeeds {
     size_t xfrag_bytes = 0, xsum_bytes = 0, xinv_bytes = 0, partial_bytes = 0, counters = 0;
 };
@@ -121,7 +165,7 @@ int gemv_make(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols
 int gemv_prep(cudaStream_t st, int sms, const GemvOp& op, const float* d_x, const GemvBufs& b);
 // Runs the GEMV on prepped fragments (TMA path) or on x directly (generic).
 int gemv_run(cn_ctx* ctx, cudaStream_t st, const GemvOp& op, const float* d_x, const GemvBufs& b,
-             float* d_y);
+             float* d_y, const XchgOut* xo = nullptr);
 int gemv_reserve(const GemvPlan& p, GemvNeeds* n);
 // RMSNorm of `rows` rows of n values into y, and, when op is a tiled GEMV,
 // its activation records for op in b (one kernel).
@@ -130,7 +174,10 @@ int norm_prep(cudaStream_t st, const float* x, const float* w, float* y, int n, 
 // Same after a residual add: x_out = x_in + delta (x_out must not alias
 // x_in), then y = RMSNorm(x_out) * w and op's records.
 int add_norm_prep(cudaStream_t st, const float* x_in, const float* delta, float* x_out, const float* w,
-                  float* y, int n, int rows, float eps, const GemvOp* op, const GemvBufs& b);
+                  float* y, int n, int rows, float eps, const GemvOp* op, const GemvBufs& b,
+                  const XchgIn* xin = nullptr);
+// Waits (bounded) until every rank's flag reached this use's sequence number.
+int xchg_wait(cudaStream_t st, const XchgIn& xin);
 // The record target of op in b (kind -1 when op reads plain fp32).
 PrepTarget prep_target(const GemvOp* op, const GemvBufs& b);
 float gemv_step1_scale(int type);
@@ -149,10 +196,11 @@ size_t gemv_i8_xbytes(int64_t cols, int batch);
 size_t gemv_i8_partial_bytes(int ctas);
 int gemv_i8_prepare();
 int gemv_i8_run(cudaStream_t st, uint32_t* err, const CUtensorMap* map, int64_t rows, int64_t cols,
-                int batch, int ctas, const uint8_t* xrec, float* partials, int* counters, float* y);
+                int batch, int ctas, const uint8_t* xrec, float* partials, int* counters, float* y,
+                const XchgOut* xo = nullptr);
 int gemv_i8_run_group(cudaStream_t st, uint32_t* err, int nmat, const CUtensorMap* const* maps,
                       const int64_t* rows, int64_t cols, int batch, int ctas, const uint8_t* xrec,
-                      float* partials, int* counters, float* const* y);
+                      float* partials, int* counters, float* const* y, const XchgOut* xo = nullptr);
 
 // Several GEMVs that read the same activations (same inner dimension and
 // batch, all on the integer path) run as one launch: q/k/v, gate/up.
@@ -178,8 +226,19 @@ int gemv_tc_run(cudaStream_t st, uint32_t* err, const CUtensorMap* map, int64_t 
 int gemv_launch(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols,
                 const CUtensorMap* map, const float* d_x, float* d_y, int batch);
 
+// tensor-parallel exchange descriptors (tp.cu); uses = exchanges per step
+int tp_step_launch(const cn_tp* tp, cudaStream_t s);
+XchgOut tp_reduce_out(const cn_tp* tp, uint32_t uses, uint32_t use, int done_index);
+XchgIn tp_reduce_in(const cn_tp* tp, uint32_t uses, uint32_t use, uint32_t* err);
+XchgOut tp_gather_out(const cn_tp* tp, int64_t local_rows, uint32_t uses, uint32_t use, int done_index);
+float* tp_logits(const cn_tp* tp);
+
 int dequant_launch(int type, const void* d_blocks, float* d_out, int64_t n, cudaStream_t s);
 int synth_launch(int type, int64_t rows, int64_t cols, uint64_t seed, int dist, void* d_out,
                  cudaStream_t s);
+// Region [row0, row0 + nrows) x [col0, col0 + ncols) of the rows x cols tensor
+// that synth_launch would generate (columns in whole blocks).
+int synth_slice_launch(int type, int64_t rows, int64_t cols, int64_t row0, int64_t nrows, int64_t col0,
+                       int64_t ncols, uint64_t seed, int dist, void* d_out, cudaStream_t s);
 
 }  // namespace cn

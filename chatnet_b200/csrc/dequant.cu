@@ -148,38 +148,53 @@ int dequant_launch(int type, const void* d_blocks, float* d_out, int64_t n, cuda
 
 // ---- synthetic generator (device) ----------------------------------------------
 
-__global__ void synth_blocks_kernel(int type, uint64_t seed, int64_t nblocks, uint8_t* out) {
-    for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < nblocks;
-         b += (int64_t)gridDim.x * blockDim.x) {
+// The generators index blocks / elements of the FULL tensor (rows_full x
+// cols_full), so any [row0, row0 + nrows) x [col0, col0 + ncols) slice gets
+// exactly the bytes of that region of the whole tensor (tensor-parallel
+// shards are generated where they live).  Local block lb of the slice is
+// global block (row0 + lb / nbc) * bpr_full + cb0 + lb % nbc.
+__global__ void synth_blocks_kernel(int type, uint64_t seed, int64_t bpr_full, int64_t row0, int64_t cb0,
+                                    int64_t nbc, int64_t nblocks, uint8_t* out) {
+    for (int64_t lb = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; lb < nblocks;
+         lb += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t b = (row0 + lb / nbc) * bpr_full + cb0 + lb % nbc;
         if (type == CN_TYPE_Q4_0) {
-            synth::q4_0_block(seed, b, out + b * 18);
+            synth::q4_0_block(seed, b, out + lb * 18);
         } else if (type == CN_TYPE_Q4_K) {
             __align__(16) uint8_t tmp[144];
             synth::q4_k_block(seed, b, tmp);
-            uint4* o = reinterpret_cast<uint4*>(out + b * 144);  // 144 = 9 x 16
-            const uint4* s = reinterpret_cast<const uint4*>(tmp);
-            for (int i = 0; i < 9; i++) o[i] = s[i];
+            uint4* o = reinterpret_cast<uint4*>(out + lb * 144);  // 144 = 9 x 16
+            const uint4* src = reinterpret_cast<const uint4*>(tmp);
+            for (int i = 0; i < 9; i++) o[i] = src[i];
         } else {
-            synth::q6_k_block(seed, b, out + b * 210);
+            synth::q6_k_block(seed, b, out + lb * 210);
         }
     }
 }
 
-__global__ void synth_f32_kernel(uint64_t seed, int64_t n, int dist, float* out) {
+__global__ void synth_f32_kernel(uint64_t seed, int64_t cols_full, int64_t row0, int64_t col0, int64_t ncols,
+                                 int64_t n, int dist, float* out) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * blockDim.x)
-        out[i] = dist == CN_DIST_NORM_W ? synth::norm_weight_elem(seed, i) : synth::normal_elem(seed, i);
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t g = (row0 + i / ncols) * cols_full + col0 + i % ncols;
+        out[i] = dist == CN_DIST_NORM_W ? synth::norm_weight_elem(seed, g) : synth::normal_elem(seed, g);
+    }
 }
 
-__global__ void synth_f16_kernel(uint64_t seed, int64_t n, uint16_t* out) {
+__global__ void synth_f16_kernel(uint64_t seed, int64_t cols_full, int64_t row0, int64_t col0, int64_t ncols,
+                                 int64_t n, uint16_t* out) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * blockDim.x)
-        out[i] = synth::f2h(synth::normal_elem(seed, i));
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t g = (row0 + i / ncols) * cols_full + col0 + i % ncols;
+        out[i] = synth::f2h(synth::normal_elem(seed, g));
+    }
 }
 
-int synth_launch(int type, int64_t rows, int64_t cols, uint64_t seed, int dist, void* d_out,
-                 cudaStream_t s) {
-    const int64_t n = rows * cols;
+int synth_slice_launch(int type, int64_t rows, int64_t cols, int64_t row0, int64_t nrows, int64_t col0,
+                       int64_t ncols, uint64_t seed, int dist, void* d_out, cudaStream_t s) {
+    CN_CHECK(row0 >= 0 && nrows >= 0 && row0 + nrows <= rows && col0 >= 0 && ncols >= 0 && col0 + ncols <= cols,
+             CN_ERR_INVALID_ARG, "slice outside the tensor");
+    const int64_t n = nrows * ncols;
     if (n == 0) return CN_OK;
     if (type == CN_TYPE_Q4_0 || type == CN_TYPE_Q4_K || type == CN_TYPE_Q6_K) {
         int want = type == CN_TYPE_Q4_0 ? CN_DIST_CFG0_Q4_0
@@ -188,22 +203,28 @@ int synth_launch(int type, int64_t rows, int64_t cols, uint64_t seed, int dist, 
         CN_CHECK(dist == want, CN_ERR_INVALID_ARG, "distribution %d does not match type %d", dist,
                  type);
         int bs = type == CN_TYPE_Q4_0 ? 32 : 256;
-        CN_CHECK(cols % bs == 0, CN_ERR_INVALID_ARG, "cols %lld not a multiple of %d",
-                 (long long)cols, bs);
-        int64_t nb = n / bs;
-        synth_blocks_kernel<<<grid_for(nb, 128), 128, 0, s>>>(type, seed, nb, (uint8_t*)d_out);
+        CN_CHECK(cols % bs == 0 && col0 % bs == 0 && ncols % bs == 0, CN_ERR_INVALID_ARG,
+                 "columns not whole blocks of %d", bs);
+        const int64_t nbc = ncols / bs, nb = nrows * nbc;
+        synth_blocks_kernel<<<grid_for(nb, 128), 128, 0, s>>>(type, seed, cols / bs, row0, col0 / bs, nbc, nb,
+                                                              (uint8_t*)d_out);
     } else if (type == CN_TYPE_F32) {
         CN_CHECK(dist == CN_DIST_NORMAL || dist == CN_DIST_NORM_W, CN_ERR_INVALID_ARG,
                  "bad F32 distribution %d", dist);
-        synth_f32_kernel<<<grid_for(n, 256), 256, 0, s>>>(seed, n, dist, (float*)d_out);
+        synth_f32_kernel<<<grid_for(n, 256), 256, 0, s>>>(seed, cols, row0, col0, ncols, n, dist, (float*)d_out);
     } else if (type == CN_TYPE_F16) {
         CN_CHECK(dist == CN_DIST_NORMAL, CN_ERR_INVALID_ARG, "bad F16 distribution %d", dist);
-        synth_f16_kernel<<<grid_for(n, 256), 256, 0, s>>>(seed, n, (uint16_t*)d_out);
+        synth_f16_kernel<<<grid_for(n, 256), 256, 0, s>>>(seed, cols, row0, col0, ncols, n, (uint16_t*)d_out);
     } else {
         return set_error(CN_ERR_UNSUPPORTED, "no generator for type %d", type);
     }
     CN_CUDA(cudaGetLastError());
     return CN_OK;
+}
+
+int synth_launch(int type, int64_t rows, int64_t cols, uint64_t seed, int dist, void* d_out,
+                 cudaStream_t s) {
+    return synth_slice_launch(type, rows, cols, 0, rows, 0, cols, seed, dist, d_out, s);
 }
 
 }  // namespace cn

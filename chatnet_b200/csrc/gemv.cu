@@ -591,22 +591,72 @@ __global__ void xprep_kernel(const float* __restrict__ x, int K, int batch, Prep
 // x_in (other CTAs still read x_in).
 constexpr int kNormThreads = 256;
 
+// Bounded wait of one thread for an exchange: every rank's flag must reach
+// this use's sequence number; on timeout the error word is raised and the
+// caller runs on (its results are then flagged garbage).
+__device__ __forceinline__ uint32_t xchg_wait_dev(const XchgIn& xi) {
+    const uint32_t seq = *xi.seq_base * xi.uses + xi.seq_add;
+    const uint64_t t0 = globaltimer_ns();
+    for (int p = 0; p < xi.size; p++) {
+        for (;;) {
+            uint32_t f;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(xi.flags + p) : "memory");
+            if ((int32_t)(f - seq) >= 0) break;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                atomicOr(xi.err, kErrTimeout);
+                return seq;
+            }
+            __nanosleep(64);
+        }
+    }
+    return seq;
+}
+
+__global__ void xchg_wait_kernel(XchgIn xi) {
+    pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x == 0) xchg_wait_dev(xi);
+}
+
+// The exchange's summed input at element i of row b (ranks added in rank
+// order, so every rank computes the same bits).
+__device__ __forceinline__ float4 xchg_sum4(const XchgIn& xi, const float* base, size_t off) {
+    float4 s = __ldcg(reinterpret_cast<const float4*>(base + off));
+    for (int p = 1; p < xi.size; p++) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(base + p * xi.rank_stride + off));
+        s.x = __fadd_rn(s.x, v.x);
+        s.y = __fadd_rn(s.y, v.y);
+        s.z = __fadd_rn(s.z, v.z);
+        s.w = __fadd_rn(s.w, v.w);
+    }
+    return s;
+}
+
 __global__ void __launch_bounds__(kNormThreads)
     add_norm_prep_kernel(const float* __restrict__ x_in, const float* __restrict__ delta,
                          float* __restrict__ x_out, const float* __restrict__ w, float* __restrict__ y,
-                         int n, float eps, PrepTarget pt) {
+                         int n, float eps, PrepTarget pt, XchgIn xi) {
     pdl_trigger();
     pdl_wait();
     __shared__ float red[kNormThreads / 32];
     __shared__ __align__(16) float vals[256];
+    __shared__ uint32_t s_seq;
     const int u = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
     const float* xr = x_in + (size_t)b * n;
     const float* dr = delta ? delta + (size_t)b * n : nullptr;
+    // tensor parallel: delta is the sum of every rank's partial (in rank order)
+    const float* xbase = nullptr;
+    if (xi.size > 1) {
+        if (tid == 0) s_seq = xchg_wait_dev(xi);
+        __syncthreads();
+        xbase = xi.src + (s_seq & 1u) * xi.parity_stride + (size_t)b * n;
+        dr = nullptr;
+    }
     float ss = 0.f;
     for (int i = 4 * tid; i < n; i += 4 * kNormThreads) {
         float4 v = *reinterpret_cast<const float4*>(xr + i);
-        if (dr) {
-            const float4 d = *reinterpret_cast<const float4*>(dr + i);
+        if (dr || xbase) {
+            const float4 d = xbase ? xchg_sum4(xi, xbase, i) : *reinterpret_cast<const float4*>(dr + i);
             v.x = __fadd_rn(v.x, d.x);
             v.y = __fadd_rn(v.y, d.y);
             v.z = __fadd_rn(v.z, d.z);
@@ -628,8 +678,15 @@ __global__ void __launch_bounds__(kNormThreads)
     const int i = u * 256 + tid;
     if (i < n) {
         float v = xr[i];
-        if (dr) {
-            v = __fadd_rn(v, dr[i]);
+        if (dr || xbase) {
+            float d;
+            if (xbase) {
+                d = __ldcg(xbase + i);
+                for (int p = 1; p < xi.size; p++) d = __fadd_rn(d, __ldcg(xbase + p * xi.rank_stride + i));
+            } else {
+                d = dr[i];
+            }
+            v = __fadd_rn(v, d);
             x_out[(size_t)b * n + i] = v;
         }
         const float o = __fmul_rn(__fmul_rn(v, rms), w[i]);
@@ -953,15 +1010,30 @@ int gemv_prep(cudaStream_t st, int sms, const GemvOp& op, const float* d_x, cons
 }
 
 int add_norm_prep(cudaStream_t st, const float* x_in, const float* delta, float* x_out, const float* w,
-                  float* y, int n, int rows, float eps, const GemvOp* op, const GemvBufs& b) {
+                  float* y, int n, int rows, float eps, const GemvOp* op, const GemvBufs& b,
+                  const XchgIn* xin) {
+    const bool xch = xin && xin->size > 1;
     CN_CHECK(n % 4 == 0 && (reinterpret_cast<uintptr_t>(x_in) & 15) == 0 &&
                  (!delta || (reinterpret_cast<uintptr_t>(delta) & 15) == 0),
              CN_ERR_INVALID_ARG, "norm: dim must be a multiple of 4 and rows 16-byte aligned");
-    CN_CHECK(!delta || (x_out && x_out != x_in), CN_ERR_INVALID_ARG, "norm: x_out must not alias x_in");
+    CN_CHECK(!(delta || xch) || (x_out && x_out != x_in), CN_ERR_INVALID_ARG, "norm: x_out must not alias x_in");
+    CN_CHECK(!xch || (xin->src && xin->flags && xin->seq_base && xin->err &&
+                      (reinterpret_cast<uintptr_t>(xin->src) & 15) == 0 && xin->rank_stride % 4 == 0 &&
+                      xin->parity_stride % 4 == 0),
+             CN_ERR_INVALID_ARG, "norm: bad exchange input");
     PrepTarget pt = prep_target(op, b);
     if (pt.kind >= 0 && n % 256 != 0) pt.kind = -1;  // the GEMV preps for itself
+    XchgIn xi;
+    if (xch) xi = *xin;
     CN_CUDA(launch_k(true, add_norm_prep_kernel, dim3((n + 255) / 256, rows), dim3(kNormThreads), 0, st, x_in,
-                     delta, x_out, w, y, n, eps, pt));
+                     delta, x_out, w, y, n, eps, pt, xi));
+    CN_CUDA(cudaGetLastError());
+    return CN_OK;
+}
+
+int xchg_wait(cudaStream_t st, const XchgIn& xin) {
+    CN_CHECK(xin.size > 1 && xin.flags && xin.seq_base && xin.err, CN_ERR_INVALID_ARG, "bad exchange");
+    CN_CUDA(launch_k(true, xchg_wait_kernel, dim3(1), dim3(32), 0, st, xin));
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }
@@ -972,8 +1044,10 @@ int norm_prep(cudaStream_t st, const float* x, const float* w, float* y, int n, 
 }
 
 int gemv_run(cn_ctx* ctx, cudaStream_t st, const GemvOp& op, const float* d_x, const GemvBufs& b,
-             float* d_y) {
+             float* d_y, const XchgOut* xo) {
     CN_CHECK((reinterpret_cast<uintptr_t>(d_y) & 3) == 0, CN_ERR_INVALID_ARG, "y must be aligned");
+    CN_CHECK(!xo || xo->size <= 1 || op.plan.path == kPathI8, CN_ERR_UNSUPPORTED,
+             "tensor-parallel exchange needs the integer GEMV (Q4_K, batch <= 8)");
     if (!op.tma) {
         int blk = op.type == CN_TYPE_Q4_0 ? 32 : (op.type == CN_TYPE_Q4_K || op.type == CN_TYPE_Q6_K) ? 256 : 1;
         int threads = 256;
@@ -987,7 +1061,7 @@ int gemv_run(cn_ctx* ctx, cudaStream_t st, const GemvOp& op, const float* d_x, c
     }
     if (op.plan.path == kPathI8)
         return gemv_i8_run(st, ctx->dev_err, &op.map, op.rows, op.cols, op.batch, op.plan.ctas,
-                           reinterpret_cast<const uint8_t*>(b.xfrag), b.partials, b.counters, d_y);
+                           reinterpret_cast<const uint8_t*>(b.xfrag), b.partials, b.counters, d_y, xo);
     if (op.plan.path == kPathTc)
         return gemv_tc_run(st, ctx->dev_err, &op.map, op.rows, op.cols, op.batch, op.plan.ctas,
                            reinterpret_cast<const uint8_t*>(b.xfrag), b.partials, b.counters, d_y);

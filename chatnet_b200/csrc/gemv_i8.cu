@@ -23,6 +23,8 @@
 //    d * sum - dmin * sum_j m_j XS_j, times 2^-e, joins the row's fp32 sum.
 //  * Stream-K over (128-row tile, unit) as in gemv.cu, deterministic fix-up.
 // Every mbarrier wait is bounded (error word, then uniform fall-through).
+#include <stdlib.h>
+
 #include "cn_common.cuh"
 #include "cn_internal.h"
 #include "gemv_i8.cuh"
@@ -66,7 +68,22 @@ struct Args {
     float* partials;      // [2 * ctas][128][8]
     int* counters;        // [tiles][kCons], zero on entry, left zero
     uint32_t* err;
+    XchgOut xo;           // size > 1: outputs go to every rank (one matrix only)
 };
+
+// Stores output value (b, row) of matrix m: locally, or, in an exchange, into
+// every rank's buffer (peer stores over NVLink).
+__device__ __forceinline__ void store_out(const Args& a, float* y, int64_t rows, int b, int64_t row, float v,
+                                          uint32_t parity) {
+    if (a.xo.size <= 1) {
+        y[(size_t)b * rows + row] = v;
+        return;
+    }
+    const int64_t off = parity * a.xo.parity_stride + b * a.xo.dst_ld + a.xo.dst_row0 + row;
+#pragma unroll
+    for (int p = 0; p < kMaxTp; p++)
+        if (p < a.xo.size) a.xo.dst[p][off] = v;
+}
 
 // matrix of a tile, its first row in that matrix, its row count and output
 __device__ __forceinline__ int mat_of(const Args& a, int tile) {
@@ -140,7 +157,7 @@ __device__ __forceinline__ int owned_seq(int nt, int t) {
 template <int NB>
 __device__ void finish_subtile(const Args& a, int r, int t, int warp, int tile, int cta, int C,
                                int64_t total, bool shared_tile, int my_slot,
-                               const float (&acc)[Geo<NB>::NT]) {
+                               const float (&acc)[Geo<NB>::NT], uint32_t parity) {
     constexpr int NT = Geo<NB>::NT;
     const int m = mat_of(a, tile);
     const int64_t rows = pick64(a.rows, m);
@@ -151,7 +168,7 @@ __device__ void finish_subtile(const Args& a, int r, int t, int warp, int tile, 
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
                 const int b = owned_seq<NB>(nt, t);
-                if (b >= 0) y[(size_t)b * rows + row] = acc[nt];
+                if (b >= 0) store_out(a, y, rows, b, row, acc[nt], parity);
             }
         }
         return;
@@ -184,7 +201,7 @@ __device__ void finish_subtile(const Args& a, int r, int t, int warp, int tile, 
             const int slot = 2 * c + (tile == first_tile ? 0 : 1);
             s += __ldcg(a.partials + ((size_t)slot * kRows + r) * 8 + b);
         }
-        if (row < rows) y[(size_t)b * rows + row] = s;
+        if (row < rows) store_out(a, y, rows, b, row, s, parity);
     }
     __syncwarp();
     if ((threadIdx.x & 31) == 0) atomicExch(ctr, 0);
@@ -290,6 +307,8 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB>::kCtasPerSm)
 
     // ---- consumers ----
     pdl_wait();
+    const uint32_t seq = a.xo.size > 1 ? *a.xo.seq_base * a.xo.uses + a.xo.seq_add : 0u;
+    const uint32_t parity = seq & 1u;
     const int g = lane >> 2, t = lane & 3;
     const int row0 = 16 * warp + g, row1 = row0 + 8;
     const int r_own = (t & 1) ? row1 : row0;
@@ -409,19 +428,54 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB>::kCtasPerSm)
         const bool head_cut = (et == tile0) && (u0 != 0);
         const bool tail_cut = eu + seg != a.units;
         finish_subtile<NB>(a, r_own, t, warp, et, cta, C, total, head_cut || tail_cut, et == tile0 ? 0 : 1,
-                           acc);
+                           acc, parity);
         et++;
         eu = 0;
+    }
+    if (a.xo.size > 1) {
+        // exchange: once every CTA's peer stores are visible system-wide, the
+        // last CTA raises this rank's flag on every rank
+        // (the barrier orders every consumer's peer stores before thread 0's
+        // system-scope fence, which then covers them all)
+        asm volatile("bar.sync 1, %0;" ::"n"(kCons * 32) : "memory");
+        if (threadIdx.x == 0) {
+            __threadfence_system();
+            int old;
+            asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(a.xo.done) : "memory");
+            if (old == (int)gridDim.x - 1) {
+                *a.xo.done = 0;
+                __threadfence_system();
+#pragma unroll
+                for (int p = 0; p < kMaxTp; p++)
+                    if (p < a.xo.size)
+                        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.xo.flag[p]), "r"(seq) : "memory");
+            }
+        }
     }
 }
 
 // ---- host ---------------------------------------------------------------------------
 
+// Fewest units a CTA should get (CHATNET_GEMV_MIN_UNITS, default 2): small
+// GEMVs then use fewer, longer-running CTAs.
+static int min_units_per_cta() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("CHATNET_GEMV_MIN_UNITS");
+        v = e ? atoi(e) : 2;
+        if (v < 1) v = 1;
+    }
+    return v;
+}
+
 int gemv_i8_ctas(int sms, int tiles, int units, int batch) {
-    // every resident CTA, each at least 2 units; at most 8 CTAs share a tile
+    // every resident CTA, each at least min_units_per_cta() units (but at
+    // least one CTA per SM); at most 8 CTAs share a tile
     const int per_sm = i8::n_tiles(batch) == 1 ? i8::Geo<1>::kCtasPerSm : i8::Geo<8>::kCtasPerSm;
     const int64_t total = (int64_t)tiles * units;
-    int64_t want = total / 2 > 0 ? total / 2 : 1;
+    int64_t want = total / min_units_per_cta();
+    if (want < sms) want = total / 2 < sms ? total / 2 : sms;
+    if (want < 1) want = 1;
     const int64_t cap = (int64_t)tiles * 7;
     if (want > cap) want = cap;
     return per_sm * sms < want ? per_sm * sms : (int)want;
@@ -448,10 +502,12 @@ int gemv_i8_prepare() {
 
 int gemv_i8_run_group(cudaStream_t st, uint32_t* err, int nmat, const CUtensorMap* const* maps,
                       const int64_t* rows, int64_t cols, int batch, int ctas, const uint8_t* xrec,
-                      float* partials, int* counters, float* const* y) {
+                      float* partials, int* counters, float* const* y, const XchgOut* xo) {
     CN_CHECK(batch >= 1 && batch <= i8::kMaxNB && cols % 256 == 0 && ctas > 0 && nmat >= 1 &&
                  nmat <= i8::kMaxMats,
              CN_ERR_INVALID_ARG, "integer GEMV: bad shape");
+    CN_CHECK(!xo || xo->size <= 1 || (nmat == 1 && xo->size <= kMaxTp && xo->done && xo->seq_base),
+             CN_ERR_INVALID_ARG, "integer GEMV: bad exchange");
     int rc = gemv_i8_prepare();
     if (rc) return rc;
     i8::Maps mp;
@@ -474,6 +530,7 @@ int gemv_i8_run_group(cudaStream_t st, uint32_t* err, int nmat, const CUtensorMa
     a.partials = partials;
     a.counters = counters;
     a.err = err;
+    if (xo) a.xo = *xo;
     switch (batch) {
 #define CN_I8(NB)                                                                                  \
     case NB:                                                                                       \
@@ -488,8 +545,9 @@ int gemv_i8_run_group(cudaStream_t st, uint32_t* err, int nmat, const CUtensorMa
 }
 
 int gemv_i8_run(cudaStream_t st, uint32_t* err, const CUtensorMap* map, int64_t rows, int64_t cols,
-                int batch, int ctas, const uint8_t* xrec, float* partials, int* counters, float* y) {
-    return gemv_i8_run_group(st, err, 1, &map, &rows, cols, batch, ctas, xrec, partials, counters, &y);
+                int batch, int ctas, const uint8_t* xrec, float* partials, int* counters, float* y,
+                const XchgOut* xo) {
+    return gemv_i8_run_group(st, err, 1, &map, &rows, cols, batch, ctas, xrec, partials, counters, &y, xo);
 }
 
 }  // namespace cn

@@ -54,6 +54,10 @@ struct cn_llama {
     float *x = nullptr, *x2 = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr,
           *att = nullptr, *tmp = nullptr, *gate = nullptr, *up = nullptr, *logits = nullptr, *part = nullptr;
     int* attn_ctr = nullptr;  // [max_batch][n_kv] attention merge counters
+    // tensor parallelism: this rank's share of heads, FFN rows and vocabulary
+    cn_tp* tp = nullptr;
+    int nh = 0, nkv = 0, qdim = 0, hid = 0, vocab_l = 0, tp_rank = 0;
+    bool logits_owned = true;
     int *tokens = nullptr, *pos = nullptr, *amax = nullptr;
     int *h_tokens = nullptr, *h_pos = nullptr, *h_amax = nullptr;
     cn::GemvBufs gb{nullptr, nullptr, nullptr, nullptr, nullptr};
@@ -118,7 +122,7 @@ static int build_step(cn_llama* m, int B) {
         if (gemv_group_make(m->ctx, o + 4, 2, &st.gu[l]) != CN_OK) st.gu[l].n = 0;
     }
     set_error(CN_OK, "");
-    int rc = attention_plan(c.n_heads, c.n_kv_heads, c.head_dim, c.ctx_len, B, m->ctx->sms,
+    int rc = attention_plan(m->nh, m->nkv, c.head_dim, c.ctx_len, B, m->ctx->sms,
                             c.kv_dtype == CN_KV_F16, &st.ap);
     if (rc) return rc;
     if ((rc = attention_prepare(st.ap))) return rc;
@@ -157,25 +161,28 @@ static int gemv_g(cn_llama* m, cudaStream_t s, const GemvGroup& g, const float* 
 }
 
 static int gemv(cn_llama* m, cudaStream_t s, const GemvOp& op, const float* x, float* y,
-                PrepCache& pc) {
+                PrepCache& pc, const XchgOut* xo = nullptr) {
     if (op.tma && !pc.holds(x, op)) {
         int rc = gemv_prep(s, m->ctx->sms, op, x, m->gb);
         if (rc) return rc;
         pc.set(x, op);
     }
-    return gemv_run(m->ctx, s, op, x, m->gb, y);
+    return gemv_run(m->ctx, s, op, x, m->gb, y, xo);
 }
 
 // Residual add of the pending delta (if any) into the stream, RMSNorm into
 // xn, and the records of the GEMV that reads xn next, in one kernel.  *x is
 // the current stream; with a delta it moves to the other buffer.
+// (With tensor parallelism the pending delta is the exchange `xin`: the
+// sum of every rank's partial output.)
 static int norm(cn_llama* m, cudaStream_t s, const cn_tensor* w, int B, const GemvOp& next, float** x,
-                const float** delta, PrepCache& pc) {
-    float* out = *delta ? (*x == m->x ? m->x2 : m->x) : nullptr;
-    int rc = add_norm_prep(s, *x, *delta, out, (const float*)w->d, m->xn, m->cfg.dim, B, m->cfg.rms_eps,
-                           &next, m->gb);
+                const float** delta, PrepCache& pc, const XchgIn* xin = nullptr) {
+    const bool add = *delta || (xin && xin->size > 1);
+    float* out = add ? (*x == m->x ? m->x2 : m->x) : nullptr;
+    int rc = add_norm_prep(s, *x, xin && xin->size > 1 ? nullptr : *delta, out, (const float*)w->d, m->xn,
+                           m->cfg.dim, B, m->cfg.rms_eps, &next, m->gb, xin);
     if (rc) return rc;
-    if (*delta) *x = out;
+    if (add) *x = out;
     *delta = nullptr;
     pc = PrepCache();
     if (next.tma && m->cfg.dim % 256 == 0) pc.set(m->xn, next);
@@ -187,17 +194,26 @@ static int norm(cn_llama* m, cudaStream_t s, const cn_tensor* w, int B, const Ge
 static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
     const cn_llama_config& c = m->cfg;
     Step& st = m->steps[B];
-    const int dim = c.dim, hid = c.hidden_dim, kvd = m->kvdim;
+    const int hid = m->hid, kvd = m->kvdim, qdim = m->qdim;
     const cn_tensor* emb = m->t[T_EMB];
-    int rc = launch_embed(emb->type, emb->d, emb->row_bytes, m->tokens, c.vocab, dim, B, m->x,
-                          m->ctx->dev_err, s);
+    // tensor parallelism: exchanges per step (O and down of every layer,
+    // then lm_head); this step's sequence numbers derive from a counter the
+    // first kernel bumps
+    const bool tp = m->tp && m->tp->size > 1;
+    const uint32_t uses = 2u * (uint32_t)c.n_layers + 1u;
+    int rc;
+    if (tp && (rc = tp_step_launch(m->tp, s))) return rc;
+    rc = launch_embed(emb->type, emb->d, emb->row_bytes, m->tokens, c.vocab, c.dim, B, m->x,
+                      m->ctx->dev_err, s);
     if (rc) return rc;
     PrepCache pc;
     float* x = m->x;
     const float* delta = nullptr;  // output of the last projection, not yet added to x
+    XchgIn xin;                    // tensor parallel: the exchange that delivers it
     for (int l = 0; l < c.n_layers; l++) {
         const GemvOp* ops = &st.ops[(size_t)l * 7];
-        if ((rc = norm(m, s, LT(m, l, L_ANORM), B, ops[0], &x, &delta, pc))) return rc;
+        if ((rc = norm(m, s, LT(m, l, L_ANORM), B, ops[0], &x, &delta, pc, &xin))) return rc;
+        xin = XchgIn();
         if (st.qkv[l].n) {
             float* ys[3] = {m->q, m->k, m->v};
             if ((rc = gemv_g(m, s, st.qkv[l], m->xn, ys, pc))) return rc;
@@ -214,10 +230,10 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
         ra.pos_dev = m->pos;
         ra.pos_host = 0;
         ra.batch = B;
-        ra.n_heads = c.n_heads;
-        ra.n_kv = c.n_kv_heads;
+        ra.n_heads = m->nh;
+        ra.n_kv = m->nkv;
         ra.hd = c.head_dim;
-        ra.q_stride = dim;
+        ra.q_stride = qdim;
         ra.kv_stride = kvd;
         ra.kcache = m->kc;
         ra.vcache = m->vc;
@@ -234,10 +250,10 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
         aa.pos_dev = m->pos;
         aa.pos_host = 0;
         aa.batch = B;
-        aa.n_heads = c.n_heads;
-        aa.n_kv = c.n_kv_heads;
+        aa.n_heads = m->nh;
+        aa.n_kv = m->nkv;
         aa.hd = c.head_dim;
-        aa.q_stride = dim;
+        aa.q_stride = qdim;
         aa.cache_seq_stride = m->seq_stride;
         aa.cache_layer_off = ra.cache_layer_off;
         aa.kv_f16 = ra.kv_f16;
@@ -245,15 +261,22 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
         aa.part = m->part;
         aa.counters = m->attn_ctr;
         aa.out = m->att;
-        aa.out_stride = dim;
+        aa.out_stride = qdim;
         aa.prep = prep_target(&ops[3], m->gb);
-        if ((c.n_heads / c.n_kv_heads) * c.head_dim % 256 != 0) aa.prep.kind = -1;
+        if ((m->nh / m->nkv) * c.head_dim % 256 != 0) aa.prep.kind = -1;
         if ((rc = launch_attention(aa, st.ap, s))) return rc;
         pc = PrepCache();
         if (aa.prep.kind >= 0) pc.set(m->att, ops[3]);
-        if ((rc = gemv(m, s, ops[3], m->att, m->tmp, pc))) return rc;
-        delta = m->tmp;
-        if ((rc = norm(m, s, LT(m, l, L_FNORM), B, ops[4], &x, &delta, pc))) return rc;
+        if (tp) {
+            const XchgOut xo = tp_reduce_out(m->tp, uses, 2u * l, 0);
+            if ((rc = gemv(m, s, ops[3], m->att, m->tmp, pc, &xo))) return rc;
+            xin = tp_reduce_in(m->tp, uses, 2u * l, m->ctx->dev_err);
+        } else {
+            if ((rc = gemv(m, s, ops[3], m->att, m->tmp, pc))) return rc;
+            delta = m->tmp;
+        }
+        if ((rc = norm(m, s, LT(m, l, L_FNORM), B, ops[4], &x, &delta, pc, &xin))) return rc;
+        xin = XchgIn();
         if (st.gu[l].n) {
             float* ys[2] = {m->gate, m->up};
             if ((rc = gemv_g(m, s, st.gu[l], m->xn, ys, pc))) return rc;
@@ -265,22 +288,36 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
         if ((rc = launch_silu_prep(m->gate, m->up, hid, B, spt, s))) return rc;
         pc = PrepCache();
         if (spt.kind >= 0 && hid % 256 == 0) pc.set(m->gate, ops[6]);
-        if ((rc = gemv(m, s, ops[6], m->gate, m->tmp, pc))) return rc;
-        delta = m->tmp;
+        if (tp) {
+            const XchgOut xo = tp_reduce_out(m->tp, uses, 2u * l + 1u, 1);
+            if ((rc = gemv(m, s, ops[6], m->gate, m->tmp, pc, &xo))) return rc;
+            xin = tp_reduce_in(m->tp, uses, 2u * l + 1u, m->ctx->dev_err);
+        } else {
+            if ((rc = gemv(m, s, ops[6], m->gate, m->tmp, pc))) return rc;
+            delta = m->tmp;
+        }
     }
     const GemvOp& head = st.ops[(size_t)c.n_layers * 7];
-    if ((rc = norm(m, s, m->t[T_ONORM], B, head, &x, &delta, pc))) return rc;
-    if ((rc = gemv(m, s, head, m->xn, m->logits, pc))) return rc;
+    if ((rc = norm(m, s, m->t[T_ONORM], B, head, &x, &delta, pc, &xin))) return rc;
+    if (tp) {
+        // lm_head rows of this rank go to every rank's logits (all-gather)
+        const XchgOut xo = tp_gather_out(m->tp, m->vocab_l, uses, uses - 1u, 2);
+        if ((rc = gemv(m, s, head, m->xn, m->tmp, pc, &xo))) return rc;
+        if ((rc = xchg_wait(s, tp_reduce_in(m->tp, uses, uses - 1u, m->ctx->dev_err)))) return rc;
+    } else {
+        if ((rc = gemv(m, s, head, m->xn, m->logits, pc))) return rc;
+    }
     return launch_argmax(m->logits, c.vocab, B, m->amax, s);
 }
 
-static int run_step(cn_llama* m, int B) {
+// Builds the step for B sequences and, with graphs on, captures it once.
+static int prepare_step(cn_llama* m, int B) {
     cudaStream_t s = m->ctx->stream;
     int rc = build_step(m, B);
     if (rc) return rc;
     Step& st = m->steps[B];
-    if (!m->use_graph) return enqueue_step(m, B, s);
-    if (!st.graph) {
+    if (!m->use_graph || st.graph) return CN_OK;
+    {
         cudaGraph_t g = nullptr;
         CN_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
         rc = enqueue_step(m, B, s);
@@ -297,7 +334,14 @@ static int run_step(cn_llama* m, int B) {
             return cuda_error(e, "cudaGraphInstantiate");
         }
     }
-    CN_CUDA(cudaGraphLaunch(st.graph, s));
+    return CN_OK;
+}
+
+static int run_step(cn_llama* m, int B) {
+    int rc = prepare_step(m, B);
+    if (rc) return rc;
+    if (!m->use_graph) return enqueue_step(m, B, m->ctx->stream);
+    CN_CUDA(cudaGraphLaunch(m->steps[B].graph, m->ctx->stream));
     return CN_OK;
 }
 
@@ -311,15 +355,19 @@ static int check_dev_err_reset(cn_llama* m) {
     return set_error(CN_ERR_INVALID_ARG, "token id or position out of range (0x%x)", e);
 }
 
-__global__ void kv_synth_kernel(uint64_t seed, int layers, int npos, int ctx, int kvd, int f16,
-                                void* out) {
+// Fills the cache's first npos positions with the generator's values of the
+// WHOLE model's cache ([layers*ctx, kvd_full]): a tensor-parallel rank holds
+// columns [col0, col0 + kvd) of it.
+__global__ void kv_synth_kernel(uint64_t seed, int layers, int npos, int ctx, int kvd, int kvd_full, int col0,
+                                int f16, void* out) {
     const int64_t n = (int64_t)layers * npos * kvd;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         int64_t l = i / ((int64_t)npos * kvd);
         int64_t r = i % ((int64_t)npos * kvd);
         int64_t idx = (l * ctx + r / kvd) * kvd + r % kvd;
-        float v = synth::normal_elem(seed, (uint64_t)idx);
+        int64_t g = (l * ctx + r / kvd) * kvd_full + col0 + r % kvd;
+        float v = synth::normal_elem(seed, (uint64_t)g);
         if (f16) reinterpret_cast<__half*>(out)[idx] = __float2half_rn(v);
         else reinterpret_cast<float*>(out)[idx] = v;
     }
@@ -328,6 +376,7 @@ __global__ void kv_synth_kernel(uint64_t seed, int layers, int npos, int ctx, in
 static void free_model(cn_llama* m) {
     for (int b = 0; b <= kMaxBatch; b++)
         if (m->steps[b].graph) cudaGraphExecDestroy(m->steps[b].graph);
+    if (!m->logits_owned) m->logits = nullptr;
     void* bufs[] = {m->kc, m->vc, m->rope, m->x, m->x2, m->attn_ctr, m->xn, m->q, m->k, m->v, m->att, m->tmp,
                     m->gate, m->up, m->logits, m->part, m->tokens, m->pos, m->amax,
                     m->gb.xfrag, m->gb.xsum, m->gb.partials, m->gb.counters, m->gb.xinv};
@@ -344,11 +393,12 @@ using namespace cn;
 
 extern "C" {
 
-int cn_llama_create(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* const* tensors,
-                    int n_tensors, cn_llama** out) {
+static int create_model(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* const* tensors, int n_tensors,
+                        cn_tp* tp, cn_llama** out) {
     CN_CHECK(ctx && cfg && tensors && out, CN_ERR_INVALID_ARG, "null argument");
     *out = nullptr;
     const cn_llama_config c = *cfg;
+    const int W = tp ? tp->size : 1, R = tp ? tp->rank : 0;
     CN_CHECK(c.n_layers > 0 && c.dim > 0 && c.hidden_dim > 0 && c.n_heads > 0 && c.n_kv_heads > 0 &&
                  c.head_dim > 0 && c.vocab > 0 && c.ctx_len > 0,
              CN_ERR_INVALID_ARG, "non-positive hyper-parameter");
@@ -361,29 +411,40 @@ int cn_llama_create(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* const* t
              "bad kv_dtype %d", c.kv_dtype);
     CN_CHECK(n_tensors == CN_LLAMA_TENSORS(c.n_layers), CN_ERR_INVALID_ARG,
              "expected %d tensors, got %d", CN_LLAMA_TENSORS(c.n_layers), n_tensors);
-    const int kvd = c.n_kv_heads * c.head_dim;
+    if (tp) {
+        CN_CHECK(tp->ctx == ctx && (W == 1 || tp->connected), CN_ERR_INVALID_ARG,
+                 "tensor-parallel group not connected on this context");
+        CN_CHECK(c.n_kv_heads % W == 0 && c.hidden_dim % W == 0 && c.vocab % W == 0, CN_ERR_INVALID_ARG,
+                 "kv heads, hidden_dim and vocab must divide by the group size %d", W);
+        CN_CHECK(tp->dim == c.dim && tp->vocab == c.vocab && tp->max_batch >= c.max_batch, CN_ERR_INVALID_ARG,
+                 "tensor-parallel buffers sized for another model");
+    }
+    // this rank's share (the whole model when W == 1)
+    const int nh = c.n_heads / W, nkv = c.n_kv_heads / W, hid = c.hidden_dim / W, vocab_l = c.vocab / W;
+    const int qdim = nh * c.head_dim;
+    const int kvd = nkv * c.head_dim;
     int rc;
     if ((rc = check_shape(tensors[T_EMB], "token_embd.weight", c.vocab, c.dim, false))) return rc;
-    if ((rc = check_shape(tensors[T_OUT], "output.weight", c.vocab, c.dim, false))) return rc;
+    if ((rc = check_shape(tensors[T_OUT], "output.weight", vocab_l, c.dim, false))) return rc;
     if ((rc = check_shape(tensors[T_ONORM], "output_norm.weight", 1, c.dim, true))) return rc;
     for (int l = 0; l < c.n_layers; l++) {
         const cn_tensor* const* L = tensors + 3 + 9 * l;
         if ((rc = check_shape(L[L_ANORM], "attn_norm.weight", 1, c.dim, true))) return rc;
-        if ((rc = check_shape(L[L_Q], "attn_q.weight", c.dim, c.dim, false))) return rc;
+        if ((rc = check_shape(L[L_Q], "attn_q.weight", qdim, c.dim, false))) return rc;
         if ((rc = check_shape(L[L_K], "attn_k.weight", kvd, c.dim, false))) return rc;
         if ((rc = check_shape(L[L_V], "attn_v.weight", kvd, c.dim, false))) return rc;
-        if ((rc = check_shape(L[L_O], "attn_output.weight", c.dim, c.dim, false))) return rc;
+        if ((rc = check_shape(L[L_O], "attn_output.weight", c.dim, qdim, false))) return rc;
         if ((rc = check_shape(L[L_FNORM], "ffn_norm.weight", 1, c.dim, true))) return rc;
-        if ((rc = check_shape(L[L_GATE], "ffn_gate.weight", c.hidden_dim, c.dim, false))) return rc;
-        if ((rc = check_shape(L[L_UP], "ffn_up.weight", c.hidden_dim, c.dim, false))) return rc;
-        if ((rc = check_shape(L[L_DOWN], "ffn_down.weight", c.dim, c.hidden_dim, false))) return rc;
+        if ((rc = check_shape(L[L_GATE], "ffn_gate.weight", hid, c.dim, false))) return rc;
+        if ((rc = check_shape(L[L_UP], "ffn_up.weight", hid, c.dim, false))) return rc;
+        if ((rc = check_shape(L[L_DOWN], "ffn_down.weight", c.dim, hid, false))) return rc;
     }
     for (int i = 0; i < n_tensors; i++)
         CN_CHECK(tensors[i]->ctx == ctx, CN_ERR_INVALID_ARG, "tensor %d belongs to another context", i);
     {
         AttnPlan ap;
-        if ((rc = attention_plan(c.n_heads, c.n_kv_heads, c.head_dim, c.ctx_len, c.max_batch,
-                                 ctx->sms, c.kv_dtype == CN_KV_F16, &ap)))
+        if ((rc = attention_plan(nh, nkv, c.head_dim, c.ctx_len, c.max_batch, ctx->sms,
+                                 c.kv_dtype == CN_KV_F16, &ap)))
             return rc;
     }
 
@@ -393,6 +454,13 @@ int cn_llama_create(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* const* t
     m->ctx = ctx;
     m->cfg = c;
     m->t.assign(tensors, tensors + n_tensors);
+    m->tp = (tp && W > 1) ? tp : nullptr;
+    m->tp_rank = R;
+    m->nh = nh;
+    m->nkv = nkv;
+    m->qdim = qdim;
+    m->hid = hid;
+    m->vocab_l = vocab_l;
     m->kvdim = kvd;
     m->kv_elem = c.kv_dtype == CN_KV_F16 ? 2 : 4;
     m->seq_stride = (int64_t)c.n_layers * c.ctx_len * kvd;
@@ -421,15 +489,20 @@ int cn_llama_create(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* const* t
                                    cudaMemcpyHostToDevice);
         if (e != cudaSuccess) return fail(cuda_error(e, "rope upload"));
     }
-    const size_t fd = (size_t)B * c.dim * 4, fk = (size_t)B * kvd * 4, fh = (size_t)B * c.hidden_dim * 4;
+    const size_t fd = (size_t)B * c.dim * 4, fq = (size_t)B * qdim * 4, fk = (size_t)B * kvd * 4,
+                 fh = (size_t)B * hid * 4;
+    if (m->tp) {
+        m->logits = tp_logits(m->tp);  // all-gathered by the lm_head GEMVs
+        m->logits_owned = false;
+    }
     if ((rc = dmalloc((void**)&m->x, fd)) || (rc = dmalloc((void**)&m->x2, fd)) ||
         (rc = dmalloc((void**)&m->xn, fd)) ||
-        (rc = dmalloc((void**)&m->attn_ctr, (size_t)B * c.n_kv_heads * sizeof(int))) ||
-        (rc = dmalloc((void**)&m->q, fd)) || (rc = dmalloc((void**)&m->k, fk)) ||
-        (rc = dmalloc((void**)&m->v, fk)) || (rc = dmalloc((void**)&m->att, fd)) ||
+        (rc = dmalloc((void**)&m->attn_ctr, (size_t)B * nkv * sizeof(int))) ||
+        (rc = dmalloc((void**)&m->q, fq)) || (rc = dmalloc((void**)&m->k, fk)) ||
+        (rc = dmalloc((void**)&m->v, fk)) || (rc = dmalloc((void**)&m->att, fq)) ||
         (rc = dmalloc((void**)&m->tmp, fd)) || (rc = dmalloc((void**)&m->gate, fh)) ||
         (rc = dmalloc((void**)&m->up, fh)) ||
-        (rc = dmalloc((void**)&m->logits, (size_t)B * c.vocab * 4)) ||
+        (!m->tp && (rc = dmalloc((void**)&m->logits, (size_t)B * c.vocab * 4))) ||
         (rc = dmalloc((void**)&m->tokens, B * 4)) || (rc = dmalloc((void**)&m->pos, B * 4)) ||
         (rc = dmalloc((void**)&m->amax, B * 4)))
         return fail(rc);
@@ -438,7 +511,7 @@ int cn_llama_create(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* const* t
         size_t part = 0;
         for (int b = 1; b <= B; b++) {
             AttnPlan ap;
-            attention_plan(c.n_heads, c.n_kv_heads, c.head_dim, c.ctx_len, b, ctx->sms, c.kv_dtype == CN_KV_F16, &ap);
+            attention_plan(nh, nkv, c.head_dim, c.ctx_len, b, ctx->sms, c.kv_dtype == CN_KV_F16, &ap);
             if (ap.part_floats > part) part = ap.part_floats;
         }
         if ((rc = dmalloc((void**)&m->part, part * 4))) return fail(rc);
@@ -494,6 +567,25 @@ int cn_llama_create(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* const* t
     set_error(CN_OK, "");
     *out = m;
     return CN_OK;
+}
+
+int cn_llama_create(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* const* tensors,
+                    int n_tensors, cn_llama** out) {
+    return create_model(ctx, cfg, tensors, n_tensors, nullptr, out);
+}
+
+int cn_llama_create_tp(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* const* tensors, int n_tensors,
+                       cn_tp* tp, cn_llama** out) {
+    CN_CHECK(tp, CN_ERR_INVALID_ARG, "null tensor-parallel group");
+    return create_model(ctx, cfg, tensors, n_tensors, tp, out);
+}
+
+int cn_llama_prepare(cn_llama* m, int batch) {
+    CN_CHECK(m, CN_ERR_INVALID_ARG, "null model");
+    CN_CHECK(batch >= 1 && batch <= m->cfg.max_batch, CN_ERR_INVALID_ARG,
+             "batch %d outside [1, %d]", batch, m->cfg.max_batch);
+    cudaSetDevice(m->ctx->device);
+    return prepare_step(m, batch);
 }
 
 int cn_llama_destroy(cn_llama* m) {
@@ -692,10 +784,11 @@ int cn_llama_kv_synth(cn_llama* m, int seq, int npos, uint64_t seed_k, uint64_t 
         int64_t n = (int64_t)m->cfg.n_layers * npos * m->kvdim;
         int blocks = (int)((n + 255) / 256 > 148 * 64 ? 148 * 64 : (n + 255) / 256);
         int f16 = m->cfg.kv_dtype == CN_KV_F16;
+        const int kvd_full = m->cfg.n_kv_heads * m->cfg.head_dim, col0 = m->tp_rank * m->kvdim;
         kv_synth_kernel<<<blocks, 256, 0, s>>>(seed_k, m->cfg.n_layers, npos, m->cfg.ctx_len, m->kvdim,
-                                               f16, kb);
+                                               kvd_full, col0, f16, kb);
         kv_synth_kernel<<<blocks, 256, 0, s>>>(seed_v, m->cfg.n_layers, npos, m->cfg.ctx_len, m->kvdim,
-                                               f16, vb);
+                                               kvd_full, col0, f16, vb);
         CN_CUDA(cudaGetLastError());
     }
     CN_CUDA(cudaStreamSynchronize(s));

@@ -74,18 +74,42 @@ def tensor_shape(cfg: LlamaConfig, name: str) -> tuple[int, int]:
             "ffn_down": (cfg.dim, cfg.hidden_dim)}[kind]
 
 
+def shard_region(cfg: LlamaConfig, name: str, rank: int, size: int) -> tuple[int, int, int, int]:
+    """(row0, nrows, col0, ncols) of tensor `name` held by tensor-parallel rank
+    `rank` of `size`: rows of q/k/v/gate/up/lm_head (heads, FFN rows,
+    vocabulary), columns of O/down (their input), everything else whole."""
+    rows, cols = tensor_shape(cfg, name)
+    if size == 1 or name == "token_embd.weight" or name.endswith("norm.weight"):
+        return 0, rows, 0, cols
+    kind = "output" if name == "output.weight" else name.split(".")[2]
+    if kind in ("attn_output", "ffn_down"):
+        n = cols // size
+        return 0, rows, rank * n, n
+    n = rows // size
+    return rank * n, n, 0, cols
+
+
 class CudaLlamaModel:
     """IModel for Llama on one B200 (cn_llama_*)."""
 
-    def __init__(self, ctx, cfg: LlamaConfig, tensors: list):
-        self.ctx, self.cfg = ctx, cfg
+    def __init__(self, ctx, cfg: LlamaConfig, tensors: list, tp=None):
+        """tensors: the whole model's (or, with `tp`, this rank's shards, see shard_shape)."""
+        self.ctx, self.cfg, self.tp = ctx, cfg, tp
         self._tensors = list(tensors)  # keep the borrowed weights alive
         arr = (C.c_void_p * len(tensors))(*[t.handle for t in tensors])
         h = C.c_void_p()
         c = cfg.to_c()
-        check(N.lib().cn_llama_create(ctx.handle, C.byref(c), arr, len(tensors), C.byref(h)),
-              "cn_llama_create")
+        if tp is None:
+            check(N.lib().cn_llama_create(ctx.handle, C.byref(c), arr, len(tensors), C.byref(h)),
+                  "cn_llama_create")
+        else:
+            check(N.lib().cn_llama_create_tp(ctx.handle, C.byref(c), arr, len(tensors), tp.handle,
+                                             C.byref(h)), "cn_llama_create_tp")
         self.handle = h.value
+
+    def prepare(self, batch: int) -> None:
+        """Build and graph-capture the step without running it."""
+        check(N.lib().cn_llama_prepare(self.handle, batch), "cn_llama_prepare")
 
     # IModel.Forward
     def forward(self, token_ids, position: int, logits: np.ndarray | None = None) -> np.ndarray:

@@ -100,6 +100,15 @@ int cn_tensor_upload(cn_ctx* ctx, const void* host_blocks, uint64_t bytes, int t
 int cn_tensor_synth(cn_ctx* ctx, int type, int64_t rows, int64_t cols, uint64_t seed,
                     int dist, cn_tensor** out);
 
+/* Like cn_tensor_synth, but allocates and fills only the region
+ * [row0, row0 + nrows) x [col0, col0 + ncols) of the rows x cols tensor that
+ * cn_tensor_synth would produce (columns in whole blocks): a tensor-parallel
+ * rank generates its own shard.  (no reference counterpart: synthetic
+ * inputs) */
+int cn_tensor_synth_slice(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int64_t row0,
+                          int64_t nrows, int64_t col0, int64_t ncols, uint64_t seed, int dist,
+                          cn_tensor** out);
+
 /* Copies a tensor's bytes back to host memory (bytes must match). */
 int cn_tensor_download(const cn_tensor* t, void* host, uint64_t bytes);
 int cn_tensor_free(cn_tensor* t);
@@ -232,6 +241,37 @@ int cn_llama_step_kernels(cn_llama* m, int batch, int* out_count);
  * counterpart: roofline measurement) */
 int cn_llama_time_gemv(cn_llama* m, int proj, int batch, int iters, float* us_per_launch,
                        double* bytes_per_launch);
+
+/* ---- tensor parallelism (one process per GPU) ---------------------------
+ * (no reference counterpart: the reference runs on one CPU.)  Rank r of a
+ * group of `size` GPUs holds shards of every projection: q/k/v/gate/up and
+ * lm_head rows (r-th contiguous slice of heads, FFN rows, vocabulary), O and
+ * down columns (r-th slice of their input).  The partial outputs of O and
+ * down, and the lm_head slices, are exchanged inside the GEMV epilogue:
+ * every value is stored straight into each rank's buffer over NVLink (CUDA
+ * IPC), and the consumer kernel waits for every rank's flag.  Usage: every
+ * rank calls cn_tp_create, shares cn_tp_handle's bytes with the others (any
+ * host channel), calls cn_tp_connect with all ranks' handles in rank order,
+ * then cn_llama_create_tp.  All ranks must then run the same sequence of
+ * steps; a rank that stops makes the others' kernels give up after ~2 s
+ * (CN_ERR_TIMEOUT), after which the group must be rebuilt. */
+typedef struct cn_tp cn_tp;
+#define CN_TP_HANDLE_BYTES 64
+int cn_tp_create(cn_ctx* ctx, int rank, int size, int max_batch, int dim, int vocab, cn_tp** out);
+int cn_tp_handle(const cn_tp* tp, void* handle_out /* CN_TP_HANDLE_BYTES */);
+int cn_tp_connect(cn_tp* tp, const void* handles /* size * CN_TP_HANDLE_BYTES, rank order */);
+int cn_tp_destroy(cn_tp* tp);
+/* cn_llama_create for rank tp->rank of a tensor-parallel group: cfg is the
+ * whole model's; the tensors are this rank's shards (shapes as for
+ * cn_llama_create with n_heads, n_kv_heads, hidden_dim and vocab divided by
+ * the group size for the sharded dimensions).  The exchanged projections
+ * must run on the integer Q4_K GEMV (Q4_K weights, max_batch <= 8). */
+int cn_llama_create_tp(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* const* tensors,
+                       int n_tensors, cn_tp* tp, cn_llama** out);
+/* Builds (and graph-captures) the step for `batch` sequences without running
+ * it, so a tensor-parallel group can synchronise on the host before its
+ * first step.  (no reference counterpart) */
+int cn_llama_prepare(cn_llama* m, int batch);
 
 /* KV cache access for seeding and checking (no reference counterpart; the
  * reference fills its cache only through Forward).  Element type follows

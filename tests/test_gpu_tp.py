@@ -1,0 +1,84 @@
+"""Tensor parallelism across GPUs (one process per GPU, cn_tp_* + CUDA IPC):
+a small Q4_K Llama sharded over 2 ranks decodes the same logits as the
+oracle's single-CPU restatement (max relative error 1e-3, equal argmax), and
+every rank ends with bitwise the same all-gathered logits.  Needs two GPUs;
+skipped otherwise."""
+from __future__ import annotations
+
+import multiprocessing as mp
+import queue
+
+import numpy as np
+import pytest
+import torch
+
+import chatnet_b200 as cn
+from chatnet_b200 import configs as cf
+from chatnet_b200.llama import tensor_names
+from tests import _oracle
+from tests.parity import REL_TOL, rel_err
+from tests.tp_worker import run_rank
+
+pytestmark = pytest.mark.gpu
+
+
+def tp_dc(max_batch=1, n_layers=2):
+    dc = cf.with_layers(cf.CONFIGS[4], n_layers, max_batch)
+    m = cf.replace(dc.model, dim=512, hidden_dim=1024, n_heads=8, n_kv_heads=2, head_dim=64,
+                   vocab=512, ctx_len=64, kv_f16=True)
+    return cf.replace(dc, model=m, kv_filled=20, decode_pos=20)
+
+
+def run_group(dc, size, steps):
+    ctx = mp.get_context("spawn")
+    to_parent = ctx.Queue()
+    to_child = [ctx.Queue() for _ in range(size)]
+    procs = [ctx.Process(target=run_rank, args=(r, size, dc, steps, to_parent, to_child[r]), daemon=True)
+             for r in range(size)]
+    for p in procs:
+        p.start()
+    try:
+        def collect(kind):
+            got = {}
+            while len(got) < size:
+                k, r, v = to_parent.get(timeout=300)
+                if k == "error":
+                    raise AssertionError(f"rank {r}: {v}")
+                assert k == kind, (k, kind)
+                got[r] = v
+            return [got[r] for r in range(size)]
+        handles = collect("handle")
+        for q in to_child:
+            q.put(handles)
+        collect("ready")
+        for q in to_child:
+            q.put("go")
+        return collect("done")
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("batch", [1, 3])
+def test_tp2_decode_matches_oracle(oracle, batch):
+    dc = tp_dc(max_batch=batch)
+    steps = 3
+    res = run_group(dc, 2, steps)
+    # every rank holds the same all-gathered logits
+    for s in range(steps):
+        np.testing.assert_array_equal(res[0][s][0], res[1][s][0])
+        np.testing.assert_array_equal(res[0][s][1], res[1][s][1])
+    host = cf.host_tensors(dc)
+    names = tensor_names(dc.model.n_layers)
+    types = [cf.tensor_type(dc, n) for n in names]
+    for b in range(batch):
+        k, v = cf.host_kv(dc, b)
+        orc = _oracle.OracleLlama(oracle, dc.model, host, types, names, k.copy(), v.copy())
+        for s in range(steps):
+            ref = orc.forward([cf.token(dc, b, s)], dc.decode_pos + s)
+            got = res[0][s][0][b]
+            assert rel_err(got, ref) <= REL_TOL, (b, s, rel_err(got, ref))
+            assert int(res[0][s][1][b]) == int(np.argmax(ref))
