@@ -151,6 +151,13 @@ class Context:
               "cn_matvec")
         return y[0] if squeeze else y
 
+    def matmul(self, W: Tensor, x: np.ndarray) -> np.ndarray:
+        """Prefill matmul (cn_matmul): y[t] = W x[t] for every row t of x."""
+        x2 = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, W.cols)
+        y = np.empty((x2.shape[0], W.rows), dtype=np.float32)
+        check(N.lib().cn_matmul(self.handle, W.handle, _fptr(x2), _fptr(y), x2.shape[0]), "cn_matmul")
+        return y
+
     def close(self) -> None:
         if self.handle:
             for t in list(self._tensors):

@@ -78,6 +78,8 @@ SIGNATURES: dict[str, tuple] = {
     "cn_matvec": (_i, [_vp, _vp, _fp, _fp, _i]),
     "cn_dequantize_dev": (_i, [_i, _vp, _vp, _i64, _vp]),
     "cn_matvec_dev": (_i, [_vp, _i, _vp, _i, _i, _vp, _vp, _i]),
+    "cn_matmul": (_i, [_vp, _vp, _fp, _fp, _i]),
+    "cn_matmul_dev": (_i, [_vp, _i, _vp, _i, _i, _vp, _vp, _i]),
     "cn_matvec_noalloc_dev": (_i, [_i, _vp, _i, _i, _vp, _vp, _i, _vp]),
     "cn_llama_create": (_i, [_vp, _vp, C.POINTER(_vp), _i, C.POINTER(_vp)]),
     "cn_llama_destroy": (_i, [_vp]),

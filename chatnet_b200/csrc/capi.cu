@@ -154,6 +154,7 @@ int cn_destroy(cn_ctx* ctx) {
     cudaFree(ctx->counters);
     cudaFree(ctx->xinv);
     cudaFree(ctx->dstage);
+    cudaFree(ctx->xhalf);
     cudaFreeHost(ctx->hstage);
     cudaFree(ctx->dev_err);
     cudaStreamDestroy(ctx->stream);
@@ -396,7 +397,49 @@ int cn_matvec(cn_ctx* ctx, const cn_tensor* W, const float* host_x, float* host_
     return check_dev_err(ctx);
 }
 
+static int matmul_dev(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols,
+                      const float* d_x, float* d_y, int n_tokens) {
+    CN_CHECK(type == CN_TYPE_Q4_0, CN_ERR_UNSUPPORTED, "matmul: type %d not supported (Q4_0)", type);
+    CN_CHECK(n_tokens >= 1 && rows >= 1 && cols >= 256 && cols % 256 == 0, CN_ERR_INVALID_ARG,
+             "matmul: bad shape (%lld x %lld, %d tokens)", (long long)rows, (long long)cols, n_tokens);
+    const size_t hb = (size_t)n_tokens * cols * sizeof(__half);
+    int rc = ensure(&ctx->xhalf, &ctx->xhalf_bytes, hb, false);
+    if (rc) return rc;
+    __half* xh = static_cast<__half*>(ctx->xhalf);
+    rc = to_half(ctx->stream, d_x, xh, (int64_t)n_tokens * cols);
+    if (rc) return rc;
+    const int64_t ldy = rows;
+    return matmul_q4_0(ctx->stream, ctx->dev_err, 1, &d_w, &rows, cols, xh, n_tokens, &d_y, &ldy,
+                       false);
+}
+
+int cn_matmul(cn_ctx* ctx, const cn_tensor* W, const float* host_x, float* host_y, int n_tokens) {
+    CN_CHECK(ctx && W && host_x && host_y, CN_ERR_INVALID_ARG, "null argument");
+    CN_CHECK(n_tokens >= 1, CN_ERR_INVALID_ARG, "n_tokens %d < 1", n_tokens);
+    DeviceGuard dg(ctx->device);
+    size_t xb = (size_t)n_tokens * W->cols * sizeof(float);
+    size_t yb = (size_t)n_tokens * W->rows * sizeof(float);
+    size_t yoff = (xb + 255) & ~size_t(255);
+    int rc = stage(ctx, yoff + yb);
+    if (rc) return rc;
+    float* dx = reinterpret_cast<float*>(ctx->dstage);
+    float* dy = reinterpret_cast<float*>(static_cast<uint8_t*>(ctx->dstage) + yoff);
+    CN_CUDA(cudaMemcpyAsync(dx, host_x, xb, cudaMemcpyHostToDevice, ctx->stream));
+    rc = matmul_dev(ctx, W->type, W->d, W->rows, W->cols, dx, dy, n_tokens);
+    if (rc) return rc;
+    CN_CUDA(cudaMemcpyAsync(host_y, dy, yb, cudaMemcpyDeviceToHost, ctx->stream));
+    CN_CUDA(cudaStreamSynchronize(ctx->stream));
+    return check_dev_err(ctx);
+}
+
 // ---- device level --------------------------------------------------------------
+
+int cn_matmul_dev(cn_ctx* ctx, int type, const void* d_w, int out_dim, int in_dim,
+                  const float* d_x, float* d_y, int n_tokens) {
+    CN_CHECK(ctx && d_w && d_x && d_y, CN_ERR_INVALID_ARG, "null argument");
+    DeviceGuard dg(ctx->device);
+    return matmul_dev(ctx, type, d_w, out_dim, in_dim, d_x, d_y, n_tokens);
+}
 
 int cn_dequantize_dev(int type, const void* d_blocks, float* d_out, int64_t n_elements,
                       void* stream) {

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -25,6 +26,10 @@ struct cn_ctx {
     size_t counter_count = 0;
     float* xinv = nullptr;
     size_t xinv_bytes = 0;
+
+    // fp16 copy of the prefill matmul's activations
+    void* xhalf = nullptr;
+    size_t xhalf_bytes = 0;
 
     // staging for the host-pointer entry points
     void* dstage = nullptr;
@@ -72,6 +77,20 @@ int ensure(void** p, size_t* have, size_t need, bool zero);
 // (row_bytes not a multiple of 16, or unaligned base).
 int encode_weight_map(int type, const void* d_w, int64_t rows, uint64_t row_bytes,
                       CUtensorMap* out);
+
+// Encodes a 2-D tiled TMA descriptor (zero fill out of bounds, no interleave).
+int encode_tiled_2d(CUtensorMapDataType dt, void* base, const cuuint64_t (&dims)[2],
+                    const cuuint64_t (&strides)[1], const cuuint32_t (&box)[2],
+                    CUtensorMapSwizzle swz, CUtensorMap* out);
+
+// Prefill dequant-matmul (matmul.cu): y[i][t][r] (+)= dot(W_i[r], x[t]) for
+// M tokens and nmat <= 3 Q4_0 matrices with the same K (K % 256 == 0); x is
+// fp16 [M][K] (16-byte aligned), y[i] fp32 [M][ldy[i]].
+int matmul_q4_0(cudaStream_t st, uint32_t* err, int nmat, const void* const* w, const int64_t* rows,
+                int64_t K, const __half* x, int M, float* const* y, const int64_t* ldy,
+                bool accumulate);
+// fp32 -> fp16, n % 4 == 0, both 16-byte aligned.
+int to_half(cudaStream_t st, const float* x, __half* y, int64_t n);
 
 // Scratch requirements of one GEMV call.
 struct GemvPlan {

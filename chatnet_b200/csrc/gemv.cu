@@ -816,6 +816,18 @@ static int box_bytes(int type) {
     }
 }
 
+int encode_tiled_2d(CUtensorMapDataType dt, void* base, const cuuint64_t (&dims)[2],
+                    const cuuint64_t (&strides)[1], const cuuint32_t (&box)[2],
+                    CUtensorMapSwizzle swz, CUtensorMap* out) {
+    EncodeTiledFn enc = get_encode();
+    if (!enc) return set_error(CN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(out, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(CN_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return CN_OK;
+}
+
 int encode_weight_map(int type, const void* d_w, int64_t rows, uint64_t rb, CUtensorMap* out) {
     int bx = box_bytes(type);
     if (bx == 0) return set_error(CN_ERR_UNSUPPORTED, "no tiled GEMV for type %d", type);

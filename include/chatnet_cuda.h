@@ -146,6 +146,14 @@ int cn_dequantize(cn_ctx* ctx, const cn_tensor* W, int64_t row0, int64_t nrows, 
  * MatVecMulGeneric(Q4_K) (Tensors/TensorMath.cs:548-656). */
 int cn_matvec(cn_ctx* ctx, const cn_tensor* W, const float* host_x, float* host_y, int batch);
 
+/* Prefill matmul: y[t][r] = dot(W[r], x[t]) for n_tokens tokens at once (x
+ * [n_tokens][cols] fp32, y [n_tokens][rows] fp32), the batched form of the
+ * matvec that ChatNet runs once per prompt token (InferenceEngine.cs:235-239
+ * -> TensorMath.MatVecMulQ4_0, Tensors/TensorMath.cs:548-578).  Runs on the
+ * tcgen05 tensor cores: activations rounded to fp16, weights expanded to
+ * fp16, fp32 accumulation.  Q4_0 weights with cols % 256 == 0. */
+int cn_matmul(cn_ctx* ctx, const cn_tensor* W, const float* host_x, float* host_y, int n_tokens);
+
 /* ---- device level: device pointers, asynchronous ------------------------ */
 
 /* Bit-exact dequantization of n_elements values (same semantics as the
@@ -158,6 +166,11 @@ int cn_dequantize_dev(int type, const void* d_blocks, float* d_out, int64_t n_el
  * stream: y[b][r] = dot(W[r], x[b]).  Same math as cn_matvec. */
 int cn_matvec_dev(cn_ctx* ctx, int type, const void* d_w, int out_dim, int in_dim,
                   const float* d_x, float* d_y, int batch);
+
+/* Prefill matmul of cn_matmul on device pointers, using ctx's scratch and
+ * stream (enqueued; no synchronisation). */
+int cn_matmul_dev(cn_ctx* ctx, int type, const void* d_w, int out_dim, int in_dim,
+                  const float* d_x, float* d_y, int n_tokens);
 
 /* The fused dequant-GEMV of cn_matvec_dev for callers that cannot allocate
  * device memory (hosts that own every buffer, or forbid cudaMalloc/cudaFree
