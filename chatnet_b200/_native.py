@@ -84,6 +84,8 @@ SIGNATURES: dict[str, tuple] = {
     "cn_llama_create": (_i, [_vp, _vp, C.POINTER(_vp), _i, C.POINTER(_vp)]),
     "cn_llama_destroy": (_i, [_vp]),
     "cn_llama_forward": (_i, [_vp, C.POINTER(_i), _i, _i, _fp]),
+    "cn_llama_prefill_hidden_dev": (_i, [_vp, _vp, _i, _i, _vp]),
+    "cn_llama_prefill_kernels": (_i, [_vp, C.POINTER(_i)]),
     "cn_llama_decode": (_i, [_vp, C.POINTER(_i), C.POINTER(_i), _i, _fp, C.POINTER(_i)]),
     "cn_llama_kv_write": (_i, [_vp, _i, _i, _i, _i, _vp, _vp]),
     "cn_llama_kv_read": (_i, [_vp, _i, _i, _i, _i, _vp, _vp]),

@@ -8,6 +8,10 @@ with fewer layers is a prefix of the full one.
             a separate output included), fp32 KV cache with positions 0..510
             filled with N(0,1) and 511 left zero (the reference's cache starts
             zeroed, LlamaModel.cs:60-61), decoding position 512.
+  config 3: prefill of 512 tokens through one Llama-2-7B-shaped layer, Q4_0
+            weights, 32/32 heads of 128; the layer input is seeded N(0,1)
+            activations [512][4096] (prefill_x), positions 0..511, fp32 KV
+            cache starting empty.
   config 4: Llama-2-70B-shaped decode, Q4_K weights, fp16 KV cache with
             positions 0..2046 filled, decoding position 2047 (context 2048).
 Norm weights are fp32 1 + N(0, 0.01); N(0,1) is the exact Irwin-Hall(12)
@@ -32,6 +36,7 @@ class DecodeConfig:
     kv_filled: int      # positions 0..kv_filled-1 hold N(0,1)
     decode_pos: int
     name: str
+    prefill: int = 0    # prompt tokens of a prefill config (0: decode config)
 
 
 TINYLLAMA = LlamaConfig(dim=2048, hidden_dim=5632, n_layers=22, n_heads=32, n_kv_heads=4,
@@ -41,9 +46,15 @@ LLAMA2_70B = LlamaConfig(dim=8192, hidden_dim=28672, n_layers=80, n_heads=64, n_
                          head_dim=128, vocab=32000, ctx_len=2048, rope_base=10000.0, rms_eps=1e-5,
                          kv_f16=True)
 
+LLAMA2_7B_LAYER = LlamaConfig(dim=4096, hidden_dim=11008, n_layers=1, n_heads=32, n_kv_heads=32,
+                              head_dim=128, vocab=32000, ctx_len=512, rope_base=10000.0, rms_eps=1e-5,
+                              kv_f16=False)
+
 CONFIGS = {
     1: DecodeConfig(1, TINYLLAMA, TYPE_Q4_0, kv_filled=511, decode_pos=512,
                     name="tinyllama-1.1b-q4_0-decode@512"),
+    3: DecodeConfig(3, LLAMA2_7B_LAYER, TYPE_Q4_0, kv_filled=0, decode_pos=0,
+                    name="llama2-7b-layer-q4_0-prefill@512", prefill=512),
     4: DecodeConfig(4, LLAMA2_70B, TYPE_Q4_K, kv_filled=2047, decode_pos=2047,
                     name="llama2-70b-q4_k-decode@2047"),
 }
@@ -124,3 +135,9 @@ def host_kv(dc: DecodeConfig, seq: int) -> tuple[np.ndarray, np.ndarray]:
         a[:, dc.kv_filled:, :] = 0
         out.append(a.reshape(m.n_layers * m.ctx_len, m.kv_dim))
     return out[0], out[1]
+
+
+def prefill_x(dc: DecodeConfig, n: int | None = None) -> np.ndarray:
+    """Seeded N(0,1) layer input [n][dim] of a prefill config."""
+    n = dc.prefill if n is None else n
+    return synth_fill(TYPE_F32, n, dc.model.dim, synth_seed(dc.config_id, f"prefill.x.{n}"), DIST_NORMAL)

@@ -28,6 +28,7 @@ namespace cn {
 enum { T_EMB = 0, T_OUT = 1, T_ONORM = 2 };
 enum { L_ANORM = 0, L_Q, L_K, L_V, L_O, L_FNORM, L_GATE, L_UP, L_DOWN };
 constexpr int kMaxBatch = 32;
+constexpr int kPrefillMin = 16;  // prompts of at least this many tokens take the prefill matmul
 
 struct Step {
     bool built = false;
@@ -64,6 +65,14 @@ struct cn_llama {
     size_t counter_bytes = 0;
     cn::Step steps[cn::kMaxBatch + 1];
     bool use_graph = true;
+    // prompt processing (prefill) scratch for up to pf_cap tokens, allocated
+    // on first use: residual stream, q/k/v, gate/up (fp32), the fp16
+    // operand of the next matmul, token ids and positions
+    int pf_cap = 0;
+    float *pf_x = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_g = nullptr,
+          *pf_u = nullptr;
+    __half* pf_h = nullptr;
+    int *pf_tok = nullptr, *pf_pos = nullptr;
 };
 
 namespace cn {
@@ -379,13 +388,129 @@ static void free_model(cn_llama* m) {
     if (!m->logits_owned) m->logits = nullptr;
     void* bufs[] = {m->kc, m->vc, m->rope, m->x, m->x2, m->attn_ctr, m->xn, m->q, m->k, m->v, m->att, m->tmp,
                     m->gate, m->up, m->logits, m->part, m->tokens, m->pos, m->amax,
-                    m->gb.xfrag, m->gb.xsum, m->gb.partials, m->gb.counters, m->gb.xinv};
+                    m->gb.xfrag, m->gb.xsum, m->gb.partials, m->gb.counters, m->gb.xinv,
+                    m->pf_x, m->pf_q, m->pf_k, m->pf_v, m->pf_g, m->pf_u, m->pf_h, m->pf_tok, m->pf_pos};
     for (void* p : bufs) cudaFree(p);
     cudaFreeHost(m->h_tokens);
     cudaFreeHost(m->h_pos);
     cudaFreeHost(m->h_amax);
     delete m;
 }
+
+// ---- prefill: n tokens through the decoder at once (tcgen05 matmul) ----------
+
+// Whether the model's projections can run on the prefill matmul (Q4_0 with
+// inner dimensions that are multiples of 256, one GPU).
+static bool prefill_supported(const cn_llama* m) {
+    if (m->tp && m->tp->size > 1) return false;
+    const cn_llama_config& c = m->cfg;
+    if (c.dim % 256 != 0 || c.hidden_dim % 256 != 0 || (c.head_dim != 64 && c.head_dim != 128))
+        return false;
+    for (int l = 0; l < c.n_layers; l++)
+        for (int j : {L_Q, L_K, L_V, L_O, L_GATE, L_UP, L_DOWN})
+            if (LT(m, l, j)->type != CN_TYPE_Q4_0) return false;
+    return true;
+}
+
+static int prefill_reserve(cn_llama* m, int n) {
+    if (n <= m->pf_cap) return CN_OK;
+    CN_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    void* old[] = {m->pf_x, m->pf_q, m->pf_k, m->pf_v, m->pf_g, m->pf_u, m->pf_h, m->pf_tok, m->pf_pos};
+    for (void* p : old) cudaFree(p);
+    m->pf_x = m->pf_q = m->pf_k = m->pf_v = m->pf_g = m->pf_u = nullptr;
+    m->pf_h = nullptr;
+    m->pf_tok = m->pf_pos = nullptr;
+    m->pf_cap = 0;
+    const cn_llama_config& c = m->cfg;
+    const size_t N = (size_t)n;
+    const size_t hmax = (size_t)(c.hidden_dim > c.dim ? c.hidden_dim : c.dim);
+    int rc;
+    if ((rc = dmalloc((void**)&m->pf_x, N * c.dim * 4, false)) ||
+        (rc = dmalloc((void**)&m->pf_q, N * m->qdim * 4, false)) ||
+        (rc = dmalloc((void**)&m->pf_k, N * m->kvdim * 4, false)) ||
+        (rc = dmalloc((void**)&m->pf_v, N * m->kvdim * 4, false)) ||
+        (rc = dmalloc((void**)&m->pf_g, N * c.hidden_dim * 4, false)) ||
+        (rc = dmalloc((void**)&m->pf_u, N * c.hidden_dim * 4, false)) ||
+        (rc = dmalloc((void**)&m->pf_h, N * hmax * 2, false)) ||
+        (rc = dmalloc((void**)&m->pf_tok, N * 4, false)) || (rc = dmalloc((void**)&m->pf_pos, N * 4, false)))
+        return rc;
+    m->pf_cap = n;
+    return CN_OK;
+}
+
+// Runs the hidden states m->pf_x [n][dim] (positions pos..pos+n-1 of
+// sequence slot 0) through every layer, in place; the layers' K/V rows land
+// in the cache.  Per layer: RmsNorm -> q/k/v matmul (one launch) -> RoPE and
+// cache store -> causal attention -> O matmul added into the residual ->
+// RmsNorm -> gate/up matmul (one launch) -> SiLU * up -> down matmul added
+// into the residual (LlamaModel.Forward, Models/Llama/LlamaModel.cs:93-238,
+// for n tokens at once).
+static int prefill_layers(cn_llama* m, int n, int pos) {
+    const cn_llama_config& c = m->cfg;
+    cudaStream_t s = m->ctx->stream;
+    uint32_t* err = m->ctx->dev_err;
+    const int qd = m->qdim, kvd = m->kvdim, hid = c.hidden_dim;
+    int rc;
+    if ((rc = prefill_positions(s, m->pf_pos, n, pos))) return rc;
+    for (int l = 0; l < c.n_layers; l++) {
+        const int64_t cache_off = (int64_t)l * c.ctx_len * kvd;  // sequence slot 0
+        if ((rc = prefill_norm(s, m->pf_x, (const float*)LT(m, l, L_ANORM)->d, m->pf_h, c.dim, n, c.rms_eps)))
+            return rc;
+        {
+            const void* w[3] = {LT(m, l, L_Q)->d, LT(m, l, L_K)->d, LT(m, l, L_V)->d};
+            const int64_t rows[3] = {qd, kvd, kvd};
+            float* y[3] = {m->pf_q, m->pf_k, m->pf_v};
+            if ((rc = matmul_q4_0(s, err, 3, w, rows, c.dim, m->pf_h, n, y, rows, false))) return rc;
+        }
+        RopeKvArgs ra;
+        ra.q = m->pf_q;
+        ra.k = m->pf_k;
+        ra.v = m->pf_v;
+        ra.rope = m->rope;
+        ra.pos_dev = m->pf_pos;
+        ra.pos_host = 0;
+        ra.batch = n;
+        ra.n_heads = m->nh;
+        ra.n_kv = m->nkv;
+        ra.hd = c.head_dim;
+        ra.q_stride = qd;
+        ra.kv_stride = kvd;
+        ra.kcache = m->kc;
+        ra.vcache = m->vc;
+        ra.cache_seq_stride = 0;  // every token belongs to sequence slot 0
+        ra.cache_layer_off = cache_off;
+        ra.kv_f16 = c.kv_dtype == CN_KV_F16;
+        ra.ctx_len = c.ctx_len;
+        ra.err = err;
+        if ((rc = launch_rope_kv(ra, s))) return rc;
+        if ((rc = prefill_attention(s, m->pf_q, qd, m->kc, m->vc, c.kv_dtype == CN_KV_F16, cache_off, m->nh,
+                                    m->nkv, c.head_dim, n, pos, m->pf_h, qd)))
+            return rc;
+        {
+            const void* w = LT(m, l, L_O)->d;
+            const int64_t rows = c.dim;
+            if ((rc = matmul_q4_0(s, err, 1, &w, &rows, qd, m->pf_h, n, &m->pf_x, &rows, true))) return rc;
+        }
+        if ((rc = prefill_norm(s, m->pf_x, (const float*)LT(m, l, L_FNORM)->d, m->pf_h, c.dim, n, c.rms_eps)))
+            return rc;
+        {
+            const void* w[2] = {LT(m, l, L_GATE)->d, LT(m, l, L_UP)->d};
+            const int64_t rows[2] = {hid, hid};
+            float* y[2] = {m->pf_g, m->pf_u};
+            if ((rc = matmul_q4_0(s, err, 2, w, rows, c.dim, m->pf_h, n, y, rows, false))) return rc;
+        }
+        if ((rc = prefill_silu(s, m->pf_g, m->pf_u, m->pf_h, (int64_t)n * hid))) return rc;
+        {
+            const void* w = LT(m, l, L_DOWN)->d;
+            const int64_t rows = c.dim;
+            if ((rc = matmul_q4_0(s, err, 1, &w, &rows, hid, m->pf_h, n, &m->pf_x, &rows, true))) return rc;
+        }
+    }
+    return CN_OK;
+}
+
+// Kernels one prefill_layers call launches (positions, then 10 per layer).
+static int prefill_kernels(const cn_llama* m) { return 1 + 10 * m->cfg.n_layers; }
 
 }  // namespace cn
 
@@ -588,6 +713,29 @@ int cn_llama_prepare(cn_llama* m, int batch) {
     return prepare_step(m, batch);
 }
 
+int cn_llama_prefill_hidden_dev(cn_llama* m, const float* x_dev, int n, int pos, float* out_dev) {
+    CN_CHECK(m && x_dev && out_dev, CN_ERR_INVALID_ARG, "null argument");
+    CN_CHECK(n >= 1 && pos >= 0 && pos + n <= m->cfg.ctx_len, CN_ERR_INVALID_ARG,
+             "positions [%d, %d) outside the context of %d", pos, pos + n, m->cfg.ctx_len);
+    CN_CHECK(prefill_supported(m), CN_ERR_UNSUPPORTED,
+             "prefill needs Q4_0 projections, dim and hidden_dim multiples of 256, head_dim 64 or 128, one GPU");
+    cudaSetDevice(m->ctx->device);
+    cudaStream_t s = m->ctx->stream;
+    int rc = prefill_reserve(m, n);
+    if (rc) return rc;
+    const size_t bytes = (size_t)n * m->cfg.dim * 4;
+    CN_CUDA(cudaMemcpyAsync(m->pf_x, x_dev, bytes, cudaMemcpyDeviceToDevice, s));
+    if ((rc = prefill_layers(m, n, pos))) return rc;
+    CN_CUDA(cudaMemcpyAsync(out_dev, m->pf_x, bytes, cudaMemcpyDeviceToDevice, s));
+    return CN_OK;
+}
+
+int cn_llama_prefill_kernels(cn_llama* m, int* n_kernels) {
+    CN_CHECK(m && n_kernels, CN_ERR_INVALID_ARG, "null argument");
+    *n_kernels = prefill_kernels(m);
+    return CN_OK;
+}
+
 int cn_llama_destroy(cn_llama* m) {
     if (!m) return CN_OK;
     cudaSetDevice(m->ctx->device);
@@ -725,6 +873,34 @@ int cn_llama_forward(cn_llama* m, const int* tokens, int n, int pos, float* logi
     CN_CHECK(n >= 1, CN_ERR_INVALID_ARG, "no tokens");
     CN_CHECK(pos >= 0 && pos + n <= m->cfg.ctx_len, CN_ERR_INVALID_ARG,
              "positions [%d, %d) outside the context of %d", pos, pos + n, m->cfg.ctx_len);
+    if (n >= kPrefillMin && prefill_supported(m)) {
+        // the prompt in one pass: embed n tokens, all layers on the matmul,
+        // then the head of the last token through the decode GEMV
+        for (int t = 0; t < n; t++)
+            CN_CHECK(tokens[t] >= 0 && tokens[t] < m->cfg.vocab, CN_ERR_INVALID_ARG,
+                     "token id %d outside [0, %d)", tokens[t], m->cfg.vocab);
+        cudaSetDevice(m->ctx->device);
+        cudaStream_t s = m->ctx->stream;
+        const cn_llama_config& c = m->cfg;
+        int rc = prefill_reserve(m, n);
+        if (rc) return rc;
+        CN_CUDA(cudaMemcpyAsync(m->pf_tok, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s));
+        const cn_tensor* emb = m->t[T_EMB];
+        if ((rc = launch_embed(emb->type, emb->d, emb->row_bytes, m->pf_tok, c.vocab, c.dim, n, m->pf_x,
+                               m->ctx->dev_err, s)))
+            return rc;
+        if ((rc = prefill_layers(m, n, pos))) return rc;
+        if ((rc = launch_rmsnorm(m->pf_x + (size_t)(n - 1) * c.dim, (const float*)m->t[T_ONORM]->d, m->xn,
+                                 c.dim, 1, c.rms_eps, s)))
+            return rc;
+        const cn_tensor* w = m->t[T_OUT];
+        if ((rc = gemv_launch(m->ctx, w->type, w->d, w->rows, w->cols, w->has_map ? &w->map : nullptr, m->xn,
+                              m->logits, 1)))
+            return rc;
+        CN_CUDA(cudaMemcpyAsync(logits_host, m->logits, (size_t)c.vocab * 4, cudaMemcpyDeviceToHost, s));
+        CN_CUDA(cudaStreamSynchronize(s));
+        return check_dev_err_reset(m);
+    }
     for (int t = 0; t < n; t++) {
         int p = pos + t;
         int rc = cn_llama_decode(m, tokens + t, &p, 1, t == n - 1 ? logits_host : nullptr, nullptr);

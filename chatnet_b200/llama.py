@@ -122,6 +122,16 @@ class CudaLlamaModel:
               "cn_llama_forward")
         return logits
 
+    def prefill_hidden_dev(self, x_ptr: int, n: int, pos: int, out_ptr: int) -> None:
+        """All layers on n hidden states at once (device pointers, enqueued)."""
+        check(N.lib().cn_llama_prefill_hidden_dev(self.handle, C.c_void_p(x_ptr), n, pos, C.c_void_p(out_ptr)),
+              "cn_llama_prefill_hidden_dev")
+
+    def prefill_kernels(self) -> int:
+        n = C.c_int(0)
+        check(N.lib().cn_llama_prefill_kernels(self.handle, C.byref(n)), "cn_llama_prefill_kernels")
+        return n.value
+
     def decode(self, tokens, positions, logits: bool = True, argmax: bool = True):
         """One batched decode step: sequence b (KV slot b) at positions[b]."""
         tok = np.ascontiguousarray(tokens, dtype=np.int32)

@@ -223,9 +223,25 @@ int cn_llama_create(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* const* t
 int cn_llama_destroy(cn_llama* m);
 
 /* IModel.Forward (Abstractions/IModel.cs:18, LlamaModel.cs:93-238): runs the
- * n tokens of KV slot 0 at positions pos..pos+n-1, one at a time, and writes
- * the logits of the last one to logits_host [vocab]. */
+ * n tokens of KV slot 0 at positions pos..pos+n-1 and writes the logits of
+ * the last one to logits_host [vocab].  Prompts of 16 or more tokens on a
+ * one-GPU model with Q4_0 projections run as one prefill pass (every layer
+ * on the tcgen05 matmul for all n tokens, see cn_llama_prefill_hidden_dev);
+ * otherwise the tokens run one decode step at a time, as the reference does
+ * (InferenceEngine.cs:235-239). */
 int cn_llama_forward(cn_llama* m, const int* tokens, int n, int pos, float* logits_host);
+
+/* Prefill on device buffers: runs the hidden states x_dev [n][dim] (fp32)
+ * through every layer at once, for positions pos..pos+n-1 of KV slot 0 (whose
+ * cache rows are written), and writes the layer stack's output to out_dev
+ * [n][dim] (may equal x_dev).  Enqueued on the context stream, not waited
+ * for.  Needs Q4_0 projections, dim and hidden_dim multiples of 256, head_dim
+ * 64 or 128, and one GPU (CN_ERR_UNSUPPORTED otherwise).
+ * (no counterpart in the reference: the per-layer part of LlamaModel.Forward,
+ * Models/Llama/LlamaModel.cs:93-238, for n tokens at once) */
+int cn_llama_prefill_hidden_dev(cn_llama* m, const float* x_dev, int n, int pos, float* out_dev);
+/* Kernel launches of one cn_llama_prefill_hidden_dev call. */
+int cn_llama_prefill_kernels(cn_llama* m, int* n_kernels);
 
 /* One decode step for `batch` sequences: sequence b (KV slot b) reads token
  * tokens[b] at position pos[b].  logits_host [batch][vocab] and argmax_host

@@ -122,3 +122,11 @@ class OracleLlama:
                                          fp(logits), nthreads)
         assert rc == 0, rc
         return logits
+
+    def layers(self, x: np.ndarray, pos: int, nthreads: int = 0) -> np.ndarray:
+        """All layers on one hidden state x [dim] at position pos (or_llama_layers)."""
+        h = np.array(x, dtype=np.float32, copy=True)
+        rc = self.o.lib.or_llama_layers(C.byref(self.cfg), self.ptrs, self.types, self.k.ctypes.data,
+                                        self.v.ctypes.data, fp(h), pos, 0, self.cfg.n_layers, nthreads)
+        assert rc == 0, rc
+        return h
