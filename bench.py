@@ -3,6 +3,7 @@
 config 4) on B200, through libchatnet_cuda.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--config 4|1]
+    python bench.py --config 3 ...           # prefill: 512 tokens through one 7B layer
     python bench.py --impl reference ...     # the reference's CPU algorithm (oracle port)
 
 A step is one decode step of `batch` sequences (each at position 2047 of a
@@ -21,8 +22,15 @@ Printed JSON line (rank 0):
              stream: algorithmic bytes per launch / mean launch time
   cpu_baseline  the oracle port of the reference's C# CPU path timed on the
              host's cores on a 2-layer sample, extrapolated to 80 layers
-With --gpus N > 1 every rank decodes its own replica (data-parallel
-replicas; tensor parallelism is not built), so `scaling` is weak.
+With --gpus N > 1 the ranks run the model tensor-parallel (default; the
+same sequences, strong scaling) or as independent replicas (--parallel
+replicas, weak scaling).
+
+--config 3 (prefill): a step is one pass of 512 tokens' hidden states through
+one Llama-2-7B-shaped Q4_0 layer (cn_llama_prefill_hidden_dev); `value` is
+tokens/s, `e2e` adds the copy of the 8 MiB input from pinned host memory and
+of the output back, and the roofline is the gate/up matmul's TFLOP/s against
+the measured dense bf16 peak.  With N > 1 the ranks run replicas.
 """
 from __future__ import annotations
 
@@ -51,7 +59,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=1)
-    ap.add_argument("--config", type=int, default=4, choices=(1, 4))
+    ap.add_argument("--config", type=int, default=4, choices=(1, 3, 4))
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--parallel", default="tp", choices=("tp", "replicas"),
                     help="N > 1: tensor parallelism over the N GPUs (default), or N independent replicas")
@@ -118,6 +126,16 @@ class ClockSampler:
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peak_tflops() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured burst"
+        except (KeyError, ValueError):
+            pass
+    return 1590.0, "fallback"
 
 
 def measured_peak_gbs() -> tuple[float, str]:
@@ -244,6 +262,194 @@ def gemv_mode(a) -> int:
 
 
 # ---------------------------------------------------------------------------
+# config 3: prefill
+# ---------------------------------------------------------------------------
+PREFILL_FLOPS = 209.38e9  # projections 207.23 GFLOP + causal attention 2.15 GFLOP
+
+
+class CpuPrefillSample:
+    """The oracle port of the reference's CPU path for config 3: the first
+    `n` prompt tokens through the layer one at a time (as ChatNet's prompt
+    loop runs them), timed together."""
+
+    def __init__(self, dc, n: int):
+        from chatnet_b200 import configs as cf
+        from chatnet_b200.llama import tensor_names
+        from tests import _oracle
+        self.n = n
+        orc = _oracle.load()
+        host = cf.host_tensors(dc)
+        names = tensor_names(dc.model.n_layers)
+        types = [cf.tensor_type(dc, nm) for nm in names]
+        m = dc.model
+        k = np.zeros((m.n_layers * m.ctx_len, m.kv_dim), np.float32)
+        self.ol = _oracle.OracleLlama(orc, m, host, types, names, k, k.copy())
+        self.x = cf.prefill_x(dc)
+
+    def run_once(self) -> float:
+        """Seconds per token."""
+        t0 = time.perf_counter()
+        for t in range(self.n):
+            self.ol.layers(self.x[t], t)
+        return (time.perf_counter() - t0) / self.n
+
+    def describe(self, reps: int) -> str:
+        return (f"prompt tokens 0..{self.n - 1} of 512 through the layer one at a time (attention "
+                f"over <= {self.n} positions, so slightly cheaper per token than the full prompt), "
+                f"median of {reps} runs, per-token time")
+
+
+def prefill_main(a, world: int, rank: int, local: int, dc) -> int:
+    n = dc.prefill
+    m = dc.model
+    workload = {"workload": dc.name, "config_id": 3, "tokens": n, "n_layers": m.n_layers, "dim": m.dim,
+                "ffn": m.hidden_dim, "heads": f"{m.n_heads}/{m.n_kv_heads}", "head_dim": m.head_dim,
+                "positions": f"0..{n - 1}", "weights": "Q4_0", "kv_cache": "fp32",
+                "parallelism": "single GPU" if world == 1 else f"replicas x{world}",
+                "l2": "weights 113.8 MB and activations re-read each step; L2 not flushed (a layer's "
+                      "working set is about 200 MB, above the 126 MB L2)",
+                "flops_per_step": PREFILL_FLOPS}
+    if a.impl == "reference":
+        if rank != 0:
+            return 0
+        cs = CpuPrefillSample(dc, 16)
+        times = []
+        for i in range(a.warmup + a.steps):
+            t = cs.run_once()
+            if i >= a.warmup:
+                times.append(t)
+        val = 1.0 / statistics.median(times)
+        line = {"metric": "prefill tok/s", "value": val, "unit": "tok/s", "n_gpus": 0, "steps": a.steps,
+                "warmup": a.warmup, "ms_per_step": n * 1e3 / val, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "impl": "reference", "config": workload,
+                "cpu_baseline": {"value": val, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                                 "sample": cs.describe(a.steps)},
+                "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    import torch
+    import chatnet_b200 as cn
+    from chatnet_b200 import configs as cf
+    from chatnet_b200.llama import CudaLlamaModel
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    ctx = cn.Context(local)
+    ext = torch.cuda.ExternalStream(ctx.stream)
+    tensors = cf.device_tensors(ctx, dc)
+    model = CudaLlamaModel(ctx, m, tensors)
+    xh = torch.from_numpy(cf.prefill_x(dc)).pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    xd = xh.to(f"cuda:{local}")
+    od = torch.empty_like(xd)
+    torch.cuda.synchronize()
+
+    def step():
+        model.prefill_hidden_dev(xd.data_ptr(), n, 0, od.data_ptr())
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ctx.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(max(a.warmup, 3)):
+        step()
+    ctx.synchronize()
+    if a.nvtx_step:
+        torch.cuda.nvtx.range_push("timed_step")
+        step()
+        ctx.synchronize()
+        torch.cuda.nvtx.range_pop()
+        print(json.dumps({"nvtx_step": True, "kernels": model.prefill_kernels()}), flush=True)
+        return 0
+
+    barrier()
+    clk = ClockSampler(local)
+    clk.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ext)
+    for _ in range(a.steps):
+        step()
+    e1.record(ext)
+    e1.synchronize()
+    clocks = clk.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
+    value = world * n * 1000.0 / ms
+
+    # end to end: host activations in, host output back, every step
+    barrier()
+    e0.record(ext)
+    for _ in range(a.steps):
+        with torch.cuda.stream(ext):
+            xd.copy_(xh, non_blocking=True)
+        step()
+        with torch.cuda.stream(ext):
+            oh.copy_(od, non_blocking=True)
+    e1.record(ext)
+    e1.synchronize()
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1) / a.steps)
+    e2e = world * n * 1000.0 / ms_e2e
+    assert torch.isfinite(oh).all()
+
+    # roofline: the gate/up matmul (the largest launch) timed alone
+    us, flops = model.time_matmul(2, n, iters=20)
+    peak, peak_kind = measured_peak_tflops()
+    achieved = flops / (us * 1e-6) / 1e12
+    us_by_group = {g: model.time_matmul(i, n, iters=20)[0] for i, g in enumerate(("qkv", "o", "gate_up", "down"))}
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cs = CpuPrefillSample(dc, 16)
+        per_tok = statistics.median([cs.run_once() for _ in range(3)])
+        cpu = {"value": 1.0 / per_tok, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": cs.describe(3)}
+    if rank == 0:
+        line = {
+            "metric": "prefill tok/s", "value": value, "unit": "tok/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q4_0 weights -> fp16 x fp16 activations (tcgen05 kind::f16) -> f32",
+            "data": "synthetic (seeded generator, config shapes and distributions)", "config": workload,
+            "layer_tflops": PREFILL_FLOPS / (ms * 1e-3) / 1e12,
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": int(xh.numel() * 4),
+                    "d2h_bytes_per_step": int(oh.numel() * 4)},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "kernel": f"matmul_q4_0_kernel gate/up {2 * m.hidden_dim}x{m.dim} M{n}",
+                         "us_per_launch": us, "flops_per_launch": flops,
+                         "us_per_launch_by_group": us_by_group,
+                         "peak_source": f"MEASURED_PEAKS.json bf16_tflops ({peak_kind})"},
+            "cpu_baseline": cpu,
+            "gpu_launches": model.prefill_kernels() * a.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.synchronize()
+    del xd, od, xh, oh  # torch's buffers go before the library's context
+    torch.cuda.synchronize()
+    model.close()
+    for t in tensors:
+        t.free()
+    if dist is not None:
+        dist.destroy_process_group()
+    ctx.close()
+    return 0
+
+
+# ---------------------------------------------------------------------------
 def main():
     a = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -265,6 +471,8 @@ def main():
 
     if a.gemv:
         return gemv_mode(a)
+    if a.config == 3:
+        return prefill_main(a, world, rank, local, dc)
 
     if a.impl == "reference":
         if rank != 0:

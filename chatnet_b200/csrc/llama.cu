@@ -868,6 +868,61 @@ int cn_llama_time_gemv(cn_llama* m, int proj, int batch, int iters, float* us_pe
     return check_dev_err_reset(m);
 }
 
+int cn_llama_time_matmul(cn_llama* m, int group, int n, int iters, float* us_per_launch,
+                         double* flops_per_launch) {
+    CN_CHECK(m && us_per_launch && flops_per_launch, CN_ERR_INVALID_ARG, "null argument");
+    CN_CHECK(group >= 0 && group <= 3 && iters >= 1 && n >= 1, CN_ERR_INVALID_ARG, "bad group/n/iters");
+    CN_CHECK(prefill_supported(m), CN_ERR_UNSUPPORTED, "model cannot run the prefill matmul");
+    cudaSetDevice(m->ctx->device);
+    int rc = prefill_reserve(m, n);
+    if (rc) return rc;
+    const cn_llama_config& c = m->cfg;
+    const int64_t qd = m->qdim, kvd = m->kvdim, hid = c.hidden_dim, dim = c.dim;
+    cudaStream_t s = m->ctx->stream;
+    CN_CUDA(cudaMemsetAsync(m->pf_h, 0, (size_t)n * (hid > dim ? hid : dim) * 2, s));
+    CN_CUDA(cudaMemsetAsync(m->pf_x, 0, (size_t)n * dim * 4, s));
+    const int L = c.n_layers;
+    double flops = 0;
+    auto launch = [&](int i) -> int {
+        const int l = i % L;
+        if (group == 0) {
+            const void* w[3] = {LT(m, l, L_Q)->d, LT(m, l, L_K)->d, LT(m, l, L_V)->d};
+            const int64_t rows[3] = {qd, kvd, kvd};
+            float* y[3] = {m->pf_q, m->pf_k, m->pf_v};
+            flops = 2.0 * n * (double)(qd + 2 * kvd) * dim;
+            return matmul_q4_0(s, m->ctx->dev_err, 3, w, rows, dim, m->pf_h, n, y, rows, false);
+        }
+        if (group == 2) {
+            const void* w[2] = {LT(m, l, L_GATE)->d, LT(m, l, L_UP)->d};
+            const int64_t rows[2] = {hid, hid};
+            float* y[2] = {m->pf_g, m->pf_u};
+            flops = 2.0 * n * (double)(2 * hid) * dim;
+            return matmul_q4_0(s, m->ctx->dev_err, 2, w, rows, dim, m->pf_h, n, y, rows, false);
+        }
+        const void* w = LT(m, l, group == 1 ? L_O : L_DOWN)->d;
+        const int64_t rows = dim, K = group == 1 ? qd : hid;
+        flops = 2.0 * n * (double)dim * K;
+        return matmul_q4_0(s, m->ctx->dev_err, 1, &w, &rows, K, m->pf_h, n, &m->pf_x, &rows, true);
+    };
+    for (int i = 0; i < 3; i++)
+        if ((rc = launch(i))) return rc;
+    cudaEvent_t e0, e1;
+    CN_CUDA(cudaEventCreate(&e0));
+    CN_CUDA(cudaEventCreate(&e1));
+    CN_CUDA(cudaEventRecord(e0, s));
+    for (int i = 0; i < iters; i++)
+        if ((rc = launch(i + 3))) return rc;
+    CN_CUDA(cudaEventRecord(e1, s));
+    CN_CUDA(cudaEventSynchronize(e1));
+    float ms = 0.f;
+    CN_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    *us_per_launch = ms * 1000.f / iters;
+    *flops_per_launch = flops;
+    return check_dev_err_reset(m);
+}
+
 int cn_llama_forward(cn_llama* m, const int* tokens, int n, int pos, float* logits_host) {
     CN_CHECK(m && tokens && logits_host, CN_ERR_INVALID_ARG, "null argument");
     CN_CHECK(n >= 1, CN_ERR_INVALID_ARG, "no tokens");

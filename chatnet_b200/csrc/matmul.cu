@@ -315,14 +315,20 @@ __global__ void __launch_bounds__(mm::kThreads, 1)
             tmem_ld32(lane_base + 32 * j, v);
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
             if (live) {
+                float* p = y + (size_t)(tok0 + 32 * j) * ldy + row;
+                const int nt = a.M - (tok0 + 32 * j);  // tokens of this chunk inside M
+                if (a.accumulate) {
+                    // all 32 loads in flight before the first store
+                    float old[32];
 #pragma unroll
-                for (int t = 0; t < 32; t++) {
-                    const int tok = tok0 + 32 * j + t;
-                    if (tok < a.M) {
-                        float* p = y + (size_t)tok * ldy + row;
-                        const float val = __uint_as_float(v[t]);
-                        *p = a.accumulate ? *p + val : val;
-                    }
+                    for (int t = 0; t < 32; t++) old[t] = t < nt ? p[(size_t)t * ldy] : 0.f;
+#pragma unroll
+                    for (int t = 0; t < 32; t++)
+                        if (t < nt) p[(size_t)t * ldy] = old[t] + __uint_as_float(v[t]);
+                } else {
+#pragma unroll
+                    for (int t = 0; t < 32; t++)
+                        if (t < nt) p[(size_t)t * ldy] = __uint_as_float(v[t]);
                 }
             }
         }

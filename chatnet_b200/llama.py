@@ -167,6 +167,13 @@ class CudaLlamaModel:
               "cn_llama_time_gemv")
         return us.value, nb.value
 
+    def time_matmul(self, group: int, n: int, iters: int) -> tuple[float, float]:
+        """Mean us and FLOPs of one prefill matmul launch (0 qkv, 1 O, 2 gate/up, 3 down)."""
+        us, fl = C.c_float(0), C.c_double(0)
+        check(N.lib().cn_llama_time_matmul(self.handle, group, n, iters, C.byref(us), C.byref(fl)),
+              "cn_llama_time_matmul")
+        return us.value, fl.value
+
     def kv_synth(self, seq: int, npos: int, seed_k: int, seed_v: int) -> None:
         check(N.lib().cn_llama_kv_synth(self.handle, seq, npos, seed_k, seed_v), "cn_llama_kv_synth")
 

@@ -270,6 +270,14 @@ int cn_llama_step_kernels(cn_llama* m, int batch, int* out_count);
  * counterpart: roofline measurement) */
 int cn_llama_time_gemv(cn_llama* m, int proj, int batch, int iters, float* us_per_launch,
                        double* bytes_per_launch);
+/* Times one prefill matmul launch for n tokens as cn_llama_prefill_hidden_dev
+ * runs it: group 0 = q/k/v (one launch), 1 = O, 2 = gate/up (one launch),
+ * 3 = down; `iters` launches cycling through the layers, CUDA events on the
+ * context's stream.  Reports the mean time per launch and its FLOPs
+ * (2 * n * rows * cols).  Overwrites the prefill scratch.  (no reference
+ * counterpart: roofline measurement) */
+int cn_llama_time_matmul(cn_llama* m, int group, int n, int iters, float* us_per_launch,
+                         double* flops_per_launch);
 
 /* ---- tensor parallelism (one process per GPU) ---------------------------
  * (no reference counterpart: the reference runs on one CPU.)  Rank r of a
