@@ -95,6 +95,7 @@ SIGNATURES: dict[str, tuple] = {
     "cn_llama_step_kernels": (_i, [_vp, _i, C.POINTER(_i)]),
     "cn_llama_time_gemv": (_i, [_vp, _i, _i, _i, C.POINTER(_f), C.POINTER(C.c_double)]),
     "cn_llama_time_matmul": (_i, [_vp, _i, _i, _i, C.POINTER(_f), C.POINTER(C.c_double)]),
+    "cn_llama_profile_step": (_i, [_vp, _i, C.POINTER(_f), _i]),
     "cn_tensor_synth_slice": (_i, [_vp, _i, _i64, _i64, _i64, _i64, _i64, _i64, _u64, _i, C.POINTER(_vp)]),
     "cn_tp_create": (_i, [_vp, _i, _i, _i, _i, _i, C.POINTER(_vp)]),
     "cn_tp_handle": (_i, [_vp, _vp]),

@@ -40,7 +40,7 @@ struct cn_ctx {
 
 // A tensor-parallel rank's exchange state (tp.cu).  `buf` (IPC-exported)
 // holds [flags: kMaxTp uint32, padded to 256 B][slots: 2 parities x size ranks
-// x max_batch x dim fp32][logits: max_batch x vocab fp32]; peer[p] is rank
+// x max_batch x dim {fp32, seq} pairs][logits: max_batch x vocab fp32]; peer[p] is rank
 // p's buf mapped into this process (peer[rank] == buf).
 struct cn_tp {
     cn_ctx* ctx = nullptr;
@@ -156,10 +156,15 @@ struct PrepTarget {
 
 // Tensor-parallel exchange, producer side: a GEMV whose output is a partial
 // sum (O and down split along their input) or a slice (lm_head rows) stores
-// every output value into each rank's buffer over NVLink and, when all of
-// its CTAs are done, raises its flag on every rank.  Destination of value
-// (b, row) on rank p: dst[p] + parity * parity_stride + b * dst_ld + dst_row0
-// + row, parity = seq & 1, seq = *seq_base * uses + seq_add.
+// every output value into each rank's buffer over NVLink.  Two forms:
+//  * ll = 1 (residual partial sums): each value travels with its use's
+//    sequence number in one 8-byte store {value bits, seq}, so a consumer
+//    that reads the pair sees a value exactly when its sequence number
+//    matches; no fence, counter or flag.  Destination (b, row) on rank p:
+//    8-byte element dst[p] + parity * parity_stride + b * dst_ld + dst_row0 + row.
+//  * ll = 0 (lm_head slices): plain fp32 stores at the same index; when all
+//    the GEMV's CTAs are done the last one raises its flag on every rank.
+// parity = seq & 1, seq = *seq_base * uses + seq_add.
 constexpr int kMaxTp = 8;
 struct XchgOut {
     int size = 1, rank = 0;
@@ -169,9 +174,11 @@ struct XchgOut {
     const uint32_t* seq_base = nullptr;
     uint32_t uses = 1, seq_add = 0;
     int* done = nullptr;  // completion counter, zero on entry, left zero
+    int ll = 0;
 };
-// Consumer side: wait until flags[p] >= seq for every rank p, then the
-// summed input is sum_p src[parity * parity_stride + p * rank_stride + ...].
+// Consumer side: the summed input is sum_p src[parity * parity_stride +
+// p * rank_stride + ...], in 8-byte {value, seq} elements read until their
+// seq matches (ll = 1), or fp32 after every flags[p] >= seq (ll = 0).
 struct XchgIn {
     int size = 1;
     const float* src = nullptr;
@@ -180,6 +187,7 @@ struct XchgIn {
     const uint32_t* seq_base = nullptr;
     uint32_t uses = 1, seq_add = 0;
     uint32_t* err = nullptr;
+    int ll = 0;
 };
 
 struct GemvNeeds {
@@ -257,6 +265,8 @@ int gemv_launch(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t co
 int tp_step_launch(const cn_tp* tp, cudaStream_t s);
 XchgOut tp_reduce_out(const cn_tp* tp, uint32_t uses, uint32_t use, int done_index);
 XchgIn tp_reduce_in(const cn_tp* tp, uint32_t uses, uint32_t use, uint32_t* err);
+// The lm_head all-gather's completion (flags) for xchg_wait.
+XchgIn tp_gather_in(const cn_tp* tp, uint32_t uses, uint32_t use, uint32_t* err);
 XchgOut tp_gather_out(const cn_tp* tp, int64_t local_rows, uint32_t uses, uint32_t use, int done_index);
 float* tp_logits(const cn_tp* tp);
 

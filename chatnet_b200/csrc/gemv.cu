@@ -618,6 +618,77 @@ __global__ void xchg_wait_kernel(XchgIn xi) {
     if (threadIdx.x == 0) xchg_wait_dev(xi);
 }
 
+// One element of the exchange's summed input (as ll_sum4).
+__device__ __forceinline__ float ll_sum1(const XchgIn& xi, const uint64_t* base, size_t i, uint32_t seq,
+                                         uint64_t t0) {
+    uint64_t v[kMaxTp];
+    for (;;) {
+#pragma unroll
+        for (int p = 0; p < kMaxTp; p++)
+            if (p < xi.size)
+                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];"
+                             : "=l"(v[p]) : "l"(base + p * xi.rank_stride + i) : "memory");
+        bool ok = true;
+#pragma unroll
+        for (int p = 0; p < kMaxTp; p++)
+            if (p < xi.size) ok = ok && (uint32_t)(v[p] >> 32) == seq;
+        if (ok) break;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(xi.err, kErrTimeout);
+            break;
+        }
+    }
+    float d = __uint_as_float((uint32_t)v[0]);
+#pragma unroll
+    for (int p = 1; p < kMaxTp; p++)
+        if (p < xi.size) d = __fadd_rn(d, __uint_as_float((uint32_t)v[p]));
+    return d;
+}
+
+// The exchange's summed input at elements i..i+3 of a row (8-byte pairs;
+// ranks added in rank order, so every rank computes the same bits).  All
+// ranks' pairs are requested before any is checked, so the loads overlap;
+// the batch is re-read until every sequence number matches (bounded).
+__device__ __forceinline__ float4 ll_sum4(const XchgIn& xi, const uint64_t* base, size_t i, uint32_t seq,
+                                          uint64_t t0) {
+    uint64_t v[kMaxTp][4];
+    for (;;) {
+#pragma unroll
+        for (int p = 0; p < kMaxTp; p++) {
+            if (p < xi.size) {
+                const uint64_t* q = base + p * xi.rank_stride + i;
+                asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];"
+                             : "=l"(v[p][0]), "=l"(v[p][1]) : "l"(q) : "memory");
+                asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];"
+                             : "=l"(v[p][2]), "=l"(v[p][3]) : "l"(q + 2) : "memory");
+            }
+        }
+        bool ok = true;
+#pragma unroll
+        for (int p = 0; p < kMaxTp; p++)
+            if (p < xi.size)
+#pragma unroll
+                for (int e = 0; e < 4; e++) ok = ok && (uint32_t)(v[p][e] >> 32) == seq;
+        if (ok) break;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(xi.err, kErrTimeout);
+            break;
+        }
+    }
+    float4 s = make_float4(__uint_as_float((uint32_t)v[0][0]), __uint_as_float((uint32_t)v[0][1]),
+                           __uint_as_float((uint32_t)v[0][2]), __uint_as_float((uint32_t)v[0][3]));
+#pragma unroll
+    for (int p = 1; p < kMaxTp; p++) {
+        if (p < xi.size) {
+            s.x = __fadd_rn(s.x, __uint_as_float((uint32_t)v[p][0]));
+            s.y = __fadd_rn(s.y, __uint_as_float((uint32_t)v[p][1]));
+            s.z = __fadd_rn(s.z, __uint_as_float((uint32_t)v[p][2]));
+            s.w = __fadd_rn(s.w, __uint_as_float((uint32_t)v[p][3]));
+        }
+    }
+    return s;
+}
+
 // The exchange's summed input at element i of row b (ranks added in rank
 // order, so every rank computes the same bits).
 __device__ __forceinline__ float4 xchg_sum4(const XchgIn& xi, const float* base, size_t off) {
@@ -646,17 +717,27 @@ __global__ void __launch_bounds__(kNormThreads)
     const float* dr = delta ? delta + (size_t)b * n : nullptr;
     // tensor parallel: delta is the sum of every rank's partial (in rank order)
     const float* xbase = nullptr;
+    const uint64_t* llbase = nullptr;
+    uint32_t seq = 0;
+    const uint64_t t0 = globaltimer_ns();
     if (xi.size > 1) {
-        if (tid == 0) s_seq = xchg_wait_dev(xi);
-        __syncthreads();
-        xbase = xi.src + (s_seq & 1u) * xi.parity_stride + (size_t)b * n;
+        if (xi.ll) {
+            seq = *xi.seq_base * xi.uses + xi.seq_add;
+            llbase = reinterpret_cast<const uint64_t*>(xi.src) + (seq & 1u) * xi.parity_stride + (size_t)b * n;
+        } else {
+            if (tid == 0) s_seq = xchg_wait_dev(xi);
+            __syncthreads();
+            xbase = xi.src + (s_seq & 1u) * xi.parity_stride + (size_t)b * n;
+        }
         dr = nullptr;
     }
     float ss = 0.f;
     for (int i = 4 * tid; i < n; i += 4 * kNormThreads) {
         float4 v = *reinterpret_cast<const float4*>(xr + i);
-        if (dr || xbase) {
-            const float4 d = xbase ? xchg_sum4(xi, xbase, i) : *reinterpret_cast<const float4*>(dr + i);
+        if (dr || xbase || llbase) {
+            const float4 d = llbase  ? ll_sum4(xi, llbase, i, seq, t0)
+                             : xbase ? xchg_sum4(xi, xbase, i)
+                                     : *reinterpret_cast<const float4*>(dr + i);
             v.x = __fadd_rn(v.x, d.x);
             v.y = __fadd_rn(v.y, d.y);
             v.z = __fadd_rn(v.z, d.z);
@@ -678,9 +759,11 @@ __global__ void __launch_bounds__(kNormThreads)
     const int i = u * 256 + tid;
     if (i < n) {
         float v = xr[i];
-        if (dr || xbase) {
+        if (dr || xbase || llbase) {
             float d;
-            if (xbase) {
+            if (llbase) {
+                d = ll_sum1(xi, llbase, i, seq, t0);
+            } else if (xbase) {
                 d = __ldcg(xbase + i);
                 for (int p = 1; p < xi.size; p++) d = __fadd_rn(d, __ldcg(xbase + p * xi.rank_stride + i));
             } else {
@@ -1044,7 +1127,8 @@ int add_norm_prep(cudaStream_t st, const float* x_in, const float* delta, float*
 }
 
 int xchg_wait(cudaStream_t st, const XchgIn& xin) {
-    CN_CHECK(xin.size > 1 && xin.flags && xin.seq_base && xin.err, CN_ERR_INVALID_ARG, "bad exchange");
+    CN_CHECK(xin.size > 1 && !xin.ll && xin.flags && xin.seq_base && xin.err, CN_ERR_INVALID_ARG,
+             "bad exchange");
     CN_CUDA(launch_k(true, xchg_wait_kernel, dim3(1), dim3(32), 0, st, xin));
     CN_CUDA(cudaGetLastError());
     return CN_OK;

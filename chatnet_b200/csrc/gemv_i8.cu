@@ -74,12 +74,23 @@ struct Args {
 // Stores output value (b, row) of matrix m: locally, or, in an exchange, into
 // every rank's buffer (peer stores over NVLink).
 __device__ __forceinline__ void store_out(const Args& a, float* y, int64_t rows, int b, int64_t row, float v,
-                                          uint32_t parity) {
+                                          uint32_t seq) {
     if (a.xo.size <= 1) {
         y[(size_t)b * rows + row] = v;
         return;
     }
-    const int64_t off = parity * a.xo.parity_stride + b * a.xo.dst_ld + a.xo.dst_row0 + row;
+    const int64_t off = (seq & 1u) * a.xo.parity_stride + b * a.xo.dst_ld + a.xo.dst_row0 + row;
+    if (a.xo.ll) {
+        // value and sequence number in one 8-byte store: the pair is atomic
+        const uint64_t pair = ((uint64_t)seq << 32) | __float_as_uint(v);
+#pragma unroll
+        for (int p = 0; p < kMaxTp; p++)
+            if (p < a.xo.size)
+                asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(reinterpret_cast<uint64_t*>(a.xo.dst[p]) + off),
+                             "l"(pair)
+                             : "memory");
+        return;
+    }
 #pragma unroll
     for (int p = 0; p < kMaxTp; p++)
         if (p < a.xo.size) a.xo.dst[p][off] = v;
@@ -157,7 +168,7 @@ __device__ __forceinline__ int owned_seq(int nt, int t) {
 template <int NB>
 __device__ void finish_subtile(const Args& a, int r, int t, int warp, int tile, int cta, int C,
                                int64_t total, bool shared_tile, int my_slot,
-                               const float (&acc)[Geo<NB>::NT], uint32_t parity) {
+                               const float (&acc)[Geo<NB>::NT], uint32_t seq) {
     constexpr int NT = Geo<NB>::NT;
     const int m = mat_of(a, tile);
     const int64_t rows = pick64(a.rows, m);
@@ -168,7 +179,7 @@ __device__ void finish_subtile(const Args& a, int r, int t, int warp, int tile, 
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
                 const int b = owned_seq<NB>(nt, t);
-                if (b >= 0) store_out(a, y, rows, b, row, acc[nt], parity);
+                if (b >= 0) store_out(a, y, rows, b, row, acc[nt], seq);
             }
         }
         return;
@@ -201,7 +212,7 @@ __device__ void finish_subtile(const Args& a, int r, int t, int warp, int tile, 
             const int slot = 2 * c + (tile == first_tile ? 0 : 1);
             s += __ldcg(a.partials + ((size_t)slot * kRows + r) * 8 + b);
         }
-        if (row < rows) store_out(a, y, rows, b, row, s, parity);
+        if (row < rows) store_out(a, y, rows, b, row, s, seq);
     }
     __syncwarp();
     if ((threadIdx.x & 31) == 0) atomicExch(ctr, 0);
@@ -308,7 +319,6 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB>::kCtasPerSm)
     // ---- consumers ----
     pdl_wait();
     const uint32_t seq = a.xo.size > 1 ? *a.xo.seq_base * a.xo.uses + a.xo.seq_add : 0u;
-    const uint32_t parity = seq & 1u;
     const int g = lane >> 2, t = lane & 3;
     const int row0 = 16 * warp + g, row1 = row0 + 8;
     const int r_own = (t & 1) ? row1 : row0;
@@ -428,23 +438,25 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB>::kCtasPerSm)
         const bool head_cut = (et == tile0) && (u0 != 0);
         const bool tail_cut = eu + seg != a.units;
         finish_subtile<NB>(a, r_own, t, warp, et, cta, C, total, head_cut || tail_cut, et == tile0 ? 0 : 1,
-                           acc, parity);
+                           acc, seq);
         et++;
         eu = 0;
     }
-    if (a.xo.size > 1) {
-        // exchange: once every CTA's peer stores are visible system-wide, the
+    if (a.xo.size > 1 && !a.xo.ll) {
+        // gather: once every CTA's peer stores are visible system-wide, the
         // last CTA raises this rank's flag on every rank
         // (the barrier orders every consumer's peer stores before thread 0's
-        // system-scope fence, which then covers them all)
+        // system-scope release fence, which then covers them all; an
+        // acquire-release fence is enough here and costs less than a
+        // sequentially consistent one)
         asm volatile("bar.sync 1, %0;" ::"n"(kCons * 32) : "memory");
         if (threadIdx.x == 0) {
-            __threadfence_system();
+            asm volatile("fence.acq_rel.sys;" ::: "memory");
             int old;
             asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(a.xo.done) : "memory");
             if (old == (int)gridDim.x - 1) {
                 *a.xo.done = 0;
-                __threadfence_system();
+                asm volatile("fence.acq_rel.sys;" ::: "memory");
 #pragma unroll
                 for (int p = 0; p < kMaxTp; p++)
                     if (p < a.xo.size)
@@ -506,7 +518,7 @@ int gemv_i8_run_group(cudaStream_t st, uint32_t* err, int nmat, const CUtensorMa
     CN_CHECK(batch >= 1 && batch <= i8::kMaxNB && cols % 256 == 0 && ctas > 0 && nmat >= 1 &&
                  nmat <= i8::kMaxMats,
              CN_ERR_INVALID_ARG, "integer GEMV: bad shape");
-    CN_CHECK(!xo || xo->size <= 1 || (nmat == 1 && xo->size <= kMaxTp && xo->done && xo->seq_base),
+    CN_CHECK(!xo || xo->size <= 1 || (nmat == 1 && xo->size <= kMaxTp && (xo->ll || xo->done) && xo->seq_base),
              CN_ERR_INVALID_ARG, "integer GEMV: bad exchange");
     int rc = gemv_i8_prepare();
     if (rc) return rc;

@@ -200,6 +200,25 @@ static int norm(cn_llama* m, cudaStream_t s, const cn_tensor* w, int B, const Ge
 
 // Enqueues one decode step for B sequences (tokens/positions already in
 // m->tokens / m->pos).
+// Per-launch profiling of an eagerly enqueued step (cn_llama_profile_step):
+// when set, every stage of enqueue_step records an event after its launches.
+struct StepProfile {
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> kind;
+};
+static StepProfile* g_prof = nullptr;
+enum { P_START = 0, P_TP, P_EMBED, P_NORM, P_QKV, P_ROPE, P_ATTN, P_O, P_GATEUP, P_SILU, P_DOWN, P_HEAD,
+       P_WAIT, P_ARGMAX, P_KINDS };
+static int mark(cudaStream_t s, int kind) {
+    if (!g_prof) return CN_OK;
+    cudaEvent_t e;
+    CN_CUDA(cudaEventCreate(&e));
+    CN_CUDA(cudaEventRecord(e, s));
+    g_prof->ev.push_back(e);
+    g_prof->kind.push_back(kind);
+    return CN_OK;
+}
+
 static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
     const cn_llama_config& c = m->cfg;
     Step& st = m->steps[B];
@@ -211,17 +230,18 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
     const bool tp = m->tp && m->tp->size > 1;
     const uint32_t uses = 2u * (uint32_t)c.n_layers + 1u;
     int rc;
-    if (tp && (rc = tp_step_launch(m->tp, s))) return rc;
+    if (tp && ((rc = tp_step_launch(m->tp, s)) || (rc = mark(s, P_TP)))) return rc;
     rc = launch_embed(emb->type, emb->d, emb->row_bytes, m->tokens, c.vocab, c.dim, B, m->x,
                       m->ctx->dev_err, s);
-    if (rc) return rc;
+    if (rc || (rc = mark(s, P_EMBED))) return rc;
     PrepCache pc;
     float* x = m->x;
     const float* delta = nullptr;  // output of the last projection, not yet added to x
     XchgIn xin;                    // tensor parallel: the exchange that delivers it
     for (int l = 0; l < c.n_layers; l++) {
         const GemvOp* ops = &st.ops[(size_t)l * 7];
-        if ((rc = norm(m, s, LT(m, l, L_ANORM), B, ops[0], &x, &delta, pc, &xin))) return rc;
+        if ((rc = norm(m, s, LT(m, l, L_ANORM), B, ops[0], &x, &delta, pc, &xin)) || (rc = mark(s, P_NORM)))
+            return rc;
         xin = XchgIn();
         if (st.qkv[l].n) {
             float* ys[3] = {m->q, m->k, m->v};
@@ -231,6 +251,7 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
             if ((rc = gemv(m, s, ops[1], m->xn, m->k, pc))) return rc;
             if ((rc = gemv(m, s, ops[2], m->xn, m->v, pc))) return rc;
         }
+        if ((rc = mark(s, P_QKV))) return rc;
         RopeKvArgs ra;
         ra.q = m->q;
         ra.k = m->k;
@@ -251,7 +272,7 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
         ra.kv_f16 = c.kv_dtype == CN_KV_F16;
         ra.ctx_len = c.ctx_len;
         ra.err = m->ctx->dev_err;
-        if ((rc = launch_rope_kv(ra, s))) return rc;
+        if ((rc = launch_rope_kv(ra, s)) || (rc = mark(s, P_ROPE))) return rc;
         AttnArgs aa;
         aa.q = m->q;
         aa.kcache = m->kc;
@@ -273,7 +294,7 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
         aa.out_stride = qdim;
         aa.prep = prep_target(&ops[3], m->gb);
         if ((m->nh / m->nkv) * c.head_dim % 256 != 0) aa.prep.kind = -1;
-        if ((rc = launch_attention(aa, st.ap, s))) return rc;
+        if ((rc = launch_attention(aa, st.ap, s)) || (rc = mark(s, P_ATTN))) return rc;
         pc = PrepCache();
         if (aa.prep.kind >= 0) pc.set(m->att, ops[3]);
         if (tp) {
@@ -284,7 +305,9 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
             if ((rc = gemv(m, s, ops[3], m->att, m->tmp, pc))) return rc;
             delta = m->tmp;
         }
-        if ((rc = norm(m, s, LT(m, l, L_FNORM), B, ops[4], &x, &delta, pc, &xin))) return rc;
+        if ((rc = mark(s, P_O))) return rc;
+        if ((rc = norm(m, s, LT(m, l, L_FNORM), B, ops[4], &x, &delta, pc, &xin)) || (rc = mark(s, P_NORM)))
+            return rc;
         xin = XchgIn();
         if (st.gu[l].n) {
             float* ys[2] = {m->gate, m->up};
@@ -293,8 +316,9 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
             if ((rc = gemv(m, s, ops[4], m->xn, m->gate, pc))) return rc;
             if ((rc = gemv(m, s, ops[5], m->xn, m->up, pc))) return rc;
         }
+        if ((rc = mark(s, P_GATEUP))) return rc;
         const PrepTarget spt = prep_target(&ops[6], m->gb);
-        if ((rc = launch_silu_prep(m->gate, m->up, hid, B, spt, s))) return rc;
+        if ((rc = launch_silu_prep(m->gate, m->up, hid, B, spt, s)) || (rc = mark(s, P_SILU))) return rc;
         pc = PrepCache();
         if (spt.kind >= 0 && hid % 256 == 0) pc.set(m->gate, ops[6]);
         if (tp) {
@@ -305,18 +329,21 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
             if ((rc = gemv(m, s, ops[6], m->gate, m->tmp, pc))) return rc;
             delta = m->tmp;
         }
+        if ((rc = mark(s, P_DOWN))) return rc;
     }
     const GemvOp& head = st.ops[(size_t)c.n_layers * 7];
-    if ((rc = norm(m, s, m->t[T_ONORM], B, head, &x, &delta, pc, &xin))) return rc;
+    if ((rc = norm(m, s, m->t[T_ONORM], B, head, &x, &delta, pc, &xin)) || (rc = mark(s, P_NORM))) return rc;
     if (tp) {
         // lm_head rows of this rank go to every rank's logits (all-gather)
         const XchgOut xo = tp_gather_out(m->tp, m->vocab_l, uses, uses - 1u, 2);
-        if ((rc = gemv(m, s, head, m->xn, m->tmp, pc, &xo))) return rc;
-        if ((rc = xchg_wait(s, tp_reduce_in(m->tp, uses, uses - 1u, m->ctx->dev_err)))) return rc;
+        if ((rc = gemv(m, s, head, m->xn, m->tmp, pc, &xo)) || (rc = mark(s, P_HEAD))) return rc;
+        if ((rc = xchg_wait(s, tp_gather_in(m->tp, uses, uses - 1u, m->ctx->dev_err))) || (rc = mark(s, P_WAIT)))
+            return rc;
     } else {
-        if ((rc = gemv(m, s, head, m->xn, m->logits, pc))) return rc;
+        if ((rc = gemv(m, s, head, m->xn, m->logits, pc)) || (rc = mark(s, P_HEAD))) return rc;
     }
-    return launch_argmax(m->logits, c.vocab, B, m->amax, s);
+    if ((rc = launch_argmax(m->logits, c.vocab, B, m->amax, s))) return rc;
+    return mark(s, P_ARGMAX);
 }
 
 // Builds the step for B sequences and, with graphs on, captures it once.
@@ -865,6 +892,35 @@ int cn_llama_time_gemv(cn_llama* m, int proj, int batch, int iters, float* us_pe
     cudaEventDestroy(e1);
     *us_per_launch = ms * 1000.f / iters;
     *bytes_per_launch = (double)op0.rb * op0.rows + 4.0 * batch * (op0.rows + op0.cols);
+    return check_dev_err_reset(m);
+}
+
+int cn_llama_profile_step(cn_llama* m, int batch, float* us_by_stage, int n_stages) {
+    CN_CHECK(m && us_by_stage && n_stages >= 1, CN_ERR_INVALID_ARG, "null argument");
+    CN_CHECK(batch >= 1 && batch <= m->cfg.max_batch, CN_ERR_INVALID_ARG, "bad batch");
+    cudaSetDevice(m->ctx->device);
+    int rc = build_step(m, batch);
+    if (rc) return rc;
+    cudaStream_t s = m->ctx->stream;
+    CN_CUDA(cudaStreamSynchronize(s));
+    StepProfile prof;
+    g_prof = &prof;
+    rc = mark(s, P_START);
+    if (!rc) rc = enqueue_step(m, batch, s);
+    g_prof = nullptr;
+    if (!rc) {
+        const cudaError_t e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) rc = cuda_error(e, "profile step");
+    }
+    for (int k = 0; k < n_stages; k++) us_by_stage[k] = 0.f;
+    for (size_t i = 1; !rc && i < prof.ev.size(); i++) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, prof.ev[i - 1], prof.ev[i]);
+        const int k = prof.kind[i];
+        if (k < n_stages) us_by_stage[k] += ms * 1000.f;
+    }
+    for (cudaEvent_t e : prof.ev) cudaEventDestroy(e);
+    if (rc) return rc;
     return check_dev_err_reset(m);
 }
 

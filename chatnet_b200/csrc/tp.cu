@@ -4,10 +4,13 @@
 // CUDA IPC handle, and maps every other rank's buffer after the host has
 // passed the handles around.  The GEMVs whose outputs must be combined
 // (O and down: partial sums; lm_head: row slices) store into every rank's
-// buffer from their epilogue and raise a flag there (gemv_i8.cu); the next
-// kernel on each rank waits for all flags and reads its own buffer
-// (gemv.cu).  A flag holds the sequence number of the last exchange its rank
-// completed: step * uses_per_step + use, so the waits need no reset.
+// buffer from their epilogue (gemv_i8.cu) and the next kernel on each rank
+// reads its own buffer (gemv.cu).  Every exchange has a sequence number,
+// step * uses_per_step + use.  The residual partial sums travel as 8-byte
+// {value, seq} pairs that the reader checks one by one (no flag, no fence);
+// the lm_head slices are plain floats followed by a flag per rank holding
+// the sequence number of the last gather that rank completed.  Neither
+// needs a reset.
 #include <string.h>
 
 #include <new>
@@ -34,8 +37,10 @@ XchgOut tp_reduce_out(const cn_tp* tp, uint32_t uses, uint32_t use, int done_ind
     x.size = tp->size;
     x.rank = tp->rank;
     const int64_t per_rank = (int64_t)tp->max_batch * tp->dim;
+    x.ll = 1;
     for (int p = 0; p < tp->size; p++) {
-        x.dst[p] = reinterpret_cast<float*>(static_cast<uint8_t*>(tp->peer[p]) + tp->slots_off) + tp->rank * per_rank;
+        x.dst[p] = reinterpret_cast<float*>(
+            reinterpret_cast<uint64_t*>(static_cast<uint8_t*>(tp->peer[p]) + tp->slots_off) + tp->rank * per_rank);
         x.flag[p] = reinterpret_cast<uint32_t*>(tp->peer[p]) + tp->rank;
     }
     x.parity_stride = tp->size * per_rank;
@@ -51,7 +56,8 @@ XchgOut tp_reduce_out(const cn_tp* tp, uint32_t uses, uint32_t use, int done_ind
 XchgIn tp_reduce_in(const cn_tp* tp, uint32_t uses, uint32_t use, uint32_t* err) {
     XchgIn x;
     x.size = tp->size;
-    x.src = reinterpret_cast<const float*>(tp->buf + tp->slots_off);
+    x.src = reinterpret_cast<const float*>(tp->buf + tp->slots_off);  // 8-byte {value, seq} elements
+    x.ll = 1;
     x.rank_stride = (int64_t)tp->max_batch * tp->dim;
     x.parity_stride = tp->size * x.rank_stride;
     x.flags = reinterpret_cast<const uint32_t*>(tp->buf);
@@ -62,8 +68,15 @@ XchgIn tp_reduce_in(const cn_tp* tp, uint32_t uses, uint32_t use, uint32_t* err)
     return x;
 }
 
+XchgIn tp_gather_in(const cn_tp* tp, uint32_t uses, uint32_t use, uint32_t* err) {
+    XchgIn x = tp_reduce_in(tp, uses, use, err);
+    x.ll = 0;
+    return x;
+}
+
 XchgOut tp_gather_out(const cn_tp* tp, int64_t local_rows, uint32_t uses, uint32_t use, int done_index) {
     XchgOut x = tp_reduce_out(tp, uses, use, done_index);
+    x.ll = 0;
     for (int p = 0; p < tp->size; p++)
         x.dst[p] = reinterpret_cast<float*>(static_cast<uint8_t*>(tp->peer[p]) + tp->logits_off);
     x.parity_stride = 0;
@@ -96,7 +109,7 @@ int cn_tp_create(cn_ctx* ctx, int rank, int size, int max_batch, int dim, int vo
     t->dim = dim;
     t->vocab = vocab;
     t->slots_off = 256;
-    t->logits_off = t->slots_off + (size_t)2 * size * max_batch * dim * 4;
+    t->logits_off = t->slots_off + (size_t)2 * size * max_batch * dim * 8;
     t->bytes = t->logits_off + (size_t)max_batch * vocab * 4;
     CN_CUDA(cudaSetDevice(ctx->device));
     cudaError_t e = cudaMalloc(&t->buf, t->bytes);

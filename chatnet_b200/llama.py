@@ -167,6 +167,15 @@ class CudaLlamaModel:
               "cn_llama_time_gemv")
         return us.value, nb.value
 
+    STAGES = ("start", "tp_step", "embed", "norm", "qkv", "rope", "attn", "o", "gate_up", "silu", "down",
+              "head", "xchg_wait", "argmax")
+
+    def profile_step(self, batch: int) -> dict[str, float]:
+        """us per stage of one eagerly run decode step (cn_llama_profile_step)."""
+        arr = (C.c_float * len(self.STAGES))()
+        check(N.lib().cn_llama_profile_step(self.handle, batch, arr, len(self.STAGES)), "cn_llama_profile_step")
+        return {k: arr[i] for i, k in enumerate(self.STAGES) if i > 0}
+
     def time_matmul(self, group: int, n: int, iters: int) -> tuple[float, float]:
         """Mean us and FLOPs of one prefill matmul launch (0 qkv, 1 O, 2 gate/up, 3 down)."""
         us, fl = C.c_float(0), C.c_double(0)

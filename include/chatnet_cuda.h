@@ -270,6 +270,15 @@ int cn_llama_step_kernels(cn_llama* m, int batch, int* out_count);
  * counterpart: roofline measurement) */
 int cn_llama_time_gemv(cn_llama* m, int proj, int batch, int iters, float* us_per_launch,
                        double* bytes_per_launch);
+/* Runs one decode step for `batch` without its graph, recording an event
+ * after each stage, and adds each stage's time (us) into us_by_stage[kind]
+ * (kinds: 0 unused, 1 tensor-parallel step counter, 2 embedding, 3 add +
+ * RmsNorm + prep, 4 q/k/v, 5 RoPE + KV store, 6 attention, 7 O, 8 gate/up,
+ * 9 SiLU + prep, 10 down, 11 lm_head, 12 exchange wait, 13 argmax; at most
+ * n_stages entries are written).  Events between launches serialise them, so
+ * the sum exceeds the graph's step time.  (no reference counterpart:
+ * diagnostics) */
+int cn_llama_profile_step(cn_llama* m, int batch, float* us_by_stage, int n_stages);
 /* Times one prefill matmul launch for n tokens as cn_llama_prefill_hidden_dev
  * runs it: group 0 = q/k/v (one launch), 1 = O, 2 = gate/up (one launch),
  * 3 = down; `iters` launches cycling through the layers, CUDA events on the
