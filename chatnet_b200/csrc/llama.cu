@@ -272,7 +272,10 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
         ra.kv_f16 = c.kv_dtype == CN_KV_F16;
         ra.ctx_len = c.ctx_len;
         ra.err = m->ctx->dev_err;
-        if ((rc = launch_rope_kv(ra, s)) || (rc = mark(s, P_ROPE))) return rc;
+        // the tensor-core attention (fp16 cache) rotates q and stores the new
+        // k/v rows itself; otherwise RoPE and the cache store run first
+        const bool fuse_rope = st.ap.mma;
+        if (!fuse_rope && ((rc = launch_rope_kv(ra, s)) || (rc = mark(s, P_ROPE)))) return rc;
         AttnArgs aa;
         aa.q = m->q;
         aa.kcache = m->kc;
@@ -293,6 +296,13 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
         aa.out = m->att;
         aa.out_stride = qdim;
         aa.prep = prep_target(&ops[3], m->gb);
+        if (fuse_rope) {
+            aa.rope.k = m->k;
+            aa.rope.v = m->v;
+            aa.rope.rope = m->rope;
+            aa.rope.kv_stride = kvd;
+            aa.rope.on = 1;
+        }
         if ((m->nh / m->nkv) * c.head_dim % 256 != 0) aa.prep.kind = -1;
         if ((rc = launch_attention(aa, st.ap, s)) || (rc = mark(s, P_ATTN))) return rc;
         pc = PrepCache();

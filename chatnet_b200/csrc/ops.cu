@@ -431,7 +431,7 @@ __global__ void __launch_bounds__(kAttnThreads)
                     const __half* __restrict__ vcache, const int* __restrict__ pos_dev, int pos_host,
                     int n_heads, int n_kv, int q_stride, int64_t cache_seq_stride, int64_t cache_layer_off,
                     int ctx_len, int splits, float scale, float* __restrict__ part, int* __restrict__ counters,
-                    float* __restrict__ out, int out_stride, PrepTarget pt) {
+                    float* __restrict__ out, int out_stride, PrepTarget pt, RopeIn ri) {
     pdl_trigger();
     pdl_wait();
     static_assert(kAttnThreads == 256 && kMmaChunk == 16 * (kAttnThreads / 32), "16 positions per warp");
@@ -464,21 +464,63 @@ __global__ void __launch_bounds__(kAttnThreads)
         const __half* kbase = kcache + (int64_t)b * cache_seq_stride + cache_layer_off + kh * HD;
         const __half* vbase = vcache + (int64_t)b * cache_seq_stride + cache_layer_off + kh * HD;
         constexpr int CPR = HD / 8;  // 16-byte chunks per row
+        // with ri.on, row pos of the cache is written here (from the new k/v)
+        const int r_new = ri.on ? pos - p0 : -1;
         for (int i = tid; i < kMmaChunk * CPR; i += kAttnThreads) {
             const int r = i / CPR, c = i % CPR;
+            if (r == r_new) continue;  // written below, not copied (no zero fill racing it)
             const bool in = r < L;
             const int64_t go = (int64_t)(p0 + (in ? r : 0)) * kvdim + c * 8;
             cp_async16(smem_u32(Ks + r * RS + c * 8), kbase + go, in ? 16 : 0);
             cp_async16(smem_u32(Vs + r * RS + c * 8), vbase + go, in ? 16 : 0);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
+        if (r_new >= 0 && r_new < L) {
+            // TensorMath.ApplyRoPE on the new k row, then k and v into the cache
+            // (the rope_kv_kernel arithmetic, bit for bit)
+            const float2* tab = ri.rope + (size_t)pos * (HD / 2);
+            const float* kr = ri.k + (size_t)b * ri.kv_stride + kh * HD;
+            const float* vr = ri.v + (size_t)b * ri.kv_stride + kh * HD;
+            __half* kw = const_cast<__half*>(kbase) + (int64_t)pos * kvdim;
+            __half* vw = const_cast<__half*>(vbase) + (int64_t)pos * kvdim;
+            for (int p = tid; p < HD / 2; p += kAttnThreads) {
+                const float2 cs = tab[p];
+                const float x0 = kr[2 * p], x1 = kr[2 * p + 1];
+                const __half h0 = __float2half_rn(__fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y)));
+                const __half h1 = __float2half_rn(__fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x)));
+                Ks[r_new * RS + 2 * p] = h0;
+                Ks[r_new * RS + 2 * p + 1] = h1;
+                kw[2 * p] = h0;
+                kw[2 * p + 1] = h1;
+                const __half v0 = __float2half_rn(vr[2 * p]), v1 = __float2half_rn(vr[2 * p + 1]);
+                Vs[r_new * RS + 2 * p] = v0;
+                Vs[r_new * RS + 2 * p + 1] = v1;
+                vw[2 * p] = v0;
+                vw[2 * p + 1] = v1;
+            }
+        }
         // query heads: fp16 hi in rows 0-7, the fp16 remainder in rows 8-15
-        for (int i = tid; i < 8 * HD; i += kAttnThreads) {
-            const int gi = i / HD, d = i % HD;
-            const float v = gi < kv_mul ? q[(size_t)b * q_stride + (kh * kv_mul + gi) * HD + d] : 0.f;
-            const __half hi = __float2half_rn(v);
-            Qs[gi * RS + d] = hi;
-            Qs[(8 + gi) * RS + d] = __float2half_rn(v - __half2float(hi));
+        // (rotated here when ri.on, as rope_kv_kernel would have)
+        for (int i = tid; i < 8 * HD / 2; i += kAttnThreads) {
+            const int gi = i / (HD / 2), p = i % (HD / 2);
+            float v0 = 0.f, v1 = 0.f;
+            if (gi < kv_mul) {
+                const float* qr = q + (size_t)b * q_stride + (kh * kv_mul + gi) * HD;
+                v0 = qr[2 * p];
+                v1 = qr[2 * p + 1];
+                if (ri.on) {
+                    const float2 cs = ri.rope[(size_t)pos * (HD / 2) + p];
+                    const float r0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
+                    const float r1 = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
+                    v0 = r0;
+                    v1 = r1;
+                }
+            }
+            const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+            Qs[gi * RS + 2 * p] = h0;
+            Qs[gi * RS + 2 * p + 1] = h1;
+            Qs[(8 + gi) * RS + 2 * p] = __float2half_rn(v0 - __half2float(h0));
+            Qs[(8 + gi) * RS + 2 * p + 1] = __float2half_rn(v1 - __half2float(h1));
         }
         asm volatile("cp.async.wait_group 0;" ::: "memory");
         __syncthreads();
@@ -800,6 +842,8 @@ int attention_prepare(const AttnPlan& p) {
 
 int launch_attention(const AttnArgs& a, const AttnPlan& p, cudaStream_t s) {
     dim3 grid(p.splits, a.n_kv, a.batch);
+    CN_CHECK(!a.rope.on || (p.mma && a.rope.k && a.rope.v && a.rope.rope), CN_ERR_INVALID_ARG,
+             "attention: RoPE fusion needs the tensor-core kernel");
     const float scale = 1.0f / sqrtf((float)a.hd);
     CN_CHECK(a.out_stride % 4 == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 &&
                  (reinterpret_cast<uintptr_t>(a.part) & 15) == 0,
@@ -813,7 +857,7 @@ int launch_attention(const AttnArgs& a, const AttnPlan& p, cudaStream_t s) {
         CN_CUDA(launch_k(true, k, grid, dim3(kAttnThreads), p.smem, s, a.q, (const __half*)a.kcache,
                          (const __half*)a.vcache, a.pos_dev, a.pos_host, a.n_heads, a.n_kv, a.q_stride,
                          a.cache_seq_stride, a.cache_layer_off, a.ctx_len, p.splits, scale, a.part,
-                         a.counters, a.out, a.out_stride, pt));
+                         a.counters, a.out, a.out_stride, pt, a.rope));
     } else if (a.kv_f16) {
         CN_CUDA(launch_k(true, attn_split_kernel<__half>, grid, dim3(kAttnThreads), p.smem, s,
             a.q, (const __half*)a.kcache, (const __half*)a.vcache, a.pos_dev, a.pos_host, a.n_heads,

@@ -30,6 +30,17 @@ struct AttnPlan {
     size_t part_floats = 0, smem = 0;
 };
 
+// RoPE and the KV-cache store done inside the tensor-core attention kernel
+// (fp16 cache): q and the new k row are rotated as they are loaded, and the
+// split that holds position pos writes the new k and v rows to the cache.
+struct RopeIn {
+    const float* k = nullptr;      // [batch][kv_stride] new k rows (not rotated)
+    const float* v = nullptr;      // [batch][kv_stride] new v rows
+    const float2* rope = nullptr;  // [ctx][hd/2] (cos, sin)
+    int kv_stride = 0;
+    int on = 0;
+};
+
 struct AttnArgs {
     const float* q;  // [batch][q_stride] (rotated)
     const void* kcache;
@@ -44,6 +55,7 @@ struct AttnArgs {
     float* out;      // [batch][out_stride]
     int out_stride;
     PrepTarget prep;  // the O projection's records (kind -1: none)
+    RopeIn rope;      // on: q not yet rotated, the new k/v rows not yet in the cache
 };
 
 int launch_rmsnorm(const float* x, const float* w, float* y, int n, int rows, float eps,
