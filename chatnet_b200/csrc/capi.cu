@@ -398,7 +398,7 @@ int cn_matvec(cn_ctx* ctx, const cn_tensor* W, const float* host_x, float* host_
 }
 
 static int matmul_dev(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols,
-                      const float* d_x, float* d_y, int n_tokens) {
+                      const float* d_x, float* d_y, int n_tokens, const CUtensorMap* wmap_opt = nullptr) {
     CN_CHECK(type == CN_TYPE_Q4_0, CN_ERR_UNSUPPORTED, "matmul: type %d not supported (Q4_0)", type);
     CN_CHECK(n_tokens >= 1 && rows >= 1 && cols >= 256 && cols % 256 == 0, CN_ERR_INVALID_ARG,
              "matmul: bad shape (%lld x %lld, %d tokens)", (long long)rows, (long long)cols, n_tokens);
@@ -409,8 +409,8 @@ static int matmul_dev(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int6
     rc = to_half(ctx->stream, d_x, xh, (int64_t)n_tokens * cols);
     if (rc) return rc;
     const int64_t ldy = rows;
-    return matmul_q4_0(ctx->stream, ctx->dev_err, 1, &d_w, &rows, cols, xh, n_tokens, &d_y, &ldy,
-                       false);
+    return matmul_q4_0(ctx->stream, ctx->dev_err, 1, &d_w, wmap_opt ? &wmap_opt : nullptr, &rows, cols, xh,
+                       n_tokens, &d_y, &ldy, false);
 }
 
 int cn_matmul(cn_ctx* ctx, const cn_tensor* W, const float* host_x, float* host_y, int n_tokens) {
@@ -425,7 +425,7 @@ int cn_matmul(cn_ctx* ctx, const cn_tensor* W, const float* host_x, float* host_
     float* dx = reinterpret_cast<float*>(ctx->dstage);
     float* dy = reinterpret_cast<float*>(static_cast<uint8_t*>(ctx->dstage) + yoff);
     CN_CUDA(cudaMemcpyAsync(dx, host_x, xb, cudaMemcpyHostToDevice, ctx->stream));
-    rc = matmul_dev(ctx, W->type, W->d, W->rows, W->cols, dx, dy, n_tokens);
+    rc = matmul_dev(ctx, W->type, W->d, W->rows, W->cols, dx, dy, n_tokens, W->has_map ? &W->map : nullptr);
     if (rc) return rc;
     CN_CUDA(cudaMemcpyAsync(host_y, dy, yb, cudaMemcpyDeviceToHost, ctx->stream));
     CN_CUDA(cudaStreamSynchronize(ctx->stream));

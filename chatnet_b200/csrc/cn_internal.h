@@ -86,8 +86,9 @@ int encode_tiled_2d(CUtensorMapDataType dt, void* base, const cuuint64_t (&dims)
 // Prefill dequant-matmul (matmul.cu): y[i][t][r] (+)= dot(W_i[r], x[t]) for
 // M tokens and nmat <= 3 Q4_0 matrices with the same K (K % 256 == 0); x is
 // fp16 [M][K] (16-byte aligned), y[i] fp32 [M][ldy[i]].
-int matmul_q4_0(cudaStream_t st, uint32_t* err, int nmat, const void* const* w, const int64_t* rows,
-                int64_t K, const __half* x, int M, float* const* y, const int64_t* ldy,
+// wmaps[i] may be null (the weight map is then encoded per call).
+int matmul_q4_0(cudaStream_t st, uint32_t* err, int nmat, const void* const* w, const CUtensorMap* const* wmaps,
+                const int64_t* rows, int64_t K, const __half* x, int M, float* const* y, const int64_t* ldy,
                 bool accumulate);
 // fp32 -> fp16, n % 4 == 0, both 16-byte aligned.
 int to_half(cudaStream_t st, const float* x, __half* y, int64_t n);

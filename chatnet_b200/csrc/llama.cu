@@ -436,6 +436,9 @@ static void free_model(cn_llama* m) {
 
 // ---- prefill: n tokens through the decoder at once (tcgen05 matmul) ----------
 
+// A weight tensor's TMA descriptor, or null (the matmul then encodes one).
+static const CUtensorMap* wmap(const cn_tensor* t) { return t->has_map ? &t->map : nullptr; }
+
 // Whether the model's projections can run on the prefill matmul (Q4_0 with
 // inner dimensions that are multiples of 256, one GPU).
 static bool prefill_supported(const cn_llama* m) {
@@ -495,9 +498,10 @@ static int prefill_layers(cn_llama* m, int n, int pos) {
             return rc;
         {
             const void* w[3] = {LT(m, l, L_Q)->d, LT(m, l, L_K)->d, LT(m, l, L_V)->d};
+            const CUtensorMap* wm[3] = {wmap(LT(m, l, L_Q)), wmap(LT(m, l, L_K)), wmap(LT(m, l, L_V))};
             const int64_t rows[3] = {qd, kvd, kvd};
             float* y[3] = {m->pf_q, m->pf_k, m->pf_v};
-            if ((rc = matmul_q4_0(s, err, 3, w, rows, c.dim, m->pf_h, n, y, rows, false))) return rc;
+            if ((rc = matmul_q4_0(s, err, 3, w, wm, rows, c.dim, m->pf_h, n, y, rows, false))) return rc;
         }
         RopeKvArgs ra;
         ra.q = m->pf_q;
@@ -525,22 +529,25 @@ static int prefill_layers(cn_llama* m, int n, int pos) {
             return rc;
         {
             const void* w = LT(m, l, L_O)->d;
+            const CUtensorMap* wm = wmap(LT(m, l, L_O));
             const int64_t rows = c.dim;
-            if ((rc = matmul_q4_0(s, err, 1, &w, &rows, qd, m->pf_h, n, &m->pf_x, &rows, true))) return rc;
+            if ((rc = matmul_q4_0(s, err, 1, &w, &wm, &rows, qd, m->pf_h, n, &m->pf_x, &rows, true))) return rc;
         }
         if ((rc = prefill_norm(s, m->pf_x, (const float*)LT(m, l, L_FNORM)->d, m->pf_h, c.dim, n, c.rms_eps)))
             return rc;
         {
             const void* w[2] = {LT(m, l, L_GATE)->d, LT(m, l, L_UP)->d};
+            const CUtensorMap* wm[2] = {wmap(LT(m, l, L_GATE)), wmap(LT(m, l, L_UP))};
             const int64_t rows[2] = {hid, hid};
             float* y[2] = {m->pf_g, m->pf_u};
-            if ((rc = matmul_q4_0(s, err, 2, w, rows, c.dim, m->pf_h, n, y, rows, false))) return rc;
+            if ((rc = matmul_q4_0(s, err, 2, w, wm, rows, c.dim, m->pf_h, n, y, rows, false))) return rc;
         }
         if ((rc = prefill_silu(s, m->pf_g, m->pf_u, m->pf_h, (int64_t)n * hid))) return rc;
         {
             const void* w = LT(m, l, L_DOWN)->d;
+            const CUtensorMap* wm = wmap(LT(m, l, L_DOWN));
             const int64_t rows = c.dim;
-            if ((rc = matmul_q4_0(s, err, 1, &w, &rows, hid, m->pf_h, n, &m->pf_x, &rows, true))) return rc;
+            if ((rc = matmul_q4_0(s, err, 1, &w, &wm, &rows, hid, m->pf_h, n, &m->pf_x, &rows, true))) return rc;
         }
     }
     return CN_OK;
@@ -956,19 +963,22 @@ int cn_llama_time_matmul(cn_llama* m, int group, int n, int iters, float* us_per
             const int64_t rows[3] = {qd, kvd, kvd};
             float* y[3] = {m->pf_q, m->pf_k, m->pf_v};
             flops = 2.0 * n * (double)(qd + 2 * kvd) * dim;
-            return matmul_q4_0(s, m->ctx->dev_err, 3, w, rows, dim, m->pf_h, n, y, rows, false);
+            const CUtensorMap* wm[3] = {wmap(LT(m, l, L_Q)), wmap(LT(m, l, L_K)), wmap(LT(m, l, L_V))};
+            return matmul_q4_0(s, m->ctx->dev_err, 3, w, wm, rows, dim, m->pf_h, n, y, rows, false);
         }
         if (group == 2) {
             const void* w[2] = {LT(m, l, L_GATE)->d, LT(m, l, L_UP)->d};
             const int64_t rows[2] = {hid, hid};
             float* y[2] = {m->pf_g, m->pf_u};
             flops = 2.0 * n * (double)(2 * hid) * dim;
-            return matmul_q4_0(s, m->ctx->dev_err, 2, w, rows, dim, m->pf_h, n, y, rows, false);
+            const CUtensorMap* wm[2] = {wmap(LT(m, l, L_GATE)), wmap(LT(m, l, L_UP))};
+            return matmul_q4_0(s, m->ctx->dev_err, 2, w, wm, rows, dim, m->pf_h, n, y, rows, false);
         }
         const void* w = LT(m, l, group == 1 ? L_O : L_DOWN)->d;
+        const CUtensorMap* wm = wmap(LT(m, l, group == 1 ? L_O : L_DOWN));
         const int64_t rows = dim, K = group == 1 ? qd : hid;
         flops = 2.0 * n * (double)dim * K;
-        return matmul_q4_0(s, m->ctx->dev_err, 1, &w, &rows, K, m->pf_h, n, &m->pf_x, &rows, true);
+        return matmul_q4_0(s, m->ctx->dev_err, 1, &w, &wm, &rows, K, m->pf_h, n, &m->pf_x, &rows, true);
     };
     for (int i = 0; i < 3; i++)
         if ((rc = launch(i))) return rc;
