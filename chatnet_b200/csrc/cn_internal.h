@@ -94,12 +94,16 @@ int matmul_q4_0(cudaStream_t st, uint32_t* err, int nmat, const void* const* w, 
 int to_half(cudaStream_t st, const float* x, __half* y, int64_t n);
 
 // Prefill kernels around the matmul (prefill.cu).
-int prefill_positions(cudaStream_t st, int* pos_dev, int n, int pos0);  // pos_dev[i] = pos0 + i
 int prefill_norm(cudaStream_t st, const float* x, const float* w, __half* y, int n, int M, float eps);
 int prefill_silu(cudaStream_t st, const float* g, const float* u, __half* h, int64_t n);
+// RoPE of the M prompt tokens' q (in place) and k, k/v into the cache and
+// their fp16 copies into kh/vh [M][kvdim].
+int prefill_rope(cudaStream_t st, float* q, const float* k, const float* v, const float2* rope, int pos0, int M,
+                 int qdim, int kvdim, int hd, void* kcache, void* vcache, int64_t cache_off, bool kv_f16, __half* kh,
+                 __half* vh);
 int prefill_attention(cudaStream_t st, const float* q, int q_stride, const void* kcache,
                       const void* vcache, bool kv_f16, int64_t cache_off, int n_heads, int n_kv,
-                      int hd, int M, int pos0, __half* out, int out_stride);
+                      int hd, int M, int pos0, const __half* kh, const __half* vh, __half* out, int out_stride);
 
 // Scratch requirements of one GEMV call.
 struct GemvPlan {

@@ -67,12 +67,12 @@ struct cn_llama {
     bool use_graph = true;
     // prompt processing (prefill) scratch for up to pf_cap tokens, allocated
     // on first use: residual stream, q/k/v, gate/up (fp32), the fp16
-    // operand of the next matmul, token ids and positions
+    // operand of the next matmul, fp16 copies of the new k/v rows, token ids
     int pf_cap = 0;
     float *pf_x = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_g = nullptr,
           *pf_u = nullptr;
-    __half* pf_h = nullptr;
-    int *pf_tok = nullptr, *pf_pos = nullptr;
+    __half *pf_h = nullptr, *pf_kh = nullptr, *pf_vh = nullptr;
+    int* pf_tok = nullptr;
 };
 
 namespace cn {
@@ -426,7 +426,8 @@ static void free_model(cn_llama* m) {
     void* bufs[] = {m->kc, m->vc, m->rope, m->x, m->x2, m->attn_ctr, m->xn, m->q, m->k, m->v, m->att, m->tmp,
                     m->gate, m->up, m->logits, m->part, m->tokens, m->pos, m->amax,
                     m->gb.xfrag, m->gb.xsum, m->gb.partials, m->gb.counters, m->gb.xinv,
-                    m->pf_x, m->pf_q, m->pf_k, m->pf_v, m->pf_g, m->pf_u, m->pf_h, m->pf_tok, m->pf_pos};
+                    m->pf_x, m->pf_q, m->pf_k, m->pf_v, m->pf_g, m->pf_u, m->pf_h, m->pf_kh, m->pf_vh,
+                    m->pf_tok};
     for (void* p : bufs) cudaFree(p);
     cudaFreeHost(m->h_tokens);
     cudaFreeHost(m->h_pos);
@@ -455,11 +456,12 @@ static bool prefill_supported(const cn_llama* m) {
 static int prefill_reserve(cn_llama* m, int n) {
     if (n <= m->pf_cap) return CN_OK;
     CN_CUDA(cudaStreamSynchronize(m->ctx->stream));
-    void* old[] = {m->pf_x, m->pf_q, m->pf_k, m->pf_v, m->pf_g, m->pf_u, m->pf_h, m->pf_tok, m->pf_pos};
+    void* old[] = {m->pf_x, m->pf_q, m->pf_k, m->pf_v, m->pf_g, m->pf_u, m->pf_h, m->pf_kh, m->pf_vh,
+                   m->pf_tok};
     for (void* p : old) cudaFree(p);
     m->pf_x = m->pf_q = m->pf_k = m->pf_v = m->pf_g = m->pf_u = nullptr;
-    m->pf_h = nullptr;
-    m->pf_tok = m->pf_pos = nullptr;
+    m->pf_h = m->pf_kh = m->pf_vh = nullptr;
+    m->pf_tok = nullptr;
     m->pf_cap = 0;
     const cn_llama_config& c = m->cfg;
     const size_t N = (size_t)n;
@@ -472,7 +474,9 @@ static int prefill_reserve(cn_llama* m, int n) {
         (rc = dmalloc((void**)&m->pf_g, N * c.hidden_dim * 4, false)) ||
         (rc = dmalloc((void**)&m->pf_u, N * c.hidden_dim * 4, false)) ||
         (rc = dmalloc((void**)&m->pf_h, N * hmax * 2, false)) ||
-        (rc = dmalloc((void**)&m->pf_tok, N * 4, false)) || (rc = dmalloc((void**)&m->pf_pos, N * 4, false)))
+        (rc = dmalloc((void**)&m->pf_kh, N * m->kvdim * 2, false)) ||
+        (rc = dmalloc((void**)&m->pf_vh, N * m->kvdim * 2, false)) ||
+        (rc = dmalloc((void**)&m->pf_tok, N * 4, false)))
         return rc;
     m->pf_cap = n;
     return CN_OK;
@@ -491,7 +495,6 @@ static int prefill_layers(cn_llama* m, int n, int pos) {
     uint32_t* err = m->ctx->dev_err;
     const int qd = m->qdim, kvd = m->kvdim, hid = c.hidden_dim;
     int rc;
-    if ((rc = prefill_positions(s, m->pf_pos, n, pos))) return rc;
     for (int l = 0; l < c.n_layers; l++) {
         const int64_t cache_off = (int64_t)l * c.ctx_len * kvd;  // sequence slot 0
         if ((rc = prefill_norm(s, m->pf_x, (const float*)LT(m, l, L_ANORM)->d, m->pf_h, c.dim, n, c.rms_eps)))
@@ -503,29 +506,11 @@ static int prefill_layers(cn_llama* m, int n, int pos) {
             float* y[3] = {m->pf_q, m->pf_k, m->pf_v};
             if ((rc = matmul_q4_0(s, err, 3, w, wm, rows, c.dim, m->pf_h, n, y, rows, false))) return rc;
         }
-        RopeKvArgs ra;
-        ra.q = m->pf_q;
-        ra.k = m->pf_k;
-        ra.v = m->pf_v;
-        ra.rope = m->rope;
-        ra.pos_dev = m->pf_pos;
-        ra.pos_host = 0;
-        ra.batch = n;
-        ra.n_heads = m->nh;
-        ra.n_kv = m->nkv;
-        ra.hd = c.head_dim;
-        ra.q_stride = qd;
-        ra.kv_stride = kvd;
-        ra.kcache = m->kc;
-        ra.vcache = m->vc;
-        ra.cache_seq_stride = 0;  // every token belongs to sequence slot 0
-        ra.cache_layer_off = cache_off;
-        ra.kv_f16 = c.kv_dtype == CN_KV_F16;
-        ra.ctx_len = c.ctx_len;
-        ra.err = err;
-        if ((rc = launch_rope_kv(ra, s))) return rc;
+        if ((rc = prefill_rope(s, m->pf_q, m->pf_k, m->pf_v, m->rope, pos, n, qd, kvd, c.head_dim, m->kc, m->vc,
+                               cache_off, c.kv_dtype == CN_KV_F16, m->pf_kh, m->pf_vh)))
+            return rc;
         if ((rc = prefill_attention(s, m->pf_q, qd, m->kc, m->vc, c.kv_dtype == CN_KV_F16, cache_off, m->nh,
-                                    m->nkv, c.head_dim, n, pos, m->pf_h, qd)))
+                                    m->nkv, c.head_dim, n, pos, m->pf_kh, m->pf_vh, m->pf_h, qd)))
             return rc;
         {
             const void* w = LT(m, l, L_O)->d;
@@ -553,8 +538,8 @@ static int prefill_layers(cn_llama* m, int n, int pos) {
     return CN_OK;
 }
 
-// Kernels one prefill_layers call launches (positions, then 10 per layer).
-static int prefill_kernels(const cn_llama* m) { return 1 + 10 * m->cfg.n_layers; }
+// Kernels one prefill_layers call launches (10 per layer).
+static int prefill_kernels(const cn_llama* m) { return 10 * m->cfg.n_layers; }
 
 }  // namespace cn
 

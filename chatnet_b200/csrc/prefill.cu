@@ -41,67 +41,172 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
 
 }  // namespace
 
-// y[t] = fp16(RmsNorm(x[t]) * w), the reference's operation order.
+// y[t] = fp16(RmsNorm(x[t]) * w), the reference's operation order; n % 4 == 0.
 __global__ void norm_half_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                  __half* __restrict__ y, int n, float eps) {
     __shared__ float red[32];
-    const float* xr = x + (size_t)blockIdx.x * n;
-    __half* yr = y + (size_t)blockIdx.x * n;
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)blockIdx.x * n);
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    uint2* yr = reinterpret_cast<uint2*>(y + (size_t)blockIdx.x * n);
+    const int n4 = n / 4;
     float ss = 0.f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        const float4 v = xr[i];
+        ss = fmaf(v.x, v.x, ss);
+        ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss);
+        ss = fmaf(v.w, v.w, ss);
+    }
     ss = pf_warp_sum(ss);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
     float tot = 0.f;
     for (int i = 0; i < (int)(blockDim.x >> 5); i++) tot += red[i];
     const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), eps)));
-    for (int i = threadIdx.x; i < n; i += blockDim.x)
-        yr[i] = __float2half_rn(__fmul_rn(__fmul_rn(xr[i], rms), w[i]));
-}
-
-// h = fp16(g / (1 + exp(-g)) * u).
-__global__ void silu_half_kernel(const float* __restrict__ g, const float* __restrict__ u,
-                                 __half* __restrict__ h, int64_t n) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const float x = g[i];
-        const float s = __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
-        h[i] = __float2half_rn(__fmul_rn(s, u[i]));
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        const float4 v = xr[i], g = w4[i];
+        uint2 o;
+        o.x = pack_half2(__fmul_rn(__fmul_rn(v.x, rms), g.x), __fmul_rn(__fmul_rn(v.y, rms), g.y));
+        o.y = pack_half2(__fmul_rn(__fmul_rn(v.z, rms), g.z), __fmul_rn(__fmul_rn(v.w, rms), g.w));
+        yr[i] = o;
     }
 }
 
-__global__ void positions_kernel(int* __restrict__ pos, int n, int pos0) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) pos[i] = pos0 + i;
+__device__ __forceinline__ float silu_mul1(float g, float u) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
+// h = fp16(g / (1 + exp(-g)) * u), four values per thread; n % 4 == 0.
+__global__ void silu_half_kernel(const float* __restrict__ g, const float* __restrict__ u,
+                                 __half* __restrict__ h, int64_t n) {
+    const int64_t n4 = n / 4;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float4 a = reinterpret_cast<const float4*>(g)[i], b = reinterpret_cast<const float4*>(u)[i];
+        uint2 o;
+        o.x = pack_half2(silu_mul1(a.x, b.x), silu_mul1(a.y, b.y));
+        o.y = pack_half2(silu_mul1(a.z, b.z), silu_mul1(a.w, b.w));
+        reinterpret_cast<uint2*>(h)[i] = o;
+    }
+}
+
+// TensorMath.ApplyRoPE (interleaved pairs) on the q and k rows of the n prompt
+// tokens (token t at position pos0 + t), then k and v into the cache, with
+// rope_kv_kernel's arithmetic.  Also leaves fp16 copies of the new k and v
+// rows in kh/vh [n][kvdim] for the attention kernel.  One CTA per token, four
+// values per thread.
+__global__ void rope_prefill_kernel(float* __restrict__ q, const float* __restrict__ k,
+                                    const float* __restrict__ v, const float2* __restrict__ rope, int pos0,
+                                    int qdim, int kvdim, int hd, void* kcache, void* vcache, int64_t cache_off,
+                                    int kv_f16, __half* __restrict__ kh, __half* __restrict__ vh) {
+    const int t = blockIdx.x, pos = pos0 + t;
+    const float4* tab = reinterpret_cast<const float4*>(rope + (size_t)pos * (hd / 2));  // two pairs per float4
+    const int hd4 = hd / 4;
+    float4* q4 = reinterpret_cast<float4*>(q + (size_t)t * qdim);
+    const float4* k4 = reinterpret_cast<const float4*>(k + (size_t)t * kvdim);
+    const float4* v4 = reinterpret_cast<const float4*>(v + (size_t)t * kvdim);
+    const int64_t base = cache_off + (int64_t)pos * kvdim;
+    auto rot = [](float4 x, float4 cs) {
+        float4 r;
+        r.x = __fsub_rn(__fmul_rn(x.x, cs.x), __fmul_rn(x.y, cs.y));
+        r.y = __fadd_rn(__fmul_rn(x.x, cs.y), __fmul_rn(x.y, cs.x));
+        r.z = __fsub_rn(__fmul_rn(x.z, cs.z), __fmul_rn(x.w, cs.w));
+        r.w = __fadd_rn(__fmul_rn(x.z, cs.w), __fmul_rn(x.w, cs.z));
+        return r;
+    };
+    for (int i = threadIdx.x; i < qdim / 4; i += blockDim.x) q4[i] = rot(q4[i], tab[i % hd4]);
+    for (int i = threadIdx.x; i < kvdim / 4; i += blockDim.x) {
+        const float4 kr = rot(k4[i], tab[i % hd4]), vv = v4[i];
+        const uint2 kp = make_uint2(pack_half2(kr.x, kr.y), pack_half2(kr.z, kr.w));
+        const uint2 vp = make_uint2(pack_half2(vv.x, vv.y), pack_half2(vv.z, vv.w));
+        if (kv_f16) {
+            reinterpret_cast<uint2*>(reinterpret_cast<__half*>(kcache) + base)[i] = kp;
+            reinterpret_cast<uint2*>(reinterpret_cast<__half*>(vcache) + base)[i] = vp;
+        } else {
+            reinterpret_cast<float4*>(reinterpret_cast<float*>(kcache) + base)[i] = kr;
+            reinterpret_cast<float4*>(reinterpret_cast<float*>(vcache) + base)[i] = vv;
+        }
+        reinterpret_cast<uint2*>(kh + (size_t)t * kvdim)[i] = kp;
+        reinterpret_cast<uint2*>(vh + (size_t)t * kvdim)[i] = vp;
+    }
 }
 
 // Causal attention for M queries of one sequence.  CTA = (64-query block,
-// head); warp w owns queries 16w..16w+15 of the block.  Keys of the sequence
-// are read from the cache (fp32 or fp16) in blocks of 64 and converted to
-// fp16 in shared memory; query t (position pos0 + t) sees keys 0..pos0+t.
+// head), heaviest blocks first; warp w owns queries 16w..16w+15 of the block.
+// Keys come in blocks of 64, double-buffered: positions of this prompt
+// (>= pos0) from the fp16 copies kh/vh with cp.async, earlier positions from
+// the cache (fp32 or fp16, converted in registers).  Query t (position
+// pos0 + t) sees keys 0..pos0+t.
 constexpr int kPfQ = 64;   // queries per CTA
 constexpr int kPfK = 64;   // keys per block
 constexpr int kPfThreads = 128;
+
+__device__ __forceinline__ void pf_cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+template <int HD>
+__device__ __forceinline__ void pf_load_kv(__half* Ks, __half* Vs, int p0, int last, int pos0, int kh,
+                                           const void* kcache, const void* vcache, int kv_f16, int64_t cache_off,
+                                           int kvdim, const __half* kh16, const __half* vh16) {
+    constexpr int RS = HD + 8, C8 = HD / 8;
+    for (int i = threadIdx.x; i < kPfK * C8; i += kPfThreads) {
+        const int r = i / C8, c = i % C8;
+        const int p = p0 + r;
+        __half* kd = Ks + r * RS + 8 * c;
+        __half* vd = Vs + r * RS + 8 * c;
+        if (p > last) {
+            *reinterpret_cast<uint4*>(kd) = make_uint4(0u, 0u, 0u, 0u);
+            *reinterpret_cast<uint4*>(vd) = make_uint4(0u, 0u, 0u, 0u);
+        } else if (p >= pos0) {
+            const size_t e = (size_t)(p - pos0) * kvdim + kh * HD + 8 * c;
+            pf_cp_async16(smem_u32(kd), kh16 + e);
+            pf_cp_async16(smem_u32(vd), vh16 + e);
+        } else {
+            const int64_t e = cache_off + (int64_t)p * kvdim + kh * HD + 8 * c;
+#pragma unroll
+            for (int w = 0; w < 2; w++) {
+                const void* base = w == 0 ? kcache : vcache;
+                uint4 u;
+                if (kv_f16) {
+                    u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(base) + e);
+                } else {
+                    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + e);
+                    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + e + 4);
+                    u = make_uint4(pack_half2(a.x, a.y), pack_half2(a.z, a.w), pack_half2(b.x, b.y),
+                                   pack_half2(b.z, b.w));
+                }
+                *reinterpret_cast<uint4*>(w == 0 ? kd : vd) = u;
+            }
+        }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
 
 template <int HD>
 __global__ void __launch_bounds__(kPfThreads)
     attn_prefill_kernel(const float* __restrict__ q, int q_stride, const void* __restrict__ kcache,
                         const void* __restrict__ vcache, int kv_f16, int64_t cache_off, int kvdim,
                         int n_heads, int n_kv, int M, int pos0, float scale_log2,
+                        const __half* __restrict__ kh16, const __half* __restrict__ vh16,
                         __half* __restrict__ out, int out_stride) {
     constexpr int RS = HD + 8;  // halves per shared row (16-byte pad: conflict-free ldmatrix)
     constexpr int NT = HD / 8;  // 8-wide column tiles of the output
     constexpr int KS = HD / 16; // k-steps of Q K^T
     extern __shared__ __align__(16) uint8_t pf_smem[];
     __half* Qs = reinterpret_cast<__half*>(pf_smem);
-    __half* Ks = Qs + kPfQ * RS;
-    __half* Vs = Ks + kPfK * RS;
-    const int qb = blockIdx.x, h = blockIdx.y;
+    // K buffers at rows kPfQ + {0, kPfK}, V buffers at kPfQ + 2 kPfK + {0, kPfK}
+    auto Kb = [&](int i) { return Qs + (kPfQ + i * kPfK) * RS; };
+    auto Vb = [&](int i) { return Qs + (kPfQ + (2 + i) * kPfK) * RS; };
+    const int qb = gridDim.x - 1 - blockIdx.x, h = blockIdx.y;
     const int kh = h / (n_heads / n_kv);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t4 = lane & 3;
     const int t0 = qb * kPfQ;
+    const int last = pos0 + min(t0 + kPfQ, M) - 1;  // the block's last query position
+    const int nkb = last / kPfK + 1;
 
+    pf_load_kv<HD>(Kb(0), Vb(0), 0, last, pos0, kh, kcache, vcache, kv_f16, cache_off, kvdim, kh16, vh16);
     // queries -> fp16
     constexpr int C4 = HD / 4;
     for (int i = tid; i < kPfQ * C4; i += kPfThreads) {
@@ -127,34 +232,18 @@ __global__ void __launch_bounds__(kPfThreads)
     for (int j = 0; j < NT; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
     float mrow[2] = {-FLT_MAX, -FLT_MAX}, lrow[2] = {0.f, 0.f};
     const int qpos[2] = {pos0 + t0 + 16 * warp + g, pos0 + t0 + 16 * warp + g + 8};
-    const int last = pos0 + min(t0 + kPfQ, M) - 1;  // the block's last query position
-    const int nkb = last / kPfK + 1;
 
     for (int kb = 0; kb < nkb; kb++) {
         const int p0 = kb * kPfK;
-        __syncthreads();  // previous block's K/V no longer read
-        constexpr int C8 = HD / 8;
-        for (int i = tid; i < kPfK * C8; i += kPfThreads) {
-            const int r = i / C8, c = i % C8;
-            const int p = p0 + r;
-            uint4 kv[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
-            if (p <= last) {
-                const int64_t e = cache_off + (int64_t)p * kvdim + kh * HD + 8 * c;
-#pragma unroll
-                for (int w = 0; w < 2; w++) {
-                    const void* base = w == 0 ? kcache : vcache;
-                    if (kv_f16) {
-                        kv[w] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(base) + e);
-                    } else {
-                        const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + e);
-                        const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + e + 4);
-                        kv[w] = make_uint4(pack_half2(a.x, a.y), pack_half2(a.z, a.w), pack_half2(b.x, b.y),
-                                           pack_half2(b.z, b.w));
-                    }
-                }
-            }
-            *reinterpret_cast<uint4*>(Ks + r * RS + 8 * c) = kv[0];
-            *reinterpret_cast<uint4*>(Vs + r * RS + 8 * c) = kv[1];
+        __half* Ks = Kb(kb & 1);
+        __half* Vs = Vb(kb & 1);
+        if (kb + 1 < nkb) {
+            // the other buffer was last read in block kb - 1 (barrier at its end)
+            pf_load_kv<HD>(Kb((kb + 1) & 1), Vb((kb + 1) & 1), p0 + kPfK, last, pos0, kh, kcache, vcache, kv_f16,
+                           cache_off, kvdim, kh16, vh16);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         __syncthreads();
 
@@ -234,6 +323,7 @@ __global__ void __launch_bounds__(kPfThreads)
                 mma_16816(o[2 * jp + 1], a, b1, o[2 * jp + 1]);
             }
         }
+        __syncthreads();  // this block's K/V no longer read: its buffer may be refilled
     }
 
     // normalise and store
@@ -257,11 +347,6 @@ __global__ void __launch_bounds__(kPfThreads)
 
 // ---- host side ------------------------------------------------------------------
 
-int prefill_positions(cudaStream_t st, int* pos_dev, int n, int pos0) {
-    CN_CUDA(launch_k(false, positions_kernel, dim3((n + 255) / 256), dim3(256), 0, st, pos_dev, n, pos0));
-    return CN_OK;
-}
-
 int prefill_norm(cudaStream_t st, const float* x, const float* w, __half* y, int n, int M, float eps) {
     CN_CUDA(launch_k(false, norm_half_kernel, dim3(M), dim3(256), 0, st, x, w, y, n, eps));
     return CN_OK;
@@ -273,15 +358,24 @@ int prefill_silu(cudaStream_t st, const float* g, const float* u, __half* h, int
     return CN_OK;
 }
 
+int prefill_rope(cudaStream_t st, float* q, const float* k, const float* v, const float2* rope, int pos0, int M,
+                 int qdim, int kvdim, int hd, void* kcache, void* vcache, int64_t cache_off, bool kv_f16, __half* kh,
+                 __half* vh) {
+    CN_CHECK(hd % 4 == 0 && qdim % 4 == 0 && kvdim % 4 == 0, CN_ERR_INVALID_ARG, "prefill rope: shapes");
+    CN_CUDA(launch_k(false, rope_prefill_kernel, dim3(M), dim3(256), 0, st, q, k, v, rope, pos0, qdim, kvdim, hd,
+                     kcache, vcache, cache_off, kv_f16 ? 1 : 0, kh, vh));
+    return CN_OK;
+}
+
 int prefill_attention(cudaStream_t st, const float* q, int q_stride, const void* kcache,
                       const void* vcache, bool kv_f16, int64_t cache_off, int n_heads, int n_kv,
-                      int hd, int M, int pos0, __half* out, int out_stride) {
+                      int hd, int M, int pos0, const __half* kh, const __half* vh, __half* out, int out_stride) {
     CN_CHECK(hd == 64 || hd == 128, CN_ERR_UNSUPPORTED, "prefill attention: head_dim %d", hd);
     CN_CHECK(n_kv > 0 && n_heads % n_kv == 0 && M >= 1 && pos0 >= 0, CN_ERR_INVALID_ARG,
              "prefill attention: bad arguments");
     CN_CHECK(q_stride % 4 == 0 && out_stride % 2 == 0, CN_ERR_INVALID_ARG, "prefill attention: strides");
     const int RS = hd + 8;
-    const size_t smem = (size_t)(kPfQ + 2 * kPfK) * RS * sizeof(__half);
+    const size_t smem = (size_t)(kPfQ + 4 * kPfK) * RS * sizeof(__half);
     const float scale_log2 = 1.4426950408889634f / sqrtf((float)hd);
     const dim3 grid((M + kPfQ - 1) / kPfQ, n_heads);
     const int kvdim = n_kv * hd;
@@ -294,11 +388,17 @@ int prefill_attention(cudaStream_t st, const float* q, int q_stride, const void*
         }
         CN_CUDA(launch_k(false, attn_prefill_kernel<128>, grid, dim3(kPfThreads), smem, st, q, q_stride,
                          kcache, vcache, kv_f16 ? 1 : 0, cache_off, kvdim, n_heads, n_kv, M, pos0,
-                         scale_log2, out, out_stride));
+                         scale_log2, kh, vh, out, out_stride));
     } else {
+        static bool attr64 = false;
+        if (!attr64) {
+            CN_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<64>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            attr64 = true;
+        }
         CN_CUDA(launch_k(false, attn_prefill_kernel<64>, grid, dim3(kPfThreads), smem, st, q, q_stride,
                          kcache, vcache, kv_f16 ? 1 : 0, cache_off, kvdim, n_heads, n_kv, M, pos0,
-                         scale_log2, out, out_stride));
+                         scale_log2, kh, vh, out, out_stride));
     }
     return CN_OK;
 }
