@@ -6,26 +6,35 @@
 // weights of DequantQ4_0.Dequantize (Tensors/Quantization/DequantQ4_0.cs:28-58),
 // which ChatNet runs as M sequential matvecs (InferenceEngine.cs:235-239).
 //
-//  * A tile is 128 weight rows x 256 tokens.  The weights are the MMA's A
-//    operand and live in tensor memory: eight decode warps in two
-//    warpgroups (one weight row per thread, the thread's lane of tensor
-//    memory; warpgroup g takes block g of the two Q4_0 blocks of every
-//    64-position stage) read the row's raw blocks from a shared-memory ring
-//    that TMA fills with 128 rows x 144 bytes (8 blocks, 4 stages) at a time,
-//    expand their block to 32 fp16 values ((q - 8) exact, times d, one
-//    rounding) and write them to tensor memory with tcgen05.st.  The
+//  * A tile is 128 weight rows x 128 tokens.  The kernel is persistent: one
+//    CTA per SM walks the tiles (weight row tile-major, so the CTAs running
+//    at the same time share weight tiles in L2), and its accumulator in
+//    tensor memory is double-buffered, so the epilogue of one tile overlaps
+//    the MMAs of the next.
+//  * The weights are the MMA's A operand and live in tensor memory: eight
+//    decode warps in two warpgroups (one weight row per thread, the thread's
+//    lane of tensor memory; warpgroup g takes blocks 2g and 2g + 1 of the
+//    four Q4_0 blocks of every 128-position stage) read the row's raw blocks
+//    from a shared-memory ring that TMA fills with 128 rows x 144 bytes (8
+//    blocks, 2 stages) at a time, expand them to fp16 ((q - 8) exact, times
+//    d, one rounding) and write them to tensor memory with tcgen05.st.  The
 //    expanded weights never touch shared memory.
-//  * The activations (fp16, K-major) are the B operand: TMA tiles of 256
-//    tokens x 64 positions with 128-byte swizzle in a 5-stage ring.
-//  * One thread issues tcgen05.mma kind::f16 (M=128, N=256, K=16; fp32
-//    accumulator in tensor-memory columns 0-255), four per 64-position stage,
-//    and commits each stage to the barrier that frees its A slot and B stage.
-//  * The decode warps then read the accumulator back (tcgen05.ld, one weight
-//    row per thread, 32 tokens per load; warpgroup g takes tokens
-//    128g..128g+127) and store Y with coalesced rows, optionally adding into
-//    Y (the residual stream).
+//  * The activations (fp16, K-major) are the B operand: per stage two TMA
+//    tiles of 128 tokens x 64 positions with 128-byte swizzle, in a 4-stage
+//    ring.
+//  * One thread issues tcgen05.mma kind::f16 (M=128, N=128, K=16; fp32
+//    accumulator in tensor-memory columns [0, 128) or [128, 256)), eight per
+//    stage, and commits each stage to the barrier that frees its A slot and
+//    B stage, and each tile to the barrier that hands its accumulator on.
+//    The decode warps and the TMA producer signal one barrier per stage (one
+//    arrival per warp), so the issuing thread waits once per eight MMAs: its
+//    barrier wait costs about as long as two N = 128 MMAs take, and the
+//    test of the next stage's barrier is issued before this stage's MMAs.
+//  * Four epilogue warps read the accumulator back (tcgen05.ld, one weight
+//    row per thread, 32 tokens per load), release it, and store Y with
+//    coalesced rows (optionally adding into Y, the residual stream).
 //  * Up to three weight matrices with the same K share one launch (q/k/v,
-//    gate/up): grid.x runs over their row tiles, grid.y over token tiles.
+//    gate/up): the tiles run over their row tiles.
 // Every mbarrier wait is bounded.  A thread that gives up raises the error
 // word and stops waiting (its control flow stays uniform; results are
 // garbage and flagged).  The CTA still waits for its own copies and MMAs
@@ -37,21 +46,25 @@ namespace cn {
 namespace mm {
 
 constexpr int kRows = 128;               // weight rows per tile (MMA M, tensor-memory lanes)
-constexpr int kNT = 256;                 // tokens per tile (MMA N)
-constexpr int kKS = 64;                  // K positions per stage (one 128-byte swizzle row)
-constexpr int kStages = 5;
-constexpr int kBStage = kNT * kKS * 2;   // 32 KB of activations per stage
-constexpr int kRaw = 144 * kRows;        // raw Q4_0 bytes of 8 blocks x 128 rows (4 stages)
-constexpr int kRawStages = 3;
+constexpr int kNT = 128;                 // tokens per tile (MMA N)
+constexpr int kKS = 128;                 // K positions per stage (two 128-byte swizzle rows)
+constexpr int kStages = 4;
+constexpr int kBHalf = kNT * 64 * 2;     // 16 KB: one swizzled tile of 64 positions
+constexpr int kBStage = 2 * kBHalf;      // 32 KB of activations per stage
+constexpr int kRaw = 144 * kRows;        // raw Q4_0 bytes of 8 blocks x 128 rows (2 stages)
+constexpr int kRawStages = 5;
+constexpr int kDBufs = 2;                // accumulator buffers
 constexpr int kRawOff = kStages * kBStage;
 constexpr int kACols = kKS / 2;          // tensor-memory columns of one A stage (2 fp16 each)
-constexpr int kACol = kNT;               // accumulator in columns [0, 256), A ring after it
+constexpr int kACol = kDBufs * kNT;      // accumulator(s) first, the A ring after them
 constexpr int kTmemCols = 512;
-constexpr int kDecode = 256;             // decode + epilogue threads: warps 0-7
-constexpr int kThreads = kDecode + 64;   // warp 8 TMA, warp 9 MMA
-constexpr int kWarpTma = 8, kWarpMma = 9;
+constexpr int kDecode = 256;             // decode threads: warps 0-7
+constexpr int kEpi = 128;                // epilogue threads: warps 8-11
+constexpr int kDecodeWarps = kDecode / 32, kEpiWarps = kEpi / 32;  // barrier arrivals (one per warp)
+constexpr int kThreads = kDecode + kEpi + 64;  // warp 12 TMA, warp 13 MMA
+constexpr int kWarpEpi0 = 8, kWarpTma = 12, kWarpMma = 13;
 constexpr int kBarOff = kRawOff + kRawStages * kRaw;
-constexpr int kSmem = kBarOff + 256 + 1024;  // barriers, and slack to align the ring to 1 KB
+constexpr int kSmem = kBarOff + 512 + 1024;  // barriers, and slack to align the ring to 1 KB
 constexpr int kMaxMats = 3;
 static_assert(kACol + kStages * kACols <= kTmemCols, "tensor memory plan");
 static_assert(kRawOff % 1024 == 0 && kRaw % 128 == 0 && kBarOff % 8 == 0, "ring alignment");
@@ -78,6 +91,8 @@ struct Args {
     int64_t rb;                 // bytes per weight row (K / 32 * 18)
     int M, K;                   // K % 256 == 0
     int accumulate;             // 1: Y += result, 0: Y = result
+    int tok_tiles;              // token tiles of 128; tile t = row tile t / tok_tiles, token tile t % tok_tiles
+    int tiles;                  // row tiles x token tiles
     uint32_t* err;
 };
 
@@ -92,49 +107,52 @@ __device__ __forceinline__ uint32_t h2_mul(uint32_t a, uint32_t b) {
     return r;
 }
 
-// Expands one Q4_0 block into 32 fp16 weights in K order, two per word: o[c]
-// holds positions 2c (low half) and 2c + 1.  wd holds the five 4-byte words
-// the block touches in a pair of blocks (36 bytes, 4-byte aligned): for
-// BLK 0 bytes 0-19 (d at 0-1, quants at 2-17), for BLK 1 bytes 16-35 (d at
-// 18-19, quants at 20-35).  Position j < 16 of a block is the low nibble of
-// quant byte j, position 16 + j its high nibble; the value is
-// fp16((q - 8) * d).
-template <int BLK>
-__device__ __forceinline__ void expand_q4_0(const uint32_t (&wd)[5], uint32_t (&o)[16]) {
+// Expands two consecutive Q4_0 blocks, the 36 bytes wd[0..8] (block 0: d
+// at bytes 0-1, quants at 2-17; block 1: d at 18-19, quants at 20-35), into
+// 64 fp16 weights in K order, two per word: o[c] holds positions 2c (low
+// half) and 2c + 1.  Position j < 16 of a block is the low nibble of quant
+// byte j, position 16 + j its high nibble; the value is fp16((q - 8) * d).
+__device__ __forceinline__ void expand_q4_0_pair(const uint32_t (&wd)[9], uint32_t (&o)[32]) {
     constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024 in both halves
     constexpr uint32_t kBias = 0x64086408u;   // fp16 1032 = 1024 + 8
-    uint32_t q[4], d;
-    if (BLK == 0) {
-        d = wd[0] & 0xFFFFu;
 #pragma unroll
-        for (int i = 0; i < 4; i++) q[i] = __funnelshift_r(wd[i], wd[i + 1], 16);
-    } else {
-        d = wd[0] >> 16;
+    for (int blk = 0; blk < 2; blk++) {
+        uint32_t q[4], d;
+        if (blk == 0) {
+            d = wd[0] & 0xFFFFu;
 #pragma unroll
-        for (int i = 0; i < 4; i++) q[i] = wd[1 + i];
-    }
-    const uint32_t d2 = d | (d << 16);
+            for (int i = 0; i < 4; i++) q[i] = __funnelshift_r(wd[i], wd[i + 1], 16);
+        } else {
+            d = wd[4] >> 16;
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
+            for (int i = 0; i < 4; i++) q[i] = wd[5 + i];
+        }
+        const uint32_t d2 = d | (d << 16);
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-            // quant bytes 4i + 2h and 4i + 2h + 1 in the low byte of each half
-            const uint32_t t = __byte_perm(q[i], 0u, h ? 0x4342u : 0x4140u);
-            const uint32_t lo = lop3_and_or(t, 0x000F000Fu, kMagic);       // 1024 + q
-            const uint32_t hi = lop3_and_or(t >> 4, 0x000F000Fu, kMagic);
-            o[2 * i + h] = h2_mul(h2_sub(lo, kBias), d2);                  // (q - 8) exact, then * d
-            o[8 + 2 * i + h] = h2_mul(h2_sub(hi, kBias), d2);
+        for (int i = 0; i < 4; i++) {
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                // quant bytes 4i + 2h and 4i + 2h + 1 in the low byte of each half
+                const uint32_t t = __byte_perm(q[i], 0u, h ? 0x4342u : 0x4140u);
+                const uint32_t lo = lop3_and_or(t, 0x000F000Fu, kMagic);       // 1024 + q
+                const uint32_t hi = lop3_and_or(t >> 4, 0x000F000Fu, kMagic);
+                o[16 * blk + 2 * i + h] = h2_mul(h2_sub(lo, kBias), d2);      // (q - 8) exact, then * d
+                o[16 * blk + 8 + 2 * i + h] = h2_mul(h2_sub(hi, kBias), d2);
+            }
         }
     }
 }
 
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
     asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-        "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+        "%28, %29, %30, %31, %32};" ::"r"(taddr),
         "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
         "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
-        "r"(v[15])
+        "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
+        "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
+        "r"(v[29]), "r"(v[30]), "r"(v[31])
         : "memory");
 }
 
@@ -171,6 +189,19 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint32_t a_tmem, uint64
         : "memory");
 }
 
+// Non-blocking test of a barrier phase (1 once the phase with this parity completed).
+__device__ __forceinline__ uint32_t mbar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done;
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile(
         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -195,32 +226,38 @@ __global__ void __launch_bounds__(mm::kThreads, 1)
     using namespace mm;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    uint64_t* full_b = reinterpret_cast<uint64_t*>(smem + kBarOff);
-    uint64_t* full_a = full_b + kStages;
-    uint64_t* empty = full_a + kStages;
-    uint64_t* dfull = empty + kStages;
-    uint64_t* raw_full = dfull + 1;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBarOff);  // A slot written and B stage landed
+    uint64_t* empty = full + kStages;
+    uint64_t* raw_full = empty + kStages;
     uint64_t* raw_empty = raw_full + kRawStages;
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(raw_empty + kRawStages);
+    uint64_t* dfull = raw_empty + kRawStages;  // [kDBufs] accumulator written
+    uint64_t* dempty = dfull + kDBufs;         // [kDBufs] accumulator read back
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(dempty + kDBufs);
     const uint8_t* raw = smem + kRawOff;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tile = blockIdx.x;
-    const int m = a.nmat > 2 && tile >= a.toff[2] ? 2 : (a.nmat > 1 && tile >= a.toff[1] ? 1 : 0);
-    const int64_t row0 = (int64_t)(tile - (m == 2 ? a.toff[2] : m == 1 ? a.toff[1] : 0)) * kRows;
-    const int tok0 = blockIdx.y * kNT;
-    const int nst = a.K / kKS;
+    const int nst = a.K / kKS;     // stages per tile
+    const int nch = nst / 2;       // raw runs per tile
+    // the tiles of this CTA: blockIdx.x, + gridDim.x, ...
+    auto tile_mat = [&](int t, int& m, int64_t& row0, int& tok0) {
+        const int rt = t / a.tok_tiles;
+        m = a.nmat > 2 && rt >= a.toff[2] ? 2 : (a.nmat > 1 && rt >= a.toff[1] ? 1 : 0);
+        row0 = (int64_t)(rt - (m == 2 ? a.toff[2] : m == 1 ? a.toff[1] : 0)) * kRows;
+        tok0 = (t % a.tok_tiles) * kNT;
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) {
-            mbar_init(&full_b[s], 1);
-            mbar_init(&full_a[s], kDecode);
+            mbar_init(&full[s], kDecodeWarps + 1);  // the decode warps and the producer's expect_tx
             mbar_init(&empty[s], 1);
         }
-        mbar_init(dfull, 1);
         for (int s = 0; s < kRawStages; s++) {
             mbar_init(&raw_full[s], 1);
-            mbar_init(&raw_empty[s], kDecode);
+            mbar_init(&raw_empty[s], kDecodeWarps);
+        }
+        for (int d = 0; d < kDBufs; d++) {
+            mbar_init(&dfull[d], 1);
+            mbar_init(&dempty[d], kEpiWarps);
         }
         fence_mbar_init();
     }
@@ -239,146 +276,178 @@ __global__ void __launch_bounds__(mm::kThreads, 1)
     if (warp == kWarpTma) {
         // ---- producer (TMA): raw weight runs and activation stages ----
         if (lane == 0) {
-            const CUtensorMap* wmap = m == 2 ? &maps.w[2] : m == 1 ? &maps.w[1] : &maps.w[0];
-            const int nch = nst / 4;
-            // the weights depend on no earlier kernel: the first runs go out
-            // before the wait for the activations
-            const int pre = nch < kRawStages ? nch : kRawStages;
-            for (int c = 0; c < pre; c++) {
-                mbar_expect_tx(&raw_full[c], kRaw);
-                tma_load_2d(smem + kRawOff + c * kRaw, wmap, 18 * c, (int)row0, &raw_full[c]);
-            }
             pdl_wait();  // X is the previous kernel's output
-            int issued = 0, raw_issued = pre;
-            for (int s = 0; s < nst; s++) {
-                const int c = s / 4;
-                if ((s & 3) == 0 && c >= kRawStages) {
-                    // run c reuses the slot of run c - kRawStages once every decode thread left it
-                    const int rs = c % kRawStages;
-                    if (!mbar_wait(&raw_empty[rs], (uint32_t)((c / kRawStages) - 1) & 1)) {
+            int gs = 0, gc = 0;  // stages and runs issued so far (over all tiles)
+            bool ok = true;
+            for (int t = blockIdx.x; t < a.tiles && ok; t += gridDim.x) {
+                int m, tok0;
+                int64_t row0;
+                tile_mat(t, m, row0, tok0);
+                const CUtensorMap* wmap = m == 2 ? &maps.w[2] : m == 1 ? &maps.w[1] : &maps.w[0];
+                for (int s = 0; s < nst; s++) {
+                    if ((s & 1) == 0) {
+                        const int rs = gc % kRawStages;
+                        if (gc >= kRawStages && !mbar_wait(&raw_empty[rs], (uint32_t)((gc / kRawStages) - 1) & 1)) {
+                            atomicOr(a.err, kErrTimeout);
+                            ok = false;
+                            break;
+                        }
+                        mbar_expect_tx(&raw_full[rs], kRaw);
+                        tma_load_2d(smem + kRawOff + rs * kRaw, wmap, 18 * (s / 2), (int)row0, &raw_full[rs]);
+                        gc++;
+                    }
+                    const int slot = gs % kStages;
+                    if (gs >= kStages && !mbar_wait(&empty[slot], (uint32_t)((gs / kStages) - 1) & 1)) {
                         atomicOr(a.err, kErrTimeout);
+                        ok = false;
                         break;
                     }
-                    mbar_expect_tx(&raw_full[rs], kRaw);
-                    tma_load_2d(smem + kRawOff + rs * kRaw, wmap, 18 * c, (int)row0, &raw_full[rs]);
-                    raw_issued = c + 1;
+                    mbar_expect_tx(&full[slot], kBStage);
+                    tma_load_2d(smem + slot * kBStage, &maps.x, s * kKS, tok0, &full[slot]);
+                    tma_load_2d(smem + slot * kBStage + kBHalf, &maps.x, s * kKS + 64, tok0, &full[slot]);
+                    gs++;
                 }
-                const int slot = s % kStages;
-                if (s >= kStages && !mbar_wait(&empty[slot], (uint32_t)((s / kStages) - 1) & 1)) {
-                    atomicOr(a.err, kErrTimeout);
-                    break;
-                }
-                mbar_expect_tx(&full_b[slot], kBStage);
-                tma_load_2d(smem + slot * kBStage, &maps.x, s * kKS, tok0, &full_b[slot]);
-                issued = s + 1;
             }
             // no copy may still be landing when the CTA exits
-            for (int s = issued - kStages < 0 ? 0 : issued - kStages; s < issued; s++)
-                mbar_wait(&full_b[s % kStages], (uint32_t)(s / kStages) & 1);
-            for (int c = raw_issued - kRawStages < 0 ? 0 : raw_issued - kRawStages; c < raw_issued; c++)
-                mbar_wait(&raw_full[c % kRawStages], (uint32_t)(c / kRawStages) & 1);
+            for (int i = gs - kStages < 0 ? 0 : gs - kStages; i < gs; i++)
+                mbar_wait(&full[i % kStages], (uint32_t)(i / kStages) & 1);
+            for (int i = gc - kRawStages < 0 ? 0 : gc - kRawStages; i < gc; i++)
+                mbar_wait(&raw_full[i % kRawStages], (uint32_t)(i / kRawStages) & 1);
         }
     } else if (warp == kWarpMma) {
         // ---- MMA issuer ----
         if (lane == 0) {
-            for (int s = 0; s < nst; s++) {
-                const int slot = s % kStages;
-                const uint32_t ph = (uint32_t)(s / kStages) & 1;
-                if (!mbar_wait(&full_b[slot], ph) || !mbar_wait(&full_a[slot], ph)) {
+            int gs = 0, i = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < a.tiles && ok; t += gridDim.x, i++) {
+                const int db = i % kDBufs;
+                if (i >= kDBufs && !mbar_wait(&dempty[db], (uint32_t)((i / kDBufs) - 1) & 1)) {
                     atomicOr(a.err, kErrTimeout);
                     break;
                 }
                 tc_fence_after();
-                const uint32_t b0 = smem_u32(smem + slot * kBStage);
+                const uint32_t d_tmem = tmem + db * kNT;
+                // the test of a stage's barrier is issued before the previous
+                // stage's MMAs, so its latency hides behind their issue
+                uint32_t ready = mbar_test(&full[gs % kStages], (uint32_t)(gs / kStages) & 1);
+                for (int s = 0; s < nst; s++, gs++) {
+                    const int slot = gs % kStages;
+                    const uint32_t ph = (uint32_t)(gs / kStages) & 1;
+                    if (!ready && !mbar_wait(&full[slot], ph)) {
+                        atomicOr(a.err, kErrTimeout);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const int ns = gs + 1;
+                    ready = s + 1 < nst ? mbar_test(&full[ns % kStages], (uint32_t)(ns / kStages) & 1) : 0u;
+                    const uint32_t b0 = smem_u32(smem + slot * kBStage);
 #pragma unroll
-                for (int kk = 0; kk < kKS / 16; kk++)
-                    mma_f16(tmem, tmem + kACol + slot * kACols + 8 * kk, desc_sw128(b0 + 32 * kk),
-                            (s | kk) != 0);
-                mma_commit(&empty[slot]);
+                    for (int kk = 0; kk < kKS / 16; kk++)
+                        mma_f16(d_tmem, tmem + kACol + slot * kACols + 8 * kk,
+                                desc_sw128(b0 + (kk / 4) * kBHalf + 32 * (kk % 4)), (s | kk) != 0);
+                    mma_commit(&empty[slot]);
+                }
+                mma_commit(&dfull[db]);  // completes once every MMA issued above has
             }
-            mma_commit(dfull);  // completes once every MMA issued above has
         }
-    } else {
-        // ---- weight decode into tensor memory, then the epilogue ----
-        const int r = threadIdx.x & (kRows - 1);  // tile row == tensor-memory lane
-        const int wg = threadIdx.x >> 7;          // which block of each stage, which token half
-        const int64_t row = row0 + r;
-        const int64_t nrows = pick(a.rows, m);
-        const bool live = row < nrows;  // rows past the matrix arrive as zeros (TMA fill)
-        const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-        const int nch = nst / 4;  // 144-byte runs of 8 blocks (256 positions, 4 stages)
+    } else if (warp >= kWarpEpi0) {
+        // ---- epilogue: accumulator row r, 32 tokens per tensor-memory load ----
+        const int r = threadIdx.x & (kRows - 1);
+        const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
         bool failed = false;
-        for (int c = 0; c < nch; c++) {
-            const int rs = c % kRawStages;
-            if (!failed && !mbar_wait(&raw_full[rs], (uint32_t)(c / kRawStages) & 1)) {
+        pdl_wait();  // Y may be the previous kernel's data
+        int i = 0;
+        for (int t = blockIdx.x; t < a.tiles; t += gridDim.x, i++) {
+            int m, tok0;
+            int64_t row0;
+            tile_mat(t, m, row0, tok0);
+            const int db = i % kDBufs;
+            if (!failed && !mbar_wait(&dfull[db], (uint32_t)(i / kDBufs) & 1)) {
                 atomicOr(a.err, kErrTimeout);
                 failed = true;
             }
-            // this thread's words of its row: block wg of stage q = words
-            // 9q + 4wg .. 9q + 4wg + 4 of the row's 36
-            const uint32_t* src = reinterpret_cast<const uint32_t*>(raw + rs * kRaw + r * 144) + 4 * wg;
-            uint32_t cur[20];
+            tc_fence_after();
+            const int64_t row = row0 + r;
+            const bool live = row < pick(a.rows, m);
+            float* y = pick(a.y, m);
+            const int64_t ldy = pick(a.ldy, m);
+#pragma unroll 1
+            for (int j = 0; j < kNT / 32; j++) {
+                uint32_t v[32];
+                tmem_ld32(tmem + lane_off + db * kNT + 32 * j, v);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (j == kNT / 32 - 1) {
+                    // the accumulator is read (the warp-wide wait covers every
+                    // lane's load): hand it back to the MMA issuer
+                    tc_fence_before();
+                    if (lane == 0) mbar_arrive(&dempty[db]);
+                }
+                if (live) {
+                    float* p = y + (size_t)(tok0 + 32 * j) * ldy + row;
+                    const int nt = a.M - (tok0 + 32 * j);  // tokens of this chunk inside M
+                    if (a.accumulate) {
+                        // 16 loads in flight before the first store
 #pragma unroll
-            for (int q = 0; q < 4; q++)
+                        for (int h = 0; h < 2; h++) {
+                            float old[16];
 #pragma unroll
-                for (int k = 0; k < 5; k++) cur[5 * q + k] = src[9 * q + k];
-            mbar_arrive(&raw_empty[rs]);
+                            for (int u = 0; u < 16; u++) old[u] = 16 * h + u < nt ? p[(size_t)(16 * h + u) * ldy] : 0.f;
 #pragma unroll
-            for (int q = 0; q < 4; q++) {
-                const int s = 4 * c + q, slot = s % kStages;
-                if (s >= kStages && !failed &&
-                    !mbar_wait(&empty[slot], (uint32_t)((s / kStages) - 1) & 1)) {
+                            for (int u = 0; u < 16; u++)
+                                if (16 * h + u < nt) p[(size_t)(16 * h + u) * ldy] = old[u] + __uint_as_float(v[16 * h + u]);
+                        }
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < 32; u++)
+                            if (u < nt) p[(size_t)u * ldy] = __uint_as_float(v[u]);
+                    }
+                }
+            }
+        }
+    } else {
+        // ---- weight decode into tensor memory ----
+        const int r = threadIdx.x & (kRows - 1);  // tile row == tensor-memory lane
+        const int wg = threadIdx.x >> 7;          // blocks 2wg, 2wg + 1 of each stage
+        const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        bool failed = false;
+        int gs = 0, gc = 0;
+        for (int t = blockIdx.x; t < a.tiles; t += gridDim.x) {
+            for (int c = 0; c < nch; c++, gc++) {
+                const int rs = gc % kRawStages;
+                if (!failed && !mbar_wait(&raw_full[rs], (uint32_t)(gc / kRawStages) & 1)) {
                     atomicOr(a.err, kErrTimeout);
                     failed = true;
                 }
-                tc_fence_after();
-                uint32_t wd[5], o[16];
+                // this thread's words of its row (rows past the matrix arrive as
+                // zeros): blocks 4q + 2wg, 4q + 2wg + 1 of stage q = words
+                // 18q + 9wg .. 18q + 9wg + 8 of the row's 36
+                const uint32_t* src = reinterpret_cast<const uint32_t*>(raw + rs * kRaw + r * 144) + 9 * wg;
+                uint32_t cur[18];
 #pragma unroll
-                for (int k = 0; k < 5; k++) wd[k] = cur[5 * q + k];
-                if (wg == 0)
-                    expand_q4_0<0>(wd, o);
-                else
-                    expand_q4_0<1>(wd, o);
-                tmem_st16(lane_base + kACol + slot * kACols + 16 * wg, o);
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                tc_fence_before();
-                mbar_arrive(&full_a[slot]);
-            }
-        }
-
-        // epilogue: accumulator row r, 32 tokens per tensor-memory load
-        if (!failed && !mbar_wait(dfull, 0)) {
-            atomicOr(a.err, kErrTimeout);
-            failed = true;
-        }
-        tc_fence_after();
-        pdl_wait();  // Y may be the previous kernel's data
-        float* y = pick(a.y, m);
-        const int64_t ldy = pick(a.ldy, m);
-#pragma unroll 1
-        for (int jj = 0; jj < kNT / 64; jj++) {
-            const int j = (kNT / 64) * wg + jj;  // this warpgroup's half of the tokens
-            uint32_t v[32];
-            tmem_ld32(lane_base + 32 * j, v);
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            if (live) {
-                float* p = y + (size_t)(tok0 + 32 * j) * ldy + row;
-                const int nt = a.M - (tok0 + 32 * j);  // tokens of this chunk inside M
-                if (a.accumulate) {
-                    // 16 loads in flight before the first store
+                for (int q = 0; q < 2; q++)
 #pragma unroll
-                    for (int h = 0; h < 2; h++) {
-                        float old[16];
+                    for (int k = 0; k < 9; k++) cur[9 * q + k] = src[18 * q + k];
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&raw_empty[rs]);
 #pragma unroll
-                        for (int t = 0; t < 16; t++) old[t] = 16 * h + t < nt ? p[(size_t)(16 * h + t) * ldy] : 0.f;
-#pragma unroll
-                        for (int t = 0; t < 16; t++)
-                            if (16 * h + t < nt) p[(size_t)(16 * h + t) * ldy] = old[t] + __uint_as_float(v[16 * h + t]);
+                for (int q = 0; q < 2; q++, gs++) {
+                    const int slot = gs % kStages;
+                    if (gs >= kStages && !failed &&
+                        !mbar_wait(&empty[slot], (uint32_t)((gs / kStages) - 1) & 1)) {
+                        atomicOr(a.err, kErrTimeout);
+                        failed = true;
                     }
-                } else {
+                    tc_fence_after();
+                    uint32_t wd[9], o[32];
 #pragma unroll
-                    for (int t = 0; t < 32; t++)
-                        if (t < nt) p[(size_t)t * ldy] = __uint_as_float(v[t]);
+                    for (int k = 0; k < 9; k++) wd[k] = cur[9 * q + k];
+                    expand_q4_0_pair(wd, o);
+                    tmem_st32(lane_base + kACol + slot * kACols + 32 * wg, o);
+                    // warp-wide: every lane's stores of this stage are done
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    tc_fence_before();
+                    if (lane == 0) mbar_arrive(&full[slot]);
                 }
             }
         }
@@ -413,7 +482,7 @@ int encode_act_map(const __half* x, int M, int64_t K, CUtensorMap* out) {
              CN_ERR_UNSUPPORTED, "activation layout not TMA-tileable");
     cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
     cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-    cuuint32_t box[2] = {(cuuint32_t)mm::kKS, (cuuint32_t)mm::kNT};
+    cuuint32_t box[2] = {64, (cuuint32_t)mm::kNT};  // one 128-byte swizzle row of fp16
     return encode_tiled_2d(CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<__half*>(x), dims, strides,
                            box, CU_TENSOR_MAP_SWIZZLE_128B, out);
 }
@@ -461,6 +530,8 @@ int matmul_q4_0(cudaStream_t st, uint32_t* err, int nmat, const void* const* w, 
         if (i < nmat) tiles += (int)((rows[i] + mm::kRows - 1) / mm::kRows);
     }
     a.toff[nmat] = tiles;
+    a.tok_tiles = (M + mm::kNT - 1) / mm::kNT;
+    a.tiles = tiles * a.tok_tiles;
     a.rb = K / 32 * 18;
     a.M = M;
     a.K = (int)K;
@@ -468,7 +539,13 @@ int matmul_q4_0(cudaStream_t st, uint32_t* err, int nmat, const void* const* w, 
     a.err = err;
     int rc = encode_act_map(x, M, K, &maps.x);
     if (rc) return rc;
-    const dim3 grid(tiles, (M + mm::kNT - 1) / mm::kNT);
+    static int sms = 0;
+    if (sms <= 0) {
+        int dev = 0;
+        CN_CUDA(cudaGetDevice(&dev));
+        CN_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    }
+    const dim3 grid(a.tiles < sms ? a.tiles : sms);  // persistent: one CTA per SM
     CN_CUDA(launch_k(false, matmul_q4_0_kernel, grid, dim3(mm::kThreads), (size_t)mm::kSmem, st, maps, a));
     return CN_OK;
 }
