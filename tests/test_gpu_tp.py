@@ -29,6 +29,15 @@ def tp_dc(max_batch=1, n_layers=2):
     return cf.replace(dc, model=m, kv_filled=20, decode_pos=20)
 
 
+def tp8_dc(n_layers=2):
+    """Shapes that shard over 2, 4 and 8 ranks: 32 heads of 64 over 8 kv heads (one
+    per rank at 8), O and down input split into whole 256-column super-blocks."""
+    dc = cf.with_layers(cf.CONFIGS[4], n_layers, 1)
+    m = cf.replace(dc.model, dim=2048, hidden_dim=2048, n_heads=32, n_kv_heads=8, head_dim=64,
+                   vocab=512, ctx_len=64, kv_f16=True)
+    return cf.replace(dc, model=m, kv_filled=20, decode_pos=20)
+
+
 def run_group(dc, size, steps):
     ctx = mp.get_context("spawn")
     to_parent = ctx.Queue()
@@ -82,3 +91,32 @@ def test_tp2_decode_matches_oracle(oracle, batch):
             got = res[0][s][0][b]
             assert rel_err(got, ref) <= REL_TOL, (b, s, rel_err(got, ref))
             assert int(res[0][s][1][b]) == int(np.argmax(ref))
+
+
+def _check_against_oracle(oracle, dc, res, steps, batch):
+    size = len(res)
+    for s in range(steps):
+        for r in range(1, size):
+            np.testing.assert_array_equal(res[0][s][0], res[r][s][0])
+            np.testing.assert_array_equal(res[0][s][1], res[r][s][1])
+    host = cf.host_tensors(dc)
+    names = tensor_names(dc.model.n_layers)
+    types = [cf.tensor_type(dc, n) for n in names]
+    for b in range(batch):
+        k, v = cf.host_kv(dc, b)
+        orc = _oracle.OracleLlama(oracle, dc.model, host, types, names, k.copy(), v.copy())
+        for s in range(steps):
+            ref = orc.forward([cf.token(dc, b, s)], dc.decode_pos + s)
+            got = res[0][s][0][b]
+            assert rel_err(got, ref) <= REL_TOL, (b, s, rel_err(got, ref))
+            assert int(res[0][s][1][b]) == int(np.argmax(ref))
+
+
+@pytest.mark.parametrize("size", [2, 4, 8])
+def test_tp_n_decode_matches_oracle(oracle, size):
+    """The same model on 2, 4 and 8 ranks (where that many GPUs exist)."""
+    if torch.cuda.device_count() < size:
+        pytest.skip(f"needs {size} GPUs")
+    dc = tp8_dc()
+    steps = 3
+    _check_against_oracle(oracle, dc, run_group(dc, size, steps), steps, 1)
