@@ -427,7 +427,8 @@ def prefill_main(a, world: int, rank: int, local: int, dc) -> int:
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": int(xh.numel() * 4),
                     "d2h_bytes_per_step": int(oh.numel() * 4)},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak,
+                         "traffic": committed_traffic(f"matmul_q4_0_{2 * m.hidden_dim}x{m.dim}_m{n}"),
                          "kernel": f"matmul_q4_0_kernel gate/up {2 * m.hidden_dim}x{m.dim} M{n}",
                          "us_per_launch": us, "flops_per_launch": flops,
                          "us_per_launch_by_group": us_by_group,

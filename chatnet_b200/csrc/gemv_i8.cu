@@ -480,6 +480,17 @@ static int min_units_per_cta() {
     return v;
 }
 
+// Most CTAs that share one tile (CHATNET_GEMV_TILE_CAP, default 7).
+static int tile_share_cap() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("CHATNET_GEMV_TILE_CAP");
+        v = e ? atoi(e) : 7;
+        if (v < 1) v = 1;
+    }
+    return v;
+}
+
 int gemv_i8_ctas(int sms, int tiles, int units, int batch) {
     // every resident CTA, each at least min_units_per_cta() units (but at
     // least one CTA per SM); at most 8 CTAs share a tile
@@ -488,7 +499,7 @@ int gemv_i8_ctas(int sms, int tiles, int units, int batch) {
     int64_t want = total / min_units_per_cta();
     if (want < sms) want = total / 2 < sms ? total / 2 : sms;
     if (want < 1) want = 1;
-    const int64_t cap = (int64_t)tiles * 7;
+    const int64_t cap = (int64_t)tiles * tile_share_cap();
     if (want > cap) want = cap;
     return per_sm * sms < want ? per_sm * sms : (int)want;
 }
