@@ -85,6 +85,18 @@ SIGNATURES: dict[str, tuple] = {
     "cn_llama_destroy": (_i, [_vp]),
     "cn_llama_forward": (_i, [_vp, C.POINTER(_i), _i, _i, _fp]),
     "cn_llama_prefill_hidden_dev": (_i, [_vp, _vp, _i, _i, _vp]),
+    "cn_gguf_open": (_i, [C.c_char_p, C.POINTER(_vp)]),
+    "cn_gguf_close": (_i, [_vp]),
+    "cn_gguf_tensor_count": (_i, [_vp, C.POINTER(_i)]),
+    "cn_gguf_tensor_info": (_i, [_vp, _i, C.POINTER(C.c_char_p), C.POINTER(_i), C.POINTER(_i),
+                                 C.POINTER(_u64), C.POINTER(_u64), C.POINTER(_u64)]),
+    "cn_gguf_find": (_i, [_vp, C.c_char_p, C.POINTER(_i)]),
+    "cn_gguf_get_int": (_i, [_vp, C.c_char_p, C.POINTER(C.c_int64)]),
+    "cn_gguf_get_float": (_i, [_vp, C.c_char_p, C.POINTER(C.c_double)]),
+    "cn_gguf_get_string": (_i, [_vp, C.c_char_p, C.POINTER(C.c_char_p)]),
+    "cn_gguf_llama_config": (_i, [_vp, _vp]),
+    "cn_gguf_upload": (_i, [_vp, _vp, C.c_char_p, C.POINTER(_vp)]),
+    "cn_llama_create_from_gguf": (_i, [_vp, _vp, _i, _i, C.POINTER(_vp), C.POINTER(_vp), _i]),
     "cn_llama_prefill_kernels": (_i, [_vp, C.POINTER(_i)]),
     "cn_llama_decode": (_i, [_vp, C.POINTER(_i), C.POINTER(_i), _i, _fp, C.POINTER(_i)]),
     "cn_llama_kv_write": (_i, [_vp, _i, _i, _i, _i, _vp, _vp]),

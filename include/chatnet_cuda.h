@@ -288,6 +288,53 @@ int cn_llama_profile_step(cn_llama* m, int batch, float* us_by_stage, int n_stag
 int cn_llama_time_matmul(cn_llama* m, int group, int n, int iters, float* us_per_launch,
                          double* flops_per_launch);
 
+/* ---- GGUF files ------------------------------------------------------------ */
+
+typedef struct cn_gguf cn_gguf;
+
+/* GgufReader.Load (Gguf/GgufReader.cs:34-75) with the mapping of
+ * MemoryMappedWeights (Memory/MemoryMappedWeights.cs:23-40): parses a GGUF
+ * version 2 or 3 file (metadata, tensor descriptors, data section aligned to
+ * general.alignment, default 32) and maps it read-only.  Bad magic, version
+ * or a truncated header: CN_ERR_INVALID_ARG (InvalidDataException); a file
+ * that cannot be opened: CN_ERR_NOT_FOUND. */
+int cn_gguf_open(const char* path, cn_gguf** out);
+int cn_gguf_close(cn_gguf* g);
+int cn_gguf_tensor_count(const cn_gguf* g, int* n);
+/* Tensor i's descriptor (GgufTensorInfo): name (valid until cn_gguf_close),
+ * ggml type, dimensions (dims[0] innermost; 4 entries, unused ones 1), byte
+ * size (GgufTensorInfo.ByteSize) and absolute offset in the file.  Any output
+ * pointer may be NULL. */
+int cn_gguf_tensor_info(const cn_gguf* g, int i, const char** name, int* type, int* n_dims,
+                        uint64_t* dims, uint64_t* bytes, uint64_t* file_offset);
+/* Index of a tensor by name; CN_ERR_NOT_FOUND ("Tensor not found: ...") otherwise. */
+int cn_gguf_find(const cn_gguf* g, const char* name, int* index);
+/* Metadata values (GgufMetadata.GetInt32 / TryGet / GetString). */
+int cn_gguf_get_int(const cn_gguf* g, const char* key, int64_t* out);
+int cn_gguf_get_float(const cn_gguf* g, const char* key, double* out);
+int cn_gguf_get_string(const cn_gguf* g, const char* key, const char** out);
+/* GgufReader.ExtractModelConfig (GgufReader.cs:80-176) for a Llama decoder:
+ * <arch>.embedding_length, block_count, attention.head_count(_kv),
+ * feed_forward_length, context_length, rope.freq_base,
+ * attention.layer_norm_rms_epsilon, attention.key_length (head_dim, else
+ * dim / heads), vocabulary = length of tokenizer.ggml.tokens, else
+ * <arch>.vocab_size, with the reader's defaults and bare-key fallbacks.
+ * kv_dtype = CN_KV_F32, max_batch = 1.  Architectures the reference runs with
+ * another decoder (ModelFactory.cs:23-39): CN_ERR_UNSUPPORTED. */
+int cn_gguf_llama_config(const cn_gguf* g, cn_llama_config* cfg);
+/* Uploads one tensor byte for byte (cn_tensor_upload, [rows = product of
+ * dims[1..], cols = dims[0]]). */
+int cn_gguf_upload(cn_ctx* ctx, const cn_gguf* g, const char* name, cn_tensor** out);
+/* LlamaWeights.ResolveAll (Models/Llama/LlamaWeights.cs:78-145) + the
+ * LlamaModel constructor: uploads every tensor cn_llama_create needs (an
+ * absent output.weight means lm_head tied to token_embd.weight) and builds
+ * the model with the file's config, max_batch and kv_dtype.  The uploaded
+ * tensors go to tensors_out (CN_LLAMA_TENSORS(n_layers) entries, the tied
+ * lm_head repeating token_embd); free each distinct one with cn_tensor_free
+ * after cn_llama_destroy. */
+int cn_llama_create_from_gguf(cn_ctx* ctx, const cn_gguf* g, int max_batch, int kv_dtype,
+                              cn_llama** out, cn_tensor** tensors_out, int n_tensors_out);
+
 /* ---- tensor parallelism (one process per GPU) ---------------------------
  * (no reference counterpart: the reference runs on one CPU.)  Rank r of a
  * group of `size` GPUs holds shards of every projection: q/k/v/gate/up and
