@@ -31,6 +31,10 @@ CN_ERR_NCCL = -7
 TYPE_F32 = 0
 TYPE_F16 = 1
 TYPE_Q4_0 = 2
+TYPE_Q4_1 = 3
+TYPE_Q5_0 = 6
+TYPE_Q5_1 = 7
+TYPE_Q8_0 = 8
 TYPE_Q4_K = 12
 TYPE_Q6_K = 14
 

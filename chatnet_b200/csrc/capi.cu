@@ -32,7 +32,7 @@ int cuda_error(cudaError_t e, const char* what) {
 
 bool type_supported(int type) {
     return type == CN_TYPE_Q4_0 || type == CN_TYPE_Q4_K || type == CN_TYPE_Q6_K ||
-           type == CN_TYPE_F32 || type == CN_TYPE_F16;
+           type == CN_TYPE_F32 || type == CN_TYPE_F16 || is_block32(type);
 }
 
 uint64_t row_bytes(int type, int64_t cols) { return cn_byte_size(type, (uint64_t)cols); }
@@ -97,6 +97,10 @@ uint64_t cn_byte_size(int type, uint64_t elements) {
         case CN_TYPE_F32: return elements * 4;
         case CN_TYPE_F16: return elements * 2;
         case CN_TYPE_Q4_0: return (elements + 31) / 32 * 18;
+        case CN_TYPE_Q4_1: return (elements + 31) / 32 * 20;
+        case CN_TYPE_Q5_0: return (elements + 31) / 32 * 22;
+        case CN_TYPE_Q5_1: return (elements + 31) / 32 * 24;
+        case CN_TYPE_Q8_0: return (elements + 31) / 32 * 34;
         case CN_TYPE_Q4_K: return (elements + 255) / 256 * 144;
         case CN_TYPE_Q6_K: return (elements + 255) / 256 * 210;
         default: return 0;

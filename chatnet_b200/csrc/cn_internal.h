@@ -68,6 +68,13 @@ struct cn_tensor {
 namespace cn {
 
 uint64_t row_bytes(int type, int64_t cols);
+// The 32-weight block codecs decoded through the generic paths (formats.cuh).
+__host__ __device__ inline bool is_block32(int type) {
+    return type == CN_TYPE_Q4_1 || type == CN_TYPE_Q5_0 || type == CN_TYPE_Q5_1 || type == CN_TYPE_Q8_0;
+}
+__host__ __device__ inline int block32_bytes(int type) {
+    return type == CN_TYPE_Q4_1 ? 20 : type == CN_TYPE_Q5_0 ? 22 : type == CN_TYPE_Q5_1 ? 24 : 34;
+}
 bool type_supported(int type);
 
 int ensure(void** p, size_t* have, size_t need, bool zero);

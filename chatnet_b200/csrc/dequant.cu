@@ -102,6 +102,20 @@ __global__ void dequant_q6_k_kernel(const uint8_t* __restrict__ q, float* __rest
     }
 }
 
+// One thread per 32-element block of Q4_1 / Q5_0 / Q5_1 / Q8_0; a partial
+// last block writes only its `remaining` elements, as the reference loops do.
+__global__ void dequant_b32_kernel(int type, const uint8_t* __restrict__ q, float* __restrict__ out, int64_t n,
+                                   int bpb) {
+    const int64_t nb = (n + 31) / 32;
+    for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < nb;
+         b += (int64_t)gridDim.x * blockDim.x) {
+        const uint8_t* p = q + b * bpb;
+        const int64_t rem = n - b * 32;
+        const int cnt = rem < 32 ? (int)rem : 32;
+        for (int j = 0; j < cnt; j++) out[b * 32 + j] = block32_elem(type, p, j);
+    }
+}
+
 __global__ void convert_f16_kernel(const uint16_t* __restrict__ h, float* __restrict__ out,
                                    int64_t n) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
@@ -121,6 +135,11 @@ int dequant_launch(int type, const void* d_blocks, float* d_out, int64_t n, cuda
     if (n == 0) return CN_OK;
     CN_CHECK(d_blocks && d_out, CN_ERR_INVALID_ARG, "null pointer");
     const uint8_t* q = static_cast<const uint8_t*>(d_blocks);
+    if (is_block32(type)) {
+        dequant_b32_kernel<<<grid_for((n + 31) / 32, 256), 256, 0, s>>>(type, q, d_out, n, block32_bytes(type));
+        CN_CUDA(cudaGetLastError());
+        return CN_OK;
+    }
     switch (type) {
         case CN_TYPE_Q4_0:
             dequant_q4_0_kernel<<<grid_for((n + 31) / 32, 256), 256, 0, s>>>(q, d_out, n);

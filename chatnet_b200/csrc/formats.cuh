@@ -1,4 +1,5 @@
-// formats.cuh -- GGUF block formats (Q4_0, Q4_K, Q6_K) on the device.
+// formats.cuh -- GGUF block formats (Q4_0, Q4_K, Q6_K; Q4_1, Q5_0, Q5_1, Q8_0
+// through the generic paths) on the device.
 //
 // Two kinds of decode live here:
 //  * bit-exact scalar dequantization that follows the reference's rounding
@@ -28,6 +29,29 @@ __device__ __forceinline__ void q4k_scale_min(const uint8_t* q, int j, int& sc, 
         sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
         m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
     }
+}
+
+// Element j (0..31) of one 32-weight block of Q4_1, Q5_0, Q5_1 or Q8_0, with
+// the reference's operation order (no fused multiply-add):
+//   Q4_1  q * d + m, q the low (j < 16) or high nibble of byte j % 16
+//                                          DequantQ4_1.cs:24-56 (d@0, m@2, qs@4)
+//   Q5_0  (q5 - 16) * d, q5 = nibble | bit j of qh << 4
+//                                          DequantQ5_0.cs:29-68 (d@0, qh@2, qs@6)
+//   Q5_1  q5 * d + m                       DequantQ5_1.cs:30-69 (d@0, m@2, qh@4, qs@8)
+//   Q8_0  (sbyte)q * d                     DequantQ8_0.cs:19-41 (d@0, qs@2)
+__device__ __forceinline__ float block32_elem(int type, const uint8_t* p, int j) {
+    if (type == CN_TYPE_Q8_0) return __fmul_rn((float)(int8_t)p[2 + j], ld_half(p));
+    const int qs_off = type == CN_TYPE_Q4_1 ? 4 : type == CN_TYPE_Q5_0 ? 6 : 8;
+    const uint8_t byte = p[qs_off + (j & 15)];
+    int q = j < 16 ? (byte & 0x0F) : ((byte >> 4) & 0x0F);
+    if (type != CN_TYPE_Q4_1) {
+        const int qh_off = type == CN_TYPE_Q5_0 ? 2 : 4;
+        const uint32_t qh = (uint32_t)p[qh_off] | ((uint32_t)p[qh_off + 1] << 8) | ((uint32_t)p[qh_off + 2] << 16) |
+                            ((uint32_t)p[qh_off + 3] << 24);
+        q |= (int)((qh >> j) & 1u) << 4;
+    }
+    if (type == CN_TYPE_Q5_0) return __fmul_rn((float)(q - 16), ld_half(p));
+    return __fadd_rn(__fmul_rn((float)q, ld_half(p)), ld_half(p + 2));
 }
 
 // ---- GEMV fragment decode -------------------------------------------------

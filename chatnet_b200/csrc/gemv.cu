@@ -841,6 +841,10 @@ __device__ float block_dot(int type, const uint8_t* row, int blk, const float* x
         }
     } else if (type == CN_TYPE_F32) {
         s = reinterpret_cast<const float*>(row)[blk] * x[blk];
+    } else if (is_block32(type)) {
+        const uint8_t* p = row + (size_t)blk * block32_bytes(type);
+        const float* xb = x + (size_t)blk * 32;
+        for (int j = 0; j < 32; j++) s = fmaf(block32_elem(type, p, j), xb[j], s);
     } else if (type == CN_TYPE_F16) {
         s = ld_half(row + 2 * (size_t)blk) * x[blk];
     }
@@ -1043,7 +1047,8 @@ int gemv_make(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols
         else if (encode_weight_map(type, d_w, rows, op->rb, &op->map) != CN_OK) op->tma = false;
     }
     if (!op->tma) {
-        int blk = type == CN_TYPE_Q4_0 ? 32 : (type == CN_TYPE_Q4_K || type == CN_TYPE_Q6_K) ? 256 : 1;
+        int blk = type == CN_TYPE_Q4_0 || is_block32(type) ? 32
+                  : (type == CN_TYPE_Q4_K || type == CN_TYPE_Q6_K) ? 256 : 1;
         CN_CHECK(cols % blk == 0, CN_ERR_INVALID_ARG, "inDim %lld not a multiple of %d",
                  (long long)cols, blk);
     }
@@ -1145,7 +1150,8 @@ int gemv_run(cn_ctx* ctx, cudaStream_t st, const GemvOp& op, const float* d_x, c
     CN_CHECK(!xo || xo->size <= 1 || op.plan.path == kPathI8, CN_ERR_UNSUPPORTED,
              "tensor-parallel exchange needs the integer GEMV (Q4_K, batch <= 8)");
     if (!op.tma) {
-        int blk = op.type == CN_TYPE_Q4_0 ? 32 : (op.type == CN_TYPE_Q4_K || op.type == CN_TYPE_Q6_K) ? 256 : 1;
+        int blk = op.type == CN_TYPE_Q4_0 || is_block32(op.type) ? 32
+                  : (op.type == CN_TYPE_Q4_K || op.type == CN_TYPE_Q6_K) ? 256 : 1;
         int threads = 256;
         int64_t warps = op.rows * op.batch;
         int64_t blocks = (warps * 32 + threads - 1) / threads;

@@ -716,6 +716,8 @@ __global__ void embed_kernel(int type, const uint8_t* __restrict__ emb, uint64_t
             int q = (lo | (((qh[l] >> (2 * s)) & 3) << 4)) - 32;
             int si = half * 8 + l / 16 + 2 * s;
             v = __fmul_rn(__fmul_rn(ld_half(p + 208), (float)(int8_t)p[192 + si]), (float)q);
+        } else if (is_block32(type)) {
+            v = block32_elem(type, row + (i / 32) * block32_bytes(type), i % 32);
         } else if (type == CN_TYPE_F16) {
             v = ld_half(row + 2 * i);
         } else {

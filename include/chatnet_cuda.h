@@ -49,6 +49,10 @@ extern "C" {
 #define CN_TYPE_F32 0
 #define CN_TYPE_F16 1
 #define CN_TYPE_Q4_0 2
+#define CN_TYPE_Q4_1 3
+#define CN_TYPE_Q5_0 6
+#define CN_TYPE_Q5_1 7
+#define CN_TYPE_Q8_0 8
 #define CN_TYPE_Q4_K 12
 #define CN_TYPE_Q6_K 14
 

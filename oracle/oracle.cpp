@@ -79,6 +79,10 @@ extern "C" uint64_t or_byte_size(int type, uint64_t elements) {
         case OR_F32: return elements * 4;
         case OR_F16: return elements * 2;
         case OR_Q4_0: return (elements + 31) / 32 * 18;
+        case OR_Q4_1: return (elements + 31) / 32 * 20;
+        case OR_Q5_0: return (elements + 31) / 32 * 22;
+        case OR_Q5_1: return (elements + 31) / 32 * 24;
+        case OR_Q8_0: return (elements + 31) / 32 * 34;
         case OR_Q4_K: return (elements + 255) / 256 * 144;
         case OR_Q6_K: return (elements + 255) / 256 * 210;
         default: return 0;
@@ -108,6 +112,59 @@ static void dequant_q4_0(const uint8_t* q, float* out, int64_t n) {
             out[dst + 16 + j] = (float)high * scale;
         }
         src += 16;
+        dst += half + second;
+    }
+}
+
+// The 32-weight codecs.  Dequantize writes `count` (or half / second-half)
+// elements of a partial last block, like the Q4_0 loop above.
+// DequantQ8_0.Dequantize (DequantQ8_0.cs:19-41): (sbyte)q * d.
+static void dequant_q8_0(const uint8_t* q, float* out, int64_t n) {
+    int64_t nb = (n + 31) / 32, src = 0, dst = 0;
+    for (int64_t b = 0; b < nb; b++) {
+        float scale = h2f(q + src);
+        src += 2;
+        int64_t remaining = n - dst;
+        int count = remaining < 32 ? (int)remaining : 32;
+        for (int i = 0; i < count; i++) out[dst + i] = (float)(int8_t)q[src + i] * scale;
+        src += 32;
+        dst += count;
+    }
+}
+
+// DequantQ4_1.Dequantize (DequantQ4_1.cs:24-56): q * d + m (d@0, m@2, qs@4).
+// DequantQ5_0.Dequantize (DequantQ5_0.cs:29-68): (q5 - 16) * d (d@0, qh@2, qs@6).
+// DequantQ5_1.Dequantize (DequantQ5_1.cs:30-69): q5 * d + m (d@0, m@2, qh@4, qs@8).
+// q5 = nibble | ((qh >> j) & 1) << 4, j the element's index in the block.
+static void dequant_b32(int type, const uint8_t* q, float* out, int64_t n) {
+    const int bpb = type == OR_Q4_1 ? 20 : type == OR_Q5_0 ? 22 : 24;
+    const int qs_off = type == OR_Q4_1 ? 4 : type == OR_Q5_0 ? 6 : 8;
+    const int qh_off = type == OR_Q5_0 ? 2 : 4;
+    int64_t nb = (n + 31) / 32, dst = 0;
+    for (int64_t b = 0; b < nb; b++) {
+        const uint8_t* blk = q + b * bpb;
+        float scale = h2f(blk);
+        float min = type == OR_Q5_0 ? 0.f : h2f(blk + 2);
+        uint32_t qh = 0;
+        if (type != OR_Q4_1)
+            qh = (uint32_t)blk[qh_off] | ((uint32_t)blk[qh_off + 1] << 8) | ((uint32_t)blk[qh_off + 2] << 16) |
+                 ((uint32_t)blk[qh_off + 3] << 24);
+        int64_t remaining = n - dst;
+        int half = remaining < 16 ? (int)remaining : 16;
+        int second = remaining < 32 ? (remaining > 16 ? (int)(remaining - 16) : 0) : 16;
+        for (int h = 0; h < 2; h++) {
+            int cnt = h == 0 ? half : second;
+            for (int j = 0; j < cnt; j++) {
+                int nib = h == 0 ? (blk[qs_off + j] & 0x0F) : ((blk[qs_off + j] >> 4) & 0x0F);
+                int idx = 16 * h + j;
+                if (type == OR_Q4_1) {
+                    out[dst + idx] = (float)nib * scale + min;
+                } else {
+                    int q5 = nib | (int)((qh >> idx) & 1u) << 4;
+                    out[dst + idx] = type == OR_Q5_0 ? (float)(q5 - 16) * scale : (float)q5 * scale + min;
+                }
+            }
+        }
         dst += half + second;
     }
 }
@@ -185,6 +242,10 @@ extern "C" int or_dequantize(int type, const uint8_t* src, float* dst, int64_t n
     if (n < 0) return -1;
     switch (type) {
         case OR_Q4_0: dequant_q4_0(src, dst, n); return 0;
+        case OR_Q8_0: dequant_q8_0(src, dst, n); return 0;
+        case OR_Q4_1:
+        case OR_Q5_0:
+        case OR_Q5_1: dequant_b32(type, src, dst, n); return 0;
         case OR_Q4_K: dequant_q4_k(src, dst, n); return 0;
         case OR_Q6_K: dequant_q6_k(src, dst, n); return 0;
         case OR_F32: memcpy(dst, src, (size_t)n * 4); return 0;
@@ -361,6 +422,52 @@ static float dot_f32(const float* a, const float* b, int length) {
     return sum;
 }
 
+// DequantQ8_0.DotProductScalar (DequantQ8_0.cs:94-119): per block, sum of
+// (sbyte)q * x in order, then sum += blockSum * d.
+static float dot_q8_0(const uint8_t* row, const float* x, int n) {
+    float sum = 0.f;
+    for (int b = 0; b < n / 32; b++) {
+        const uint8_t* blk = row + (size_t)b * 34;
+        float scale = h2f(blk), bs = 0.f;
+        for (int i = 0; i < 32; i++) bs += (float)(int8_t)blk[2 + i] * x[32 * b + i];
+        sum += bs * scale;
+    }
+    return sum;
+}
+
+// DequantQ4_1.DotProductScalar (DequantQ4_1.cs:134-171),
+// DequantQ5_0.DotProductScalar (DequantQ5_0.cs:77-114),
+// DequantQ5_1.DotProductScalar (DequantQ5_1.cs:78-119): per block, the low
+// then the high half, sum += blockSum * d (+ inputSum * m for Q4_1 / Q5_1).
+static float dot_b32(int type, const uint8_t* row, const float* x, int n) {
+    const int bpb = type == OR_Q4_1 ? 20 : type == OR_Q5_0 ? 22 : 24;
+    const int qs_off = type == OR_Q4_1 ? 4 : type == OR_Q5_0 ? 6 : 8;
+    const int qh_off = type == OR_Q5_0 ? 2 : 4;
+    float sum = 0.f;
+    for (int b = 0; b < n / 32; b++) {
+        const uint8_t* blk = row + (size_t)b * bpb;
+        const float* xb = x + 32 * b;
+        float scale = h2f(blk);
+        float min = type == OR_Q5_0 ? 0.f : h2f(blk + 2);
+        uint32_t qh = 0;
+        if (type != OR_Q4_1)
+            qh = (uint32_t)blk[qh_off] | ((uint32_t)blk[qh_off + 1] << 8) | ((uint32_t)blk[qh_off + 2] << 16) |
+                 ((uint32_t)blk[qh_off + 3] << 24);
+        float bs = 0.f, is = 0.f;
+        for (int h = 0; h < 2; h++)
+            for (int j = 0; j < 16; j++) {
+                int idx = 16 * h + j;
+                int nib = h == 0 ? (blk[qs_off + j] & 0x0F) : ((blk[qs_off + j] >> 4) & 0x0F);
+                int q = type == OR_Q4_1 ? nib : (nib | (int)((qh >> idx) & 1u) << 4);
+                if (type == OR_Q5_0) q -= 16;
+                bs += (float)q * xb[idx];
+                if (type != OR_Q5_0) is += xb[idx];
+            }
+        sum += type == OR_Q5_0 ? bs * scale : bs * scale + is * min;
+    }
+    return sum;
+}
+
 // LlamaModel.MatVecMulF16 row (LlamaModel.cs:570-598): scalar, in order.
 static float dot_f16(const uint8_t* row, const float* x, int n) {
     float dot = 0.f;
@@ -371,6 +478,10 @@ static float dot_f16(const uint8_t* row, const float* x, int n) {
 extern "C" float or_dot(int type, const uint8_t* row, const float* x, int n) {
     switch (type) {
         case OR_Q4_0: return dot_q4_0(row, x, n);
+        case OR_Q8_0: return dot_q8_0(row, x, n);
+        case OR_Q4_1:
+        case OR_Q5_0:
+        case OR_Q5_1: return dot_b32(type, row, x, n);
         case OR_Q4_K: return dot_q4_k(row, x, n);
         case OR_Q6_K: return dot_q6_k(row, x, n);
         case OR_F32: return dot_f32((const float*)row, x, n);
@@ -416,6 +527,10 @@ static void parallel_rows(int rows, int nthreads, F&& body) {
 static int row_bytes(int type, int in_dim, size_t* bpr) {
     switch (type) {
         case OR_Q4_0: *bpr = (size_t)(in_dim / 32) * 18; return 0;
+        case OR_Q4_1: *bpr = (size_t)(in_dim / 32) * 20; return 0;
+        case OR_Q5_0: *bpr = (size_t)(in_dim / 32) * 22; return 0;
+        case OR_Q5_1: *bpr = (size_t)(in_dim / 32) * 24; return 0;
+        case OR_Q8_0: *bpr = (size_t)(in_dim / 32) * 34; return 0;
         case OR_Q4_K: *bpr = (size_t)(in_dim / 256) * 144; return 0;
         case OR_Q6_K: *bpr = (size_t)(in_dim / 256) * 210; return 0;
         case OR_F32: *bpr = (size_t)in_dim * 4; return 0;

@@ -91,12 +91,60 @@ def cases() -> list[dict]:
     out.append(dict(name="Q4K_MultiBlock_DotProduct", ref=f"{T}:728-759", type=12, n=512,
                     blocks=blk, dequant=deq, x=[0.5] * 512,
                     dot=float(sum(d * 0.5 for d in deq)), tol=0.1))
+    # Q4_1_Dequantize_ProducesCorrectValues (:93-110): d=2, m=1, qs=0 -> 0*2+1
+    blk = half_bytes(2.0) + half_bytes(1.0) + [0] * 16
+    out.append(dict(name="Q4_1_Dequantize_ProducesCorrectValues", ref=f"{T}:93-110", type=3, n=32,
+                    blocks=blk, dequant=[1.0] * 32, tol=0.01))
+
+    # Q4_1_DotProduct_MatchesScalar (:111-136): d=1, m=0.5, nibbles 5, x=1
+    blk = half_bytes(1.0) + half_bytes(0.5) + [0x55] * 16
+    out.append(dict(name="Q4_1_DotProduct_MatchesScalar", ref=f"{T}:111-136", type=3, n=32,
+                    blocks=blk, dequant=[5.5] * 32, x=[1.0] * 32, dot=5.5 * 32, tol=0.01))
+
+    # Q5_0_Dequantize_ZeroQuants (:141-157): d=1, qh=qs=0 -> (0-16)*1
+    blk = half_bytes(1.0) + [0] * 20
+    out.append(dict(name="Q5_0_Dequantize_ZeroQuants", ref=f"{T}:141-157", type=6, n=32,
+                    blocks=blk, dequant=[-16.0] * 32, tol=0.01))
+
+    # Q5_0_DotProduct_MatchesDequantize (:158-186): d=0.5, qh bits 0-15 set,
+    # nibbles 0xA, x=0.5: positions 0-15 (26-16)*0.5, 16-31 (10-16)*0.5
+    blk = half_bytes(0.5) + [0xFF, 0xFF, 0x00, 0x00] + [0xAA] * 16
+    deq = [5.0] * 16 + [-3.0] * 16
+    out.append(dict(name="Q5_0_DotProduct_MatchesDequantize", ref=f"{T}:158-186", type=6, n=32,
+                    blocks=blk, dequant=deq, x=[0.5] * 32, dot=float(sum(d * 0.5 for d in deq)), tol=0.01))
+
+    # Q5_1_Dequantize_WithMinOffset (:189-206): d=1, m=2, zero quants -> 2
+    blk = half_bytes(1.0) + half_bytes(2.0) + [0] * 20
+    out.append(dict(name="Q5_1_Dequantize_WithMinOffset", ref=f"{T}:189-206", type=7, n=32,
+                    blocks=blk, dequant=[2.0] * 32, tol=0.01))
+
+    # Q5_1_DotProduct_MatchesDequantize (:207-231): d=0.25, m=0.5, nibbles 3, x=1
+    blk = half_bytes(0.25) + half_bytes(0.5) + [0] * 4 + [0x33] * 16
+    out.append(dict(name="Q5_1_DotProduct_MatchesDequantize", ref=f"{T}:207-231", type=7, n=32,
+                    blocks=blk, dequant=[1.25] * 32, x=[1.0] * 32, dot=1.25 * 32, tol=0.01))
+
+    # Q8_0_Dequantize_ProducesCorrectValues (:237-254): d=0.5, q=10 -> 5
+    blk = half_bytes(0.5) + [10] * 32
+    out.append(dict(name="Q8_0_Dequantize_ProducesCorrectValues", ref=f"{T}:237-254", type=8, n=32,
+                    blocks=blk, dequant=[5.0] * 32, tol=0.01))
+
+    # Q8_0_Dequantize_NegativeValues (:255-272): d=1, q=0xF6 (-10)
+    blk = half_bytes(1.0) + [0xF6] * 32
+    out.append(dict(name="Q8_0_Dequantize_NegativeValues", ref=f"{T}:255-272", type=8, n=32,
+                    blocks=blk, dequant=[-10.0] * 32, tol=0.01))
+
+    # Q8_0_DotProduct_MatchesDequantize (:273-299): d=0.25, q=0..31, x=1
+    blk = half_bytes(0.25) + list(range(32))
+    deq = [0.25 * i for i in range(32)]
+    out.append(dict(name="Q8_0_DotProduct_MatchesDequantize", ref=f"{T}:273-299", type=8, n=32,
+                    blocks=blk, dequant=deq, x=[1.0] * 32, dot=float(sum(deq)), tol=0.01))
     return out
 
 
-# GgufTensorInfo_ByteSize_AllTypes (:642-698), the rows for the hot path's types
-# plus F32/F16: (type, block size, bytes per block)
-BYTESIZE = [(0, 1, 4), (1, 1, 2), (2, 32, 18), (12, 256, 144), (14, 256, 210)]
+# GgufTensorInfo_ByteSize_AllTypes (:642-698), the rows for the types this
+# library decodes: (type, block size, bytes per block)
+BYTESIZE = [(0, 1, 4), (1, 1, 2), (2, 32, 18), (3, 32, 20), (6, 32, 22), (7, 32, 24), (8, 32, 34),
+            (12, 256, 144), (14, 256, 210)]
 
 
 def main() -> None:

@@ -42,7 +42,8 @@ def test_abi_version():
 @pytest.mark.parametrize("t,elems,expected", [
     (cn.TYPE_Q4_0, 2048, 1152), (cn.TYPE_Q4_0, 33, 36), (cn.TYPE_Q4_K, 4096, 2304),
     (cn.TYPE_Q4_K, 257, 288), (cn.TYPE_Q6_K, 4096, 3360), (cn.TYPE_F32, 10, 40),
-    (cn.TYPE_F16, 10, 20), (3, 32, 0)])
+    (cn.TYPE_F16, 10, 20), (cn.TYPE_Q4_1, 32, 20), (cn.TYPE_Q5_0, 64, 44), (cn.TYPE_Q5_1, 33, 48),
+    (cn.TYPE_Q8_0, 32, 34), (10, 256, 0)])
 def test_byte_size(t, elems, expected, oracle):
     assert cn.byte_size(t, elems) == expected
     assert oracle.lib.or_byte_size(t, elems) == expected

@@ -178,3 +178,41 @@ def test_matvec_activation_range(ctx, oracle, name, magnitude):
     ref = oracle.matvec(t, blocks, x, rows)
     assert np.isfinite(y).all()
     assert rel_err(y, ref) <= REL_TOL
+
+
+# The 32-weight codecs decoded through the generic paths: Q4_1, Q5_0, Q5_1, Q8_0
+# (block bytes, offsets of the fp16 fields d and m)
+B32 = {"q4_1": (cn.TYPE_Q4_1, 20, (0, 2)), "q5_0": (cn.TYPE_Q5_0, 22, (0,)),
+       "q5_1": (cn.TYPE_Q5_1, 24, (0, 2)), "q8_0": (cn.TYPE_Q8_0, 34, (0,))}
+
+
+def _rand_b32(name, rows, cols, seed):
+    t, bpb, halves = B32[name]
+    rng = np.random.default_rng(seed)
+    nb = rows * ((cols + 31) // 32)
+    blocks = rng.integers(0, 256, size=(nb, bpb), dtype=np.uint8)
+    for k, off in enumerate(halves):  # finite scales (d) and minima (m)
+        v = (np.abs(rng.standard_normal(nb)) * 0.01 if k == 0 else rng.standard_normal(nb) * 0.01).astype(np.float16)
+        blocks[:, off:off + 2] = v.view(np.uint8).reshape(nb, 2)
+    return t, blocks.ravel()
+
+
+@pytest.mark.parametrize("name", list(B32))
+def test_block32_dequantize_bit_exact(ctx, oracle, name):
+    t, blocks = _rand_b32(name, 37, 96, 11)
+    W = ctx.upload(blocks, t, 37, 96)
+    assert bits_equal(ctx.dequantize(W), oracle.dequantize(t, blocks, 37 * 96).reshape(37, 96))
+    # a partial last block (45 = 32 + 13 values in one row)
+    t, blocks = _rand_b32(name, 1, 45, 12)
+    W = ctx.upload(blocks, t, 1, 45)
+    assert bits_equal(ctx.dequantize(W).ravel(), oracle.dequantize(t, blocks, 45))
+
+
+@pytest.mark.parametrize("name", list(B32))
+@pytest.mark.parametrize("batch", [1, 3])
+def test_block32_matvec_parity(ctx, oracle, name, batch):
+    rows, cols = 300, 2048
+    t, blocks = _rand_b32(name, rows, cols, 13)
+    W = ctx.upload(blocks, t, rows, cols)
+    x = _x(batch, cols, f"b32.x.{name}.{batch}")
+    assert rel_err(ctx.matvec(W, x), oracle.matvec(t, blocks, x, rows)) <= REL_TOL
