@@ -158,7 +158,7 @@ def test_matvec_errors(ctx):
     with pytest.raises(ValueError):
         ctx.matvec(W, np.zeros((33, 64), np.float32))
     with pytest.raises(cn.NotSupportedError):
-        ctx.upload(np.zeros(20, np.uint8), 3, 1, 32)   # Q4_1: not on this path
+        ctx.upload(np.zeros(84, np.uint8), 10, 1, 256)  # Q2_K: no decoder here
     with pytest.raises(ValueError):
         ctx.upload(np.zeros(17, np.uint8), cn.TYPE_Q4_0, 1, 32)  # wrong byte count
 
