@@ -97,6 +97,8 @@ class Context:
         self.handle = h.value
         self.device = device
         self._tensors: "weakref.WeakSet[Tensor]" = weakref.WeakSet()
+        # decoders built on this context (closed before it, since they use its stream)
+        self._models: weakref.WeakSet = weakref.WeakSet()
 
     def _own(self, t: "Tensor") -> "Tensor":
         self._tensors.add(t)
@@ -161,6 +163,8 @@ class Context:
 
     def close(self) -> None:
         if self.handle:
+            for m in list(self._models):
+                m.close()
             for t in list(self._tensors):
                 t.free()
             N.lib().cn_destroy(self.handle)

@@ -403,18 +403,20 @@ int cn_matvec(cn_ctx* ctx, const cn_tensor* W, const float* host_x, float* host_
 
 static int matmul_dev(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols,
                       const float* d_x, float* d_y, int n_tokens, const CUtensorMap* wmap_opt = nullptr) {
-    CN_CHECK(type == CN_TYPE_Q4_0, CN_ERR_UNSUPPORTED, "matmul: type %d not supported (Q4_0)", type);
+    CN_CHECK(matmul_type_ok(type), CN_ERR_UNSUPPORTED, "matmul: type %d not supported (Q4_0, Q4_K)", type);
     CN_CHECK(n_tokens >= 1 && rows >= 1 && cols >= 256 && cols % 256 == 0, CN_ERR_INVALID_ARG,
              "matmul: bad shape (%lld x %lld, %d tokens)", (long long)rows, (long long)cols, n_tokens);
+    // fp16 rows of x (each scaled by a power of two), then their inverse scales
     const size_t hb = (size_t)n_tokens * cols * sizeof(__half);
-    int rc = ensure(&ctx->xhalf, &ctx->xhalf_bytes, hb, false);
+    int rc = ensure(&ctx->xhalf, &ctx->xhalf_bytes, hb + (size_t)n_tokens * sizeof(float), false);
     if (rc) return rc;
     __half* xh = static_cast<__half*>(ctx->xhalf);
-    rc = to_half(ctx->stream, d_x, xh, (int64_t)n_tokens * cols);
+    float* xs = reinterpret_cast<float*>(static_cast<uint8_t*>(ctx->xhalf) + hb);
+    rc = to_half_rows(ctx->stream, d_x, xh, xs, (int)cols, n_tokens);
     if (rc) return rc;
     const int64_t ldy = rows;
-    return matmul_q4_0(ctx->stream, ctx->dev_err, 1, &d_w, wmap_opt ? &wmap_opt : nullptr, &rows, cols, xh,
-                       n_tokens, &d_y, &ldy, false);
+    return matmul_quant(ctx->stream, ctx->dev_err, type, 1, &d_w, wmap_opt ? &wmap_opt : nullptr, &rows, cols,
+                        xh, xs, n_tokens, &d_y, &ldy, false);
 }
 
 int cn_matmul(cn_ctx* ctx, const cn_tensor* W, const float* host_x, float* host_y, int n_tokens) {

@@ -181,6 +181,38 @@ __device__ __forceinline__ float half_bits_to_float(uint16_t h) {
     return __half2float(__ushort_as_half(h));
 }
 
+// A row's fp16 scaling: the power of two s with amax * s in [2^14, 2^15)
+// (clamped to 2^-126..2^126; s = 1 when amax is 0, inf or NaN) and inv = 1/s.
+// fp16 then holds the row's largest value well inside its range, and
+// multiplying a product by inv is exact.
+__device__ __forceinline__ void row_pow2_scale(float amax, float& s, float& inv) {
+    const int eb = (int)((__float_as_uint(amax) >> 23) & 0xFFu);  // amax in [2^(eb-127), 2^(eb-126))
+    if (!(amax > 0.f) || eb == 255) {
+        s = inv = 1.f;
+        return;
+    }
+    int k = 141 - (eb > 0 ? eb : 1);
+    k = k < -126 ? -126 : k > 126 ? 126 : k;
+    s = __uint_as_float((uint32_t)(k + 127) << 23);
+    inv = __uint_as_float((uint32_t)(127 - k) << 23);
+}
+
+// Largest of the non-negative v over the block (every thread gets it); red holds 32 floats.
+__device__ __forceinline__ float block_absmax(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    __syncthreads();  // red may still be read from an earlier reduction
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float m = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) m = fmaxf(m, red[i]);
+    return m;
+}
+
+__device__ __forceinline__ float absmax4(float4 v) {
+    return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+}
+
 // Loads a 32-bit word from shared memory at a 2-byte aligned address.
 __device__ __forceinline__ uint32_t lds_u32_a2(const uint8_t* p) {
     const int mis = (int)(reinterpret_cast<uintptr_t>(p) & 3);

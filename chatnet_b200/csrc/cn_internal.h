@@ -91,18 +91,23 @@ int encode_tiled_2d(CUtensorMapDataType dt, void* base, const cuuint64_t (&dims)
                     CUtensorMapSwizzle swz, CUtensorMap* out);
 
 // Prefill dequant-matmul (matmul.cu): y[i][t][r] (+)= dot(W_i[r], x[t]) for
-// M tokens and nmat <= 3 Q4_0 matrices with the same K (K % 256 == 0); x is
-// fp16 [M][K] (16-byte aligned), y[i] fp32 [M][ldy[i]].
-// wmaps[i] may be null (the weight map is then encoded per call).
-int matmul_q4_0(cudaStream_t st, uint32_t* err, int nmat, const void* const* w, const CUtensorMap* const* wmaps,
-                const int64_t* rows, int64_t K, const __half* x, int M, float* const* y, const int64_t* ldy,
-                bool accumulate);
-// fp32 -> fp16, n % 4 == 0, both 16-byte aligned.
-int to_half(cudaStream_t st, const float* x, __half* y, int64_t n);
+// M tokens and nmat <= 3 matrices of one weight type (Q4_0 or Q4_K) with the
+// same K (K % 256 == 0); x is fp16 [M][K] (16-byte aligned), y[i] fp32
+// [M][ldy[i]].  Token t's results are multiplied by xs[t] (x's inverse row
+// scale) when xs is not null.  wmaps[i] may be null (the weight map is then
+// encoded per call).
+int matmul_quant(cudaStream_t st, uint32_t* err, int type, int nmat, const void* const* w,
+                 const CUtensorMap* const* wmaps, const int64_t* rows, int64_t K, const __half* x, const float* xs,
+                 int M, float* const* y, const int64_t* ldy, bool accumulate);
+inline bool matmul_type_ok(int type) { return type == CN_TYPE_Q4_0 || type == CN_TYPE_Q4_K; }
+// M rows of n fp32 values -> fp16 rows scaled by a power of two each, the
+// inverses in inv[M] (prefill.cu); n % 4 == 0, x and y 16-byte aligned.
+int to_half_rows(cudaStream_t st, const float* x, __half* y, float* inv, int n, int M);
 
 // Prefill kernels around the matmul (prefill.cu).
-int prefill_norm(cudaStream_t st, const float* x, const float* w, __half* y, int n, int M, float eps);
-int prefill_silu(cudaStream_t st, const float* g, const float* u, __half* h, int64_t n);
+int prefill_norm(cudaStream_t st, const float* x, const float* w, __half* y, float* inv, int n, int M,
+                 float eps);
+int prefill_silu(cudaStream_t st, const float* g, const float* u, __half* h, float* inv, int n, int M);
 // RoPE of the M prompt tokens' q (in place) and k, k/v into the cache and
 // their fp16 copies into kh/vh [M][kvdim].
 int prefill_rope(cudaStream_t st, float* q, const float* k, const float* v, const float2* rope, int pos0, int M,

@@ -73,6 +73,7 @@ struct cn_llama {
           *pf_u = nullptr;
     __half *pf_h = nullptr, *pf_kh = nullptr, *pf_vh = nullptr;
     int* pf_tok = nullptr;
+    float* pf_xs = nullptr;  // [pf_cap] inverse row scales of pf_h
 };
 
 namespace cn {
@@ -427,7 +428,7 @@ static void free_model(cn_llama* m) {
                     m->gate, m->up, m->logits, m->part, m->tokens, m->pos, m->amax,
                     m->gb.xfrag, m->gb.xsum, m->gb.partials, m->gb.counters, m->gb.xinv,
                     m->pf_x, m->pf_q, m->pf_k, m->pf_v, m->pf_g, m->pf_u, m->pf_h, m->pf_kh, m->pf_vh,
-                    m->pf_tok};
+                    m->pf_tok, m->pf_xs};
     for (void* p : bufs) cudaFree(p);
     cudaFreeHost(m->h_tokens);
     cudaFreeHost(m->h_pos);
@@ -440,8 +441,8 @@ static void free_model(cn_llama* m) {
 // A weight tensor's TMA descriptor, or null (the matmul then encodes one).
 static const CUtensorMap* wmap(const cn_tensor* t) { return t->has_map ? &t->map : nullptr; }
 
-// Whether the model's projections can run on the prefill matmul (Q4_0 with
-// inner dimensions that are multiples of 256, one GPU).
+// Whether the model's projections can run on the prefill matmul (Q4_0 or
+// Q4_K with inner dimensions that are multiples of 256, one GPU).
 static bool prefill_supported(const cn_llama* m) {
     if (m->tp && m->tp->size > 1) return false;
     const cn_llama_config& c = m->cfg;
@@ -449,19 +450,52 @@ static bool prefill_supported(const cn_llama* m) {
         return false;
     for (int l = 0; l < c.n_layers; l++)
         for (int j : {L_Q, L_K, L_V, L_O, L_GATE, L_UP, L_DOWN})
-            if (LT(m, l, j)->type != CN_TYPE_Q4_0) return false;
+            if (!matmul_type_ok(LT(m, l, j)->type)) return false;
     return true;
 }
+
+// One launch group of layer l's projections (q/k/v, o, gate/up or down, all
+// with inner dimension K) on the fp16 rows m->pf_h, whose inverse row scales
+// are m->pf_xs when `scaled`: one matmul launch per run of matrices of the
+// same weight type (a single launch when the group's types agree).  With
+// count_only, returns the number of launches instead.
+static int mm_group(cn_llama* m, int l, int nmat, const int* slots, const int64_t* rows, int64_t K, int n,
+                    float* const* y, const int64_t* ldy, bool accumulate, bool scaled, bool count_only = false) {
+    int launches = 0;
+    for (int i = 0; i < nmat;) {
+        const int type = LT(m, l, slots[i])->type;
+        int j = i + 1;
+        while (j < nmat && LT(m, l, slots[j])->type == type) j++;
+        launches++;
+        if (!count_only) {
+            const void* w[3];
+            const CUtensorMap* wm[3];
+            for (int k = i; k < j; k++) {
+                w[k - i] = LT(m, l, slots[k])->d;
+                wm[k - i] = wmap(LT(m, l, slots[k]));
+            }
+            int rc = matmul_quant(m->ctx->stream, m->ctx->dev_err, type, j - i, w, wm, rows + i, K, m->pf_h,
+                                  scaled ? m->pf_xs : nullptr, n, y + i, ldy + i, accumulate);
+            if (rc) return rc;
+        }
+        i = j;
+    }
+    return count_only ? launches : CN_OK;
+}
+
+static const int kSlotsQKV[3] = {L_Q, L_K, L_V}, kSlotsO[1] = {L_O}, kSlotsGU[2] = {L_GATE, L_UP},
+                 kSlotsDown[1] = {L_DOWN};
 
 static int prefill_reserve(cn_llama* m, int n) {
     if (n <= m->pf_cap) return CN_OK;
     CN_CUDA(cudaStreamSynchronize(m->ctx->stream));
     void* old[] = {m->pf_x, m->pf_q, m->pf_k, m->pf_v, m->pf_g, m->pf_u, m->pf_h, m->pf_kh, m->pf_vh,
-                   m->pf_tok};
+                   m->pf_tok, m->pf_xs};
     for (void* p : old) cudaFree(p);
     m->pf_x = m->pf_q = m->pf_k = m->pf_v = m->pf_g = m->pf_u = nullptr;
     m->pf_h = m->pf_kh = m->pf_vh = nullptr;
     m->pf_tok = nullptr;
+    m->pf_xs = nullptr;
     m->pf_cap = 0;
     const cn_llama_config& c = m->cfg;
     const size_t N = (size_t)n;
@@ -476,7 +510,8 @@ static int prefill_reserve(cn_llama* m, int n) {
         (rc = dmalloc((void**)&m->pf_h, N * hmax * 2, false)) ||
         (rc = dmalloc((void**)&m->pf_kh, N * m->kvdim * 2, false)) ||
         (rc = dmalloc((void**)&m->pf_vh, N * m->kvdim * 2, false)) ||
-        (rc = dmalloc((void**)&m->pf_tok, N * 4, false)))
+        (rc = dmalloc((void**)&m->pf_tok, N * 4, false)) ||
+        (rc = dmalloc((void**)&m->pf_xs, N * 4, false)))
         return rc;
     m->pf_cap = n;
     return CN_OK;
@@ -492,19 +527,17 @@ static int prefill_reserve(cn_llama* m, int n) {
 static int prefill_layers(cn_llama* m, int n, int pos) {
     const cn_llama_config& c = m->cfg;
     cudaStream_t s = m->ctx->stream;
-    uint32_t* err = m->ctx->dev_err;
     const int qd = m->qdim, kvd = m->kvdim, hid = c.hidden_dim;
     int rc;
     for (int l = 0; l < c.n_layers; l++) {
         const int64_t cache_off = (int64_t)l * c.ctx_len * kvd;  // sequence slot 0
-        if ((rc = prefill_norm(s, m->pf_x, (const float*)LT(m, l, L_ANORM)->d, m->pf_h, c.dim, n, c.rms_eps)))
+        if ((rc = prefill_norm(s, m->pf_x, (const float*)LT(m, l, L_ANORM)->d, m->pf_h, m->pf_xs, c.dim, n,
+                               c.rms_eps)))
             return rc;
         {
-            const void* w[3] = {LT(m, l, L_Q)->d, LT(m, l, L_K)->d, LT(m, l, L_V)->d};
-            const CUtensorMap* wm[3] = {wmap(LT(m, l, L_Q)), wmap(LT(m, l, L_K)), wmap(LT(m, l, L_V))};
             const int64_t rows[3] = {qd, kvd, kvd};
             float* y[3] = {m->pf_q, m->pf_k, m->pf_v};
-            if ((rc = matmul_q4_0(s, err, 3, w, wm, rows, c.dim, m->pf_h, n, y, rows, false))) return rc;
+            if ((rc = mm_group(m, l, 3, kSlotsQKV, rows, c.dim, n, y, rows, false, true))) return rc;
         }
         if ((rc = prefill_rope(s, m->pf_q, m->pf_k, m->pf_v, m->rope, pos, n, qd, kvd, c.head_dim, m->kc, m->vc,
                                cache_off, c.kv_dtype == CN_KV_F16, m->pf_kh, m->pf_vh)))
@@ -513,33 +546,41 @@ static int prefill_layers(cn_llama* m, int n, int pos) {
                                     m->nkv, c.head_dim, n, pos, m->pf_kh, m->pf_vh, m->pf_h, qd)))
             return rc;
         {
-            const void* w = LT(m, l, L_O)->d;
-            const CUtensorMap* wm = wmap(LT(m, l, L_O));
             const int64_t rows = c.dim;
-            if ((rc = matmul_q4_0(s, err, 1, &w, &wm, &rows, qd, m->pf_h, n, &m->pf_x, &rows, true))) return rc;
+            if ((rc = mm_group(m, l, 1, kSlotsO, &rows, qd, n, &m->pf_x, &rows, true, false))) return rc;
         }
-        if ((rc = prefill_norm(s, m->pf_x, (const float*)LT(m, l, L_FNORM)->d, m->pf_h, c.dim, n, c.rms_eps)))
+        if ((rc = prefill_norm(s, m->pf_x, (const float*)LT(m, l, L_FNORM)->d, m->pf_h, m->pf_xs, c.dim, n,
+                               c.rms_eps)))
             return rc;
         {
-            const void* w[2] = {LT(m, l, L_GATE)->d, LT(m, l, L_UP)->d};
-            const CUtensorMap* wm[2] = {wmap(LT(m, l, L_GATE)), wmap(LT(m, l, L_UP))};
             const int64_t rows[2] = {hid, hid};
             float* y[2] = {m->pf_g, m->pf_u};
-            if ((rc = matmul_q4_0(s, err, 2, w, wm, rows, c.dim, m->pf_h, n, y, rows, false))) return rc;
+            if ((rc = mm_group(m, l, 2, kSlotsGU, rows, c.dim, n, y, rows, false, true))) return rc;
         }
-        if ((rc = prefill_silu(s, m->pf_g, m->pf_u, m->pf_h, (int64_t)n * hid))) return rc;
+        if ((rc = prefill_silu(s, m->pf_g, m->pf_u, m->pf_h, m->pf_xs, hid, n))) return rc;
         {
-            const void* w = LT(m, l, L_DOWN)->d;
-            const CUtensorMap* wm = wmap(LT(m, l, L_DOWN));
             const int64_t rows = c.dim;
-            if ((rc = matmul_q4_0(s, err, 1, &w, &wm, &rows, hid, m->pf_h, n, &m->pf_x, &rows, true))) return rc;
+            if ((rc = mm_group(m, l, 1, kSlotsDown, &rows, hid, n, &m->pf_x, &rows, true, true))) return rc;
         }
     }
     return CN_OK;
 }
 
-// Kernels one prefill_layers call launches (10 per layer).
-static int prefill_kernels(const cn_llama* m) { return 10 * m->cfg.n_layers; }
+// Kernels one prefill_layers call launches: 6 per layer besides the matmuls,
+// and one matmul per same-type run of each projection group (4 per layer
+// when every group's types agree).
+static int prefill_kernels(const cn_llama* m) {
+    cn_llama* mm = const_cast<cn_llama*>(m);
+    const int64_t r[3] = {0, 0, 0};
+    float* y[3] = {nullptr, nullptr, nullptr};
+    int k = 0;
+    for (int l = 0; l < m->cfg.n_layers; l++)
+        k += 6 + mm_group(mm, l, 3, kSlotsQKV, r, 0, 0, y, r, false, false, true) +
+             mm_group(mm, l, 1, kSlotsO, r, 0, 0, y, r, false, false, true) +
+             mm_group(mm, l, 2, kSlotsGU, r, 0, 0, y, r, false, false, true) +
+             mm_group(mm, l, 1, kSlotsDown, r, 0, 0, y, r, false, false, true);
+    return k;
+}
 
 }  // namespace cn
 
@@ -939,31 +980,26 @@ int cn_llama_time_matmul(cn_llama* m, int group, int n, int iters, float* us_per
     cudaStream_t s = m->ctx->stream;
     CN_CUDA(cudaMemsetAsync(m->pf_h, 0, (size_t)n * (hid > dim ? hid : dim) * 2, s));
     CN_CUDA(cudaMemsetAsync(m->pf_x, 0, (size_t)n * dim * 4, s));
+    CN_CUDA(cudaMemsetAsync(m->pf_xs, 0, (size_t)n * 4, s));
     const int L = c.n_layers;
     double flops = 0;
     auto launch = [&](int i) -> int {
         const int l = i % L;
         if (group == 0) {
-            const void* w[3] = {LT(m, l, L_Q)->d, LT(m, l, L_K)->d, LT(m, l, L_V)->d};
             const int64_t rows[3] = {qd, kvd, kvd};
             float* y[3] = {m->pf_q, m->pf_k, m->pf_v};
             flops = 2.0 * n * (double)(qd + 2 * kvd) * dim;
-            const CUtensorMap* wm[3] = {wmap(LT(m, l, L_Q)), wmap(LT(m, l, L_K)), wmap(LT(m, l, L_V))};
-            return matmul_q4_0(s, m->ctx->dev_err, 3, w, wm, rows, dim, m->pf_h, n, y, rows, false);
+            return mm_group(m, l, 3, kSlotsQKV, rows, dim, n, y, rows, false, true);
         }
         if (group == 2) {
-            const void* w[2] = {LT(m, l, L_GATE)->d, LT(m, l, L_UP)->d};
             const int64_t rows[2] = {hid, hid};
             float* y[2] = {m->pf_g, m->pf_u};
             flops = 2.0 * n * (double)(2 * hid) * dim;
-            const CUtensorMap* wm[2] = {wmap(LT(m, l, L_GATE)), wmap(LT(m, l, L_UP))};
-            return matmul_q4_0(s, m->ctx->dev_err, 2, w, wm, rows, dim, m->pf_h, n, y, rows, false);
+            return mm_group(m, l, 2, kSlotsGU, rows, dim, n, y, rows, false, true);
         }
-        const void* w = LT(m, l, group == 1 ? L_O : L_DOWN)->d;
-        const CUtensorMap* wm = wmap(LT(m, l, group == 1 ? L_O : L_DOWN));
         const int64_t rows = dim, K = group == 1 ? qd : hid;
         flops = 2.0 * n * (double)dim * K;
-        return matmul_q4_0(s, m->ctx->dev_err, 1, &w, &wm, &rows, K, m->pf_h, n, &m->pf_x, &rows, true);
+        return mm_group(m, l, 1, group == 1 ? kSlotsO : kSlotsDown, &rows, K, n, &m->pf_x, &rows, true, group == 3);
     };
     for (int i = 0; i < 3; i++)
         if ((rc = launch(i))) return rc;

@@ -1,10 +1,14 @@
-// matmul.cu -- prefill: Q4_0 dequant-matmul on the 5th-generation tensor
-// cores (tcgen05, tensor memory, TMA).
+// matmul.cu -- prefill: Q4_0 / Q4_K dequant-matmul on the 5th-generation
+// tensor cores (tcgen05, tensor memory, TMA).
 //
 // Y[m][n] (+)= sum_k X[m][k] * W[n][k] for M tokens in one pass: the batched
-// form of TensorMath.MatVecMulQ4_0 (Tensors/TensorMath.cs:548-578) with the
-// weights of DequantQ4_0.Dequantize (Tensors/Quantization/DequantQ4_0.cs:28-58),
-// which ChatNet runs as M sequential matvecs (InferenceEngine.cs:235-239).
+// form of TensorMath.MatVecMulQ4_0 / MatVecMulGeneric(Q4_K)
+// (Tensors/TensorMath.cs:548-578, :624-656) with the weights of
+// DequantQ4_0.Dequantize (Tensors/Quantization/DequantQ4_0.cs:28-58) or
+// DequantQ4K.Dequantize (DequantQ4K.cs:37-77), which ChatNet runs as M
+// sequential matvecs (InferenceEngine.cs:235-239).  Both formats store 256
+// weights of a row in 144 bytes (8 Q4_0 blocks, or one Q4_K super-block), so
+// the raw ring is the same; only the expansion differs.
 //
 //  * A tile is 128 weight rows x 128 tokens.  The kernel is persistent: one
 //    CTA per SM walks the tiles (weight row tile-major, so the CTAs running
@@ -89,6 +93,7 @@ struct Args {
     float* y[kMaxMats];         // [M][ldy[m]]
     int64_t ldy[kMaxMats];
     int64_t rb;                 // bytes per weight row (K / 32 * 18)
+    const float* xs;            // per-token factor of the result (x's inverse scale), or null
     int M, K;                   // K % 256 == 0
     int accumulate;             // 1: Y += result, 0: Y = result
     int tok_tiles;              // token tiles of 128; tile t = row tile t / tok_tiles, token tile t % tok_tiles
@@ -138,6 +143,32 @@ __device__ __forceinline__ void expand_q4_0_pair(const uint32_t (&wd)[9], uint32
                 const uint32_t hi = lop3_and_or(t >> 4, 0x000F000Fu, kMagic);
                 o[16 * blk + 2 * i + h] = h2_mul(h2_sub(lo, kBias), d2);      // (q - 8) exact, then * d
                 o[16 * blk + 8 + 2 * i + h] = h2_mul(h2_sub(hi, kBias), d2);
+            }
+        }
+    }
+}
+
+// Expands two Q4_K sub-blocks into 64 fp16 weights in K order (o[c] holds
+// positions 2c, 2c + 1).  qw[0..3] and qw[4..7] are the sub-blocks' 16 quant
+// bytes each (DequantQ4K.cs:59-71: position j < 16 is the low nibble of byte
+// j, 16 + j its high nibble).  The weight d * sc * q - dmin * m is formed as
+// fma(sc * q, d, -fp16(dmin * m)): q, sc * q (<= 945) and d are exact in
+// fp16, so only the sub-block's minimum term and the result are rounded.
+// d2: d in both halves; sc2/ndm2: the sub-blocks' sc and -dmin * m pairs.
+__device__ __forceinline__ void expand_q4k_pair(const uint32_t (&qw)[8], uint32_t d2, const uint32_t (&sc2)[2],
+                                                const uint32_t (&ndm2)[2], uint32_t (&o)[32]) {
+    constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024 in both halves
+#pragma unroll
+    for (int blk = 0; blk < 2; blk++) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const uint32_t t = __byte_perm(qw[4 * blk + i], 0u, h ? 0x4342u : 0x4140u);
+                const uint32_t lo = h2_mul(h2_sub(lop3_and_or(t, 0x000F000Fu, kMagic), kMagic), sc2[blk]);
+                const uint32_t hi = h2_mul(h2_sub(lop3_and_or(t >> 4, 0x000F000Fu, kMagic), kMagic), sc2[blk]);
+                o[16 * blk + 2 * i + h] = h2_fma(lo, d2, ndm2[blk]);
+                o[16 * blk + 8 + 2 * i + h] = h2_fma(hi, d2, ndm2[blk]);
             }
         }
     }
@@ -221,8 +252,9 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t addr) {
 
 }  // namespace mm
 
+template <int WT>
 __global__ void __launch_bounds__(mm::kThreads, 1)
-    matmul_q4_0_kernel(const __grid_constant__ mm::Maps maps, const mm::Args a) {
+    matmul_q_kernel(const __grid_constant__ mm::Maps maps, const mm::Args a) {
     using namespace mm;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -383,6 +415,14 @@ __global__ void __launch_bounds__(mm::kThreads, 1)
                     tc_fence_before();
                     if (lane == 0) mbar_arrive(&dempty[db]);
                 }
+                if (a.xs) {
+                    // undo token t's activation scaling (an exact power of two)
+                    const int tk = tok0 + 32 * j + lane;
+                    const float sc = tk < a.M ? a.xs[tk] : 1.f;
+#pragma unroll
+                    for (int u = 0; u < 32; u++)
+                        v[u] = __float_as_uint(__uint_as_float(v[u]) * __shfl_sync(0xffffffffu, sc, u));
+                }
                 if (live) {
                     float* p = y + (size_t)(tok0 + 32 * j) * ldy + row;
                     const int nt = a.M - (tok0 + 32 * j);  // tokens of this chunk inside M
@@ -420,14 +460,52 @@ __global__ void __launch_bounds__(mm::kThreads, 1)
                     failed = true;
                 }
                 // this thread's words of its row (rows past the matrix arrive as
-                // zeros): blocks 4q + 2wg, 4q + 2wg + 1 of stage q = words
-                // 18q + 9wg .. 18q + 9wg + 8 of the row's 36
-                const uint32_t* src = reinterpret_cast<const uint32_t*>(raw + rs * kRaw + r * 144) + 9 * wg;
+                // zeros).  Q4_0: blocks 4q + 2wg, 4q + 2wg + 1 of stage q = words
+                // 18q + 9wg .. 18q + 9wg + 8 of the row's 36.  Q4_K: the header
+                // (words 0-3: d, dmin, packed scales) and sub-blocks 4q + 2wg,
+                // 4q + 2wg + 1 = words 4 + 16q + 8wg .. +7.
+                const uint32_t* row32 = reinterpret_cast<const uint32_t*>(raw + rs * kRaw + r * 144);
                 uint32_t cur[18];
+                uint32_t d2 = 0, sc2[2][2], ndm2[2][2];  // Q4_K: d, [stage][sub-block] sc and -dmin * m
+                if (WT == CN_TYPE_Q4_0) {
 #pragma unroll
-                for (int q = 0; q < 2; q++)
+                    for (int q = 0; q < 2; q++)
 #pragma unroll
-                    for (int k = 0; k < 9; k++) cur[9 * q + k] = src[18 * q + k];
+                        for (int k = 0; k < 9; k++) cur[9 * q + k] = row32[9 * wg + 18 * q + k];
+                } else {
+                    uint32_t hw[4];
+#pragma unroll
+                    for (int k = 0; k < 4; k++) hw[k] = row32[k];
+#pragma unroll
+                    for (int q = 0; q < 2; q++)
+#pragma unroll
+                        for (int k = 0; k < 8; k++) cur[8 * q + k] = row32[4 + 16 * q + 8 * wg + k];
+                    // DequantQ4K.DecodeScales (DequantQ4K.cs:218-241) for this
+                    // thread's four sub-blocks (byte b of the 12 scale bytes is
+                    // byte b % 4 of word 1 + b / 4; stage 0 holds sub-blocks
+                    // j < 4, stage 1 those >= 4), then sc and dmin * m
+                    d2 = (hw[0] & 0xFFFFu) * 0x10001u;
+                    const float dmin = half_bits_to_float((uint16_t)(hw[0] >> 16));
+#pragma unroll
+                    for (int q = 0; q < 2; q++)
+#pragma unroll
+                        for (int e = 0; e < 2; e++) {
+                            const int sh = 8 * (2 * wg + e);  // byte j % 4 of a word
+                            const int b0 = (int)(hw[1] >> sh) & 0xFF, b1 = (int)(hw[2] >> sh) & 0xFF;
+                            int sc, mm_;
+                            if (q == 0) {
+                                sc = b0 & 63;
+                                mm_ = b1 & 63;
+                            } else {
+                                const int b2 = (int)(hw[3] >> sh) & 0xFF;
+                                sc = (b2 & 0xF) | ((b0 >> 6) << 4);
+                                mm_ = (b2 >> 4) | ((b1 >> 6) << 4);
+                            }
+                            const float dm = __fmul_rn(dmin, (float)mm_);
+                            sc2[q][e] = pack_half2((float)sc, (float)sc);
+                            ndm2[q][e] = pack_half2(-dm, -dm);
+                        }
+                }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&raw_empty[rs]);
 #pragma unroll
@@ -439,10 +517,18 @@ __global__ void __launch_bounds__(mm::kThreads, 1)
                         failed = true;
                     }
                     tc_fence_after();
-                    uint32_t wd[9], o[32];
+                    uint32_t o[32];
+                    if (WT == CN_TYPE_Q4_0) {
+                        uint32_t wd[9];
 #pragma unroll
-                    for (int k = 0; k < 9; k++) wd[k] = cur[9 * q + k];
-                    expand_q4_0_pair(wd, o);
+                        for (int k = 0; k < 9; k++) wd[k] = cur[9 * q + k];
+                        expand_q4_0_pair(wd, o);
+                    } else {
+                        uint32_t qw[8];
+#pragma unroll
+                        for (int k = 0; k < 8; k++) qw[k] = cur[8 * q + k];
+                        expand_q4k_pair(qw, d2, sc2[q], ndm2[q], o);
+                    }
                     tmem_st32(lane_base + kACol + slot * kACols + 32 * wg, o);
                     // warp-wide: every lane's stores of this stage are done
                     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -462,19 +548,6 @@ __global__ void __launch_bounds__(mm::kThreads, 1)
     }
 }
 
-// fp32 -> fp16 rows (the activation operand of the matmul).
-__global__ void to_half_kernel(const float* __restrict__ x, __half* __restrict__ y, int64_t n4) {
-    pdl_wait();
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const float4 v = reinterpret_cast<const float4*>(x)[i];
-        uint2 o;
-        o.x = pack_half2(v.x, v.y);
-        o.y = pack_half2(v.z, v.w);
-        reinterpret_cast<uint2*>(y)[i] = o;
-    }
-}
-
 // ---- host side ------------------------------------------------------------------
 
 int encode_act_map(const __half* x, int M, int64_t K, CUtensorMap* out) {
@@ -487,22 +560,18 @@ int encode_act_map(const __half* x, int M, int64_t K, CUtensorMap* out) {
                            box, CU_TENSOR_MAP_SWIZZLE_128B, out);
 }
 
-int to_half(cudaStream_t st, const float* x, __half* y, int64_t n) {
-    CN_CHECK(n % 4 == 0, CN_ERR_INVALID_ARG, "fp16 conversion needs a multiple of 4 values");
-    const int64_t n4 = n / 4;
-    const int blocks = (int)((n4 + 255) / 256 < 4096 ? (n4 + 255) / 256 : 4096);
-    CN_CUDA(launch_k(false, to_half_kernel, dim3(blocks > 0 ? blocks : 1), dim3(256), 0, st, x, y, n4));
-    return CN_OK;
-}
-
-int matmul_q4_0(cudaStream_t st, uint32_t* err, int nmat, const void* const* w, const CUtensorMap* const* wmaps,
-                const int64_t* rows, int64_t K, const __half* x, int M, float* const* y, const int64_t* ldy,
-                bool accumulate) {
+int matmul_quant(cudaStream_t st, uint32_t* err, int type, int nmat, const void* const* w,
+                 const CUtensorMap* const* wmaps, const int64_t* rows, int64_t K, const __half* x, const float* xs,
+                 int M, float* const* y, const int64_t* ldy, bool accumulate) {
+    CN_CHECK(type == CN_TYPE_Q4_0 || type == CN_TYPE_Q4_K, CN_ERR_UNSUPPORTED,
+             "matmul: weight type %d (Q4_0 or Q4_K)", type);
     CN_CHECK(nmat >= 1 && nmat <= mm::kMaxMats && K > 0 && K % 256 == 0 && M >= 1, CN_ERR_INVALID_ARG,
              "matmul: bad shape (nmat %d, K %lld, M %d)", nmat, (long long)K, M);
     static bool attr = false;
     if (!attr) {
-        CN_CUDA(cudaFuncSetAttribute(matmul_q4_0_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        CN_CUDA(cudaFuncSetAttribute(matmul_q_kernel<CN_TYPE_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     mm::kSmem));
+        CN_CUDA(cudaFuncSetAttribute(matmul_q_kernel<CN_TYPE_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      mm::kSmem));
         attr = true;
     }
@@ -517,7 +586,7 @@ int matmul_q4_0(cudaStream_t st, uint32_t* err, int nmat, const void* const* w, 
         if (wmaps && wmaps[mi]) {
             maps.w[i] = *wmaps[mi];
         } else {
-            int rc = encode_weight_map(CN_TYPE_Q4_0, w[mi], rows[mi], (uint64_t)(K / 32 * 18), &maps.w[i]);
+            int rc = encode_weight_map(type, w[mi], rows[mi], (uint64_t)(K / 32 * 18), &maps.w[i]);
             if (rc) return rc;
         }
         a.rows[i] = rows[mi];
@@ -533,6 +602,7 @@ int matmul_q4_0(cudaStream_t st, uint32_t* err, int nmat, const void* const* w, 
     a.tok_tiles = (M + mm::kNT - 1) / mm::kNT;
     a.tiles = tiles * a.tok_tiles;
     a.rb = K / 32 * 18;
+    a.xs = xs;
     a.M = M;
     a.K = (int)K;
     a.accumulate = accumulate ? 1 : 0;
@@ -546,7 +616,10 @@ int matmul_q4_0(cudaStream_t st, uint32_t* err, int nmat, const void* const* w, 
         CN_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     }
     const dim3 grid(a.tiles < sms ? a.tiles : sms);  // persistent: one CTA per SM
-    CN_CUDA(launch_k(false, matmul_q4_0_kernel, grid, dim3(mm::kThreads), (size_t)mm::kSmem, st, maps, a));
+    if (type == CN_TYPE_Q4_0)
+        CN_CUDA(launch_k(false, matmul_q_kernel<CN_TYPE_Q4_0>, grid, dim3(mm::kThreads), (size_t)mm::kSmem, st, maps, a));
+    else
+        CN_CUDA(launch_k(false, matmul_q_kernel<CN_TYPE_Q4_K>, grid, dim3(mm::kThreads), (size_t)mm::kSmem, st, maps, a));
     return CN_OK;
 }
 

@@ -4,7 +4,13 @@
 //   norm_half_kernel      TensorMath.RmsNorm (Tensors/TensorMath.cs:97-165), one
 //                         token per CTA, output rounded to fp16 for the matmul
 //   silu_half_kernel      TensorMath.SiluElementwiseMul (TensorMath.cs:253-286),
-//                         output rounded to fp16 for the down projection
+//                         one token per CTA, output rounded to fp16 for the
+//                         down projection
+//
+// Both scale each token's row by a power of two before rounding to fp16
+// (row_pow2_scale) and leave the inverse in inv[t]; the matmul multiplies
+// token t's results by it, so activations of any magnitude keep fp16's
+// relative precision (SwiGLU products of synthetic weights exceed 65504).
 //   attn_prefill_kernel   LlamaModel.ComputeAttention + TensorMath.Softmax
 //                         (Models/Llama/LlamaModel.cs:241-346, TensorMath.cs:177-241)
 //                         for M queries at positions pos0..pos0+M-1 with causal
@@ -41,21 +47,24 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
 
 }  // namespace
 
-// y[t] = fp16(RmsNorm(x[t]) * w), the reference's operation order; n % 4 == 0.
+// y[t] = fp16(s_t * RmsNorm(x[t]) * w), the reference's operation order, and
+// inv[t] = 1 / s_t; n % 4 == 0.  s_t comes from rms * max|x * w|, the row's
+// largest output up to rounding.
 __global__ void norm_half_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                 __half* __restrict__ y, int n, float eps) {
+                                 __half* __restrict__ y, float* __restrict__ inv, int n, float eps) {
     __shared__ float red[32];
     const float4* xr = reinterpret_cast<const float4*>(x + (size_t)blockIdx.x * n);
     const float4* w4 = reinterpret_cast<const float4*>(w);
     uint2* yr = reinterpret_cast<uint2*>(y + (size_t)blockIdx.x * n);
     const int n4 = n / 4;
-    float ss = 0.f;
+    float ss = 0.f, xw = 0.f;
     for (int i = threadIdx.x; i < n4; i += blockDim.x) {
-        const float4 v = xr[i];
+        const float4 v = xr[i], g = w4[i];
         ss = fmaf(v.x, v.x, ss);
         ss = fmaf(v.y, v.y, ss);
         ss = fmaf(v.z, v.z, ss);
         ss = fmaf(v.w, v.w, ss);
+        xw = fmaxf(xw, absmax4(make_float4(v.x * g.x, v.y * g.y, v.z * g.z, v.w * g.w)));
     }
     ss = pf_warp_sum(ss);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
@@ -63,31 +72,69 @@ __global__ void norm_half_kernel(const float* __restrict__ x, const float* __res
     float tot = 0.f;
     for (int i = 0; i < (int)(blockDim.x >> 5); i++) tot += red[i];
     const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), eps)));
+    float sc, iv;
+    row_pow2_scale(block_absmax(xw, red) * rms, sc, iv);
     for (int i = threadIdx.x; i < n4; i += blockDim.x) {
         const float4 v = xr[i], g = w4[i];
         uint2 o;
-        o.x = pack_half2(__fmul_rn(__fmul_rn(v.x, rms), g.x), __fmul_rn(__fmul_rn(v.y, rms), g.y));
-        o.y = pack_half2(__fmul_rn(__fmul_rn(v.z, rms), g.z), __fmul_rn(__fmul_rn(v.w, rms), g.w));
+        o.x = pack_half2(__fmul_rn(__fmul_rn(v.x, rms), g.x) * sc, __fmul_rn(__fmul_rn(v.y, rms), g.y) * sc);
+        o.y = pack_half2(__fmul_rn(__fmul_rn(v.z, rms), g.z) * sc, __fmul_rn(__fmul_rn(v.w, rms), g.w) * sc);
         yr[i] = o;
     }
+    if (threadIdx.x == 0) inv[blockIdx.x] = iv;
 }
 
 __device__ __forceinline__ float silu_mul1(float g, float u) {
     return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
 }
 
-// h = fp16(g / (1 + exp(-g)) * u), four values per thread; n % 4 == 0.
+// h[t] = fp16(s_t * g / (1 + exp(-g)) * u) for token t's row of n values and
+// inv[t] = 1 / s_t; n % 4 == 0.  s_t comes from max(max(|g|, 0.2785) * |u|),
+// a bound on the row's largest output: silu(g) <= g for g >= 0 and
+// |silu(g)| < 0.2785 for g < 0.  The second pass re-reads g and u (cache hits).
 __global__ void silu_half_kernel(const float* __restrict__ g, const float* __restrict__ u,
-                                 __half* __restrict__ h, int64_t n) {
-    const int64_t n4 = n / 4;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const float4 a = reinterpret_cast<const float4*>(g)[i], b = reinterpret_cast<const float4*>(u)[i];
-        uint2 o;
-        o.x = pack_half2(silu_mul1(a.x, b.x), silu_mul1(a.y, b.y));
-        o.y = pack_half2(silu_mul1(a.z, b.z), silu_mul1(a.w, b.w));
-        reinterpret_cast<uint2*>(h)[i] = o;
+                                 __half* __restrict__ h, float* __restrict__ inv, int n) {
+    __shared__ float red[32];
+    const size_t base = (size_t)blockIdx.x * n;
+    const float4* g4 = reinterpret_cast<const float4*>(g + base);
+    const float4* u4 = reinterpret_cast<const float4*>(u + base);
+    uint2* h2 = reinterpret_cast<uint2*>(h + base);
+    const int n4 = n / 4;
+    constexpr float kNegMax = 0.2785f;
+    float bound = 0.f;
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        const float4 a = g4[i], b = u4[i];
+        bound = fmaxf(bound, absmax4(make_float4(fmaxf(fabsf(a.x), kNegMax) * b.x, fmaxf(fabsf(a.y), kNegMax) * b.y,
+                                                 fmaxf(fabsf(a.z), kNegMax) * b.z, fmaxf(fabsf(a.w), kNegMax) * b.w)));
     }
+    float sc, iv;
+    row_pow2_scale(block_absmax(bound, red), sc, iv);
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        const float4 a = g4[i], b = u4[i];
+        h2[i] = make_uint2(pack_half2(silu_mul1(a.x, b.x) * sc, silu_mul1(a.y, b.y) * sc),
+                           pack_half2(silu_mul1(a.z, b.z) * sc, silu_mul1(a.w, b.w) * sc));
+    }
+    if (threadIdx.x == 0) inv[blockIdx.x] = iv;
+}
+
+// fp16(s_t * x[t]) for M rows of n values (the activation operand of
+// cn_matmul) and inv[t] = 1 / s_t; n % 4 == 0.
+__global__ void half_rows_kernel(const float* __restrict__ x, __half* __restrict__ y, float* __restrict__ inv,
+                                 int n) {
+    __shared__ float red[32];
+    pdl_wait();
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)blockIdx.x * n);
+    uint2* yr = reinterpret_cast<uint2*>(y + (size_t)blockIdx.x * n);
+    const int n4 = n / 4;
+    float amax = 0.f;
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) amax = fmaxf(amax, absmax4(xr[i]));
+    float sc, iv;
+    row_pow2_scale(block_absmax(amax, red), sc, iv);
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        const float4 v = xr[i];
+        yr[i] = make_uint2(pack_half2(v.x * sc, v.y * sc), pack_half2(v.z * sc, v.w * sc));
+    }
+    if (threadIdx.x == 0) inv[blockIdx.x] = iv;
 }
 
 // TensorMath.ApplyRoPE (interleaved pairs) on the q and k rows of the n prompt
@@ -347,14 +394,22 @@ __global__ void __launch_bounds__(kPfThreads)
 
 // ---- host side ------------------------------------------------------------------
 
-int prefill_norm(cudaStream_t st, const float* x, const float* w, __half* y, int n, int M, float eps) {
-    CN_CUDA(launch_k(false, norm_half_kernel, dim3(M), dim3(256), 0, st, x, w, y, n, eps));
+int prefill_norm(cudaStream_t st, const float* x, const float* w, __half* y, float* inv, int n, int M,
+                 float eps) {
+    CN_CHECK(n % 4 == 0 && M >= 1, CN_ERR_INVALID_ARG, "prefill norm: shapes");
+    CN_CUDA(launch_k(false, norm_half_kernel, dim3(M), dim3(256), 0, st, x, w, y, inv, n, eps));
     return CN_OK;
 }
 
-int prefill_silu(cudaStream_t st, const float* g, const float* u, __half* h, int64_t n) {
-    const int64_t blocks = (n + 255) / 256 < 8192 ? (n + 255) / 256 : 8192;
-    CN_CUDA(launch_k(false, silu_half_kernel, dim3((unsigned)blocks), dim3(256), 0, st, g, u, h, n));
+int prefill_silu(cudaStream_t st, const float* g, const float* u, __half* h, float* inv, int n, int M) {
+    CN_CHECK(n % 4 == 0 && M >= 1, CN_ERR_INVALID_ARG, "prefill silu: shapes");
+    CN_CUDA(launch_k(false, silu_half_kernel, dim3(M), dim3(256), 0, st, g, u, h, inv, n));
+    return CN_OK;
+}
+
+int to_half_rows(cudaStream_t st, const float* x, __half* y, float* inv, int n, int M) {
+    CN_CHECK(n % 4 == 0 && M >= 1, CN_ERR_INVALID_ARG, "fp16 rows: shapes");
+    CN_CUDA(launch_k(false, half_rows_kernel, dim3(M), dim3(256), 0, st, x, y, inv, n));
     return CN_OK;
 }
 

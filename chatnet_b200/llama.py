@@ -106,6 +106,9 @@ class CudaLlamaModel:
             check(N.lib().cn_llama_create_tp(ctx.handle, C.byref(c), arr, len(tensors), tp.handle,
                                              C.byref(h)), "cn_llama_create_tp")
         self.handle = h.value
+        models = getattr(ctx, "_models", None)
+        if models is not None:
+            models.add(self)
 
     def prepare(self, batch: int) -> None:
         """Build and graph-capture the step without running it."""

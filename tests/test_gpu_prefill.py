@@ -18,10 +18,10 @@ from tests.parity import REL_TOL, rel_err
 pytestmark = pytest.mark.gpu
 
 
-def small(n_layers=2, kv_f16=False, ctx=256, head_dim=64, n_heads=4, n_kv=2):
+def small(n_layers=2, kv_f16=False, ctx=256, head_dim=64, n_heads=4, n_kv=2, wtype=cn.TYPE_Q4_0):
     m = LlamaConfig(dim=n_heads * head_dim, hidden_dim=512, n_layers=n_layers, n_heads=n_heads,
                     n_kv_heads=n_kv, head_dim=head_dim, vocab=500, ctx_len=ctx, kv_f16=kv_f16)
-    return cf.DecodeConfig(3, m, cn.TYPE_Q4_0, kv_filled=0, decode_pos=0, name="small-prefill")
+    return cf.DecodeConfig(3, m, wtype, kv_filled=0, decode_pos=0, name="small-prefill")
 
 
 class Rig:
@@ -82,6 +82,20 @@ def test_prefill_hidden_matches_sequential(ctx, oracle, n, head_dim, kv_f16):
     r.close()
 
 
+def test_prefill_q4_k_model(ctx, oracle):
+    """A Q4_K model (config 4's weight type) takes the same prefill path."""
+    dc = small(wtype=cn.TYPE_Q4_K, kv_f16=True)
+    r = Rig(ctx, oracle, dc)
+    assert r.gpu.prefill_kernels() == 10 * dc.model.n_layers
+    x = cf.prefill_x(dc, 90)
+    _check_tokens(r.prefill(x, 0), r.oracle.layers, x, 0)
+    toks = [cf.token(dc, 1, s) for s in range(24)]
+    got = r.gpu.forward(toks, 90)
+    ref = r.oracle.forward(toks, 90)
+    assert rel_err(got, ref) <= REL_TOL and int(np.argmax(got)) == int(np.argmax(ref))
+    r.close()
+
+
 def test_prefill_after_cached_positions(ctx, oracle):
     """A second prompt chunk attends to the first chunk's cache rows."""
     dc = small()
@@ -120,7 +134,7 @@ def test_prefill_config3_layer(ctx, oracle):
 
 
 def test_prefill_rejects_unsupported(ctx):
-    dc = cf.replace(small(), weight_type=cn.TYPE_Q4_K)
+    dc = cf.replace(small(), weight_type=cn.TYPE_Q6_K)
     ts = cf.device_tensors(ctx, dc)
     g = CudaLlamaModel(ctx, dc.model, ts)
     x = torch.zeros(20, 256, device="cuda")
