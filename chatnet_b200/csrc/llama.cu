@@ -788,7 +788,7 @@ int cn_llama_prefill_hidden_dev(cn_llama* m, const float* x_dev, int n, int pos,
     CN_CHECK(n >= 1 && pos >= 0 && pos + n <= m->cfg.ctx_len, CN_ERR_INVALID_ARG,
              "positions [%d, %d) outside the context of %d", pos, pos + n, m->cfg.ctx_len);
     CN_CHECK(prefill_supported(m), CN_ERR_UNSUPPORTED,
-             "prefill needs Q4_0 projections, dim and hidden_dim multiples of 256, head_dim 64 or 128, one GPU");
+             "prefill needs Q4_0 or Q4_K projections, dim and hidden_dim multiples of 256, head_dim 64 or 128, one GPU");
     cudaSetDevice(m->ctx->device);
     cudaStream_t s = m->ctx->stream;
     int rc = prefill_reserve(m, n);

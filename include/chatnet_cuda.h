@@ -153,9 +153,11 @@ int cn_matvec(cn_ctx* ctx, const cn_tensor* W, const float* host_x, float* host_
 /* Prefill matmul: y[t][r] = dot(W[r], x[t]) for n_tokens tokens at once (x
  * [n_tokens][cols] fp32, y [n_tokens][rows] fp32), the batched form of the
  * matvec that ChatNet runs once per prompt token (InferenceEngine.cs:235-239
- * -> TensorMath.MatVecMulQ4_0, Tensors/TensorMath.cs:548-578).  Runs on the
- * tcgen05 tensor cores: activations rounded to fp16, weights expanded to
- * fp16, fp32 accumulation.  Q4_0 weights with cols % 256 == 0. */
+ * -> TensorMath.MatVecMulQ4_0 / MatVecMulGeneric(Q4_K), Tensors/TensorMath.cs:
+ * 548-578, 624-656).  Runs on the tcgen05 tensor cores: each token's row
+ * scaled by a power of two and rounded to fp16, weights expanded to fp16,
+ * fp32 accumulation.  Q4_0 or Q4_K weights with cols % 256 == 0; other
+ * types return CN_ERR_UNSUPPORTED. */
 int cn_matmul(cn_ctx* ctx, const cn_tensor* W, const float* host_x, float* host_y, int n_tokens);
 
 /* ---- device level: device pointers, asynchronous ------------------------ */
@@ -229,8 +231,8 @@ int cn_llama_destroy(cn_llama* m);
 /* IModel.Forward (Abstractions/IModel.cs:18, LlamaModel.cs:93-238): runs the
  * n tokens of KV slot 0 at positions pos..pos+n-1 and writes the logits of
  * the last one to logits_host [vocab].  Prompts of 16 or more tokens on a
- * one-GPU model with Q4_0 projections run as one prefill pass (every layer
- * on the tcgen05 matmul for all n tokens, see cn_llama_prefill_hidden_dev);
+ * one-GPU model with Q4_0 or Q4_K projections run as one prefill pass (every
+ * layer on the tcgen05 matmul for all n tokens, see cn_llama_prefill_hidden_dev);
  * otherwise the tokens run one decode step at a time, as the reference does
  * (InferenceEngine.cs:235-239). */
 int cn_llama_forward(cn_llama* m, const int* tokens, int n, int pos, float* logits_host);
