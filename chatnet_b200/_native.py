@@ -35,8 +35,14 @@ TYPE_Q4_1 = 3
 TYPE_Q5_0 = 6
 TYPE_Q5_1 = 7
 TYPE_Q8_0 = 8
+TYPE_Q2_K = 10
+TYPE_Q3_K = 11
 TYPE_Q4_K = 12
+TYPE_Q5_K = 13
 TYPE_Q6_K = 14
+TYPE_Q8_K = 15
+TYPE_IQ4_NL = 20
+TYPE_IQ4_XS = 23
 
 DIST_CFG0_Q4_0 = 1
 DIST_CFG2_Q4_K = 2

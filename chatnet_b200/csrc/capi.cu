@@ -32,7 +32,7 @@ int cuda_error(cudaError_t e, const char* what) {
 
 bool type_supported(int type) {
     return type == CN_TYPE_Q4_0 || type == CN_TYPE_Q4_K || type == CN_TYPE_Q6_K ||
-           type == CN_TYPE_F32 || type == CN_TYPE_F16 || is_block32(type);
+           type == CN_TYPE_F32 || type == CN_TYPE_F16 || is_block32(type) || is_superblock(type);
 }
 
 uint64_t row_bytes(int type, int64_t cols) { return cn_byte_size(type, (uint64_t)cols); }
@@ -103,6 +103,12 @@ uint64_t cn_byte_size(int type, uint64_t elements) {
         case CN_TYPE_Q8_0: return (elements + 31) / 32 * 34;
         case CN_TYPE_Q4_K: return (elements + 255) / 256 * 144;
         case CN_TYPE_Q6_K: return (elements + 255) / 256 * 210;
+        case CN_TYPE_IQ4_NL: return (elements + 31) / 32 * 18;
+        case CN_TYPE_Q2_K:
+        case CN_TYPE_Q3_K:
+        case CN_TYPE_Q5_K:
+        case CN_TYPE_Q8_K:
+        case CN_TYPE_IQ4_XS: return (elements + 255) / 256 * superblock_bytes(type);
         default: return 0;
     }
 }

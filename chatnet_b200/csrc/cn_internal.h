@@ -70,10 +70,21 @@ namespace cn {
 uint64_t row_bytes(int type, int64_t cols);
 // The 32-weight block codecs decoded through the generic paths (formats.cuh).
 __host__ __device__ inline bool is_block32(int type) {
-    return type == CN_TYPE_Q4_1 || type == CN_TYPE_Q5_0 || type == CN_TYPE_Q5_1 || type == CN_TYPE_Q8_0;
+    return type == CN_TYPE_Q4_1 || type == CN_TYPE_Q5_0 || type == CN_TYPE_Q5_1 || type == CN_TYPE_Q8_0 ||
+           type == CN_TYPE_IQ4_NL;
 }
 __host__ __device__ inline int block32_bytes(int type) {
-    return type == CN_TYPE_Q4_1 ? 20 : type == CN_TYPE_Q5_0 ? 22 : type == CN_TYPE_Q5_1 ? 24 : 34;
+    return type == CN_TYPE_Q4_1 ? 20 : type == CN_TYPE_Q5_0 ? 22 : type == CN_TYPE_Q5_1 ? 24
+           : type == CN_TYPE_IQ4_NL ? 18 : 34;
+}
+// The 256-weight super-block codecs decoded through the generic paths.
+__host__ __device__ inline bool is_superblock(int type) {
+    return type == CN_TYPE_Q2_K || type == CN_TYPE_Q3_K || type == CN_TYPE_Q5_K || type == CN_TYPE_Q8_K ||
+           type == CN_TYPE_IQ4_XS;
+}
+__host__ __device__ inline int superblock_bytes(int type) {
+    return type == CN_TYPE_Q2_K ? 84 : type == CN_TYPE_Q3_K ? 110 : type == CN_TYPE_Q5_K ? 176
+           : type == CN_TYPE_Q8_K ? 292 : 136;
 }
 bool type_supported(int type);
 

@@ -116,6 +116,15 @@ __global__ void dequant_b32_kernel(int type, const uint8_t* __restrict__ q, floa
     }
 }
 
+// One thread per element of the whole super-blocks of Q2_K / Q3_K / Q5_K /
+// Q8_K / IQ4_XS (the reference decodes n / 256 super-blocks).
+__global__ void dequant_superblock_kernel(int type, const uint8_t* __restrict__ q, float* __restrict__ out,
+                                          int64_t n, int bpb) {
+    const int64_t m = n / 256 * 256;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < m; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = superblock_elem(type, q + (i >> 8) * bpb, (int)(i & 255));
+}
+
 __global__ void convert_f16_kernel(const uint16_t* __restrict__ h, float* __restrict__ out,
                                    int64_t n) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
@@ -137,6 +146,13 @@ int dequant_launch(int type, const void* d_blocks, float* d_out, int64_t n, cuda
     const uint8_t* q = static_cast<const uint8_t*>(d_blocks);
     if (is_block32(type)) {
         dequant_b32_kernel<<<grid_for((n + 31) / 32, 256), 256, 0, s>>>(type, q, d_out, n, block32_bytes(type));
+        CN_CUDA(cudaGetLastError());
+        return CN_OK;
+    }
+    if (is_superblock(type)) {
+        if (n / 256 == 0) return CN_OK;
+        dequant_superblock_kernel<<<grid_for(n / 256 * 256, 256), 256, 0, s>>>(type, q, d_out, n,
+                                                                                superblock_bytes(type));
         CN_CUDA(cudaGetLastError());
         return CN_OK;
     }

@@ -39,8 +39,19 @@ __device__ __forceinline__ void q4k_scale_min(const uint8_t* q, int j, int& sc, 
 //                                          DequantQ5_0.cs:29-68 (d@0, qh@2, qs@6)
 //   Q5_1  q5 * d + m                       DequantQ5_1.cs:30-69 (d@0, m@2, qh@4, qs@8)
 //   Q8_0  (sbyte)q * d                     DequantQ8_0.cs:19-41 (d@0, qs@2)
+// DequantIQ.IQ4NL_Table (DequantIQ.cs:29-33), the 16 levels of IQ4_NL / IQ4_XS.
+__device__ __forceinline__ float iq4nl_level(int i) {
+    const int8_t lv[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+    return (float)lv[i];
+}
+
 __device__ __forceinline__ float block32_elem(int type, const uint8_t* p, int j) {
     if (type == CN_TYPE_Q8_0) return __fmul_rn((float)(int8_t)p[2 + j], ld_half(p));
+    if (type == CN_TYPE_IQ4_NL) {
+        // scale * table[nibble] (DequantIQ.cs:45-76; d@0, qs@2 as Q4_0)
+        const uint8_t byte = p[2 + (j & 15)];
+        return __fmul_rn(ld_half(p), iq4nl_level(j < 16 ? (byte & 0x0F) : (byte >> 4)));
+    }
     const int qs_off = type == CN_TYPE_Q4_1 ? 4 : type == CN_TYPE_Q5_0 ? 6 : 8;
     const uint8_t byte = p[qs_off + (j & 15)];
     int q = j < 16 ? (byte & 0x0F) : ((byte >> 4) & 0x0F);
@@ -52,6 +63,57 @@ __device__ __forceinline__ float block32_elem(int type, const uint8_t* p, int j)
     }
     if (type == CN_TYPE_Q5_0) return __fmul_rn((float)(q - 16), ld_half(p));
     return __fadd_rn(__fmul_rn((float)q, ld_half(p)), ld_half(p + 2));
+}
+
+// Element e (0..255) of one super-block of Q2_K, Q3_K, Q5_K, Q8_K or IQ4_XS,
+// with the reference's operation order (no fused multiply-add):
+//   Q2_K  d*(sc&15) * q2 - dmin*(sc>>4); element e: group e/128, 2-bit shift
+//         2*((e/32)%4), half (e/16)%2, scale byte 8g + 2*shift + half, quant
+//         byte 16 + 32g + 16*half + e%16        DequantQ2K.cs:32-88 (d@80, dmin@82)
+//   Q3_K  d * sc * (q3 - 4), sc 6-bit - 32 (DecodeScales), q3 = 2 bits of
+//         qs[e/4] | hmask bit e%8 of byte e/8 << 2
+//                                              DequantQ3K.cs:35-70, :124-148 (d@108)
+//   Q5_K  d*sc * q5 - dmin*m (scales as Q4_K), q5 = nibble | qh bit << 4
+//                                              DequantQ5K.cs:36-90 (qh@16, qs@48)
+//   Q8_K  (sbyte)q * d, d fp32                 DequantQ8K.cs:25-47
+//   IQ4_XS d*sc * table[nibble], sc = ((byte 4+sub & 63) | 2 bits of the
+//         uint16 at 2 << 6) - 32               DequantIQ.cs:143-180 (qs@8)
+__device__ __forceinline__ float superblock_elem(int type, const uint8_t* p, int e) {
+    if (type == CN_TYPE_Q2_K) {
+        const int g = e >> 7, si = (e >> 5) & 3, h = (e >> 4) & 1;
+        const int sb = p[8 * g + 2 * si + h];
+        const float dl = __fmul_rn(ld_half(p + 80), (float)(sb & 0x0F));
+        const float ml = __fmul_rn(ld_half(p + 82), (float)((sb >> 4) & 0x0F));
+        const int q = (p[16 + 32 * g + 16 * h + (e & 15)] >> (2 * si)) & 3;
+        return __fsub_rn(__fmul_rn(dl, (float)q), ml);
+    }
+    if (type == CN_TYPE_Q3_K) {
+        const int k = e >> 4;
+        const uint8_t* sc8 = p + 96;
+        int sc = k < 8 ? (sc8[k] & 0x0F) : ((sc8[k - 8] >> 4) & 0x0F);
+        sc = (sc | (((sc8[8 + (k & 3)] >> (2 * (k >> 2))) & 3) << 4)) - 32;
+        const int q3 = ((p[32 + (e >> 2)] >> (2 * (e & 3))) & 3) | (((p[e >> 3] >> (e & 7)) & 1) << 2);
+        return __fmul_rn(__fmul_rn(ld_half(p + 108), (float)sc), (float)(q3 - 4));
+    }
+    if (type == CN_TYPE_Q5_K) {
+        const int sub = e >> 5, j = e & 31;
+        int sc, m;
+        q4k_scale_min(p + 4, sub, sc, m);
+        const float dsc = __fmul_rn(ld_half(p), (float)sc), dm = __fmul_rn(ld_half(p + 2), (float)m);
+        const uint8_t byte = p[48 + 16 * sub + (j & 15)];
+        const int q5 = (j < 16 ? (byte & 0x0F) : (byte >> 4)) | (((p[16 + (e >> 3)] >> (e & 7)) & 1) << 4);
+        return __fsub_rn(__fmul_rn(dsc, (float)q5), dm);
+    }
+    if (type == CN_TYPE_Q8_K) {
+        const uint32_t u = (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+        return __fmul_rn((float)(int8_t)p[4 + e], __uint_as_float(u));
+    }
+    // IQ4_XS
+    const int sub = e >> 5, j = e & 31;
+    const int sh = p[2] | (p[3] << 8);
+    const int sc = ((p[4 + sub] & 0x3F) | (((sh >> (2 * sub)) & 3) << 6)) - 32;
+    const uint8_t byte = p[8 + 16 * sub + (j & 15)];
+    return __fmul_rn(__fmul_rn(ld_half(p), (float)sc), iq4nl_level(j < 16 ? (byte & 0x0F) : (byte >> 4)));
 }
 
 // ---- GEMV fragment decode -------------------------------------------------

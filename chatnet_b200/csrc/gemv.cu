@@ -845,6 +845,10 @@ __device__ float block_dot(int type, const uint8_t* row, int blk, const float* x
         const uint8_t* p = row + (size_t)blk * block32_bytes(type);
         const float* xb = x + (size_t)blk * 32;
         for (int j = 0; j < 32; j++) s = fmaf(block32_elem(type, p, j), xb[j], s);
+    } else if (is_superblock(type)) {
+        const uint8_t* p = row + (size_t)blk * superblock_bytes(type);
+        const float* xb = x + (size_t)blk * 256;
+        for (int e = 0; e < 256; e++) s = fmaf(superblock_elem(type, p, e), xb[e], s);
     } else if (type == CN_TYPE_F16) {
         s = ld_half(row + 2 * (size_t)blk) * x[blk];
     }
@@ -1048,7 +1052,7 @@ int gemv_make(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols
     }
     if (!op->tma) {
         int blk = type == CN_TYPE_Q4_0 || is_block32(type) ? 32
-                  : (type == CN_TYPE_Q4_K || type == CN_TYPE_Q6_K) ? 256 : 1;
+                  : (type == CN_TYPE_Q4_K || type == CN_TYPE_Q6_K || is_superblock(type)) ? 256 : 1;
         CN_CHECK(cols % blk == 0, CN_ERR_INVALID_ARG, "inDim %lld not a multiple of %d",
                  (long long)cols, blk);
     }
@@ -1151,7 +1155,7 @@ int gemv_run(cn_ctx* ctx, cudaStream_t st, const GemvOp& op, const float* d_x, c
              "tensor-parallel exchange needs the integer GEMV (Q4_K, batch <= 8)");
     if (!op.tma) {
         int blk = op.type == CN_TYPE_Q4_0 || is_block32(op.type) ? 32
-                  : (op.type == CN_TYPE_Q4_K || op.type == CN_TYPE_Q6_K) ? 256 : 1;
+                  : (op.type == CN_TYPE_Q4_K || op.type == CN_TYPE_Q6_K || is_superblock(op.type)) ? 256 : 1;
         int threads = 256;
         int64_t warps = op.rows * op.batch;
         int64_t blocks = (warps * 32 + threads - 1) / threads;

@@ -433,7 +433,9 @@ __global__ void __launch_bounds__(kAttnThreads)
                     int ctx_len, int splits, float scale, float* __restrict__ part, int* __restrict__ counters,
                     float* __restrict__ out, int out_stride, PrepTarget pt, RopeIn ri) {
     pdl_trigger();
-    pdl_wait();
+    // Cache rows below the current position were written by earlier steps,
+    // so their copies start before the wait for the q/k/v kernel; the row at
+    // the current position, q and everything written here come after it.
     static_assert(kAttnThreads == 256 && kMmaChunk == 16 * (kAttnThreads / 32), "16 positions per warp");
     constexpr int RS = HD + 8;  // halves per shared row (16-byte pad against bank conflicts)
     extern __shared__ __align__(16) float sm[];
@@ -455,6 +457,7 @@ __global__ void __launch_bounds__(kAttnThreads)
     __half* Qs = Vs + kMmaChunk * RS;  // [16][RS]
 
     if (L == 0) {  // nothing of this split is inside 0..pos: an empty partial
+        pdl_wait();
         for (int e = tid; e < kv_mul * prow; e += blockDim.x) {
             const int gi = e / prow, d = e % prow;
             pr_base[((size_t)gi * splits + s) * prow + d] = d == HD ? -FLT_MAX : 0.f;
@@ -464,18 +467,27 @@ __global__ void __launch_bounds__(kAttnThreads)
         const __half* kbase = kcache + (int64_t)b * cache_seq_stride + cache_layer_off + kh * HD;
         const __half* vbase = vcache + (int64_t)b * cache_seq_stride + cache_layer_off + kh * HD;
         constexpr int CPR = HD / 8;  // 16-byte chunks per row
-        // with ri.on, row pos of the cache is written here (from the new k/v)
-        const int r_new = ri.on ? pos - p0 : -1;
+        // row pos of the cache: this step's k/v (written here with ri.on, or
+        // by the preceding kernel otherwise)
+        const int r_new = pos - p0;
         for (int i = tid; i < kMmaChunk * CPR; i += kAttnThreads) {
             const int r = i / CPR, c = i % CPR;
-            if (r == r_new) continue;  // written below, not copied (no zero fill racing it)
+            if (r == r_new) continue;  // after the wait (no zero fill racing it)
             const bool in = r < L;
             const int64_t go = (int64_t)(p0 + (in ? r : 0)) * kvdim + c * 8;
             cp_async16(smem_u32(Ks + r * RS + c * 8), kbase + go, in ? 16 : 0);
             cp_async16(smem_u32(Vs + r * RS + c * 8), vbase + go, in ? 16 : 0);
         }
+        pdl_wait();
+        if (!ri.on && r_new >= 0 && r_new < L) {
+            for (int c = tid; c < CPR; c += kAttnThreads) {
+                const int64_t go = (int64_t)pos * kvdim + c * 8;
+                cp_async16(smem_u32(Ks + r_new * RS + c * 8), kbase + go, 16);
+                cp_async16(smem_u32(Vs + r_new * RS + c * 8), vbase + go, 16);
+            }
+        }
         asm volatile("cp.async.commit_group;" ::: "memory");
-        if (r_new >= 0 && r_new < L) {
+        if (ri.on && r_new >= 0 && r_new < L) {
             // TensorMath.ApplyRoPE on the new k row, then k and v into the cache
             // (the rope_kv_kernel arithmetic, bit for bit)
             const float2* tab = ri.rope + (size_t)pos * (HD / 2);
@@ -718,6 +730,8 @@ __global__ void embed_kernel(int type, const uint8_t* __restrict__ emb, uint64_t
             v = __fmul_rn(__fmul_rn(ld_half(p + 208), (float)(int8_t)p[192 + si]), (float)q);
         } else if (is_block32(type)) {
             v = block32_elem(type, row + (i / 32) * block32_bytes(type), i % 32);
+        } else if (is_superblock(type)) {
+            v = superblock_elem(type, row + (i / 256) * superblock_bytes(type), i % 256);
         } else if (type == CN_TYPE_F16) {
             v = ld_half(row + 2 * i);
         } else {

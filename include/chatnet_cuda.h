@@ -53,8 +53,14 @@ extern "C" {
 #define CN_TYPE_Q5_0 6
 #define CN_TYPE_Q5_1 7
 #define CN_TYPE_Q8_0 8
+#define CN_TYPE_Q2_K 10
+#define CN_TYPE_Q3_K 11
 #define CN_TYPE_Q4_K 12
+#define CN_TYPE_Q5_K 13
 #define CN_TYPE_Q6_K 14
+#define CN_TYPE_Q8_K 15
+#define CN_TYPE_IQ4_NL 20
+#define CN_TYPE_IQ4_XS 23
 
 typedef struct cn_ctx cn_ctx;
 typedef struct cn_tensor cn_tensor;

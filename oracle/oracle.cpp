@@ -85,6 +85,12 @@ extern "C" uint64_t or_byte_size(int type, uint64_t elements) {
         case OR_Q8_0: return (elements + 31) / 32 * 34;
         case OR_Q4_K: return (elements + 255) / 256 * 144;
         case OR_Q6_K: return (elements + 255) / 256 * 210;
+        case OR_Q2_K: return (elements + 255) / 256 * 84;
+        case OR_Q3_K: return (elements + 255) / 256 * 110;
+        case OR_Q5_K: return (elements + 255) / 256 * 176;
+        case OR_Q8_K: return (elements + 255) / 256 * 292;
+        case OR_IQ4_NL: return (elements + 31) / 32 * 18;
+        case OR_IQ4_XS: return (elements + 255) / 256 * 136;
         default: return 0;
     }
 }
@@ -238,6 +244,141 @@ static void dequant_q6_k(const uint8_t* q, float* out, int64_t n) {
     }
 }
 
+// ---- the other K-quants and the IQ4 codecs (generic paths on the device) ----
+
+// DequantIQ.IQ4NL_Table (DequantIQ.cs:29-33): the 16 non-linear levels.
+static const float kIq4nl[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+
+// DequantQ3K.DecodeScales (DequantQ3K.cs:124-148): 16 six-bit scales, minus 32.
+static void decode_scales_q3k(const uint8_t* q, int* sc) {
+    for (int i = 0; i < 8; i++) {
+        sc[i] = q[i] & 0x0F;
+        sc[i + 8] = (q[i] >> 4) & 0x0F;
+    }
+    for (int i = 0; i < 4; i++) {
+        const uint8_t hb = q[8 + i];
+        sc[i] |= ((hb >> 0) & 3) << 4;
+        sc[i + 4] |= ((hb >> 2) & 3) << 4;
+        sc[i + 8] |= ((hb >> 4) & 3) << 4;
+        sc[i + 12] |= ((hb >> 6) & 3) << 4;
+    }
+    for (int i = 0; i < 16; i++) sc[i] -= 32;
+}
+
+static inline float f32_le(const uint8_t* p) {
+    const uint32_t u = (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+// DequantQ2K.Dequantize (DequantQ2K.cs:32-88): two groups of 128, four
+// 2-bit shifts each, two 16-element halves per shift; dl * q - ml with
+// dl = d * (sc & 15), ml = dmin * (sc >> 4) (d@80, dmin@82, scales@0, qs@16).
+static void dequant_q2_k(const uint8_t* q, float* out, int64_t n) {
+    for (int64_t b = 0; b < n / 256; b++) {
+        const uint8_t* blk = q + b * 84;
+        const float d = h2f(blk + 80), dmin = h2f(blk + 82);
+        float* o = out + b * 256;
+        int si = 0;
+        for (int g = 0; g < 2; g++)
+            for (int shift = 0; shift < 8; shift += 2) {
+                for (int h = 0; h < 2; h++) {
+                    const float dl = d * (float)(blk[si + h] & 0x0F);
+                    const float ml = dmin * (float)((blk[si + h] >> 4) & 0x0F);
+                    for (int l = 0; l < 16; l++) *o++ = dl * (float)((blk[16 + 32 * g + 16 * h + l] >> shift) & 3) - ml;
+                }
+                si += 2;
+            }
+    }
+}
+
+// DequantQ3K.Dequantize (DequantQ3K.cs:35-70): d * scale * (q3 - 4), q3 = the
+// 2 bits of qs[i / 4] at (i % 4) * 2 | bit i % 8 of hmask[i / 8] << 2
+// (hmask@0, qs@32, scales@96, d@108).
+static void dequant_q3_k(const uint8_t* q, float* out, int64_t n) {
+    int sc[16];
+    for (int64_t b = 0; b < n / 256; b++) {
+        const uint8_t* blk = q + b * 110;
+        const float d = h2f(blk + 108);
+        decode_scales_q3k(blk + 96, sc);
+        for (int i = 0; i < 256; i++) {
+            const int q2 = (blk[32 + i / 4] >> ((i % 4) * 2)) & 3;
+            const int q3 = q2 | (((blk[i / 8] >> (i % 8)) & 1) << 2);
+            out[b * 256 + i] = d * (float)sc[i / 16] * (float)(q3 - 4);
+        }
+    }
+}
+
+// DequantQ5K.Dequantize (DequantQ5K.cs:36-90): d * sc * q5 - dmin * m (scales
+// as Q4_K), q5 = nibble | bit e % 8 of qh[e / 8] << 4 for element e
+// (d@0, dmin@2, scales@4, qh@16, qs@48; sub-block s uses qs bytes 16s..16s+15).
+static void dequant_q5_k(const uint8_t* q, float* out, int64_t n) {
+    int sc[8], m[8];
+    for (int64_t b = 0; b < n / 256; b++) {
+        const uint8_t* blk = q + b * 176;
+        const float d = h2f(blk), dmin = h2f(blk + 2);
+        decode_scales_q4k(blk + 4, sc, m);
+        for (int sub = 0; sub < 8; sub++) {
+            const float dsc = d * (float)sc[sub], dm = dmin * (float)m[sub];
+            for (int h = 0; h < 2; h++)
+                for (int j = 0; j < 16; j++) {
+                    const int e = sub * 32 + 16 * h + j;
+                    const int nib = h == 0 ? (blk[48 + sub * 16 + j] & 0x0F) : ((blk[48 + sub * 16 + j] >> 4) & 0x0F);
+                    const int q5 = nib | (((blk[16 + e / 8] >> (e % 8)) & 1) << 4);
+                    out[b * 256 + e] = dsc * (float)q5 - dm;
+                }
+        }
+    }
+}
+
+// DequantQ8K.Dequantize (DequantQ8K.cs:25-47): (sbyte)q * d, d an fp32 at 0.
+static void dequant_q8_k(const uint8_t* q, float* out, int64_t n) {
+    for (int64_t b = 0; b < n / 256; b++) {
+        const uint8_t* blk = q + b * 292;
+        const float d = f32_le(blk);
+        for (int i = 0; i < 256; i++) out[b * 256 + i] = (float)(int8_t)blk[4 + i] * d;
+    }
+}
+
+// DequantIQ.IQ4NL.Dequantize (DequantIQ.cs:45-76): scale * table[nibble],
+// Q4_0's layout and partial last block.
+static void dequant_iq4_nl(const uint8_t* q, float* out, int64_t n) {
+    int64_t nb = (n + 31) / 32, src = 0, dst = 0;
+    for (int64_t b = 0; b < nb; b++) {
+        const float scale = h2f(q + src);
+        src += 2;
+        const int64_t remaining = n - dst;
+        const int half = remaining < 16 ? (int)remaining : 16;
+        const int second = remaining < 32 ? (remaining > 16 ? (int)(remaining - 16) : 0) : 16;
+        for (int j = 0; j < half; j++) out[dst + j] = scale * kIq4nl[q[src + j] & 0x0F];
+        for (int j = 0; j < second; j++) out[dst + 16 + j] = scale * kIq4nl[(q[src + j] >> 4) & 0x0F];
+        src += 16;
+        dst += half + second;
+    }
+}
+
+// DequantIQ.IQ4XS.Dequantize (DequantIQ.cs:143-180): per 32-element sub-block
+// sc = ((byte[4 + sub] & 63) | ((scales_h >> 2 sub) & 3) << 6) - 32 (scales_h
+// the uint16 at 2; the scale bytes 4..11 overlap the first quant bytes, as
+// in the reference), value = d * sc * table[nibble] (qs@8).
+static void dequant_iq4_xs(const uint8_t* q, float* out, int64_t n) {
+    for (int64_t b = 0; b < n / 256; b++) {
+        const uint8_t* blk = q + b * 136;
+        const float d = h2f(blk);
+        const int sh = blk[2] | (blk[3] << 8);
+        for (int sub = 0; sub < 8; sub++) {
+            const int sc = ((blk[4 + sub] & 0x3F) | (((sh >> (2 * sub)) & 3) << 6)) - 32;
+            const float dsc = d * (float)sc;
+            for (int j = 0; j < 16; j++) {
+                const uint8_t v = blk[8 + sub * 16 + j];
+                out[b * 256 + sub * 32 + j] = dsc * kIq4nl[v & 0x0F];
+                out[b * 256 + sub * 32 + j + 16] = dsc * kIq4nl[(v >> 4) & 0x0F];
+            }
+        }
+    }
+}
+
 extern "C" int or_dequantize(int type, const uint8_t* src, float* dst, int64_t n) {
     if (n < 0) return -1;
     switch (type) {
@@ -248,6 +389,12 @@ extern "C" int or_dequantize(int type, const uint8_t* src, float* dst, int64_t n
         case OR_Q5_1: dequant_b32(type, src, dst, n); return 0;
         case OR_Q4_K: dequant_q4_k(src, dst, n); return 0;
         case OR_Q6_K: dequant_q6_k(src, dst, n); return 0;
+        case OR_Q2_K: dequant_q2_k(src, dst, n); return 0;
+        case OR_Q3_K: dequant_q3_k(src, dst, n); return 0;
+        case OR_Q5_K: dequant_q5_k(src, dst, n); return 0;
+        case OR_Q8_K: dequant_q8_k(src, dst, n); return 0;
+        case OR_IQ4_NL: dequant_iq4_nl(src, dst, n); return 0;
+        case OR_IQ4_XS: dequant_iq4_xs(src, dst, n); return 0;
         case OR_F32: memcpy(dst, src, (size_t)n * 4); return 0;
         case OR_F16:
             for (int64_t i = 0; i < n; i++) dst[i] = h2f(src + 2 * i);
@@ -475,6 +622,135 @@ static float dot_f16(const uint8_t* row, const float* x, int n) {
     return dot;
 }
 
+// DequantQ2K.DotProductScalar (DequantQ2K.cs:96-155): blockSum += (dl * q - ml) * x.
+static float dot_q2_k(const uint8_t* row, const float* x, int n) {
+    float sum = 0.f;
+    for (int b = 0; b < n / 256; b++) {
+        const uint8_t* blk = row + (size_t)b * 84;
+        const float d = h2f(blk + 80), dmin = h2f(blk + 82);
+        const float* in = x + 256 * b;
+        float bs = 0.f;
+        int si = 0, y = 0;
+        for (int g = 0; g < 2; g++)
+            for (int shift = 0; shift < 8; shift += 2) {
+                for (int h = 0; h < 2; h++) {
+                    const float dl = d * (float)(blk[si + h] & 0x0F);
+                    const float ml = dmin * (float)((blk[si + h] >> 4) & 0x0F);
+                    for (int l = 0; l < 16; l++)
+                        bs += (dl * (float)((blk[16 + 32 * g + 16 * h + l] >> shift) & 3) - ml) * in[y++];
+                }
+                si += 2;
+            }
+        sum += bs;
+    }
+    return sum;
+}
+
+// DequantQ3K.DotProductScalar (DequantQ3K.cs:79-118): integer scale * (q3 - 4),
+// times x, summed per super-block, then sum += d * blockSum.
+static float dot_q3_k(const uint8_t* row, const float* x, int n) {
+    float sum = 0.f;
+    int sc[16];
+    for (int b = 0; b < n / 256; b++) {
+        const uint8_t* blk = row + (size_t)b * 110;
+        const float d = h2f(blk + 108);
+        decode_scales_q3k(blk + 96, sc);
+        float bs = 0.f;
+        for (int i = 0; i < 256; i++) {
+            const int q2 = (blk[32 + i / 4] >> ((i % 4) * 2)) & 3;
+            const int q3 = q2 | (((blk[i / 8] >> (i % 8)) & 1) << 2);
+            bs += (float)(sc[i / 16] * (q3 - 4)) * x[256 * b + i];
+        }
+        sum += d * bs;
+    }
+    return sum;
+}
+
+// DequantQ5K.DotProductScalar (DequantQ5K.cs:99-154): blockSum += (dsc * q5 - dm) * x.
+static float dot_q5_k(const uint8_t* row, const float* x, int n) {
+    float sum = 0.f;
+    int sc[8], m[8];
+    for (int b = 0; b < n / 256; b++) {
+        const uint8_t* blk = row + (size_t)b * 176;
+        const float d = h2f(blk), dmin = h2f(blk + 2);
+        decode_scales_q4k(blk + 4, sc, m);
+        float bs = 0.f;
+        for (int sub = 0; sub < 8; sub++) {
+            const float dsc = d * (float)sc[sub], dm = dmin * (float)m[sub];
+            for (int h = 0; h < 2; h++)
+                for (int j = 0; j < 16; j++) {
+                    const int e = sub * 32 + 16 * h + j;
+                    const int nib = h == 0 ? (blk[48 + sub * 16 + j] & 0x0F) : ((blk[48 + sub * 16 + j] >> 4) & 0x0F);
+                    const int q5 = nib | (((blk[16 + e / 8] >> (e % 8)) & 1) << 4);
+                    bs += (dsc * (float)q5 - dm) * x[256 * b + e];
+                }
+        }
+        sum += bs;
+    }
+    return sum;
+}
+
+// DequantQ8K.DotProductVec128 (DequantQ8K.cs:58-96): two 4-lane accumulators
+// of (q * d) * x over the row, then Vector128.Sum(acc0 + acc1).
+static float dot_q8_k(const uint8_t* row, const float* x, int n) {
+    __m128 acc0 = _mm_setzero_ps(), acc1 = _mm_setzero_ps();
+    for (int b = 0; b < n / 256; b++) {
+        const uint8_t* blk = row + (size_t)b * 292;
+        const __m128 vs = _mm_set1_ps(f32_le(blk));
+        const float* in = x + 256 * b;
+        for (int i = 0; i < 256; i += 8) {
+            const __m128 v0 = _mm_setr_ps((float)(int8_t)blk[4 + i], (float)(int8_t)blk[5 + i],
+                                          (float)(int8_t)blk[6 + i], (float)(int8_t)blk[7 + i]);
+            const __m128 v1 = _mm_setr_ps((float)(int8_t)blk[8 + i], (float)(int8_t)blk[9 + i],
+                                          (float)(int8_t)blk[10 + i], (float)(int8_t)blk[11 + i]);
+            acc0 = _mm_add_ps(acc0, _mm_mul_ps(_mm_mul_ps(v0, vs), _mm_loadu_ps(in + i)));
+            acc1 = _mm_add_ps(acc1, _mm_mul_ps(_mm_mul_ps(v1, vs), _mm_loadu_ps(in + i + 4)));
+        }
+    }
+    return sum128(_mm_add_ps(acc0, acc1));
+}
+
+// DequantIQ.IQ4NL.DotProductScalar (DequantIQ.cs:85-118): per block, the low
+// then the high nibbles' table values times x, then sum += blockSum * scale.
+static float dot_iq4_nl(const uint8_t* row, const float* x, int n) {
+    float sum = 0.f;
+    for (int b = 0; b < n / 32; b++) {
+        const uint8_t* blk = row + (size_t)b * 18;
+        const float scale = h2f(blk);
+        float bs = 0.f;
+        for (int j = 0; j < 16; j++) bs += kIq4nl[blk[2 + j] & 0x0F] * x[32 * b + j];
+        for (int j = 0; j < 16; j++) bs += kIq4nl[(blk[2 + j] >> 4) & 0x0F] * x[32 * b + 16 + j];
+        sum += bs * scale;
+    }
+    return sum;
+}
+
+// DequantIQ.IQ4XS.DotProductScalar (DequantIQ.cs:189-233): per sub-block the
+// low and high nibble of each byte in turn, blockSum += dsc * subSum.
+static float dot_iq4_xs(const uint8_t* row, const float* x, int n) {
+    float sum = 0.f;
+    for (int b = 0; b < n / 256; b++) {
+        const uint8_t* blk = row + (size_t)b * 136;
+        const float d = h2f(blk);
+        const int sh = blk[2] | (blk[3] << 8);
+        float bs = 0.f;
+        for (int sub = 0; sub < 8; sub++) {
+            const int sc = ((blk[4 + sub] & 0x3F) | (((sh >> (2 * sub)) & 3) << 6)) - 32;
+            const float dsc = d * (float)sc;
+            const float* in = x + 256 * b + 32 * sub;
+            float ss = 0.f;
+            for (int j = 0; j < 16; j++) {
+                const uint8_t v = blk[8 + sub * 16 + j];
+                ss += kIq4nl[v & 0x0F] * in[j];
+                ss += kIq4nl[(v >> 4) & 0x0F] * in[j + 16];
+            }
+            bs += dsc * ss;
+        }
+        sum += bs;
+    }
+    return sum;
+}
+
 extern "C" float or_dot(int type, const uint8_t* row, const float* x, int n) {
     switch (type) {
         case OR_Q4_0: return dot_q4_0(row, x, n);
@@ -484,6 +760,12 @@ extern "C" float or_dot(int type, const uint8_t* row, const float* x, int n) {
         case OR_Q5_1: return dot_b32(type, row, x, n);
         case OR_Q4_K: return dot_q4_k(row, x, n);
         case OR_Q6_K: return dot_q6_k(row, x, n);
+        case OR_Q2_K: return dot_q2_k(row, x, n);
+        case OR_Q3_K: return dot_q3_k(row, x, n);
+        case OR_Q5_K: return dot_q5_k(row, x, n);
+        case OR_Q8_K: return dot_q8_k(row, x, n);
+        case OR_IQ4_NL: return dot_iq4_nl(row, x, n);
+        case OR_IQ4_XS: return dot_iq4_xs(row, x, n);
         case OR_F32: return dot_f32((const float*)row, x, n);
         case OR_F16: return dot_f16(row, x, n);
         default: return NAN;
@@ -533,6 +815,12 @@ static int row_bytes(int type, int in_dim, size_t* bpr) {
         case OR_Q8_0: *bpr = (size_t)(in_dim / 32) * 34; return 0;
         case OR_Q4_K: *bpr = (size_t)(in_dim / 256) * 144; return 0;
         case OR_Q6_K: *bpr = (size_t)(in_dim / 256) * 210; return 0;
+        case OR_Q2_K: *bpr = (size_t)(in_dim / 256) * 84; return 0;
+        case OR_Q3_K: *bpr = (size_t)(in_dim / 256) * 110; return 0;
+        case OR_Q5_K: *bpr = (size_t)(in_dim / 256) * 176; return 0;
+        case OR_Q8_K: *bpr = (size_t)(in_dim / 256) * 292; return 0;
+        case OR_IQ4_NL: *bpr = (size_t)(in_dim / 32) * 18; return 0;
+        case OR_IQ4_XS: *bpr = (size_t)(in_dim / 256) * 136; return 0;
         case OR_F32: *bpr = (size_t)in_dim * 4; return 0;
         case OR_F16: *bpr = (size_t)in_dim * 2; return 0;
         default: return -2;

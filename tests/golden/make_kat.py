@@ -138,13 +138,78 @@ def cases() -> list[dict]:
     deq = [0.25 * i for i in range(32)]
     out.append(dict(name="Q8_0_DotProduct_MatchesDequantize", ref=f"{T}:273-299", type=8, n=32,
                     blocks=blk, dequant=deq, x=[1.0] * 32, dot=float(sum(deq)), tol=0.01))
+
+    # Q2K_Dequantize_ProducesFiniteValues (:351-367): d=1 @80, dmin=0.5 @82,
+    # scale bytes 0x21 (sc 1, m 2), quants 0 -> 1*1*0 - 0.5*2
+    blk = [0x21] * 16 + [0] * 64 + half_bytes(1.0) + half_bytes(0.5)
+    out.append(dict(name="Q2K_Dequantize_ProducesFiniteValues", ref=f"{T}:351-367", type=10, n=256,
+                    blocks=blk, dequant=[-1.0] * 256, finite=True, tol=0.01))
+
+    # Q2K_DotProduct_MatchesDequantize (:369-394): d=.5, dmin=.25, scales 0x11,
+    # quant bytes 0x55 (every 2-bit field 1), x=1 -> 0.5*1*1 - 0.25*1 each
+    blk = [0x11] * 16 + [0x55] * 64 + half_bytes(0.5) + half_bytes(0.25)
+    out.append(dict(name="Q2K_DotProduct_MatchesDequantize", ref=f"{T}:369-394", type=10, n=256,
+                    blocks=blk, dequant=[0.25] * 256, x=[1.0] * 256, dot=64.0, tol=0.1))
+
+    # Q3K_Dequantize_ProducesFiniteValues (:400-414): d=1 @108, all else 0:
+    # scales 0 - 32, q3 0 -> 1 * -32 * (0 - 4)
+    blk = [0] * 108 + half_bytes(1.0)
+    out.append(dict(name="Q3K_Dequantize_ProducesFiniteValues", ref=f"{T}:400-414", type=11, n=256,
+                    blocks=blk, dequant=[128.0] * 256, finite=True, tol=0.01))
+
+    # Q3K_DotProduct_MatchesDequantize (:416-439): d=0.1, qs bytes 0x55 (q2 1),
+    # hmask 0, scales -32 -> d * -32 * (1 - 4), x=1
+    blk = [0] * 32 + [0x55] * 64 + [0] * 12 + half_bytes(0.1)
+    v = np.float32(np.float32(f16(0.1)) * np.float32(-32)) * np.float32(-3)
+    out.append(dict(name="Q3K_DotProduct_MatchesDequantize", ref=f"{T}:416-439", type=11, n=256,
+                    blocks=blk, dequant=[float(v)] * 256, x=[1.0] * 256, dot=float(v) * 256, tol=0.1))
+
+    # Q5K_Dequantize_ProducesFiniteValues (:495-511): d=1, dmin=0.5, scale
+    # bytes 0x11 (sc = m = 17 for sub-blocks 0..3, 1 for 4..7), quants 0
+    blk = half_bytes(1.0) + half_bytes(0.5) + [0x11] * 12 + [0] * 160
+    deq = [(-8.5 if (i // 32) < 4 else -0.5) for i in range(256)]
+    out.append(dict(name="Q5K_Dequantize_ProducesFiniteValues", ref=f"{T}:495-511", type=13, n=256,
+                    blocks=blk, dequant=deq, finite=True, tol=0.01))
+
+    # Q5K_DotProduct_MatchesDequantize (:513-538): d=.5, dmin=.25, scales 0x11,
+    # qs 0x55, qh 0 (q5 = 5), x=1
+    blk = half_bytes(0.5) + half_bytes(0.25) + [0x11] * 12 + [0] * 32 + [0x55] * 128
+    deq = [(0.5 * 17 * 5 - 0.25 * 17) if (i // 32) < 4 else (0.5 * 1 * 5 - 0.25 * 1) for i in range(256)]
+    out.append(dict(name="Q5K_DotProduct_MatchesDequantize", ref=f"{T}:513-538", type=13, n=256,
+                    blocks=blk, dequant=deq, x=[1.0] * 256, dot=float(sum(deq)), tol=0.1))
+
+    # Q8K_Dequantize_ProducesCorrectValues (:544-562): fp32 d=0.5, q=10 -> 5
+    f32 = lambda v: list(np.array([v], dtype="<f4").view(np.uint8))
+    blk = [int(b) for b in f32(0.5)] + [10] * 256 + [0] * 32
+    out.append(dict(name="Q8K_Dequantize_ProducesCorrectValues", ref=f"{T}:544-562", type=15, n=256,
+                    blocks=blk, dequant=[5.0] * 256, tol=0.01))
+
+    # Q8K_DotProduct_MatchesDequantize (:564-588): d=0.25, byte i = i % 20, x=1
+    blk = [int(b) for b in f32(0.25)] + [i % 20 for i in range(4, 260)] + [0] * 32
+    deq = [0.25 * (i % 20) for i in range(4, 260)]
+    out.append(dict(name="Q8K_DotProduct_MatchesDequantize", ref=f"{T}:564-588", type=15, n=256,
+                    blocks=blk, dequant=deq, x=[1.0] * 256, dot=float(sum(deq)), tol=0.01))
+
+    # IQ4NL_Dequantize_UsesLookupTable (:594-611): scale 1, byte 2 = 0x80:
+    # element 0 -> table[0] = -127, element 16 -> table[8] = 1, the rest table[0]
+    blk = half_bytes(1.0) + [0x80] + [0] * 15
+    deq = [-127.0] * 16 + [1.0] + [-127.0] * 15
+    out.append(dict(name="IQ4NL_Dequantize_UsesLookupTable", ref=f"{T}:594-611", type=20, n=32,
+                    blocks=blk, dequant=deq, tol=0.01))
+
+    # IQ4NL_DotProduct_MatchesDequantize (:613-636): scale 0.01, all index 8 (1), x=1
+    blk = half_bytes(0.01) + [0x88] * 16
+    v = float(np.float32(f16(0.01)))
+    out.append(dict(name="IQ4NL_DotProduct_MatchesDequantize", ref=f"{T}:613-636", type=20, n=32,
+                    blocks=blk, dequant=[v] * 32, x=[1.0] * 32, dot=v * 32, tol=0.1))
     return out
 
 
 # GgufTensorInfo_ByteSize_AllTypes (:642-698), the rows for the types this
 # library decodes: (type, block size, bytes per block)
 BYTESIZE = [(0, 1, 4), (1, 1, 2), (2, 32, 18), (3, 32, 20), (6, 32, 22), (7, 32, 24), (8, 32, 34),
-            (12, 256, 144), (14, 256, 210)]
+            (10, 256, 84), (11, 256, 110), (12, 256, 144), (13, 256, 176), (14, 256, 210), (15, 256, 292),
+            (20, 32, 18), (23, 256, 136)]
 
 
 def main() -> None:

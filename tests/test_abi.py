@@ -43,7 +43,8 @@ def test_abi_version():
     (cn.TYPE_Q4_0, 2048, 1152), (cn.TYPE_Q4_0, 33, 36), (cn.TYPE_Q4_K, 4096, 2304),
     (cn.TYPE_Q4_K, 257, 288), (cn.TYPE_Q6_K, 4096, 3360), (cn.TYPE_F32, 10, 40),
     (cn.TYPE_F16, 10, 20), (cn.TYPE_Q4_1, 32, 20), (cn.TYPE_Q5_0, 64, 44), (cn.TYPE_Q5_1, 33, 48),
-    (cn.TYPE_Q8_0, 32, 34), (10, 256, 0)])
+    (cn.TYPE_Q8_0, 32, 34), (cn.TYPE_Q2_K, 256, 84), (cn.TYPE_Q3_K, 512, 220), (cn.TYPE_Q5_K, 257, 352),
+    (cn.TYPE_Q8_K, 256, 292), (cn.TYPE_IQ4_NL, 33, 36), (cn.TYPE_IQ4_XS, 256, 136), (16, 256, 0)])
 def test_byte_size(t, elems, expected, oracle):
     assert cn.byte_size(t, elems) == expected
     assert oracle.lib.or_byte_size(t, elems) == expected

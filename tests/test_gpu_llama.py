@@ -9,7 +9,7 @@ import pytest
 
 import chatnet_b200 as cn
 from chatnet_b200 import configs as cf
-from chatnet_b200.llama import CudaLlamaModel, tensor_names
+from chatnet_b200.llama import CudaLlamaModel, tensor_names, tensor_shape
 from tests import _oracle
 from tests.parity import REL_TOL, rel_err
 
@@ -193,3 +193,39 @@ def test_config4_two_layers_batched(ctx, oracle):
         assert rel_err(lg[s], ref) <= REL_TOL
         assert am[s] == int(np.argmax(ref))
     p.close()
+
+
+def test_mixed_codec_model(ctx, oracle):
+    """A decoder whose projections, embedding and lm_head use the generic
+    codecs (every K-quant and IQ4 type the reference decodes besides Q4_K /
+    Q6_K, one per tensor kind) matches the oracle's Forward."""
+    from tests.test_gpu_quant import _rand_b32, _rand_sb
+    dc = cf.replace(small_dc(), kv_filled=0, decode_pos=0)
+    m = dc.model
+    kinds = {"attn_q": "q5_k", "attn_k": "q3_k", "attn_v": "q2_k", "attn_output": "iq4_xs",
+             "ffn_gate": "q8_k", "ffn_up": "iq4_nl", "ffn_down": "q5_k"}
+    host = cf.host_tensors(dc)
+    names = tensor_names(m.n_layers)
+    types = []
+    for i, n in enumerate(names):
+        rows, cols = tensor_shape(m, n)
+        kind = n.split(".")[2] if n.startswith("blk.") else n.split(".")[0]
+        codec = {"token_embd": "q2_k", "output": "iq4_xs"}.get(kind, kinds.get(kind))
+        if codec is None:  # norms stay fp32
+            types.append(cf.tensor_type(dc, n))
+            continue
+        t, blocks = (_rand_b32 if codec == "iq4_nl" else _rand_sb)(codec, rows, cols, 100 + i)
+        host[n] = blocks
+        types.append(t)
+    tensors = [ctx.upload(host[n], t, *tensor_shape(m, n)) for n, t in zip(names, types)]
+    g = CudaLlamaModel(ctx, m, tensors)
+    k = np.zeros((m.n_layers * m.ctx_len, m.kv_dim), np.float32)
+    orc = _oracle.OracleLlama(oracle, m, host, types, names, k, k.copy())
+    for pos in range(3):
+        t = cf.token(dc, 0, pos)
+        got, ref = g.forward([t], pos), orc.forward([t], pos)
+        assert rel_err(got, ref) <= REL_TOL, pos
+        assert int(np.argmax(got)) == int(np.argmax(ref))
+    g.close()
+    for t in tensors:
+        t.free()

@@ -158,7 +158,7 @@ def test_matvec_errors(ctx):
     with pytest.raises(ValueError):
         ctx.matvec(W, np.zeros((33, 64), np.float32))
     with pytest.raises(cn.NotSupportedError):
-        ctx.upload(np.zeros(84, np.uint8), 10, 1, 256)  # Q2_K: no decoder here
+        ctx.upload(np.zeros(66, np.uint8), 16, 1, 256)  # IQ2_XXS: no decoder here
     with pytest.raises(ValueError):
         ctx.upload(np.zeros(17, np.uint8), cn.TYPE_Q4_0, 1, 32)  # wrong byte count
 
@@ -183,7 +183,8 @@ def test_matvec_activation_range(ctx, oracle, name, magnitude):
 # The 32-weight codecs decoded through the generic paths: Q4_1, Q5_0, Q5_1, Q8_0
 # (block bytes, offsets of the fp16 fields d and m)
 B32 = {"q4_1": (cn.TYPE_Q4_1, 20, (0, 2)), "q5_0": (cn.TYPE_Q5_0, 22, (0,)),
-       "q5_1": (cn.TYPE_Q5_1, 24, (0, 2)), "q8_0": (cn.TYPE_Q8_0, 34, (0,))}
+       "q5_1": (cn.TYPE_Q5_1, 24, (0, 2)), "q8_0": (cn.TYPE_Q8_0, 34, (0,)),
+       "iq4_nl": (cn.TYPE_IQ4_NL, 18, (0,))}
 
 
 def _rand_b32(name, rows, cols, seed):
@@ -215,4 +216,44 @@ def test_block32_matvec_parity(ctx, oracle, name, batch):
     t, blocks = _rand_b32(name, rows, cols, 13)
     W = ctx.upload(blocks, t, rows, cols)
     x = _x(batch, cols, f"b32.x.{name}.{batch}")
+    assert rel_err(ctx.matvec(W, x), oracle.matvec(t, blocks, x, rows)) <= REL_TOL
+
+
+# The 256-weight super-block codecs on the generic paths: Q2_K, Q3_K, Q5_K,
+# Q8_K, IQ4_XS (block bytes, offsets of the fp16 scale fields; Q8_K's scale
+# is an fp32 at 0)
+SB = {"q2_k": (cn.TYPE_Q2_K, 84, (80, 82)), "q3_k": (cn.TYPE_Q3_K, 110, (108,)),
+      "q5_k": (cn.TYPE_Q5_K, 176, (0, 2)), "q8_k": (cn.TYPE_Q8_K, 292, ()),
+      "iq4_xs": (cn.TYPE_IQ4_XS, 136, (0,))}
+
+
+def _rand_sb(name, rows, cols, seed):
+    t, bpb, halves = SB[name]
+    rng = np.random.default_rng(seed)
+    nb = rows * (cols // 256)
+    blocks = rng.integers(0, 256, size=(nb, bpb), dtype=np.uint8)
+    for off in halves:  # finite scales
+        v = (np.abs(rng.standard_normal(nb)) * 0.01).astype(np.float16)
+        blocks[:, off:off + 2] = v.view(np.uint8).reshape(nb, 2)
+    if t == cn.TYPE_Q8_K:
+        v = (np.abs(rng.standard_normal(nb)) * 0.01).astype("<f4")
+        blocks[:, 0:4] = v.view(np.uint8).reshape(nb, 4)
+    return t, blocks.ravel()
+
+
+@pytest.mark.parametrize("name", list(SB))
+def test_superblock_dequantize_bit_exact(ctx, oracle, name):
+    t, blocks = _rand_sb(name, 37, 768, 21)
+    W = ctx.upload(blocks, t, 37, 768)
+    assert bits_equal(ctx.dequantize(W), oracle.dequantize(t, blocks, 37 * 768).reshape(37, 768))
+    assert bits_equal(ctx.dequantize(W, 5, 7), oracle.dequantize(t, blocks, 37 * 768).reshape(37, 768)[5:12])
+
+
+@pytest.mark.parametrize("name", list(SB))
+@pytest.mark.parametrize("batch", [1, 3])
+def test_superblock_matvec_parity(ctx, oracle, name, batch):
+    rows, cols = 300, 2048
+    t, blocks = _rand_sb(name, rows, cols, 23)
+    W = ctx.upload(blocks, t, rows, cols)
+    x = _x(batch, cols, f"sb.x.{name}.{batch}")
     assert rel_err(ctx.matvec(W, x), oracle.matvec(t, blocks, x, rows)) <= REL_TOL
