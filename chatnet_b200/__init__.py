@@ -163,6 +163,15 @@ class Context:
         check(N.lib().cn_matmul(self.handle, W.handle, _fptr(x2), _fptr(y), x2.shape[0]), "cn_matmul")
         return y
 
+    def sample_dev(self, d_logits: int, vocab: int, batch: int, temperature: float, top_k: int = 40,
+                   top_p: float = 0.9, r=None) -> np.ndarray:
+        """TemperatureSampler.Sample on device logits [batch][vocab] (cn_sample_dev)."""
+        rr = np.ascontiguousarray(np.zeros(batch) if r is None else r, dtype=np.float32)
+        out = np.empty(batch, dtype=np.int32)
+        check(N.lib().cn_sample_dev(self.handle, C.c_void_p(d_logits), vocab, batch, float(temperature),
+                                    int(top_k), float(top_p), rr.ctypes.data, out.ctypes.data), "cn_sample_dev")
+        return out
+
     def close(self) -> None:
         if self.handle:
             for m in list(self._models):

@@ -165,6 +165,7 @@ int cn_destroy(cn_ctx* ctx) {
     cudaFree(ctx->xinv);
     cudaFree(ctx->dstage);
     cudaFree(ctx->xhalf);
+    cudaFree(ctx->samp);
     cudaFreeHost(ctx->hstage);
     cudaFree(ctx->dev_err);
     cudaStreamDestroy(ctx->stream);

@@ -31,6 +31,10 @@ struct cn_ctx {
     void* xhalf = nullptr;
     size_t xhalf_bytes = 0;
 
+    // device sampler scratch (sample.cu)
+    void* samp = nullptr;
+    size_t samp_bytes = 0;
+
     // staging for the host-pointer entry points
     void* dstage = nullptr;
     size_t dstage_bytes = 0;
@@ -89,6 +93,10 @@ __host__ __device__ inline int superblock_bytes(int type) {
 bool type_supported(int type);
 
 int ensure(void** p, size_t* have, size_t need, bool zero);
+
+// TemperatureSampler.Sample on device logits [batch][vocab] (sample.cu).
+int sample_launch(cn_ctx* ctx, const float* d_logits, int vocab, int batch, float temperature, int top_k,
+                  float top_p, const float* r_host, int* tokens_host);
 
 // Encodes the TMA descriptor a GEMV uses for a [rows][row_bytes] weight
 // matrix, or returns CN_ERR_UNSUPPORTED if the layout cannot be tiled

@@ -843,6 +843,15 @@ int cn_llama_decode(cn_llama* m, const int* tokens, const int* pos, int batch, f
     return CN_OK;
 }
 
+int cn_llama_sample(cn_llama* m, int batch, float temperature, int top_k, float top_p, const float* r_host,
+                    int* tokens_host) {
+    CN_CHECK(m, CN_ERR_INVALID_ARG, "null model");
+    CN_CHECK(batch >= 1 && batch <= m->cfg.max_batch, CN_ERR_INVALID_ARG, "batch %d outside [1, %d]", batch,
+             m->cfg.max_batch);
+    cudaSetDevice(m->ctx->device);
+    return sample_launch(m->ctx, m->logits, m->cfg.vocab, batch, temperature, top_k, top_p, r_host, tokens_host);
+}
+
 int cn_llama_set_inputs(cn_llama* m, const int* tokens, const int* pos, int batch) {
     CN_CHECK(m && tokens && pos, CN_ERR_INVALID_ARG, "null argument");
     CN_CHECK(batch >= 1 && batch <= m->cfg.max_batch, CN_ERR_INVALID_ARG,

@@ -159,6 +159,16 @@ class CudaLlamaModel:
         """Enqueue one decode step on the device inputs (no host copies, no wait)."""
         check(N.lib().cn_llama_step(self.handle, batch), "cn_llama_step")
 
+    def sample(self, batch: int, temperature: float, top_k: int = 40, top_p: float = 0.9,
+               r=None) -> np.ndarray:
+        """TemperatureSampler.Sample on the device logits of the last step
+        (cn_llama_sample); r[b] = the caller's uniform draw per sequence."""
+        rr = np.ascontiguousarray(np.zeros(batch) if r is None else r, dtype=np.float32)
+        out = np.empty(batch, dtype=np.int32)
+        check(N.lib().cn_llama_sample(self.handle, batch, float(temperature), int(top_k), float(top_p),
+                                      rr.ctypes.data, out.ctypes.data), "cn_llama_sample")
+        return out
+
     def step_kernels(self, batch: int) -> int:
         n = C.c_int(0)
         check(N.lib().cn_llama_step_kernels(self.handle, batch, C.byref(n)), "cn_llama_step_kernels")

@@ -179,6 +179,11 @@ int cn_dequantize_dev(int type, const void* d_blocks, float* d_out, int64_t n_el
 int cn_matvec_dev(cn_ctx* ctx, int type, const void* d_w, int out_dim, int in_dim,
                   const float* d_x, float* d_y, int batch);
 
+/* cn_llama_sample on caller-owned device logits [batch][vocab] (ctx's stream;
+ * returns when tokens_host is written). */
+int cn_sample_dev(cn_ctx* ctx, const float* d_logits, int vocab, int batch, float temperature, int top_k,
+                  float top_p, const float* r_host, int* tokens_host);
+
 /* Prefill matmul of cn_matmul on device pointers, using ctx's scratch and
  * stream (enqueued; no synchronisation). */
 int cn_matmul_dev(cn_ctx* ctx, int type, const void* d_w, int out_dim, int in_dim,
@@ -272,6 +277,19 @@ int cn_llama_decode(cn_llama* m, const int* tokens, const int* pos, int batch, f
  * cn_llama_step of each batch size captures the CUDA graph. */
 int cn_llama_set_inputs(cn_llama* m, const int* tokens, const int* pos, int batch);
 int cn_llama_step(cn_llama* m, int batch);
+
+/* TemperatureSampler.Sample (Samplers/TemperatureSampler.cs:33-113) on the
+ * device, for the logits the last decode step left there (sequences
+ * 0..batch-1): logits * (1 / temperature), softmax, the top_k largest
+ * probabilities in descending order cut at the first running sum >= top_p,
+ * renormalised, then the first entry whose running sum exceeds r_host[b] --
+ * the caller's Random.NextDouble() draw, so the host keeps the reference's
+ * random stream.  temperature <= 0 returns the argmax (first maximum).
+ * top_k must be >= 1 when sampling.  tokens_host [batch].  Probabilities
+ * match the reference's to fp32 rounding (the softmax sum runs as a tree),
+ * so a draw within rounding of a boundary may pick the neighbouring entry. */
+int cn_llama_sample(cn_llama* m, int batch, float temperature, int top_k, float top_p, const float* r_host,
+                    int* tokens_host);
 /* Kernel launches one decode step makes for `batch` (nodes of its graph). */
 int cn_llama_step_kernels(cn_llama* m, int batch, int* out_count);
 /* Times one projection's fused dequant-GEMV as the step runs it (activation

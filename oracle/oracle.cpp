@@ -953,6 +953,99 @@ extern "C" int or_argmax(const float* logits, int n) {
     return best;
 }
 
+// TemperatureSampler.Sample (Samplers/TemperatureSampler.cs:33-113) with the
+// caller's draw r in place of _rng.NextDouble().  *margin receives the
+// smallest distance of a running sum to the value it was compared with (top_p
+// for the nucleus cut-off, r for the draw) up to the decision: results that
+// differ by less than fp32 rounding of the probabilities can only move a
+// decision whose margin is that small.
+static void samp_swap(float* p, int* ix, int a, int b) {
+    const float tf = p[a];
+    p[a] = p[b];
+    p[b] = tf;
+    const int ti = ix[a];
+    ix[a] = ix[b];
+    ix[b] = ti;
+}
+
+// PartialSortDescending (TemperatureSampler.cs:119-162): median-of-three
+// quickselect that leaves the k largest in p[0..k-1].
+static void samp_partial_sort(float* p, int* ix, int left, int right, int k) {
+    while (left < right) {
+        const int mid = left + (right - left) / 2;
+        if (p[mid] > p[left]) samp_swap(p, ix, left, mid);
+        if (p[right] > p[left]) samp_swap(p, ix, left, right);
+        if (p[mid] > p[right]) samp_swap(p, ix, mid, right);
+        const float pivot = p[right];
+        int store = left;
+        for (int i = left; i < right; i++)
+            if (p[i] > pivot) samp_swap(p, ix, i, store++);
+        samp_swap(p, ix, store, right);
+        if (store == k - 1) return;
+        if (store < k - 1) left = store + 1;
+        else right = store - 1;
+    }
+}
+
+extern "C" int or_sample_temperature(const float* logits, int vocab, float temperature, int top_k, float top_p,
+                                     float r, float* margin) {
+    *margin = INFINITY;
+    if (temperature <= 0.f) {
+        int best = 0;
+        float bv = logits[0];
+        for (int i = 1; i < vocab; i++)
+            if (logits[i] > bv) {
+                bv = logits[i];
+                best = i;
+            }
+        return best;
+    }
+    std::vector<float> p(vocab);
+    std::vector<int> ix(vocab);
+    const float inv_temp = 1.0f / temperature;
+    for (int i = 0; i < vocab; i++) {
+        p[i] = logits[i] * inv_temp;
+        ix[i] = i;
+    }
+    or_softmax(p.data(), vocab);
+    const int k = top_k < vocab ? top_k : vocab;
+    samp_partial_sort(p.data(), ix.data(), 0, vocab - 1, k);
+    // InsertionSortDescending (TemperatureSampler.cs:168-184)
+    for (int i = 1; i < k; i++) {
+        const float kp = p[i];
+        const int ki = ix[i];
+        int j = i - 1;
+        while (j >= 0 && p[j] < kp) {
+            p[j + 1] = p[j];
+            ix[j + 1] = ix[j];
+            j--;
+        }
+        p[j + 1] = kp;
+        ix[j + 1] = ki;
+    }
+    float cumulative = 0.f;
+    int cutoff = k;
+    for (int i = 0; i < k; i++) {
+        cumulative += p[i];
+        *margin = fminf(*margin, fabsf(cumulative - top_p));
+        if (cumulative >= top_p) {
+            cutoff = i + 1;
+            break;
+        }
+    }
+    float sum = 0.f;
+    for (int i = 0; i < cutoff; i++) sum += p[i];
+    const float inv_sum = 1.0f / sum;
+    for (int i = 0; i < cutoff; i++) p[i] *= inv_sum;
+    float acc = 0.f;
+    for (int i = 0; i < cutoff; i++) {
+        acc += p[i];
+        *margin = fminf(*margin, fabsf(r - acc));
+        if (r < acc) return ix[i];
+    }
+    return ix[cutoff - 1];
+}
+
 // ---------------------------------------------------------------------------
 // Llama forward (LlamaModel.cs:93-238)
 // ---------------------------------------------------------------------------

@@ -78,6 +78,10 @@ void or_rope(float* q, float* k, int pos, int head_dim, int n_heads,
              int n_kv_heads, float freq_base);
 void or_add(float* a, const float* b, int length);
 int or_argmax(const float* logits, int n);
+/* TemperatureSampler.Sample with the draw r given; *margin = distance of the
+ * closest running sum to its threshold (top_p or r). */
+int or_sample_temperature(const float* logits, int vocab, float temperature, int top_k, float top_p, float r,
+                          float* margin);
 
 /* Llama model restatement.  Tensors are passed as one flat array in the
  * order used by libchatnet_cuda's cn_llama_create:

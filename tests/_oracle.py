@@ -40,6 +40,7 @@ _SIG = {
     "or_rope": (None, [_fp, _fp, _i, _i, _i, _i, _f]),
     "or_add": (None, [_fp, _fp, _i]),
     "or_argmax": (_i, [_fp, _i]),
+    "or_sample_temperature": (_i, [_fp, _i, _f, _i, _f, _f, _fp]),
     "or_llama_forward": (_i, [C.POINTER(LlamaConfig), C.POINTER(_vp), C.POINTER(_i), _vp, _vp,
                               C.POINTER(_i), _i, _i, _fp, _i]),
     "or_llama_layers": (_i, [C.POINTER(LlamaConfig), C.POINTER(_vp), C.POINTER(_i), _vp, _vp,
@@ -66,6 +67,13 @@ class Oracle:
     def dot(self, type_: int, row: np.ndarray, x: np.ndarray) -> float:
         x = np.ascontiguousarray(x, dtype=np.float32)
         return float(self.lib.or_dot(type_, row.ctypes.data, fp(x), x.size))
+
+    def sample(self, logits: np.ndarray, temperature: float, top_k: int, top_p: float, r: float):
+        """TemperatureSampler.Sample with draw r: (token, decision margin)."""
+        lg = np.ascontiguousarray(logits, dtype=np.float32)
+        m = np.zeros(1, np.float32)
+        tok = self.lib.or_sample_temperature(fp(lg), lg.size, temperature, top_k, top_p, r, fp(m))
+        return int(tok), float(m[0])
 
     def matvec(self, type_: int, W: np.ndarray, x: np.ndarray, rows: int, nthreads: int = 0):
         x = np.ascontiguousarray(x, dtype=np.float32)
