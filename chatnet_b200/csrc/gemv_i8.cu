@@ -39,17 +39,22 @@ constexpr int kCons = 8;           // consumer warps, 16 rows each
 constexpr int kThreads = (kCons + 1) * 32;
 
 // Three CTAs per SM with three stages each when one n-tile of activation
-// digits suffices (batch 1, 2), else two CTAs with four stages.
-template <int NB>
+// digits suffices (batch 1, 2), else two CTAs with four stages.  DEEP: one
+// CTA per SM with ~200 KB of stages, for grids of at most one CTA per SM
+// (short or few rows, e.g. tensor-parallel shards): the bytes one CTA keeps
+// in flight, not the SM count, then bound the weight stream.
+template <int NB, int DEEP = 0>
 struct Geo {
     static constexpr int NT = n_tiles(NB);
     static constexpr int kRec = (rec_bytes(NT) + 127) / 128 * 128;
     static constexpr int kStage = kRaw + kRec;
-    static constexpr int kCtasPerSm = NT == 1 ? 3 : 2;
-    static constexpr int kStages = (NT == 1 ? 72 * 1024 : 110 * 1024) / kStage;
+    static constexpr int kCtasPerSm = DEEP ? 1 : NT == 1 ? 3 : 2;
+    static constexpr int kStages = (DEEP ? 200 * 1024 : NT == 1 ? 72 * 1024 : 110 * 1024) / kStage;
     static constexpr int kSmem = kStages * kStage + 256;
 };
 static_assert(Geo<1>::kStages >= 3 && Geo<3>::kStages >= 4 && Geo<8>::kStages >= 4, "pipeline depth");
+static_assert(Geo<1, 1>::kStages >= 8 && Geo<8, 1>::kStages >= 7 && Geo<8, 1>::kSmem <= 227 * 1024,
+              "deep pipeline depth");
 
 // Up to kMaxMats weight matrices with the same inner dimension share one
 // launch (and one activation record): their 128-row tiles are numbered one
@@ -220,11 +225,11 @@ __device__ void finish_subtile(const Args& a, int r, int t, int warp, int tile, 
 
 }  // namespace i8
 
-template <int NB>
-__global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB>::kCtasPerSm)
+template <int NB, int DEEP>
+__global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB, DEEP>::kCtasPerSm)
     gemv_i8_q4k_kernel(const __grid_constant__ i8::Maps maps, const i8::Args a) {
     using namespace i8;
-    using G = Geo<NB>;
+    using G = Geo<NB, DEEP>;
     constexpr int NT = G::NT;
     constexpr int kStages = G::kStages, kStage = G::kStage;
     constexpr int kRecB = rec_bytes(NT);
@@ -480,26 +485,53 @@ static int min_units_per_cta() {
     return v;
 }
 
-// Most CTAs that share one tile (CHATNET_GEMV_TILE_CAP, default 7).
-static int tile_share_cap() {
-    static int v = -1;
-    if (v < 0) {
+// Most CTAs that share one tile for batches of two n-tiles or more
+// (CHATNET_GEMV_TILE_CAP overrides, for every batch): 7, but 1 when a row has
+// at most 16 units, where the split-K fix-up of a shared tile costs more than
+// its extra parallelism saves.
+static int tile_cap_env() {
+    static int v = -2;
+    if (v == -2) {
         const char* e = getenv("CHATNET_GEMV_TILE_CAP");
-        v = e ? atoi(e) : 7;
-        if (v < 1) v = 1;
+        v = e ? (atoi(e) < 1 ? 1 : atoi(e)) : -1;
     }
     return v;
 }
+static int tile_share_cap(int units) {
+    const int v = tile_cap_env();
+    if (v > 0) return v;
+    return units <= 16 ? 1 : 7;
+}
 
 int gemv_i8_ctas(int sms, int tiles, int units, int batch) {
-    // every resident CTA, each at least min_units_per_cta() units (but at
-    // least one CTA per SM); at most 8 CTAs share a tile
     const int per_sm = i8::n_tiles(batch) == 1 ? i8::Geo<1>::kCtasPerSm : i8::Geo<8>::kCtasPerSm;
+    if (const char* e = getenv("CHATNET_GEMV_CTAS")) {  // experiments: a fixed grid
+        const int v = atoi(e);
+        if (v > 0) return v < per_sm * sms ? v : per_sm * sms;
+    }
     const int64_t total = (int64_t)tiles * units;
+    // One n-tile of activation digits (batch 1, 2): at most one CTA per SM,
+    // which then runs the deep pipeline (gemv_i8_run_group).  With at least
+    // as many tiles as SMs, one CTA per SM splits the units evenly; with
+    // fewer, s CTAs per tile: 1 for rows of at most 16 units (the split's
+    // fix-up costs more than it saves there), else the largest s <= 7 with
+    // tiles * s <= sms.  Measured on B200 (prep + GEMV replayed from a graph,
+    // batch 1, us), this grid against 444 three-stage CTAs: 57344x8192 50.6
+    // vs 54.5, 10240x8192 15.6 vs 20.8, 8192x28672 29.3 vs 39.6, 8192x3584
+    // 9.2 vs 19.7, 8192x1024 5.4 vs 9.0.
+    if (i8::n_tiles(batch) == 1 && tile_cap_env() < 0) {
+        if (tiles >= sms) return sms;
+        int sh = units <= 16 ? 1 : sms / tiles;
+        sh = sh < 1 ? 1 : sh > 7 ? 7 : sh;
+        if (sh > units) sh = units;
+        return tiles * sh;
+    }
+    // otherwise every resident CTA, each at least min_units_per_cta() units
+    // (but at least one CTA per SM); at most tile_share_cap() CTAs per tile
     int64_t want = total / min_units_per_cta();
     if (want < sms) want = total / 2 < sms ? total / 2 : sms;
     if (want < 1) want = 1;
-    const int64_t cap = (int64_t)tiles * tile_share_cap();
+    const int64_t cap = (int64_t)tiles * tile_share_cap(units);
     if (want > cap) want = cap;
     return per_sm * sms < want ? per_sm * sms : (int)want;
 }
@@ -509,16 +541,21 @@ size_t gemv_i8_xbytes(int64_t cols, int batch) {
 }
 size_t gemv_i8_partial_bytes(int ctas) { return (size_t)2 * ctas * i8::kRows * 8 * sizeof(float); }
 
+static int g_sms[64] = {0};
+
 int gemv_i8_prepare() {
     static bool done[64] = {false};
     int dev = 0;
     CN_CUDA(cudaGetDevice(&dev));
     if (done[dev & 63]) return CN_OK;
-#define CN_ATTR(NB)                                                                               \
-    CN_CUDA(cudaFuncSetAttribute(gemv_i8_q4k_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                 i8::Geo<NB>::kSmem));
+#define CN_ATTR(NB)                                                                                   \
+    CN_CUDA(cudaFuncSetAttribute(gemv_i8_q4k_kernel<NB, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
+                                 i8::Geo<NB, 0>::kSmem));                                                 \
+    CN_CUDA(cudaFuncSetAttribute(gemv_i8_q4k_kernel<NB, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
+                                 i8::Geo<NB, 1>::kSmem));
     CN_ATTR(1) CN_ATTR(2) CN_ATTR(3) CN_ATTR(4) CN_ATTR(5) CN_ATTR(6) CN_ATTR(7) CN_ATTR(8)
 #undef CN_ATTR
+    CN_CUDA(cudaDeviceGetAttribute(&g_sms[dev & 63], cudaDevAttrMultiProcessorCount, dev));
     done[dev & 63] = true;
     return CN_OK;
 }
@@ -554,11 +591,18 @@ int gemv_i8_run_group(cudaStream_t st, uint32_t* err, int nmat, const CUtensorMa
     a.counters = counters;
     a.err = err;
     if (xo) a.xo = *xo;
+    int dev = 0;
+    CN_CUDA(cudaGetDevice(&dev));
+    const bool deep = ctas <= g_sms[dev & 63];  // one CTA per SM: the deep pipeline
     switch (batch) {
 #define CN_I8(NB)                                                                                  \
     case NB:                                                                                       \
-        CN_CUDA(launch_k(true, gemv_i8_q4k_kernel<NB>, dim3(ctas), dim3(i8::kThreads),             \
-                         (size_t)i8::Geo<NB>::kSmem, st, mp, a));                                  \
+        if (deep)                                                                                  \
+            CN_CUDA(launch_k(true, gemv_i8_q4k_kernel<NB, 1>, dim3(ctas), dim3(i8::kThreads),      \
+                             (size_t)i8::Geo<NB, 1>::kSmem, st, mp, a));                           \
+        else                                                                                       \
+            CN_CUDA(launch_k(true, gemv_i8_q4k_kernel<NB, 0>, dim3(ctas), dim3(i8::kThreads),      \
+                             (size_t)i8::Geo<NB, 0>::kSmem, st, mp, a));                           \
         break;
         CN_I8(1) CN_I8(2) CN_I8(3) CN_I8(4) CN_I8(5) CN_I8(6) CN_I8(7) CN_I8(8)
 #undef CN_I8
