@@ -9,7 +9,9 @@
 //
 //  * A producer warp streams [128 rows x one 144-byte super-block] of raw
 //    blocks per unit (2-D TMA) plus the unit's activation record (bulk copy,
-//    gemv_i8.cuh) into a ring of shared-memory stages; two CTAs per SM.
+//    gemv_i8.cuh) into a ring of shared-memory stages: at batch 1-2 one CTA
+//    per SM with ~200 KB of stages (the deep instantiation), else 2-3 CTAs
+//    per SM with 3-4 stages each.
 //  * Eight consumer warps own 16 rows each.  One ldmatrix.x4 hands a warp the
 //    quant words of two sub-blocks for its 16 rows, already in the A-fragment
 //    layout of m16n8k32 (row g, bytes 4t..4t+3 of the sub-block's 16 bytes:
