@@ -588,8 +588,11 @@ __global__ void xprep_kernel(const float* __restrict__ x, int K, int batch, Prep
 // writes its own 256-value slice of x_out = x_in + delta (when delta is
 // given) and of y = x * (1 / sqrt(sum(x^2)/n + eps)) * w, elementwise in the
 // reference's order, and emits the slice's record.  x_out must not alias
-// x_in (other CTAs still read x_in).
-constexpr int kNormThreads = 256;
+// x_in (other CTAs still read x_in).  512 threads: under tensor parallelism
+// the whole-row sum reads every rank's pairs of the row (512 KB at 8 ranks
+// and dim 8192), and each pass of the loop is one round trip, so more
+// threads mean fewer passes.
+constexpr int kNormThreads = 512;
 
 // Bounded wait of one thread for an exchange: every rank's flag must reach
 // this use's sequence number; on timeout the error word is raised and the
@@ -757,7 +760,7 @@ __global__ void __launch_bounds__(kNormThreads)
     for (int i = 0; i < kNormThreads / 32; i++) ss += red[i];
     const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
     const int i = u * 256 + tid;
-    if (i < n) {
+    if (tid < 256 && i < n) {
         float v = xr[i];
         if (dr || xbase || llbase) {
             float d;
