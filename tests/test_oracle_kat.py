@@ -60,3 +60,32 @@ def test_half_roundtrip_exhaustive(oracle):
                          for s in (1e-6, 1e-3, 1, 100, 6e4)])
     got = np.array([oracle.lib.or_float_to_half(float(v)) for v in xs], dtype=np.uint16)
     np.testing.assert_array_equal(got, xs.astype(np.float16).view(np.uint16))
+
+
+# Every codec the oracle restates: (type, elements per block, bytes per block,
+# offsets of fp16 scale fields)
+_CODECS = [(2, 32, 18, (0,)), (3, 32, 20, (0, 2)), (6, 32, 22, (0,)), (7, 32, 24, (0, 2)),
+           (8, 32, 34, (0,)), (10, 256, 84, (80, 82)), (11, 256, 110, (108,)), (12, 256, 144, (0, 2)),
+           (13, 256, 176, (0, 2)), (14, 256, 210, (208,)), (15, 256, 292, ()), (20, 32, 18, (0,)),
+           (23, 256, 136, (0,))]
+
+
+@pytest.mark.parametrize("t,blk,bpb,halves", _CODECS, ids=lambda v: str(v))
+def test_dot_matches_dequantize_random(oracle, t, blk, bpb, halves):
+    """Each codec's fused DotProduct agrees with its Dequantize on random
+    blocks (the two restated code paths of one format check each other)."""
+    rng = np.random.default_rng(t)
+    nb = 2048 // blk
+    b = rng.integers(0, 256, size=(nb, bpb), dtype=np.uint8)
+    for off in halves:
+        b[:, off:off + 2] = (np.abs(rng.standard_normal(nb)) * 0.01).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    if t == 15:  # Q8_K: fp32 scale
+        b[:, 0:4] = (np.abs(rng.standard_normal(nb)) * 0.01).astype("<f4").view(np.uint8).reshape(nb, 4)
+    blocks = b.ravel()
+    x = rng.standard_normal(2048).astype(np.float32)
+    deq = oracle.dequantize(t, blocks, 2048).astype(np.float64)
+    assert np.all(np.isfinite(deq))
+    want = float(np.dot(deq, x))
+    got = oracle.dot(t, blocks, x)
+    scale = float(np.sum(np.abs(deq * x))) + 1e-30
+    assert abs(got - want) <= 1e-5 * scale, (got, want)
