@@ -110,7 +110,8 @@ int encode_tiled_2d(CUtensorMapDataType dt, void* base, const cuuint64_t (&dims)
                     CUtensorMapSwizzle swz, CUtensorMap* out);
 
 // Prefill dequant-matmul (matmul.cu): y[i][t][r] (+)= dot(W_i[r], x[t]) for
-// M tokens and nmat <= 3 matrices of one weight type (Q4_0 or Q4_K) with the
+// M tokens and nmat <= 3 matrices of one weight type (Q4_0, Q4_K, or Q6_K
+// with row bytes a multiple of 16) with the
 // same K (K % 256 == 0); x is fp16 [M][K] (16-byte aligned), y[i] fp32
 // [M][ldy[i]].  Token t's results are multiplied by xs[t] (x's inverse row
 // scale) when xs is not null.  wmaps[i] may be null (the weight map is then
@@ -118,7 +119,9 @@ int encode_tiled_2d(CUtensorMapDataType dt, void* base, const cuuint64_t (&dims)
 int matmul_quant(cudaStream_t st, uint32_t* err, int type, int nmat, const void* const* w,
                  const CUtensorMap* const* wmaps, const int64_t* rows, int64_t K, const __half* x, const float* xs,
                  int M, float* const* y, const int64_t* ldy, bool accumulate);
-inline bool matmul_type_ok(int type) { return type == CN_TYPE_Q4_0 || type == CN_TYPE_Q4_K; }
+inline bool matmul_type_ok(int type) {
+    return type == CN_TYPE_Q4_0 || type == CN_TYPE_Q4_K || type == CN_TYPE_Q6_K;
+}
 // M rows of n fp32 values -> fp16 rows scaled by a power of two each, the
 // inverses in inv[M] (prefill.cu); n % 4 == 0, x and y 16-byte aligned.
 int to_half_rows(cudaStream_t st, const float* x, __half* y, float* inv, int n, int M);

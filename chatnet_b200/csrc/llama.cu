@@ -28,7 +28,9 @@ namespace cn {
 enum { T_EMB = 0, T_OUT = 1, T_ONORM = 2 };
 enum { L_ANORM = 0, L_Q, L_K, L_V, L_O, L_FNORM, L_GATE, L_UP, L_DOWN };
 constexpr int kMaxBatch = 32;
-constexpr int kPrefillMin = 16;  // prompts of at least this many tokens take the prefill matmul
+// Prompts of at least m->prefill_min tokens (0: never) take the prefill
+// matmul in cn_llama_forward; off unless cn_llama_set_prefill turns it on.
+constexpr int kPrefillMin = 16;  // the smallest threshold cn_llama_set_prefill accepts
 
 struct Step {
     bool built = false;
@@ -69,6 +71,7 @@ struct cn_llama {
     // on first use: residual stream, q/k/v, gate/up (fp32), the fp16
     // operand of the next matmul, fp16 copies of the new k/v rows, token ids
     int pf_cap = 0;
+    int prefill_min = 0;  // cn_llama_forward's prefill threshold (0: sequential steps)
     float *pf_x = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_g = nullptr,
           *pf_u = nullptr;
     __half *pf_h = nullptr, *pf_kh = nullptr, *pf_vh = nullptr;
@@ -441,16 +444,19 @@ static void free_model(cn_llama* m) {
 // A weight tensor's TMA descriptor, or null (the matmul then encodes one).
 static const CUtensorMap* wmap(const cn_tensor* t) { return t->has_map ? &t->map : nullptr; }
 
-// Whether the model's projections can run on the prefill matmul (Q4_0 or
-// Q4_K with inner dimensions that are multiples of 256, one GPU).
+// Whether the model's projections can run on the prefill matmul (Q4_0, Q4_K,
+// or Q6_K with rows of a multiple of 16 bytes, inner dimensions multiples of
+// 256, one GPU).
 static bool prefill_supported(const cn_llama* m) {
     if (m->tp && m->tp->size > 1) return false;
     const cn_llama_config& c = m->cfg;
     if (c.dim % 256 != 0 || c.hidden_dim % 256 != 0 || (c.head_dim != 64 && c.head_dim != 128))
         return false;
     for (int l = 0; l < c.n_layers; l++)
-        for (int j : {L_Q, L_K, L_V, L_O, L_GATE, L_UP, L_DOWN})
-            if (!matmul_type_ok(LT(m, l, j)->type)) return false;
+        for (int j : {L_Q, L_K, L_V, L_O, L_GATE, L_UP, L_DOWN}) {
+            const cn_tensor* t = LT(m, l, j);
+            if (!matmul_type_ok(t->type) || (t->type == CN_TYPE_Q6_K && t->row_bytes % 16 != 0)) return false;
+        }
     return true;
 }
 
@@ -788,7 +794,7 @@ int cn_llama_prefill_hidden_dev(cn_llama* m, const float* x_dev, int n, int pos,
     CN_CHECK(n >= 1 && pos >= 0 && pos + n <= m->cfg.ctx_len, CN_ERR_INVALID_ARG,
              "positions [%d, %d) outside the context of %d", pos, pos + n, m->cfg.ctx_len);
     CN_CHECK(prefill_supported(m), CN_ERR_UNSUPPORTED,
-             "prefill needs Q4_0 or Q4_K projections, dim and hidden_dim multiples of 256, head_dim 64 or 128, one GPU");
+             "prefill needs Q4_0, Q4_K or 16-byte-row Q6_K projections, dim and hidden_dim multiples of 256, head_dim 64 or 128, one GPU");
     cudaSetDevice(m->ctx->device);
     cudaStream_t s = m->ctx->stream;
     int rc = prefill_reserve(m, n);
@@ -840,6 +846,14 @@ int cn_llama_decode(cn_llama* m, const int* tokens, const int* pos, int batch, f
     CN_CUDA(cudaStreamSynchronize(s));
     if ((rc = check_dev_err_reset(m))) return rc;
     if (argmax_host) memcpy(argmax_host, m->h_amax, batch * 4);
+    return CN_OK;
+}
+
+int cn_llama_set_prefill(cn_llama* m, int min_tokens) {
+    CN_CHECK(m, CN_ERR_INVALID_ARG, "null model");
+    CN_CHECK(min_tokens == 0 || min_tokens >= kPrefillMin, CN_ERR_INVALID_ARG,
+             "prefill threshold %d: 0 or at least %d", min_tokens, kPrefillMin);
+    m->prefill_min = min_tokens;
     return CN_OK;
 }
 
@@ -1034,7 +1048,7 @@ int cn_llama_forward(cn_llama* m, const int* tokens, int n, int pos, float* logi
     CN_CHECK(n >= 1, CN_ERR_INVALID_ARG, "no tokens");
     CN_CHECK(pos >= 0 && pos + n <= m->cfg.ctx_len, CN_ERR_INVALID_ARG,
              "positions [%d, %d) outside the context of %d", pos, pos + n, m->cfg.ctx_len);
-    if (n >= kPrefillMin && prefill_supported(m)) {
+    if (m->prefill_min > 0 && n >= m->prefill_min && prefill_supported(m)) {
         // the prompt in one pass: embed n tokens, all layers on the matmul,
         // then the head of the last token through the decode GEMV
         for (int t = 0; t < n; t++)

@@ -55,8 +55,22 @@ constexpr int kKS = 128;                 // K positions per stage (two 128-byte 
 constexpr int kStages = 4;
 constexpr int kBHalf = kNT * 64 * 2;     // 16 KB: one swizzled tile of 64 positions
 constexpr int kBStage = 2 * kBHalf;      // 32 KB of activations per stage
-constexpr int kRaw = 144 * kRows;        // raw Q4_0 bytes of 8 blocks x 128 rows (2 stages)
-constexpr int kRawStages = 5;
+// Raw weight ring: one stage holds 256 positions of 128 rows -- 144 bytes
+// per row for Q4_0 (8 blocks) and Q4_K (one super-block).  Q6_K's 210-byte
+// super-blocks are only 2-byte aligned, so its stages hold the 16-byte
+// aligned 240-byte window around each (as the decode GEMV loads them).
+// Both rings take 92,160 bytes.
+template <int WT>
+struct RawGeo {
+    static constexpr int kRow = WT == CN_TYPE_Q6_K ? 240 : 144;
+    static constexpr int kBytes = kRow * 128;
+    static constexpr int kStages = WT == CN_TYPE_Q6_K ? 3 : 5;
+};
+constexpr int kRawStages = 5;  // barriers reserved (the most any ring uses)
+constexpr int kRawRing = 5 * 144 * 128;
+static_assert(RawGeo<CN_TYPE_Q6_K>::kStages * RawGeo<CN_TYPE_Q6_K>::kBytes == kRawRing &&
+                  RawGeo<CN_TYPE_Q4_K>::kStages * RawGeo<CN_TYPE_Q4_K>::kBytes == kRawRing,
+              "raw rings");
 constexpr int kDBufs = 2;                // accumulator buffers
 constexpr int kRawOff = kStages * kBStage;
 constexpr int kACols = kKS / 2;          // tensor-memory columns of one A stage (2 fp16 each)
@@ -67,11 +81,12 @@ constexpr int kEpi = 128;                // epilogue threads: warps 8-11
 constexpr int kDecodeWarps = kDecode / 32, kEpiWarps = kEpi / 32;  // barrier arrivals (one per warp)
 constexpr int kThreads = kDecode + kEpi + 64;  // warp 12 TMA, warp 13 MMA
 constexpr int kWarpEpi0 = 8, kWarpTma = 12, kWarpMma = 13;
-constexpr int kBarOff = kRawOff + kRawStages * kRaw;
+constexpr int kBarOff = kRawOff + kRawRing;
 constexpr int kSmem = kBarOff + 512 + 1024;  // barriers, and slack to align the ring to 1 KB
 constexpr int kMaxMats = 3;
 static_assert(kACol + kStages * kACols <= kTmemCols, "tensor memory plan");
-static_assert(kRawOff % 1024 == 0 && kRaw % 128 == 0 && kBarOff % 8 == 0, "ring alignment");
+static_assert(kRawOff % 1024 == 0 && RawGeo<CN_TYPE_Q6_K>::kBytes % 128 == 0 && kBarOff % 8 == 0,
+              "ring alignment");
 
 // TMA descriptors: the activations and each weight matrix (8-byte elements,
 // rows x row bytes, boxes of 144 bytes x 128 rows, as for the decode GEMV).
@@ -92,7 +107,7 @@ struct Args {
     int64_t rows[kMaxMats];
     float* y[kMaxMats];         // [M][ldy[m]]
     int64_t ldy[kMaxMats];
-    int64_t rb;                 // bytes per weight row (K / 32 * 18)
+    int64_t rb;                 // bytes per weight row
     const float* xs;            // per-token factor of the result (x's inverse scale), or null
     int M, K;                   // K % 256 == 0
     int accumulate;             // 1: Y += result, 0: Y = result
@@ -171,6 +186,39 @@ __device__ __forceinline__ void expand_q4k_pair(const uint32_t (&qw)[8], uint32_
                 o[16 * blk + 8 + 2 * i + h] = h2_fma(hi, d2, ndm2[blk]);
             }
         }
+    }
+}
+
+// Expands this thread's 64 positions of half h of a Q6_K super-block (sb:
+// its first byte in shared memory, 2-byte aligned) into fp16, o[c] holding
+// positions 2c, 2c + 1.  Position 32s + l of the half (DequantQ6K.cs:37-88)
+// takes the low (s < 2) or high nibble of ql[64h + l + 32(s & 1)], bits 2s of
+// qh[32h + l] and scale 8h + l/16 + 2s, and is (d * sc) * (q - 32) in fp32 --
+// the reference's value -- rounded once to fp16.  Warpgroup wg holds s = 2wg,
+// 2wg + 1: slice position j = ql byte 64h + j, nibble wg, qh bits 4wg + 2(j/32).
+__device__ __forceinline__ void expand_q6k_half(const uint8_t* sb, int h, int wg, float d, uint32_t (&o)[32]) {
+    uint32_t qh[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) qh[k] = lds_u32_a2(sb + 128 + 32 * h + 4 * k);
+    float dsc[4];  // [j / 32][l / 16]
+#pragma unroll
+    for (int jj = 0; jj < 2; jj++)
+#pragma unroll
+        for (int ll = 0; ll < 2; ll++)
+            dsc[2 * jj + ll] = __fmul_rn(d, (float)(int8_t)sb[192 + 8 * h + ll + 4 * wg + 2 * jj]);
+#pragma unroll
+    for (int k = 0; k < 16; k++) {
+        const uint32_t w = lds_u32_a2(sb + 64 * h + 4 * k);
+        const uint32_t nib = (wg ? (w >> 4) : w) & 0x0F0F0F0Fu;
+        const int jj = k >> 3;
+        const uint32_t hb = (qh[k & 7] >> (4 * wg + 2 * jj)) & 0x03030303u;
+        const uint32_t q4 = nib | (hb << 4);
+        const float t = dsc[2 * jj + ((k & 7) >> 2)];
+        float v[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) v[e] = __fmul_rn(t, (float)((int)((q4 >> (8 * e)) & 0xFFu) - 32));
+        o[2 * k] = pack_half2(v[0], v[1]);
+        o[2 * k + 1] = pack_half2(v[2], v[3]);
     }
 }
 
@@ -255,6 +303,7 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t addr) {
 template <int WT>
 __global__ void __launch_bounds__(mm::kThreads, 1)
     matmul_q_kernel(const __grid_constant__ mm::Maps maps, const mm::Args a) {
+    using RG = mm::RawGeo<WT>;
     using namespace mm;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -318,14 +367,18 @@ __global__ void __launch_bounds__(mm::kThreads, 1)
                 const CUtensorMap* wmap = m == 2 ? &maps.w[2] : m == 1 ? &maps.w[1] : &maps.w[0];
                 for (int s = 0; s < nst; s++) {
                     if ((s & 1) == 0) {
-                        const int rs = gc % kRawStages;
-                        if (gc >= kRawStages && !mbar_wait(&raw_empty[rs], (uint32_t)((gc / kRawStages) - 1) & 1)) {
+                        const int rs = gc % RG::kStages;
+                        if (gc >= RG::kStages &&
+                            !mbar_wait(&raw_empty[rs], (uint32_t)((gc / RG::kStages) - 1) & 1)) {
                             atomicOr(a.err, kErrTimeout);
                             ok = false;
                             break;
                         }
-                        mbar_expect_tx(&raw_full[rs], kRaw);
-                        tma_load_2d(smem + kRawOff + rs * kRaw, wmap, 18 * (s / 2), (int)row0, &raw_full[rs]);
+                        // x in 8-byte elements: 18 per Q4 run; Q6_K: the 16-byte
+                        // aligned start of super-block s / 2
+                        const int x = WT == CN_TYPE_Q6_K ? ((210 * (s / 2)) >> 4) * 2 : 18 * (s / 2);
+                        mbar_expect_tx(&raw_full[rs], RG::kBytes);
+                        tma_load_2d(smem + kRawOff + rs * RG::kBytes, wmap, x, (int)row0, &raw_full[rs]);
                         gc++;
                     }
                     const int slot = gs % kStages;
@@ -343,8 +396,8 @@ __global__ void __launch_bounds__(mm::kThreads, 1)
             // no copy may still be landing when the CTA exits
             for (int i = gs - kStages < 0 ? 0 : gs - kStages; i < gs; i++)
                 mbar_wait(&full[i % kStages], (uint32_t)(i / kStages) & 1);
-            for (int i = gc - kRawStages < 0 ? 0 : gc - kRawStages; i < gc; i++)
-                mbar_wait(&raw_full[i % kRawStages], (uint32_t)(i / kRawStages) & 1);
+            for (int i = gc - RG::kStages < 0 ? 0 : gc - RG::kStages; i < gc; i++)
+                mbar_wait(&raw_full[i % RG::kStages], (uint32_t)(i / RG::kStages) & 1);
         }
     } else if (warp == kWarpMma) {
         // ---- MMA issuer ----
@@ -454,17 +507,42 @@ __global__ void __launch_bounds__(mm::kThreads, 1)
         int gs = 0, gc = 0;
         for (int t = blockIdx.x; t < a.tiles; t += gridDim.x) {
             for (int c = 0; c < nch; c++, gc++) {
-                const int rs = gc % kRawStages;
-                if (!failed && !mbar_wait(&raw_full[rs], (uint32_t)(gc / kRawStages) & 1)) {
+                const int rs = gc % RG::kStages;
+                if (!failed && !mbar_wait(&raw_full[rs], (uint32_t)(gc / RG::kStages) & 1)) {
                     atomicOr(a.err, kErrTimeout);
                     failed = true;
+                }
+                if (WT == CN_TYPE_Q6_K) {
+                    // read in place (the window stays until both stages are
+                    // expanded); d is the fp16 at byte 208 of the super-block
+                    const uint8_t* sb = raw + rs * RG::kBytes + r * RG::kRow + ((210 * c) & 15);
+                    const float d = half_bits_to_float(lds_u16(sb + 208));
+#pragma unroll 1
+                    for (int q = 0; q < 2; q++, gs++) {
+                        const int slot = gs % kStages;
+                        if (gs >= kStages && !failed &&
+                            !mbar_wait(&empty[slot], (uint32_t)((gs / kStages) - 1) & 1)) {
+                            atomicOr(a.err, kErrTimeout);
+                            failed = true;
+                        }
+                        tc_fence_after();
+                        uint32_t o[32];
+                        expand_q6k_half(sb, q, wg, d, o);
+                        tmem_st32(lane_base + kACol + slot * kACols + 32 * wg, o);
+                        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                        tc_fence_before();
+                        if (lane == 0) mbar_arrive(&full[slot]);
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&raw_empty[rs]);
+                    continue;
                 }
                 // this thread's words of its row (rows past the matrix arrive as
                 // zeros).  Q4_0: blocks 4q + 2wg, 4q + 2wg + 1 of stage q = words
                 // 18q + 9wg .. 18q + 9wg + 8 of the row's 36.  Q4_K: the header
                 // (words 0-3: d, dmin, packed scales) and sub-blocks 4q + 2wg,
                 // 4q + 2wg + 1 = words 4 + 16q + 8wg .. +7.
-                const uint32_t* row32 = reinterpret_cast<const uint32_t*>(raw + rs * kRaw + r * 144);
+                const uint32_t* row32 = reinterpret_cast<const uint32_t*>(raw + rs * RG::kBytes + r * RG::kRow);
                 uint32_t cur[18];
                 uint32_t d2 = 0, sc2[2][2], ndm2[2][2];  // Q4_K: d, [stage][sub-block] sc and -dmin * m
                 if (WT == CN_TYPE_Q4_0) {
@@ -563,8 +641,7 @@ int encode_act_map(const __half* x, int M, int64_t K, CUtensorMap* out) {
 int matmul_quant(cudaStream_t st, uint32_t* err, int type, int nmat, const void* const* w,
                  const CUtensorMap* const* wmaps, const int64_t* rows, int64_t K, const __half* x, const float* xs,
                  int M, float* const* y, const int64_t* ldy, bool accumulate) {
-    CN_CHECK(type == CN_TYPE_Q4_0 || type == CN_TYPE_Q4_K, CN_ERR_UNSUPPORTED,
-             "matmul: weight type %d (Q4_0 or Q4_K)", type);
+    CN_CHECK(matmul_type_ok(type), CN_ERR_UNSUPPORTED, "matmul: weight type %d (Q4_0, Q4_K or Q6_K)", type);
     CN_CHECK(nmat >= 1 && nmat <= mm::kMaxMats && K > 0 && K % 256 == 0 && M >= 1, CN_ERR_INVALID_ARG,
              "matmul: bad shape (nmat %d, K %lld, M %d)", nmat, (long long)K, M);
     static bool attr = false;
@@ -572,6 +649,8 @@ int matmul_quant(cudaStream_t st, uint32_t* err, int type, int nmat, const void*
         CN_CUDA(cudaFuncSetAttribute(matmul_q_kernel<CN_TYPE_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      mm::kSmem));
         CN_CUDA(cudaFuncSetAttribute(matmul_q_kernel<CN_TYPE_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     mm::kSmem));
+        CN_CUDA(cudaFuncSetAttribute(matmul_q_kernel<CN_TYPE_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      mm::kSmem));
         attr = true;
     }
@@ -586,7 +665,7 @@ int matmul_quant(cudaStream_t st, uint32_t* err, int type, int nmat, const void*
         if (wmaps && wmaps[mi]) {
             maps.w[i] = *wmaps[mi];
         } else {
-            int rc = encode_weight_map(type, w[mi], rows[mi], (uint64_t)(K / 32 * 18), &maps.w[i]);
+            int rc = encode_weight_map(type, w[mi], rows[mi], row_bytes(type, K), &maps.w[i]);
             if (rc) return rc;
         }
         a.rows[i] = rows[mi];
@@ -601,7 +680,7 @@ int matmul_quant(cudaStream_t st, uint32_t* err, int type, int nmat, const void*
     a.toff[nmat] = tiles;
     a.tok_tiles = (M + mm::kNT - 1) / mm::kNT;
     a.tiles = tiles * a.tok_tiles;
-    a.rb = K / 32 * 18;
+    a.rb = (int64_t)row_bytes(type, K);
     a.xs = xs;
     a.M = M;
     a.K = (int)K;
@@ -618,8 +697,10 @@ int matmul_quant(cudaStream_t st, uint32_t* err, int type, int nmat, const void*
     const dim3 grid(a.tiles < sms ? a.tiles : sms);  // persistent: one CTA per SM
     if (type == CN_TYPE_Q4_0)
         CN_CUDA(launch_k(false, matmul_q_kernel<CN_TYPE_Q4_0>, grid, dim3(mm::kThreads), (size_t)mm::kSmem, st, maps, a));
-    else
+    else if (type == CN_TYPE_Q4_K)
         CN_CUDA(launch_k(false, matmul_q_kernel<CN_TYPE_Q4_K>, grid, dim3(mm::kThreads), (size_t)mm::kSmem, st, maps, a));
+    else
+        CN_CUDA(launch_k(false, matmul_q_kernel<CN_TYPE_Q6_K>, grid, dim3(mm::kThreads), (size_t)mm::kSmem, st, maps, a));
     return CN_OK;
 }
 

@@ -155,6 +155,11 @@ class CudaLlamaModel:
                                           pos.ctypes.data_as(C.POINTER(C.c_int)), tok.size),
               "cn_llama_set_inputs")
 
+    def set_prefill(self, min_tokens: int) -> None:
+        """Prompts of min_tokens (>= 16) or more take the prefill pass in
+        forward(); 0 (the default) keeps the reference's token-by-token loop."""
+        check(N.lib().cn_llama_set_prefill(self.handle, int(min_tokens)), "cn_llama_set_prefill")
+
     def step(self, batch: int) -> None:
         """Enqueue one decode step on the device inputs (no host copies, no wait)."""
         check(N.lib().cn_llama_step(self.handle, batch), "cn_llama_step")

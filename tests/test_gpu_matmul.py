@@ -35,10 +35,12 @@ MATMUL_CASES = [
 ]
 
 
-@pytest.mark.parametrize("wtype", [cn.TYPE_Q4_0, cn.TYPE_Q4_K], ids=["q4_0", "q4_k"])
+@pytest.mark.parametrize("wtype", [cn.TYPE_Q4_0, cn.TYPE_Q4_K, cn.TYPE_Q6_K], ids=["q4_0", "q4_k", "q6_k"])
 @pytest.mark.parametrize("rows,cols,tokens", MATMUL_CASES,
                          ids=[f"{r}x{c}-m{m}" for r, c, m in MATMUL_CASES])
 def test_matmul_parity(ctx, oracle, rows, cols, tokens, wtype):
+    if wtype == cn.TYPE_Q6_K and cn.byte_size(wtype, cols) % 16:
+        pytest.skip("Q6_K rows of this width are not 16-byte multiples (no TMA tiling)")
     blocks = _w(rows, cols, f"mm.{rows}x{cols}", wtype)
     W = ctx.upload(blocks, wtype, rows, cols)
     x = _x(tokens, cols, f"mm.x.{rows}.{cols}.{tokens}")
@@ -68,9 +70,12 @@ def test_matmul_rejects_bad_input(ctx):
     W = ctx.upload(_w(16, 96, "mm.bad"), cn.TYPE_Q4_0, 16, 96)  # cols not a multiple of 256
     with pytest.raises(ValueError):
         ctx.matmul(W, np.zeros((4, 96), np.float32))
-    W6 = ctx.upload(cn.synth_fill(cn.TYPE_Q6_K, 16, 256, 5), cn.TYPE_Q6_K, 16, 256)
+    W6 = ctx.upload(cn.synth_fill(cn.TYPE_Q6_K, 16, 256, 5), cn.TYPE_Q6_K, 16, 256)  # 210-byte rows
     with pytest.raises((ValueError, NotImplementedError)):
         ctx.matmul(W6, np.zeros((4, 256), np.float32))
+    W2 = ctx.upload(np.zeros(16 * 84, np.uint8), cn.TYPE_Q2_K, 16, 256)  # no matmul decoder
+    with pytest.raises((ValueError, NotImplementedError)):
+        ctx.matmul(W2, np.zeros((4, 256), np.float32))
 
 
 def test_matmul_q4_k_scale_extremes(ctx, oracle):
