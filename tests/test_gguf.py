@@ -26,7 +26,11 @@ def test_descriptors_offsets_and_bytes(tmp_path):
     tensors = [("a.weight", cn.TYPE_Q4_0, (64, 3), _raw(cn.TYPE_Q4_0, 3, 64, 1)),
                ("b.weight", cn.TYPE_Q4_K, (512, 2), _raw(cn.TYPE_Q4_K, 2, 512, 2)),
                ("c.weight", cn.TYPE_Q6_K, (256, 5), _raw(cn.TYPE_Q6_K, 5, 256, 3)),
-               ("norm.weight", cn.TYPE_F32, (7,), _raw(cn.TYPE_F32, 1, 7, 4))]
+               ("norm.weight", cn.TYPE_F32, (7,), _raw(cn.TYPE_F32, 1, 7, 4)),
+               # the generic codecs: GGUF byte sizes from cn_byte_size (GgufTensorInfo.ByteSize)
+               ("q5k.weight", cn.TYPE_Q5_K, (512, 3), bytes(range(256)) * 4 + bytes(32)),
+               ("iq4nl.weight", cn.TYPE_IQ4_NL, (64, 2), bytes(72)),
+               ("q8k.weight", cn.TYPE_Q8_K, (256, 1), bytes(292))]
     md = [("general.architecture", gw.STR, "llama"), ("x.u8", gw.U8, 7), ("x.i8", gw.I8, -3),
           ("x.u16", gw.U16, 500), ("x.i16", gw.I16, -500), ("x.i32", gw.I32, -70000),
           ("x.u64", gw.U64, 1 << 40), ("x.i64", gw.I64, -(1 << 40)), ("x.f64", gw.F64, 0.125),
