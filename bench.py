@@ -4,6 +4,7 @@ config 4) on B200, through libchatnet_cuda.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--config 4|1]
     python bench.py --config 3 ...           # prefill: 512 tokens through one 7B layer
+    python bench.py --config 0|2 ...         # Q-matvec HBM GB/s (one JSON line per shape/batch)
     python bench.py --impl reference ...     # the reference's CPU algorithm (oracle port)
 
 A step is one decode step of `batch` sequences (each at position 2047 of a
@@ -21,7 +22,7 @@ Printed JSON line (rank 0):
              gate/up projections, 28672 x 8192) timed alone on the context
              stream: algorithmic bytes per launch / mean launch time
   cpu_baseline  the oracle port of the reference's C# CPU path timed on the
-             host's cores on a 2-layer sample, extrapolated to 80 layers
+             host's cores over the whole step (CpuSample)
 With --gpus N > 1 the ranks run the model tensor-parallel (default; the
 same sequences, strong scaling) or as independent replicas (--parallel
 replicas, weak scaling).
@@ -31,6 +32,17 @@ one Llama-2-7B-shaped Q4_0 layer (cn_llama_prefill_hidden_dev); `value` is
 tokens/s, `e2e` adds the copy of the 8 MiB input from pinned host memory and
 of the output back, and the roofline is the gate/up matmul's TFLOP/s against
 the measured dense bf16 peak.  With N > 1 the ranks run replicas.
+
+--config 0 / --config 2 (Q-matvec GB/s): a step is one fused dequant-GEMV
+(x-prep + GEMV, the work of cn_matvec_dev) of config 0's Q4_0 5632x2048 matrix
+or of each config-2 shape (Q4_K 4096x4096, 11008x4096, 4096x11008; Q6_K
+32000x4096) at batches 1, 4, 16 and 32.  The calls cycle through enough
+distinct seeded copies of the matrix to fill twice the 126 MB L2 (cold L2)
+and run from one CUDA graph of >= 100 calls (no host gaps); `value` is the
+algorithmic bytes (weights + x + y) per call over the median of the
+replays' per-call times, `e2e` the same through cn_matvec with host buffers
+(x in, y out, synchronous), and `cpu_baseline` the oracle's MatVecMul port
+on the same matrix on all host cores.
 """
 from __future__ import annotations
 
@@ -58,8 +70,9 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--batch", type=int, default=1)
-    ap.add_argument("--config", type=int, default=4, choices=(1, 3, 4))
+    ap.add_argument("--batch", type=int, default=None,
+                    help="sequences per step (default 1; --config 2: all of 1, 4, 16, 32 unless given)")
+    ap.add_argument("--config", type=int, default=4, choices=(0, 1, 2, 3, 4))
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--parallel", default="tp", choices=("tp", "replicas"),
                     help="N > 1: tensor parallelism over the N GPUs (default), or N independent replicas")
@@ -182,9 +195,15 @@ def committed_traffic(kernel_key: str):
 # CPU baseline: the oracle port of the reference's C# path
 # ---------------------------------------------------------------------------
 class CpuSample:
-    """The oracle port of the reference's CPU path on a CPU_SAMPLE_LAYERS-layer
-    sample of the model (same seeded tensors as the device copy), timed per
-    token and extrapolated to the full depth (every layer costs the same)."""
+    """The oracle port of the reference's C# CPU path, one token through every
+    layer and lm_head, timed on the host's cores (the oracle's row split over
+    all threads, as Parallel.For does).  The tensors come from the oracle's own
+    generator, so this leg never loads libchatnet_cuda.  A model too large for
+    host memory (config 4: 38.5 GB) keeps the seeded weights of its first
+    `sample_layers` layers and runs layer l with those of layer
+    l % sample_layers: each layer still streams its 481 MB of weights from
+    DRAM (far above the host's caches), so the step costs what the full model's
+    would.  Batches cost batch x one sequence (the reference has no batching)."""
 
     def __init__(self, dc_full, batch: int):
         import ctypes as C
@@ -193,37 +212,215 @@ class CpuSample:
         from tests import _oracle
         self.C, self._o = C, _oracle
         self.full, self.batch = dc_full, batch
-        self.orc = _oracle.load()
-        dc = cf.with_layers(dc_full, CPU_SAMPLE_LAYERS)
+        self.orc = orc = _oracle.load()
+        L = dc_full.model.n_layers
+        self.sample_layers = L if L <= 22 else CPU_SAMPLE_LAYERS
+        dc = cf.with_layers(dc_full, self.sample_layers)
         self.dc = dc
-        host = cf.host_tensors(dc)
-        names = tensor_names(CPU_SAMPLE_LAYERS)
+        host = _oracle.host_tensors(orc, dc)
+        names = tensor_names(self.sample_layers)
         types = [cf.tensor_type(dc, n) for n in names]
-        k, v = cf.host_kv(dc, 0)
-        self.ol = _oracle.OracleLlama(self.orc, dc.model, host, types, names, k, v)
-        self.x0 = self.orc.dequantize(types[0], host["token_embd.weight"][cf.token(dc, 0)],
-                                      dc.model.dim)
+        k, v = _oracle.host_kv(orc, dc, 0)
+        self.ol = _oracle.OracleLlama(orc, dc.model, host, types, names, k, v)
+        self.x0 = orc.dequantize(types[0], host["token_embd.weight"][_oracle.token(orc, dc, 0)],
+                                 dc.model.dim)
         self.logits = np.empty(dc.model.vocab, np.float32)
 
     def run_once(self) -> float:
-        """Seconds for one step of `batch` sequences (extrapolated)."""
+        """Seconds for one step of `batch` sequences."""
         C, fp, ol, orc = self.C, self._o.fp, self.ol, self.orc
         x = self.x0.copy()
+        S, L = self.sample_layers, self.full.model.n_layers
+        rc = 0
         t0 = time.perf_counter()
-        rc = orc.lib.or_llama_layers(C.byref(ol.cfg), ol.ptrs, ol.types, ol.k.ctypes.data,
-                                     ol.v.ctypes.data, fp(x), self.dc.decode_pos, 0,
-                                     CPU_SAMPLE_LAYERS, 0)
-        t1 = time.perf_counter()
+        for l0 in range(0, L, S):
+            rc |= orc.lib.or_llama_layers(C.byref(ol.cfg), ol.ptrs, ol.types, ol.k.ctypes.data,
+                                          ol.v.ctypes.data, fp(x), self.dc.decode_pos, 0, min(S, L - l0), 0)
         rc |= orc.lib.or_llama_head(C.byref(ol.cfg), ol.ptrs, ol.types, fp(x), fp(self.logits), 0)
-        t2 = time.perf_counter()
+        t1 = time.perf_counter()
         assert rc == 0
-        per_token = (t1 - t0) * self.full.model.n_layers / CPU_SAMPLE_LAYERS + (t2 - t1)
-        return self.batch * per_token  # B independent forwards on the CPU path
+        return self.batch * (t1 - t0)
 
     def describe(self, reps: int) -> str:
-        return (f"{CPU_SAMPLE_LAYERS} of {self.full.model.n_layers} layers + lm_head per token "
-                f"({self.dc.model.dim}-dim, position {self.dc.decode_pos}), x{self.batch} "
-                f"sequences, median of {reps} runs, extrapolated linearly in layers")
+        m = self.full.model
+        reuse = ("" if self.sample_layers == m.n_layers else
+                 f" (weights of {self.sample_layers} seeded layers reused cyclically; each layer's "
+                 f"weights exceed the host caches)")
+        per = "" if self.batch == 1 else f", x{self.batch} sequences (batch = {self.batch} x one sequence)"
+        return (f"all {m.n_layers} layers + lm_head per token{reuse}, {m.dim}-dim, position "
+                f"{self.dc.decode_pos}{per}, median of {reps} runs, oracle port on {os.cpu_count()} host threads")
+
+
+# ---------------------------------------------------------------------------
+# configs 0 and 2: Q-matvec GB/s
+# ---------------------------------------------------------------------------
+MATVEC_CASES = {
+    0: [("q4_0", 5632, 2048, (1,))],
+    2: [("q4_k", 4096, 4096, (1, 4, 16, 32)), ("q4_k", 11008, 4096, (1, 4, 16, 32)),
+        ("q4_k", 4096, 11008, (1, 4, 16, 32)), ("q6_k", 32000, 4096, (1, 4, 16, 32))],
+}
+L2_BYTES = 126 * 2**20
+
+
+def matvec_dtype(name: str, batch: int) -> str:
+    if name == "q4_k" and batch <= 8 and os.environ.get("CHATNET_GEMV", "i8") not in ("tc", "mma"):
+        return "q4_k x int22 activation digits (int8 mma, exact) -> s32 -> f32"
+    return f"{name} x fp16(hi+lo) -> f32"
+
+
+def matvec_bytes(type_bytes_per_row: int, rows: int, cols: int, batch: int) -> int:
+    """Algorithmic bytes of one call: the weight blocks once, x and y once."""
+    return type_bytes_per_row * rows + 4 * batch * (rows + cols)
+
+
+def matvec_main(a, world: int, rank: int, local: int) -> int:
+    """One JSON line per (shape, batch) of config 0 or 2."""
+    from chatnet_b200.llama import LlamaConfig  # noqa: F401  (package import only; no library load)
+    tmap = {"q4_0": 2, "q4_k": 12, "q6_k": 14}
+    cases = [(nm, r, c, b) for nm, r, c, bs in MATVEC_CASES[a.config] for b in bs
+             if a.batch is None or b == a.batch]
+    steps = max(a.steps, 1)
+    reps = max(5, min(steps, 20))
+
+    def seed_name(nm, r, c, i):
+        return f"cfg{a.config}.{nm}.{r}x{c}.copy{i}"
+
+    def cpu_time(orc, nm, r, c, b, seconds=3.0):
+        """Median seconds per call of the oracle's MatVecMul port (all host threads)."""
+        t = tmap[nm]
+        W = orc.synth_fill(t, r, c, orc.synth_seed(a.config, seed_name(nm, r, c, 0)))
+        x = orc.synth_fill(0, b, c, orc.synth_seed(a.config, f"cfg{a.config}.x.{c}.{b}"))
+        times, t_end = [], time.perf_counter() + seconds
+        while len(times) < 3 or (time.perf_counter() < t_end and len(times) < 50):
+            t0 = time.perf_counter()
+            orc.matvec(t, W, x, r)
+            times.append(time.perf_counter() - t0)
+        return statistics.median(times), len(times)
+
+    workload0 = {"config_id": a.config, "parallelism": "single GPU" if world == 1 else f"replicas x{world}",
+                 "l2": "cold: calls cycle through distinct copies of the matrix filling 2x the 126 MB L2"}
+    if a.impl == "reference":
+        if rank != 0:
+            return 0
+        from tests import _oracle
+        orc = _oracle.load()
+        for nm, r, c, b in cases:
+            rb = int(orc.lib.or_byte_size(tmap[nm], c))
+            nbytes = matvec_bytes(rb, r, c, b)
+            sec, n = cpu_time(orc, nm, r, c, b, seconds=max(2.0, 0.1 * (steps + a.warmup)))
+            val = nbytes / sec / 1e9
+            wl = dict(workload0, workload=f"{nm} {r}x{c} batch {b}", rows=r, cols=c, batch=b)
+            print(json.dumps({
+                "metric": "Q-matvec GB/s", "value": val, "unit": "GB/s", "n_gpus": 0, "steps": n,
+                "warmup": a.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference", "config": wl,
+                "cpu_baseline": {"value": val, "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+                                 "sample": f"{n} calls of the oracle's MatVecMul port, median"},
+                "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+                flush=True)
+        return 0
+
+    import ctypes as C
+    import torch
+    import chatnet_b200 as cn
+    from chatnet_b200 import _native as N
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    ctx = cn.Context(local)
+    ext = torch.cuda.ExternalStream(ctx.stream)
+    peak, peak_kind = measured_peak_gbs()
+    orc = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        from tests import _oracle
+        orc = _oracle.load()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for nm, r, c, b in cases:
+        t = tmap[nm]
+        rb = cn.byte_size(t, c)
+        nbytes = matvec_bytes(rb, r, c, b)
+        copies = max(2, -(-2 * L2_BYTES // (rb * r)))
+        Ws = [ctx.synth(t, r, c, cn.synth_seed(a.config, seed_name(nm, r, c, i))) for i in range(copies)]
+        x = torch.from_numpy(cn.synth_fill(cn.TYPE_F32, b, c, cn.synth_seed(a.config, f"cfg{a.config}.x.{c}.{b}")))
+        xd = x.to(f"cuda:{local}")
+        yd = torch.empty(b, r, device=f"cuda:{local}")
+        torch.cuda.synchronize()
+        launches = -(-max(100, copies) // copies) * copies
+        handles = (C.c_void_p * copies)(*[w.handle for w in Ws])
+        us = np.zeros(reps, np.float32)
+        kpl = C.c_int(0)
+        for _ in range(max(1, a.warmup // 5)):  # warm-up replays (the call itself warms up twice)
+            N.check(N.lib().cn_time_matvec(ctx.handle, handles, copies, xd.data_ptr(), yd.data_ptr(), b,
+                                           launches, 1, us.ctypes.data_as(C.POINTER(C.c_float)),
+                                           C.byref(kpl)), "cn_time_matvec")
+        if dist is not None:
+            dist.barrier()
+        clk = ClockSampler(local)
+        clk.start()
+        time.sleep(0.2)
+        N.check(N.lib().cn_time_matvec(ctx.handle, handles, copies, xd.data_ptr(), yd.data_ptr(), b, launches,
+                                       reps, us.ctypes.data_as(C.POINTER(C.c_float)), C.byref(kpl)),
+                "cn_time_matvec")
+        clocks = clk.stop()
+        us_med = max_over_ranks(float(np.median(us)))
+        value = world * nbytes / (us_med * 1e-6) / 1e9
+        # end to end: cn_matvec with pinned host buffers (x in, y out, synchronous)
+        xh = x.pin_memory()
+        yh = torch.empty(b, r).pin_memory()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_e2e = max(steps, copies)
+        xp = C.cast(xh.data_ptr(), C.POINTER(C.c_float))
+        yp = C.cast(yh.data_ptr(), C.POINTER(C.c_float))
+        for i in range(3):
+            N.check(N.lib().cn_matvec(ctx.handle, Ws[i % copies].handle, xp, yp, b), "cn_matvec")
+        e0.record(ext)
+        for i in range(n_e2e):
+            N.check(N.lib().cn_matvec(ctx.handle, Ws[i % copies].handle, xp, yp, b), "cn_matvec")
+        e1.record(ext)
+        e1.synchronize()
+        us_e2e = max_over_ranks(e0.elapsed_time(e1) * 1e3 / n_e2e)
+        assert torch.isfinite(yh).all()
+        cpu = None
+        if orc is not None:
+            sec, n = cpu_time(orc, nm, r, c, b)
+            cpu = {"value": nbytes / sec / 1e9, "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+                   "sample": f"{n} calls of the oracle's MatVecMul port on copy 0 of the matrix, median "
+                             f"({sec * 1e3:.2f} ms per call)"}
+        if rank == 0:
+            wl = dict(workload0, workload=f"{nm} {r}x{c} batch {b}", rows=r, cols=c, batch=b,
+                      weight_copies=copies, calls_per_graph=launches, replays=reps)
+            achieved = nbytes / (us_med * 1e-6) / 1e9
+            print(json.dumps({
+                "metric": "Q-matvec GB/s", "value": value, "unit": "GB/s", "n_gpus": world, "steps": reps,
+                "warmup": a.warmup, "ms_per_step": us_med * 1e-3, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": matvec_dtype(nm, b),
+                "data": "synthetic (seeded generator, config shapes and distributions)", "config": wl,
+                "e2e": {"value": nbytes / (us_e2e * 1e-6) / 1e9, "unit": "GB/s", "us_per_call": us_e2e,
+                        "h2d_bytes_per_step": 4 * b * c, "d2h_bytes_per_step": 4 * b * r},
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": achieved / peak, "traffic": committed_traffic(f"gemv_{nm}_{r}x{c}_b{b}"),
+                             "kernel": f"x-prep + fused dequant-GEMV {nm} {r}x{c} batch {b}",
+                             "us_per_launch": us_med, "bytes_per_launch": nbytes,
+                             "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
+                "cpu_baseline": cpu, "gpu_launches": int(kpl.value) * launches * reps, "clocks": clocks}),
+                flush=True)
+        del xd, yd
+        for w in Ws:
+            w.free()
+    ctx.close()
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
 
 
 def gemv_mode(a) -> int:
@@ -278,13 +475,13 @@ class CpuPrefillSample:
         from tests import _oracle
         self.n = n
         orc = _oracle.load()
-        host = cf.host_tensors(dc)
+        host = _oracle.host_tensors(orc, dc)  # the oracle's generator: no product library here
         names = tensor_names(dc.model.n_layers)
         types = [cf.tensor_type(dc, nm) for nm in names]
         m = dc.model
         k = np.zeros((m.n_layers * m.ctx_len, m.kv_dim), np.float32)
         self.ol = _oracle.OracleLlama(orc, m, host, types, names, k, k.copy())
-        self.x = cf.prefill_x(dc)
+        self.x = _oracle.prefill_x(orc, dc)
 
     def run_once(self) -> float:
         """Seconds per token."""
@@ -456,6 +653,12 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.gemv:
+        return gemv_mode(a)
+    if a.config in (0, 2):
+        return matvec_main(a, world, rank, local)
+    if a.batch is None:
+        a.batch = 1
     from chatnet_b200 import configs as cf
     dc = cf.with_batch(cf.CONFIGS[a.config], a.batch)
     workload = {"workload": dc.name, "config_id": a.config, "batch": a.batch,
@@ -470,8 +673,6 @@ def main():
                 "l2": "inputs larger than L2 (weights 38.5 GB)" if a.config == 4 else
                       "inputs larger than L2 (weights 0.58 GB)"}
 
-    if a.gemv:
-        return gemv_mode(a)
     if a.config == 3:
         return prefill_main(a, world, rank, local, dc)
 

@@ -88,9 +88,11 @@ SIGNATURES: dict[str, tuple] = {
     "cn_matvec": (_i, [_vp, _vp, _fp, _fp, _i]),
     "cn_dequantize_dev": (_i, [_i, _vp, _vp, _i64, _vp]),
     "cn_matvec_dev": (_i, [_vp, _i, _vp, _i, _i, _vp, _vp, _i]),
+    "cn_time_matvec": (_i, [_vp, C.POINTER(_vp), _i, _vp, _vp, _i, _i, _i, _fp, C.POINTER(_i)]),
     "cn_matmul": (_i, [_vp, _vp, _fp, _fp, _i]),
     "cn_matmul_dev": (_i, [_vp, _i, _vp, _i, _i, _vp, _vp, _i]),
     "cn_matvec_noalloc_dev": (_i, [_i, _vp, _i, _i, _vp, _vp, _i, _vp]),
+    "cn_matvec_noalloc_status": (_i, [_vp]),
     "cn_llama_create": (_i, [_vp, _vp, C.POINTER(_vp), _i, C.POINTER(_vp)]),
     "cn_llama_destroy": (_i, [_vp]),
     "cn_llama_forward": (_i, [_vp, C.POINTER(_i), _i, _i, _fp]),

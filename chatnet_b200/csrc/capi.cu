@@ -191,6 +191,9 @@ static int tensor_alloc(cn_ctx* ctx, int type, int64_t rows, int64_t cols, cn_te
              type);
     CN_CHECK(rows > 0 && cols > 0, CN_ERR_INVALID_ARG, "bad shape [%lld, %lld]", (long long)rows,
              (long long)cols);
+    // the kernels index rows and columns with 32-bit ints
+    CN_CHECK(rows < (1ll << 31) && cols < (1ll << 31), CN_ERR_INVALID_ARG,
+             "shape [%lld, %lld]: rows and columns must be below 2^31", (long long)rows, (long long)cols);
     cn_tensor* t = new (std::nothrow) cn_tensor();
     CN_CHECK(t, CN_ERR_OOM, "host allocation failed");
     t->ctx = ctx;
@@ -215,7 +218,9 @@ int cn_tensor_upload(cn_ctx* ctx, const void* host_blocks, uint64_t bytes, int t
                      int64_t cols, cn_tensor** out) {
     CN_CHECK(ctx && host_blocks && out, CN_ERR_INVALID_ARG, "null argument");
     DeviceGuard dg(ctx->device);
-    uint64_t want = row_bytes(type, cols) * (uint64_t)(rows > 0 ? rows : 0);
+    uint64_t want = 0;
+    CN_CHECK(!__builtin_mul_overflow(row_bytes(type, cols), (uint64_t)(rows > 0 ? rows : 0), &want),
+             CN_ERR_INVALID_ARG, "tensor [%lld, %lld] is too large", (long long)rows, (long long)cols);
     CN_CHECK(!type_supported(type) || bytes == want, CN_ERR_INVALID_ARG,
              "tensor bytes %llu != rows * ByteSize(cols) = %llu", (unsigned long long)bytes,
              (unsigned long long)want);
@@ -464,6 +469,15 @@ int cn_matvec_dev(cn_ctx* ctx, int type, const void* d_w, int out_dim, int in_di
     CN_CHECK(ctx && d_w && d_x && d_y, CN_ERR_INVALID_ARG, "null argument");
     DeviceGuard dg(ctx->device);
     return gemv_launch(ctx, type, d_w, out_dim, in_dim, nullptr, d_x, d_y, batch);
+}
+
+int cn_time_matvec(cn_ctx* ctx, const cn_tensor* const* ws, int n_w, const float* d_x, float* d_y, int batch,
+                   int launches, int reps, float* us_out, int* kernels_per_launch) {
+    CN_CHECK(ctx && ws && d_x && d_y && us_out, CN_ERR_INVALID_ARG, "null argument");
+    DeviceGuard dg(ctx->device);
+    int rc = gemv_time(ctx, ws, n_w, d_x, d_y, batch, launches, reps, us_out, kernels_per_launch);
+    if (rc) return rc;
+    return check_dev_err(ctx);
 }
 
 }  // extern "C"

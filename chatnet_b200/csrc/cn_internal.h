@@ -299,6 +299,10 @@ int gemv_tc_run(cudaStream_t st, uint32_t* err, const CUtensorMap* map, int64_t 
 // be null (encoded on the fly when possible, else the generic kernel runs).
 int gemv_launch(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols,
                 const CUtensorMap* map, const float* d_x, float* d_y, int batch);
+// Times `launches` GEMVs (prep + GEMV each) cycling through ws[0..n_w) from
+// one CUDA graph, replayed `reps` times: us_out[r] = replay r's mean per launch.
+int gemv_time(cn_ctx* ctx, const cn_tensor* const* ws, int n_w, const float* d_x, float* d_y, int batch,
+              int launches, int reps, float* us_out, int* kernels_per_launch);
 
 // tensor-parallel exchange descriptors (tp.cu); uses = exchanges per step
 int tp_step_launch(const cn_tp* tp, cudaStream_t s);

@@ -27,6 +27,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <vector>
+
 #include "cn_common.cuh"
 #include "cn_internal.h"
 #include "formats.cuh"
@@ -887,17 +889,15 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 static EncodeTiledFn get_encode() {
-    static EncodeTiledFn fn = nullptr;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
+    // initialised once, thread-safely (function-local static)
+    static const EncodeTiledFn fn = [] {
         void* p = nullptr;
         cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-                cudaSuccess &&
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    }
+            return reinterpret_cast<EncodeTiledFn>(p);
+        return static_cast<EncodeTiledFn>(nullptr);
+    }();
     return fn;
 }
 
@@ -1245,30 +1245,93 @@ int gemv_reserve(const GemvPlan& p, GemvNeeds* n) {
     return CN_OK;
 }
 
+// Grows the context's GEMV scratch to what `op` needs.
+static int ctx_reserve(cn_ctx* ctx, const GemvOp& op) {
+    if (!op.tma) return CN_OK;
+    const GemvPlan& p = op.plan;
+    int rc = ensure(&ctx->xfrag, &ctx->xfrag_bytes, p.xfrag_bytes, false);
+    if (!rc && p.xsum_bytes) rc = ensure((void**)&ctx->xsum, &ctx->xsum_bytes, p.xsum_bytes, false);
+    if (!rc) rc = ensure((void**)&ctx->partials, &ctx->partial_bytes, p.partial_bytes, false);
+    if (!rc) rc = ensure((void**)&ctx->xinv, &ctx->xinv_bytes, p.xinv_bytes, false);
+    if (!rc) {
+        size_t cb = ctx->counter_count * sizeof(int);
+        rc = ensure((void**)&ctx->counters, &cb, p.counters * sizeof(int), true);
+        ctx->counter_count = cb / sizeof(int);
+    }
+    return rc;
+}
+
+static GemvBufs ctx_bufs(cn_ctx* ctx) {
+    return GemvBufs{(uint4*)ctx->xfrag, ctx->xsum, ctx->partials, ctx->counters, ctx->xinv};
+}
+
 int gemv_launch(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols,
                 const CUtensorMap* map, const float* d_x, float* d_y, int batch) {
     CN_CHECK((reinterpret_cast<uintptr_t>(d_x) & 15) == 0 && (reinterpret_cast<uintptr_t>(d_y) & 3) == 0,
              CN_ERR_INVALID_ARG, "x must be 16-byte aligned and y 4-byte aligned");
     GemvOp op;
     int rc = gemv_make(ctx, type, d_w, rows, cols, map, batch, &op);
-    if (rc) return rc;
-    if (op.tma) {
-        const GemvPlan& p = op.plan;
-        rc = ensure(&ctx->xfrag, &ctx->xfrag_bytes, p.xfrag_bytes, false);
-        if (!rc && p.xsum_bytes) rc = ensure((void**)&ctx->xsum, &ctx->xsum_bytes, p.xsum_bytes, false);
-        if (!rc) rc = ensure((void**)&ctx->partials, &ctx->partial_bytes, p.partial_bytes, false);
-        if (!rc) rc = ensure((void**)&ctx->xinv, &ctx->xinv_bytes, p.xinv_bytes, false);
-        if (!rc) {
-            size_t cb = ctx->counter_count * sizeof(int);
-            rc = ensure((void**)&ctx->counters, &cb, p.counters * sizeof(int), true);
-            ctx->counter_count = cb / sizeof(int);
-        }
-        if (rc) return rc;
-    }
-    GemvBufs b{(uint4*)ctx->xfrag, ctx->xsum, ctx->partials, ctx->counters, ctx->xinv};
+    if (rc || (rc = ctx_reserve(ctx, op))) return rc;
+    const GemvBufs b = ctx_bufs(ctx);
     rc = gemv_prep(ctx->stream, ctx->sms, op, d_x, b);
     if (rc) return rc;
     return gemv_run(ctx, ctx->stream, op, d_x, b, d_y);
+}
+
+int gemv_time(cn_ctx* ctx, const cn_tensor* const* ws, int n_w, const float* d_x, float* d_y, int batch,
+              int launches, int reps, float* us_out, int* kernels_per_launch) {
+    CN_CHECK(n_w >= 1 && launches >= 1 && reps >= 1, CN_ERR_INVALID_ARG, "bad timing request");
+    CN_CHECK((reinterpret_cast<uintptr_t>(d_x) & 15) == 0 && (reinterpret_cast<uintptr_t>(d_y) & 3) == 0,
+             CN_ERR_INVALID_ARG, "x must be 16-byte aligned and y 4-byte aligned");
+    std::vector<GemvOp> ops(n_w);
+    for (int i = 0; i < n_w; i++) {
+        const cn_tensor* w = ws[i];
+        CN_CHECK(w && w->ctx == ctx && w->rows == ws[0]->rows && w->cols == ws[0]->cols && w->type == ws[0]->type,
+                 CN_ERR_INVALID_ARG, "timed matrices must share one shape and type on this context");
+        int rc = gemv_make(ctx, w->type, w->d, w->rows, w->cols, w->has_map ? &w->map : nullptr, batch, &ops[i]);
+        if (rc || (rc = ctx_reserve(ctx, ops[i]))) return rc;
+    }
+    const GemvBufs b = ctx_bufs(ctx);
+    cudaStream_t s = ctx->stream;
+    // one graph holds `launches` ops (prep + GEMV each) cycling through the
+    // matrices, so no host launch gap lands inside the timed replays
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    CN_CUDA(cudaStreamSynchronize(s));
+    CN_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    int rc = CN_OK;
+    for (int i = 0; i < launches && !rc; i++) {
+        rc = gemv_prep(s, ctx->sms, ops[i % n_w], d_x, b);
+        if (!rc) rc = gemv_run(ctx, s, ops[i % n_w], d_x, b, d_y);
+    }
+    cudaError_t e = cudaStreamEndCapture(s, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return cuda_error(e, "cudaStreamEndCapture");
+    e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return cuda_error(e, "cudaGraphInstantiate");
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    e = cudaEventCreate(&e0);
+    if (e == cudaSuccess) e = cudaEventCreate(&e1);
+    for (int r = 0; r < 2 && e == cudaSuccess; r++) e = cudaGraphLaunch(ge, s);  // warm-up
+    for (int r = 0; r < reps && e == cudaSuccess; r++) {
+        e = cudaEventRecord(e0, s);
+        if (e == cudaSuccess) e = cudaGraphLaunch(ge, s);
+        if (e == cudaSuccess) e = cudaEventRecord(e1, s);
+        if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+        float ms = 0.f;
+        if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+        us_out[r] = ms * 1000.f / launches;
+    }
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    cudaGraphExecDestroy(ge);
+    if (e != cudaSuccess) return cuda_error(e, "timed GEMV replays");
+    if (kernels_per_launch) *kernels_per_launch = ops[0].tma ? 2 : 1;
+    return CN_OK;
 }
 
 }  // namespace cn

@@ -27,6 +27,8 @@
 // Every mbarrier wait is bounded (error word, then uniform fall-through).
 #include <stdlib.h>
 
+#include <mutex>
+
 #include "cn_common.cuh"
 #include "cn_internal.h"
 #include "gemv_i8.cuh"
@@ -546,9 +548,11 @@ size_t gemv_i8_partial_bytes(int ctas) { return (size_t)2 * ctas * i8::kRows * 8
 static int g_sms[64] = {0};
 
 int gemv_i8_prepare() {
+    static std::mutex mu;  // callers may be several host threads (the no-alloc entry point has no context)
     static bool done[64] = {false};
     int dev = 0;
     CN_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(mu);
     if (done[dev & 63]) return CN_OK;
 #define CN_ATTR(NB)                                                                                   \
     CN_CUDA(cudaFuncSetAttribute(gemv_i8_q4k_kernel<NB, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \

@@ -34,6 +34,8 @@
 // word and runs on without waiting (control flow stays uniform, the results
 // are garbage and flagged); the CTA still waits for its own copies and MMAs
 // and frees its tensor memory.
+#include <mutex>
+
 #include "cn_common.cuh"
 #include "cn_internal.h"
 #include "gemv_tc.cuh"
@@ -524,9 +526,11 @@ size_t gemv_tc_partial_bytes(int ctas) { return (size_t)2 * ctas * tc::kRows * 8
 // Sets the kernels' shared-memory limit on the current device (once per
 // device; call outside any stream capture).
 int gemv_tc_prepare() {
+    static std::mutex mu;  // callers may be several host threads (the no-alloc entry point has no context)
     static bool done[64] = {false};
     int dev = 0;
     CN_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(mu);
     if (done[dev & 63]) return CN_OK;
     CN_CUDA(cudaFuncSetAttribute(gemv_tc_q4k_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmem));
     CN_CUDA(cudaFuncSetAttribute(gemv_tc_q4k_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmem));

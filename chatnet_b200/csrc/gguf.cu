@@ -165,14 +165,19 @@ static bool is_int(const Value* v) {
                  v->type == kI32 || v->type == kU64 || v->type == kI64 || v->type == kBool);
 }
 
-// GgufMetadata.GetInt32 semantics: the value when the key holds an integer, else the default.
+// GgufMetadata.GetInt32 semantics (Gguf/GgufMetadata.cs:53-63): only int32,
+// uint32, int64 and uint64 values count (other integer widths give the
+// default), and the value is cast to a 32-bit int the way C#'s unchecked
+// (int) cast does -- the low 32 bits, so a uint32 0xFFFFFFFF reads as -1.
 static int64_t meta_int(const cn_gguf* g, const std::string& key, int64_t def) {
     const Value* v = meta_get(g, key);
-    return is_int(v) ? v->i : def;
+    if (!v || !(v->type == kU32 || v->type == kI32 || v->type == kU64 || v->type == kI64)) return def;
+    return (int64_t)(int32_t)(uint32_t)(uint64_t)v->i;
 }
 
-// The float lookups of ExtractModelConfig.GetArchFloat: float, double, then
-// integer values under the architecture's key, then under the bare key.
+// One key's part of ExtractModelConfig.GetArchFloat (Gguf/GgufReader.cs:93-108):
+// a float, a double, a uint32 or an int32 value, in that order of type tests;
+// any other type (other integer widths, bool) does not count.
 static bool meta_float(const cn_gguf* g, const std::string& key, double* out) {
     const Value* v = meta_get(g, key);
     if (!v) return false;
@@ -180,8 +185,12 @@ static bool meta_float(const cn_gguf* g, const std::string& key, double* out) {
         *out = v->f;
         return true;
     }
-    if (is_int(v) && v->type != kBool) {
-        *out = (double)v->i;
+    if (v->type == kU32) {
+        *out = (double)(uint32_t)(uint64_t)v->i;
+        return true;
+    }
+    if (v->type == kI32) {
+        *out = (double)(int32_t)v->i;
         return true;
     }
     return false;
@@ -252,9 +261,17 @@ int cn_gguf_open(const char* path, cn_gguf** out) {
         }
         t.n_dims = (int)nd;
         uint64_t elems = nd ? 1 : 0;
+        bool overflow = false;
         for (uint32_t d = 0; d < nd; d++) {
             t.dims[d] = c.get<uint64_t>();
-            elems *= t.dims[d];
+            overflow |= __builtin_mul_overflow(elems, t.dims[d], &elems);
+        }
+        // no real tensor comes near 2^56 elements; past that the byte size
+        // (up to 4 bytes per element) could wrap around
+        if (overflow || elems >= (1ull << 56)) {
+            const std::string name = t.name;
+            gguf_free(g);
+            return set_error(CN_ERR_INVALID_ARG, "%s: tensor '%s' has too many elements", path, name.c_str());
         }
         t.type = (int)c.get<uint32_t>();
         t.offset = c.get<uint64_t>();
@@ -270,7 +287,9 @@ int cn_gguf_open(const char* path, cn_gguf** out) {
     g->data_off = (c.pos + mask) & ~mask;
     for (const Tensor& t : g->tensors) {
         if (t.bytes == 0 && t.n_dims > 0 && t.type != CN_TYPE_F32) continue;  // a type without a byte size
-        if (g->data_off + t.offset > g->size || t.bytes > g->size - g->data_off - t.offset) {
+        uint64_t start = 0;
+        if (__builtin_add_overflow(g->data_off, t.offset, &start) || start > g->size ||
+            t.bytes > g->size - start) {
             const std::string name = t.name;
             gguf_free(g);
             return set_error(CN_ERR_INVALID_ARG, "%s: tensor '%s' runs past the end of the file", path,

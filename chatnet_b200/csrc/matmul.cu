@@ -43,6 +43,8 @@
 // word and stops waiting (its control flow stays uniform; results are
 // garbage and flagged).  The CTA still waits for its own copies and MMAs
 // before it frees its tensor memory.
+#include <mutex>
+
 #include "cn_common.cuh"
 #include "cn_internal.h"
 
@@ -644,16 +646,25 @@ int matmul_quant(cudaStream_t st, uint32_t* err, int type, int nmat, const void*
     CN_CHECK(matmul_type_ok(type), CN_ERR_UNSUPPORTED, "matmul: weight type %d (Q4_0, Q4_K or Q6_K)", type);
     CN_CHECK(nmat >= 1 && nmat <= mm::kMaxMats && K > 0 && K % 256 == 0 && M >= 1, CN_ERR_INVALID_ARG,
              "matmul: bad shape (nmat %d, K %lld, M %d)", nmat, (long long)K, M);
-    static bool attr = false;
-    if (!attr) {
-        CN_CUDA(cudaFuncSetAttribute(matmul_q_kernel<CN_TYPE_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     mm::kSmem));
-        CN_CUDA(cudaFuncSetAttribute(matmul_q_kernel<CN_TYPE_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     mm::kSmem));
-        CN_CUDA(cudaFuncSetAttribute(matmul_q_kernel<CN_TYPE_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     mm::kSmem));
-        attr = true;
+    int dev = 0;
+    CN_CUDA(cudaGetDevice(&dev));
+    static std::mutex mu;
+    static bool attr[64] = {false};
+    static int sm_count[64] = {0};
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!attr[dev & 63]) {
+            CN_CUDA(cudaFuncSetAttribute(matmul_q_kernel<CN_TYPE_Q4_0>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, mm::kSmem));
+            CN_CUDA(cudaFuncSetAttribute(matmul_q_kernel<CN_TYPE_Q4_K>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, mm::kSmem));
+            CN_CUDA(cudaFuncSetAttribute(matmul_q_kernel<CN_TYPE_Q6_K>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, mm::kSmem));
+            CN_CUDA(cudaDeviceGetAttribute(&sm_count[dev & 63], cudaDevAttrMultiProcessorCount, dev));
+            attr[dev & 63] = true;
+        }
     }
+    const int sms = sm_count[dev & 63];
     mm::Args a = {};
     mm::Maps maps;
     a.nmat = nmat;
@@ -688,12 +699,6 @@ int matmul_quant(cudaStream_t st, uint32_t* err, int type, int nmat, const void*
     a.err = err;
     int rc = encode_act_map(x, M, K, &maps.x);
     if (rc) return rc;
-    static int sms = 0;
-    if (sms <= 0) {
-        int dev = 0;
-        CN_CUDA(cudaGetDevice(&dev));
-        CN_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    }
     const dim3 grid(a.tiles < sms ? a.tiles : sms);  // persistent: one CTA per SM
     if (type == CN_TYPE_Q4_0)
         CN_CUDA(launch_k(false, matmul_q_kernel<CN_TYPE_Q4_0>, grid, dim3(mm::kThreads), (size_t)mm::kSmem, st, maps, a));

@@ -24,10 +24,15 @@
 //    parts that must start at zero (tile counters, error word) on its stream.
 //  * The first call on each device looks up the array's device address
 //    (cudaGetSymbolAddress) with that device current; make that first call
-//    outside any stream capture.
+//    outside any stream capture.  The address is remembered per device
+//    together with the unique id of the CUDA context it was looked up in, so
+//    a host that resets the device (cudaDeviceReset) and keeps using the
+//    library gets a fresh lookup on its next call (again outside a capture).
 //  * The call only enqueues work and does not wait for it, so a kernel that
-//    gives up waiting (bounded mbarrier polls) is not reported here: its
-//    bit stays in the array's first word until the next call clears it.
+//    gives up waiting (bounded mbarrier polls) cannot be reported by the call
+//    itself: its bit stays in the array's first word.  cn_matvec_noalloc_status
+//    waits for the stream, reads and clears that word, and returns
+//    CN_ERR_TIMEOUT if it was set -- again without allocating.
 #include <mutex>
 
 #include "cn_common.cuh"
@@ -44,18 +49,56 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes]
 namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-void* g_addr[kMaxDevices] = {};
+struct Slot {
+    unsigned long long ctx_id = 0;  // the CUDA context the address belongs to (0: none yet)
+    void* addr = nullptr;
+};
+Slot g_slot[kMaxDevices];
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+// Unique id of the calling thread's current CUDA context (the device's
+// primary context, which the runtime made current); ids are never reused
+// within a process, so a reset device shows up as a new id.
+int current_ctx_id(unsigned long long* id) {
+    static CtxGetCurrentFn get_cur = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    if (!get_cur || !get_id) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_cur = reinterpret_cast<CtxGetCurrentFn>(p);
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<CtxGetIdFn>(p);
+        CN_CHECK(get_cur && get_id, CN_ERR_CUDA, "driver entry points cuCtxGetCurrent/cuCtxGetId not found");
+    }
+    CUcontext c = nullptr;
+    CN_CHECK(get_cur(&c) == CUDA_SUCCESS && c, CN_ERR_CUDA, "no current CUDA context");
+    CN_CHECK(get_id(c, id) == CUDA_SUCCESS, CN_ERR_CUDA, "cuCtxGetId failed");
+    return CN_OK;
+}
 
 int scratch_address(int device, uint8_t** out) {
     CN_CHECK(device >= 0 && device < kMaxDevices, CN_ERR_INVALID_ARG, "device %d out of range", device);
     std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_addr[device]) {
+    // before the runtime's first use of the device no context is current yet;
+    // the lookup below creates it
+    unsigned long long id = 0;
+    const bool have_id = current_ctx_id(&id) == CN_OK;
+    Slot& s = g_slot[device];
+    if (!have_id || !s.addr || s.ctx_id != id) {
         void* p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess) return cuda_error(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
-        g_addr[device] = p;
+        int rc = current_ctx_id(&id);
+        if (rc) return rc;
+        s.addr = p;
+        s.ctx_id = id;
     }
-    *out = static_cast<uint8_t*>(g_addr[device]);
+    *out = static_cast<uint8_t*>(s.addr);
     return CN_OK;
 }
 
@@ -119,4 +162,22 @@ extern "C" int cn_matvec_noalloc_dev(int type, const void* d_w, int out_dim, int
     rc = gemv_prep(c.stream, c.sms, op, d_x, b);
     if (rc) return rc;
     return gemv_run(&c, c.stream, op, d_x, b, d_y);
+}
+
+extern "C" int cn_matvec_noalloc_status(void* stream) {
+    int device = 0;
+    CN_CUDA(cudaGetDevice(&device));
+    uint8_t* base = nullptr;
+    int rc = scratch_address(device, &base);
+    if (rc) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    uint32_t word = 0;
+    CN_CUDA(cudaMemcpyAsync(&word, base, sizeof(word), cudaMemcpyDeviceToHost, s));
+    CN_CUDA(cudaStreamSynchronize(s));
+    if (word == 0) return CN_OK;
+    CN_CUDA(cudaMemsetAsync(base, 0, sizeof(word), s));
+    CN_CUDA(cudaStreamSynchronize(s));
+    if (word & kErrTimeout)
+        return set_error(CN_ERR_TIMEOUT, "a no-alloc GEMV gave up waiting (device error word 0x%x)", word);
+    return set_error(CN_ERR_INVALID_ARG, "a no-alloc GEMV rejected its arguments (device error word 0x%x)", word);
 }

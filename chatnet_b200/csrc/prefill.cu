@@ -21,6 +21,8 @@
 // these kernels compute the same per-token results in one pass.
 #include <float.h>
 
+#include <mutex>
+
 #include "cn_common.cuh"
 #include "cn_internal.h"
 
@@ -434,23 +436,25 @@ int prefill_attention(cudaStream_t st, const float* q, int q_stride, const void*
     const float scale_log2 = 1.4426950408889634f / sqrtf((float)hd);
     const dim3 grid((M + kPfQ - 1) / kPfQ, n_heads);
     const int kvdim = n_kv * hd;
-    if (hd == 128) {
-        static bool attr = false;
-        if (!attr) {
-            CN_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<128>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            attr = true;
+    {
+        int dev = 0;
+        CN_CUDA(cudaGetDevice(&dev));
+        static std::mutex mu;
+        static bool attr[64] = {false};
+        std::lock_guard<std::mutex> lock(mu);
+        if (!attr[dev & 63]) {
+            // the larger (head_dim 128) request covers both instantiations
+            const int big = (kPfQ + 4 * kPfK) * (128 + 8) * (int)sizeof(__half);
+            CN_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+            CN_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+            attr[dev & 63] = true;
         }
+    }
+    if (hd == 128) {
         CN_CUDA(launch_k(false, attn_prefill_kernel<128>, grid, dim3(kPfThreads), smem, st, q, q_stride,
                          kcache, vcache, kv_f16 ? 1 : 0, cache_off, kvdim, n_heads, n_kv, M, pos0,
                          scale_log2, kh, vh, out, out_stride));
     } else {
-        static bool attr64 = false;
-        if (!attr64) {
-            CN_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<64>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            attr64 = true;
-        }
         CN_CUDA(launch_k(false, attn_prefill_kernel<64>, grid, dim3(kPfThreads), smem, st, q, q_stride,
                          kcache, vcache, kv_f16 ? 1 : 0, cache_off, kvdim, n_heads, n_kv, M, pos0,
                          scale_log2, kh, vh, out, out_stride));

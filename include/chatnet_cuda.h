@@ -179,6 +179,15 @@ int cn_dequantize_dev(int type, const void* d_blocks, float* d_out, int64_t n_el
 int cn_matvec_dev(cn_ctx* ctx, int type, const void* d_w, int out_dim, int in_dim,
                   const float* d_x, float* d_y, int batch);
 
+/* Measurement hook for the op-level GEMV (bench.py's GB/s lines): captures
+ * `launches` calls of cn_matvec_dev's work (x-prep + fused GEMV) cycling
+ * through the n_w same-shaped matrices ws (distinct copies keep L2 cold),
+ * replays the graph `reps` times on ctx's stream and writes each replay's
+ * mean microseconds per call to us_out[reps].  *kernels_per_launch = kernels
+ * one call launches.  (no counterpart in the reference: timing only) */
+int cn_time_matvec(cn_ctx* ctx, const cn_tensor* const* ws, int n_w, const float* d_x, float* d_y,
+                   int batch, int launches, int reps, float* us_out, int* kernels_per_launch);
+
 /* cn_llama_sample on caller-owned device logits [batch][vocab] (ctx's stream;
  * returns when tokens_host is written). */
 int cn_sample_dev(cn_ctx* ctx, const float* d_logits, int vocab, int batch, float temperature, int top_k,
@@ -195,13 +204,20 @@ int cn_matmul_dev(cn_ctx* ctx, int type, const void* d_w, int out_dim, int in_di
  * array inside the library, present on every GPU that loads it; calls needing
  * more are rejected with CN_ERR_INVALID_ARG (batch 1..4 fits inner dimensions
  * beyond 100k).  Calls share that array, so calls whose GPU work overlaps
- * race: serialise them.  The first call on each device looks up the array's
- * address and must not happen during a stream capture.  `stream` is a
- * cudaStream_t (NULL = legacy default stream); the call only enqueues work.
+ * race: serialise them.  The first call on each device (and the first after
+ * a cudaDeviceReset) looks up the array's address and must not happen during
+ * a stream capture.  `stream` is a cudaStream_t (NULL = legacy default
+ * stream); the call only enqueues work.
  * (no counterpart in the reference: an allocation-free variant of
  * cn_matvec_dev) */
 int cn_matvec_noalloc_dev(int type, const void* d_w, int out_dim, int in_dim, const float* d_x,
                           float* d_y, int batch, void* stream);
+/* Waits for `stream`, then reads and clears the no-alloc array's device error
+ * word: CN_ERR_TIMEOUT if a cn_matvec_noalloc_dev kernel since the last
+ * check gave up waiting (its y is then incomplete), CN_OK otherwise.
+ * Allocates nothing.  (no counterpart in the reference: the error report of
+ * the allocation-free GEMV) */
+int cn_matvec_noalloc_status(void* stream);
 
 /* ---- model level: one Llama decoder resident on the device ------------- */
 

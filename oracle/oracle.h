@@ -118,6 +118,15 @@ int or_llama_head(const or_llama_config* cfg, const void* const* tensors,
                   const int* types, const float* x, float* logits,
                   int nthreads);
 
+/* Seeded synthetic inputs of the benchmark configs (synth.cpp): the same
+ * bytes as the product's generator (cn_synth_seed / cn_synth_fill), so CPU
+ * legs never load the product library.  norm_weight selects 1 + 0.01*N for
+ * F32.  Returns 0, -1 for a bad shape or size, -2 for a type without a
+ * generator (only Q4_0, Q4_K, Q6_K, F32 and F16 have one). */
+uint64_t or_synth_seed(int config_id, const char* name);
+int or_synth_fill(int type, int64_t rows, int64_t cols, uint64_t seed,
+                  int norm_weight, void* out, uint64_t bytes);
+
 #ifdef __cplusplus
 }
 #endif

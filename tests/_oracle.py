@@ -46,6 +46,8 @@ _SIG = {
     "or_llama_layers": (_i, [C.POINTER(LlamaConfig), C.POINTER(_vp), C.POINTER(_i), _vp, _vp,
                              _fp, _i, _i, _i, _i]),
     "or_llama_head": (_i, [C.POINTER(LlamaConfig), C.POINTER(_vp), C.POINTER(_i), _fp, _fp, _i]),
+    "or_synth_seed": (C.c_uint64, [_i, C.c_char_p]),
+    "or_synth_fill": (_i, [_i, C.c_int64, C.c_int64, C.c_uint64, _i, _vp, C.c_uint64]),
 }
 
 
@@ -75,6 +77,22 @@ class Oracle:
         tok = self.lib.or_sample_temperature(fp(lg), lg.size, temperature, top_k, top_p, r, fp(m))
         return int(tok), float(m[0])
 
+    # ---- the configs' seeded synthetic inputs, without the product library ----
+    def synth_seed(self, config_id: int, name: str) -> int:
+        return int(self.lib.or_synth_seed(config_id, name.encode()))
+
+    def synth_fill(self, type_: int, rows: int, cols: int, seed: int, norm_weight: bool = False) -> np.ndarray:
+        """Same bytes as chatnet_b200.synth_fill (checked by test_oracle_synth)."""
+        nbytes = int(self.lib.or_byte_size(type_, cols)) * rows
+        out = np.empty(nbytes, dtype=np.uint8)
+        rc = self.lib.or_synth_fill(type_, rows, cols, seed, 1 if norm_weight else 0, out.ctypes.data, nbytes)
+        assert rc == 0, rc
+        if type_ == 0:
+            return out.view(np.float32).reshape(rows, cols)
+        if type_ == 1:
+            return out.view(np.float16).reshape(rows, cols)
+        return out.reshape(rows, -1)
+
     def matvec(self, type_: int, W: np.ndarray, x: np.ndarray, rows: int, nthreads: int = 0):
         x = np.ascontiguousarray(x, dtype=np.float32)
         x2 = x.reshape(-1, x.shape[-1])
@@ -87,7 +105,7 @@ class Oracle:
 
 def build() -> Path:
     if not LIB.exists() or LIB.stat().st_mtime < max(
-            p.stat().st_mtime for p in ORACLE_DIR.glob("oracle.*")):
+            p.stat().st_mtime for p in (*ORACLE_DIR.glob("*.cpp"), *ORACLE_DIR.glob("*.h"))):
         subprocess.run(["make", "-s", "-C", str(ORACLE_DIR)], check=True)
     return LIB
 
@@ -138,3 +156,38 @@ class OracleLlama:
                                         self.v.ctypes.data, fp(h), pos, 0, self.cfg.n_layers, nthreads)
         assert rc == 0, rc
         return h
+
+
+# ---- the configs' tensors from the oracle-side generator (bench CPU legs) ----
+def host_tensors(orc: Oracle, dc, names=None) -> dict[str, np.ndarray]:
+    """chatnet_b200.configs.host_tensors through the oracle's generator."""
+    from chatnet_b200 import configs as cf
+    from chatnet_b200.llama import tensor_names, tensor_shape
+    out = {}
+    for name in names or tensor_names(dc.model.n_layers):
+        rows, cols = tensor_shape(dc.model, name)
+        out[name] = orc.synth_fill(cf.tensor_type(dc, name), rows, cols, orc.synth_seed(dc.config_id, name),
+                                   name.endswith("norm.weight"))
+    return out
+
+
+def token(orc: Oracle, dc, seq: int, step: int = 0) -> int:
+    return orc.synth_seed(dc.config_id, f"token.{seq}.{step}") % dc.model.vocab
+
+
+def host_kv(orc: Oracle, dc, seq: int) -> tuple[np.ndarray, np.ndarray]:
+    """chatnet_b200.configs.host_kv through the oracle's generator."""
+    m = dc.model
+    out = []
+    for which in ("k", "v"):
+        a = orc.synth_fill(1 if m.kv_f16 else 0, m.n_layers * m.ctx_len, m.kv_dim,
+                           orc.synth_seed(dc.config_id, f"kv.{which}.{seq}"))
+        a = a.reshape(m.n_layers, m.ctx_len, m.kv_dim).copy()
+        a[:, dc.kv_filled:, :] = 0
+        out.append(a.reshape(m.n_layers * m.ctx_len, m.kv_dim))
+    return out[0], out[1]
+
+
+def prefill_x(orc: Oracle, dc, n: int | None = None) -> np.ndarray:
+    n = dc.prefill if n is None else n
+    return orc.synth_fill(0, n, dc.model.dim, orc.synth_seed(dc.config_id, f"prefill.x.{n}"))

@@ -97,6 +97,39 @@ def test_llama_config_keys_defaults_fallbacks(tmp_path):
             g.llama_config()
 
 
+def test_llama_config_key_types(tmp_path):
+    """GetInt32 counts only 32/64-bit integers and casts to int (a uint32 0xFFFFFFFF under the
+    architecture's key is -1, so the bare key is used); GetArchFloat counts float, double,
+    uint32 and int32 only (Gguf/GgufMetadata.cs:53-63, Gguf/GgufReader.cs:84-108)."""
+    md = [("general.architecture", gw.STR, "llama"),
+          ("llama.embedding_length", gw.U8, 64),            # u8: not an int to GetInt32 -> bare/default
+          ("llama.block_count", gw.U32, 0xFFFFFFFF),       # reads as -1 -> bare key
+          ("block_count", gw.U32, 5),
+          ("llama.context_length", gw.U64, (1 << 32) + 300),  # (int) of a ulong: the low 32 bits
+          ("llama.feed_forward_length", gw.I16, 999),      # i16: ignored -> default 5632
+          ("llama.rope.freq_base", gw.I64, 77),            # long: not a GetArchFloat type -> bare key
+          ("rope.freq_base", gw.I32, 5000),
+          ("llama.attention.layer_norm_rms_epsilon", gw.U16, 3)]  # ignored -> default
+    p = tmp_path / "k.gguf"
+    gw.write_gguf(p, md, [])
+    with GgufFile(p) as g:
+        c = g.llama_config()
+    assert c.dim == 2048 and c.n_layers == 5 and c.ctx_len == 300 and c.hidden_dim == 5632
+    assert c.rope_base == 5000.0 and abs(c.rms_eps - 1e-5) < 1e-12
+
+
+def test_reader_rejects_overflowing_shapes(tmp_path):
+    # 256 x 2^60 Q4_K elements: the element count and byte size would wrap around
+    p = tmp_path / "o.gguf"
+    gw.write_gguf(p, [], [("big", cn.TYPE_Q4_K, (256, 1 << 60), b"")])
+    with pytest.raises(ValueError, match="too many elements"):
+        GgufFile(p)
+    p2 = tmp_path / "o2.gguf"
+    gw.write_gguf(p2, [], [("wrap", cn.TYPE_F32, (1 << 33, 1 << 33), b"")])
+    with pytest.raises(ValueError):
+        GgufFile(p2)
+
+
 def test_reader_errors(tmp_path):
     good = tmp_path / "g.gguf"
     gw.write_gguf(good, [("general.architecture", gw.STR, "llama")],

@@ -35,18 +35,26 @@ def _noalloc(t, W, rows, cols, x, batch):
     stream = torch.cuda.current_stream().cuda_stream
     N.check(N.lib().cn_matvec_noalloc_dev(t, W.device_ptr, rows, cols, x.data_ptr(), y.data_ptr(),
                                           batch, stream), "cn_matvec_noalloc_dev")
+    # no kernel of the call gave up waiting (the status call reads and clears the error word)
+    N.check(N.lib().cn_matvec_noalloc_status(stream), "cn_matvec_noalloc_status")
     torch.cuda.synchronize()
     return y.cpu().numpy()
 
 
+# the last three take the untiled (warp-per-row) path: inner dimension not a
+# multiple of 256, or a codec without a tiled kernel
 CASES = [(cn.TYPE_Q4_K, 11008, 4096, 1), (cn.TYPE_Q4_0, 5632, 2048, 3),
-         (cn.TYPE_Q6_K, 4096, 4096, 4), (cn.TYPE_Q4_K, 37, 512, 2)]
+         (cn.TYPE_Q6_K, 4096, 4096, 4), (cn.TYPE_Q4_K, 37, 512, 2),
+         (cn.TYPE_Q4_0, 300, 2080, 2), (cn.TYPE_Q8_0, 257, 1024, 1), (cn.TYPE_Q5_K, 129, 768, 3)]
 
 
 def test_noalloc_matches_matvec_dev(ctx):
     import torch
     for i, (t, rows, cols, batch) in enumerate(CASES):
-        W = ctx.synth(t, rows, cols, cn.synth_seed(7, f"noalloc.w.{i}"))
+        if t in (cn.TYPE_Q4_0, cn.TYPE_Q4_K, cn.TYPE_Q6_K):
+            W = ctx.synth(t, rows, cols, cn.synth_seed(7, f"noalloc.w.{i}"))
+        else:  # no seeded generator for this codec: random block bytes with a small fp16 scale
+            W = ctx.upload(_random_blocks(t, rows, cols, i), t, rows, cols)
         x = torch.from_numpy(
             cn.synth_fill(cn.TYPE_F32, batch, cols, cn.synth_seed(7, f"noalloc.x.{i}"))).cuda()
         ref = _matvec_dev(ctx, t, W, rows, cols, x, batch)
@@ -57,6 +65,20 @@ def test_noalloc_matches_matvec_dev(ctx):
         assert rel_err(y1, ref) <= REL_TOL, (i, rel_err(y1, ref))
         assert rel_err(y2, ref) <= REL_TOL, (i, rel_err(y2, ref))
         W.free()
+
+
+def _random_blocks(t, rows, cols, seed):
+    """Random bytes of `rows` rows of type t whose fp16 scale fields hold 0.01 (so values stay finite)."""
+    rng = np.random.default_rng(1000 + seed)
+    rb = cn.byte_size(t, cols)
+    raw = rng.integers(0, 256, size=(rows, rb), dtype=np.uint8)
+    blk, bpb = {cn.TYPE_Q8_0: (32, 34), cn.TYPE_Q5_K: (256, 176)}[t]
+    v = raw.reshape(rows, cols // blk, bpb)
+    half = np.frombuffer(np.float16(0.01).tobytes(), np.uint8)
+    v[:, :, 0:2] = half  # Q8_0: d; Q5_K: d
+    if t == cn.TYPE_Q5_K:
+        v[:, :, 2:4] = half  # dmin
+    return raw
 
 
 def test_noalloc_allocates_nothing(ctx):
