@@ -588,6 +588,20 @@ def prefill_main(a, world: int, rank: int, local: int, dc) -> int:
     ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
     value = world * n * 1000.0 / ms
 
+    # the same passes with every operand rounded to fp16 once (the faster, less
+    # precise setting), for comparison; then back to the default
+    model.set_prefill_precision(0)
+    for _ in range(2):
+        step()
+    barrier()
+    e0.record(ext)
+    for _ in range(a.steps):
+        step()
+    e1.record(ext)
+    e1.synchronize()
+    ms_fp16 = max_over_ranks(e0.elapsed_time(e1) / a.steps)
+    model.set_prefill_precision(1)
+
     # end to end: host activations in, host output back, every step
     barrier()
     e0.record(ext)
@@ -618,7 +632,11 @@ def prefill_main(a, world: int, rank: int, local: int, dc) -> int:
         line = {
             "metric": "prefill tok/s", "value": value, "unit": "tok/s", "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "q4_0 weights -> fp16 x fp16 activations (tcgen05 kind::f16) -> f32",
+            "vs_baseline": None,
+            "dtype": "q4_0 weights x activations on tcgen05 kind::f16 -> f32; q/k projections and scores as "
+                     "exact hi+lo fp16 pairs (3 MMAs per k-step), the rest fp16",
+            "fp16_operands": {"ms_per_step": ms_fp16, "tok_s": world * n * 1000.0 / ms_fp16,
+                              "note": "cn_llama_set_prefill_precision(0): every operand rounded to fp16 once"},
             "data": "synthetic (seeded generator, config shapes and distributions)", "config": workload,
             "layer_tflops": PREFILL_FLOPS / (ms * 1e-3) / 1e12,
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": int(xh.numel() * 4),

@@ -117,6 +117,7 @@ SIGNATURES: dict[str, tuple] = {
     "cn_llama_set_inputs": (_i, [_vp, C.POINTER(_i), C.POINTER(_i), _i]),
     "cn_llama_step": (_i, [_vp, _i]),
     "cn_llama_set_prefill": (_i, [_vp, _i]),
+    "cn_llama_set_prefill_precision": (_i, [_vp, _i]),
     "cn_llama_sample": (_i, [_vp, _i, C.c_float, _i, C.c_float, _vp, _vp]),
     "cn_sample_dev": (_i, [_vp, _vp, _i, _i, C.c_float, _i, C.c_float, _vp, _vp]),
     "cn_llama_step_kernels": (_i, [_vp, _i, C.POINTER(_i)]),

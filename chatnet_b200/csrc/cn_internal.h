@@ -67,6 +67,7 @@ struct cn_tensor {
     bool owns = true;
     bool has_map = false;
     CUtensorMap map;
+    float split_scale = 0.f;  // matmul_split_scale's cached result (0: not yet computed)
 };
 
 namespace cn {
@@ -118,7 +119,18 @@ int encode_tiled_2d(CUtensorMapDataType dt, void* base, const cuuint64_t (&dims)
 // encoded per call).
 int matmul_quant(cudaStream_t st, uint32_t* err, int type, int nmat, const void* const* w,
                  const CUtensorMap* const* wmaps, const int64_t* rows, int64_t K, const __half* x, const float* xs,
-                 int M, float* const* y, const int64_t* ldy, bool accumulate);
+                 int M, float* const* y, const int64_t* ldy, bool accumulate, const __half* xlo = nullptr,
+                 const float* wscale = nullptr);
+// Split variant of matmul_quant (xlo != null): x carries its low halves in
+// xlo (fp16(x - fp16(x)), same layout), the weights are expanded at the
+// powers of two wscale[i] (matmul_split_scale) as exact hi + lo fp16 pairs, and
+// each k-step runs three MMAs; near-fp32 accuracy at about three times the MMA
+// work.
+// The power of two 2^E a tensor's weights are expanded at in the split
+// variant (largest possible |weight| * 2^E <= 2^14), computed on first use
+// with a reduction over its blocks' scales (synchronises the stream) and
+// cached in the tensor.
+int matmul_split_scale(cn_tensor* t, cudaStream_t st, float* out);
 inline bool matmul_type_ok(int type) {
     return type == CN_TYPE_Q4_0 || type == CN_TYPE_Q4_K || type == CN_TYPE_Q6_K;
 }
@@ -126,18 +138,22 @@ inline bool matmul_type_ok(int type) {
 // inverses in inv[M] (prefill.cu); n % 4 == 0, x and y 16-byte aligned.
 int to_half_rows(cudaStream_t st, const float* x, __half* y, float* inv, int n, int M);
 
-// Prefill kernels around the matmul (prefill.cu).
+// Prefill kernels around the matmul (prefill.cu).  With ylo, the norm also
+// writes each value's fp16 rounding residual (the split matmul's low halves).
 int prefill_norm(cudaStream_t st, const float* x, const float* w, __half* y, float* inv, int n, int M,
-                 float eps);
+                 float eps, __half* ylo = nullptr);
 int prefill_silu(cudaStream_t st, const float* g, const float* u, __half* h, float* inv, int n, int M);
 // RoPE of the M prompt tokens' q (in place) and k, k/v into the cache and
-// their fp16 copies into kh/vh [M][kvdim].
+// their fp16 copies into kh/vh [M][kvdim] (with kl, also k's fp16 residuals).
 int prefill_rope(cudaStream_t st, float* q, const float* k, const float* v, const float2* rope, int pos0, int M,
                  int qdim, int kvdim, int hd, void* kcache, void* vcache, int64_t cache_off, bool kv_f16, __half* kh,
-                 __half* vh);
+                 __half* vh, __half* kl = nullptr);
+// Causal prefill attention; split: scores from q and k as hi + lo fp16 pairs
+// (kl: k's residuals, needed for fp32 caches).
 int prefill_attention(cudaStream_t st, const float* q, int q_stride, const void* kcache,
                       const void* vcache, bool kv_f16, int64_t cache_off, int n_heads, int n_kv,
-                      int hd, int M, int pos0, const __half* kh, const __half* vh, __half* out, int out_stride);
+                      int hd, int M, int pos0, const __half* kh, const __half* vh, __half* out, int out_stride,
+                      bool split = false, const __half* kl = nullptr);
 
 // Scratch requirements of one GEMV call.
 struct GemvPlan {

@@ -29,8 +29,8 @@ enum { T_EMB = 0, T_OUT = 1, T_ONORM = 2 };
 enum { L_ANORM = 0, L_Q, L_K, L_V, L_O, L_FNORM, L_GATE, L_UP, L_DOWN };
 constexpr int kMaxBatch = 32;
 // Prompts of at least m->prefill_min tokens (0: never) take the prefill
-// matmul in cn_llama_forward; off unless cn_llama_set_prefill turns it on.
-constexpr int kPrefillMin = 16;  // the smallest threshold cn_llama_set_prefill accepts
+// matmul in cn_llama_forward: from kPrefillMin tokens by default.
+constexpr int kPrefillMin = 16;  // the default and the smallest threshold cn_llama_set_prefill accepts
 
 struct Step {
     bool built = false;
@@ -71,7 +71,12 @@ struct cn_llama {
     // on first use: residual stream, q/k/v, gate/up (fp32), the fp16
     // operand of the next matmul, fp16 copies of the new k/v rows, token ids
     int pf_cap = 0;
-    int prefill_min = 0;  // cn_llama_forward's prefill threshold (0: sequential steps)
+    int prefill_min = cn::kPrefillMin;  // cn_llama_forward's prefill threshold (0: sequential steps)
+    // 1: the q/k projections and the attention scores run on split (hi + lo
+    // fp16) operands, 0: every operand rounded to fp16 (cn_llama_set_prefill_precision)
+    int prefill_split = 1;
+    std::vector<float> pf_ws;  // split scales of each layer's q and k weights ([2 * layers]; empty: not yet computed)
+    __half *pf_hl = nullptr, *pf_kl = nullptr;  // low halves of the normalised input / of k
     float *pf_x = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_g = nullptr,
           *pf_u = nullptr;
     __half *pf_h = nullptr, *pf_kh = nullptr, *pf_vh = nullptr;
@@ -431,7 +436,7 @@ static void free_model(cn_llama* m) {
                     m->gate, m->up, m->logits, m->part, m->tokens, m->pos, m->amax,
                     m->gb.xfrag, m->gb.xsum, m->gb.partials, m->gb.counters, m->gb.xinv,
                     m->pf_x, m->pf_q, m->pf_k, m->pf_v, m->pf_g, m->pf_u, m->pf_h, m->pf_kh, m->pf_vh,
-                    m->pf_tok, m->pf_xs};
+                    m->pf_tok, m->pf_xs, m->pf_hl, m->pf_kl};
     for (void* p : bufs) cudaFree(p);
     cudaFreeHost(m->h_tokens);
     cudaFreeHost(m->h_pos);
@@ -463,15 +468,19 @@ static bool prefill_supported(const cn_llama* m) {
 // One launch group of layer l's projections (q/k/v, o, gate/up or down, all
 // with inner dimension K) on the fp16 rows m->pf_h, whose inverse row scales
 // are m->pf_xs when `scaled`: one matmul launch per run of matrices of the
-// same weight type (a single launch when the group's types agree).  With
+// same weight type (a single launch when the group's types agree).  The first
+// `nsplit` matrices run the split variant (low halves of the rows in
+// m->pf_hl, weight scales ws[0..nsplit)), the rest the fp16 one.  With
 // count_only, returns the number of launches instead.
 static int mm_group(cn_llama* m, int l, int nmat, const int* slots, const int64_t* rows, int64_t K, int n,
-                    float* const* y, const int64_t* ldy, bool accumulate, bool scaled, bool count_only = false) {
+                    float* const* y, const int64_t* ldy, bool accumulate, bool scaled, bool count_only = false,
+                    int nsplit = 0, const float* ws = nullptr) {
     int launches = 0;
     for (int i = 0; i < nmat;) {
         const int type = LT(m, l, slots[i])->type;
+        const bool split = i < nsplit;
         int j = i + 1;
-        while (j < nmat && LT(m, l, slots[j])->type == type) j++;
+        while (j < nmat && LT(m, l, slots[j])->type == type && (j < nsplit) == split) j++;
         launches++;
         if (!count_only) {
             const void* w[3];
@@ -481,7 +490,8 @@ static int mm_group(cn_llama* m, int l, int nmat, const int* slots, const int64_
                 wm[k - i] = wmap(LT(m, l, slots[k]));
             }
             int rc = matmul_quant(m->ctx->stream, m->ctx->dev_err, type, j - i, w, wm, rows + i, K, m->pf_h,
-                                  scaled ? m->pf_xs : nullptr, n, y + i, ldy + i, accumulate);
+                                  scaled ? m->pf_xs : nullptr, n, y + i, ldy + i, accumulate,
+                                  split ? m->pf_hl : nullptr, split ? ws + i : nullptr);
             if (rc) return rc;
         }
         i = j;
@@ -492,14 +502,30 @@ static int mm_group(cn_llama* m, int l, int nmat, const int* slots, const int64_
 static const int kSlotsQKV[3] = {L_Q, L_K, L_V}, kSlotsO[1] = {L_O}, kSlotsGU[2] = {L_GATE, L_UP},
                  kSlotsDown[1] = {L_DOWN};
 
+// Each q/k weight matrix's split-variant expansion scale, computed once
+// (synchronises the stream).
+static int prefill_scales(cn_llama* m) {
+    if (!m->pf_ws.empty()) return CN_OK;
+    const int L = m->cfg.n_layers;
+    std::vector<float> ws(2 * (size_t)L);
+    for (int l = 0; l < L; l++)
+        for (int j = 0; j < 2; j++) {
+            int rc = matmul_split_scale(const_cast<cn_tensor*>(LT(m, l, j == 0 ? L_Q : L_K)), m->ctx->stream,
+                                        &ws[2 * (size_t)l + j]);
+            if (rc) return rc;
+        }
+    m->pf_ws.swap(ws);
+    return CN_OK;
+}
+
 static int prefill_reserve(cn_llama* m, int n) {
     if (n <= m->pf_cap) return CN_OK;
     CN_CUDA(cudaStreamSynchronize(m->ctx->stream));
     void* old[] = {m->pf_x, m->pf_q, m->pf_k, m->pf_v, m->pf_g, m->pf_u, m->pf_h, m->pf_kh, m->pf_vh,
-                   m->pf_tok, m->pf_xs};
+                   m->pf_tok, m->pf_xs, m->pf_hl, m->pf_kl};
     for (void* p : old) cudaFree(p);
     m->pf_x = m->pf_q = m->pf_k = m->pf_v = m->pf_g = m->pf_u = nullptr;
-    m->pf_h = m->pf_kh = m->pf_vh = nullptr;
+    m->pf_h = m->pf_kh = m->pf_vh = m->pf_hl = m->pf_kl = nullptr;
     m->pf_tok = nullptr;
     m->pf_xs = nullptr;
     m->pf_cap = 0;
@@ -517,7 +543,9 @@ static int prefill_reserve(cn_llama* m, int n) {
         (rc = dmalloc((void**)&m->pf_kh, N * m->kvdim * 2, false)) ||
         (rc = dmalloc((void**)&m->pf_vh, N * m->kvdim * 2, false)) ||
         (rc = dmalloc((void**)&m->pf_tok, N * 4, false)) ||
-        (rc = dmalloc((void**)&m->pf_xs, N * 4, false)))
+        (rc = dmalloc((void**)&m->pf_xs, N * 4, false)) ||
+        (rc = dmalloc((void**)&m->pf_hl, N * c.dim * 2, false)) ||
+        (rc = dmalloc((void**)&m->pf_kl, N * m->kvdim * 2, false)))
         return rc;
     m->pf_cap = n;
     return CN_OK;
@@ -534,22 +562,27 @@ static int prefill_layers(cn_llama* m, int n, int pos) {
     const cn_llama_config& c = m->cfg;
     cudaStream_t s = m->ctx->stream;
     const int qd = m->qdim, kvd = m->kvdim, hid = c.hidden_dim;
+    const bool split = m->prefill_split != 0, kv16 = c.kv_dtype == CN_KV_F16;
     int rc;
+    if (split && (rc = prefill_scales(m))) return rc;
     for (int l = 0; l < c.n_layers; l++) {
         const int64_t cache_off = (int64_t)l * c.ctx_len * kvd;  // sequence slot 0
         if ((rc = prefill_norm(s, m->pf_x, (const float*)LT(m, l, L_ANORM)->d, m->pf_h, m->pf_xs, c.dim, n,
-                               c.rms_eps)))
+                               c.rms_eps, split ? m->pf_hl : nullptr)))
             return rc;
         {
+            // q and k feed the softmax, which magnifies their errors: split operands
             const int64_t rows[3] = {qd, kvd, kvd};
             float* y[3] = {m->pf_q, m->pf_k, m->pf_v};
-            if ((rc = mm_group(m, l, 3, kSlotsQKV, rows, c.dim, n, y, rows, false, true))) return rc;
+            if ((rc = mm_group(m, l, 3, kSlotsQKV, rows, c.dim, n, y, rows, false, true, false, split ? 2 : 0,
+                               split ? &m->pf_ws[2 * (size_t)l] : nullptr)))
+                return rc;
         }
         if ((rc = prefill_rope(s, m->pf_q, m->pf_k, m->pf_v, m->rope, pos, n, qd, kvd, c.head_dim, m->kc, m->vc,
-                               cache_off, c.kv_dtype == CN_KV_F16, m->pf_kh, m->pf_vh)))
+                               cache_off, kv16, m->pf_kh, m->pf_vh, split && !kv16 ? m->pf_kl : nullptr)))
             return rc;
-        if ((rc = prefill_attention(s, m->pf_q, qd, m->kc, m->vc, c.kv_dtype == CN_KV_F16, cache_off, m->nh,
-                                    m->nkv, c.head_dim, n, pos, m->pf_kh, m->pf_vh, m->pf_h, qd)))
+        if ((rc = prefill_attention(s, m->pf_q, qd, m->kc, m->vc, kv16, cache_off, m->nh, m->nkv, c.head_dim, n,
+                                    pos, m->pf_kh, m->pf_vh, m->pf_h, qd, split, split && !kv16 ? m->pf_kl : nullptr)))
             return rc;
         {
             const int64_t rows = c.dim;
@@ -581,7 +614,7 @@ static int prefill_kernels(const cn_llama* m) {
     float* y[3] = {nullptr, nullptr, nullptr};
     int k = 0;
     for (int l = 0; l < m->cfg.n_layers; l++)
-        k += 6 + mm_group(mm, l, 3, kSlotsQKV, r, 0, 0, y, r, false, false, true) +
+        k += 6 + mm_group(mm, l, 3, kSlotsQKV, r, 0, 0, y, r, false, false, true, m->prefill_split ? 2 : 0) +
              mm_group(mm, l, 1, kSlotsO, r, 0, 0, y, r, false, false, true) +
              mm_group(mm, l, 2, kSlotsGU, r, 0, 0, y, r, false, false, true) +
              mm_group(mm, l, 1, kSlotsDown, r, 0, 0, y, r, false, false, true);
@@ -857,6 +890,13 @@ int cn_llama_set_prefill(cn_llama* m, int min_tokens) {
     return CN_OK;
 }
 
+int cn_llama_set_prefill_precision(cn_llama* m, int split) {
+    CN_CHECK(m, CN_ERR_INVALID_ARG, "null model");
+    CN_CHECK(split == 0 || split == 1, CN_ERR_INVALID_ARG, "prefill precision %d: 0 or 1", split);
+    m->prefill_split = split;
+    return CN_OK;
+}
+
 int cn_llama_sample(cn_llama* m, int batch, float temperature, int top_k, float top_p, const float* r_host,
                     int* tokens_host) {
     CN_CHECK(m, CN_ERR_INVALID_ARG, "null model");
@@ -1004,6 +1044,9 @@ int cn_llama_time_matmul(cn_llama* m, int group, int n, int iters, float* us_per
     CN_CUDA(cudaMemsetAsync(m->pf_h, 0, (size_t)n * (hid > dim ? hid : dim) * 2, s));
     CN_CUDA(cudaMemsetAsync(m->pf_x, 0, (size_t)n * dim * 4, s));
     CN_CUDA(cudaMemsetAsync(m->pf_xs, 0, (size_t)n * 4, s));
+    CN_CUDA(cudaMemsetAsync(m->pf_hl, 0, (size_t)n * dim * 2, s));
+    const bool split = m->prefill_split != 0;
+    if (split && (rc = prefill_scales(m))) return rc;
     const int L = c.n_layers;
     double flops = 0;
     auto launch = [&](int i) -> int {
@@ -1011,8 +1054,9 @@ int cn_llama_time_matmul(cn_llama* m, int group, int n, int iters, float* us_per
         if (group == 0) {
             const int64_t rows[3] = {qd, kvd, kvd};
             float* y[3] = {m->pf_q, m->pf_k, m->pf_v};
-            flops = 2.0 * n * (double)(qd + 2 * kvd) * dim;
-            return mm_group(m, l, 3, kSlotsQKV, rows, dim, n, y, rows, false, true);
+            flops = 2.0 * n * (double)(qd + 2 * kvd) * dim;  // algorithmic (the split's extra MMAs not counted)
+            return mm_group(m, l, 3, kSlotsQKV, rows, dim, n, y, rows, false, true, false, split ? 2 : 0,
+                            split ? &m->pf_ws[2 * (size_t)l] : nullptr);
         }
         if (group == 2) {
             const int64_t rows[2] = {hid, hid};

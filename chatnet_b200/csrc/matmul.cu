@@ -43,6 +43,10 @@
 // word and stops waiting (its control flow stays uniform; results are
 // garbage and flagged).  The CTA still waits for its own copies and MMAs
 // before it frees its tensor memory.
+#include <math.h>
+#include <string.h>
+
+#include <cmath>
 #include <mutex>
 
 #include "cn_common.cuh"
@@ -77,6 +81,20 @@ constexpr int kDBufs = 2;                // accumulator buffers
 constexpr int kRawOff = kStages * kBStage;
 constexpr int kACols = kKS / 2;          // tensor-memory columns of one A stage (2 fp16 each)
 constexpr int kACol = kDBufs * kNT;      // accumulator(s) first, the A ring after them
+// The split (hi + lo) variant: every weight and activation is carried as an
+// exact pair of fp16 halves and each k-step runs three MMAs (Whi Xhi, Whi Xlo,
+// Wlo Xhi) into the same accumulator.  A stage then holds both activation
+// halves (64 KB) and an A slot both weight halves (128 columns), so the ring
+// has two stages; shared and tensor memory add up to the same totals.
+template <bool SPLIT>
+struct SGeo {
+    static constexpr int kStages = SPLIT ? 2 : mm::kStages;
+    static constexpr int kBStage = SPLIT ? 2 * mm::kBStage : mm::kBStage;
+    static constexpr int kACols = SPLIT ? 2 * mm::kACols : mm::kACols;
+};
+static_assert(SGeo<true>::kStages * SGeo<true>::kBStage == kStages * kBStage &&
+                  SGeo<true>::kStages * SGeo<true>::kACols == kStages * kACols,
+              "split ring sizes");
 constexpr int kTmemCols = 512;
 constexpr int kDecode = 256;             // decode threads: warps 0-7
 constexpr int kEpi = 128;                // epilogue threads: warps 8-11
@@ -94,6 +112,7 @@ static_assert(kRawOff % 1024 == 0 && RawGeo<CN_TYPE_Q6_K>::kBytes % 128 == 0 && 
 // rows x row bytes, boxes of 144 bytes x 128 rows, as for the decode GEMV).
 struct Maps {
     CUtensorMap x;
+    CUtensorMap xlo;  // split variant: the activations' low halves
     CUtensorMap w[kMaxMats];
 };
 static_assert(kSmem <= 227 * 1024, "shared memory");
@@ -111,6 +130,8 @@ struct Args {
     int64_t ldy[kMaxMats];
     int64_t rb;                 // bytes per weight row
     const float* xs;            // per-token factor of the result (x's inverse scale), or null
+    float wscale[kMaxMats];     // split variant: power of two the weights are expanded at (2^E)
+    float oscale[kMaxMats];     // factor of matrix m's results (2^-E; 1 outside the split variant)
     int M, K;                   // K % 256 == 0
     int accumulate;             // 1: Y += result, 0: Y = result
     int tok_tiles;              // token tiles of 128; tile t = row tile t / tok_tiles, token tile t % tok_tiles
@@ -224,6 +245,119 @@ __device__ __forceinline__ void expand_q6k_half(const uint8_t* sb, int h, int wg
     }
 }
 
+// ---- split variant: each weight as an exact pair of fp16 halves ----------
+// Weights are expanded at 2^E (ws), a power of two chosen per matrix so that
+// its largest weight stays below 2^14; the epilogue multiplies by 2^-E.
+
+// hi = fp16(w), lo = fp16(w - hi) for two fp32 weights, packed in pairs.
+__device__ __forceinline__ void split_pair(float w0, float w1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(w0, w1);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = pack_half2(w0 - __low2float(h), w1 - __high2float(h));  // the differences are exact in fp32
+}
+
+// The four low (or high, sh = 4) nibbles of w as floats, exactly: the nibble
+// becomes the low mantissa bits of 2^23.
+__device__ __forceinline__ void nib4_f32(uint32_t w, int sh, float (&f)[4]) {
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+        f[k] = __uint_as_float(0x4B000000u | ((w >> (8 * k + sh)) & 15u)) - 8388608.0f;
+}
+
+// Q4_0, split: two blocks as expand_q4_0_pair lays them out.  With D = d * ws
+// (11 significant bits) cut into Dhi (its top 7 bits) and Dlo = D - Dhi (the
+// other 4), (q - 8) * Dhi needs at most 11 bits and (q - 8) * Dlo at most 8,
+// so both fp16 products are exact and hi + lo is the weight (q - 8) * d * ws.
+__device__ __forceinline__ void expand_q4_0_pair_split(const uint32_t (&wd)[9], float ws, uint32_t (&ohi)[32],
+                                                       uint32_t (&olo)[32]) {
+    constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024 in both halves
+    constexpr uint32_t kBias = 0x64086408u;   // fp16 1032 = 1024 + 8
+#pragma unroll
+    for (int blk = 0; blk < 2; blk++) {
+        uint32_t q[4], d;
+        if (blk == 0) {
+            d = wd[0] & 0xFFFFu;
+#pragma unroll
+            for (int i = 0; i < 4; i++) q[i] = __funnelshift_r(wd[i], wd[i + 1], 16);
+        } else {
+            d = wd[4] >> 16;
+#pragma unroll
+            for (int i = 0; i < 4; i++) q[i] = wd[5 + i];
+        }
+        const float D = half_bits_to_float((uint16_t)d) * ws;
+        const float Dhi = __uint_as_float(__float_as_uint(D) & 0xFFFE0000u);
+        const uint32_t dh2 = pack_half2(Dhi, Dhi), dl2 = pack_half2(D - Dhi, D - Dhi);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const uint32_t t = __byte_perm(q[i], 0u, h ? 0x4342u : 0x4140u);
+                const uint32_t lo = h2_sub(lop3_and_or(t, 0x000F000Fu, kMagic), kBias);  // q - 8, exact
+                const uint32_t hi = h2_sub(lop3_and_or(t >> 4, 0x000F000Fu, kMagic), kBias);
+                ohi[16 * blk + 2 * i + h] = h2_mul(lo, dh2);
+                olo[16 * blk + 2 * i + h] = h2_mul(lo, dl2);
+                ohi[16 * blk + 8 + 2 * i + h] = h2_mul(hi, dh2);
+                olo[16 * blk + 8 + 2 * i + h] = h2_mul(hi, dl2);
+            }
+        }
+    }
+}
+
+// Q4_K, split: two sub-blocks as expand_q4k_pair lays them out.  The weight is
+// the reference's fp32 value (d*sc)*q - dmin*m (DequantQ4K.cs:59-71), here at
+// 2^E: dsc = fp32(d*sc) * ws and dm = fp32(dmin*m) * ws per sub-block.
+__device__ __forceinline__ void expand_q4k_pair_split(const uint32_t (&qw)[8], const float (&dsc)[2],
+                                                      const float (&dm)[2], uint32_t (&ohi)[32],
+                                                      uint32_t (&olo)[32]) {
+#pragma unroll
+    for (int blk = 0; blk < 2; blk++) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            float fl[4], fh[4];
+            nib4_f32(qw[4 * blk + i], 0, fl);
+            nib4_f32(qw[4 * blk + i], 4, fh);
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                split_pair(__fsub_rn(__fmul_rn(dsc[blk], fl[2 * h]), dm[blk]),
+                           __fsub_rn(__fmul_rn(dsc[blk], fl[2 * h + 1]), dm[blk]), ohi[16 * blk + 2 * i + h],
+                           olo[16 * blk + 2 * i + h]);
+                split_pair(__fsub_rn(__fmul_rn(dsc[blk], fh[2 * h]), dm[blk]),
+                           __fsub_rn(__fmul_rn(dsc[blk], fh[2 * h + 1]), dm[blk]), ohi[16 * blk + 8 + 2 * i + h],
+                           olo[16 * blk + 8 + 2 * i + h]);
+            }
+        }
+    }
+}
+
+// Q6_K, split: expand_q6k_half's positions, each the reference's fp32 value
+// (d * sc) * (q - 32) at 2^E (d already multiplied by ws), as hi + lo.
+__device__ __forceinline__ void expand_q6k_half_split(const uint8_t* sb, int h, int wg, float d, uint32_t (&ohi)[32],
+                                                      uint32_t (&olo)[32]) {
+    uint32_t qh[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) qh[k] = lds_u32_a2(sb + 128 + 32 * h + 4 * k);
+    float dsc[4];
+#pragma unroll
+    for (int jj = 0; jj < 2; jj++)
+#pragma unroll
+        for (int ll = 0; ll < 2; ll++)
+            dsc[2 * jj + ll] = __fmul_rn(d, (float)(int8_t)sb[192 + 8 * h + ll + 4 * wg + 2 * jj]);
+#pragma unroll
+    for (int k = 0; k < 16; k++) {
+        const uint32_t w = lds_u32_a2(sb + 64 * h + 4 * k);
+        const uint32_t nib = (wg ? (w >> 4) : w) & 0x0F0F0F0Fu;
+        const int jj = k >> 3;
+        const uint32_t hb = (qh[k & 7] >> (4 * wg + 2 * jj)) & 0x03030303u;
+        const uint32_t q4 = nib | (hb << 4);
+        const float t = dsc[2 * jj + ((k & 7) >> 2)];
+        float v[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) v[e] = __fmul_rn(t, (float)((int)((q4 >> (8 * e)) & 0xFFu) - 32));
+        split_pair(v[0], v[1], ohi[2 * k], olo[2 * k]);
+        split_pair(v[2], v[3], ohi[2 * k + 1], olo[2 * k + 1]);
+    }
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
@@ -302,10 +436,11 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t addr) {
 
 }  // namespace mm
 
-template <int WT>
+template <int WT, bool SPLIT>
 __global__ void __launch_bounds__(mm::kThreads, 1)
     matmul_q_kernel(const __grid_constant__ mm::Maps maps, const mm::Args a) {
     using RG = mm::RawGeo<WT>;
+    using SG = mm::SGeo<SPLIT>;
     using namespace mm;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -330,7 +465,7 @@ __global__ void __launch_bounds__(mm::kThreads, 1)
     };
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; s++) {
+        for (int s = 0; s < SG::kStages; s++) {
             mbar_init(&full[s], kDecodeWarps + 1);  // the decode warps and the producer's expect_tx
             mbar_init(&empty[s], 1);
         }
@@ -383,21 +518,27 @@ __global__ void __launch_bounds__(mm::kThreads, 1)
                         tma_load_2d(smem + kRawOff + rs * RG::kBytes, wmap, x, (int)row0, &raw_full[rs]);
                         gc++;
                     }
-                    const int slot = gs % kStages;
-                    if (gs >= kStages && !mbar_wait(&empty[slot], (uint32_t)((gs / kStages) - 1) & 1)) {
+                    const int slot = gs % SG::kStages;
+                    if (gs >= SG::kStages &&
+                        !mbar_wait(&empty[slot], (uint32_t)((gs / SG::kStages) - 1) & 1)) {
                         atomicOr(a.err, kErrTimeout);
                         ok = false;
                         break;
                     }
-                    mbar_expect_tx(&full[slot], kBStage);
-                    tma_load_2d(smem + slot * kBStage, &maps.x, s * kKS, tok0, &full[slot]);
-                    tma_load_2d(smem + slot * kBStage + kBHalf, &maps.x, s * kKS + 64, tok0, &full[slot]);
+                    mbar_expect_tx(&full[slot], SG::kBStage);
+                    uint8_t* bst = smem + slot * SG::kBStage;
+                    tma_load_2d(bst, &maps.x, s * kKS, tok0, &full[slot]);
+                    tma_load_2d(bst + kBHalf, &maps.x, s * kKS + 64, tok0, &full[slot]);
+                    if (SPLIT) {  // the low halves after the high ones
+                        tma_load_2d(bst + 2 * kBHalf, &maps.xlo, s * kKS, tok0, &full[slot]);
+                        tma_load_2d(bst + 3 * kBHalf, &maps.xlo, s * kKS + 64, tok0, &full[slot]);
+                    }
                     gs++;
                 }
             }
             // no copy may still be landing when the CTA exits
-            for (int i = gs - kStages < 0 ? 0 : gs - kStages; i < gs; i++)
-                mbar_wait(&full[i % kStages], (uint32_t)(i / kStages) & 1);
+            for (int i = gs - SG::kStages < 0 ? 0 : gs - SG::kStages; i < gs; i++)
+                mbar_wait(&full[i % SG::kStages], (uint32_t)(i / SG::kStages) & 1);
             for (int i = gc - RG::kStages < 0 ? 0 : gc - RG::kStages; i < gc; i++)
                 mbar_wait(&raw_full[i % RG::kStages], (uint32_t)(i / RG::kStages) & 1);
         }
@@ -416,10 +557,10 @@ __global__ void __launch_bounds__(mm::kThreads, 1)
                 const uint32_t d_tmem = tmem + db * kNT;
                 // the test of a stage's barrier is issued before the previous
                 // stage's MMAs, so its latency hides behind their issue
-                uint32_t ready = mbar_test(&full[gs % kStages], (uint32_t)(gs / kStages) & 1);
+                uint32_t ready = mbar_test(&full[gs % SG::kStages], (uint32_t)(gs / SG::kStages) & 1);
                 for (int s = 0; s < nst; s++, gs++) {
-                    const int slot = gs % kStages;
-                    const uint32_t ph = (uint32_t)(gs / kStages) & 1;
+                    const int slot = gs % SG::kStages;
+                    const uint32_t ph = (uint32_t)(gs / SG::kStages) & 1;
                     if (!ready && !mbar_wait(&full[slot], ph)) {
                         atomicOr(a.err, kErrTimeout);
                         ok = false;
@@ -427,12 +568,20 @@ __global__ void __launch_bounds__(mm::kThreads, 1)
                     }
                     tc_fence_after();
                     const int ns = gs + 1;
-                    ready = s + 1 < nst ? mbar_test(&full[ns % kStages], (uint32_t)(ns / kStages) & 1) : 0u;
-                    const uint32_t b0 = smem_u32(smem + slot * kBStage);
+                    ready = s + 1 < nst ? mbar_test(&full[ns % SG::kStages], (uint32_t)(ns / SG::kStages) & 1) : 0u;
+                    const uint32_t b0 = smem_u32(smem + slot * SG::kBStage);
 #pragma unroll
-                    for (int kk = 0; kk < kKS / 16; kk++)
-                        mma_f16(d_tmem, tmem + kACol + slot * kACols + 8 * kk,
-                                desc_sw128(b0 + (kk / 4) * kBHalf + 32 * (kk % 4)), (s | kk) != 0);
+                    for (int kk = 0; kk < kKS / 16; kk++) {
+                        const uint32_t a_hi = tmem + kACol + slot * SG::kACols + 8 * kk;
+                        const uint64_t b_hi = desc_sw128(b0 + (kk / 4) * kBHalf + 32 * (kk % 4));
+                        mma_f16(d_tmem, a_hi, b_hi, (s | kk) != 0);
+                        if (SPLIT) {
+                            // Whi Xlo and Wlo Xhi into the same accumulator (Wlo Xlo is
+                            // below the pair's own rounding)
+                            mma_f16(d_tmem, a_hi, desc_sw128(b0 + (2 + kk / 4) * kBHalf + 32 * (kk % 4)), 1u);
+                            mma_f16(d_tmem, a_hi + kACols, b_hi, 1u);
+                        }
+                    }
                     mma_commit(&empty[slot]);
                 }
                 mma_commit(&dfull[db]);  // completes once every MMA issued above has
@@ -470,10 +619,11 @@ __global__ void __launch_bounds__(mm::kThreads, 1)
                     tc_fence_before();
                     if (lane == 0) mbar_arrive(&dempty[db]);
                 }
-                if (a.xs) {
-                    // undo token t's activation scaling (an exact power of two)
+                if (a.xs || SPLIT) {
+                    // undo token t's activation scaling and the split variant's
+                    // weight scaling (both exact powers of two)
                     const int tk = tok0 + 32 * j + lane;
-                    const float sc = tk < a.M ? a.xs[tk] : 1.f;
+                    const float sc = (a.xs && tk < a.M ? a.xs[tk] : 1.f) * pick(a.oscale, m);
 #pragma unroll
                     for (int u = 0; u < 32; u++)
                         v[u] = __float_as_uint(__uint_as_float(v[u]) * __shfl_sync(0xffffffffu, sc, u));
@@ -508,6 +658,9 @@ __global__ void __launch_bounds__(mm::kThreads, 1)
         bool failed = false;
         int gs = 0, gc = 0;
         for (int t = blockIdx.x; t < a.tiles; t += gridDim.x) {
+            int tmat, tok0_;
+            int64_t row0_;
+            tile_mat(t, tmat, row0_, tok0_);  // the tile's matrix (its split scale)
             for (int c = 0; c < nch; c++, gc++) {
                 const int rs = gc % RG::kStages;
                 if (!failed && !mbar_wait(&raw_full[rs], (uint32_t)(gc / RG::kStages) & 1)) {
@@ -521,16 +674,23 @@ __global__ void __launch_bounds__(mm::kThreads, 1)
                     const float d = half_bits_to_float(lds_u16(sb + 208));
 #pragma unroll 1
                     for (int q = 0; q < 2; q++, gs++) {
-                        const int slot = gs % kStages;
-                        if (gs >= kStages && !failed &&
-                            !mbar_wait(&empty[slot], (uint32_t)((gs / kStages) - 1) & 1)) {
+                        const int slot = gs % SG::kStages;
+                        if (gs >= SG::kStages && !failed &&
+                            !mbar_wait(&empty[slot], (uint32_t)((gs / SG::kStages) - 1) & 1)) {
                             atomicOr(a.err, kErrTimeout);
                             failed = true;
                         }
                         tc_fence_after();
                         uint32_t o[32];
-                        expand_q6k_half(sb, q, wg, d, o);
-                        tmem_st32(lane_base + kACol + slot * kACols + 32 * wg, o);
+                        const uint32_t col = lane_base + kACol + slot * SG::kACols + 32 * wg;
+                        if (SPLIT) {
+                            uint32_t ol[32];
+                            expand_q6k_half_split(sb, q, wg, d * pick(a.wscale, tmat), o, ol);
+                            tmem_st32(col + kACols, ol);
+                        } else {
+                            expand_q6k_half(sb, q, wg, d, o);
+                        }
+                        tmem_st32(col, o);
                         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                         tc_fence_before();
                         if (lane == 0) mbar_arrive(&full[slot]);
@@ -547,6 +707,7 @@ __global__ void __launch_bounds__(mm::kThreads, 1)
                 const uint32_t* row32 = reinterpret_cast<const uint32_t*>(raw + rs * RG::kBytes + r * RG::kRow);
                 uint32_t cur[18];
                 uint32_t d2 = 0, sc2[2][2], ndm2[2][2];  // Q4_K: d, [stage][sub-block] sc and -dmin * m
+                float dscf[2][2], dmf[2][2];             // Q4_K split: fp32 d*sc and dmin*m at 2^E
                 if (WT == CN_TYPE_Q4_0) {
 #pragma unroll
                     for (int q = 0; q < 2; q++)
@@ -584,32 +745,50 @@ __global__ void __launch_bounds__(mm::kThreads, 1)
                             const float dm = __fmul_rn(dmin, (float)mm_);
                             sc2[q][e] = pack_half2((float)sc, (float)sc);
                             ndm2[q][e] = pack_half2(-dm, -dm);
+                            if (SPLIT) {
+                                const float ws = pick(a.wscale, tmat);
+                                dscf[q][e] = __fmul_rn(half_bits_to_float((uint16_t)(hw[0] & 0xFFFFu)), (float)sc) * ws;
+                                dmf[q][e] = dm * ws;
+                            }
                         }
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&raw_empty[rs]);
 #pragma unroll
                 for (int q = 0; q < 2; q++, gs++) {
-                    const int slot = gs % kStages;
-                    if (gs >= kStages && !failed &&
-                        !mbar_wait(&empty[slot], (uint32_t)((gs / kStages) - 1) & 1)) {
+                    const int slot = gs % SG::kStages;
+                    if (gs >= SG::kStages && !failed &&
+                        !mbar_wait(&empty[slot], (uint32_t)((gs / SG::kStages) - 1) & 1)) {
                         atomicOr(a.err, kErrTimeout);
                         failed = true;
                     }
                     tc_fence_after();
                     uint32_t o[32];
+                    const uint32_t col = lane_base + kACol + slot * SG::kACols + 32 * wg;
                     if (WT == CN_TYPE_Q4_0) {
                         uint32_t wd[9];
 #pragma unroll
                         for (int k = 0; k < 9; k++) wd[k] = cur[9 * q + k];
-                        expand_q4_0_pair(wd, o);
+                        if (SPLIT) {
+                            uint32_t ol[32];
+                            expand_q4_0_pair_split(wd, pick(a.wscale, tmat), o, ol);
+                            tmem_st32(col + kACols, ol);
+                        } else {
+                            expand_q4_0_pair(wd, o);
+                        }
                     } else {
                         uint32_t qw[8];
 #pragma unroll
                         for (int k = 0; k < 8; k++) qw[k] = cur[8 * q + k];
-                        expand_q4k_pair(qw, d2, sc2[q], ndm2[q], o);
+                        if (SPLIT) {
+                            uint32_t ol[32];
+                            expand_q4k_pair_split(qw, dscf[q], dmf[q], o, ol);
+                            tmem_st32(col + kACols, ol);
+                        } else {
+                            expand_q4k_pair(qw, d2, sc2[q], ndm2[q], o);
+                        }
                     }
-                    tmem_st32(lane_base + kACol + slot * kACols + 32 * wg, o);
+                    tmem_st32(col, o);
                     // warp-wide: every lane's stores of this stage are done
                     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                     tc_fence_before();
@@ -642,10 +821,13 @@ int encode_act_map(const __half* x, int M, int64_t K, CUtensorMap* out) {
 
 int matmul_quant(cudaStream_t st, uint32_t* err, int type, int nmat, const void* const* w,
                  const CUtensorMap* const* wmaps, const int64_t* rows, int64_t K, const __half* x, const float* xs,
-                 int M, float* const* y, const int64_t* ldy, bool accumulate) {
+                 int M, float* const* y, const int64_t* ldy, bool accumulate, const __half* xlo,
+                 const float* wscale) {
     CN_CHECK(matmul_type_ok(type), CN_ERR_UNSUPPORTED, "matmul: weight type %d (Q4_0, Q4_K or Q6_K)", type);
     CN_CHECK(nmat >= 1 && nmat <= mm::kMaxMats && K > 0 && K % 256 == 0 && M >= 1, CN_ERR_INVALID_ARG,
              "matmul: bad shape (nmat %d, K %lld, M %d)", nmat, (long long)K, M);
+    const bool split = xlo != nullptr;
+    CN_CHECK(!split || wscale, CN_ERR_INVALID_ARG, "matmul: the split variant needs the weight scales");
     int dev = 0;
     CN_CUDA(cudaGetDevice(&dev));
     static std::mutex mu;
@@ -654,12 +836,11 @@ int matmul_quant(cudaStream_t st, uint32_t* err, int type, int nmat, const void*
     {
         std::lock_guard<std::mutex> lock(mu);
         if (!attr[dev & 63]) {
-            CN_CUDA(cudaFuncSetAttribute(matmul_q_kernel<CN_TYPE_Q4_0>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, mm::kSmem));
-            CN_CUDA(cudaFuncSetAttribute(matmul_q_kernel<CN_TYPE_Q4_K>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, mm::kSmem));
-            CN_CUDA(cudaFuncSetAttribute(matmul_q_kernel<CN_TYPE_Q6_K>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, mm::kSmem));
+#define CN_MM_ATTR(T, S) \
+    CN_CUDA(cudaFuncSetAttribute(matmul_q_kernel<T, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, mm::kSmem));
+            CN_MM_ATTR(CN_TYPE_Q4_0, false) CN_MM_ATTR(CN_TYPE_Q4_K, false) CN_MM_ATTR(CN_TYPE_Q6_K, false)
+            CN_MM_ATTR(CN_TYPE_Q4_0, true) CN_MM_ATTR(CN_TYPE_Q4_K, true) CN_MM_ATTR(CN_TYPE_Q6_K, true)
+#undef CN_MM_ATTR
             CN_CUDA(cudaDeviceGetAttribute(&sm_count[dev & 63], cudaDevAttrMultiProcessorCount, dev));
             attr[dev & 63] = true;
         }
@@ -682,6 +863,8 @@ int matmul_quant(cudaStream_t st, uint32_t* err, int type, int nmat, const void*
         a.rows[i] = rows[mi];
         a.y[i] = y[mi];
         a.ldy[i] = ldy[mi];
+        a.wscale[i] = split ? wscale[mi] : 1.f;
+        a.oscale[i] = split ? 1.f / wscale[mi] : 1.f;  // exact: a power of two
         CN_CHECK(w[mi] && y[mi] && rows[mi] > 0 && ldy[mi] >= rows[mi], CN_ERR_INVALID_ARG,
                  "matmul: bad matrix %d", mi);
         CN_CHECK((reinterpret_cast<uintptr_t>(w[mi]) & 15) == 0, CN_ERR_UNSUPPORTED,
@@ -699,13 +882,87 @@ int matmul_quant(cudaStream_t st, uint32_t* err, int type, int nmat, const void*
     a.err = err;
     int rc = encode_act_map(x, M, K, &maps.x);
     if (rc) return rc;
+    if (split) {
+        if ((rc = encode_act_map(xlo, M, K, &maps.xlo))) return rc;
+    } else {
+        maps.xlo = maps.x;
+    }
     const dim3 grid(a.tiles < sms ? a.tiles : sms);  // persistent: one CTA per SM
-    if (type == CN_TYPE_Q4_0)
-        CN_CUDA(launch_k(false, matmul_q_kernel<CN_TYPE_Q4_0>, grid, dim3(mm::kThreads), (size_t)mm::kSmem, st, maps, a));
-    else if (type == CN_TYPE_Q4_K)
-        CN_CUDA(launch_k(false, matmul_q_kernel<CN_TYPE_Q4_K>, grid, dim3(mm::kThreads), (size_t)mm::kSmem, st, maps, a));
-    else
-        CN_CUDA(launch_k(false, matmul_q_kernel<CN_TYPE_Q6_K>, grid, dim3(mm::kThreads), (size_t)mm::kSmem, st, maps, a));
+#define CN_MM_LAUNCH(T)                                                                                         \
+    CN_CUDA(split ? launch_k(false, matmul_q_kernel<T, true>, grid, dim3(mm::kThreads), (size_t)mm::kSmem, st, maps, a) \
+                  : launch_k(false, matmul_q_kernel<T, false>, grid, dim3(mm::kThreads), (size_t)mm::kSmem, st, maps, a));
+    if (type == CN_TYPE_Q4_0) {
+        CN_MM_LAUNCH(CN_TYPE_Q4_0)
+    } else if (type == CN_TYPE_Q4_K) {
+        CN_MM_LAUNCH(CN_TYPE_Q4_K)
+    } else {
+        CN_MM_LAUNCH(CN_TYPE_Q6_K)
+    }
+#undef CN_MM_LAUNCH
+    return CN_OK;
+}
+
+// Largest fp16 scale fields of a weight tensor's blocks: out[0] = max |d|,
+// out[1] = max |dmin| (Q4_K), as float bits (non-negative floats order like
+// their bit patterns).
+__global__ void scale_max_kernel(int type, const uint8_t* __restrict__ w, int64_t nblocks, unsigned* out) {
+    const int bpb = type == CN_TYPE_Q4_0 ? 18 : type == CN_TYPE_Q4_K ? 144 : 210;
+    const int doff = type == CN_TYPE_Q6_K ? 208 : 0;
+    unsigned m0 = 0, m1 = 0;
+    for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < nblocks; b += (int64_t)gridDim.x * blockDim.x) {
+        const uint8_t* p = w + b * bpb;
+        m0 = max(m0, __float_as_uint(fabsf(half_bits_to_float((uint16_t)(p[doff] | (p[doff + 1] << 8))))));
+        if (type == CN_TYPE_Q4_K)
+            m1 = max(m1, __float_as_uint(fabsf(half_bits_to_float((uint16_t)(p[2] | (p[3] << 8))))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        m0 = max(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+        m1 = max(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+    }
+    if ((threadIdx.x & 31) == 0) {
+        atomicMax(out, m0);
+        atomicMax(out + 1, m1);
+    }
+}
+
+int matmul_split_scale(cn_tensor* t, cudaStream_t st, float* out) {
+    CN_CHECK(t && out && matmul_type_ok(t->type), CN_ERR_INVALID_ARG, "split scale: bad tensor");
+    if (t->split_scale > 0.f) {
+        *out = t->split_scale;
+        return CN_OK;
+    }
+    const int bpb = t->type == CN_TYPE_Q4_0 ? 18 : t->type == CN_TYPE_Q4_K ? 144 : 210;
+    const int64_t nblocks = (int64_t)(t->bytes / bpb);
+    unsigned* d = nullptr;
+    CN_CUDA(cudaMalloc(&d, 2 * sizeof(unsigned)));
+    unsigned h[2] = {0, 0};
+    cudaError_t e = cudaMemsetAsync(d, 0, 2 * sizeof(unsigned), st);
+    if (e == cudaSuccess) {
+        int blocks = (int)((nblocks + 255) / 256);
+        blocks = blocks < 1 ? 1 : blocks > 1024 ? 1024 : blocks;
+        scale_max_kernel<<<blocks, 256, 0, st>>>(t->type, static_cast<const uint8_t*>(t->d), nblocks, d);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(h, d, sizeof(h), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    cudaFree(d);
+    if (e != cudaSuccess) return cuda_error(e, "split scale");
+    float dmax, dminmax;
+    memcpy(&dmax, &h[0], 4);
+    memcpy(&dminmax, &h[1], 4);
+    // the largest |weight| the format allows with these scales
+    const double bound = t->type == CN_TYPE_Q4_0   ? 8.0 * dmax
+                         : t->type == CN_TYPE_Q4_K ? 63.0 * 15.0 * dmax + 63.0 * dminmax
+                                                   : 128.0 * 32.0 * dmax;
+    int e2 = 0;
+    if (bound > 0.0 && std::isfinite(bound)) {
+        frexp(16384.0 / bound, &e2);  // 16384 / bound in [2^(e2-1), 2^e2)
+        e2 -= 1;                      // bound * 2^e2 <= 2^14
+        e2 = e2 < -100 ? -100 : e2 > 100 ? 100 : e2;
+    }
+    t->split_scale = (float)ldexp(1.0, e2);
+    *out = t->split_scale;
     return CN_OK;
 }
 

@@ -53,7 +53,8 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
 // inv[t] = 1 / s_t; n % 4 == 0.  s_t comes from rms * max|x * w|, the row's
 // largest output up to rounding.
 __global__ void norm_half_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                 __half* __restrict__ y, float* __restrict__ inv, int n, float eps) {
+                                 __half* __restrict__ y, float* __restrict__ inv, int n, float eps,
+                                 __half* __restrict__ ylo) {
     __shared__ float red[32];
     const float4* xr = reinterpret_cast<const float4*>(x + (size_t)blockIdx.x * n);
     const float4* w4 = reinterpret_cast<const float4*>(w);
@@ -78,10 +79,18 @@ __global__ void norm_half_kernel(const float* __restrict__ x, const float* __res
     row_pow2_scale(block_absmax(xw, red) * rms, sc, iv);
     for (int i = threadIdx.x; i < n4; i += blockDim.x) {
         const float4 v = xr[i], g = w4[i];
+        const float f0 = __fmul_rn(__fmul_rn(v.x, rms), g.x) * sc, f1 = __fmul_rn(__fmul_rn(v.y, rms), g.y) * sc;
+        const float f2 = __fmul_rn(__fmul_rn(v.z, rms), g.z) * sc, f3 = __fmul_rn(__fmul_rn(v.w, rms), g.w) * sc;
         uint2 o;
-        o.x = pack_half2(__fmul_rn(__fmul_rn(v.x, rms), g.x) * sc, __fmul_rn(__fmul_rn(v.y, rms), g.y) * sc);
-        o.y = pack_half2(__fmul_rn(__fmul_rn(v.z, rms), g.z) * sc, __fmul_rn(__fmul_rn(v.w, rms), g.w) * sc);
+        o.x = pack_half2(f0, f1);
+        o.y = pack_half2(f2, f3);
         yr[i] = o;
+        if (ylo) {  // the rounding residuals: y + ylo carries the value to ~2^-22
+            const __half2 h01 = *reinterpret_cast<const __half2*>(&o.x), h23 = *reinterpret_cast<const __half2*>(&o.y);
+            reinterpret_cast<uint2*>(ylo + (size_t)blockIdx.x * n)[i] =
+                make_uint2(pack_half2(f0 - __low2float(h01), f1 - __high2float(h01)),
+                           pack_half2(f2 - __low2float(h23), f3 - __high2float(h23)));
+        }
     }
     if (threadIdx.x == 0) inv[blockIdx.x] = iv;
 }
@@ -147,7 +156,8 @@ __global__ void half_rows_kernel(const float* __restrict__ x, __half* __restrict
 __global__ void rope_prefill_kernel(float* __restrict__ q, const float* __restrict__ k,
                                     const float* __restrict__ v, const float2* __restrict__ rope, int pos0,
                                     int qdim, int kvdim, int hd, void* kcache, void* vcache, int64_t cache_off,
-                                    int kv_f16, __half* __restrict__ kh, __half* __restrict__ vh) {
+                                    int kv_f16, __half* __restrict__ kh, __half* __restrict__ vh,
+                                    __half* __restrict__ kl) {
     const int t = blockIdx.x, pos = pos0 + t;
     const float4* tab = reinterpret_cast<const float4*>(rope + (size_t)pos * (hd / 2));  // two pairs per float4
     const int hd4 = hd / 4;
@@ -177,6 +187,12 @@ __global__ void rope_prefill_kernel(float* __restrict__ q, const float* __restri
         }
         reinterpret_cast<uint2*>(kh + (size_t)t * kvdim)[i] = kp;
         reinterpret_cast<uint2*>(vh + (size_t)t * kvdim)[i] = vp;
+        if (kl) {  // k's rounding residuals (fp32 caches: the attention splits Q K^T)
+            const __half2 a = *reinterpret_cast<const __half2*>(&kp.x), b = *reinterpret_cast<const __half2*>(&kp.y);
+            reinterpret_cast<uint2*>(kl + (size_t)t * kvdim)[i] =
+                make_uint2(pack_half2(kr.x - __low2float(a), kr.y - __high2float(a)),
+                           pack_half2(kr.z - __low2float(b), kr.w - __high2float(b)));
+        }
     }
 }
 
@@ -194,23 +210,30 @@ __device__ __forceinline__ void pf_cp_async16(uint32_t dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 
+// Loads keys/values p0..p0+63 of kv head kh into Ks/Vs (and, when KLs is
+// not null, the keys' fp16 rounding residuals into KLs): positions of this
+// prompt (>= pos0) from the fp16 copies with cp.async, earlier ones from the
+// cache (converted in registers), positions past `last` as zeros.
 template <int HD>
-__device__ __forceinline__ void pf_load_kv(__half* Ks, __half* Vs, int p0, int last, int pos0, int kh,
+__device__ __forceinline__ void pf_load_kv(__half* Ks, __half* Vs, __half* KLs, int p0, int last, int pos0, int kh,
                                            const void* kcache, const void* vcache, int kv_f16, int64_t cache_off,
-                                           int kvdim, const __half* kh16, const __half* vh16) {
+                                           int kvdim, const __half* kh16, const __half* vh16, const __half* kl16) {
     constexpr int RS = HD + 8, C8 = HD / 8;
     for (int i = threadIdx.x; i < kPfK * C8; i += kPfThreads) {
         const int r = i / C8, c = i % C8;
         const int p = p0 + r;
         __half* kd = Ks + r * RS + 8 * c;
         __half* vd = Vs + r * RS + 8 * c;
+        __half* ld = KLs ? KLs + r * RS + 8 * c : nullptr;
         if (p > last) {
             *reinterpret_cast<uint4*>(kd) = make_uint4(0u, 0u, 0u, 0u);
             *reinterpret_cast<uint4*>(vd) = make_uint4(0u, 0u, 0u, 0u);
+            if (ld) *reinterpret_cast<uint4*>(ld) = make_uint4(0u, 0u, 0u, 0u);
         } else if (p >= pos0) {
             const size_t e = (size_t)(p - pos0) * kvdim + kh * HD + 8 * c;
             pf_cp_async16(smem_u32(kd), kh16 + e);
             pf_cp_async16(smem_u32(vd), vh16 + e);
+            if (ld) pf_cp_async16(smem_u32(ld), kl16 + e);
         } else {
             const int64_t e = cache_off + (int64_t)p * kvdim + kh * HD + 8 * c;
 #pragma unroll
@@ -219,11 +242,20 @@ __device__ __forceinline__ void pf_load_kv(__half* Ks, __half* Vs, int p0, int l
                 uint4 u;
                 if (kv_f16) {
                     u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(base) + e);
+                    if (w == 0 && ld) *reinterpret_cast<uint4*>(ld) = make_uint4(0u, 0u, 0u, 0u);  // exact already
                 } else {
                     const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + e);
                     const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + e + 4);
                     u = make_uint4(pack_half2(a.x, a.y), pack_half2(a.z, a.w), pack_half2(b.x, b.y),
                                    pack_half2(b.z, b.w));
+                    if (w == 0 && ld) {
+                        const __half2* h = reinterpret_cast<const __half2*>(&u);
+                        *reinterpret_cast<uint4*>(ld) = make_uint4(
+                            pack_half2(a.x - __low2float(h[0]), a.y - __high2float(h[0])),
+                            pack_half2(a.z - __low2float(h[1]), a.w - __high2float(h[1])),
+                            pack_half2(b.x - __low2float(h[2]), b.y - __high2float(h[2])),
+                            pack_half2(b.z - __low2float(h[3]), b.w - __high2float(h[3])));
+                    }
                 }
                 *reinterpret_cast<uint4*>(w == 0 ? kd : vd) = u;
             }
@@ -232,21 +264,28 @@ __device__ __forceinline__ void pf_load_kv(__half* Ks, __half* Vs, int p0, int l
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-template <int HD>
+// SPLIT: the scores use q and k as exact pairs of fp16 halves, S = Qhi Khi +
+// Qlo Khi + Qhi Klo (fp32 accumulation), so they carry near-fp32 precision
+// into a peaked softmax; Klo is read only for fp32 caches (kl16 / klo on),
+// since an fp16 cache holds its keys exactly.  Shared memory holds Q (and
+// Qlo), two K, two V (and two Klo) blocks.
+template <int HD, bool SPLIT>
 __global__ void __launch_bounds__(kPfThreads)
     attn_prefill_kernel(const float* __restrict__ q, int q_stride, const void* __restrict__ kcache,
                         const void* __restrict__ vcache, int kv_f16, int64_t cache_off, int kvdim,
                         int n_heads, int n_kv, int M, int pos0, float scale_log2,
                         const __half* __restrict__ kh16, const __half* __restrict__ vh16,
-                        __half* __restrict__ out, int out_stride) {
+                        __half* __restrict__ out, int out_stride, const __half* __restrict__ kl16, int klo) {
     constexpr int RS = HD + 8;  // halves per shared row (16-byte pad: conflict-free ldmatrix)
     constexpr int NT = HD / 8;  // 8-wide column tiles of the output
     constexpr int KS = HD / 16; // k-steps of Q K^T
+    constexpr int QR = SPLIT ? 2 * kPfQ : kPfQ;  // rows of Q (and Qlo)
     extern __shared__ __align__(16) uint8_t pf_smem[];
     __half* Qs = reinterpret_cast<__half*>(pf_smem);
-    // K buffers at rows kPfQ + {0, kPfK}, V buffers at kPfQ + 2 kPfK + {0, kPfK}
-    auto Kb = [&](int i) { return Qs + (kPfQ + i * kPfK) * RS; };
-    auto Vb = [&](int i) { return Qs + (kPfQ + (2 + i) * kPfK) * RS; };
+    __half* Qls = Qs + kPfQ * RS;
+    auto Kb = [&](int i) { return Qs + (QR + i * kPfK) * RS; };
+    auto Vb = [&](int i) { return Qs + (QR + (2 + i) * kPfK) * RS; };
+    auto KLb = [&](int i) { return (SPLIT && klo) ? Qs + (QR + (4 + i) * kPfK) * RS : (__half*)nullptr; };
     const int qb = gridDim.x - 1 - blockIdx.x, h = blockIdx.y;
     const int kh = h / (n_heads / n_kv);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -255,8 +294,9 @@ __global__ void __launch_bounds__(kPfThreads)
     const int last = pos0 + min(t0 + kPfQ, M) - 1;  // the block's last query position
     const int nkb = last / kPfK + 1;
 
-    pf_load_kv<HD>(Kb(0), Vb(0), 0, last, pos0, kh, kcache, vcache, kv_f16, cache_off, kvdim, kh16, vh16);
-    // queries -> fp16
+    pf_load_kv<HD>(Kb(0), Vb(0), KLb(0), 0, last, pos0, kh, kcache, vcache, kv_f16, cache_off, kvdim, kh16, vh16,
+                   kl16);
+    // queries -> fp16 (and their residuals)
     constexpr int C4 = HD / 4;
     for (int i = tid; i < kPfQ * C4; i += kPfThreads) {
         const int r = i / C4, c = i % C4;
@@ -266,14 +306,22 @@ __global__ void __launch_bounds__(kPfThreads)
         o.x = pack_half2(v.x, v.y);
         o.y = pack_half2(v.z, v.w);
         *reinterpret_cast<uint2*>(Qs + r * RS + 4 * c) = o;
+        if (SPLIT) {
+            const __half2 a = *reinterpret_cast<const __half2*>(&o.x), b = *reinterpret_cast<const __half2*>(&o.y);
+            *reinterpret_cast<uint2*>(Qls + r * RS + 4 * c) =
+                make_uint2(pack_half2(v.x - __low2float(a), v.y - __high2float(a)),
+                           pack_half2(v.z - __low2float(b), v.w - __high2float(b)));
+        }
     }
     __syncthreads();
-    uint32_t qf[KS][4];
+    uint32_t qf[KS][4], qlf[SPLIT ? KS : 1][4];
     {
         const int r = 16 * warp + (lane & 7) + 8 * ((lane >> 3) & 1);
 #pragma unroll
-        for (int ks = 0; ks < KS; ks++)
+        for (int ks = 0; ks < KS; ks++) {
             ldsm_x4(smem_u32(Qs + r * RS + 16 * ks + 8 * (lane >> 4)), qf[ks]);
+            if (SPLIT) ldsm_x4(smem_u32(Qls + r * RS + 16 * ks + 8 * (lane >> 4)), qlf[SPLIT ? ks : 0]);
+        }
     }
 
     float o[NT][4];
@@ -286,10 +334,11 @@ __global__ void __launch_bounds__(kPfThreads)
         const int p0 = kb * kPfK;
         __half* Ks = Kb(kb & 1);
         __half* Vs = Vb(kb & 1);
+        __half* KLs = KLb(kb & 1);
         if (kb + 1 < nkb) {
             // the other buffer was last read in block kb - 1 (barrier at its end)
-            pf_load_kv<HD>(Kb((kb + 1) & 1), Vb((kb + 1) & 1), p0 + kPfK, last, pos0, kh, kcache, vcache, kv_f16,
-                           cache_off, kvdim, kh16, vh16);
+            pf_load_kv<HD>(Kb((kb + 1) & 1), Vb((kb + 1) & 1), KLb((kb + 1) & 1), p0 + kPfK, last, pos0, kh, kcache,
+                           vcache, kv_f16, cache_off, kvdim, kh16, vh16, kl16);
             asm volatile("cp.async.wait_group 1;" ::: "memory");
         } else {
             asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -306,10 +355,22 @@ __global__ void __launch_bounds__(kPfThreads)
             for (int jp = 0; jp < 4; jp++) {  // two 8-key tiles per ldmatrix.x4
                 uint32_t b[4];
                 const int key = 16 * jp + (lane & 7) + 8 * (lane >> 4);
-                ldsm_x4(smem_u32(Ks + key * RS + 16 * ks + 8 * ((lane >> 3) & 1)), b);
+                const int koff = key * RS + 16 * ks + 8 * ((lane >> 3) & 1);
+                ldsm_x4(smem_u32(Ks + koff), b);
                 const uint32_t b0[2] = {b[0], b[1]}, b1[2] = {b[2], b[3]};
                 mma_16816(s[2 * jp], qf[ks], b0, s[2 * jp]);
                 mma_16816(s[2 * jp + 1], qf[ks], b1, s[2 * jp + 1]);
+                if (SPLIT) {
+                    mma_16816(s[2 * jp], qlf[SPLIT ? ks : 0], b0, s[2 * jp]);
+                    mma_16816(s[2 * jp + 1], qlf[SPLIT ? ks : 0], b1, s[2 * jp + 1]);
+                    if (KLs) {
+                        uint32_t bl[4];
+                        ldsm_x4(smem_u32(KLs + koff), bl);
+                        const uint32_t l0[2] = {bl[0], bl[1]}, l1[2] = {bl[2], bl[3]};
+                        mma_16816(s[2 * jp], qf[ks], l0, s[2 * jp]);
+                        mma_16816(s[2 * jp + 1], qf[ks], l1, s[2 * jp + 1]);
+                    }
+                }
             }
         }
         // scale (log2 domain), causal mask, online softmax
@@ -397,9 +458,9 @@ __global__ void __launch_bounds__(kPfThreads)
 // ---- host side ------------------------------------------------------------------
 
 int prefill_norm(cudaStream_t st, const float* x, const float* w, __half* y, float* inv, int n, int M,
-                 float eps) {
+                 float eps, __half* ylo) {
     CN_CHECK(n % 4 == 0 && M >= 1, CN_ERR_INVALID_ARG, "prefill norm: shapes");
-    CN_CUDA(launch_k(false, norm_half_kernel, dim3(M), dim3(256), 0, st, x, w, y, inv, n, eps));
+    CN_CUDA(launch_k(false, norm_half_kernel, dim3(M), dim3(256), 0, st, x, w, y, inv, n, eps, ylo));
     return CN_OK;
 }
 
@@ -417,25 +478,30 @@ int to_half_rows(cudaStream_t st, const float* x, __half* y, float* inv, int n, 
 
 int prefill_rope(cudaStream_t st, float* q, const float* k, const float* v, const float2* rope, int pos0, int M,
                  int qdim, int kvdim, int hd, void* kcache, void* vcache, int64_t cache_off, bool kv_f16, __half* kh,
-                 __half* vh) {
+                 __half* vh, __half* kl) {
     CN_CHECK(hd % 4 == 0 && qdim % 4 == 0 && kvdim % 4 == 0, CN_ERR_INVALID_ARG, "prefill rope: shapes");
     CN_CUDA(launch_k(false, rope_prefill_kernel, dim3(M), dim3(256), 0, st, q, k, v, rope, pos0, qdim, kvdim, hd,
-                     kcache, vcache, cache_off, kv_f16 ? 1 : 0, kh, vh));
+                     kcache, vcache, cache_off, kv_f16 ? 1 : 0, kh, vh, kl));
     return CN_OK;
+}
+
+// Shared memory of attn_prefill_kernel: Q [+ Qlo], 2 K, 2 V [+ 2 Klo] blocks.
+static size_t attn_smem(int hd, bool split, bool klo) {
+    const int rows = kPfQ * (split ? 2 : 1) + kPfK * (4 + (split && klo ? 2 : 0));
+    return (size_t)rows * (hd + 8) * sizeof(__half);
 }
 
 int prefill_attention(cudaStream_t st, const float* q, int q_stride, const void* kcache,
                       const void* vcache, bool kv_f16, int64_t cache_off, int n_heads, int n_kv,
-                      int hd, int M, int pos0, const __half* kh, const __half* vh, __half* out, int out_stride) {
+                      int hd, int M, int pos0, const __half* kh, const __half* vh, __half* out, int out_stride,
+                      bool split, const __half* kl) {
     CN_CHECK(hd == 64 || hd == 128, CN_ERR_UNSUPPORTED, "prefill attention: head_dim %d", hd);
     CN_CHECK(n_kv > 0 && n_heads % n_kv == 0 && M >= 1 && pos0 >= 0, CN_ERR_INVALID_ARG,
              "prefill attention: bad arguments");
     CN_CHECK(q_stride % 4 == 0 && out_stride % 2 == 0, CN_ERR_INVALID_ARG, "prefill attention: strides");
-    const int RS = hd + 8;
-    const size_t smem = (size_t)(kPfQ + 4 * kPfK) * RS * sizeof(__half);
-    const float scale_log2 = 1.4426950408889634f / sqrtf((float)hd);
-    const dim3 grid((M + kPfQ - 1) / kPfQ, n_heads);
-    const int kvdim = n_kv * hd;
+    CN_CHECK(!split || kv_f16 || kl, CN_ERR_INVALID_ARG, "prefill attention: split scores on an fp32 cache need k's residuals");
+    const bool klo = split && !kv_f16;
+    const size_t smem = attn_smem(hd, split, klo);
     {
         int dev = 0;
         CN_CUDA(cudaGetDevice(&dev));
@@ -443,22 +509,29 @@ int prefill_attention(cudaStream_t st, const float* q, int q_stride, const void*
         static bool attr[64] = {false};
         std::lock_guard<std::mutex> lock(mu);
         if (!attr[dev & 63]) {
-            // the larger (head_dim 128) request covers both instantiations
-            const int big = (kPfQ + 4 * kPfK) * (128 + 8) * (int)sizeof(__half);
-            CN_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
-            CN_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+            // the largest layout of each instantiation
+            const int f128 = (int)attn_smem(128, false, false), s128 = (int)attn_smem(128, true, true);
+            const int f64 = (int)attn_smem(64, false, false), s64 = (int)attn_smem(64, true, true);
+            CN_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, f128));
+            CN_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, s128));
+            CN_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, f64));
+            CN_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, s64));
             attr[dev & 63] = true;
         }
     }
+    const float scale_log2 = 1.4426950408889634f / sqrtf((float)hd);
+    const dim3 grid((M + kPfQ - 1) / kPfQ, n_heads);
+    const int kvdim = n_kv * hd;
+    const int kf = kv_f16 ? 1 : 0, klo_i = klo ? 1 : 0;
+#define CN_PF_ATTN(HD, S)                                                                                          \
+    CN_CUDA(launch_k(false, attn_prefill_kernel<HD, S>, grid, dim3(kPfThreads), smem, st, q, q_stride, kcache, vcache, \
+                     kf, cache_off, kvdim, n_heads, n_kv, M, pos0, scale_log2, kh, vh, out, out_stride, kl, klo_i));
     if (hd == 128) {
-        CN_CUDA(launch_k(false, attn_prefill_kernel<128>, grid, dim3(kPfThreads), smem, st, q, q_stride,
-                         kcache, vcache, kv_f16 ? 1 : 0, cache_off, kvdim, n_heads, n_kv, M, pos0,
-                         scale_log2, kh, vh, out, out_stride));
+        if (split) { CN_PF_ATTN(128, true) } else { CN_PF_ATTN(128, false) }
     } else {
-        CN_CUDA(launch_k(false, attn_prefill_kernel<64>, grid, dim3(kPfThreads), smem, st, q, q_stride,
-                         kcache, vcache, kv_f16 ? 1 : 0, cache_off, kvdim, n_heads, n_kv, M, pos0,
-                         scale_log2, kh, vh, out, out_stride));
+        if (split) { CN_PF_ATTN(64, true) } else { CN_PF_ATTN(64, false) }
     }
+#undef CN_PF_ATTN
     return CN_OK;
 }
 

@@ -156,9 +156,14 @@ class CudaLlamaModel:
               "cn_llama_set_inputs")
 
     def set_prefill(self, min_tokens: int) -> None:
-        """Prompts of min_tokens (>= 16) or more take the prefill pass in
-        forward(); 0 (the default) keeps the reference's token-by-token loop."""
+        """Prompts of min_tokens (>= 16; 16 by default) or more take the prefill
+        pass in forward(); 0 keeps the reference's token-by-token loop."""
         check(N.lib().cn_llama_set_prefill(self.handle, int(min_tokens)), "cn_llama_set_prefill")
+
+    def set_prefill_precision(self, split: int) -> None:
+        """1 (default): q/k projections and attention scores on split (hi + lo
+        fp16) operands; 0: every prefill operand rounded to fp16 once."""
+        check(N.lib().cn_llama_set_prefill_precision(self.handle, int(split)), "cn_llama_set_prefill_precision")
 
     def step(self, batch: int) -> None:
         """Enqueue one decode step on the device inputs (no host copies, no wait)."""

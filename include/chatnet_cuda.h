@@ -257,21 +257,30 @@ int cn_llama_destroy(cn_llama* m);
 
 /* IModel.Forward (Abstractions/IModel.cs:18, LlamaModel.cs:93-238): runs the
  * n tokens of KV slot 0 at positions pos..pos+n-1 and writes the logits of
- * the last one to logits_host [vocab].  The tokens run one decode step at a
- * time, as the reference does (InferenceEngine.cs:235-239), unless
- * cn_llama_set_prefill turned the prefill pass on. */
+ * the last one to logits_host [vocab].  A prompt of 16 or more tokens (the
+ * threshold cn_llama_set_prefill sets) runs as one prefill pass when the
+ * model supports it (cn_llama_prefill_hidden_dev); shorter ones, and models
+ * the pass cannot run, take one decode step per token as the reference does
+ * (InferenceEngine.cs:235-239). */
 int cn_llama_forward(cn_llama* m, const int* tokens, int n, int pos, float* logits_host);
 
-/* Prompts of min_tokens (>= 16) or more tokens in cn_llama_forward then run as
- * one prefill pass on a one-GPU model whose projections are Q4_0, Q4_K or
- * Q6_K with 16-byte rows (every layer on the tcgen05 matmul for all n tokens,
- * see cn_llama_prefill_hidden_dev); 0 turns it off (the default).  The
- * prefill pass rounds activations and weights to fp16 for the tensor cores:
- * hidden states agree with the sequential steps to about 1e-3 on the
- * benchmark's configs, but rounding shared by a whole q/k projection can be
- * amplified by a peaked softmax to ~1e-2 on other weights.  (no reference
+/* Prompts of min_tokens (>= 16; 16 by default) or more tokens in
+ * cn_llama_forward run as one prefill pass on a one-GPU model whose
+ * projections are Q4_0, Q4_K or Q6_K with 16-byte rows (every layer on the
+ * tcgen05 matmul for all n tokens, see cn_llama_prefill_hidden_dev); 0 turns
+ * it off, so every prompt token runs as a decode step.  (no reference
  * counterpart: the reference has only the sequential loop) */
 int cn_llama_set_prefill(cn_llama* m, int min_tokens);
+
+/* Precision of the prefill pass.  1 (the default): the q and k projections
+ * carry weights and activations as exact pairs of fp16 halves (three MMAs per
+ * k-step) and the attention scores use q and k the same way, so the rounding
+ * a whole projection shares cannot be magnified by a peaked softmax; hidden
+ * states then agree with the sequential steps to within 1e-3 also at trained
+ * weight magnitudes.  0: every operand rounded to fp16 once (faster; about
+ * 5e-4 on the benchmark's synthetic configs, but up to ~1e-2 where a peaked
+ * softmax magnifies the shared rounding).  (no reference counterpart) */
+int cn_llama_set_prefill_precision(cn_llama* m, int split);
 
 /* Prefill on device buffers: runs the hidden states x_dev [n][dim] (fp32)
  * through every layer at once, for positions pos..pos+n-1 of KV slot 0 (whose
