@@ -792,6 +792,113 @@ __global__ void __launch_bounds__(kNormThreads)
     }
 }
 
+// The same fused residual add + RmsNorm + prep as one thread-block cluster
+// of up to kNormCluster CTAs per batch row: CTA r of a row owns a contiguous
+// range of the row's 256-position units, reads only its slice of x, of the
+// delta and (tensor parallel) of every rank's exchange slots, and keeps the
+// summed values in shared memory.  The CTAs' partial sums of squares are
+// added through distributed shared memory (in CTA order, so every CTA and
+// every rank gets the same rms), then each CTA writes its slice and its
+// units' records.  Compared with add_norm_prep_kernel, which has every CTA
+// read the whole row (under tensor parallelism every rank's whole row), the
+// row is read once.
+constexpr int kNormCluster = 8;
+constexpr int kNormClThreads = 256;
+constexpr int kNormClMaxVals = 4096;  // values a CTA holds: rows up to 8 x 4096 = 32768
+
+__global__ void __launch_bounds__(kNormClThreads)
+    add_norm_prep_cl_kernel(const float* __restrict__ x_in, const float* __restrict__ delta,
+                            float* __restrict__ x_out, const float* __restrict__ w, float* __restrict__ y,
+                            int n, float eps, PrepTarget pt, XchgIn xi) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ __align__(16) float vals[kNormClMaxVals];
+    __shared__ float red[kNormClThreads / 32];
+    __shared__ float s_part;
+    __shared__ uint32_t s_seq;
+    const int C = (int)cluster_size(), r = (int)cluster_rank();
+    const int b = blockIdx.y, tid = threadIdx.x;
+    const int units = n / 256;
+    const int u0 = units * r / C, u1 = units * (r + 1) / C;
+    const int i0 = u0 * 256, i1 = u1 * 256;
+    const float* xr = x_in + (size_t)b * n;
+    const float* dr = delta ? delta + (size_t)b * n : nullptr;
+    const float* xbase = nullptr;
+    const uint64_t* llbase = nullptr;
+    uint32_t seq = 0;
+    const uint64_t t0 = globaltimer_ns();
+    if (xi.size > 1) {
+        if (xi.ll) {
+            seq = *xi.seq_base * xi.uses + xi.seq_add;
+            llbase = reinterpret_cast<const uint64_t*>(xi.src) + (seq & 1u) * xi.parity_stride + (size_t)b * n;
+        } else {
+            if (tid == 0) s_seq = xchg_wait_dev(xi);
+            __syncthreads();
+            xbase = xi.src + (s_seq & 1u) * xi.parity_stride + (size_t)b * n;
+        }
+        dr = nullptr;
+    }
+    const bool add = dr || xbase || llbase;
+    float ss = 0.f;
+    for (int i = i0 + 4 * tid; i < i1; i += 4 * kNormClThreads) {
+        float4 v = *reinterpret_cast<const float4*>(xr + i);
+        if (add) {
+            const float4 d = llbase  ? ll_sum4(xi, llbase, i, seq, t0)
+                             : xbase ? xchg_sum4(xi, xbase, i)
+                                     : *reinterpret_cast<const float4*>(dr + i);
+            v.x = __fadd_rn(v.x, d.x);
+            v.y = __fadd_rn(v.y, d.y);
+            v.z = __fadd_rn(v.z, d.z);
+            v.w = __fadd_rn(v.w, d.w);
+            *reinterpret_cast<float4*>(x_out + (size_t)b * n + i) = v;
+        }
+        *reinterpret_cast<float4*>(vals + (i - i0)) = v;
+        ss = fmaf(v.x, v.x, ss);
+        ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss);
+        ss = fmaf(v.w, v.w, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    if (tid == 0) {
+        float t = 0.f;
+#pragma unroll
+        for (int i = 0; i < kNormClThreads / 32; i++) t += red[i];
+        s_part = t;
+    }
+    cluster_arrive();  // s_part (and this CTA's values) are ready
+    cluster_wait();
+    float tot = 0.f;
+    for (int c = 0; c < C; c++) tot += ld_peer_f32(&s_part, (uint32_t)c);
+    cluster_arrive();  // done reading the peers' s_part (matched by the wait before exit)
+    const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), eps)));
+    for (int i = i0 + 4 * tid; i < i1; i += 4 * kNormClThreads) {
+        float4 v = *reinterpret_cast<const float4*>(vals + (i - i0));
+        const float4 g = *reinterpret_cast<const float4*>(w + i);
+        v.x = __fmul_rn(__fmul_rn(v.x, rms), g.x);
+        v.y = __fmul_rn(__fmul_rn(v.y, rms), g.y);
+        v.z = __fmul_rn(__fmul_rn(v.z, rms), g.z);
+        v.w = __fmul_rn(__fmul_rn(v.w, rms), g.w);
+        *reinterpret_cast<float4*>(y + (size_t)b * n + i) = v;
+        *reinterpret_cast<float4*>(vals + (i - i0)) = v;
+    }
+    if (pt.kind >= 0) {
+        __syncthreads();
+        const int lane = tid & 31;
+        for (int u = u0 + (tid >> 5); u < u1; u += kNormClThreads / 32) {
+            const int c = lane >> 2, t = lane & 3;
+            const float* vu = vals + (u - u0) * 256;
+            const float4 a0 = *reinterpret_cast<const float4*>(vu + 32 * c + 4 * t);
+            const float4 a1 = *reinterpret_cast<const float4*>(vu + 32 * c + 16 + 4 * t);
+            const float v8[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            emit_any(pt, v8, u, b, (int)gridDim.y, lane);
+        }
+    }
+    cluster_wait();  // no CTA leaves while a peer may still read its s_part
+}
+
 // ---- generic (untiled) fallback -------------------------------------------------
 //
 // For shapes the TMA path cannot tile (row bytes not a multiple of 16, or K
@@ -1132,8 +1239,15 @@ int add_norm_prep(cudaStream_t st, const float* x_in, const float* delta, float*
     if (pt.kind >= 0 && n % 256 != 0) pt.kind = -1;  // the GEMV preps for itself
     XchgIn xi;
     if (xch) xi = *xin;
-    CN_CUDA(launch_k(true, add_norm_prep_kernel, dim3((n + 255) / 256, rows), dim3(kNormThreads), 0, st, x_in,
-                     delta, x_out, w, y, n, eps, pt, xi));
+    const int units = n / 256;
+    if (n % 256 == 0 && units >= 1 && (units + kNormCluster - 1) / kNormCluster * 256 <= kNormClMaxVals) {
+        const int C = units < kNormCluster ? units : kNormCluster;
+        CN_CUDA(launch_cluster_k(true, C, add_norm_prep_cl_kernel, dim3(C, rows), dim3(kNormClThreads), 0, st,
+                                 x_in, delta, x_out, w, y, n, eps, pt, xi));
+    } else {
+        CN_CUDA(launch_k(true, add_norm_prep_kernel, dim3((n + 255) / 256, rows), dim3(kNormThreads), 0, st, x_in,
+                         delta, x_out, w, y, n, eps, pt, xi));
+    }
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }

@@ -72,11 +72,15 @@ struct cn_llama {
     // operand of the next matmul, fp16 copies of the new k/v rows, token ids
     int pf_cap = 0;
     int prefill_min = cn::kPrefillMin;  // cn_llama_forward's prefill threshold (0: sequential steps)
-    // 1: the q/k projections and the attention scores run on split (hi + lo
-    // fp16) operands, 0: every operand rounded to fp16 (cn_llama_set_prefill_precision)
-    int prefill_split = 1;
-    std::vector<float> pf_ws;  // split scales of each layer's q and k weights ([2 * layers]; empty: not yet computed)
-    __half *pf_hl = nullptr, *pf_kl = nullptr;  // low halves of the normalised input / of k
+    // cn_llama_set_prefill_precision: 0 every prefill operand rounded to fp16
+    // once; 1 the attention path (q/k/v and O projections, and the attention's
+    // operands) on split (hi + lo fp16) operands; 2 (the default) every
+    // projection split as well
+    int prefill_split = 2;
+    std::vector<float> pf_ws;  // split scales, [layer * 9 + slot] (projection slots; empty: not yet computed)
+    // low halves: of the current matmul input rows, and of the new k and v
+    // rows (fp32 caches)
+    __half *pf_hl = nullptr, *pf_kl = nullptr, *pf_vl = nullptr;
     float *pf_x = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_g = nullptr,
           *pf_u = nullptr;
     __half *pf_h = nullptr, *pf_kh = nullptr, *pf_vh = nullptr;
@@ -436,7 +440,7 @@ static void free_model(cn_llama* m) {
                     m->gate, m->up, m->logits, m->part, m->tokens, m->pos, m->amax,
                     m->gb.xfrag, m->gb.xsum, m->gb.partials, m->gb.counters, m->gb.xinv,
                     m->pf_x, m->pf_q, m->pf_k, m->pf_v, m->pf_g, m->pf_u, m->pf_h, m->pf_kh, m->pf_vh,
-                    m->pf_tok, m->pf_xs, m->pf_hl, m->pf_kl};
+                    m->pf_tok, m->pf_xs, m->pf_hl, m->pf_kl, m->pf_vl};
     for (void* p : bufs) cudaFree(p);
     cudaFreeHost(m->h_tokens);
     cudaFreeHost(m->h_pos);
@@ -470,11 +474,11 @@ static bool prefill_supported(const cn_llama* m) {
 // are m->pf_xs when `scaled`: one matmul launch per run of matrices of the
 // same weight type (a single launch when the group's types agree).  The first
 // `nsplit` matrices run the split variant (low halves of the rows in
-// m->pf_hl, weight scales ws[0..nsplit)), the rest the fp16 one.  With
+// m->pf_hl, weight scales m->pf_ws), the rest the fp16 one.  With
 // count_only, returns the number of launches instead.
 static int mm_group(cn_llama* m, int l, int nmat, const int* slots, const int64_t* rows, int64_t K, int n,
                     float* const* y, const int64_t* ldy, bool accumulate, bool scaled, bool count_only = false,
-                    int nsplit = 0, const float* ws = nullptr) {
+                    int nsplit = 0) {
     int launches = 0;
     for (int i = 0; i < nmat;) {
         const int type = LT(m, l, slots[i])->type;
@@ -485,13 +489,15 @@ static int mm_group(cn_llama* m, int l, int nmat, const int* slots, const int64_
         if (!count_only) {
             const void* w[3];
             const CUtensorMap* wm[3];
+            float ws[3] = {1.f, 1.f, 1.f};
             for (int k = i; k < j; k++) {
                 w[k - i] = LT(m, l, slots[k])->d;
                 wm[k - i] = wmap(LT(m, l, slots[k]));
+                if (split) ws[k - i] = m->pf_ws[(size_t)l * 9 + slots[k]];
             }
             int rc = matmul_quant(m->ctx->stream, m->ctx->dev_err, type, j - i, w, wm, rows + i, K, m->pf_h,
                                   scaled ? m->pf_xs : nullptr, n, y + i, ldy + i, accumulate,
-                                  split ? m->pf_hl : nullptr, split ? ws + i : nullptr);
+                                  split ? m->pf_hl : nullptr, split ? ws : nullptr);
             if (rc) return rc;
         }
         i = j;
@@ -502,30 +508,39 @@ static int mm_group(cn_llama* m, int l, int nmat, const int* slots, const int64_
 static const int kSlotsQKV[3] = {L_Q, L_K, L_V}, kSlotsO[1] = {L_O}, kSlotsGU[2] = {L_GATE, L_UP},
                  kSlotsDown[1] = {L_DOWN};
 
-// Each q/k weight matrix's split-variant expansion scale, computed once
-// (synchronises the stream).
+// Every projection's split-variant expansion scale, computed once
+// (synchronises the stream; cached in the tensors as well).
 static int prefill_scales(cn_llama* m) {
     if (!m->pf_ws.empty()) return CN_OK;
     const int L = m->cfg.n_layers;
-    std::vector<float> ws(2 * (size_t)L);
+    std::vector<float> ws(9 * (size_t)L, 1.f);
     for (int l = 0; l < L; l++)
-        for (int j = 0; j < 2; j++) {
-            int rc = matmul_split_scale(const_cast<cn_tensor*>(LT(m, l, j == 0 ? L_Q : L_K)), m->ctx->stream,
-                                        &ws[2 * (size_t)l + j]);
+        for (int j : {L_Q, L_K, L_V, L_O, L_GATE, L_UP, L_DOWN}) {
+            int rc = matmul_split_scale(const_cast<cn_tensor*>(LT(m, l, j)), m->ctx->stream, &ws[9 * (size_t)l + j]);
             if (rc) return rc;
         }
     m->pf_ws.swap(ws);
     return CN_OK;
 }
 
+// Matrices of each projection group that run the split variant at the
+// model's prefill precision: {q/k/v, o, gate/up, down}.
+static void split_counts(const cn_llama* m, int (&ns)[4]) {
+    const int p = m->prefill_split;
+    ns[0] = p >= 1 ? 3 : 0;
+    ns[1] = p >= 1 ? 1 : 0;
+    ns[2] = p >= 2 ? 2 : 0;
+    ns[3] = p >= 2 ? 1 : 0;
+}
+
 static int prefill_reserve(cn_llama* m, int n) {
     if (n <= m->pf_cap) return CN_OK;
     CN_CUDA(cudaStreamSynchronize(m->ctx->stream));
     void* old[] = {m->pf_x, m->pf_q, m->pf_k, m->pf_v, m->pf_g, m->pf_u, m->pf_h, m->pf_kh, m->pf_vh,
-                   m->pf_tok, m->pf_xs, m->pf_hl, m->pf_kl};
+                   m->pf_tok, m->pf_xs, m->pf_hl, m->pf_kl, m->pf_vl};
     for (void* p : old) cudaFree(p);
     m->pf_x = m->pf_q = m->pf_k = m->pf_v = m->pf_g = m->pf_u = nullptr;
-    m->pf_h = m->pf_kh = m->pf_vh = m->pf_hl = m->pf_kl = nullptr;
+    m->pf_h = m->pf_kh = m->pf_vh = m->pf_hl = m->pf_kl = m->pf_vl = nullptr;
     m->pf_tok = nullptr;
     m->pf_xs = nullptr;
     m->pf_cap = 0;
@@ -544,8 +559,9 @@ static int prefill_reserve(cn_llama* m, int n) {
         (rc = dmalloc((void**)&m->pf_vh, N * m->kvdim * 2, false)) ||
         (rc = dmalloc((void**)&m->pf_tok, N * 4, false)) ||
         (rc = dmalloc((void**)&m->pf_xs, N * 4, false)) ||
-        (rc = dmalloc((void**)&m->pf_hl, N * c.dim * 2, false)) ||
-        (rc = dmalloc((void**)&m->pf_kl, N * m->kvdim * 2, false)))
+        (rc = dmalloc((void**)&m->pf_hl, N * hmax * 2, false)) ||
+        (rc = dmalloc((void**)&m->pf_kl, N * m->kvdim * 2, false)) ||
+        (rc = dmalloc((void**)&m->pf_vl, N * m->kvdim * 2, false)))
         return rc;
     m->pf_cap = n;
     return CN_OK;
@@ -562,44 +578,49 @@ static int prefill_layers(cn_llama* m, int n, int pos) {
     const cn_llama_config& c = m->cfg;
     cudaStream_t s = m->ctx->stream;
     const int qd = m->qdim, kvd = m->kvdim, hid = c.hidden_dim;
-    const bool split = m->prefill_split != 0, kv16 = c.kv_dtype == CN_KV_F16;
+    const bool kv16 = c.kv_dtype == CN_KV_F16;
+    int ns[4];
+    split_counts(m, ns);
+    const bool attn_split = ns[0] > 0, ffn_split = ns[2] > 0;
+    __half* kl = attn_split && !kv16 ? m->pf_kl : nullptr;
+    __half* vl = attn_split && !kv16 ? m->pf_vl : nullptr;
     int rc;
-    if (split && (rc = prefill_scales(m))) return rc;
+    if ((attn_split || ffn_split) && (rc = prefill_scales(m))) return rc;
     for (int l = 0; l < c.n_layers; l++) {
         const int64_t cache_off = (int64_t)l * c.ctx_len * kvd;  // sequence slot 0
         if ((rc = prefill_norm(s, m->pf_x, (const float*)LT(m, l, L_ANORM)->d, m->pf_h, m->pf_xs, c.dim, n,
-                               c.rms_eps, split ? m->pf_hl : nullptr)))
+                               c.rms_eps, attn_split ? m->pf_hl : nullptr)))
             return rc;
         {
-            // q and k feed the softmax, which magnifies their errors: split operands
             const int64_t rows[3] = {qd, kvd, kvd};
             float* y[3] = {m->pf_q, m->pf_k, m->pf_v};
-            if ((rc = mm_group(m, l, 3, kSlotsQKV, rows, c.dim, n, y, rows, false, true, false, split ? 2 : 0,
-                               split ? &m->pf_ws[2 * (size_t)l] : nullptr)))
-                return rc;
+            if ((rc = mm_group(m, l, 3, kSlotsQKV, rows, c.dim, n, y, rows, false, true, false, ns[0]))) return rc;
         }
         if ((rc = prefill_rope(s, m->pf_q, m->pf_k, m->pf_v, m->rope, pos, n, qd, kvd, c.head_dim, m->kc, m->vc,
-                               cache_off, kv16, m->pf_kh, m->pf_vh, split && !kv16 ? m->pf_kl : nullptr)))
+                               cache_off, kv16, m->pf_kh, m->pf_vh, kl, vl)))
             return rc;
         if ((rc = prefill_attention(s, m->pf_q, qd, m->kc, m->vc, kv16, cache_off, m->nh, m->nkv, c.head_dim, n,
-                                    pos, m->pf_kh, m->pf_vh, m->pf_h, qd, split, split && !kv16 ? m->pf_kl : nullptr)))
+                                    pos, m->pf_kh, m->pf_vh, m->pf_h, qd, attn_split, kl, vl,
+                                    attn_split ? m->pf_hl : nullptr)))
             return rc;
         {
             const int64_t rows = c.dim;
-            if ((rc = mm_group(m, l, 1, kSlotsO, &rows, qd, n, &m->pf_x, &rows, true, false))) return rc;
+            if ((rc = mm_group(m, l, 1, kSlotsO, &rows, qd, n, &m->pf_x, &rows, true, false, false, ns[1]))) return rc;
         }
         if ((rc = prefill_norm(s, m->pf_x, (const float*)LT(m, l, L_FNORM)->d, m->pf_h, m->pf_xs, c.dim, n,
-                               c.rms_eps)))
+                               c.rms_eps, ffn_split ? m->pf_hl : nullptr)))
             return rc;
         {
             const int64_t rows[2] = {hid, hid};
             float* y[2] = {m->pf_g, m->pf_u};
-            if ((rc = mm_group(m, l, 2, kSlotsGU, rows, c.dim, n, y, rows, false, true))) return rc;
+            if ((rc = mm_group(m, l, 2, kSlotsGU, rows, c.dim, n, y, rows, false, true, false, ns[2]))) return rc;
         }
-        if ((rc = prefill_silu(s, m->pf_g, m->pf_u, m->pf_h, m->pf_xs, hid, n))) return rc;
+        if ((rc = prefill_silu(s, m->pf_g, m->pf_u, m->pf_h, m->pf_xs, hid, n, ffn_split ? m->pf_hl : nullptr)))
+            return rc;
         {
             const int64_t rows = c.dim;
-            if ((rc = mm_group(m, l, 1, kSlotsDown, &rows, hid, n, &m->pf_x, &rows, true, true))) return rc;
+            if ((rc = mm_group(m, l, 1, kSlotsDown, &rows, hid, n, &m->pf_x, &rows, true, true, false, ns[3])))
+                return rc;
         }
     }
     return CN_OK;
@@ -612,12 +633,13 @@ static int prefill_kernels(const cn_llama* m) {
     cn_llama* mm = const_cast<cn_llama*>(m);
     const int64_t r[3] = {0, 0, 0};
     float* y[3] = {nullptr, nullptr, nullptr};
-    int k = 0;
+    int k = 0, ns[4];
+    split_counts(m, ns);
     for (int l = 0; l < m->cfg.n_layers; l++)
-        k += 6 + mm_group(mm, l, 3, kSlotsQKV, r, 0, 0, y, r, false, false, true, m->prefill_split ? 2 : 0) +
-             mm_group(mm, l, 1, kSlotsO, r, 0, 0, y, r, false, false, true) +
-             mm_group(mm, l, 2, kSlotsGU, r, 0, 0, y, r, false, false, true) +
-             mm_group(mm, l, 1, kSlotsDown, r, 0, 0, y, r, false, false, true);
+        k += 6 + mm_group(mm, l, 3, kSlotsQKV, r, 0, 0, y, r, false, false, true, ns[0]) +
+             mm_group(mm, l, 1, kSlotsO, r, 0, 0, y, r, false, false, true, ns[1]) +
+             mm_group(mm, l, 2, kSlotsGU, r, 0, 0, y, r, false, false, true, ns[2]) +
+             mm_group(mm, l, 1, kSlotsDown, r, 0, 0, y, r, false, false, true, ns[3]);
     return k;
 }
 
@@ -892,7 +914,7 @@ int cn_llama_set_prefill(cn_llama* m, int min_tokens) {
 
 int cn_llama_set_prefill_precision(cn_llama* m, int split) {
     CN_CHECK(m, CN_ERR_INVALID_ARG, "null model");
-    CN_CHECK(split == 0 || split == 1, CN_ERR_INVALID_ARG, "prefill precision %d: 0 or 1", split);
+    CN_CHECK(split >= 0 && split <= 2, CN_ERR_INVALID_ARG, "prefill precision %d: 0, 1 or 2", split);
     m->prefill_split = split;
     return CN_OK;
 }
@@ -1044,9 +1066,10 @@ int cn_llama_time_matmul(cn_llama* m, int group, int n, int iters, float* us_per
     CN_CUDA(cudaMemsetAsync(m->pf_h, 0, (size_t)n * (hid > dim ? hid : dim) * 2, s));
     CN_CUDA(cudaMemsetAsync(m->pf_x, 0, (size_t)n * dim * 4, s));
     CN_CUDA(cudaMemsetAsync(m->pf_xs, 0, (size_t)n * 4, s));
-    CN_CUDA(cudaMemsetAsync(m->pf_hl, 0, (size_t)n * dim * 2, s));
-    const bool split = m->prefill_split != 0;
-    if (split && (rc = prefill_scales(m))) return rc;
+    CN_CUDA(cudaMemsetAsync(m->pf_hl, 0, (size_t)n * (hid > dim ? hid : dim) * 2, s));
+    int ns[4];
+    split_counts(m, ns);
+    if ((ns[0] || ns[2]) && (rc = prefill_scales(m))) return rc;
     const int L = c.n_layers;
     double flops = 0;
     auto launch = [&](int i) -> int {
@@ -1055,18 +1078,18 @@ int cn_llama_time_matmul(cn_llama* m, int group, int n, int iters, float* us_per
             const int64_t rows[3] = {qd, kvd, kvd};
             float* y[3] = {m->pf_q, m->pf_k, m->pf_v};
             flops = 2.0 * n * (double)(qd + 2 * kvd) * dim;  // algorithmic (the split's extra MMAs not counted)
-            return mm_group(m, l, 3, kSlotsQKV, rows, dim, n, y, rows, false, true, false, split ? 2 : 0,
-                            split ? &m->pf_ws[2 * (size_t)l] : nullptr);
+            return mm_group(m, l, 3, kSlotsQKV, rows, dim, n, y, rows, false, true, false, ns[0]);
         }
         if (group == 2) {
             const int64_t rows[2] = {hid, hid};
             float* y[2] = {m->pf_g, m->pf_u};
             flops = 2.0 * n * (double)(2 * hid) * dim;
-            return mm_group(m, l, 2, kSlotsGU, rows, dim, n, y, rows, false, true);
+            return mm_group(m, l, 2, kSlotsGU, rows, dim, n, y, rows, false, true, false, ns[2]);
         }
         const int64_t rows = dim, K = group == 1 ? qd : hid;
         flops = 2.0 * n * (double)dim * K;
-        return mm_group(m, l, 1, group == 1 ? kSlotsO : kSlotsDown, &rows, K, n, &m->pf_x, &rows, true, group == 3);
+        return mm_group(m, l, 1, group == 1 ? kSlotsO : kSlotsDown, &rows, K, n, &m->pf_x, &rows, true, group == 3,
+                        false, group == 1 ? ns[1] : ns[3]);
     };
     for (int i = 0; i < 3; i++)
         if ((rc = launch(i))) return rc;

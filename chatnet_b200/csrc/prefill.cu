@@ -104,7 +104,7 @@ __device__ __forceinline__ float silu_mul1(float g, float u) {
 // a bound on the row's largest output: silu(g) <= g for g >= 0 and
 // |silu(g)| < 0.2785 for g < 0.  The second pass re-reads g and u (cache hits).
 __global__ void silu_half_kernel(const float* __restrict__ g, const float* __restrict__ u,
-                                 __half* __restrict__ h, float* __restrict__ inv, int n) {
+                                 __half* __restrict__ h, float* __restrict__ inv, int n, __half* __restrict__ hlo) {
     __shared__ float red[32];
     const size_t base = (size_t)blockIdx.x * n;
     const float4* g4 = reinterpret_cast<const float4*>(g + base);
@@ -122,8 +122,16 @@ __global__ void silu_half_kernel(const float* __restrict__ g, const float* __res
     row_pow2_scale(block_absmax(bound, red), sc, iv);
     for (int i = threadIdx.x; i < n4; i += blockDim.x) {
         const float4 a = g4[i], b = u4[i];
-        h2[i] = make_uint2(pack_half2(silu_mul1(a.x, b.x) * sc, silu_mul1(a.y, b.y) * sc),
-                           pack_half2(silu_mul1(a.z, b.z) * sc, silu_mul1(a.w, b.w) * sc));
+        const float f0 = silu_mul1(a.x, b.x) * sc, f1 = silu_mul1(a.y, b.y) * sc;
+        const float f2 = silu_mul1(a.z, b.z) * sc, f3 = silu_mul1(a.w, b.w) * sc;
+        const uint2 o = make_uint2(pack_half2(f0, f1), pack_half2(f2, f3));
+        h2[i] = o;
+        if (hlo) {
+            const __half2 h01 = *reinterpret_cast<const __half2*>(&o.x), h23 = *reinterpret_cast<const __half2*>(&o.y);
+            reinterpret_cast<uint2*>(hlo + base)[i] =
+                make_uint2(pack_half2(f0 - __low2float(h01), f1 - __high2float(h01)),
+                           pack_half2(f2 - __low2float(h23), f3 - __high2float(h23)));
+        }
     }
     if (threadIdx.x == 0) inv[blockIdx.x] = iv;
 }
@@ -157,7 +165,7 @@ __global__ void rope_prefill_kernel(float* __restrict__ q, const float* __restri
                                     const float* __restrict__ v, const float2* __restrict__ rope, int pos0,
                                     int qdim, int kvdim, int hd, void* kcache, void* vcache, int64_t cache_off,
                                     int kv_f16, __half* __restrict__ kh, __half* __restrict__ vh,
-                                    __half* __restrict__ kl) {
+                                    __half* __restrict__ kl, __half* __restrict__ vl) {
     const int t = blockIdx.x, pos = pos0 + t;
     const float4* tab = reinterpret_cast<const float4*>(rope + (size_t)pos * (hd / 2));  // two pairs per float4
     const int hd4 = hd / 4;
@@ -187,11 +195,15 @@ __global__ void rope_prefill_kernel(float* __restrict__ q, const float* __restri
         }
         reinterpret_cast<uint2*>(kh + (size_t)t * kvdim)[i] = kp;
         reinterpret_cast<uint2*>(vh + (size_t)t * kvdim)[i] = vp;
-        if (kl) {  // k's rounding residuals (fp32 caches: the attention splits Q K^T)
+        if (kl) {  // k's and v's rounding residuals (fp32 caches: the attention splits them)
             const __half2 a = *reinterpret_cast<const __half2*>(&kp.x), b = *reinterpret_cast<const __half2*>(&kp.y);
             reinterpret_cast<uint2*>(kl + (size_t)t * kvdim)[i] =
                 make_uint2(pack_half2(kr.x - __low2float(a), kr.y - __high2float(a)),
                            pack_half2(kr.z - __low2float(b), kr.w - __high2float(b)));
+            const __half2 c = *reinterpret_cast<const __half2*>(&vp.x), d = *reinterpret_cast<const __half2*>(&vp.y);
+            reinterpret_cast<uint2*>(vl + (size_t)t * kvdim)[i] =
+                make_uint2(pack_half2(vv.x - __low2float(c), vv.y - __high2float(c)),
+                           pack_half2(vv.z - __low2float(d), vv.w - __high2float(d)));
         }
     }
 }
@@ -215,9 +227,10 @@ __device__ __forceinline__ void pf_cp_async16(uint32_t dst, const void* src) {
 // prompt (>= pos0) from the fp16 copies with cp.async, earlier ones from the
 // cache (converted in registers), positions past `last` as zeros.
 template <int HD>
-__device__ __forceinline__ void pf_load_kv(__half* Ks, __half* Vs, __half* KLs, int p0, int last, int pos0, int kh,
-                                           const void* kcache, const void* vcache, int kv_f16, int64_t cache_off,
-                                           int kvdim, const __half* kh16, const __half* vh16, const __half* kl16) {
+__device__ __forceinline__ void pf_load_kv(__half* Ks, __half* Vs, __half* KLs, __half* VLs, int p0, int last,
+                                           int pos0, int kh, const void* kcache, const void* vcache, int kv_f16,
+                                           int64_t cache_off, int kvdim, const __half* kh16, const __half* vh16,
+                                           const __half* kl16, const __half* vl16) {
     constexpr int RS = HD + 8, C8 = HD / 8;
     for (int i = threadIdx.x; i < kPfK * C8; i += kPfThreads) {
         const int r = i / C8, c = i % C8;
@@ -225,15 +238,18 @@ __device__ __forceinline__ void pf_load_kv(__half* Ks, __half* Vs, __half* KLs, 
         __half* kd = Ks + r * RS + 8 * c;
         __half* vd = Vs + r * RS + 8 * c;
         __half* ld = KLs ? KLs + r * RS + 8 * c : nullptr;
+        __half* lv = VLs ? VLs + r * RS + 8 * c : nullptr;
         if (p > last) {
             *reinterpret_cast<uint4*>(kd) = make_uint4(0u, 0u, 0u, 0u);
             *reinterpret_cast<uint4*>(vd) = make_uint4(0u, 0u, 0u, 0u);
             if (ld) *reinterpret_cast<uint4*>(ld) = make_uint4(0u, 0u, 0u, 0u);
+            if (lv) *reinterpret_cast<uint4*>(lv) = make_uint4(0u, 0u, 0u, 0u);
         } else if (p >= pos0) {
             const size_t e = (size_t)(p - pos0) * kvdim + kh * HD + 8 * c;
             pf_cp_async16(smem_u32(kd), kh16 + e);
             pf_cp_async16(smem_u32(vd), vh16 + e);
             if (ld) pf_cp_async16(smem_u32(ld), kl16 + e);
+            if (lv) pf_cp_async16(smem_u32(lv), vl16 + e);
         } else {
             const int64_t e = cache_off + (int64_t)p * kvdim + kh * HD + 8 * c;
 #pragma unroll
@@ -242,15 +258,17 @@ __device__ __forceinline__ void pf_load_kv(__half* Ks, __half* Vs, __half* KLs, 
                 uint4 u;
                 if (kv_f16) {
                     u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(base) + e);
-                    if (w == 0 && ld) *reinterpret_cast<uint4*>(ld) = make_uint4(0u, 0u, 0u, 0u);  // exact already
+                    __half* lo = w == 0 ? ld : lv;
+                    if (lo) *reinterpret_cast<uint4*>(lo) = make_uint4(0u, 0u, 0u, 0u);  // exact already
                 } else {
                     const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + e);
                     const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + e + 4);
                     u = make_uint4(pack_half2(a.x, a.y), pack_half2(a.z, a.w), pack_half2(b.x, b.y),
                                    pack_half2(b.z, b.w));
-                    if (w == 0 && ld) {
+                    __half* lo = w == 0 ? ld : lv;
+                    if (lo) {
                         const __half2* h = reinterpret_cast<const __half2*>(&u);
-                        *reinterpret_cast<uint4*>(ld) = make_uint4(
+                        *reinterpret_cast<uint4*>(lo) = make_uint4(
                             pack_half2(a.x - __low2float(h[0]), a.y - __high2float(h[0])),
                             pack_half2(a.z - __low2float(h[1]), a.w - __high2float(h[1])),
                             pack_half2(b.x - __low2float(h[2]), b.y - __high2float(h[2])),
@@ -275,7 +293,8 @@ __global__ void __launch_bounds__(kPfThreads)
                         const void* __restrict__ vcache, int kv_f16, int64_t cache_off, int kvdim,
                         int n_heads, int n_kv, int M, int pos0, float scale_log2,
                         const __half* __restrict__ kh16, const __half* __restrict__ vh16,
-                        __half* __restrict__ out, int out_stride, const __half* __restrict__ kl16, int klo) {
+                        __half* __restrict__ out, int out_stride, const __half* __restrict__ kl16,
+                        const __half* __restrict__ vl16, int klo, __half* __restrict__ out_lo) {
     constexpr int RS = HD + 8;  // halves per shared row (16-byte pad: conflict-free ldmatrix)
     constexpr int NT = HD / 8;  // 8-wide column tiles of the output
     constexpr int KS = HD / 16; // k-steps of Q K^T
@@ -286,6 +305,7 @@ __global__ void __launch_bounds__(kPfThreads)
     auto Kb = [&](int i) { return Qs + (QR + i * kPfK) * RS; };
     auto Vb = [&](int i) { return Qs + (QR + (2 + i) * kPfK) * RS; };
     auto KLb = [&](int i) { return (SPLIT && klo) ? Qs + (QR + (4 + i) * kPfK) * RS : (__half*)nullptr; };
+    auto VLb = [&](int i) { return (SPLIT && klo) ? Qs + (QR + (6 + i) * kPfK) * RS : (__half*)nullptr; };
     const int qb = gridDim.x - 1 - blockIdx.x, h = blockIdx.y;
     const int kh = h / (n_heads / n_kv);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -294,8 +314,8 @@ __global__ void __launch_bounds__(kPfThreads)
     const int last = pos0 + min(t0 + kPfQ, M) - 1;  // the block's last query position
     const int nkb = last / kPfK + 1;
 
-    pf_load_kv<HD>(Kb(0), Vb(0), KLb(0), 0, last, pos0, kh, kcache, vcache, kv_f16, cache_off, kvdim, kh16, vh16,
-                   kl16);
+    pf_load_kv<HD>(Kb(0), Vb(0), KLb(0), VLb(0), 0, last, pos0, kh, kcache, vcache, kv_f16, cache_off, kvdim, kh16,
+                   vh16, kl16, vl16);
     // queries -> fp16 (and their residuals)
     constexpr int C4 = HD / 4;
     for (int i = tid; i < kPfQ * C4; i += kPfThreads) {
@@ -335,10 +355,11 @@ __global__ void __launch_bounds__(kPfThreads)
         __half* Ks = Kb(kb & 1);
         __half* Vs = Vb(kb & 1);
         __half* KLs = KLb(kb & 1);
+        __half* VLs = VLb(kb & 1);
         if (kb + 1 < nkb) {
             // the other buffer was last read in block kb - 1 (barrier at its end)
-            pf_load_kv<HD>(Kb((kb + 1) & 1), Vb((kb + 1) & 1), KLb((kb + 1) & 1), p0 + kPfK, last, pos0, kh, kcache,
-                           vcache, kv_f16, cache_off, kvdim, kh16, vh16, kl16);
+            pf_load_kv<HD>(Kb((kb + 1) & 1), Vb((kb + 1) & 1), KLb((kb + 1) & 1), VLb((kb + 1) & 1), p0 + kPfK, last,
+                           pos0, kh, kcache, vcache, kv_f16, cache_off, kvdim, kh16, vh16, kl16, vl16);
             asm volatile("cp.async.wait_group 1;" ::: "memory");
         } else {
             asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -403,7 +424,10 @@ __global__ void __launch_bounds__(kPfThreads)
 #pragma unroll
             for (int e = 0; e < 4; e++) {
                 const int hr = e >> 1;
-                pv[e] = s[j][e] == -FLT_MAX ? 0.f : exp2f(s[j][e] - mrow[hr]);
+                // rounded to fp16 here, so the normaliser sums exactly the
+                // weights P V uses (a common offset of the V rows then passes
+                // through unscaled)
+                pv[e] = s[j][e] == -FLT_MAX ? 0.f : __half2float(__float2half_rn(exp2f(s[j][e] - mrow[hr])));
                 rs[hr] += pv[e];
             }
             pa[j >> 1][(j & 1) * 2 + 0] = pack_half2(pv[0], pv[1]);
@@ -427,10 +451,18 @@ __global__ void __launch_bounds__(kPfThreads)
             for (int jp = 0; jp < NT / 2; jp++) {
                 uint32_t b[4];
                 const int key = 16 * kk + (lane & 7) + 8 * ((lane >> 3) & 1);
-                ldsm_x4_t(smem_u32(Vs + key * RS + 16 * jp + 8 * (lane >> 4)), b);
+                const int voff = key * RS + 16 * jp + 8 * (lane >> 4);
+                ldsm_x4_t(smem_u32(Vs + voff), b);
                 const uint32_t b0[2] = {b[0], b[1]}, b1[2] = {b[2], b[3]};
                 mma_16816(o[2 * jp], a, b0, o[2 * jp]);
                 mma_16816(o[2 * jp + 1], a, b1, o[2 * jp + 1]);
+                if (SPLIT && VLs) {  // fp32 cache: V's residuals as well
+                    uint32_t bl[4];
+                    ldsm_x4_t(smem_u32(VLs + voff), bl);
+                    const uint32_t l0[2] = {bl[0], bl[1]}, l1[2] = {bl[2], bl[3]};
+                    mma_16816(o[2 * jp], a, l0, o[2 * jp]);
+                    mma_16816(o[2 * jp + 1], a, l1, o[2 * jp + 1]);
+                }
             }
         }
         __syncthreads();  // this block's K/V no longer read: its buffer may be refilled
@@ -449,9 +481,16 @@ __global__ void __launch_bounds__(kPfThreads)
         const float inv = lrow[hr] > 0.f ? 1.0f / lrow[hr] : 0.f;
         __half* orow = out + (size_t)tq * out_stride + h * HD;
 #pragma unroll
-        for (int j = 0; j < NT; j++)
-            *reinterpret_cast<uint32_t*>(orow + 8 * j + 2 * t4) =
-                pack_half2(o[j][2 * hr] * inv, o[j][2 * hr + 1] * inv);
+        for (int j = 0; j < NT; j++) {
+            const float f0 = o[j][2 * hr] * inv, f1 = o[j][2 * hr + 1] * inv;
+            const uint32_t hv = pack_half2(f0, f1);
+            *reinterpret_cast<uint32_t*>(orow + 8 * j + 2 * t4) = hv;
+            if (SPLIT && out_lo) {  // the O projection's low halves
+                const __half2 hh = *reinterpret_cast<const __half2*>(&hv);
+                *reinterpret_cast<uint32_t*>(out_lo + (size_t)tq * out_stride + h * HD + 8 * j + 2 * t4) =
+                    pack_half2(f0 - __low2float(hh), f1 - __high2float(hh));
+            }
+        }
     }
 }
 
@@ -464,9 +503,10 @@ int prefill_norm(cudaStream_t st, const float* x, const float* w, __half* y, flo
     return CN_OK;
 }
 
-int prefill_silu(cudaStream_t st, const float* g, const float* u, __half* h, float* inv, int n, int M) {
+int prefill_silu(cudaStream_t st, const float* g, const float* u, __half* h, float* inv, int n, int M,
+                 __half* hlo) {
     CN_CHECK(n % 4 == 0 && M >= 1, CN_ERR_INVALID_ARG, "prefill silu: shapes");
-    CN_CUDA(launch_k(false, silu_half_kernel, dim3(M), dim3(256), 0, st, g, u, h, inv, n));
+    CN_CUDA(launch_k(false, silu_half_kernel, dim3(M), dim3(256), 0, st, g, u, h, inv, n, hlo));
     return CN_OK;
 }
 
@@ -478,28 +518,30 @@ int to_half_rows(cudaStream_t st, const float* x, __half* y, float* inv, int n, 
 
 int prefill_rope(cudaStream_t st, float* q, const float* k, const float* v, const float2* rope, int pos0, int M,
                  int qdim, int kvdim, int hd, void* kcache, void* vcache, int64_t cache_off, bool kv_f16, __half* kh,
-                 __half* vh, __half* kl) {
+                 __half* vh, __half* kl, __half* vl) {
     CN_CHECK(hd % 4 == 0 && qdim % 4 == 0 && kvdim % 4 == 0, CN_ERR_INVALID_ARG, "prefill rope: shapes");
+    CN_CHECK(!kl == !vl, CN_ERR_INVALID_ARG, "prefill rope: k and v residuals go together");
     CN_CUDA(launch_k(false, rope_prefill_kernel, dim3(M), dim3(256), 0, st, q, k, v, rope, pos0, qdim, kvdim, hd,
-                     kcache, vcache, cache_off, kv_f16 ? 1 : 0, kh, vh, kl));
+                     kcache, vcache, cache_off, kv_f16 ? 1 : 0, kh, vh, kl, vl));
     return CN_OK;
 }
 
-// Shared memory of attn_prefill_kernel: Q [+ Qlo], 2 K, 2 V [+ 2 Klo] blocks.
+// Shared memory of attn_prefill_kernel: Q [+ Qlo], 2 K, 2 V [+ 2 Klo, 2 Vlo] blocks.
 static size_t attn_smem(int hd, bool split, bool klo) {
-    const int rows = kPfQ * (split ? 2 : 1) + kPfK * (4 + (split && klo ? 2 : 0));
+    const int rows = kPfQ * (split ? 2 : 1) + kPfK * (4 + (split && klo ? 4 : 0));
     return (size_t)rows * (hd + 8) * sizeof(__half);
 }
 
 int prefill_attention(cudaStream_t st, const float* q, int q_stride, const void* kcache,
                       const void* vcache, bool kv_f16, int64_t cache_off, int n_heads, int n_kv,
                       int hd, int M, int pos0, const __half* kh, const __half* vh, __half* out, int out_stride,
-                      bool split, const __half* kl) {
+                      bool split, const __half* kl, const __half* vl, __half* out_lo) {
     CN_CHECK(hd == 64 || hd == 128, CN_ERR_UNSUPPORTED, "prefill attention: head_dim %d", hd);
     CN_CHECK(n_kv > 0 && n_heads % n_kv == 0 && M >= 1 && pos0 >= 0, CN_ERR_INVALID_ARG,
              "prefill attention: bad arguments");
     CN_CHECK(q_stride % 4 == 0 && out_stride % 2 == 0, CN_ERR_INVALID_ARG, "prefill attention: strides");
-    CN_CHECK(!split || kv_f16 || kl, CN_ERR_INVALID_ARG, "prefill attention: split scores on an fp32 cache need k's residuals");
+    CN_CHECK(!split || kv_f16 || (kl && vl), CN_ERR_INVALID_ARG,
+             "prefill attention: the split form on an fp32 cache needs k's and v's residuals");
     const bool klo = split && !kv_f16;
     const size_t smem = attn_smem(hd, split, klo);
     {
@@ -525,7 +567,8 @@ int prefill_attention(cudaStream_t st, const float* q, int q_stride, const void*
     const int kf = kv_f16 ? 1 : 0, klo_i = klo ? 1 : 0;
 #define CN_PF_ATTN(HD, S)                                                                                          \
     CN_CUDA(launch_k(false, attn_prefill_kernel<HD, S>, grid, dim3(kPfThreads), smem, st, q, q_stride, kcache, vcache, \
-                     kf, cache_off, kvdim, n_heads, n_kv, M, pos0, scale_log2, kh, vh, out, out_stride, kl, klo_i));
+                     kf, cache_off, kvdim, n_heads, n_kv, M, pos0, scale_log2, kh, vh, out, out_stride, kl, vl, klo_i, \
+                     out_lo));
     if (hd == 128) {
         if (split) { CN_PF_ATTN(128, true) } else { CN_PF_ATTN(128, false) }
     } else {

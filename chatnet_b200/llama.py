@@ -161,8 +161,9 @@ class CudaLlamaModel:
         check(N.lib().cn_llama_set_prefill(self.handle, int(min_tokens)), "cn_llama_set_prefill")
 
     def set_prefill_precision(self, split: int) -> None:
-        """1 (default): q/k projections and attention scores on split (hi + lo
-        fp16) operands; 0: every prefill operand rounded to fp16 once."""
+        """0: every prefill operand rounded to fp16 once; 1: the attention path
+        (q/k/v and O projections, the attention's operands) on split (hi + lo
+        fp16) operands; 2 (default): every projection split as well."""
         check(N.lib().cn_llama_set_prefill_precision(self.handle, int(split)), "cn_llama_set_prefill_precision")
 
     def step(self, batch: int) -> None:

@@ -272,14 +272,19 @@ int cn_llama_forward(cn_llama* m, const int* tokens, int n, int pos, float* logi
  * counterpart: the reference has only the sequential loop) */
 int cn_llama_set_prefill(cn_llama* m, int min_tokens);
 
-/* Precision of the prefill pass.  1 (the default): the q and k projections
- * carry weights and activations as exact pairs of fp16 halves (three MMAs per
- * k-step) and the attention scores use q and k the same way, so the rounding
- * a whole projection shares cannot be magnified by a peaked softmax; hidden
- * states then agree with the sequential steps to within 1e-3 also at trained
- * weight magnitudes.  0: every operand rounded to fp16 once (faster; about
- * 5e-4 on the benchmark's synthetic configs, but up to ~1e-2 where a peaked
- * softmax magnifies the shared rounding).  (no reference counterpart) */
+/* Precision of the prefill pass (hidden states against the reference's
+ * sequential fp32 steps, one layer, trained-model-like Q4_K_M weights:
+ * measured worst token / median).
+ *   2 (the default): every projection carries weights and activations as
+ *     exact pairs of fp16 halves (three MMAs per k-step) and the attention
+ *     uses q, k (and, for fp32 caches, v) and its output the same way:
+ *     near-fp32 results, 2-3e-4 / 1-2e-4, about 2x the matmul time of 0;
+ *   1: only the attention path (q/k/v and O projections, attention) split,
+ *     the feed-forward matmuls on fp16 operands: ~1e-3 / 7e-4;
+ *   0: every operand rounded to fp16 once (fastest): ~2e-3 / 1.4e-3, and on
+ *     ill-conditioned inputs (a peaked softmax, tokens at the SwiGLU knee)
+ *     up to a few 1e-2.
+ * (no reference counterpart) */
 int cn_llama_set_prefill_precision(cn_llama* m, int split);
 
 /* Prefill on device buffers: runs the hidden states x_dev [n][dim] (fp32)
