@@ -801,7 +801,7 @@ __global__ void __launch_bounds__(kNormThreads)
 // every rank gets the same rms), then each CTA writes its slice and its
 // units' records.  Compared with add_norm_prep_kernel, which has every CTA
 // read the whole row (under tensor parallelism every rank's whole row), the
-// row is read once.
+// row is read once; used for tensor-parallel exchanges.
 constexpr int kNormCluster = 8;
 constexpr int kNormClThreads = 256;
 constexpr int kNormClMaxVals = 4096;  // values a CTA holds: rows up to 8 x 4096 = 32768
@@ -1240,7 +1240,10 @@ int add_norm_prep(cudaStream_t st, const float* x_in, const float* delta, float*
     XchgIn xi;
     if (xch) xi = *xin;
     const int units = n / 256;
-    if (n % 256 == 0 && units >= 1 && (units + kNormCluster - 1) / kNormCluster * 256 <= kNormClMaxVals) {
+    // tensor parallel: the cluster form reads every rank's slots once per row
+    // instead of once per CTA; on one GPU the plain form schedules sooner
+    // behind a GEMV that holds whole SMs (a cluster needs free SMs in one GPC)
+    if (xch && n % 256 == 0 && units >= 1 && (units + kNormCluster - 1) / kNormCluster * 256 <= kNormClMaxVals) {
         const int C = units < kNormCluster ? units : kNormCluster;
         CN_CUDA(launch_cluster_k(true, C, add_norm_prep_cl_kernel, dim3(C, rows), dim3(kNormClThreads), 0, st,
                                  x_in, delta, x_out, w, y, n, eps, pt, xi));

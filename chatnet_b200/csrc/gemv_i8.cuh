@@ -69,16 +69,21 @@ __device__ __forceinline__ void emit_i8(const float (&v)[8], int u, int b, int b
         *reinterpret_cast<uint2*>(reg + ((size_t)(c * NT + nt) * 32 + L) * 8) = make_uint2(b0, b1);
     };
     if (batch == 1) {
+        // balanced base-15 digits via plain ones: with the offset
+        // 7 * (15^6 - 1) / 14 every X' = X + offset lies in [0, 15^6), its
+        // base-15 digits u_i are in [0, 14], and d_i = u_i - 7 are the balanced
+        // digits of X (|X| <= 2^22 < 5695312).  n / 15 = umulhi(n, 0x88888889) >> 3.
+        uint32_t U[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) U[k] = (uint32_t)(X[k] + 5695312);
 #pragma unroll
         for (int i = 0; i < 6; i++) {
-            // digit i of X: balanced base 15
             int d[8];
 #pragma unroll
             for (int k = 0; k < 8; k++) {
-                int r = X[k] % 15;
-                r += r < 0 ? 15 : 0;
-                d[k] = r > 7 ? r - 15 : r;
-                X[k] = (X[k] - d[k]) / 15;
+                const uint32_t q = __umulhi(U[k], 0x88888889u) >> 3;
+                d[k] = (int)(U[k] - 15u * q) - 7;
+                U[k] = q;
             }
             uint32_t w0 = 0, w1 = 0;
 #pragma unroll

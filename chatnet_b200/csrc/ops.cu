@@ -235,6 +235,19 @@ __device__ __forceinline__ void attn_finish(float* __restrict__ pr_base, int spl
         const float* wr = wsm + g * splits;
         float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
         int t = 0;
+        for (; t + 16 <= splits; t += 16) {  // sixteen independent loads in flight
+            float4 v[16];
+#pragma unroll
+            for (int k = 0; k < 16; k++) v[k] = __ldcg(reinterpret_cast<const float4*>(pr + (size_t)(t + k) * prow));
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                const float w = wr[t + k];
+                o.x = fmaf(w, v[k].x, o.x);
+                o.y = fmaf(w, v[k].y, o.y);
+                o.z = fmaf(w, v[k].z, o.z);
+                o.w = fmaf(w, v[k].w, o.w);
+            }
+        }
         for (; t + 4 <= splits; t += 4) {  // four independent loads in flight
             float4 v[4];
 #pragma unroll
