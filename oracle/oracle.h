@@ -126,6 +126,11 @@ int or_llama_head(const or_llama_config* cfg, const void* const* tensors,
 uint64_t or_synth_seed(int config_id, const char* name);
 int or_synth_fill(int type, int64_t rows, int64_t cols, uint64_t seed,
                   int norm_weight, void* out, uint64_t bytes);
+/* Rows [row0, row0 + rows) of what or_synth_fill would write for a tensor of
+ * at least row0 + rows rows (the generator is counter-based). */
+int or_synth_fill_rows(int type, int64_t row0, int64_t rows, int64_t cols,
+                       uint64_t seed, int norm_weight, void* out,
+                       uint64_t bytes);
 
 #ifdef __cplusplus
 }

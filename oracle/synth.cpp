@@ -130,40 +130,45 @@ uint64_t or_synth_seed(int config_id, const char* name) {
     return fin(h ^ ((uint64_t)(uint32_t)config_id * kG));
 }
 
-int or_synth_fill(int type, int64_t rows, int64_t cols, uint64_t seed, int norm_weight, void* out,
-                  uint64_t bytes) {
-    if (!out || rows < 0 || cols < 0) return -1;
-    const uint64_t n = (uint64_t)rows * (uint64_t)cols;
+int or_synth_fill_rows(int type, int64_t row0, int64_t rows, int64_t cols, uint64_t seed, int norm_weight,
+                       void* out, uint64_t bytes) {
+    if (!out || row0 < 0 || rows < 0 || cols < 0) return -1;
+    const uint64_t n = (uint64_t)rows * (uint64_t)cols, e0 = (uint64_t)row0 * (uint64_t)cols;
     if (or_byte_size(type, (uint64_t)cols) * (uint64_t)rows != bytes) return -1;
     uint8_t* o = static_cast<uint8_t*>(out);
     switch (type) {
         case OR_Q4_0:
             if (cols % 32) return -1;
-            par(n / 32, [&](uint64_t b) { q4_0(seed, b, o + 18 * b); });
+            par(n / 32, [&](uint64_t b) { q4_0(seed, e0 / 32 + b, o + 18 * b); });
             return 0;
         case OR_Q4_K:
             if (cols % 256) return -1;
-            par(n / 256, [&](uint64_t b) { q4_k(seed, b, o + 144 * b); });
+            par(n / 256, [&](uint64_t b) { q4_k(seed, e0 / 256 + b, o + 144 * b); });
             return 0;
         case OR_Q6_K:
             if (cols % 256) return -1;
-            par(n / 256, [&](uint64_t b) { q6_k(seed, b, o + 210 * b); });
+            par(n / 256, [&](uint64_t b) { q6_k(seed, e0 / 256 + b, o + 210 * b); });
             return 0;
         case OR_F32: {
             float* f = static_cast<float*>(out);
             par(n, [&](uint64_t i) {
-                const float v = normal(seed, 3 * i);
+                const float v = normal(seed, 3 * (e0 + i));
                 f[i] = norm_weight ? 1.0f + 0.01f * v : v;
             });
             return 0;
         }
         case OR_F16: {
             uint16_t* h = static_cast<uint16_t*>(out);
-            par(n, [&](uint64_t i) { h[i] = or_float_to_half(normal(seed, 3 * i)); });
+            par(n, [&](uint64_t i) { h[i] = or_float_to_half(normal(seed, 3 * (e0 + i))); });
             return 0;
         }
     }
     return -2;
+}
+
+int or_synth_fill(int type, int64_t rows, int64_t cols, uint64_t seed, int norm_weight, void* out,
+                  uint64_t bytes) {
+    return or_synth_fill_rows(type, 0, rows, cols, seed, norm_weight, out, bytes);
 }
 
 }  // extern "C"

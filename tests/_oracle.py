@@ -48,6 +48,7 @@ _SIG = {
     "or_llama_head": (_i, [C.POINTER(LlamaConfig), C.POINTER(_vp), C.POINTER(_i), _fp, _fp, _i]),
     "or_synth_seed": (C.c_uint64, [_i, C.c_char_p]),
     "or_synth_fill": (_i, [_i, C.c_int64, C.c_int64, C.c_uint64, _i, _vp, C.c_uint64]),
+    "or_synth_fill_rows": (_i, [_i, C.c_int64, C.c_int64, C.c_int64, C.c_uint64, _i, _vp, C.c_uint64]),
 }
 
 
@@ -81,11 +82,14 @@ class Oracle:
     def synth_seed(self, config_id: int, name: str) -> int:
         return int(self.lib.or_synth_seed(config_id, name.encode()))
 
-    def synth_fill(self, type_: int, rows: int, cols: int, seed: int, norm_weight: bool = False) -> np.ndarray:
-        """Same bytes as chatnet_b200.synth_fill (checked by test_oracle_synth)."""
+    def synth_fill(self, type_: int, rows: int, cols: int, seed: int, norm_weight: bool = False,
+                   row0: int = 0) -> np.ndarray:
+        """Same bytes as chatnet_b200.synth_fill (checked by test_oracle_synth);
+        with row0, rows [row0, row0 + rows) of a larger tensor."""
         nbytes = int(self.lib.or_byte_size(type_, cols)) * rows
         out = np.empty(nbytes, dtype=np.uint8)
-        rc = self.lib.or_synth_fill(type_, rows, cols, seed, 1 if norm_weight else 0, out.ctypes.data, nbytes)
+        rc = self.lib.or_synth_fill_rows(type_, row0, rows, cols, seed, 1 if norm_weight else 0, out.ctypes.data,
+                                         nbytes)
         assert rc == 0, rc
         if type_ == 0:
             return out.view(np.float32).reshape(rows, cols)
@@ -185,6 +189,18 @@ def host_kv(orc: Oracle, dc, seq: int) -> tuple[np.ndarray, np.ndarray]:
         a = a.reshape(m.n_layers, m.ctx_len, m.kv_dim).copy()
         a[:, dc.kv_filled:, :] = 0
         out.append(a.reshape(m.n_layers * m.ctx_len, m.kv_dim))
+    return out[0], out[1]
+
+
+def layer_kv(orc: Oracle, dc, seq: int, layer: int) -> tuple[np.ndarray, np.ndarray]:
+    """Layer `layer`'s [ctx, kv_dim] slice of host_kv(dc, seq), generated alone."""
+    m = dc.model
+    out = []
+    for which in ("k", "v"):
+        a = orc.synth_fill(1 if m.kv_f16 else 0, m.ctx_len, m.kv_dim, orc.synth_seed(dc.config_id, f"kv.{which}.{seq}"),
+                           row0=layer * m.ctx_len).copy()
+        a[dc.kv_filled:, :] = 0
+        out.append(a)
     return out[0], out[1]
 
 

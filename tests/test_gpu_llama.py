@@ -195,6 +195,63 @@ def test_config4_two_layers_batched(ctx, oracle):
     p.close()
 
 
+def _oracle_full_depth(orc, dc, toks: list[int]) -> np.ndarray:
+    """LlamaModel.Forward of every sequence's token at dc.decode_pos through all
+    of dc's layers, generating one layer's weights (and that layer's slice of
+    each sequence's KV cache) at a time from the seeded generator, so host
+    memory holds one layer (481 MB at config 4) instead of the model."""
+    from chatnet_b200.llama import LAYER_TENSORS
+    m = dc.model
+    one = cf.with_layers(dc, 1)
+    head = _oracle.host_tensors(orc, dc, names=["token_embd.weight", "output.weight", "output_norm.weight"])
+    names1 = tensor_names(1)
+    types1 = [cf.tensor_type(dc, n) for n in names1]
+    xs = [orc.dequantize(types1[0], head["token_embd.weight"][t], m.dim) for t in toks]
+    ol = None
+    for layer in range(m.n_layers):
+        lay = _oracle.host_tensors(orc, dc, names=[f"blk.{layer}.{k}.weight" for k in LAYER_TENSORS])
+        host = dict(head)
+        host.update({f"blk.0.{k}.weight": lay[f"blk.{layer}.{k}.weight"] for k in LAYER_TENSORS})
+        for b in range(len(toks)):
+            k, v = _oracle.layer_kv(orc, dc, b, layer)
+            ol = _oracle.OracleLlama(orc, one.model, host, types1, names1, k, v)
+            xs[b] = ol.layers(xs[b], dc.decode_pos)
+    out = np.empty((len(toks), m.vocab), np.float32)
+    for b in range(len(toks)):
+        rc = orc.lib.or_llama_head(_oracle.C.byref(ol.cfg), ol.ptrs, ol.types, _oracle.fp(xs[b]), _oracle.fp(out[b]), 0)
+        assert rc == 0
+    return out
+
+
+def test_config4_full_depth_b16_and_b1(ctx, oracle):
+    """Config 4 at its full depth and both of its batch sizes: all 80
+    Llama-2-70B-shaped Q4_K layers with the fp16 cache filled to position
+    2046, one decode step of 16 sequences (the fp16 hi + lo GEMV family) and
+    one of sequence 0 alone (the integer GEMV), against the oracle's Forward of
+    each sequence: logits within 1e-3 and the same greedy token."""
+    B = 16
+    dc = cf.with_batch(cf.CONFIGS[4], B)
+    m = dc.model
+    ts = cf.device_tensors(ctx, dc)  # 38.5 GB generated on the device
+    g = CudaLlamaModel(ctx, m, ts)
+    for b in range(B):
+        g.kv_synth(b, dc.kv_filled, *cf.kv_seeds(dc, b))
+    toks = [cf.token(dc, b) for b in range(B)]
+    lg16, am16 = g.decode(toks, [dc.decode_pos] * B)
+    lg1, am1 = g.decode(toks[:1], [dc.decode_pos])
+    g.close()
+    for t in ts:
+        t.free()
+    ref = _oracle_full_depth(oracle, dc, toks)
+    errs = [rel_err(lg16[b], ref[b]) for b in range(B)]
+    print(f"config4 80 layers: B=16 worst logits rel err {max(errs):.2e}, B=1 {rel_err(lg1[0], ref[0]):.2e}")
+    for b in range(B):
+        assert errs[b] <= REL_TOL, (b, errs[b])
+        assert int(am16[b]) == int(np.argmax(ref[b])), b
+    assert rel_err(lg1[0], ref[0]) <= REL_TOL
+    assert int(am1[0]) == int(np.argmax(ref[0]))
+
+
 def test_mixed_codec_model(ctx, oracle):
     """A decoder whose projections, embedding and lm_head use the generic
     codecs (every K-quant and IQ4 type the reference decodes besides Q4_K /

@@ -46,6 +46,24 @@ def test_config_helpers_match(oracle):
     assert np.array_equal(_oracle.prefill_x(oracle, d3, 9), cf.prefill_x(d3, 9))
 
 
+@pytest.mark.parametrize("type_,cols", [(cn.TYPE_Q4_0, 2048), (cn.TYPE_Q4_K, 512), (cn.TYPE_Q6_K, 256),
+                                        (cn.TYPE_F32, 100), (cn.TYPE_F16, 64)])
+def test_row_slices(oracle, type_, cols):
+    seed = oracle.synth_seed(4, "rows")
+    full = oracle.synth_fill(type_, 23, cols, seed).view(np.uint8).reshape(23, -1)
+    part = oracle.synth_fill(type_, 9, cols, seed, row0=7).view(np.uint8).reshape(9, -1)
+    assert np.array_equal(full[7:16], part)
+
+
+def test_layer_kv_slices(oracle):
+    dc = cf.with_layers(cf.CONFIGS[4], 3)
+    dc = cf.replace(dc, model=cf.replace(dc.model, ctx_len=16, n_kv_heads=1, head_dim=8), kv_filled=11)
+    k, v = _oracle.host_kv(oracle, dc, 2)
+    for layer in range(3):
+        lk, lv = _oracle.layer_kv(oracle, dc, 2, layer)
+        assert np.array_equal(lk, k[layer * 16:(layer + 1) * 16]) and np.array_equal(lv, v[layer * 16:(layer + 1) * 16])
+
+
 def test_bad_requests(oracle):
     buf = np.empty(18, np.uint8)
     assert oracle.lib.or_synth_fill(cn.TYPE_Q4_0, 1, 32, 1, 0, buf.ctypes.data, 17) == -1
