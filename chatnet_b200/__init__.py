@@ -120,6 +120,16 @@ class Context:
                                        C.byref(h)), "cn_tensor_upload")
         return self._own(Tensor(self, h.value, type_, rows, cols))
 
+    def upload_slice(self, blocks: np.ndarray, type_: int, rows: int, cols: int, row0: int, nrows: int,
+                     col0: int, ncols: int) -> Tensor:
+        """Region [row0, row0+nrows) x [col0, col0+ncols) (whole blocks) of the
+        host tensor `blocks` ([rows][ByteSize(cols)] bytes): a tensor-parallel shard."""
+        buf = np.ascontiguousarray(blocks).view(np.uint8).reshape(-1)
+        h = C.c_void_p()
+        check(N.lib().cn_tensor_upload_slice(self.handle, buf.ctypes.data, buf.nbytes, type_, rows, cols, row0,
+                                             nrows, col0, ncols, C.byref(h)), "cn_tensor_upload_slice")
+        return self._own(Tensor(self, h.value, type_, nrows, ncols))
+
     def synth(self, type_: int, rows: int, cols: int, seed: int, dist: int | None = None) -> Tensor:
         if dist is None:
             dist = _DEFAULT_DIST.get(type_, DIST_NORMAL)

@@ -109,6 +109,8 @@ SIGNATURES: dict[str, tuple] = {
     "cn_gguf_llama_config": (_i, [_vp, _vp]),
     "cn_gguf_upload": (_i, [_vp, _vp, C.c_char_p, C.POINTER(_vp)]),
     "cn_llama_create_from_gguf": (_i, [_vp, _vp, _i, _i, C.POINTER(_vp), C.POINTER(_vp), _i]),
+    "cn_llama_create_from_gguf_tp": (_i, [_vp, _vp, _vp, _i, _i, C.POINTER(_vp), C.POINTER(_vp), _i]),
+    "cn_tensor_upload_slice": (_i, [_vp, _vp, _u64, _i, _i64, _i64, _i64, _i64, _i64, _i64, C.POINTER(_vp)]),
     "cn_llama_prefill_kernels": (_i, [_vp, C.POINTER(_i)]),
     "cn_llama_decode": (_i, [_vp, C.POINTER(_i), C.POINTER(_i), _i, _fp, C.POINTER(_i)]),
     "cn_llama_kv_write": (_i, [_vp, _i, _i, _i, _i, _vp, _vp]),

@@ -237,6 +237,40 @@ int cn_tensor_upload(cn_ctx* ctx, const void* host_blocks, uint64_t bytes, int t
     return CN_OK;
 }
 
+int cn_tensor_upload_slice(cn_ctx* ctx, const void* host_blocks, uint64_t bytes, int type, int64_t rows,
+                           int64_t cols, int64_t row0, int64_t nrows, int64_t col0, int64_t ncols,
+                           cn_tensor** out) {
+    CN_CHECK(ctx && host_blocks && out, CN_ERR_INVALID_ARG, "null argument");
+    DeviceGuard dg(ctx->device);
+    CN_CHECK(type_supported(type), CN_ERR_UNSUPPORTED, "Unsupported weight quantization type: %d", type);
+    CN_CHECK(rows > 0 && cols > 0 && row0 >= 0 && nrows > 0 && row0 + nrows <= rows && col0 >= 0 && ncols > 0 &&
+                 col0 + ncols <= cols,
+             CN_ERR_INVALID_ARG, "slice [%lld+%lld, %lld+%lld] outside [%lld, %lld]", (long long)row0,
+             (long long)nrows, (long long)col0, (long long)ncols, (long long)rows, (long long)cols);
+    const int64_t blk = type == CN_TYPE_F32 || type == CN_TYPE_F16 ? 1
+                        : (type == CN_TYPE_Q4_0 || is_block32(type)) ? 32 : 256;
+    CN_CHECK(col0 % blk == 0 && ncols % blk == 0, CN_ERR_INVALID_ARG,
+             "column slice must cover whole %lld-weight blocks", (long long)blk);
+    const uint64_t rb = row_bytes(type, cols);
+    uint64_t want = 0;
+    CN_CHECK(!__builtin_mul_overflow(rb, (uint64_t)rows, &want) && bytes == want, CN_ERR_INVALID_ARG,
+             "tensor bytes %llu != rows * ByteSize(cols) = %llu", (unsigned long long)bytes,
+             (unsigned long long)want);
+    const uint64_t off = row_bytes(type, col0);  // the slice's first byte within a row
+    cn_tensor* t = nullptr;
+    int rc = tensor_alloc(ctx, type, nrows, ncols, &t);
+    if (rc) return rc;
+    const uint8_t* src = static_cast<const uint8_t*>(host_blocks) + (uint64_t)row0 * rb + off;
+    cudaError_t e = cudaMemcpy2D(t->d, t->row_bytes, src, rb, t->row_bytes, (size_t)nrows, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(t->d);
+        delete t;
+        return cuda_error(e, "cudaMemcpy2D(upload slice)");
+    }
+    *out = t;
+    return CN_OK;
+}
+
 int cn_tensor_synth(cn_ctx* ctx, int type, int64_t rows, int64_t cols, uint64_t seed, int dist,
                     cn_tensor** out) {
     CN_CHECK(ctx && out, CN_ERR_INVALID_ARG, "null argument");

@@ -596,6 +596,14 @@ __global__ void xprep_kernel(const float* __restrict__ x, int K, int batch, Prep
 // threads mean fewer passes.
 constexpr int kNormThreads = 512;
 
+// An exchange wait gives up at its time limit, or at once when an earlier
+// wait of the step already gave up (the error word holds kErrTimeout): a rank
+// that never arrives then costs one limit per step, not one per exchange.
+__device__ __forceinline__ bool xchg_give_up(const XchgIn& xi, uint64_t t0) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return true;
+    return (*reinterpret_cast<volatile const uint32_t*>(xi.err) & kErrTimeout) != 0;
+}
+
 // Bounded wait of one thread for an exchange: every rank's flag must reach
 // this use's sequence number; on timeout the error word is raised and the
 // caller runs on (its results are then flagged garbage).
@@ -607,7 +615,7 @@ __device__ __forceinline__ uint32_t xchg_wait_dev(const XchgIn& xi) {
             uint32_t f;
             asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(xi.flags + p) : "memory");
             if ((int32_t)(f - seq) >= 0) break;
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            if (xchg_give_up(xi, t0)) {
                 atomicOr(xi.err, kErrTimeout);
                 return seq;
             }
@@ -638,7 +646,7 @@ __device__ __forceinline__ float ll_sum1(const XchgIn& xi, const uint64_t* base,
         for (int p = 0; p < kMaxTp; p++)
             if (p < xi.size) ok = ok && (uint32_t)(v[p] >> 32) == seq;
         if (ok) break;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (xchg_give_up(xi, t0)) {
             atomicOr(xi.err, kErrTimeout);
             break;
         }
@@ -675,7 +683,7 @@ __device__ __forceinline__ float4 ll_sum4(const XchgIn& xi, const uint64_t* base
 #pragma unroll
                 for (int e = 0; e < 4; e++) ok = ok && (uint32_t)(v[p][e] >> 32) == seq;
         if (ok) break;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (xchg_give_up(xi, t0)) {
             atomicOr(xi.err, kErrTimeout);
             break;
         }

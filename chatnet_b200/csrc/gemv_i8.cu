@@ -47,14 +47,25 @@ constexpr int kThreads = (kCons + 1) * 32;
 // CTA per SM with ~200 KB of stages, for grids of at most one CTA per SM
 // (short or few rows, e.g. tensor-parallel shards): the bytes one CTA keeps
 // in flight, not the SM count, then bound the weight stream.
+//
+// DEEP == 2 is the deep pipeline with two groups of eight consumer warps
+// that take alternate stages: a unit costs a group's warps a long latency
+// chain (about a thousand cycles), so with few units per CTA (short rows,
+// where the pipeline's fill and drain dominate) two units in flight finish
+// the range sooner.  The groups' partial sums of a tile meet in shared memory
+// at the tile's end.  With many units per CTA the weight stream bounds the
+// CTA and the extra warps only cost, so the plain deep form runs there.
 template <int NB, int DEEP = 0>
 struct Geo {
     static constexpr int NT = n_tiles(NB);
     static constexpr int kRec = (rec_bytes(NT) + 127) / 128 * 128;
     static constexpr int kStage = kRaw + kRec;
     static constexpr int kCtasPerSm = DEEP ? 1 : NT == 1 ? 3 : 2;
+    static constexpr int kGroups = DEEP == 2 ? 2 : 1;
+    static constexpr int kThreads = (kGroups * kCons + 1) * 32;
     static constexpr int kStages = (DEEP ? 200 * 1024 : NT == 1 ? 72 * 1024 : 110 * 1024) / kStage;
-    static constexpr int kSmem = kStages * kStage + 256;
+    static constexpr int kXchg = DEEP == 2 ? 2 * kCons * 32 * NT * 4 : 0;  // group partials, two buffers
+    static constexpr int kSmem = kStages * kStage + 256 + kXchg;
 };
 static_assert(Geo<1>::kStages >= 3 && Geo<3>::kStages >= 4 && Geo<8>::kStages >= 4, "pipeline depth");
 static_assert(Geo<1, 1>::kStages >= 8 && Geo<8, 1>::kStages >= 7 && Geo<8, 1>::kSmem <= 227 * 1024,
@@ -230,7 +241,7 @@ __device__ void finish_subtile(const Args& a, int r, int t, int warp, int tile, 
 }  // namespace i8
 
 template <int NB, int DEEP>
-__global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB, DEEP>::kCtasPerSm)
+__global__ void __launch_bounds__(i8::Geo<NB, DEEP>::kThreads, i8::Geo<NB, DEEP>::kCtasPerSm)
     gemv_i8_q4k_kernel(const __grid_constant__ i8::Maps maps, const i8::Args a) {
     using namespace i8;
     using G = Geo<NB, DEEP>;
@@ -241,6 +252,8 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB, DEEP>::kCtasPerSm)
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStage);
     uint64_t* empty = full + kStages;
     int* bcast = reinterpret_cast<int*>(empty + kStages);
+    float* xg = reinterpret_cast<float*>(smem + kStages * kStage + 256);  // [2][kCons][32][NT]
+    constexpr int kGroups = G::kGroups;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -262,7 +275,7 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB, DEEP>::kCtasPerSm)
     const int tile0 = cta < C ? (int)(v0 / a.units) : 0;
     const int u0 = cta < C ? (int)(v0 % a.units) : 0;
 
-    if (warp == kCons) {
+    if (warp == kGroups * kCons) {
         // ---- producer ----
         if (lane == 0) {
             // the weights depend on no earlier kernel: start the first
@@ -329,11 +342,12 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB, DEEP>::kCtasPerSm)
     pdl_wait();
     const uint32_t seq = a.xo.size > 1 ? *a.xo.seq_base * a.xo.uses + a.xo.seq_add : 0u;
     const int g = lane >> 2, t = lane & 3;
-    const int row0 = 16 * warp + g, row1 = row0 + 8;
+    const int cg = warp / kCons, cw = warp % kCons;  // consumer group, warp within it (16 rows each)
+    const int row0 = 16 * cw + g, row1 = row0 + 8;
     const int r_own = (t & 1) ? row1 : row0;
     // ldmatrix.x2: lanes 0-7 address rows 0-7 of the warp's 16, lanes 8-15
     // rows 8-15 (lanes 16-31 repeat them), at the sub-block's quant bytes
-    const uint32_t lds_off = (uint32_t)((16 * warp + (lane & 15)) * 144 + 16);
+    const uint32_t lds_off = (uint32_t)((16 * cw + (lane & 15)) * 144 + 16);
     // weights of this thread's two accumulator columns in the recombination
     // (batch 1: base 15, columns 2t and 2t+1 weigh 15^2t and 15^(2t+1))
     const float w_lo = NB == 1 ? (t == 0 ? 1.0f : t == 1 ? 225.0f : t == 2 ? 50625.0f : 11390625.0f)
@@ -343,7 +357,9 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB, DEEP>::kCtasPerSm)
     const float kMin = NB == 1 ? -16.0f : -1.0f;
     const uint32_t smem0 = smem_u32(smem);
 
-    int s = 0, n = 0, et = tile0, eu = u0;
+    int n = 0, et = tile0, eu = u0, segi = 0;
+    // this group's next stage and its phase: its units are cg, cg + kGroups, ...
+    int s = cg;
     uint32_t ph = 0;
     bool ok = true;
     while (n < nunits) {
@@ -352,7 +368,8 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB, DEEP>::kCtasPerSm)
         float acc[NT];
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) acc[nt] = 0.f;
-        for (int k = 0; k < seg; k++) {
+        // group cg takes the range's units gn with gn % kGroups == cg
+        for (int k = (kGroups - (n % kGroups) + cg) % kGroups; k < seg; k += kGroups) {
             if (ok && !mbar_wait_sleep(&full[s], ph)) {
                 atomicOr(a.err, kErrTimeout);
                 ok = false;
@@ -428,8 +445,9 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB, DEEP>::kCtasPerSm)
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
-            if (++s == kStages) {
-                s = 0;
+            s += kGroups;  // kGroups < kStages: at most one wrap
+            if (s >= kStages) {
+                s -= kStages;
                 ph ^= 1;
             }
             // recombine the digits: this thread's two columns, then across the
@@ -444,12 +462,33 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB, DEEP>::kCtasPerSm)
             }
         }
         n += seg;
+        if (kGroups > 1) {
+            // group 1's partial sums of the tile's rows go to group 0 (two
+            // buffers by segment parity: a buffer is rewritten only after the
+            // barrier of the next segment, which group 0 reaches once it has
+            // read it)
+            float* xb = xg + ((segi & 1) * kCons * 32 + cw * 32 + lane) * NT;
+            if (cg == 1) {
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++) xb[nt] = acc[nt];
+            }
+            asm volatile("bar.sync 2, %0;" ::"n"(kGroups * kCons * 32) : "memory");
+            if (cg == 1) {
+                et++;
+                eu = 0;
+                segi++;
+                continue;
+            }
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) acc[nt] += xb[nt];
+        }
         const bool head_cut = (et == tile0) && (u0 != 0);
         const bool tail_cut = eu + seg != a.units;
-        finish_subtile<NB>(a, r_own, t, warp, et, cta, C, total, head_cut || tail_cut, et == tile0 ? 0 : 1,
+        finish_subtile<NB>(a, r_own, t, cw, et, cta, C, total, head_cut || tail_cut, et == tile0 ? 0 : 1,
                            acc, seq);
         et++;
         eu = 0;
+        segi++;
     }
     if (a.xo.size > 1 && !a.xo.ll) {
         // gather: once every CTA's peer stores are visible system-wide, the
@@ -458,7 +497,7 @@ __global__ void __launch_bounds__(i8::kThreads, i8::Geo<NB, DEEP>::kCtasPerSm)
         // system-scope release fence, which then covers them all; an
         // acquire-release fence is enough here and costs less than a
         // sequentially consistent one)
-        asm volatile("bar.sync 1, %0;" ::"n"(kCons * 32) : "memory");
+        asm volatile("bar.sync 1, %0;" ::"n"(kGroups * kCons * 32) : "memory");
         if (threadIdx.x == 0) {
             asm volatile("fence.acq_rel.sys;" ::: "memory");
             int old;
@@ -561,6 +600,10 @@ int gemv_i8_prepare() {
                                  i8::Geo<NB, 1>::kSmem));
     CN_ATTR(1) CN_ATTR(2) CN_ATTR(3) CN_ATTR(4) CN_ATTR(5) CN_ATTR(6) CN_ATTR(7) CN_ATTR(8)
 #undef CN_ATTR
+    CN_CUDA(cudaFuncSetAttribute(gemv_i8_q4k_kernel<1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 i8::Geo<1, 2>::kSmem));
+    CN_CUDA(cudaFuncSetAttribute(gemv_i8_q4k_kernel<2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 i8::Geo<2, 2>::kSmem));
     CN_CUDA(cudaDeviceGetAttribute(&g_sms[dev & 63], cudaDevAttrMultiProcessorCount, dev));
     done[dev & 63] = true;
     return CN_OK;
@@ -600,14 +643,26 @@ int gemv_i8_run_group(cudaStream_t st, uint32_t* err, int nmat, const CUtensorMa
     int dev = 0;
     CN_CUDA(cudaGetDevice(&dev));
     const bool deep = ctas <= g_sms[dev & 63];  // one CTA per SM: the deep pipeline
+    // few units per CTA (batch 1-2): the deep pipeline with two consumer groups
+    const bool grouped = deep && batch <= 2 && (int64_t)tiles * a.units <= 16LL * ctas;
+    if (grouped) {
+        if (batch == 1)
+            CN_CUDA(launch_k(true, gemv_i8_q4k_kernel<1, 2>, dim3(ctas), dim3(i8::Geo<1, 2>::kThreads),
+                             (size_t)i8::Geo<1, 2>::kSmem, st, mp, a));
+        else
+            CN_CUDA(launch_k(true, gemv_i8_q4k_kernel<2, 2>, dim3(ctas), dim3(i8::Geo<2, 2>::kThreads),
+                             (size_t)i8::Geo<2, 2>::kSmem, st, mp, a));
+        CN_CUDA(cudaGetLastError());
+        return CN_OK;
+    }
     switch (batch) {
 #define CN_I8(NB)                                                                                  \
     case NB:                                                                                       \
         if (deep)                                                                                  \
-            CN_CUDA(launch_k(true, gemv_i8_q4k_kernel<NB, 1>, dim3(ctas), dim3(i8::kThreads),      \
+            CN_CUDA(launch_k(true, gemv_i8_q4k_kernel<NB, 1>, dim3(ctas), dim3(i8::Geo<NB, 1>::kThreads), \
                              (size_t)i8::Geo<NB, 1>::kSmem, st, mp, a));                           \
         else                                                                                       \
-            CN_CUDA(launch_k(true, gemv_i8_q4k_kernel<NB, 0>, dim3(ctas), dim3(i8::kThreads),      \
+            CN_CUDA(launch_k(true, gemv_i8_q4k_kernel<NB, 0>, dim3(ctas), dim3(i8::Geo<NB, 0>::kThreads), \
                              (size_t)i8::Geo<NB, 0>::kSmem, st, mp, a));                           \
         break;
         CN_I8(1) CN_I8(2) CN_I8(3) CN_I8(4) CN_I8(5) CN_I8(6) CN_I8(7) CN_I8(8)

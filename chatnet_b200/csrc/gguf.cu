@@ -417,8 +417,29 @@ int cn_gguf_upload(cn_ctx* ctx, const cn_gguf* g, const char* name, cn_tensor** 
     return cn_tensor_upload(ctx, src, t.bytes, t.type, rows, cols, out);
 }
 
-int cn_llama_create_from_gguf(cn_ctx* ctx, const cn_gguf* g, int max_batch, int kv_dtype, cn_llama** out,
-                              cn_tensor** tensors_out, int n_tensors_out) {
+// Region of tensor `name` ([rows, cols]) that tensor-parallel rank r of
+// `size` holds: rows of q/k/v/gate/up/lm_head (heads, FFN rows, vocabulary),
+// columns of O/down (their input), everything else whole.
+static void shard_region(const char* name, int64_t rows, int64_t cols, int r, int size, int64_t* row0,
+                         int64_t* nrows, int64_t* col0, int64_t* ncols) {
+    *row0 = 0;
+    *nrows = rows;
+    *col0 = 0;
+    *ncols = cols;
+    const std::string n(name);
+    if (size <= 1 || n == "token_embd.weight" || n.size() >= 11 && n.compare(n.size() - 11, 11, "norm.weight") == 0)
+        return;
+    if (n.find(".attn_output.") != std::string::npos || n.find(".ffn_down.") != std::string::npos) {
+        *ncols = cols / size;
+        *col0 = (int64_t)r * *ncols;
+        return;
+    }
+    *nrows = rows / size;
+    *row0 = (int64_t)r * *nrows;
+}
+
+static int create_from_gguf(cn_ctx* ctx, const cn_gguf* g, cn_tp* tp, int max_batch, int kv_dtype, cn_llama** out,
+                            cn_tensor** tensors_out, int n_tensors_out) {
     CN_CHECK(ctx && g && out && tensors_out, CN_ERR_INVALID_ARG, "null argument");
     cn_llama_config c;
     int rc = cn_gguf_llama_config(g, &c);
@@ -440,24 +461,63 @@ int cn_llama_create_from_gguf(cn_ctx* ctx, const cn_gguf* g, int max_batch, int 
         for (int i = 0; i < n; i++)
             if (ts[i] && !(i == 1 && ts[1] == ts[0])) cn_tensor_free(ts[i]);
     };
+    const int size = tp ? tp->size : 1, rank = tp ? tp->rank : 0;
+    if (size > 1)
+        CN_CHECK(c.n_kv_heads % size == 0 && c.hidden_dim % size == 0 && c.vocab % size == 0 &&
+                     c.dim % (256 * size) == 0 && c.hidden_dim % (256 * size) == 0,
+                 CN_ERR_INVALID_ARG,
+                 "the model does not shard over %d ranks (kv heads, hidden_dim and vocab must divide, and O/down "
+                 "inputs must split into whole 256-weight blocks)", size);
     for (int i = 0; i < n; i++) {
         int idx;
-        if (i == 1 && cn_gguf_find(g, names[i].c_str(), &idx) != CN_OK) {
+        const bool tied = i == 1 && cn_gguf_find(g, names[i].c_str(), &idx) != CN_OK;
+        if (tied && size == 1) {
             ts[1] = ts[0];  // tied lm_head (LlamaWeights.cs:89-98)
             continue;
         }
-        if ((rc = cn_gguf_upload(ctx, g, names[i].c_str(), &ts[i]))) {
+        // a tied lm_head under tensor parallelism: this rank's vocabulary rows of token_embd
+        const char* nm = tied ? "token_embd.weight" : names[i].c_str();
+        if (size == 1) {
+            rc = cn_gguf_upload(ctx, g, nm, &ts[i]);
+        } else {
+            if ((rc = cn_gguf_find(g, nm, &idx))) {
+                release();
+                return rc;
+            }
+            const Tensor& t = g->tensors[idx];
+            if (!type_supported(t.type)) {
+                release();
+                return set_error(CN_ERR_UNSUPPORTED, "tensor %s: ggml type %d not supported", nm, t.type);
+            }
+            int64_t rows, cols, r0, nr, c0, nc;
+            tensor_shape(t, &rows, &cols);
+            shard_region(names[i].c_str(), rows, cols, rank, size, &r0, &nr, &c0, &nc);
+            const uint8_t* src = static_cast<const uint8_t*>(g->map) + g->data_off + t.offset;
+            rc = cn_tensor_upload_slice(ctx, src, t.bytes, t.type, rows, cols, r0, nr, c0, nc, &ts[i]);
+        }
+        if (rc) {
             release();
             return rc;
         }
     }
-    rc = cn_llama_create(ctx, &c, ts.data(), n, out);
+    rc = tp ? cn_llama_create_tp(ctx, &c, ts.data(), n, tp, out) : cn_llama_create(ctx, &c, ts.data(), n, out);
     if (rc) {
         release();
         return rc;
     }
     for (int i = 0; i < n; i++) tensors_out[i] = ts[i];
     return CN_OK;
+}
+
+int cn_llama_create_from_gguf(cn_ctx* ctx, const cn_gguf* g, int max_batch, int kv_dtype, cn_llama** out,
+                              cn_tensor** tensors_out, int n_tensors_out) {
+    return create_from_gguf(ctx, g, nullptr, max_batch, kv_dtype, out, tensors_out, n_tensors_out);
+}
+
+int cn_llama_create_from_gguf_tp(cn_ctx* ctx, const cn_gguf* g, cn_tp* tp, int max_batch, int kv_dtype,
+                                 cn_llama** out, cn_tensor** tensors_out, int n_tensors_out) {
+    CN_CHECK(tp, CN_ERR_INVALID_ARG, "null tensor-parallel group");
+    return create_from_gguf(ctx, g, tp, max_batch, kv_dtype, out, tensors_out, n_tensors_out);
 }
 
 }  // extern "C"

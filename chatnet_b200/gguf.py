@@ -86,22 +86,29 @@ class GgufFile:
         rows, cols = info.shape
         return ctx._own(Tensor(ctx, h.value, info.type, rows, cols))
 
-    def llama_model(self, ctx, max_batch: int = 1, kv_f16: bool = False) -> CudaLlamaModel:
-        """The whole decoder from this file (cn_llama_create_from_gguf)."""
+    def llama_model(self, ctx, max_batch: int = 1, kv_f16: bool = False, tp=None) -> CudaLlamaModel:
+        """The whole decoder from this file (cn_llama_create_from_gguf), or,
+        with a connected TensorParallel group, this rank's shards of it
+        (cn_llama_create_from_gguf_tp)."""
         from . import Tensor
         cfg = self.llama_config(max_batch, kv_f16)
         n = 3 + 9 * cfg.n_layers
         arr = (C.c_void_p * n)()
         h = C.c_void_p()
-        check(N.lib().cn_llama_create_from_gguf(ctx.handle, self.handle, max_batch, N.KV_F16 if kv_f16 else N.KV_F32,
-                                                C.byref(h), arr, n), "cn_llama_create_from_gguf")
+        kv = N.KV_F16 if kv_f16 else N.KV_F32
+        if tp is None:
+            check(N.lib().cn_llama_create_from_gguf(ctx.handle, self.handle, max_batch, kv, C.byref(h), arr, n),
+                  "cn_llama_create_from_gguf")
+        else:
+            check(N.lib().cn_llama_create_from_gguf_tp(ctx.handle, self.handle, tp.handle, max_batch, kv, C.byref(h),
+                                                       arr, n), "cn_llama_create_from_gguf_tp")
         seen, tensors = {}, []
         for v in arr:
             if v not in seen:
                 seen[v] = ctx._own(Tensor(ctx, v, 0, 0, 0))
             tensors.append(seen[v])
         model = CudaLlamaModel.__new__(CudaLlamaModel)
-        model.ctx, model.cfg, model.tp = ctx, cfg, None
+        model.ctx, model.cfg, model.tp = ctx, cfg, tp
         model._tensors = tensors
         model.handle = h.value
         return model

@@ -104,6 +104,17 @@ int cn_synchronize(cn_ctx* ctx);
 int cn_tensor_upload(cn_ctx* ctx, const void* host_blocks, uint64_t bytes, int type,
                      int64_t rows, int64_t cols, cn_tensor** out);
 
+/* Uploads the region [row0, row0 + nrows) x [col0, col0 + ncols) of a host
+ * tensor of rows x cols (bytes = rows * cn_byte_size(type, cols), e.g. the
+ * pointer MemoryMappedWeights.GetTensorPointer returns, Memory/
+ * MemoryMappedWeights.cs:76) as a tensor of its own: a tensor-parallel rank's
+ * shard.  Columns must cover whole blocks (32 or 256 weights); the rows are
+ * copied with one strided copy, no host staging.  (no reference
+ * counterpart: the reference runs on one CPU) */
+int cn_tensor_upload_slice(cn_ctx* ctx, const void* host_blocks, uint64_t bytes, int type, int64_t rows,
+                           int64_t cols, int64_t row0, int64_t nrows, int64_t col0, int64_t ncols,
+                           cn_tensor** out);
+
 /* Allocates a tensor and fills it on the device with the seeded synthetic
  * generator (cn_synth_fill); no host copy.  (no reference counterpart:
  * synthetic inputs for the benchmark configs) */
@@ -403,6 +414,14 @@ int cn_gguf_upload(cn_ctx* ctx, const cn_gguf* g, const char* name, cn_tensor** 
  * after cn_llama_destroy. */
 int cn_llama_create_from_gguf(cn_ctx* ctx, const cn_gguf* g, int max_batch, int kv_dtype,
                               cn_llama** out, cn_tensor** tensors_out, int n_tensors_out);
+/* cn_llama_create_from_gguf for tensor-parallel rank tp->rank of tp->size
+ * (a connected group, see below): uploads only this rank's shard of every
+ * projection straight from the mapped file (cn_tensor_upload_slice; a tied
+ * lm_head takes this rank's vocabulary rows of token_embd) and builds the
+ * rank's model with cn_llama_create_tp.  (no reference counterpart) */
+typedef struct cn_tp cn_tp;
+int cn_llama_create_from_gguf_tp(cn_ctx* ctx, const cn_gguf* g, cn_tp* tp, int max_batch, int kv_dtype,
+                                 cn_llama** out, cn_tensor** tensors_out, int n_tensors_out);
 
 /* ---- tensor parallelism (one process per GPU) ---------------------------
  * (no reference counterpart: the reference runs on one CPU.)  Rank r of a
@@ -417,7 +436,6 @@ int cn_llama_create_from_gguf(cn_ctx* ctx, const cn_gguf* g, int max_batch, int 
  * then cn_llama_create_tp.  All ranks must then run the same sequence of
  * steps; a rank that stops makes the others' kernels give up after ~2 s
  * (CN_ERR_TIMEOUT), after which the group must be rebuilt. */
-typedef struct cn_tp cn_tp;
 #define CN_TP_HANDLE_BYTES 64
 int cn_tp_create(cn_ctx* ctx, int rank, int size, int max_batch, int dim, int vocab, cn_tp** out);
 int cn_tp_handle(const cn_tp* tp, void* handle_out /* CN_TP_HANDLE_BYTES */);
