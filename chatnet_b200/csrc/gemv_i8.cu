@@ -40,7 +40,6 @@ namespace i8 {
 constexpr int kRows = 128;
 constexpr int kRaw = 144 * kRows;  // raw Q4_K bytes per unit per tile
 constexpr int kCons = 8;           // consumer warps, 16 rows each
-constexpr int kThreads = (kCons + 1) * 32;
 
 // Three CTAs per SM with three stages each when one n-tile of activation
 // digits suffices (batch 1, 2), else two CTAs with four stages.  DEEP: one
@@ -251,7 +250,6 @@ __global__ void __launch_bounds__(i8::Geo<NB, DEEP>::kThreads, i8::Geo<NB, DEEP>
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStage);
     uint64_t* empty = full + kStages;
-    int* bcast = reinterpret_cast<int*>(empty + kStages);
     float* xg = reinterpret_cast<float*>(smem + kStages * kStage + 256);  // [2][kCons][32][NT]
     constexpr int kGroups = G::kGroups;
 
@@ -516,30 +514,42 @@ __global__ void __launch_bounds__(i8::Geo<NB, DEEP>::kThreads, i8::Geo<NB, DEEP>
 
 // ---- host ---------------------------------------------------------------------------
 
-// Fewest units a CTA should get (CHATNET_GEMV_MIN_UNITS, default 2): small
-// GEMVs then use fewer, longer-running CTAs.
+// Grid-sizing knobs.  Builds with -DCHATNET_TUNING read three environment
+// overrides for grid experiments (CHATNET_GEMV_CTAS: a fixed grid;
+// CHATNET_GEMV_TILE_CAP: most CTAs sharing a tile; CHATNET_GEMV_MIN_UNITS:
+// fewest units per CTA); product builds use the measured defaults.
+#ifdef CHATNET_TUNING
+static int env_int(const char* name, int fallback) {
+    const char* e = getenv(name);
+    return e ? atoi(e) : fallback;
+}
+#endif
+
+// Fewest units a CTA should get (2): small GEMVs then use fewer, longer-running CTAs.
 static int min_units_per_cta() {
-    static int v = -1;
-    if (v < 0) {
-        const char* e = getenv("CHATNET_GEMV_MIN_UNITS");
-        v = e ? atoi(e) : 2;
-        if (v < 1) v = 1;
-    }
+#ifdef CHATNET_TUNING
+    static const int v = env_int("CHATNET_GEMV_MIN_UNITS", 2) < 1 ? 1 : env_int("CHATNET_GEMV_MIN_UNITS", 2);
     return v;
+#else
+    return 2;
+#endif
 }
 
-// Most CTAs that share one tile for batches of two n-tiles or more
-// (CHATNET_GEMV_TILE_CAP overrides, for every batch): 7, but 1 when a row has
-// at most 16 units, where the split-K fix-up of a shared tile costs more than
-// its extra parallelism saves.
+// A fixed most-CTAs-per-tile override (tuning builds), or -1.
 static int tile_cap_env() {
-    static int v = -2;
-    if (v == -2) {
-        const char* e = getenv("CHATNET_GEMV_TILE_CAP");
-        v = e ? (atoi(e) < 1 ? 1 : atoi(e)) : -1;
-    }
+#ifdef CHATNET_TUNING
+    static const int v = getenv("CHATNET_GEMV_TILE_CAP") ? (env_int("CHATNET_GEMV_TILE_CAP", 1) < 1
+                                                                ? 1 : env_int("CHATNET_GEMV_TILE_CAP", 1))
+                                                          : -1;
     return v;
+#else
+    return -1;
+#endif
 }
+
+// Most CTAs that share one tile for batches of two n-tiles or more: 7, but 1
+// when a row has at most 16 units, where the split-K fix-up of a shared tile
+// costs more than its extra parallelism saves.
 static int tile_share_cap(int units) {
     const int v = tile_cap_env();
     if (v > 0) return v;
@@ -548,10 +558,10 @@ static int tile_share_cap(int units) {
 
 int gemv_i8_ctas(int sms, int tiles, int units, int batch) {
     const int per_sm = i8::n_tiles(batch) == 1 ? i8::Geo<1>::kCtasPerSm : i8::Geo<8>::kCtasPerSm;
-    if (const char* e = getenv("CHATNET_GEMV_CTAS")) {  // experiments: a fixed grid
-        const int v = atoi(e);
-        if (v > 0) return v < per_sm * sms ? v : per_sm * sms;
-    }
+#ifdef CHATNET_TUNING
+    if (const int v = env_int("CHATNET_GEMV_CTAS", 0); v > 0)  // experiments: a fixed grid
+        return v < per_sm * sms ? v : per_sm * sms;
+#endif
     const int64_t total = (int64_t)tiles * units;
     // One n-tile of activation digits (batch 1, 2): at most one CTA per SM,
     // which then runs the deep pipeline (gemv_i8_run_group).  With at least
