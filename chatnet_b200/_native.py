@@ -145,7 +145,8 @@ class LlamaConfigC(C.Structure):
     """cn_llama_config (include/chatnet_cuda.h)."""
     _fields_ = [("dim", _i), ("hidden_dim", _i), ("n_layers", _i), ("n_heads", _i),
                 ("n_kv_heads", _i), ("head_dim", _i), ("vocab", _i), ("ctx_len", _i),
-                ("rope_base", _f), ("rms_eps", _f), ("kv_dtype", _i), ("max_batch", _i)]
+                ("rope_base", _f), ("rms_eps", _f), ("kv_dtype", _i), ("max_batch", _i),
+                ("rope_neox", _i), ("act_gelu", _i), ("norm_offset", _i)]
 
 _lib = None
 

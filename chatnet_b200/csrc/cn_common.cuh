@@ -249,6 +249,18 @@ inline cudaError_t launch_k(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
+// The FFN activation times up, with the reference's operation order:
+// SiluElementwiseMul (TensorMath.cs:253-286) g / (1 + exp(-g)) * u, or
+// GeluElementwiseMul (TensorMath.cs:294-333)
+// 0.5 g (1 + tanh(sqrt(2/pi) (g + 0.044715 g^3))) * u, each evaluated left to
+// right with one rounding per operation.
+__device__ __forceinline__ float act_mul(float g, float u, int gelu) {
+    if (!gelu) return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+    const float c3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, g), g), g);
+    const float t = tanhf(__fmul_rn(0.7978845608028654f, __fadd_rn(g, c3)));
+    return __fmul_rn(__fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.0f, t)), u);
+}
+
 // launch_k with a thread-block cluster of cluster_x CTAs along x (grid.x a
 // multiple of it).
 template <typename... KArgs, typename... Args>

@@ -143,13 +143,13 @@ int to_half_rows(cudaStream_t st, const float* x, __half* y, float* inv, int n, 
 int prefill_norm(cudaStream_t st, const float* x, const float* w, __half* y, float* inv, int n, int M,
                  float eps, __half* ylo = nullptr);
 int prefill_silu(cudaStream_t st, const float* g, const float* u, __half* h, float* inv, int n, int M,
-                 __half* hlo = nullptr);
+                 __half* hlo = nullptr, int gelu = 0);
 // RoPE of the M prompt tokens' q (in place) and k, k/v into the cache and
 // their fp16 copies into kh/vh [M][kvdim] (with kl/vl, also k's and v's fp16
 // residuals).
 int prefill_rope(cudaStream_t st, float* q, const float* k, const float* v, const float2* rope, int pos0, int M,
                  int qdim, int kvdim, int hd, void* kcache, void* vcache, int64_t cache_off, bool kv_f16, __half* kh,
-                 __half* vh, __half* kl = nullptr, __half* vl = nullptr);
+                 __half* vh, __half* kl = nullptr, __half* vl = nullptr, int neox = 0);
 // Causal prefill attention; split: q, k (and, for fp32 caches, v) as hi + lo
 // fp16 pairs (kl / vl: k's and v's residuals, needed for fp32 caches), and
 // the output's residuals into out_lo when given.

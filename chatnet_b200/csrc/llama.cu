@@ -81,6 +81,9 @@ struct cn_llama {
     // low halves: of the current matmul input rows, and of the new k and v
     // rows (fp32 caches)
     __half *pf_hl = nullptr, *pf_kl = nullptr, *pf_vl = nullptr;
+    // norm_offset models: the RMSNorm weights + 1 ([layer][2][dim], then the
+    // output norm), so every norm kernel runs unchanged
+    float* normw = nullptr;
     float *pf_x = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_g = nullptr,
           *pf_u = nullptr;
     __half *pf_h = nullptr, *pf_kh = nullptr, *pf_vh = nullptr;
@@ -91,6 +94,14 @@ struct cn_llama {
 namespace cn {
 
 static const cn_tensor* LT(const cn_llama* m, int l, int j) { return m->t[3 + 9 * l + j]; }
+
+// RMSNorm weights: layer l's attn_norm (which 0) or ffn_norm (1), or the
+// output norm (l < 0) -- the model's (w + 1) copies for norm_offset models.
+static const float* norm_w(const cn_llama* m, int l, int which) {
+    const int dim = m->cfg.dim;
+    if (m->normw) return m->normw + (l < 0 ? (size_t)2 * m->cfg.n_layers * dim : ((size_t)2 * l + which) * dim);
+    return static_cast<const float*>(l < 0 ? m->t[2]->d : LT(m, l, which ? 5 : 0)->d);
+}
 
 static int check_shape(const cn_tensor* t, const char* name, int64_t rows, int64_t cols,
                        bool f32_vector) {
@@ -197,11 +208,11 @@ static int gemv(cn_llama* m, cudaStream_t s, const GemvOp& op, const float* x, f
 // the current stream; with a delta it moves to the other buffer.
 // (With tensor parallelism the pending delta is the exchange `xin`: the
 // sum of every rank's partial output.)
-static int norm(cn_llama* m, cudaStream_t s, const cn_tensor* w, int B, const GemvOp& next, float** x,
+static int norm(cn_llama* m, cudaStream_t s, const float* w, int B, const GemvOp& next, float** x,
                 const float** delta, PrepCache& pc, const XchgIn* xin = nullptr) {
     const bool add = *delta || (xin && xin->size > 1);
     float* out = add ? (*x == m->x ? m->x2 : m->x) : nullptr;
-    int rc = add_norm_prep(s, *x, xin && xin->size > 1 ? nullptr : *delta, out, (const float*)w->d, m->xn,
+    int rc = add_norm_prep(s, *x, xin && xin->size > 1 ? nullptr : *delta, out, w, m->xn,
                            m->cfg.dim, B, m->cfg.rms_eps, &next, m->gb, xin);
     if (rc) return rc;
     if (add) *x = out;
@@ -253,7 +264,7 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
     XchgIn xin;                    // tensor parallel: the exchange that delivers it
     for (int l = 0; l < c.n_layers; l++) {
         const GemvOp* ops = &st.ops[(size_t)l * 7];
-        if ((rc = norm(m, s, LT(m, l, L_ANORM), B, ops[0], &x, &delta, pc, &xin)) || (rc = mark(s, P_NORM)))
+        if ((rc = norm(m, s, norm_w(m, l, 0), B, ops[0], &x, &delta, pc, &xin)) || (rc = mark(s, P_NORM)))
             return rc;
         xin = XchgIn();
         if (st.qkv[l].n) {
@@ -285,6 +296,7 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
         ra.kv_f16 = c.kv_dtype == CN_KV_F16;
         ra.ctx_len = c.ctx_len;
         ra.err = m->ctx->dev_err;
+        ra.neox = c.rope_neox;
         // the tensor-core attention (fp16 cache) rotates q and stores the new
         // k/v rows itself; otherwise RoPE and the cache store run first
         const bool fuse_rope = st.ap.mma;
@@ -315,6 +327,7 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
             aa.rope.rope = m->rope;
             aa.rope.kv_stride = kvd;
             aa.rope.on = 1;
+            aa.rope.neox = c.rope_neox;
         }
         if ((m->nh / m->nkv) * c.head_dim % 256 != 0) aa.prep.kind = -1;
         if ((rc = launch_attention(aa, st.ap, s)) || (rc = mark(s, P_ATTN))) return rc;
@@ -329,7 +342,7 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
             delta = m->tmp;
         }
         if ((rc = mark(s, P_O))) return rc;
-        if ((rc = norm(m, s, LT(m, l, L_FNORM), B, ops[4], &x, &delta, pc, &xin)) || (rc = mark(s, P_NORM)))
+        if ((rc = norm(m, s, norm_w(m, l, 1), B, ops[4], &x, &delta, pc, &xin)) || (rc = mark(s, P_NORM)))
             return rc;
         xin = XchgIn();
         if (st.gu[l].n) {
@@ -341,7 +354,7 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
         }
         if ((rc = mark(s, P_GATEUP))) return rc;
         const PrepTarget spt = prep_target(&ops[6], m->gb);
-        if ((rc = launch_silu_prep(m->gate, m->up, hid, B, spt, s)) || (rc = mark(s, P_SILU))) return rc;
+        if ((rc = launch_silu_prep(m->gate, m->up, hid, B, spt, s, c.act_gelu)) || (rc = mark(s, P_SILU))) return rc;
         pc = PrepCache();
         if (spt.kind >= 0 && hid % 256 == 0) pc.set(m->gate, ops[6]);
         if (tp) {
@@ -355,7 +368,7 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
         if ((rc = mark(s, P_DOWN))) return rc;
     }
     const GemvOp& head = st.ops[(size_t)c.n_layers * 7];
-    if ((rc = norm(m, s, m->t[T_ONORM], B, head, &x, &delta, pc, &xin)) || (rc = mark(s, P_NORM))) return rc;
+    if ((rc = norm(m, s, norm_w(m, -1, 0), B, head, &x, &delta, pc, &xin)) || (rc = mark(s, P_NORM))) return rc;
     if (tp) {
         // lm_head rows of this rank go to every rank's logits (all-gather)
         const XchgOut xo = tp_gather_out(m->tp, m->vocab_l, uses, uses - 1u, 2);
@@ -440,7 +453,7 @@ static void free_model(cn_llama* m) {
                     m->gate, m->up, m->logits, m->part, m->tokens, m->pos, m->amax,
                     m->gb.xfrag, m->gb.xsum, m->gb.partials, m->gb.counters, m->gb.xinv,
                     m->pf_x, m->pf_q, m->pf_k, m->pf_v, m->pf_g, m->pf_u, m->pf_h, m->pf_kh, m->pf_vh,
-                    m->pf_tok, m->pf_xs, m->pf_hl, m->pf_kl, m->pf_vl};
+                    m->pf_tok, m->pf_xs, m->pf_hl, m->pf_kl, m->pf_vl, m->normw};
     for (void* p : bufs) cudaFree(p);
     cudaFreeHost(m->h_tokens);
     cudaFreeHost(m->h_pos);
@@ -588,7 +601,7 @@ static int prefill_layers(cn_llama* m, int n, int pos) {
     if ((attn_split || ffn_split) && (rc = prefill_scales(m))) return rc;
     for (int l = 0; l < c.n_layers; l++) {
         const int64_t cache_off = (int64_t)l * c.ctx_len * kvd;  // sequence slot 0
-        if ((rc = prefill_norm(s, m->pf_x, (const float*)LT(m, l, L_ANORM)->d, m->pf_h, m->pf_xs, c.dim, n,
+        if ((rc = prefill_norm(s, m->pf_x, norm_w(m, l, 0), m->pf_h, m->pf_xs, c.dim, n,
                                c.rms_eps, attn_split ? m->pf_hl : nullptr)))
             return rc;
         {
@@ -597,7 +610,7 @@ static int prefill_layers(cn_llama* m, int n, int pos) {
             if ((rc = mm_group(m, l, 3, kSlotsQKV, rows, c.dim, n, y, rows, false, true, false, ns[0]))) return rc;
         }
         if ((rc = prefill_rope(s, m->pf_q, m->pf_k, m->pf_v, m->rope, pos, n, qd, kvd, c.head_dim, m->kc, m->vc,
-                               cache_off, kv16, m->pf_kh, m->pf_vh, kl, vl)))
+                               cache_off, kv16, m->pf_kh, m->pf_vh, kl, vl, c.rope_neox)))
             return rc;
         if ((rc = prefill_attention(s, m->pf_q, qd, m->kc, m->vc, kv16, cache_off, m->nh, m->nkv, c.head_dim, n,
                                     pos, m->pf_kh, m->pf_vh, m->pf_h, qd, attn_split, kl, vl,
@@ -607,7 +620,7 @@ static int prefill_layers(cn_llama* m, int n, int pos) {
             const int64_t rows = c.dim;
             if ((rc = mm_group(m, l, 1, kSlotsO, &rows, qd, n, &m->pf_x, &rows, true, false, false, ns[1]))) return rc;
         }
-        if ((rc = prefill_norm(s, m->pf_x, (const float*)LT(m, l, L_FNORM)->d, m->pf_h, m->pf_xs, c.dim, n,
+        if ((rc = prefill_norm(s, m->pf_x, norm_w(m, l, 1), m->pf_h, m->pf_xs, c.dim, n,
                                c.rms_eps, ffn_split ? m->pf_hl : nullptr)))
             return rc;
         {
@@ -615,7 +628,8 @@ static int prefill_layers(cn_llama* m, int n, int pos) {
             float* y[2] = {m->pf_g, m->pf_u};
             if ((rc = mm_group(m, l, 2, kSlotsGU, rows, c.dim, n, y, rows, false, true, false, ns[2]))) return rc;
         }
-        if ((rc = prefill_silu(s, m->pf_g, m->pf_u, m->pf_h, m->pf_xs, hid, n, ffn_split ? m->pf_hl : nullptr)))
+        if ((rc = prefill_silu(s, m->pf_g, m->pf_u, m->pf_h, m->pf_xs, hid, n, ffn_split ? m->pf_hl : nullptr,
+                               c.act_gelu)))
             return rc;
         {
             const int64_t rows = c.dim;
@@ -665,6 +679,10 @@ static int create_model(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* cons
              "max_batch %d outside [1, %d]", c.max_batch, kMaxBatch);
     CN_CHECK(c.kv_dtype == CN_KV_F32 || c.kv_dtype == CN_KV_F16, CN_ERR_INVALID_ARG,
              "bad kv_dtype %d", c.kv_dtype);
+    CN_CHECK((c.rope_neox == 0 || c.rope_neox == 1) && (c.act_gelu == 0 || c.act_gelu == 1) &&
+                 (c.norm_offset == 0 || c.norm_offset == 1),
+             CN_ERR_INVALID_ARG, "rope_neox, act_gelu and norm_offset are 0 or 1");
+    CN_CHECK(!c.rope_neox || c.head_dim % 8 == 0, CN_ERR_UNSUPPORTED, "split-half RoPE needs head_dim %% 8 == 0");
     CN_CHECK(n_tensors == CN_LLAMA_TENSORS(c.n_layers), CN_ERR_INVALID_ARG,
              "expected %d tensors, got %d", CN_LLAMA_TENSORS(c.n_layers), n_tensors);
     if (tp) {
@@ -744,6 +762,21 @@ static int create_model(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* cons
         cudaError_t e = cudaMemcpy(m->rope, tab.data(), tab.size() * sizeof(float2),
                                    cudaMemcpyHostToDevice);
         if (e != cudaSuccess) return fail(cuda_error(e, "rope upload"));
+    }
+    if (c.norm_offset) {
+        // RmsNormWithOffset (TensorMath.cs:335-394) scales by (weight + 1): the
+        // sums are formed once here, in fp32 as the reference forms them
+        const size_t per = (size_t)c.dim;
+        if ((rc = dmalloc((void**)&m->normw, (2 * (size_t)c.n_layers + 1) * per * 4, false))) return fail(rc);
+        for (int l = 0; l <= c.n_layers; l++)
+            for (int which = 0; which < (l < c.n_layers ? 2 : 1); which++) {
+                const float* src = static_cast<const float*>(l < c.n_layers ? LT(m, l, which ? L_FNORM : L_ANORM)->d
+                                                                             : m->t[T_ONORM]->d);
+                float* dst = m->normw + (l < c.n_layers ? (2 * (size_t)l + which) * per : 2 * (size_t)c.n_layers * per);
+                if ((rc = launch_add_scalar(dst, src, 1.0f, (int64_t)per, ctx->stream))) return fail(rc);
+            }
+        cudaError_t e0 = cudaStreamSynchronize(ctx->stream);
+        if (e0 != cudaSuccess) return fail(cuda_error(e0, "norm offset"));
     }
     const size_t fd = (size_t)B * c.dim * 4, fq = (size_t)B * qdim * 4, fk = (size_t)B * kvd * 4,
                  fh = (size_t)B * hid * 4;
@@ -1132,7 +1165,7 @@ int cn_llama_forward(cn_llama* m, const int* tokens, int n, int pos, float* logi
                                m->ctx->dev_err, s)))
             return rc;
         if ((rc = prefill_layers(m, n, pos))) return rc;
-        if ((rc = launch_rmsnorm(m->pf_x + (size_t)(n - 1) * c.dim, (const float*)m->t[T_ONORM]->d, m->xn,
+        if ((rc = launch_rmsnorm(m->pf_x + (size_t)(n - 1) * c.dim, norm_w(m, -1, 0), m->xn,
                                  c.dim, 1, c.rms_eps, s)))
             return rc;
         const cn_tensor* w = m->t[T_OUT];

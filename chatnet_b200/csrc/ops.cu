@@ -85,7 +85,7 @@ __global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ 
                                const int* __restrict__ pos_dev, int pos_host, int n_heads,
                                int n_kv, int hd, int q_stride, int kv_stride, void* kcache,
                                void* vcache, int64_t cache_seq_stride, int64_t cache_layer_off,
-                               int kv_f16, int ctx_len, uint32_t* err) {
+                               int kv_f16, int ctx_len, uint32_t* err, int neox) {
     pdl_trigger();
     pdl_wait();
     const int b = blockIdx.y;
@@ -99,28 +99,33 @@ __global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ 
     const int total = (n_heads + n_kv) * half + n_kv * hd;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
         const int64_t base = (int64_t)b * cache_seq_stride + cache_layer_off + (int64_t)pos * n_kv * hd;
+        // pair p: elements (2p, 2p + 1), or (p, p + half) for split-half RoPE
+        // (ApplyRoPENeox); the table is the same, since 2p * (1/hd) and
+        // p * (2/hd) are the same fp32 value
         if (i < n_heads * half) {
             int h = i / half, p = i % half;
-            float* vec = q + (size_t)b * q_stride + h * hd + 2 * p;
+            const int ia = neox ? p : 2 * p, ib = neox ? p + half : 2 * p + 1;
+            float* vec = q + (size_t)b * q_stride + h * hd;
             float2 cs = tab[p];
-            float x0 = vec[0], x1 = vec[1];
-            vec[0] = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
-            vec[1] = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+            float x0 = vec[ia], x1 = vec[ib];
+            vec[ia] = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+            vec[ib] = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
         } else if (i < (n_heads + n_kv) * half) {
             int j = i - n_heads * half;
             int h = j / half, p = j % half;
-            const float* vec = k + (size_t)b * kv_stride + h * hd + 2 * p;
+            const int ia = neox ? p : 2 * p, ib = neox ? p + half : 2 * p + 1;
+            const float* vec = k + (size_t)b * kv_stride + h * hd;
             float2 cs = tab[p];
-            float x0 = vec[0], x1 = vec[1];
+            float x0 = vec[ia], x1 = vec[ib];
             float r0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
             float r1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
-            int64_t off = base + h * hd + 2 * p;
+            int64_t off = base + h * hd;
             if (kv_f16) {
-                reinterpret_cast<__half*>(kcache)[off] = __float2half_rn(r0);
-                reinterpret_cast<__half*>(kcache)[off + 1] = __float2half_rn(r1);
+                reinterpret_cast<__half*>(kcache)[off + ia] = __float2half_rn(r0);
+                reinterpret_cast<__half*>(kcache)[off + ib] = __float2half_rn(r1);
             } else {
-                reinterpret_cast<float*>(kcache)[off] = r0;
-                reinterpret_cast<float*>(kcache)[off + 1] = r1;
+                reinterpret_cast<float*>(kcache)[off + ia] = r0;
+                reinterpret_cast<float*>(kcache)[off + ib] = r1;
             }
         } else {
             int d = i - (n_heads + n_kv) * half;
@@ -510,13 +515,14 @@ __global__ void __launch_bounds__(kAttnThreads)
             __half* vw = const_cast<__half*>(vbase) + (int64_t)pos * kvdim;
             for (int p = tid; p < HD / 2; p += kAttnThreads) {
                 const float2 cs = tab[p];
-                const float x0 = kr[2 * p], x1 = kr[2 * p + 1];
+                const int ia = ri.neox ? p : 2 * p, ib = ri.neox ? p + HD / 2 : 2 * p + 1;
+                const float x0 = kr[ia], x1 = kr[ib];
                 const __half h0 = __float2half_rn(__fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y)));
                 const __half h1 = __float2half_rn(__fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x)));
-                Ks[r_new * RS + 2 * p] = h0;
-                Ks[r_new * RS + 2 * p + 1] = h1;
-                kw[2 * p] = h0;
-                kw[2 * p + 1] = h1;
+                Ks[r_new * RS + ia] = h0;
+                Ks[r_new * RS + ib] = h1;
+                kw[ia] = h0;
+                kw[ib] = h1;
                 const __half v0 = __float2half_rn(vr[2 * p]), v1 = __float2half_rn(vr[2 * p + 1]);
                 Vs[r_new * RS + 2 * p] = v0;
                 Vs[r_new * RS + 2 * p + 1] = v1;
@@ -528,11 +534,13 @@ __global__ void __launch_bounds__(kAttnThreads)
         // (rotated here when ri.on, as rope_kv_kernel would have)
         for (int i = tid; i < 8 * HD / 2; i += kAttnThreads) {
             const int gi = i / (HD / 2), p = i % (HD / 2);
+            // the pair's elements: (2p, 2p + 1), or (p, p + HD/2) for split-half RoPE
+            const int ia = ri.on && ri.neox ? p : 2 * p, ib = ri.on && ri.neox ? p + HD / 2 : 2 * p + 1;
             float v0 = 0.f, v1 = 0.f;
             if (gi < kv_mul) {
                 const float* qr = q + (size_t)b * q_stride + (kh * kv_mul + gi) * HD;
-                v0 = qr[2 * p];
-                v1 = qr[2 * p + 1];
+                v0 = qr[ia];
+                v1 = qr[ib];
                 if (ri.on) {
                     const float2 cs = ri.rope[(size_t)pos * (HD / 2) + p];
                     const float r0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
@@ -542,10 +550,10 @@ __global__ void __launch_bounds__(kAttnThreads)
                 }
             }
             const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
-            Qs[gi * RS + 2 * p] = h0;
-            Qs[gi * RS + 2 * p + 1] = h1;
-            Qs[(8 + gi) * RS + 2 * p] = __float2half_rn(v0 - __half2float(h0));
-            Qs[(8 + gi) * RS + 2 * p + 1] = __float2half_rn(v1 - __half2float(h1));
+            Qs[gi * RS + ia] = h0;
+            Qs[gi * RS + ib] = h1;
+            Qs[(8 + gi) * RS + ia] = __float2half_rn(v0 - __half2float(h0));
+            Qs[(8 + gi) * RS + ib] = __float2half_rn(v1 - __half2float(h1));
         }
         asm volatile("cp.async.wait_group 0;" ::: "memory");
         __syncthreads();
@@ -649,21 +657,18 @@ __global__ void __launch_bounds__(kAttnThreads)
 
 // ---- elementwise -----------------------------------------------------------------
 
-__global__ void silu_mul_kernel(float* __restrict__ gate, const float* __restrict__ up, int64_t n) {
+__global__ void silu_mul_kernel(float* __restrict__ gate, const float* __restrict__ up, int64_t n, int gelu) {
     pdl_trigger();
     pdl_wait();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        float x = gate[i];
-        float s = __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
-        gate[i] = __fmul_rn(s, up[i]);
-    }
+         i += (int64_t)gridDim.x * blockDim.x)
+        gate[i] = act_mul(gate[i], up[i], gelu);
 }
 
 // SiluElementwiseMul fused with the prep of its output: one warp per
 // (256-position unit, row); the lanes hold the values in the record layout.
 __global__ void silu_prep_kernel(float* __restrict__ gate, const float* __restrict__ up, int n, int batch,
-                                 PrepTarget pt) {
+                                 PrepTarget pt, int gelu) {
     pdl_trigger();
     pdl_wait();
     const int lane = threadIdx.x & 31;
@@ -683,15 +688,19 @@ __global__ void silu_prep_kernel(float* __restrict__ gate, const float* __restri
             const float* uv = reinterpret_cast<const float*>(&u4);
 #pragma unroll
             for (int k = 0; k < 4; k++) {
-                const float x = gv[k];
-                const float s = __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
-                gv[k] = __fmul_rn(s, uv[k]);
+                gv[k] = act_mul(gv[k], uv[k], gelu);
                 v[4 * h + k] = gv[k];
             }
             *reinterpret_cast<float4*>(gate + off + 16 * h) = g4;
         }
         emit_any(pt, v, u, b, batch, lane);
     }
+}
+
+__global__ void add_scalar_kernel(float* __restrict__ dst, const float* __restrict__ src, float c, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = __fadd_rn(src[i], c);
 }
 
 __global__ void add_kernel(float* __restrict__ a, const float* __restrict__ b, int64_t n) {
@@ -817,7 +826,7 @@ int launch_rope_kv(const RopeKvArgs& a, cudaStream_t s) {
     dim3 grid(grid_1d(total, 256, 64), a.batch);
     CN_CUDA(launch_k(true, rope_kv_kernel, grid, dim3(256), 0, s, a.q, a.k, a.v, a.rope, a.pos_dev, a.pos_host,
                      a.n_heads, a.n_kv, a.hd, a.q_stride, a.kv_stride, a.kcache, a.vcache, a.cache_seq_stride,
-                     a.cache_layer_off, a.kv_f16, a.ctx_len, a.err));
+                     a.cache_layer_off, a.kv_f16, a.ctx_len, a.err, a.neox));
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }
@@ -902,17 +911,24 @@ int launch_attention(const AttnArgs& a, const AttnPlan& p, cudaStream_t s) {
     return CN_OK;
 }
 
-int launch_silu_mul(float* gate, const float* up, int64_t n, cudaStream_t s) {
-    CN_CUDA(launch_k(true, silu_mul_kernel, dim3(grid_1d(n, 256, 148 * 8)), dim3(256), 0, s, gate, up, n));
+int launch_silu_mul(float* gate, const float* up, int64_t n, cudaStream_t s, int gelu) {
+    CN_CUDA(launch_k(true, silu_mul_kernel, dim3(grid_1d(n, 256, 148 * 8)), dim3(256), 0, s, gate, up, n, gelu));
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }
 
-int launch_silu_prep(float* gate, const float* up, int n, int batch, const PrepTarget& pt, cudaStream_t s) {
-    if (pt.kind < 0 || n % 256 != 0) return launch_silu_mul(gate, up, (int64_t)n * batch, s);
+int launch_silu_prep(float* gate, const float* up, int n, int batch, const PrepTarget& pt, cudaStream_t s,
+                     int gelu) {
+    if (pt.kind < 0 || n % 256 != 0) return launch_silu_mul(gate, up, (int64_t)n * batch, s, gelu);
     const int64_t items = (int64_t)(n / 256) * batch;
     CN_CUDA(launch_k(true, silu_prep_kernel, dim3((unsigned)((items + 7) / 8)), dim3(256), 0, s, gate, up, n,
-                     batch, pt));
+                     batch, pt, gelu));
+    CN_CUDA(cudaGetLastError());
+    return CN_OK;
+}
+
+int launch_add_scalar(float* dst, const float* src, float c, int64_t n, cudaStream_t s) {
+    add_scalar_kernel<<<grid_1d(n, 256, 148 * 8), 256, 0, s>>>(dst, src, c, n);
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }

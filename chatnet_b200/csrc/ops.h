@@ -22,6 +22,7 @@ struct RopeKvArgs {
     int64_t cache_layer_off;   // elements to this layer
     int kv_f16, ctx_len;
     uint32_t* err;
+    int neox = 0;         // split-half pairs (ApplyRoPENeox) instead of interleaved ones
 };
 
 struct AttnPlan {
@@ -39,6 +40,7 @@ struct RopeIn {
     const float2* rope = nullptr;  // [ctx][hd/2] (cos, sin)
     int kv_stride = 0;
     int on = 0;
+    int neox = 0;  // split-half pairs (ApplyRoPENeox)
 };
 
 struct AttnArgs {
@@ -65,11 +67,14 @@ int attention_plan(int n_heads, int n_kv, int hd, int max_seq, int batch, int sm
 // Sets the kernels' shared-memory limit for plan p (call before any capture).
 int attention_prepare(const AttnPlan& p);
 int launch_attention(const AttnArgs& a, const AttnPlan& p, cudaStream_t s);
-int launch_silu_mul(float* gate, const float* up, int64_t n, cudaStream_t s);
+int launch_silu_mul(float* gate, const float* up, int64_t n, cudaStream_t s, int gelu = 0);
+// dst[i] = src[i] + c
+int launch_add_scalar(float* dst, const float* src, float c, int64_t n, cudaStream_t s);
 // gate = silu(gate) * up for `batch` rows of n values, plus the records of
 // the GEMV that reads the result (falls back to launch_silu_mul when pt has
 // no record form or n is not a multiple of 256).
-int launch_silu_prep(float* gate, const float* up, int n, int batch, const PrepTarget& pt, cudaStream_t s);
+int launch_silu_prep(float* gate, const float* up, int n, int batch, const PrepTarget& pt, cudaStream_t s,
+                     int gelu = 0);
 int launch_add(float* a, const float* b, int64_t n, cudaStream_t s);
 int launch_embed(int type, const void* emb, uint64_t row_bytes, const int* tokens, int vocab,
                  int dim, int batch, float* x, uint32_t* err, cudaStream_t s);

@@ -95,16 +95,14 @@ __global__ void norm_half_kernel(const float* __restrict__ x, const float* __res
     if (threadIdx.x == 0) inv[blockIdx.x] = iv;
 }
 
-__device__ __forceinline__ float silu_mul1(float g, float u) {
-    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
-}
-
-// h[t] = fp16(s_t * g / (1 + exp(-g)) * u) for token t's row of n values and
-// inv[t] = 1 / s_t; n % 4 == 0.  s_t comes from max(max(|g|, 0.2785) * |u|),
-// a bound on the row's largest output: silu(g) <= g for g >= 0 and
-// |silu(g)| < 0.2785 for g < 0.  The second pass re-reads g and u (cache hits).
+// h[t] = fp16(s_t * act(g) * u) for token t's row of n values (act: SiLU, or
+// GELU with gelu set) and inv[t] = 1 / s_t; n % 4 == 0.  s_t comes from
+// max(max(|g|, 0.2785) * |u|), a bound on the row's largest output for both:
+// silu(g), gelu(g) <= g for g >= 0, |silu(g)| < 0.2785 and |gelu(g)| < 0.17
+// for g < 0.  The second pass re-reads g and u (cache hits).
 __global__ void silu_half_kernel(const float* __restrict__ g, const float* __restrict__ u,
-                                 __half* __restrict__ h, float* __restrict__ inv, int n, __half* __restrict__ hlo) {
+                                 __half* __restrict__ h, float* __restrict__ inv, int n, __half* __restrict__ hlo,
+                                 int gelu) {
     __shared__ float red[32];
     const size_t base = (size_t)blockIdx.x * n;
     const float4* g4 = reinterpret_cast<const float4*>(g + base);
@@ -122,8 +120,8 @@ __global__ void silu_half_kernel(const float* __restrict__ g, const float* __res
     row_pow2_scale(block_absmax(bound, red), sc, iv);
     for (int i = threadIdx.x; i < n4; i += blockDim.x) {
         const float4 a = g4[i], b = u4[i];
-        const float f0 = silu_mul1(a.x, b.x) * sc, f1 = silu_mul1(a.y, b.y) * sc;
-        const float f2 = silu_mul1(a.z, b.z) * sc, f3 = silu_mul1(a.w, b.w) * sc;
+        const float f0 = act_mul(a.x, b.x, gelu) * sc, f1 = act_mul(a.y, b.y, gelu) * sc;
+        const float f2 = act_mul(a.z, b.z, gelu) * sc, f3 = act_mul(a.w, b.w, gelu) * sc;
         const uint2 o = make_uint2(pack_half2(f0, f1), pack_half2(f2, f3));
         h2[i] = o;
         if (hlo) {
@@ -165,7 +163,7 @@ __global__ void rope_prefill_kernel(float* __restrict__ q, const float* __restri
                                     const float* __restrict__ v, const float2* __restrict__ rope, int pos0,
                                     int qdim, int kvdim, int hd, void* kcache, void* vcache, int64_t cache_off,
                                     int kv_f16, __half* __restrict__ kh, __half* __restrict__ vh,
-                                    __half* __restrict__ kl, __half* __restrict__ vl) {
+                                    __half* __restrict__ kl, __half* __restrict__ vl, int neox) {
     const int t = blockIdx.x, pos = pos0 + t;
     const float4* tab = reinterpret_cast<const float4*>(rope + (size_t)pos * (hd / 2));  // two pairs per float4
     const int hd4 = hd / 4;
@@ -181,9 +179,47 @@ __global__ void rope_prefill_kernel(float* __restrict__ q, const float* __restri
         r.w = __fadd_rn(__fmul_rn(x.z, cs.w), __fmul_rn(x.w, cs.z));
         return r;
     };
-    for (int i = threadIdx.x; i < qdim / 4; i += blockDim.x) q4[i] = rot(q4[i], tab[i % hd4]);
+    // split-half RoPE (ApplyRoPENeox): element e of a head's first half pairs
+    // with e + hd/2 and uses table entry e (the same table)
+    const int half = hd / 2;
+    const float2* tab2 = rope + (size_t)pos * half;
+    auto rot_pairs = [](float4 a, float4 b, const float2* cs, float4& ra, float4& rb) {
+        const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+        float r0[4], r1[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            r0[e] = __fsub_rn(__fmul_rn(av[e], cs[e].x), __fmul_rn(bv[e], cs[e].y));
+            r1[e] = __fadd_rn(__fmul_rn(av[e], cs[e].y), __fmul_rn(bv[e], cs[e].x));
+        }
+        ra = make_float4(r0[0], r0[1], r0[2], r0[3]);
+        rb = make_float4(r1[0], r1[1], r1[2], r1[3]);
+    };
+    if (neox) {
+        const int hq = half / 4;  // float4 chunks per half head
+        for (int i = threadIdx.x; i < (qdim / hd) * hq; i += blockDim.x) {
+            float* a = q + (size_t)t * qdim + (i / hq) * hd + 4 * (i % hq);
+            float4 ra, rb;
+            rot_pairs(*reinterpret_cast<float4*>(a), *reinterpret_cast<float4*>(a + half), tab2 + 4 * (i % hq), ra, rb);
+            *reinterpret_cast<float4*>(a) = ra;
+            *reinterpret_cast<float4*>(a + half) = rb;
+        }
+    } else {
+        for (int i = threadIdx.x; i < qdim / 4; i += blockDim.x) q4[i] = rot(q4[i], tab[i % hd4]);
+    }
     for (int i = threadIdx.x; i < kvdim / 4; i += blockDim.x) {
-        const float4 kr = rot(k4[i], tab[i % hd4]), vv = v4[i];
+        float4 kr;
+        if (neox) {  // this chunk's elements and their partners in the other half
+            const int o = (4 * i) % hd;
+            const float* hb = k + (size_t)t * kvdim + (4 * i - o);
+            float4 ra, rb;
+            const int p = o < half ? o : o - half;
+            rot_pairs(*reinterpret_cast<const float4*>(hb + p), *reinterpret_cast<const float4*>(hb + p + half),
+                      tab2 + p, ra, rb);
+            kr = o < half ? ra : rb;
+        } else {
+            kr = rot(k4[i], tab[i % hd4]);
+        }
+        const float4 vv = v4[i];
         const uint2 kp = make_uint2(pack_half2(kr.x, kr.y), pack_half2(kr.z, kr.w));
         const uint2 vp = make_uint2(pack_half2(vv.x, vv.y), pack_half2(vv.z, vv.w));
         if (kv_f16) {
@@ -504,9 +540,9 @@ int prefill_norm(cudaStream_t st, const float* x, const float* w, __half* y, flo
 }
 
 int prefill_silu(cudaStream_t st, const float* g, const float* u, __half* h, float* inv, int n, int M,
-                 __half* hlo) {
+                 __half* hlo, int gelu) {
     CN_CHECK(n % 4 == 0 && M >= 1, CN_ERR_INVALID_ARG, "prefill silu: shapes");
-    CN_CUDA(launch_k(false, silu_half_kernel, dim3(M), dim3(256), 0, st, g, u, h, inv, n, hlo));
+    CN_CUDA(launch_k(false, silu_half_kernel, dim3(M), dim3(256), 0, st, g, u, h, inv, n, hlo, gelu));
     return CN_OK;
 }
 
@@ -518,11 +554,11 @@ int to_half_rows(cudaStream_t st, const float* x, __half* y, float* inv, int n, 
 
 int prefill_rope(cudaStream_t st, float* q, const float* k, const float* v, const float2* rope, int pos0, int M,
                  int qdim, int kvdim, int hd, void* kcache, void* vcache, int64_t cache_off, bool kv_f16, __half* kh,
-                 __half* vh, __half* kl, __half* vl) {
-    CN_CHECK(hd % 4 == 0 && qdim % 4 == 0 && kvdim % 4 == 0, CN_ERR_INVALID_ARG, "prefill rope: shapes");
+                 __half* vh, __half* kl, __half* vl, int neox) {
+    CN_CHECK(hd % 8 == 0 && qdim % 4 == 0 && kvdim % 4 == 0, CN_ERR_INVALID_ARG, "prefill rope: shapes");
     CN_CHECK(!kl == !vl, CN_ERR_INVALID_ARG, "prefill rope: k and v residuals go together");
     CN_CUDA(launch_k(false, rope_prefill_kernel, dim3(M), dim3(256), 0, st, q, k, v, rope, pos0, qdim, kvdim, hd,
-                     kcache, vcache, cache_off, kv_f16 ? 1 : 0, kh, vh, kl, vl));
+                     kcache, vcache, cache_off, kv_f16 ? 1 : 0, kh, vh, kl, vl, neox));
     return CN_OK;
 }
 

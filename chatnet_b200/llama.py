@@ -37,6 +37,10 @@ class LlamaConfig:
     rms_eps: float = 1e-5
     kv_f16: bool = False
     max_batch: int = 1
+    # variants of other ChatNet models on the same loop (cn_llama_config)
+    rope_neox: bool = False    # TensorMath.ApplyRoPENeox (split-half pairs)
+    act_gelu: bool = False     # TensorMath.GeluElementwiseMul
+    norm_offset: bool = False  # TensorMath.RmsNormWithOffset (weights stored as w - 1)
 
     @property
     def kv_dim(self) -> int:
@@ -50,7 +54,7 @@ class LlamaConfig:
         return N.LlamaConfigC(self.dim, self.hidden_dim, self.n_layers, self.n_heads,
                               self.n_kv_heads, self.head_dim, self.vocab, self.ctx_len,
                               self.rope_base, self.rms_eps, N.KV_F16 if self.kv_f16 else N.KV_F32,
-                              self.max_batch)
+                              self.max_batch, int(self.rope_neox), int(self.act_gelu), int(self.norm_offset))
 
 
 def tensor_names(n_layers: int) -> list[str]:

@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define CN_ABI_VERSION 1
+#define CN_ABI_VERSION 2
 
 /* status codes */
 #define CN_OK 0
@@ -243,6 +243,14 @@ typedef struct {
     float rope_base, rms_eps;
     int kv_dtype;  /* CN_KV_F32 or CN_KV_F16 */
     int max_batch; /* sequences decoded together, 1..32; each owns a KV slot */
+    /* Variants other ChatNet models run on the same loop (0 = Llama):
+     * rope_neox   split-half RoPE pairs (i, i + head_dim/2), TensorMath.ApplyRoPENeox
+     *             (Tensors/TensorMath.cs:475; Qwen/Phi), instead of interleaved pairs;
+     * act_gelu    GELU(gate) * up, TensorMath.GeluElementwiseMul (TensorMath.cs:294;
+     *             Gemma), instead of SiLU(gate) * up;
+     * norm_offset RMSNorm weights stored as (weight - 1), TensorMath.RmsNormWithOffset
+     *             (TensorMath.cs:335; Gemma). */
+    int rope_neox, act_gelu, norm_offset;
 } cn_llama_config;
 
 /* Number of tensors cn_llama_create takes for n_layers layers. */

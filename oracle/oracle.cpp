@@ -936,6 +936,48 @@ extern "C" void or_rope(float* q, float* k, int pos, int head_dim, int n_heads,
     }
 }
 
+// TensorMath.ApplyRoPENeox (TensorMath.cs:475-520): split-half pairs
+// (i, i + half), full rotary dimension.
+extern "C" void or_rope_neox(float* q, float* k, int pos, int head_dim, int n_heads, int n_kv_heads,
+                             float freq_base) {
+    int half = head_dim / 2;
+    float neg_log_base = -logf(freq_base);
+    float dim_inv = 2.0f / (float)head_dim;
+    for (int pass = 0; pass < 2; pass++) {
+        float* base = pass == 0 ? q : k;
+        int nh = pass == 0 ? n_heads : n_kv_heads;
+        for (int h = 0; h < nh; h++) {
+            float* v = base + (size_t)h * head_dim;
+            for (int i = 0; i < half; i++) {
+                float theta = (float)pos * expf((float)i * dim_inv * neg_log_base);
+                float c = cosf(theta), s = sinf(theta);
+                float x0 = v[i], x1 = v[i + half];
+                v[i] = x0 * c - x1 * s;
+                v[i + half] = x1 * c + x0 * s;
+            }
+        }
+    }
+}
+
+// TensorMath.GeluElementwiseMul (TensorMath.cs:294-333), tanh approximation,
+// evaluated left to right as the C# expression is.
+extern "C" void or_gelu_mul(float* gate, const float* up, int length) {
+    const float kSqrt2OverPi = 0.7978845608028654f, kCoeff = 0.044715f;
+    for (int i = 0; i < length; i++) {
+        float x = gate[i];
+        float g = 0.5f * x * (1.0f + tanhf(kSqrt2OverPi * (x + kCoeff * x * x * x)));
+        gate[i] = g * up[i];
+    }
+}
+
+// TensorMath.RmsNormWithOffset (TensorMath.cs:335-394): the sum of squares as
+// RmsNorm forms it, then input * rms * (weight + 1).
+extern "C" void or_rmsnorm_offset(const float* x, const float* w, float* y, int n, float eps) {
+    std::vector<float> w1(n);
+    for (int i = 0; i < n; i++) w1[i] = w[i] + 1.0f;
+    or_rmsnorm(x, w1.data(), y, n, eps);
+}
+
 // TensorMath.Add (TensorMath.cs:712-733).
 extern "C" void or_add(float* a, const float* b, int length) {
     for (int i = 0; i < length; i++) a[i] += b[i];
@@ -1143,23 +1185,27 @@ int run_layers(const or_llama_config& c, const void* const* t, const int* ty, vo
     int dim = c.dim, kvdim = c.n_kv_heads * c.head_dim, hid = c.hidden_dim;
     for (int l = l0; l < l1; l++) {
         int b = 3 + 9 * l;
-        or_rmsnorm(x, (const float*)t[b + 0], s.xnorm.data(), dim, c.eps);
+        // the architecture variants the model config selects (Gemma: offset
+        // norms and GELU; Qwen/Phi: split-half RoPE) on the Llama loop
+        auto norm = c.norm_offset ? or_rmsnorm_offset : or_rmsnorm;
+        norm(x, (const float*)t[b + 0], s.xnorm.data(), dim, c.eps);
         int rc = 0;
         rc |= or_matvec(ty[b + 1], T(t, b + 1), s.xnorm.data(), s.q.data(), dim, dim, nth);
         rc |= or_matvec(ty[b + 2], T(t, b + 2), s.xnorm.data(), s.k.data(), kvdim, dim, nth);
         rc |= or_matvec(ty[b + 3], T(t, b + 3), s.xnorm.data(), s.v.data(), kvdim, dim, nth);
         if (rc) return -2;
-        or_rope(s.q.data(), s.k.data(), pos, c.head_dim, c.n_heads, c.n_kv_heads, c.rope_base);
+        (c.rope_neox ? or_rope_neox : or_rope)(s.q.data(), s.k.data(), pos, c.head_dim, c.n_heads, c.n_kv_heads,
+                                                c.rope_base);
         store_kv(c, kc, l, pos, s.k.data());
         store_kv(c, vc, l, pos, s.v.data());
         attention(c, s, kc, vc, l, pos);
         if (or_matvec(ty[b + 4], T(t, b + 4), s.att.data(), s.ffn.data(), dim, dim, nth)) return -2;
         or_add(x, s.ffn.data(), dim);
-        or_rmsnorm(x, (const float*)t[b + 5], s.xnorm.data(), dim, c.eps);
+        norm(x, (const float*)t[b + 5], s.xnorm.data(), dim, c.eps);
         rc |= or_matvec(ty[b + 6], T(t, b + 6), s.xnorm.data(), s.gate.data(), hid, dim, nth);
         rc |= or_matvec(ty[b + 7], T(t, b + 7), s.xnorm.data(), s.up.data(), hid, dim, nth);
         if (rc) return -2;
-        or_silu_mul(s.gate.data(), s.up.data(), hid);
+        (c.act_gelu ? or_gelu_mul : or_silu_mul)(s.gate.data(), s.up.data(), hid);
         if (or_matvec(ty[b + 8], T(t, b + 8), s.gate.data(), s.ffn.data(), dim, hid, nth)) return -2;
         or_add(x, s.ffn.data(), dim);
     }
@@ -1187,7 +1233,7 @@ extern "C" int or_llama_layers(const or_llama_config* cfg, const void* const* te
 extern "C" int or_llama_head(const or_llama_config* cfg, const void* const* tensors,
                              const int* types, const float* x, float* logits, int nthreads) {
     std::vector<float> xn(cfg->dim);
-    or_rmsnorm(x, (const float*)tensors[2], xn.data(), cfg->dim, cfg->eps);
+    (cfg->norm_offset ? or_rmsnorm_offset : or_rmsnorm)(x, (const float*)tensors[2], xn.data(), cfg->dim, cfg->eps);
     return or_matvec(types[1], T(tensors, 1), xn.data(), logits, cfg->vocab, cfg->dim, nthreads);
 }
 

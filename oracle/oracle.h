@@ -77,6 +77,12 @@ void or_silu_mul(float* gate, const float* up, int length);
 void or_rope(float* q, float* k, int pos, int head_dim, int n_heads,
              int n_kv_heads, float freq_base);
 void or_add(float* a, const float* b, int length);
+/* Architecture variants on the same loop: ApplyRoPENeox (split-half pairs),
+ * GeluElementwiseMul, RmsNormWithOffset (TensorMath.cs:475, :294, :335). */
+void or_rope_neox(float* q, float* k, int pos, int head_dim, int n_heads,
+                  int n_kv_heads, float freq_base);
+void or_gelu_mul(float* gate, const float* up, int length);
+void or_rmsnorm_offset(const float* x, const float* w, float* y, int n, float eps);
 int or_argmax(const float* logits, int n);
 /* TemperatureSampler.Sample with the draw r given; *margin = distance of the
  * closest running sum to its threshold (top_p or r). */
@@ -95,6 +101,7 @@ typedef struct {
         ctx_len;
     float rope_base, eps;
     int kv_f16; /* 0: fp32 cache like the reference; 1: fp16 cache */
+    int rope_neox, act_gelu, norm_offset; /* architecture variants, 0 = Llama */
 } or_llama_config;
 
 /* kcache / vcache: [n_layers][ctx_len][n_kv_heads*head_dim] of float or

@@ -23,7 +23,8 @@ _i = C.c_int
 class LlamaConfig(C.Structure):
     _fields_ = [("dim", _i), ("hidden_dim", _i), ("n_layers", _i), ("n_heads", _i),
                 ("n_kv_heads", _i), ("head_dim", _i), ("vocab", _i), ("ctx_len", _i),
-                ("rope_base", _f), ("eps", _f), ("kv_f16", _i)]
+                ("rope_base", _f), ("eps", _f), ("kv_f16", _i), ("rope_neox", _i), ("act_gelu", _i),
+                ("norm_offset", _i)]
 
 
 _SIG = {
@@ -38,6 +39,9 @@ _SIG = {
     "or_softmax": (None, [_fp, _i]),
     "or_silu_mul": (None, [_fp, _fp, _i]),
     "or_rope": (None, [_fp, _fp, _i, _i, _i, _i, _f]),
+    "or_rope_neox": (None, [_fp, _fp, _i, _i, _i, _i, _f]),
+    "or_gelu_mul": (None, [_fp, _fp, _i]),
+    "or_rmsnorm_offset": (None, [_fp, _fp, _fp, _i, _f]),
     "or_add": (None, [_fp, _fp, _i]),
     "or_argmax": (_i, [_fp, _i]),
     "or_sample_temperature": (_i, [_fp, _i, _f, _i, _f, _f, _fp]),
@@ -127,7 +131,8 @@ def llama_config(cfg) -> LlamaConfig:
     """Oracle config struct from chatnet_b200.llama.LlamaConfig."""
     return LlamaConfig(cfg.dim, cfg.hidden_dim, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads,
                        cfg.head_dim, cfg.vocab, cfg.ctx_len, cfg.rope_base, cfg.rms_eps,
-                       1 if cfg.kv_f16 else 0)
+                       1 if cfg.kv_f16 else 0, int(getattr(cfg, "rope_neox", False)),
+                       int(getattr(cfg, "act_gelu", False)), int(getattr(cfg, "norm_offset", False)))
 
 
 class OracleLlama:

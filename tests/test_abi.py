@@ -36,7 +36,7 @@ def test_binding_covers_header():
 
 
 def test_abi_version():
-    assert N.lib().cn_abi_version() == 1
+    assert N.lib().cn_abi_version() == 2
 
 
 @pytest.mark.parametrize("t,elems,expected", [
