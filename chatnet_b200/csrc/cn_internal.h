@@ -253,8 +253,9 @@ struct GemvNeeds {
     size_t xfrag_bytes = 0, xsum_bytes = 0, xinv_bytes = 0, partial_bytes = 0, counters = 0;
 };
 
+// rb: the matrix's row stride in bytes (0: packed rows, row_bytes(type, cols)).
 int gemv_make(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols,
-              const CUtensorMap* map, int batch, GemvOp* op);
+              const CUtensorMap* map, int batch, GemvOp* op, uint64_t rb = 0);
 // Converts x [batch][cols] into the GEMV's activation fragments (TMA path).
 int gemv_prep(cudaStream_t st, int sms, const GemvOp& op, const float* d_x, const GemvBufs& b);
 // Runs the GEMV on prepped fragments (TMA path) or on x directly (generic).

@@ -595,6 +595,7 @@ __global__ void xprep_kernel(const float* __restrict__ x, int K, int batch, Prep
 // and dim 8192), and each pass of the loop is one round trip, so more
 // threads mean fewer passes.
 constexpr int kNormThreads = 512;
+constexpr int kNormBatch = 4;  // float4 loads per thread in flight (one GPU)
 
 // An exchange wait gives up at its time limit, or at once when an earlier
 // wait of the step already gave up (the error word holds kErrTimeout): a rank
@@ -745,21 +746,61 @@ __global__ void __launch_bounds__(kNormThreads)
         dr = nullptr;
     }
     float ss = 0.f;
-    for (int i = 4 * tid; i < n; i += 4 * kNormThreads) {
-        float4 v = *reinterpret_cast<const float4*>(xr + i);
-        if (dr || xbase || llbase) {
-            const float4 d = llbase  ? ll_sum4(xi, llbase, i, seq, t0)
-                             : xbase ? xchg_sum4(xi, xbase, i)
-                                     : *reinterpret_cast<const float4*>(dr + i);
-            v.x = __fadd_rn(v.x, d.x);
-            v.y = __fadd_rn(v.y, d.y);
-            v.z = __fadd_rn(v.z, d.z);
-            v.w = __fadd_rn(v.w, d.w);
+    const int i = u * 256 + tid;
+    const bool mine = tid < 256 && i < n;  // this thread's output element
+    float v_own = 0.f, w_own = 0.f;
+    if (xi.size <= 1) {
+        // one GPU: every load of a batch of up to kNormBatch float4 per
+        // thread (and the thread's own element and weight) is issued before
+        // the first is used, so the vector arrives in one round trip; the
+        // sums keep the per-thread order of the loop below
+        if (mine) {
+            v_own = xr[i];
+            if (dr) v_own = __fadd_rn(v_own, dr[i]);
+            w_own = w[i];
         }
-        ss = fmaf(v.x, v.x, ss);
-        ss = fmaf(v.y, v.y, ss);
-        ss = fmaf(v.z, v.z, ss);
-        ss = fmaf(v.w, v.w, ss);
+        for (int base = 4 * tid; base < n; base += kNormBatch * 4 * kNormThreads) {
+            float4 xv[kNormBatch], dv[kNormBatch];
+#pragma unroll
+            for (int k = 0; k < kNormBatch; k++) {
+                const int j = base + k * 4 * kNormThreads;
+                if (j < n) {
+                    xv[k] = *reinterpret_cast<const float4*>(xr + j);
+                    dv[k] = dr ? *reinterpret_cast<const float4*>(dr + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < kNormBatch; k++) {
+                if (base + k * 4 * kNormThreads < n) {
+                    float4 v = xv[k];
+                    if (dr) {
+                        v.x = __fadd_rn(v.x, dv[k].x);
+                        v.y = __fadd_rn(v.y, dv[k].y);
+                        v.z = __fadd_rn(v.z, dv[k].z);
+                        v.w = __fadd_rn(v.w, dv[k].w);
+                    }
+                    ss = fmaf(v.x, v.x, ss);
+                    ss = fmaf(v.y, v.y, ss);
+                    ss = fmaf(v.z, v.z, ss);
+                    ss = fmaf(v.w, v.w, ss);
+                }
+            }
+        }
+    } else {
+        for (int j = 4 * tid; j < n; j += 4 * kNormThreads) {
+            float4 v = *reinterpret_cast<const float4*>(xr + j);
+            if (xbase || llbase) {
+                const float4 d = llbase ? ll_sum4(xi, llbase, j, seq, t0) : xchg_sum4(xi, xbase, j);
+                v.x = __fadd_rn(v.x, d.x);
+                v.y = __fadd_rn(v.y, d.y);
+                v.z = __fadd_rn(v.z, d.z);
+                v.w = __fadd_rn(v.w, d.w);
+            }
+            ss = fmaf(v.x, v.x, ss);
+            ss = fmaf(v.y, v.y, ss);
+            ss = fmaf(v.z, v.z, ss);
+            ss = fmaf(v.w, v.w, ss);
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -767,20 +808,22 @@ __global__ void __launch_bounds__(kNormThreads)
     __syncthreads();
     ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < kNormThreads / 32; i++) ss += red[i];
+    for (int k = 0; k < kNormThreads / 32; k++) ss += red[k];
     const float rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
-    const int i = u * 256 + tid;
-    if (tid < 256 && i < n) {
+    if (mine && xi.size <= 1) {
+        if (dr) x_out[(size_t)b * n + i] = v_own;
+        const float o = __fmul_rn(__fmul_rn(v_own, rms), w_own);
+        y[(size_t)b * n + i] = o;
+        vals[tid] = o;
+    } else if (mine) {  // tensor parallel: the exchange's sum is the delta
         float v = xr[i];
-        if (dr || xbase || llbase) {
+        if (xbase || llbase) {
             float d;
             if (llbase) {
                 d = ll_sum1(xi, llbase, i, seq, t0);
-            } else if (xbase) {
+            } else {
                 d = __ldcg(xbase + i);
                 for (int p = 1; p < xi.size; p++) d = __fadd_rn(d, __ldcg(xbase + p * xi.rank_stride + i));
-            } else {
-                d = dr[i];
             }
             v = __fadd_rn(v, d);
             x_out[(size_t)b * n + i] = v;
@@ -1149,7 +1192,7 @@ static int launch_tma(cn_ctx* ctx, const CUtensorMap* map, const GemvPlan& p, co
 }
 
 int gemv_make(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols,
-              const CUtensorMap* map, int batch, GemvOp* op) {
+              const CUtensorMap* map, int batch, GemvOp* op, uint64_t rb) {
     CN_CHECK(type_supported(type), CN_ERR_UNSUPPORTED, "Unsupported weight quantization type: %d",
              type);
     CN_CHECK(d_w, CN_ERR_INVALID_ARG, "null weight pointer");
@@ -1162,7 +1205,8 @@ int gemv_make(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols
     op->rows = rows;
     op->cols = cols;
     op->batch = batch;
-    op->rb = row_bytes(type, cols);
+    op->rb = rb ? rb : row_bytes(type, cols);
+    CN_CHECK(op->rb >= row_bytes(type, cols), CN_ERR_INVALID_ARG, "row stride below the row's bytes");
     op->tma = tileable(type, cols, op->rb) && ((reinterpret_cast<uintptr_t>(d_w) & 15) == 0);
     if (op->tma) {
         if (map) op->map = *map;

@@ -89,6 +89,9 @@ struct cn_llama {
     __half *pf_h = nullptr, *pf_kh = nullptr, *pf_vh = nullptr;
     int* pf_tok = nullptr;
     float* pf_xs = nullptr;  // [pf_cap] inverse row scales of pf_h
+    // row-padded copies of projections whose rows are not 16-byte multiples
+    // (pad_rows); they replace the caller's tensors in t
+    std::vector<cn_tensor*> pads;
 };
 
 namespace cn {
@@ -135,7 +138,7 @@ static int build_step(cn_llama* m, int B) {
             const cn_tensor* w = LT(m, l, wj[j]);
             GemvOp op;
             int rc = gemv_make(m->ctx, w->type, w->d, w->rows, w->cols, w->has_map ? &w->map : nullptr,
-                               B, &op);
+                               B, &op, w->row_bytes);
             if (rc) return rc;
             st.ops.push_back(op);
         }
@@ -143,7 +146,7 @@ static int build_step(cn_llama* m, int B) {
         const cn_tensor* w = m->t[T_OUT];
         GemvOp op;
         int rc = gemv_make(m->ctx, w->type, w->d, w->rows, w->cols, w->has_map ? &w->map : nullptr,
-                           B, &op);
+                           B, &op, w->row_bytes);
         if (rc) return rc;
         st.ops.push_back(op);
     }
@@ -445,6 +448,53 @@ __global__ void kv_synth_kernel(uint64_t seed, int layers, int npos, int ctx, in
     }
 }
 
+// Q6_K projections whose rows are not whole 16-byte units (an inner
+// dimension that is not a multiple of 2048: Llama-2-7B's ffn_down at 11008
+// columns has 9030-byte rows) cannot be tiled by TMA.  The model keeps a
+// copy of each such matrix with every row padded to the next 16-byte
+// boundary (zero bytes after the row's blocks, never decoded) and puts it in
+// place of the caller's tensor, so the decode GEMV and the prefill matmul
+// both take their tiled paths.  The split-variant scale is taken from the
+// caller's packed tensor.
+static int pad_rows(cn_llama* m) {
+    cudaStream_t s = m->ctx->stream;
+    for (size_t i = 3; i < m->t.size(); i++) {
+        const int j = (int)((i - 3) % 9);
+        const cn_tensor* w = m->t[i];
+        if (j == L_ANORM || j == L_FNORM || w->type != CN_TYPE_Q6_K || w->row_bytes % 16 == 0 || w->cols % 256)
+            continue;
+        cn_tensor* p = new (std::nothrow) cn_tensor();
+        CN_CHECK(p, CN_ERR_OOM, "host allocation failed");
+        *p = *w;
+        p->d = nullptr;
+        p->owns = true;
+        p->has_map = false;
+        p->row_bytes = (w->row_bytes + 15) / 16 * 16;
+        p->bytes = p->row_bytes * (uint64_t)w->rows;
+        cudaError_t e = cudaMalloc(&p->d, p->bytes);
+        if (e != cudaSuccess) {
+            delete p;
+            return cuda_error(e, "padded weight copy");
+        }
+        m->pads.push_back(p);
+        e = cudaMemsetAsync(p->d, 0, p->bytes, s);
+        if (e == cudaSuccess)
+            e = cudaMemcpy2DAsync(p->d, p->row_bytes, w->d, w->row_bytes, w->row_bytes, (size_t)w->rows,
+                                  cudaMemcpyDeviceToDevice, s);
+        if (e != cudaSuccess) return cuda_error(e, "padded weight copy");
+        if (encode_weight_map(p->type, p->d, p->rows, p->row_bytes, &p->map) == CN_OK) p->has_map = true;
+        set_error(CN_OK, "");
+        cn_tensor packed = *w;
+        float ws = 0.f;
+        int rc = matmul_split_scale(&packed, s, &ws);
+        if (rc) return rc;
+        p->split_scale = ws;
+        m->t[i] = p;
+    }
+    CN_CUDA(cudaStreamSynchronize(s));
+    return CN_OK;
+}
+
 static void free_model(cn_llama* m) {
     for (int b = 0; b <= kMaxBatch; b++)
         if (m->steps[b].graph) cudaGraphExecDestroy(m->steps[b].graph);
@@ -455,6 +505,10 @@ static void free_model(cn_llama* m) {
                     m->pf_x, m->pf_q, m->pf_k, m->pf_v, m->pf_g, m->pf_u, m->pf_h, m->pf_kh, m->pf_vh,
                     m->pf_tok, m->pf_xs, m->pf_hl, m->pf_kl, m->pf_vl, m->normw};
     for (void* p : bufs) cudaFree(p);
+    for (cn_tensor* p : m->pads) {
+        cudaFree(p->d);
+        delete p;
+    }
     cudaFreeHost(m->h_tokens);
     cudaFreeHost(m->h_pos);
     cudaFreeHost(m->h_amax);
@@ -466,9 +520,9 @@ static void free_model(cn_llama* m) {
 // A weight tensor's TMA descriptor, or null (the matmul then encodes one).
 static const CUtensorMap* wmap(const cn_tensor* t) { return t->has_map ? &t->map : nullptr; }
 
-// Whether the model's projections can run on the prefill matmul (Q4_0, Q4_K,
-// or Q6_K with rows of a multiple of 16 bytes, inner dimensions multiples of
-// 256, one GPU).
+// Whether the model's projections can run on the prefill matmul (Q4_0, Q4_K
+// or Q6_K -- Q6_K rows that are not 16-byte multiples were padded by
+// pad_rows --, inner dimensions multiples of 256, one GPU).
 static bool prefill_supported(const cn_llama* m) {
     if (m->tp && m->tp->size > 1) return false;
     const cn_llama_config& c = m->cfg;
@@ -778,6 +832,7 @@ static int create_model(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* cons
         cudaError_t e0 = cudaStreamSynchronize(ctx->stream);
         if (e0 != cudaSuccess) return fail(cuda_error(e0, "norm offset"));
     }
+    if ((rc = pad_rows(m))) return fail(rc);
     const size_t fd = (size_t)B * c.dim * 4, fq = (size_t)B * qdim * 4, fk = (size_t)B * kvd * 4,
                  fh = (size_t)B * hid * 4;
     if (m->tp) {
@@ -814,13 +869,13 @@ static int create_model(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* cons
         for (int r = 0; r < 5; r++) {
             int b = reps[r] < B ? reps[r] : B;
             for (int i = 0; i < n_tensors; i++) {
-                const cn_tensor* w = tensors[i];
+                const cn_tensor* w = m->t[i];
                 if (w->type == CN_TYPE_F32 && (i == T_ONORM || (i >= 3 && (i - 3) % 9 == L_ANORM) ||
                                                (i >= 3 && (i - 3) % 9 == L_FNORM)))
                     continue;
                 GemvOp op;
                 if ((rc = gemv_make(ctx, w->type, w->d, w->rows, w->cols, w->has_map ? &w->map : nullptr,
-                                    b, &op)))
+                                    b, &op, w->row_bytes)))
                     return fail(rc);
                 gemv_reserve(op.plan, &need);
             }
@@ -829,9 +884,9 @@ static int create_model(cn_ctx* ctx, const cn_llama_config* cfg, cn_tensor* cons
                 static const int wj[5] = {L_Q, L_K, L_V, L_GATE, L_UP};
                 GemvOp o[5];
                 for (int j = 0; j < 5; j++) {
-                    const cn_tensor* w = tensors[3 + wj[j]];
+                    const cn_tensor* w = m->t[3 + wj[j]];
                     if ((rc = gemv_make(ctx, w->type, w->d, w->rows, w->cols, w->has_map ? &w->map : nullptr,
-                                        b, &o[j])))
+                                        b, &o[j], w->row_bytes)))
                         return fail(rc);
                 }
                 GemvGroup g;
@@ -882,7 +937,7 @@ int cn_llama_prefill_hidden_dev(cn_llama* m, const float* x_dev, int n, int pos,
     CN_CHECK(n >= 1 && pos >= 0 && pos + n <= m->cfg.ctx_len, CN_ERR_INVALID_ARG,
              "positions [%d, %d) outside the context of %d", pos, pos + n, m->cfg.ctx_len);
     CN_CHECK(prefill_supported(m), CN_ERR_UNSUPPORTED,
-             "prefill needs Q4_0, Q4_K or 16-byte-row Q6_K projections, dim and hidden_dim multiples of 256, head_dim 64 or 128, one GPU");
+             "prefill (LlamaModel.Forward over a prompt) needs Q4_0, Q4_K or Q6_K projections, dim and hidden_dim multiples of 256, head_dim 64 or 128, one GPU");
     cudaSetDevice(m->ctx->device);
     cudaStream_t s = m->ctx->stream;
     int rc = prefill_reserve(m, n);

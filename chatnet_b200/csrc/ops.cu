@@ -16,6 +16,7 @@
 // round-to-nearest intrinsics; reductions (sums of squares, dot products,
 // softmax sums) run in a different order than the C# loops, which changes
 // results only at the level of fp32 rounding.
+#include <stdlib.h>
 #include <float.h>
 
 #include "cn_common.cuh"
@@ -413,8 +414,8 @@ __global__ void __launch_bounds__(kAttnThreads)
 //
 // Same math as attn_split_kernel for an fp16 cache with kv_mul <= 8 query heads
 // per kv head and head_dim 64 or 128, but the two contractions run on
-// mma.sync m16n8k16 (fp16 in, fp32 accumulate).  A CTA takes 128 positions
-// (16 per warp) of one (sequence, kv head):
+// mma.sync m16n8k16 (fp16 in, fp32 accumulate).  A CTA takes CHUNK positions
+// (16 per warp, CHUNK / 16 warps) of one (sequence, kv head):
 //   * K / V rows arrive by cp.async into padded shared rows (zero-filled past
 //     the current position);
 //   * the A operand of Q K^T stacks the kv_mul query heads twice: rows 0-7
@@ -424,7 +425,9 @@ __global__ void __launch_bounds__(kAttnThreads)
 //     split into hi and lo halves; V comes in through ldmatrix.trans;
 //   * the warps' partial outputs and exp-sums are added in shared memory and
 //     the split is merged by attn_finish.
-constexpr int kMmaChunk = 128;
+// The loads of cache rows below the current position are issued before the
+// programmatic-launch wait, so they overlap the q/k/v GEMV.
+constexpr int kMmaChunkMax = 128;
 
 __device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t (&r)[4]) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -443,8 +446,8 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int sr
 }
 __device__ __forceinline__ uint32_t half2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
-template <int HD>
-__global__ void __launch_bounds__(kAttnThreads)
+template <int HD, int CHUNK>
+__global__ void __launch_bounds__(2 * CHUNK)
     attn_mma_kernel(const float* __restrict__ q, const __half* __restrict__ kcache,
                     const __half* __restrict__ vcache, const int* __restrict__ pos_dev, int pos_host,
                     int n_heads, int n_kv, int q_stride, int64_t cache_seq_stride, int64_t cache_layer_off,
@@ -454,25 +457,26 @@ __global__ void __launch_bounds__(kAttnThreads)
     // Cache rows below the current position were written by earlier steps,
     // so their copies start before the wait for the q/k/v kernel; the row at
     // the current position, q and everything written here come after it.
-    static_assert(kAttnThreads == 256 && kMmaChunk == 16 * (kAttnThreads / 32), "16 positions per warp");
+    constexpr int NW = CHUNK / 16, NT = 32 * NW;  // 16 positions per warp
+    static_assert(CHUNK % 16 == 0 && CHUNK <= kMmaChunkMax, "chunk");
     constexpr int RS = HD + 8;  // halves per shared row (16-byte pad against bank conflicts)
     extern __shared__ __align__(16) float sm[];
     __shared__ int s_last;
-    __shared__ float mx[8][8], ls[8][8];
+    __shared__ float mx[NW][8], ls[NW][8];
     const int s = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
     const int kv_mul = n_heads / n_kv;
     const int prow = HD + 4;
     int pos = pos_dev ? pos_dev[b] : pos_host;
     if (pos < 0 || pos >= ctx_len) pos = -1;  // rejected upstream; read nothing
     const int seq = pos + 1;
-    const int p0 = s * kMmaChunk;
-    const int L = max(0, min(seq, p0 + kMmaChunk) - p0);
+    const int p0 = s * CHUNK;
+    const int L = max(0, min(seq, p0 + CHUNK) - p0);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
     float* pr_base = part + ((size_t)b * n_heads + kh * kv_mul) * splits * prow;
     __half* Ks = reinterpret_cast<__half*>(sm);
-    __half* Vs = Ks + kMmaChunk * RS;
-    __half* Qs = Vs + kMmaChunk * RS;  // [16][RS]
+    __half* Vs = Ks + CHUNK * RS;
+    __half* Qs = Vs + CHUNK * RS;  // [16][RS]
 
     if (L == 0) {  // nothing of this split is inside 0..pos: an empty partial
         pdl_wait();
@@ -488,7 +492,7 @@ __global__ void __launch_bounds__(kAttnThreads)
         // row pos of the cache: this step's k/v (written here with ri.on, or
         // by the preceding kernel otherwise)
         const int r_new = pos - p0;
-        for (int i = tid; i < kMmaChunk * CPR; i += kAttnThreads) {
+        for (int i = tid; i < CHUNK * CPR; i += NT) {
             const int r = i / CPR, c = i % CPR;
             if (r == r_new) continue;  // after the wait (no zero fill racing it)
             const bool in = r < L;
@@ -498,7 +502,7 @@ __global__ void __launch_bounds__(kAttnThreads)
         }
         pdl_wait();
         if (!ri.on && r_new >= 0 && r_new < L) {
-            for (int c = tid; c < CPR; c += kAttnThreads) {
+            for (int c = tid; c < CPR; c += NT) {
                 const int64_t go = (int64_t)pos * kvdim + c * 8;
                 cp_async16(smem_u32(Ks + r_new * RS + c * 8), kbase + go, 16);
                 cp_async16(smem_u32(Vs + r_new * RS + c * 8), vbase + go, 16);
@@ -513,7 +517,7 @@ __global__ void __launch_bounds__(kAttnThreads)
             const float* vr = ri.v + (size_t)b * ri.kv_stride + kh * HD;
             __half* kw = const_cast<__half*>(kbase) + (int64_t)pos * kvdim;
             __half* vw = const_cast<__half*>(vbase) + (int64_t)pos * kvdim;
-            for (int p = tid; p < HD / 2; p += kAttnThreads) {
+            for (int p = tid; p < HD / 2; p += NT) {
                 const float2 cs = tab[p];
                 const int ia = ri.neox ? p : 2 * p, ib = ri.neox ? p + HD / 2 : 2 * p + 1;
                 const float x0 = kr[ia], x1 = kr[ib];
@@ -532,7 +536,7 @@ __global__ void __launch_bounds__(kAttnThreads)
         }
         // query heads: fp16 hi in rows 0-7, the fp16 remainder in rows 8-15
         // (rotated here when ri.on, as rope_kv_kernel would have)
-        for (int i = tid; i < 8 * HD / 2; i += kAttnThreads) {
+        for (int i = tid; i < 8 * HD / 2; i += NT) {
             const int gi = i / (HD / 2), p = i % (HD / 2);
             // the pair's elements: (2p, 2p + 1), or (p, p + HD/2) for split-half RoPE
             const int ia = ri.on && ri.neox ? p : 2 * p, ib = ri.on && ri.neox ? p + HD / 2 : 2 * p + 1;
@@ -590,7 +594,7 @@ __global__ void __launch_bounds__(kAttnThreads)
         __syncthreads();
         float M = mx[0][g];
 #pragma unroll
-        for (int w = 1; w < 8; w++) M = fmaxf(M, mx[w][g]);
+        for (int w = 1; w < NW; w++) M = fmaxf(M, mx[w][g]);
         float pe[2][2], l = 0.f;
 #pragma unroll
         for (int nt = 0; nt < 2; nt++)
@@ -629,25 +633,25 @@ __global__ void __launch_bounds__(kAttnThreads)
         }
         // sum the warps' outputs (the K rows are no longer read: every warp
         // passed the barrier after its scores)
-        float* ob = reinterpret_cast<float*>(Ks);  // [8 warps][8 heads][HD]
+        float* ob = reinterpret_cast<float*>(Ks);  // [NW warps][8 heads][HD]
 #pragma unroll
         for (int n = 0; n < HD / 8; n++)
             *reinterpret_cast<float2*>(ob + (warp * 8 + g) * HD + 8 * n + 2 * t) =
                 make_float2(o[n][0] + o[n][2], o[n][1] + o[n][3]);
         __syncthreads();
-        for (int i = tid; i < kv_mul * HD; i += kAttnThreads) {
+        for (int i = tid; i < kv_mul * HD; i += NT) {
             const int gi = i / HD, d = i % HD;
             float sum = 0.f;
 #pragma unroll
-            for (int w = 0; w < 8; w++) sum += ob[(w * 8 + gi) * HD + d];
+            for (int w = 0; w < NW; w++) sum += ob[(w * 8 + gi) * HD + d];
             pr_base[((size_t)gi * splits + s) * prow + d] = sum;
         }
         if (tid < kv_mul) {
             float Mh = mx[0][tid], lh = 0.f;
 #pragma unroll
-            for (int w = 1; w < 8; w++) Mh = fmaxf(Mh, mx[w][tid]);
+            for (int w = 1; w < NW; w++) Mh = fmaxf(Mh, mx[w][tid]);
 #pragma unroll
-            for (int w = 0; w < 8; w++) lh += ls[w][tid];
+            for (int w = 0; w < NW; w++) lh += ls[w][tid];
             pr_base[((size_t)tid * splits + s) * prow + HD] = Mh;
             pr_base[((size_t)tid * splits + s) * prow + HD + 1] = lh;
         }
@@ -835,6 +839,32 @@ static bool attn_use_mma(int n_heads, int n_kv, int hd, bool kv_f16) {
     return kv_f16 && n_heads / n_kv <= 8 && (hd == 64 || hd == 128);
 }
 
+using AttnMmaFn = void (*)(const float*, const __half*, const __half*, const int*, int, int, int, int, int64_t,
+                           int64_t, int, int, float, float*, int*, float*, int, PrepTarget, RopeIn);
+static AttnMmaFn attn_mma_fn(int hd, int chunk) {
+#ifdef CHATNET_TUNING
+    if (chunk == 32) return hd == 64 ? attn_mma_kernel<64, 32> : attn_mma_kernel<128, 32>;
+    if (chunk == 64) return hd == 64 ? attn_mma_kernel<64, 64> : attn_mma_kernel<128, 64>;
+#endif
+    (void)chunk;
+    return hd == 64 ? attn_mma_kernel<64, 128> : attn_mma_kernel<128, 128>;
+}
+
+// Positions per tensor-core attention CTA: 128.  Smaller chunks (tuning
+// builds: CHATNET_ATTN_CHUNK=32 or 64) give more, smaller CTAs that fit
+// beside the q/k/v GEMV's, but measured on B200 in the Llama-2-70B decode
+// step (batch 1, position 2047) they cost more than they save: 9.95 ms per
+// step with 128, 10.33 ms with 64, 11.69 ms with 32.
+static int attn_mma_chunk() {
+#ifdef CHATNET_TUNING
+    if (const char* e = getenv("CHATNET_ATTN_CHUNK")) {
+        const int v = atoi(e);
+        if (v == 32 || v == 64 || v == 128) return v;
+    }
+#endif
+    return kMmaChunkMax;
+}
+
 int attention_plan(int n_heads, int n_kv, int hd, int max_seq, int batch, int sms, bool kv_f16, AttnPlan* p) {
     CN_CHECK(n_kv > 0 && n_heads % n_kv == 0, CN_ERR_INVALID_ARG, "n_heads %% n_kv_heads != 0");
     CN_CHECK(n_heads / n_kv <= kMaxKvMul, CN_ERR_UNSUPPORTED, "kv_mul > %d", kMaxKvMul);
@@ -843,7 +873,7 @@ int attention_plan(int n_heads, int n_kv, int hd, int max_seq, int batch, int sm
     p->mma = attn_use_mma(n_heads, n_kv, hd, kv_f16);
     int chunk;
     if (p->mma) {
-        chunk = kMmaChunk;
+        chunk = attn_mma_chunk();
     } else {
         // about one CTA per SM in total, chunks of 32..128 positions (the
         // merge then reads few partials per (sequence, kv head))
@@ -860,7 +890,7 @@ int attention_plan(int n_heads, int n_kv, int hd, int max_seq, int batch, int sm
     const size_t q_bytes = (size_t)kv_mul * (hd + 4) * 4;
     const size_t kv_bytes = (size_t)chunk * (attn_krow<float>(hd) + hd) * 4;
     size_t smem = q_bytes + kv_bytes + (size_t)kv_mul * chunk * 4;
-    const size_t mma_smem = (size_t)(2 * kMmaChunk + 16) * (hd + 8) * 2;
+    const size_t mma_smem = (size_t)(2 * chunk + 16) * (hd + 8) * 2;
     const size_t merge_smem =
         (((size_t)kv_mul * p->splits + 3) / 4 * 4 + ((kv_mul + 3) & ~3) + (size_t)kv_mul * hd) * 4;
     if (p->mma) smem = mma_smem;
@@ -873,8 +903,10 @@ int attention_prepare(const AttnPlan& p) {
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
     CN_CUDA(cudaFuncSetAttribute(attn_split_kernel<float>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
-    CN_CUDA(cudaFuncSetAttribute(attn_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
-    CN_CUDA(cudaFuncSetAttribute(attn_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+    if (p.mma)
+        for (int hd : {64, 128})
+            CN_CUDA(cudaFuncSetAttribute(attn_mma_fn(hd, p.chunk), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)p.smem));
     return CN_OK;
 }
 
@@ -889,10 +921,9 @@ int launch_attention(const AttnArgs& a, const AttnPlan& p, cudaStream_t s) {
     PrepTarget pt = a.prep;
     if ((a.n_heads / a.n_kv) * a.hd % 256 != 0 || a.out_stride % 4 != 0) pt.kind = -1;
     if (p.mma) {
-        CN_CHECK(a.kv_f16 && attn_use_mma(a.n_heads, a.n_kv, a.hd, true) && p.chunk == kMmaChunk,
+        CN_CHECK(a.kv_f16 && attn_use_mma(a.n_heads, a.n_kv, a.hd, true) && p.chunk == attn_mma_chunk(),
                  CN_ERR_INVALID_ARG, "attention plan does not match the call");
-        auto k = a.hd == 64 ? attn_mma_kernel<64> : attn_mma_kernel<128>;
-        CN_CUDA(launch_k(true, k, grid, dim3(kAttnThreads), p.smem, s, a.q, (const __half*)a.kcache,
+        CN_CUDA(launch_k(true, attn_mma_fn(a.hd, p.chunk), grid, dim3(2 * p.chunk), p.smem, s, a.q, (const __half*)a.kcache,
                          (const __half*)a.vcache, a.pos_dev, a.pos_host, a.n_heads, a.n_kv, a.q_stride,
                          a.cache_seq_stride, a.cache_layer_off, a.ctx_len, p.splits, scale, a.part,
                          a.counters, a.out, a.out_stride, pt, a.rope));

@@ -285,8 +285,10 @@ int cn_llama_forward(cn_llama* m, const int* tokens, int n, int pos, float* logi
 
 /* Prompts of min_tokens (>= 16; 16 by default) or more tokens in
  * cn_llama_forward run as one prefill pass on a one-GPU model whose
- * projections are Q4_0, Q4_K or Q6_K with 16-byte rows (every layer on the
- * tcgen05 matmul for all n tokens, see cn_llama_prefill_hidden_dev); 0 turns
+ * projections are Q4_0, Q4_K or Q6_K (every layer on the tcgen05 matmul for
+ * all n tokens, see cn_llama_prefill_hidden_dev; a Q6_K matrix whose rows are
+ * not 16-byte multiples, such as Llama-2-7B's ffn_down at 11008 columns, runs
+ * from a row-padded copy the model makes at creation); 0 turns
  * it off, so every prompt token runs as a decode step.  (no reference
  * counterpart: the reference has only the sequential loop) */
 int cn_llama_set_prefill(cn_llama* m, int min_tokens);

@@ -135,12 +135,13 @@ def _quantizer_like_q4k(blk: np.ndarray) -> np.ndarray:
     return b.reshape(blk.shape)
 
 
-def _q4_k_m_layer(ctx, oracle, mixed: bool, n_kv: int, kv_f16: bool, scale_div: float, realistic: bool):
+def _q4_k_m_layer(ctx, oracle, mixed: bool, n_kv: int, kv_f16: bool, scale_div: float, realistic: bool,
+                  hidden: int = 4096):
     """A one-layer Q4_K(_M-style) model (dim 2048, 16 heads of 128): Q4_K
     projections, with Q6_K attn_v / ffn_down when mixed.  Returns (GPU model,
     oracle, tensors, config)."""
     from chatnet_b200.llama import tensor_shape
-    m = LlamaConfig(dim=2048, hidden_dim=4096, n_layers=1, n_heads=16, n_kv_heads=n_kv, head_dim=128, vocab=300,
+    m = LlamaConfig(dim=2048, hidden_dim=hidden, n_layers=1, n_heads=16, n_kv_heads=n_kv, head_dim=128, vocab=300,
                     ctx_len=128, kv_f16=kv_f16)
     names = tensor_names(m.n_layers)
     types = [cn.TYPE_F32 if n.endswith("norm.weight") else
@@ -197,6 +198,32 @@ def test_prefill_q4_k_m_style_model(ctx, oracle, mixed, n_kv, kv_f16):
     kg, vg = g.kv_read(0, 0, 0, n)
     assert rel_err(kg.astype(np.float32), orc.k[:n].astype(np.float32)) <= REL_TOL
     assert rel_err(vg.astype(np.float32), orc.v[:n].astype(np.float32)) <= REL_TOL
+    g.close()
+    for t in tensors:
+        t.free()
+
+
+def test_q6_k_unaligned_rows_prefill_and_decode(ctx, oracle):
+    """Q4_K_M files of Llama-2-7B store ffn_down as Q6_K over hidden 11008:
+    43 super-blocks, 9030-byte rows, not a 16-byte multiple, so TMA cannot
+    tile the packed matrix.  Here hidden 2816 (11 super-blocks, 2310-byte
+    rows) has the same property: the model runs its ffn_down from a
+    row-padded copy, the prefill pass takes every projection (11 launches,
+    none refused), and both the prefill hidden states and a decode step
+    after it match the oracle."""
+    g, orc, tensors, m = _q4_k_m_layer(ctx, oracle, True, 4, True, 64, realistic=True, hidden=2816)
+    assert (m.hidden_dim // 256) * 210 % 16 != 0
+    assert g.prefill_kernels() == 11 * m.n_layers
+    n = 24
+    x, got = _prefill_layer(ctx, g, m, n)
+    errs = [rel_err(got[t], orc.layers(x[t], t)) for t in range(n)]
+    print(f"unaligned Q6_K ffn_down: prefill worst {max(errs):.2e}")
+    assert max(errs) <= REL_TOL, (int(np.argmax(errs)), max(errs))
+    # a decode step at the next position reads the padded copy through the GEMV
+    tok = 7
+    lg, _ = g.decode([tok], [n])
+    ref = orc.forward([tok], n)
+    assert rel_err(lg[0], ref) <= REL_TOL
     g.close()
     for t in tensors:
         t.free()
@@ -318,7 +345,9 @@ def test_prefill_config3_layer(ctx, oracle):
 
 
 def test_prefill_rejects_unsupported(ctx):
-    dc = cf.replace(small(), weight_type=cn.TYPE_Q6_K)
+    """head_dim 32 has no prefill attention: NotImplementedError (such a model
+    still decodes token by token); positions past the context: ValueError."""
+    dc = small(head_dim=32, n_heads=8)
     ts = cf.device_tensors(ctx, dc)
     g = CudaLlamaModel(ctx, dc.model, ts)
     x = torch.zeros(20, 256, device="cuda")
