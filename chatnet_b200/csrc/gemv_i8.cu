@@ -49,11 +49,10 @@ constexpr int kCons = 8;           // consumer warps, 16 rows each
 //
 // DEEP == 2 is the deep pipeline with two groups of eight consumer warps
 // that take alternate stages: a unit costs a group's warps a long latency
-// chain (about a thousand cycles), so with few units per CTA (short rows,
-// where the pipeline's fill and drain dominate) two units in flight finish
-// the range sooner.  The groups' partial sums of a tile meet in shared memory
-// at the tile's end.  With many units per CTA the weight stream bounds the
-// CTA and the extra warps only cost, so the plain deep form runs there.
+// chain (about a thousand cycles, which alone would hold an SM near 35 GB/s),
+// so two units in flight keep the weight stream moving.  The groups' partial
+// sums of a tile meet in shared memory at the tile's end.  Batch 1-2 uses it
+// for every deep launch of up to 128 units per CTA (grouped_units).
 template <int NB, int DEEP = 0>
 struct Geo {
     static constexpr int NT = n_tiles(NB);
@@ -556,6 +555,21 @@ static int tile_share_cap(int units) {
     return units <= 16 ? 1 : 7;
 }
 
+// Most units per CTA for the two-consumer-group form: 128 (tuning builds:
+// CHATNET_GEMV_GROUPED_UNITS).  Measured on B200, Llama-2-70B decode step at
+// batch 1 (three interleaved runs each): 9.957 ms per step with the groups
+// only up to 16 units per CTA, 9.845 ms up to 32 (the q/k/v launch grouped
+// too), 9.848 ms up to 128 (every launch of the step grouped), and the
+// 28672 x 8192 GEMV alone 27.6 us -> 27.1 us.
+static int grouped_units() {
+#ifdef CHATNET_TUNING
+    static const int v = env_int("CHATNET_GEMV_GROUPED_UNITS", 128);
+    return v;
+#else
+    return 128;
+#endif
+}
+
 int gemv_i8_ctas(int sms, int tiles, int units, int batch) {
     const int per_sm = i8::n_tiles(batch) == 1 ? i8::Geo<1>::kCtasPerSm : i8::Geo<8>::kCtasPerSm;
 #ifdef CHATNET_TUNING
@@ -653,8 +667,8 @@ int gemv_i8_run_group(cudaStream_t st, uint32_t* err, int nmat, const CUtensorMa
     int dev = 0;
     CN_CUDA(cudaGetDevice(&dev));
     const bool deep = ctas <= g_sms[dev & 63];  // one CTA per SM: the deep pipeline
-    // few units per CTA (batch 1-2): the deep pipeline with two consumer groups
-    const bool grouped = deep && batch <= 2 && (int64_t)tiles * a.units <= 16LL * ctas;
+    // batch 1-2, up to grouped_units() units per CTA: the deep pipeline with two consumer groups
+    const bool grouped = deep && batch <= 2 && (int64_t)tiles * a.units <= (int64_t)grouped_units() * ctas;
     if (grouped) {
         if (batch == 1)
             CN_CUDA(launch_k(true, gemv_i8_q4k_kernel<1, 2>, dim3(ctas), dim3(i8::Geo<1, 2>::kThreads),
