@@ -16,14 +16,16 @@ import numpy as np
 from . import _native as N
 from ._native import (CudaError, NotSupportedError, TYPE_F16, TYPE_F32, TYPE_Q4_0, TYPE_Q4_K,
                       TYPE_Q6_K, TYPE_Q4_1, TYPE_Q5_0, TYPE_Q5_1, TYPE_Q8_0, TYPE_Q2_K, TYPE_Q3_K, TYPE_Q5_K,
-                      TYPE_Q8_K, TYPE_IQ4_NL, TYPE_IQ4_XS, DIST_CFG0_Q4_0, DIST_CFG2_Q4_K, DIST_CFG2_Q6_K, DIST_NORMAL,
+                      TYPE_Q8_K, TYPE_IQ4_NL, TYPE_IQ4_XS, TYPE_IQ2_XXS, TYPE_IQ2_XS, TYPE_IQ3_XXS,
+                      TYPE_IQ1_S, TYPE_IQ3_S, TYPE_IQ2_S, TYPE_IQ1_M, DIST_CFG0_Q4_0, DIST_CFG2_Q4_K, DIST_CFG2_Q6_K, DIST_NORMAL,
                       DIST_NORM_W, check, byte_size)
 
 __all__ = [
     "Context", "Tensor", "CudaError", "NotSupportedError", "check", "byte_size", "synth_fill",
     "synth_seed", "device_count", "TYPE_F32", "TYPE_F16", "TYPE_Q4_0", "TYPE_Q4_K", "TYPE_Q6_K",
     "TYPE_Q4_1", "TYPE_Q5_0", "TYPE_Q5_1", "TYPE_Q8_0", "TYPE_Q2_K", "TYPE_Q3_K", "TYPE_Q5_K", "TYPE_Q8_K",
-    "TYPE_IQ4_NL", "TYPE_IQ4_XS",
+    "TYPE_IQ4_NL", "TYPE_IQ4_XS", "TYPE_IQ2_XXS", "TYPE_IQ2_XS", "TYPE_IQ3_XXS", "TYPE_IQ1_S", "TYPE_IQ3_S",
+    "TYPE_IQ2_S", "TYPE_IQ1_M",
     "DIST_CFG0_Q4_0", "DIST_CFG2_Q4_K", "DIST_CFG2_Q6_K", "DIST_NORMAL", "DIST_NORM_W",
 ]
 

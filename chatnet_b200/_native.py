@@ -41,8 +41,15 @@ TYPE_Q4_K = 12
 TYPE_Q5_K = 13
 TYPE_Q6_K = 14
 TYPE_Q8_K = 15
+TYPE_IQ2_XXS = 16
+TYPE_IQ2_XS = 17
+TYPE_IQ3_XXS = 18
+TYPE_IQ1_S = 19
 TYPE_IQ4_NL = 20
+TYPE_IQ3_S = 21
+TYPE_IQ2_S = 22
 TYPE_IQ4_XS = 23
+TYPE_IQ1_M = 29
 
 DIST_CFG0_Q4_0 = 1
 DIST_CFG2_Q4_K = 2

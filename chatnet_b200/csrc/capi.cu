@@ -108,7 +108,14 @@ uint64_t cn_byte_size(int type, uint64_t elements) {
         case CN_TYPE_Q3_K:
         case CN_TYPE_Q5_K:
         case CN_TYPE_Q8_K:
-        case CN_TYPE_IQ4_XS: return (elements + 255) / 256 * superblock_bytes(type);
+        case CN_TYPE_IQ4_XS:
+        case CN_TYPE_IQ2_XXS:
+        case CN_TYPE_IQ2_XS:
+        case CN_TYPE_IQ3_XXS:
+        case CN_TYPE_IQ1_S:
+        case CN_TYPE_IQ3_S:
+        case CN_TYPE_IQ2_S:
+        case CN_TYPE_IQ1_M: return (elements + 255) / 256 * superblock_bytes(type);
         default: return 0;
     }
 }
@@ -419,7 +426,8 @@ int cn_dequantize(cn_ctx* ctx, const cn_tensor* W, int64_t row0, int64_t nrows, 
     } else if ((W->type == CN_TYPE_Q4_K || W->type == CN_TYPE_Q6_K) && W->cols % 256 != 0) {
         return set_error(CN_ERR_INVALID_ARG, "K-quant rows must hold whole super-blocks");
     } else {
-        rc = dequant_launch(W->type, src, d_out, nrows * W->cols, ctx->stream);
+        rc = dequant_launch(W->type, src, d_out, nrows * W->cols, ctx->stream,
+                            static_cast<const uint8_t*>(W->d) + W->bytes);
         if (rc) return rc;
     }
     CN_CUDA(cudaMemcpyAsync(host_out, d_out, out_bytes, cudaMemcpyDeviceToHost, ctx->stream));

@@ -85,11 +85,25 @@ __host__ __device__ inline int block32_bytes(int type) {
 // The 256-weight super-block codecs decoded through the generic paths.
 __host__ __device__ inline bool is_superblock(int type) {
     return type == CN_TYPE_Q2_K || type == CN_TYPE_Q3_K || type == CN_TYPE_Q5_K || type == CN_TYPE_Q8_K ||
-           type == CN_TYPE_IQ4_XS;
+           type == CN_TYPE_IQ4_XS || type == CN_TYPE_IQ2_XXS || type == CN_TYPE_IQ2_XS || type == CN_TYPE_IQ3_XXS ||
+           type == CN_TYPE_IQ1_S || type == CN_TYPE_IQ3_S || type == CN_TYPE_IQ2_S || type == CN_TYPE_IQ1_M;
 }
+// GgufTensorInfo.ByteSize (GgufTensorInfo.cs:30-114) per 256 elements.
 __host__ __device__ inline int superblock_bytes(int type) {
-    return type == CN_TYPE_Q2_K ? 84 : type == CN_TYPE_Q3_K ? 110 : type == CN_TYPE_Q5_K ? 176
-           : type == CN_TYPE_Q8_K ? 292 : 136;
+    switch (type) {
+        case CN_TYPE_Q2_K: return 84;
+        case CN_TYPE_Q3_K: return 110;
+        case CN_TYPE_Q5_K: return 176;
+        case CN_TYPE_Q8_K: return 292;
+        case CN_TYPE_IQ2_XXS: return 66;
+        case CN_TYPE_IQ2_XS: return 74;
+        case CN_TYPE_IQ3_XXS: return 98;
+        case CN_TYPE_IQ1_S: return 50;
+        case CN_TYPE_IQ3_S: return 110;
+        case CN_TYPE_IQ2_S: return 82;
+        case CN_TYPE_IQ1_M: return 56;
+        default: return 136;  // IQ4_XS
+    }
 }
 bool type_supported(int type);
 
@@ -334,7 +348,10 @@ XchgIn tp_gather_in(const cn_tp* tp, uint32_t uses, uint32_t use, uint32_t* err)
 XchgOut tp_gather_out(const cn_tp* tp, int64_t local_rows, uint32_t uses, uint32_t use, int done_index);
 float* tp_logits(const cn_tp* tp);
 
-int dequant_launch(int type, const void* d_blocks, float* d_out, int64_t n, cudaStream_t s);
+// d_end: one past the tensor's last byte, when d_blocks starts inside a
+// larger tensor (IQ3_S reads past a block; null: the range's own end).
+int dequant_launch(int type, const void* d_blocks, float* d_out, int64_t n, cudaStream_t s,
+                   const void* d_end = nullptr);
 int synth_launch(int type, int64_t rows, int64_t cols, uint64_t seed, int dist, void* d_out,
                  cudaStream_t s);
 // Region [row0, row0 + nrows) x [col0, col0 + ncols) of the rows x cols tensor

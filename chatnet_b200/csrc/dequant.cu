@@ -116,13 +116,14 @@ __global__ void dequant_b32_kernel(int type, const uint8_t* __restrict__ q, floa
     }
 }
 
-// One thread per element of the whole super-blocks of Q2_K / Q3_K / Q5_K /
-// Q8_K / IQ4_XS (the reference decodes n / 256 super-blocks).
+// One thread per element of the whole super-blocks of the 256-element codecs
+// on the generic paths (the reference decodes n / 256 super-blocks; `end`
+// bounds IQ3_S's reads past a block).
 __global__ void dequant_superblock_kernel(int type, const uint8_t* __restrict__ q, float* __restrict__ out,
-                                          int64_t n, int bpb) {
+                                          int64_t n, int bpb, const uint8_t* end) {
     const int64_t m = n / 256 * 256;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < m; i += (int64_t)gridDim.x * blockDim.x)
-        out[i] = superblock_elem(type, q + (i >> 8) * bpb, (int)(i & 255));
+        out[i] = superblock_elem(type, q + (i >> 8) * bpb, (int)(i & 255), end);
 }
 
 __global__ void convert_f16_kernel(const uint16_t* __restrict__ h, float* __restrict__ out,
@@ -139,7 +140,7 @@ static unsigned grid_for(int64_t work, int threads) {
     return (unsigned)g;
 }
 
-int dequant_launch(int type, const void* d_blocks, float* d_out, int64_t n, cudaStream_t s) {
+int dequant_launch(int type, const void* d_blocks, float* d_out, int64_t n, cudaStream_t s, const void* d_end) {
     CN_CHECK(n >= 0, CN_ERR_INVALID_ARG, "negative element count");
     if (n == 0) return CN_OK;
     CN_CHECK(d_blocks && d_out, CN_ERR_INVALID_ARG, "null pointer");
@@ -151,8 +152,9 @@ int dequant_launch(int type, const void* d_blocks, float* d_out, int64_t n, cuda
     }
     if (is_superblock(type)) {
         if (n / 256 == 0) return CN_OK;
+        const uint8_t* end = d_end ? static_cast<const uint8_t*>(d_end) : q + (n / 256) * superblock_bytes(type);
         dequant_superblock_kernel<<<grid_for(n / 256 * 256, 256), 256, 0, s>>>(type, q, d_out, n,
-                                                                                superblock_bytes(type));
+                                                                                superblock_bytes(type), end);
         CN_CUDA(cudaGetLastError());
         return CN_OK;
     }

@@ -78,7 +78,69 @@ __device__ __forceinline__ float block32_elem(int type, const uint8_t* p, int j)
 //   Q8_K  (sbyte)q * d, d fp32                 DequantQ8K.cs:25-47
 //   IQ4_XS d*sc * table[nibble], sc = ((byte 4+sub & 63) | 2 bits of the
 //         uint16 at 2 << 6) - 32               DequantIQ.cs:143-180 (qs@8)
-__device__ __forceinline__ float superblock_elem(int type, const uint8_t* p, int e) {
+// and the reference's own simplified decodes of the importance-quantised
+// types (no codebook grids; d, fp16 at byte 0, then):
+//   IQ3_S   (d*sc) * q3, negated by sign bit e%8 of byte 98 + e/8; q3 = 2 bits
+//           of qs[e/4] | qh bit e%8 of byte 66 + e/8 << 2; sc = 2 bits of
+//           byte 130 + e/32 + 1                DequantIQ.cs:244-290
+//           (the sign and scale bytes lie past the 110-byte block: the next
+//           block's bytes inside a tensor, read as 0 from `end` on)
+//   IQ3_XXS d * (q3 - 4), q3 = 3 bits 3(e%8) of the 24-bit group at 2 + 3(e/8)
+//                                              DequantIQ.cs:364-398
+//   IQ2_XS  (d*sc) * (q - 1), q = 2 bits of byte 2 + e/4; sc = nibble e/16%2
+//           of byte 66 + e/32, - 8             DequantIQ.cs:456-495
+//   IQ2_XXS d * (q - 1)                        DequantIQ.cs:568-597
+//   IQ2_S   (d*sc) * q, sc = low nibble of byte 66 + e/16, + 1; elements 0-3
+//           of each 16 negated by the high nibble's bits
+//                                              DequantIQ.cs:656-695
+//   IQ1_S   d, -d or 0: bit e%8 of qs byte 2 + e/8, else bit
+//           4(e/8 % 2) + (e%8)/2 of qh byte 34 + e/16
+//                                              DequantIQ.cs:767-805
+//   IQ1_M   as IQ1_S times sc = 1 or 0.5 (bit (e/8)%8 of byte 50 + e/64)
+//                                              DequantIQ.cs:869-912
+__device__ __forceinline__ float iq_elem(int type, const uint8_t* p, int e, const uint8_t* end) {
+    const float d = ld_half(p);
+    if (type == CN_TYPE_IQ3_S) {
+        const int sub = e >> 3, j = e & 7;
+        const uint8_t* ps = p + 130 + (sub >> 2);
+        const uint8_t* pg = p + 98 + sub;
+        const int sc = (((ps < end ? *ps : 0) >> (2 * (sub & 3))) & 3) + 1;
+        const int q3 = ((p[2 + (e >> 2)] >> (2 * (e & 3))) & 3) | (((p[66 + (e >> 3)] >> (e & 7)) & 1) << 2);
+        const float v = __fmul_rn(__fmul_rn(d, (float)sc), (float)q3);
+        return (((pg < end ? *pg : 0) >> j) & 1) ? -v : v;
+    }
+    if (type == CN_TYPE_IQ3_XXS) {
+        const uint8_t* g = p + 2 + 3 * (e >> 3);
+        const uint32_t packed = (uint32_t)g[0] | ((uint32_t)g[1] << 8) | ((uint32_t)g[2] << 16);
+        return __fmul_rn(d, (float)((int)((packed >> (3 * (e & 7))) & 7u) - 4));
+    }
+    if (type == CN_TYPE_IQ2_XS || type == CN_TYPE_IQ2_XXS || type == CN_TYPE_IQ2_S) {
+        const int sub = e >> 4, r = e & 15;
+        const int q = (p[2 + 4 * sub + (r >> 2)] >> (2 * (r & 3))) & 3;
+        if (type == CN_TYPE_IQ2_XXS) return __fmul_rn(d, (float)(q - 1));
+        if (type == CN_TYPE_IQ2_XS) {
+            const int sb = p[66 + (sub >> 1)];
+            const int sc = ((sub & 1) ? ((sb >> 4) & 0x0F) : (sb & 0x0F)) - 8;
+            return __fmul_rn(__fmul_rn(d, (float)sc), (float)(q - 1));
+        }
+        const int qh = p[66 + sub];
+        const float v = __fmul_rn(__fmul_rn(d, (float)((qh & 0x0F) + 1)), (float)q);
+        return (r < 4 && ((qh >> (4 + r)) & 1)) ? -v : v;
+    }
+    // IQ1_S, IQ1_M
+    const int sub = e >> 3, j = e & 7;
+    const int bit = (p[2 + sub] >> j) & 1;
+    const int hbit = (p[34 + (sub >> 1)] >> (4 * (sub & 1) + (j >> 1))) & 1;
+    float w = d;
+    if (type == CN_TYPE_IQ1_M) w = __fmul_rn(d, ((p[50 + (sub >> 3)] >> (sub & 7)) & 1) ? 1.0f : 0.5f);
+    return bit ? w : hbit ? -w : 0.0f;
+}
+
+// `end`: one past the last byte an IQ3_S decode may read (see above).
+__device__ __forceinline__ float superblock_elem(int type, const uint8_t* p, int e, const uint8_t* end) {
+    if (type == CN_TYPE_IQ2_XXS || type == CN_TYPE_IQ2_XS || type == CN_TYPE_IQ3_XXS || type == CN_TYPE_IQ1_S ||
+        type == CN_TYPE_IQ3_S || type == CN_TYPE_IQ2_S || type == CN_TYPE_IQ1_M)
+        return iq_elem(type, p, e, end);
     if (type == CN_TYPE_Q2_K) {
         const int g = e >> 7, si = (e >> 5) & 3, h = (e >> 4) & 1;
         const int sb = p[8 * g + 2 * si + h];

@@ -955,7 +955,8 @@ __global__ void __launch_bounds__(kNormClThreads)
 // For shapes the TMA path cannot tile (row bytes not a multiple of 16, or K
 // not a multiple of 256): one warp per (row, batch), exact block decode and
 // fp32 FMAs.  Slow but shape-agnostic.
-__device__ float block_dot(int type, const uint8_t* row, int blk, const float* x) {
+// end: one past the matrix's last byte (bounds IQ3_S's reads past a block).
+__device__ float block_dot(int type, const uint8_t* row, int blk, const float* x, const uint8_t* end) {
     float s = 0.f;
     if (type == CN_TYPE_Q4_0) {
         const uint8_t* p = row + (size_t)blk * 18;
@@ -1011,7 +1012,7 @@ __device__ float block_dot(int type, const uint8_t* row, int blk, const float* x
     } else if (is_superblock(type)) {
         const uint8_t* p = row + (size_t)blk * superblock_bytes(type);
         const float* xb = x + (size_t)blk * 256;
-        for (int e = 0; e < 256; e++) s = fmaf(superblock_elem(type, p, e), xb[e], s);
+        for (int e = 0; e < 256; e++) s = fmaf(superblock_elem(type, p, e, end), xb[e], s);
     } else if (type == CN_TYPE_F16) {
         s = ld_half(row + 2 * (size_t)blk) * x[blk];
     }
@@ -1033,7 +1034,7 @@ __global__ void gemv_generic_kernel(int type, const uint8_t* __restrict__ w, int
         const uint8_t* row = w + (size_t)r * rbytes;
         const float* xb = x + (size_t)b * cols;
         float s = 0.f;
-        for (int k = lane; k < nblk; k += 32) s += block_dot(type, row, k, xb);
+        for (int k = lane; k < nblk; k += 32) s += block_dot(type, row, k, xb, w + (size_t)rows * rbytes);
         for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
         if (lane == 0) y[(size_t)b * rows + r] = s;
     }

@@ -757,7 +757,7 @@ __global__ void embed_kernel(int type, const uint8_t* __restrict__ emb, uint64_t
         } else if (is_block32(type)) {
             v = block32_elem(type, row + (i / 32) * block32_bytes(type), i % 32);
         } else if (is_superblock(type)) {
-            v = superblock_elem(type, row + (i / 256) * superblock_bytes(type), i % 256);
+            v = superblock_elem(type, row + (i / 256) * superblock_bytes(type), i % 256, row + row_bytes);
         } else if (type == CN_TYPE_F16) {
             v = ld_half(row + 2 * i);
         } else {

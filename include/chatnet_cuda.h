@@ -59,8 +59,15 @@ extern "C" {
 #define CN_TYPE_Q5_K 13
 #define CN_TYPE_Q6_K 14
 #define CN_TYPE_Q8_K 15
+#define CN_TYPE_IQ2_XXS 16
+#define CN_TYPE_IQ2_XS 17
+#define CN_TYPE_IQ3_XXS 18
+#define CN_TYPE_IQ1_S 19
 #define CN_TYPE_IQ4_NL 20
+#define CN_TYPE_IQ3_S 21
+#define CN_TYPE_IQ2_S 22
 #define CN_TYPE_IQ4_XS 23
+#define CN_TYPE_IQ1_M 29
 
 typedef struct cn_ctx cn_ctx;
 typedef struct cn_tensor cn_tensor;

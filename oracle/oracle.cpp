@@ -91,6 +91,13 @@ extern "C" uint64_t or_byte_size(int type, uint64_t elements) {
         case OR_Q8_K: return (elements + 255) / 256 * 292;
         case OR_IQ4_NL: return (elements + 31) / 32 * 18;
         case OR_IQ4_XS: return (elements + 255) / 256 * 136;
+        case OR_IQ3_S: return (elements + 255) / 256 * 110;
+        case OR_IQ3_XXS: return (elements + 255) / 256 * 98;
+        case OR_IQ2_XS: return (elements + 255) / 256 * 74;
+        case OR_IQ2_XXS: return (elements + 255) / 256 * 66;
+        case OR_IQ2_S: return (elements + 255) / 256 * 82;
+        case OR_IQ1_S: return (elements + 255) / 256 * 50;
+        case OR_IQ1_M: return (elements + 255) / 256 * 56;
         default: return 0;
     }
 }
@@ -379,6 +386,114 @@ static void dequant_iq4_xs(const uint8_t* q, float* out, int64_t n) {
     }
 }
 
+// ---- the importance-quantised types, as the reference decodes them ---------
+//
+// DequantIQ.cs restates these without codebook grids (its own simplified
+// layouts).  IQ3_S reads its sign bytes at 98 + sub and its scale bytes at
+// 130 + sub/4 from the block start, past the 110-byte block: inside a tensor
+// those are the next block's bytes (the pointer-based DotProduct reads them
+// there; the span-based Dequantize throws for the last block of its span).
+// Here every such read goes through iq3s_byte, which returns the byte when
+// it lies before `end` and 0 past it.
+static inline uint8_t iq3s_byte(const uint8_t* blk, int k, const uint8_t* end) {
+    return blk + k < end ? blk[k] : 0;
+}
+
+// DequantIQ.IQ3S.Dequantize (DequantIQ.cs:244-290).
+static void dequant_iq3_s(const uint8_t* q, float* out, int64_t n, const uint8_t* end) {
+    for (int64_t b = 0; b < n / 256; b++) {
+        const uint8_t* blk = q + b * 110;
+        const float d = h2f(blk);
+        for (int sub = 0; sub < 32; sub++) {
+            const int sc = ((iq3s_byte(blk, 130 + sub / 4, end) >> ((sub % 4) * 2)) & 3) + 1;
+            const float dsc = d * (float)sc;
+            const uint8_t sign = iq3s_byte(blk, 98 + sub, end);
+            for (int j = 0; j < 8; j++) {
+                const int idx = sub * 8 + j;
+                const int q2 = (blk[2 + idx / 4] >> ((idx % 4) * 2)) & 3;
+                const int qh = (blk[66 + idx / 8] >> (idx % 8)) & 1;
+                float v = dsc * (float)(q2 | (qh << 2));
+                if ((sign >> j) & 1) v = -v;
+                out[b * 256 + idx] = v;
+            }
+        }
+    }
+}
+
+// DequantIQ.IQ3XXS.Dequantize (DequantIQ.cs:364-398).
+static void dequant_iq3_xxs(const uint8_t* q, float* out, int64_t n) {
+    for (int64_t b = 0; b < n / 256; b++) {
+        const uint8_t* blk = q + b * 98;
+        const float d = h2f(blk);
+        for (int sub = 0; sub < 32; sub++) {
+            const uint8_t* g = blk + 2 + sub * 3;
+            const uint32_t packed = (uint32_t)g[0] | ((uint32_t)g[1] << 8) | ((uint32_t)g[2] << 16);
+            for (int j = 0; j < 8; j++) out[b * 256 + sub * 8 + j] = d * (float)((int)((packed >> (j * 3)) & 7) - 4);
+        }
+    }
+}
+
+// DequantIQ.IQ2XS / IQ2XXS / IQ2S.Dequantize (DequantIQ.cs:456-495, :568-597,
+// :656-695): 16 sub-blocks of 16, four 2-bit quants per byte.
+static void dequant_iq2(int type, const uint8_t* q, float* out, int64_t n) {
+    const int bpb = type == OR_IQ2_XS ? 74 : type == OR_IQ2_XXS ? 66 : 82;
+    for (int64_t b = 0; b < n / 256; b++) {
+        const uint8_t* blk = q + b * bpb;
+        const float d = h2f(blk);
+        for (int sub = 0; sub < 16; sub++) {
+            float dsc = d;
+            int sign = 0;
+            if (type == OR_IQ2_XS) {
+                const int raw = (int8_t)blk[66 + sub / 2];
+                const int sc = (sub & 1) == 0 ? (raw & 0x0F) - 8 : ((raw >> 4) & 0x0F) - 8;
+                dsc = d * (float)sc;
+            } else if (type == OR_IQ2_S) {
+                const uint8_t qh = blk[66 + sub];
+                dsc = d * (float)((qh & 0x0F) + 1);
+                sign = (qh >> 4) & 0x0F;
+            }
+            for (int j = 0; j < 4; j++) {
+                const uint8_t byte = blk[2 + sub * 4 + j];
+                for (int k = 0; k < 4; k++) {
+                    const int qv = (byte >> (k * 2)) & 3;
+                    const int e = j * 4 + k;
+                    float v;
+                    if (type == OR_IQ2_S) {
+                        v = dsc * (float)qv;
+                        if (e < 4 && ((sign >> e) & 1)) v = -v;
+                    } else {
+                        v = dsc * (float)(qv - 1);
+                    }
+                    out[b * 256 + sub * 16 + e] = v;
+                }
+            }
+        }
+    }
+}
+
+// DequantIQ.IQ1S / IQ1M.Dequantize (DequantIQ.cs:767-805, :869-912): per
+// element d (or d * sc), -d (-d * sc) or 0 from a qs bit and a qh bit.
+static void dequant_iq1(int type, const uint8_t* q, float* out, int64_t n) {
+    const int bpb = type == OR_IQ1_S ? 50 : 56;
+    for (int64_t b = 0; b < n / 256; b++) {
+        const uint8_t* blk = q + b * bpb;
+        const float d = h2f(blk);
+        for (int sub = 0; sub < 32; sub++) {
+            float sc = 1.0f;
+            if (type == OR_IQ1_M && sub / 8 < 6) sc = ((blk[50 + sub / 8] >> (sub % 8)) & 1) == 1 ? 1.0f : 0.5f;
+            const uint8_t qs = blk[2 + sub];
+            for (int j = 0; j < 8; j++) {
+                const int bit = (qs >> j) & 1;
+                const int hbit = (blk[34 + sub / 2] >> ((sub % 2) * 4 + j / 2)) & 1;
+                float v;
+                if (type == OR_IQ1_S) v = bit ? d : hbit ? -d : 0.0f;
+                else v = bit ? d * sc : hbit ? -d * sc : 0.0f;
+                out[b * 256 + sub * 8 + j] = v;
+            }
+        }
+    }
+}
+
 extern "C" int or_dequantize(int type, const uint8_t* src, float* dst, int64_t n) {
     if (n < 0) return -1;
     switch (type) {
@@ -395,6 +510,13 @@ extern "C" int or_dequantize(int type, const uint8_t* src, float* dst, int64_t n
         case OR_Q8_K: dequant_q8_k(src, dst, n); return 0;
         case OR_IQ4_NL: dequant_iq4_nl(src, dst, n); return 0;
         case OR_IQ4_XS: dequant_iq4_xs(src, dst, n); return 0;
+        case OR_IQ3_S: dequant_iq3_s(src, dst, n, src + n / 256 * 110); return 0;
+        case OR_IQ3_XXS: dequant_iq3_xxs(src, dst, n); return 0;
+        case OR_IQ2_XS:
+        case OR_IQ2_XXS:
+        case OR_IQ2_S: dequant_iq2(type, src, dst, n); return 0;
+        case OR_IQ1_S:
+        case OR_IQ1_M: dequant_iq1(type, src, dst, n); return 0;
         case OR_F32: memcpy(dst, src, (size_t)n * 4); return 0;
         case OR_F16:
             for (int64_t i = 0; i < n; i++) dst[i] = h2f(src + 2 * i);
@@ -751,6 +873,127 @@ static float dot_iq4_xs(const uint8_t* row, const float* x, int n) {
     return sum;
 }
 
+// DequantIQ.IQ3S.DotProductScalar (DequantIQ.cs:299-349): per sub-block
+// subSum += (+-q3) * x, blockSum += dsc * subSum, sum += blockSum; sign and
+// scale bytes past the block as in dequant_iq3_s (`end` bounds the reads).
+static float dot_iq3_s(const uint8_t* row, const float* x, int n, const uint8_t* end) {
+    float sum = 0.f;
+    for (int b = 0; b < n / 256; b++) {
+        const uint8_t* blk = row + (size_t)b * 110;
+        const float d = h2f(blk);
+        float bs = 0.f;
+        for (int sub = 0; sub < 32; sub++) {
+            const int sc = ((iq3s_byte(blk, 130 + sub / 4, end) >> ((sub % 4) * 2)) & 3) + 1;
+            const float dsc = d * (float)sc;
+            const uint8_t sign = iq3s_byte(blk, 98 + sub, end);
+            float ss = 0.f;
+            for (int j = 0; j < 8; j++) {
+                const int idx = sub * 8 + j;
+                const int q3 = ((blk[2 + idx / 4] >> ((idx % 4) * 2)) & 3) | (((blk[66 + idx / 8] >> (idx % 8)) & 1) << 2);
+                float v = (float)q3;
+                if ((sign >> j) & 1) v = -v;
+                ss += v * x[256 * b + idx];
+            }
+            bs += dsc * ss;
+        }
+        sum += bs;
+    }
+    return sum;
+}
+
+// DequantIQ.IQ3XXS.DotProductScalar (DequantIQ.cs:407-440): blockSum +=
+// (q3 - 4) * x over the block, sum += d * blockSum.
+static float dot_iq3_xxs(const uint8_t* row, const float* x, int n) {
+    float sum = 0.f;
+    for (int b = 0; b < n / 256; b++) {
+        const uint8_t* blk = row + (size_t)b * 98;
+        const float d = h2f(blk);
+        float bs = 0.f;
+        for (int sub = 0; sub < 32; sub++) {
+            const uint8_t* g = blk + 2 + sub * 3;
+            const uint32_t packed = (uint32_t)g[0] | ((uint32_t)g[1] << 8) | ((uint32_t)g[2] << 16);
+            for (int j = 0; j < 8; j++) bs += (float)((int)((packed >> (j * 3)) & 7) - 4) * x[256 * b + sub * 8 + j];
+        }
+        sum += d * bs;
+    }
+    return sum;
+}
+
+// DequantIQ.IQ2XS / IQ2S.DotProductScalar (DequantIQ.cs:505-553, :705-752):
+// per sub-block subSum, blockSum += dsc * subSum; IQ2XXS (:607-640):
+// blockSum += (q - 1) * x over the block, sum += d * blockSum.
+static float dot_iq2(int type, const uint8_t* row, const float* x, int n) {
+    const int bpb = type == OR_IQ2_XS ? 74 : type == OR_IQ2_XXS ? 66 : 82;
+    float sum = 0.f;
+    for (int b = 0; b < n / 256; b++) {
+        const uint8_t* blk = row + (size_t)b * bpb;
+        const float d = h2f(blk);
+        float bs = 0.f;
+        for (int sub = 0; sub < 16; sub++) {
+            const float* in = x + 256 * b + 16 * sub;
+            if (type == OR_IQ2_XXS) {
+                for (int j = 0; j < 4; j++) {
+                    const uint8_t byte = blk[2 + sub * 4 + j];
+                    for (int k = 0; k < 4; k++) bs += (float)(((byte >> (2 * k)) & 3) - 1) * in[j * 4 + k];
+                }
+                continue;
+            }
+            float dsc;
+            int sign = 0;
+            if (type == OR_IQ2_XS) {
+                const int raw = (int8_t)blk[66 + sub / 2];
+                dsc = d * (float)((sub & 1) == 0 ? (raw & 0x0F) - 8 : ((raw >> 4) & 0x0F) - 8);
+            } else {
+                const uint8_t qh = blk[66 + sub];
+                dsc = d * (float)((qh & 0x0F) + 1);
+                sign = (qh >> 4) & 0x0F;
+            }
+            float ss = 0.f;
+            for (int j = 0; j < 4; j++) {
+                const uint8_t byte = blk[2 + sub * 4 + j];
+                for (int k = 0; k < 4; k++) {
+                    const int qv = (byte >> (2 * k)) & 3, e = j * 4 + k;
+                    if (type == OR_IQ2_XS) {
+                        ss += (float)(qv - 1) * in[e];
+                    } else {
+                        float v = (float)qv;
+                        if (e < 4 && ((sign >> e) & 1)) v = -v;
+                        ss += v * in[e];
+                    }
+                }
+            }
+            bs += dsc * ss;
+        }
+        sum += type == OR_IQ2_XXS ? d * bs : bs;
+    }
+    return sum;
+}
+
+// DequantIQ.IQ1S / IQ1M.DotProductScalar (DequantIQ.cs:814-856, :923-971):
+// blockSum += weight * x (weight 1 / -1 / 0, times sc for IQ1M), sum += d * blockSum.
+static float dot_iq1(int type, const uint8_t* row, const float* x, int n) {
+    const int bpb = type == OR_IQ1_S ? 50 : 56;
+    float sum = 0.f;
+    for (int b = 0; b < n / 256; b++) {
+        const uint8_t* blk = row + (size_t)b * bpb;
+        const float d = h2f(blk);
+        float bs = 0.f;
+        for (int sub = 0; sub < 32; sub++) {
+            float sc = 1.0f;
+            if (type == OR_IQ1_M && sub / 8 < 6) sc = ((blk[50 + sub / 8] >> (sub % 8)) & 1) == 1 ? 1.0f : 0.5f;
+            const uint8_t qs = blk[2 + sub];
+            for (int j = 0; j < 8; j++) {
+                const int bit = (qs >> j) & 1;
+                const int hbit = (blk[34 + sub / 2] >> ((sub % 2) * 4 + j / 2)) & 1;
+                const float w = bit ? sc : hbit ? -sc : 0.0f;
+                bs += w * x[256 * b + sub * 8 + j];
+            }
+        }
+        sum += d * bs;
+    }
+    return sum;
+}
+
 extern "C" float or_dot(int type, const uint8_t* row, const float* x, int n) {
     switch (type) {
         case OR_Q4_0: return dot_q4_0(row, x, n);
@@ -766,6 +1009,13 @@ extern "C" float or_dot(int type, const uint8_t* row, const float* x, int n) {
         case OR_Q8_K: return dot_q8_k(row, x, n);
         case OR_IQ4_NL: return dot_iq4_nl(row, x, n);
         case OR_IQ4_XS: return dot_iq4_xs(row, x, n);
+        case OR_IQ3_S: return dot_iq3_s(row, x, n, row + (size_t)(n / 256) * 110);
+        case OR_IQ3_XXS: return dot_iq3_xxs(row, x, n);
+        case OR_IQ2_XS:
+        case OR_IQ2_XXS:
+        case OR_IQ2_S: return dot_iq2(type, row, x, n);
+        case OR_IQ1_S:
+        case OR_IQ1_M: return dot_iq1(type, row, x, n);
         case OR_F32: return dot_f32((const float*)row, x, n);
         case OR_F16: return dot_f16(row, x, n);
         default: return NAN;
@@ -821,6 +1071,13 @@ static int row_bytes(int type, int in_dim, size_t* bpr) {
         case OR_Q8_K: *bpr = (size_t)(in_dim / 256) * 292; return 0;
         case OR_IQ4_NL: *bpr = (size_t)(in_dim / 32) * 18; return 0;
         case OR_IQ4_XS: *bpr = (size_t)(in_dim / 256) * 136; return 0;
+        case OR_IQ3_S: *bpr = (size_t)(in_dim / 256) * 110; return 0;
+        case OR_IQ3_XXS: *bpr = (size_t)(in_dim / 256) * 98; return 0;
+        case OR_IQ2_XS: *bpr = (size_t)(in_dim / 256) * 74; return 0;
+        case OR_IQ2_XXS: *bpr = (size_t)(in_dim / 256) * 66; return 0;
+        case OR_IQ2_S: *bpr = (size_t)(in_dim / 256) * 82; return 0;
+        case OR_IQ1_S: *bpr = (size_t)(in_dim / 256) * 50; return 0;
+        case OR_IQ1_M: *bpr = (size_t)(in_dim / 256) * 56; return 0;
         case OR_F32: *bpr = (size_t)in_dim * 4; return 0;
         case OR_F16: *bpr = (size_t)in_dim * 2; return 0;
         default: return -2;
@@ -831,7 +1088,13 @@ extern "C" int or_matvec(int type, const uint8_t* W, const float* x, float* y,
                          int out_dim, int in_dim, int nthreads) {
     size_t bpr;
     if (row_bytes(type, in_dim, &bpr)) return -2;
-    auto body = [&](int r) { y[r] = or_dot(type, W + (size_t)r * bpr, x, in_dim); };
+    // IQ3_S: the pointer-based dot reads past a row into the next one (and
+    // past the matrix reads 0), see dequant_iq3_s
+    const uint8_t* end = W + (size_t)out_dim * bpr;
+    auto body = [&](int r) {
+        y[r] = type == OR_IQ3_S ? dot_iq3_s(W + (size_t)r * bpr, x, in_dim, end)
+                                : or_dot(type, W + (size_t)r * bpr, x, in_dim);
+    };
     // ParallelRowThreshold = 512 (TensorMath.cs:28); MatVecMul (F32) and
     // MatVecMulF16 are sequential in the reference.
     bool par = out_dim >= 512 && type != OR_F32 && type != OR_F16;

@@ -47,7 +47,8 @@ extern "C" {
 /* GgmlType values (Gguf/GgufConstants.cs:41-71). */
 enum { OR_F32 = 0, OR_F16 = 1, OR_Q4_0 = 2, OR_Q4_1 = 3, OR_Q5_0 = 6, OR_Q5_1 = 7, OR_Q8_0 = 8,
        OR_Q2_K = 10, OR_Q3_K = 11, OR_Q4_K = 12, OR_Q5_K = 13, OR_Q6_K = 14, OR_Q8_K = 15,
-       OR_IQ4_NL = 20, OR_IQ4_XS = 23 };
+       OR_IQ2_XXS = 16, OR_IQ2_XS = 17, OR_IQ3_XXS = 18, OR_IQ1_S = 19, OR_IQ4_NL = 20, OR_IQ3_S = 21,
+       OR_IQ2_S = 22, OR_IQ4_XS = 23, OR_IQ1_M = 29 };
 
 float or_half_to_float(uint16_t h);
 uint16_t or_float_to_half(float f); /* IEEE round-to-nearest-even */

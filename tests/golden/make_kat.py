@@ -209,7 +209,8 @@ def cases() -> list[dict]:
 # library decodes: (type, block size, bytes per block)
 BYTESIZE = [(0, 1, 4), (1, 1, 2), (2, 32, 18), (3, 32, 20), (6, 32, 22), (7, 32, 24), (8, 32, 34),
             (10, 256, 84), (11, 256, 110), (12, 256, 144), (13, 256, 176), (14, 256, 210), (15, 256, 292),
-            (20, 32, 18), (23, 256, 136)]
+            (20, 32, 18), (23, 256, 136), (21, 256, 110), (18, 256, 98), (17, 256, 74), (16, 256, 66),
+            (22, 256, 82), (19, 256, 50), (29, 256, 56)]
 
 
 def main() -> None:

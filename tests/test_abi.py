@@ -44,7 +44,9 @@ def test_abi_version():
     (cn.TYPE_Q4_K, 257, 288), (cn.TYPE_Q6_K, 4096, 3360), (cn.TYPE_F32, 10, 40),
     (cn.TYPE_F16, 10, 20), (cn.TYPE_Q4_1, 32, 20), (cn.TYPE_Q5_0, 64, 44), (cn.TYPE_Q5_1, 33, 48),
     (cn.TYPE_Q8_0, 32, 34), (cn.TYPE_Q2_K, 256, 84), (cn.TYPE_Q3_K, 512, 220), (cn.TYPE_Q5_K, 257, 352),
-    (cn.TYPE_Q8_K, 256, 292), (cn.TYPE_IQ4_NL, 33, 36), (cn.TYPE_IQ4_XS, 256, 136), (16, 256, 0)])
+    (cn.TYPE_Q8_K, 256, 292), (cn.TYPE_IQ4_NL, 33, 36), (cn.TYPE_IQ4_XS, 256, 136),
+    (cn.TYPE_IQ2_XXS, 256, 66), (cn.TYPE_IQ2_XS, 512, 148), (cn.TYPE_IQ3_XXS, 256, 98), (cn.TYPE_IQ1_S, 257, 100),
+    (cn.TYPE_IQ3_S, 256, 110), (cn.TYPE_IQ2_S, 256, 82), (cn.TYPE_IQ1_M, 256, 56), (9, 32, 0)])
 def test_byte_size(t, elems, expected, oracle):
     assert cn.byte_size(t, elems) == expected
     assert oracle.lib.or_byte_size(t, elems) == expected

@@ -30,7 +30,8 @@ def test_descriptors_offsets_and_bytes(tmp_path):
                # the generic codecs: GGUF byte sizes from cn_byte_size (GgufTensorInfo.ByteSize)
                ("q5k.weight", cn.TYPE_Q5_K, (512, 3), bytes(range(256)) * 4 + bytes(32)),
                ("iq4nl.weight", cn.TYPE_IQ4_NL, (64, 2), bytes(72)),
-               ("q8k.weight", cn.TYPE_Q8_K, (256, 1), bytes(292))]
+               ("q8k.weight", cn.TYPE_Q8_K, (256, 1), bytes(292)),
+               ("iq2s.weight", cn.TYPE_IQ2_S, (256, 2), bytes(164)), ("iq1m.weight", cn.TYPE_IQ1_M, (512, 1), bytes(112))]
     md = [("general.architecture", gw.STR, "llama"), ("x.u8", gw.U8, 7), ("x.i8", gw.I8, -3),
           ("x.u16", gw.U16, 500), ("x.i16", gw.I16, -500), ("x.i32", gw.I32, -70000),
           ("x.u64", gw.U64, 1 << 40), ("x.i64", gw.I64, -(1 << 40)), ("x.f64", gw.F64, 0.125),

@@ -155,7 +155,7 @@ def test_matvec_errors(ctx):
     with pytest.raises(ValueError):
         ctx.matvec(W, np.zeros((33, 64), np.float32))
     with pytest.raises(cn.NotSupportedError):
-        ctx.upload(np.zeros(66, np.uint8), 16, 1, 256)  # IQ2_XXS: no decoder here
+        ctx.upload(np.zeros(36, np.uint8), 9, 1, 32)  # Q8_1: no decoder (and none in the reference)
     with pytest.raises(ValueError):
         ctx.upload(np.zeros(17, np.uint8), cn.TYPE_Q4_0, 1, 32)  # wrong byte count
 
@@ -217,11 +217,17 @@ def test_block32_matvec_parity(ctx, oracle, name, batch):
 
 
 # The 256-weight super-block codecs on the generic paths: Q2_K, Q3_K, Q5_K,
-# Q8_K, IQ4_XS (block bytes, offsets of the fp16 scale fields; Q8_K's scale
-# is an fp32 at 0)
+# Q8_K, IQ4_XS and the reference's simplified IQ2/IQ3/IQ1 decodes (block
+# bytes, offsets of the fp16 scale fields; Q8_K's scale is an fp32 at 0).
+# IQ3_S reads sign and scale bytes past its 110-byte block (the next block's
+# bytes; 0 past the tensor): the row slice below starts inside the tensor, so
+# its last block reads the following row's bytes, as the whole tensor does.
 SB = {"q2_k": (cn.TYPE_Q2_K, 84, (80, 82)), "q3_k": (cn.TYPE_Q3_K, 110, (108,)),
       "q5_k": (cn.TYPE_Q5_K, 176, (0, 2)), "q8_k": (cn.TYPE_Q8_K, 292, ()),
-      "iq4_xs": (cn.TYPE_IQ4_XS, 136, (0,))}
+      "iq4_xs": (cn.TYPE_IQ4_XS, 136, (0,)), "iq3_s": (cn.TYPE_IQ3_S, 110, (0,)),
+      "iq3_xxs": (cn.TYPE_IQ3_XXS, 98, (0,)), "iq2_xs": (cn.TYPE_IQ2_XS, 74, (0,)),
+      "iq2_xxs": (cn.TYPE_IQ2_XXS, 66, (0,)), "iq2_s": (cn.TYPE_IQ2_S, 82, (0,)),
+      "iq1_s": (cn.TYPE_IQ1_S, 50, (0,)), "iq1_m": (cn.TYPE_IQ1_M, 56, (0,))}
 
 
 def _rand_sb(name, rows, cols, seed):
