@@ -434,9 +434,15 @@ def gemv_mode(a) -> int:
     name, shape, batch = a.gemv.split(":")
     rows, cols = (int(v) for v in shape.split("x"))
     batch = int(batch)
-    t = {"q4_0": cn.TYPE_Q4_0, "q4_k": cn.TYPE_Q4_K, "q6_k": cn.TYPE_Q6_K}[name]
+    t = {"q4_0": cn.TYPE_Q4_0, "q4_k": cn.TYPE_Q4_K, "q6_k": cn.TYPE_Q6_K, "q8_0": cn.TYPE_Q8_0}[name]
     ctx = cn.Context(0)
-    W = ctx.synth(t, rows, cols, cn.synth_seed(2, f"gemv.{name}.{rows}x{cols}"))
+    if t == cn.TYPE_Q8_0:  # no seeded generator: seeded random blocks, fp16 scale 0.01
+        raw = np.random.default_rng(cn.synth_seed(2, f"gemv.{name}.{rows}x{cols}")).integers(
+            0, 256, size=(rows * cols // 32, 34), dtype=np.uint8)
+        raw[:, 0:2] = np.frombuffer(np.float16(0.01).tobytes(), np.uint8)
+        W = ctx.upload(raw.ravel(), t, rows, cols)
+    else:
+        W = ctx.synth(t, rows, cols, cn.synth_seed(2, f"gemv.{name}.{rows}x{cols}"))
     x = torch.from_numpy(cn.synth_fill(cn.TYPE_F32, batch, cols, cn.synth_seed(2, "gemv.x"))).cuda()
     y = torch.empty(batch, rows, device="cuda")
     ext = torch.cuda.ExternalStream(ctx.stream)

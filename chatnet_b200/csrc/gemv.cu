@@ -53,6 +53,12 @@ struct Fmt<CN_TYPE_Q4_0> {
     __device__ static int offset(int) { return 0; }
 };
 template <>
+struct Fmt<CN_TYPE_Q8_0> {
+    static constexpr int kBox = 272;  // bytes per row per unit (8 blocks of 34)
+    __device__ static int box_x(int u) { return 34 * u; }
+    __device__ static int offset(int) { return 0; }
+};
+template <>
 struct Fmt<CN_TYPE_Q4_K> {
     static constexpr int kBox = 144;  // one 144-byte super-block
     __device__ static int box_x(int u) { return 18 * u; }
@@ -183,6 +189,58 @@ __device__ __forceinline__ void unit_q4_0(const uint8_t* stw, const uint4* xf, i
         nib_hi(wh, p, q);
         a1[1] = h2_fma(p, k1_16, km72);
         a1[3] = h2_fma(q, k1_16, km72);
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            uint4 bx = bfrag<NT>(xf, b, nt, lane, live[nt]);
+            float tmp[4];
+            const float z[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t b0[2] = {bx.x, bx.y}, b1[2] = {bx.z, bx.w};
+            mma_16816(tmp, a0, b0, z);
+            mma_16816(tmp, a1, b1, tmp);
+            fma2(acc[nt][0], acc[nt][1], tmp[0], tmp[1], dg);
+            fma2(acc[nt][2], acc[nt][3], tmp[2], tmp[3], dh);
+        }
+    }
+}
+
+// Q8_0 (DequantQ8_0.cs:19-41; d@0, 32 int8 quants @2): each byte goes into
+// the A fragment as the fp16 1024 + (q + 128) (byte ^ 0x80 under the 0x64
+// exponent byte), minus 1152 = q, exact; d is applied to the fp32 partial
+// sums per block, as for Q4_0.
+__device__ __forceinline__ void s8_pairs(uint32_t w, uint32_t& a02, uint32_t& a13) {
+    const uint32_t u = w ^ 0x80808080u;
+    const uint32_t k1152 = 0x64806480u;  // half2(1152, 1152)
+    a02 = h2_sub(__byte_perm(u, 0x64646464u, 0x4240), k1152);
+    a13 = h2_sub(__byte_perm(u, 0x64646464u, 0x4341), k1152);
+}
+
+template <int NT>
+__device__ __forceinline__ void unit_q8_0(const uint8_t* stw, const uint4* xf, int row0, int g,
+                                          int t, int lane, const bool* live, float (&acc)[NT][4]) {
+    const uint8_t* rg = stw + (row0 + g) * 272;
+    const uint8_t* rh = rg + 8 * 272;
+#pragma unroll
+    for (int b = 0; b < 8; b++) {
+        const float dg = half_bits_to_float(lds_u16(rg + 34 * b));
+        const float dh = half_bits_to_float(lds_u16(rh + 34 * b));
+        // positions 4t..4t+3 (first k-step) and 16+4t..16+4t+3 (second)
+        uint32_t wg0, wh0, wg1, wh1;
+        if (b & 1) {
+            wg0 = word_at<0>(rg, 34 * b + 2 + 4 * t);
+            wh0 = word_at<0>(rh, 34 * b + 2 + 4 * t);
+            wg1 = word_at<0>(rg, 34 * b + 18 + 4 * t);
+            wh1 = word_at<0>(rh, 34 * b + 18 + 4 * t);
+        } else {
+            wg0 = word_at<2>(rg, 34 * b + 2 + 4 * t);
+            wh0 = word_at<2>(rh, 34 * b + 2 + 4 * t);
+            wg1 = word_at<2>(rg, 34 * b + 18 + 4 * t);
+            wh1 = word_at<2>(rh, 34 * b + 18 + 4 * t);
+        }
+        uint32_t a0[4], a1[4];
+        s8_pairs(wg0, a0[0], a0[2]);
+        s8_pairs(wh0, a0[1], a0[3]);
+        s8_pairs(wg1, a1[0], a1[2]);
+        s8_pairs(wh1, a1[1], a1[3]);
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
             uint4 bx = bfrag<NT>(xf, b, nt, lane, live[nt]);
@@ -525,6 +583,8 @@ __global__ void __launch_bounds__(kThreads, Geo<TYPE, NT>::kMinCtas)
         for (int nt = 0; nt < NT; nt++) au[nt][0] = au[nt][1] = au[nt][2] = au[nt][3] = 0.f;
         if constexpr (TYPE == CN_TYPE_Q4_0) {
             unit_q4_0<NT>(st, xf, warp * 16, g, t, lane, live, au);
+        } else if constexpr (TYPE == CN_TYPE_Q8_0) {
+            unit_q8_0<NT>(st, xf, warp * 16, g, t, lane, live, au);
         } else if constexpr (TYPE == CN_TYPE_Q4_K) {
             const float* xs = reinterpret_cast<const float*>(st + G::kW + G::kXF);
             unit_q4_k<NT>(st, xf, xs, table + warp * 128, warp * 16, g, t, lane, live, au);
@@ -1063,6 +1123,7 @@ static EncodeTiledFn get_encode() {
 static int box_bytes(int type) {
     switch (type) {
         case CN_TYPE_Q4_0: return Fmt<CN_TYPE_Q4_0>::kBox;
+        case CN_TYPE_Q8_0: return Fmt<CN_TYPE_Q8_0>::kBox;
         case CN_TYPE_Q4_K: return Fmt<CN_TYPE_Q4_K>::kBox;
         case CN_TYPE_Q6_K: return Fmt<CN_TYPE_Q6_K>::kBox;
         default: return 0;
@@ -1160,6 +1221,7 @@ int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool
         default: occ = occupancy_ctas<T, 8>(ctx); break;           \
     }
     if (type == CN_TYPE_Q4_0) { CN_OCC(CN_TYPE_Q4_0) }
+    else if (type == CN_TYPE_Q8_0) { CN_OCC(CN_TYPE_Q8_0) }
     else if (type == CN_TYPE_Q4_K) { CN_OCC(CN_TYPE_Q4_K) }
     else { CN_OCC(CN_TYPE_Q6_K) }
 #undef CN_OCC
@@ -1368,6 +1430,7 @@ int gemv_run(cn_ctx* ctx, cudaStream_t st, const GemvOp& op, const float* d_x, c
         default: return launch_tma<T, 8>(&tmp, map, p, a);           \
     }
     if (op.type == CN_TYPE_Q4_0) { CN_DISPATCH(CN_TYPE_Q4_0) }
+    if (op.type == CN_TYPE_Q8_0) { CN_DISPATCH(CN_TYPE_Q8_0) }
     if (op.type == CN_TYPE_Q4_K) { CN_DISPATCH(CN_TYPE_Q4_K) }
     CN_DISPATCH(CN_TYPE_Q6_K)
 #undef CN_DISPATCH

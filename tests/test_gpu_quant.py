@@ -216,6 +216,17 @@ def test_block32_matvec_parity(ctx, oracle, name, batch):
     assert rel_err(ctx.matvec(W, x), oracle.matvec(t, blocks, x, rows)) <= REL_TOL
 
 
+@pytest.mark.parametrize("rows,cols,batch", [(4096, 4096, 1), (300, 2048, 5), (1000, 4096, 16), (129, 768, 32),
+                                            (96, 1056, 2)])
+def test_q8_0_matvec_parity(ctx, oracle, rows, cols, batch):
+    """Q8_0 on the tiled fp16 GEMV (whole 256-column units: every n-tile
+    count, a partial row tile) and, at 1056 columns, on the generic kernel."""
+    t, blocks = _rand_b32("q8_0", rows, cols, 31 + batch)
+    W = ctx.upload(blocks, t, rows, cols)
+    x = _x(batch, cols, f"q8.x.{rows}.{cols}.{batch}")
+    assert rel_err(ctx.matvec(W, x), oracle.matvec(t, blocks, x, rows)) <= REL_TOL
+
+
 # The 256-weight super-block codecs on the generic paths: Q2_K, Q3_K, Q5_K,
 # Q8_K, IQ4_XS and the reference's simplified IQ2/IQ3/IQ1 decodes (block
 # bytes, offsets of the fp16 scale fields; Q8_K's scale is an fp32 at 0).
