@@ -65,7 +65,9 @@ struct Geo {
     static constexpr int kXchg = DEEP == 2 ? 2 * kCons * 32 * NT * 4 : 0;  // group partials, two buffers
     static constexpr int kSmem = kStages * kStage + 256 + kXchg;
 };
-static_assert(Geo<1>::kStages >= 3 && Geo<3>::kStages >= 4 && Geo<8>::kStages >= 4, "pipeline depth");
+static_assert(Geo<1>::kStages >= 3 && Geo<3>::kStages >= 4 && Geo<8>::kStages >= 4 && Geo<16>::kStages >= 3,
+              "pipeline depth");
+static_assert(Geo<16, 1>::kSmem <= 227 * 1024 && Geo<16, 1>::kStages >= 5, "16-sequence deep pipeline");
 static_assert(Geo<1, 1>::kStages >= 8 && Geo<8, 1>::kStages >= 7 && Geo<8, 1>::kSmem <= 227 * 1024,
               "deep pipeline depth");
 
@@ -83,7 +85,7 @@ struct Args {
     int64_t rows[kMaxMats];
     float* y[kMaxMats];   // [batch][rows[m]]
     const uint8_t* xrec;  // [unit][rec_bytes(NT)]
-    float* partials;      // [2 * ctas][128][8]
+    float* partials;      // [2 * ctas][128][kMaxNB]
     int* counters;        // [tiles][kCons], zero on entry, left zero
     uint32_t* err;
     XchgOut xo;           // size > 1: outputs go to every rank (one matrix only)
@@ -172,10 +174,12 @@ __device__ __forceinline__ int owner_of(int64_t v, int64_t total, int C) {
 
 // Which (row, sequence) pairs a consumer thread owns after the per-unit
 // recombination: row (t & 1 ? g + 8 : g) of its warp's 16 and, per n-tile nt,
-// sequence 2 nt + t / 2 (batch > 1) or sequence 0 for t < 2 (batch 1).
+// sequence 2 nt + t / 2 (batch > 1) or sequence 0 for t < 2 (batch 1); -1
+// past the call's batch (the 16-sequence form runs batches 9-16).
 template <int NB>
-__device__ __forceinline__ int owned_seq(int nt, int t) {
-    return NB == 1 ? (t < 2 ? 0 : -1) : (2 * nt + (t >> 1) < NB ? 2 * nt + (t >> 1) : -1);
+__device__ __forceinline__ int owned_seq(int nt, int t, int batch) {
+    const int b = NB == 1 ? (t < 2 ? 0 : -1) : 2 * nt + (t >> 1);
+    return b < NB && b < batch ? b : -1;
 }
 
 // Stores the owned values of a finished 16-row sub-tile, or, for a tile
@@ -196,16 +200,16 @@ __device__ void finish_subtile(const Args& a, int r, int t, int warp, int tile, 
         if (row < rows) {
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
-                const int b = owned_seq<NB>(nt, t);
+                const int b = owned_seq<NB>(nt, t, a.batch);
                 if (b >= 0) store_out(a, y, rows, b, row, acc[nt], seq);
             }
         }
         return;
     }
-    float* p = a.partials + ((size_t)(2 * cta + my_slot) * kRows + r) * 8;
+    float* p = a.partials + ((size_t)(2 * cta + my_slot) * kRows + r) * kMaxNB;
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
-        const int b = owned_seq<NB>(nt, t);
+        const int b = owned_seq<NB>(nt, t, a.batch);
         if (b >= 0) p[b] = acc[nt];
     }
     // __syncwarp orders the lanes' partials before lane 0's release-acquire
@@ -222,13 +226,13 @@ __device__ void finish_subtile(const Args& a, int r, int t, int warp, int tile, 
     if (old != c_last - c_first) return;
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
-        const int b = owned_seq<NB>(nt, t);
+        const int b = owned_seq<NB>(nt, t, a.batch);
         if (b < 0) continue;
         float s = 0.f;
         for (int c = c_first; c <= c_last; c++) {
             const int first_tile = (int)(range_start(total, c, C) / a.units);
             const int slot = 2 * c + (tile == first_tile ? 0 : 1);
-            s += __ldcg(a.partials + ((size_t)slot * kRows + r) * 8 + b);
+            s += __ldcg(a.partials + ((size_t)slot * kRows + r) * kMaxNB + b);
         }
         if (row < rows) store_out(a, y, rows, b, row, s, seq);
     }
@@ -593,6 +597,11 @@ int gemv_i8_ctas(int sms, int tiles, int units, int batch) {
         if (sh > units) sh = units;
         return tiles * sh;
     }
+    // Four or more n-tiles (batch 7-16): one CTA per SM as well, the deep
+    // pipeline.  Measured on B200, Llama-2-70B decode step: batch 8 19.76 ->
+    // 18.37 ms, batch 16 35.21 -> 30.93 ms against two three-stage CTAs per
+    // SM; batch 4 unchanged (12.85 / 12.76 ms), so it keeps the shared grid.
+    if (i8::n_tiles(batch) >= 4 && tile_cap_env() < 0) return total < sms ? (int)total : sms;
     // otherwise every resident CTA, each at least min_units_per_cta() units
     // (but at least one CTA per SM); at most tile_share_cap() CTAs per tile
     int64_t want = total / min_units_per_cta();
@@ -606,7 +615,7 @@ int gemv_i8_ctas(int sms, int tiles, int units, int batch) {
 size_t gemv_i8_xbytes(int64_t cols, int batch) {
     return (size_t)(cols / 256) * i8::rec_bytes(i8::n_tiles(batch));
 }
-size_t gemv_i8_partial_bytes(int ctas) { return (size_t)2 * ctas * i8::kRows * 8 * sizeof(float); }
+size_t gemv_i8_partial_bytes(int ctas) { return (size_t)2 * ctas * i8::kRows * i8::kMaxNB * sizeof(float); }
 
 static int g_sms[64] = {0};
 
@@ -622,7 +631,7 @@ int gemv_i8_prepare() {
                                  i8::Geo<NB, 0>::kSmem));                                                 \
     CN_CUDA(cudaFuncSetAttribute(gemv_i8_q4k_kernel<NB, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
                                  i8::Geo<NB, 1>::kSmem));
-    CN_ATTR(1) CN_ATTR(2) CN_ATTR(3) CN_ATTR(4) CN_ATTR(5) CN_ATTR(6) CN_ATTR(7) CN_ATTR(8)
+    CN_ATTR(1) CN_ATTR(2) CN_ATTR(3) CN_ATTR(4) CN_ATTR(5) CN_ATTR(6) CN_ATTR(7) CN_ATTR(8) CN_ATTR(16)
 #undef CN_ATTR
     CN_CUDA(cudaFuncSetAttribute(gemv_i8_q4k_kernel<1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  i8::Geo<1, 2>::kSmem));
@@ -690,6 +699,14 @@ int gemv_i8_run_group(cudaStream_t st, uint32_t* err, int nmat, const CUtensorMa
                              (size_t)i8::Geo<NB, 0>::kSmem, st, mp, a));                           \
         break;
         CN_I8(1) CN_I8(2) CN_I8(3) CN_I8(4) CN_I8(5) CN_I8(6) CN_I8(7) CN_I8(8)
+        default:  // batches 9-16: the 16-sequence form
+            if (deep)
+                CN_CUDA(launch_k(true, gemv_i8_q4k_kernel<16, 1>, dim3(ctas), dim3(i8::Geo<16, 1>::kThreads),
+                                 (size_t)i8::Geo<16, 1>::kSmem, st, mp, a));
+            else
+                CN_CUDA(launch_k(true, gemv_i8_q4k_kernel<16, 0>, dim3(ctas), dim3(i8::Geo<16, 0>::kThreads),
+                                 (size_t)i8::Geo<16, 0>::kSmem, st, mp, a));
+            break;
 #undef CN_I8
     }
     CN_CUDA(cudaGetLastError());

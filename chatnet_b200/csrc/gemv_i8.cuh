@@ -7,7 +7,7 @@
 namespace cn {
 namespace i8 {
 
-constexpr int kMaxNB = 8;  // sequences per call
+constexpr int kMaxNB = 16;  // sequences per call
 
 // Activations enter the integer GEMV as exact integers: per 256-position
 // unit u and sequence b, X = rint(x * 2^e) with e chosen so |X| <= 2^22, and
@@ -22,22 +22,27 @@ constexpr int kMaxNB = 8;  // sequences per call
 //             16+4t+i, so the lo * d(p') terms cancel and each column sums to
 //             16 * sum_p q_p d_i(p).
 //   batch >1: 3 base-256 digits, X = sum d_i 256^i, column 4b + i (column
-//             4b + 3 zero).
+//             4b + 3 zero).  Batches 9-16 use the 16-sequence form (8
+//             n-tiles, columns of absent sequences zero).
 // Record of unit u (rec_bytes(NT) bytes, NT = n-tiles of 8 columns):
 //   [0, 2048 NT)      B fragments of m16n8k32: sub-block j, n-tile nt, lane L
 //                     at ((j * NT + nt) * 32 + L) * 8: {b0, b1} = column
 //                     nt*8 + L/4 at positions 32j + 4(L%4) + 0..3 and
 //                     32j + 16 + 4(L%4) + 0..3;
-//   [2048 NT, +256)   xsd: int8 [8 sequences][4 digits k][8 sub-blocks j]:
+//   [2048 NT, +32 S)  xsd: int8 [S sequences][4 digits k][8 sub-blocks j]:
 //                     XS_j = sum of X over sub-block j = sum_k 256^k xsd[k][j]
 //                     (balanced digits, so a dp4a against the row's packed
 //                     6-bit mins gives sum_j m_j XS_j digit by digit);
-//   [2048 NT+256, +32) inv: fp32 [8 sequences], 2^-e (batch 1: 2^-e / 16,
-//                     which undoes the digits' factor 16).
-__host__ __device__ constexpr int n_tiles(int batch) { return batch == 1 ? 1 : (4 * batch + 7) / 8; }
-__host__ __device__ constexpr int rec_bytes(int nt) { return 2048 * nt + 288; }
+//   [2048 NT+32 S, +4 S) inv: fp32 [S sequences], 2^-e (batch 1: 2^-e / 16,
+//                     which undoes the digits' factor 16);
+// S = rec_seqs(NT): 8, or 16 for the 8-n-tile form.
+__host__ __device__ constexpr int n_tiles(int batch) {
+    return batch == 1 ? 1 : batch <= 8 ? (4 * batch + 7) / 8 : 8;
+}
+__host__ __device__ constexpr int rec_seqs(int nt) { return nt <= 4 ? 8 : 16; }
+__host__ __device__ constexpr int rec_bytes(int nt) { return 2048 * nt + 36 * rec_seqs(nt); }
 __host__ __device__ constexpr int xs_off(int nt) { return 2048 * nt; }
-__host__ __device__ constexpr int inv_off(int nt) { return 2048 * nt + 256; }
+__host__ __device__ constexpr int inv_off(int nt) { return 2048 * nt + 32 * rec_seqs(nt); }
 
 // One warp writes unit u of sequence b.  Lane (c = lane/4, t = lane%4) holds
 // in v[0..3] positions 32c + 4t + 0..3 and in v[4..7] positions
