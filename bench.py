@@ -166,10 +166,10 @@ def measured_peak_gbs() -> tuple[float, str]:
 
 def gemv_kernel_name(config: int, batch: int) -> str:
     """The GEMV kernel family the library runs for the config's projections
-    (Q4_K decode at batch 1..8: the integer mma.sync kernel unless the
+    (Q4_K decode at batch 1..16: the integer mma.sync kernel unless the
     environment selects another; Q4_0 and larger batches: the fp16 one)."""
     choice = os.environ.get("CHATNET_GEMV", "i8")
-    if config == 4 and batch <= 8 and choice not in ("tc", "mma"):
+    if config == 4 and batch <= 16 and choice not in ("tc", "mma"):
         return "gemv_i8_q4k"
     if config == 4 and batch <= 5 and choice == "tc":
         return "gemv_tc_q4k"
