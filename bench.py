@@ -19,8 +19,10 @@ Printed JSON line (rank 0):
   e2e        the same through cn_llama_decode with host buffers: token ids
              and positions copied in, logits and argmax copied out per step
   roofline   the dominant kernel (the fused Q4_K dequant-GEMV of the FFN
-             gate/up projections, 28672 x 8192) timed alone on the context
-             stream: algorithmic bytes per launch / mean launch time
+             gate and up projections, 57344 x 8192 as the one launch the
+             step runs) timed alone on the context stream, cycling through
+             the 80 layers' matrices: algorithmic bytes per launch / mean
+             launch time
   cpu_baseline  the oracle port of the reference's C# CPU path timed on the
              host's cores over the whole step (CpuSample)
 With --gpus N > 1 the ranks run the model tensor-parallel (default; the
@@ -882,11 +884,17 @@ def main():
     e2e = tokens_per_step * 1000.0 / ms_e2e
     assert np.isfinite(lg).all()
 
-    # roofline: the dominant kernel timed alone (FFN gate projection)
-    us, nbytes = model.time_gemv(4, B, iters=2 * dc.model.n_layers)
+    # roofline: the dominant kernel timed alone -- the FFN gate and up matrices as
+    # the one launch the step runs (a model that runs them apart: the gate GEMV)
+    hid = dc.model.hidden_dim // (world if tp_mode else 1)  # this rank's shard
+    try:
+        us, nbytes = model.time_gemv(9, B, iters=2 * dc.model.n_layers)
+        shape, what = f"{2 * hid}x{dc.model.dim}", "gate/up, one launch"
+    except cn.NotSupportedError:
+        us, nbytes = model.time_gemv(4, B, iters=2 * dc.model.n_layers)
+        shape, what = f"{hid}x{dc.model.dim}", "gate"
     peak, peak_kind = measured_peak_gbs()
     achieved = nbytes / (us * 1e-6) / 1e9
-    shape = f"{dc.model.hidden_dim // (world if tp_mode else 1)}x{dc.model.dim}"  # this rank's gate shard
     gemv_name = gemv_kernel_name(a.config, B)
     traffic = committed_traffic(f"{gemv_name}_{shape}_b{B}")
     kernels = model.step_kernels(B)
@@ -911,7 +919,7 @@ def main():
                     "d2h_bytes_per_step": B * (dc.model.vocab * 4 + 4)},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": f"{gemv_name} {shape} batch {B}",
+                         "kernel": f"{gemv_name} {shape} ({what}) batch {B}",
                          "us_per_launch": us, "bytes_per_launch": nbytes,
                          "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
             "cpu_baseline": cpu,

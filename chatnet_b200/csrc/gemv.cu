@@ -1190,12 +1190,12 @@ int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool
     p->path = kPathMma;
     if (!tma) return CN_OK;
     const int q4k_path = type == CN_TYPE_Q4_K ? gemv_q4k_path() : kPathMma;
-    // batches 9-16 take the integer kernel's 16-sequence form only on matrices
-    // of at least 8 units per SM: measured on B200 at batch 16, Llama-2-70B's
-    // 28672 x 8192 77 us against 84-92 us on the fp16 kernel, 11008 x 4096
-    // 33.5 against 36.0 us, but 4096 x 4096 (3.5 units per SM) 39.1 against 32.1 us
-    const bool i8_batch = batch <= 8 || (int64_t)p->tiles * p->units >= 8LL * ctx->sms;
-    if (q4k_path == kPathI8 && batch <= i8::kMaxNB && i8_batch) {
+    // batches 9-16 take the integer kernel's 16-sequence form (measured on B200
+    // at batch 16: Llama-2-70B's 28672 x 8192 77 us against 84-92 us on the
+    // fp16 kernel, 11008 x 4096 33.5 against 36.0 us; only a matrix of a few
+    // units per SM does worse, 4096 x 4096 39.1 against 32.1 us -- kept on the
+    // integer form so that a layer's q/k/v and gate/up still form one launch)
+    if (q4k_path == kPathI8 && batch <= i8::kMaxNB) {
         p->path = kPathI8;
         p->tiles = (int)((rows + 127) / 128);
         p->ctas = gemv_i8_ctas(ctx->sms, p->tiles, p->units, batch);

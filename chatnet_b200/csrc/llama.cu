@@ -1075,13 +1075,41 @@ int cn_llama_step_kernels(cn_llama* m, int batch, int* out_count) {
 int cn_llama_time_gemv(cn_llama* m, int proj, int batch, int iters, float* us_per_launch,
                        double* bytes_per_launch) {
     CN_CHECK(m && us_per_launch && bytes_per_launch, CN_ERR_INVALID_ARG, "null argument");
-    CN_CHECK(proj >= 0 && proj <= 7 && iters >= 1, CN_ERR_INVALID_ARG, "bad proj/iters");
+    CN_CHECK(proj >= 0 && proj <= 9 && iters >= 1, CN_ERR_INVALID_ARG, "bad proj/iters");
     CN_CHECK(batch >= 1 && batch <= m->cfg.max_batch, CN_ERR_INVALID_ARG, "bad batch");
     cudaSetDevice(m->ctx->device);
     int rc = build_step(m, batch);
     if (rc) return rc;
     Step& st = m->steps[batch];
     const int L = m->cfg.n_layers;
+    if (proj >= 8) {
+        // the grouped launch the step runs: q/k/v (8) or gate/up (9) in one GEMV
+        const std::vector<GemvGroup>& gs = proj == 8 ? st.qkv : st.gu;
+        CN_CHECK(L > 0 && gs[0].n > 0, CN_ERR_UNSUPPORTED, "this model runs those projections as separate launches");
+        float* ys[3] = {proj == 8 ? m->q : m->gate, proj == 8 ? m->k : m->up, m->v};
+        cudaStream_t s = m->ctx->stream;
+        if ((rc = gemv_prep(s, m->ctx->sms, gs[0].ops[0], m->xn, m->gb))) return rc;
+        for (int i = 0; i < 3; i++)
+            if ((rc = gemv_group_run(m->ctx, s, gs[i % L], m->gb, ys))) return rc;
+        cudaEvent_t e0, e1;
+        CN_CUDA(cudaEventCreate(&e0));
+        CN_CUDA(cudaEventCreate(&e1));
+        CN_CUDA(cudaEventRecord(e0, s));
+        for (int i = 0; i < iters; i++)
+            if ((rc = gemv_group_run(m->ctx, s, gs[(i + 3) % L], m->gb, ys))) return rc;
+        CN_CUDA(cudaEventRecord(e1, s));
+        CN_CUDA(cudaEventSynchronize(e1));
+        float ms = 0.f;
+        CN_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        *us_per_launch = ms * 1000.f / iters;
+        double bytes = 4.0 * batch * gs[0].ops[0].cols;
+        for (int k = 0; k < gs[0].n; k++)
+            bytes += (double)gs[0].ops[k].rb * gs[0].ops[k].rows + 4.0 * batch * gs[0].ops[k].rows;
+        *bytes_per_launch = bytes;
+        return check_dev_err_reset(m);
+    }
     auto op_of = [&](int i) -> const GemvOp& {
         return proj == 7 ? st.ops[(size_t)L * 7] : st.ops[(size_t)(i % L) * 7 + proj];
     };

@@ -361,10 +361,12 @@ int cn_llama_sample(cn_llama* m, int batch, float temperature, int top_k, float 
 int cn_llama_step_kernels(cn_llama* m, int batch, int* out_count);
 /* Times one projection's fused dequant-GEMV as the step runs it (activation
  * prep excluded): `iters` launches cycling through the layers' matrices of
- * projection `proj` (0..6 = q,k,v,o,gate,up,down; 7 = lm_head), with CUDA
- * events on the context's stream.  Reports the mean time per launch and
- * the launch's algorithmic bytes (weights + x + y).  (no reference
- * counterpart: roofline measurement) */
+ * projection `proj` (0..6 = q,k,v,o,gate,up,down; 7 = lm_head; 8 = the q/k/v
+ * and 9 = the gate/up matrices as the one grouped launch the step runs, or
+ * CN_ERR_UNSUPPORTED where the model runs them apart), with CUDA events on
+ * the context's stream.  Reports the mean time per launch and the launch's
+ * algorithmic bytes (weights + x + y).  (no reference counterpart: roofline
+ * measurement) */
 int cn_llama_time_gemv(cn_llama* m, int proj, int batch, int iters, float* us_per_launch,
                        double* bytes_per_launch);
 /* Runs one decode step for `batch` without its graph, recording an event
