@@ -312,7 +312,8 @@ int gemv_i8_run_group(cudaStream_t st, uint32_t* err, int nmat, const CUtensorMa
                       float* partials, int* counters, float* const* y, const XchgOut* xo = nullptr);
 
 // Several GEMVs that read the same activations (same inner dimension and
-// batch, all on the integer path) run as one launch: q/k/v, gate/up.
+// batch and weight type, all on the integer path or all on the fp16 one)
+// run as one launch: q/k/v, gate/up.
 struct GemvGroup {
     int n = 0;
     GemvOp ops[3];

@@ -96,8 +96,20 @@ struct Geo {
     static constexpr int kSmem = kFixed + kStages * kStage;
 };
 
+// Up to three matrices with the same input run as one launch (q/k/v,
+// gate/up): their 128-row tiles are numbered one after another, matrix m
+// owning tiles [toff[m], toff[m + 1]); nmat == 1 uses rows / y.
+constexpr int kMaxGroup = 3;
+struct GemvMaps {
+    CUtensorMap m[kMaxGroup];
+};
+
 struct GemvArgs {
     int64_t rows;
+    int nmat;
+    int toff[kMaxGroup + 1];
+    int64_t mrows[kMaxGroup];
+    float* my[kMaxGroup];
     int units;  // 256-position units per row
     int tiles;  // 128-row tiles
     int batch;
@@ -423,17 +435,37 @@ __device__ __forceinline__ int owner_of(int64_t v, int64_t total, int C) {
     return c;
 }
 
+// The matrix a tile belongs to: its index, its local tile number, rows and
+// output.
+__device__ __forceinline__ int tile_mat(const GemvArgs& a, int tile, int& local, int64_t& rows, float*& y) {
+    if (a.nmat <= 1) {
+        local = tile;
+        rows = a.rows;
+        y = a.y;
+        return 0;
+    }
+    const int m = (a.nmat > 2 && tile >= a.toff[2]) ? 2 : (tile >= a.toff[1]) ? 1 : 0;
+    local = tile - a.toff[m];
+    rows = a.mrows[m];
+    y = a.my[m];
+    return m;
+}
+
 // Writes the tile's rows directly (the CTA computed all of its units).
 template <int NT>
 __device__ __forceinline__ void store_rows(const GemvArgs& a, int tile, int warp, int g, int t,
                                            float (&acc)[NT][4]) {
-    const int64_t r0 = (int64_t)tile * kTileRows + warp * 16 + g, r1 = r0 + 8;
+    int local;
+    int64_t rows;
+    float* y;
+    tile_mat(a, tile, local, rows, y);
+    const int64_t r0 = (int64_t)local * kTileRows + warp * 16 + g, r1 = r0 + 8;
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
         int b = nt * 4 + t;
         if (b < a.batch) {
-            if (r0 < a.rows) a.y[(size_t)b * a.rows + r0] = acc[nt][0] + acc[nt][1];
-            if (r1 < a.rows) a.y[(size_t)b * a.rows + r1] = acc[nt][2] + acc[nt][3];
+            if (r0 < rows) y[(size_t)b * rows + r0] = acc[nt][0] + acc[nt][1];
+            if (r1 < rows) y[(size_t)b * rows + r1] = acc[nt][2] + acc[nt][3];
         }
     }
 }
@@ -471,12 +503,16 @@ __device__ void finish_shared(const GemvArgs& a, int tile, int warp, int cta, in
         const int slot = 2 * c + (tile == first_tile ? 0 : 1);
         src[ns++] = a.partials + ((size_t)slot * kTileRows + warp * 16) * BW;
     }
+    int local;
+    int64_t rows;
+    float* y;
+    tile_mat(a, tile, local, rows, y);
     for (int e = lane; e < 16 * BW; e += 32) {
         float s = 0.f;
         for (int k = 0; k < ns; k++) s += __ldcg(src[k] + e);
         const int row = e / BW, b = e % BW;
-        const int64_t r = (int64_t)tile * kTileRows + warp * 16 + row;
-        if (b < a.batch && r < a.rows) a.y[(size_t)b * a.rows + r] = s;
+        const int64_t r = (int64_t)local * kTileRows + warp * 16 + row;
+        if (b < a.batch && r < rows) y[(size_t)b * rows + r] = s;
     }
     if (lane == 0) atomicExch(ctr, 0);
 }
@@ -494,7 +530,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 
 template <int TYPE, int NT>
 __global__ void __launch_bounds__(kThreads, Geo<TYPE, NT>::kMinCtas)
-    gemv_kernel(const __grid_constant__ CUtensorMap map, const GemvArgs a) {
+    gemv_kernel(const __grid_constant__ GemvMaps maps, const GemvArgs a) {
     using G = Geo<TYPE, NT>;
     constexpr int S = G::kStages;
     // Dynamic shared memory starts at the CTA's shared window (no static
@@ -539,7 +575,13 @@ __global__ void __launch_bounds__(kThreads, Geo<TYPE, NT>::kMinCtas)
             }
             uint8_t* st = stages + s * G::kStage;
             mbar_expect_tx(&full[s], G::kBytes);
-            tma_load_2d(st, &map, Fmt<TYPE>::box_x(u), tile * kTileRows, &full[s]);
+            {
+                int local;
+                int64_t rows;
+                float* y;
+                const int m = tile_mat(a, tile, local, rows, y);
+                tma_load_2d(st, &maps.m[m], Fmt<TYPE>::box_x(u), local * kTileRows, &full[s]);
+            }
             bulk_g2s(st + G::kW, a.xfrag + (size_t)u * 8 * NT * 32, G::kXF, &full[s]);
             if constexpr (G::kXS > 0)
                 bulk_g2s(st + G::kW + G::kXF, a.xsum + (size_t)u * 8 * NT * 4, G::kXS, &full[s]);
@@ -1252,9 +1294,9 @@ int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool
 }
 
 template <int TYPE, int NT>
-static int launch_tma(cn_ctx* ctx, const CUtensorMap* map, const GemvPlan& p, const GemvArgs& a) {
+static int launch_tma(cn_ctx* ctx, const GemvMaps* maps, const GemvPlan& p, const GemvArgs& a) {
     CN_CUDA(launch_k(true, gemv_kernel<TYPE, NT>, dim3(p.ctas), dim3(kThreads), (size_t)Geo<TYPE, NT>::kSmem,
-                     ctx->stream, *map, a));
+                     ctx->stream, *maps, a));
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }
@@ -1388,6 +1430,9 @@ int norm_prep(cudaStream_t st, const float* x, const float* w, float* y, int n, 
     return add_norm_prep(st, x, nullptr, nullptr, w, y, n, rows, eps, op, b);
 }
 
+static int gemv_mma_launch(cn_ctx* ctx, cudaStream_t st, const GemvOp* ops, int n, const GemvPlan& p,
+                           const GemvBufs& b, float* const* y);
+
 int gemv_run(cn_ctx* ctx, cudaStream_t st, const GemvOp& op, const float* d_x, const GemvBufs& b,
              float* d_y, const XchgOut* xo) {
     CN_CHECK((reinterpret_cast<uintptr_t>(d_y) & 3) == 0, CN_ERR_INVALID_ARG, "y must be aligned");
@@ -1411,32 +1456,53 @@ int gemv_run(cn_ctx* ctx, cudaStream_t st, const GemvOp& op, const float* d_x, c
     if (op.plan.path == kPathTc)
         return gemv_tc_run(st, ctx->dev_err, &op.map, op.rows, op.cols, op.batch, op.plan.ctas,
                            reinterpret_cast<const uint8_t*>(b.xfrag), b.partials, b.counters, d_y);
-    GemvArgs a;
-    a.rows = op.rows;
-    a.units = op.plan.units;
-    a.tiles = op.plan.tiles;
-    a.batch = op.batch;
+    return gemv_mma_launch(ctx, st, &op, 1, op.plan, b, &d_y);
+}
+
+// The fp16 mma.sync GEMV over n matrices of one type with the same input
+// (one launch; n == 1: a single matrix).
+static int gemv_mma_launch(cn_ctx* ctx, cudaStream_t st, const GemvOp* ops, int n, const GemvPlan& p,
+                           const GemvBufs& b, float* const* y) {
+    GemvArgs a = {};
+    GemvMaps maps;
+    a.nmat = n;
+    int tiles = 0;
+    for (int i = 0; i < kMaxGroup; i++) {
+        const int mi = i < n ? i : n - 1;
+        maps.m[i] = ops[mi].map;
+        a.toff[i] = tiles;
+        if (i < n) {
+            a.mrows[i] = ops[i].rows;
+            a.my[i] = y[i];
+            tiles += (int)((ops[i].rows + kTileRows - 1) / kTileRows);
+        }
+    }
+    a.toff[kMaxGroup] = tiles;
+    CN_CHECK(tiles == p.tiles, CN_ERR_INVALID_ARG, "GEMV plan does not match its matrices");
+    a.rows = ops[0].rows;
+    a.y = y[0];
+    a.units = p.units;
+    a.tiles = p.tiles;
+    a.batch = ops[0].batch;
     a.xfrag = b.xfrag;
     a.xsum = b.xsum;
     a.xinv = b.xinv;
-    a.y = d_y;
     a.partials = b.partials;
     a.counters = b.counters;
     a.err = ctx->dev_err;
-    const GemvPlan& p = op.plan;
-    const CUtensorMap* map = &op.map;
     cn_ctx tmp = *ctx;
     tmp.stream = st;
 #define CN_DISPATCH(T)                                               \
     switch (p.nt) {                                                  \
-        case 1: return launch_tma<T, 1>(&tmp, map, p, a);            \
-        case 2: return launch_tma<T, 2>(&tmp, map, p, a);            \
-        case 4: return launch_tma<T, 4>(&tmp, map, p, a);            \
-        default: return launch_tma<T, 8>(&tmp, map, p, a);           \
+        case 1: return launch_tma<T, 1>(&tmp, &maps, p, a);          \
+        case 2: return launch_tma<T, 2>(&tmp, &maps, p, a);          \
+        case 4: return launch_tma<T, 4>(&tmp, &maps, p, a);          \
+        default: return launch_tma<T, 8>(&tmp, &maps, p, a);         \
     }
-    if (op.type == CN_TYPE_Q4_0) { CN_DISPATCH(CN_TYPE_Q4_0) }
-    if (op.type == CN_TYPE_Q8_0) { CN_DISPATCH(CN_TYPE_Q8_0) }
-    if (op.type == CN_TYPE_Q4_K) { CN_DISPATCH(CN_TYPE_Q4_K) }
+    const int type = ops[0].type;
+    if (type == CN_TYPE_Q4_0) { CN_DISPATCH(CN_TYPE_Q4_0) }
+    if (type == CN_TYPE_Q8_0) { CN_DISPATCH(CN_TYPE_Q8_0) }
+    if (type == CN_TYPE_Q4_K) { CN_DISPATCH(CN_TYPE_Q4_K) }
     CN_DISPATCH(CN_TYPE_Q6_K)
 #undef CN_DISPATCH
 }
@@ -1444,14 +1510,23 @@ int gemv_run(cn_ctx* ctx, cudaStream_t st, const GemvOp& op, const float* d_x, c
 int gemv_group_make(cn_ctx* ctx, const GemvOp* ops, int n, GemvGroup* g) {
     CN_CHECK(n >= 1 && n <= 3, CN_ERR_INVALID_ARG, "a GEMV group has 1..3 members");
     int64_t rows = 0;
+    const int path = ops[0].plan.path;
     for (int i = 0; i < n; i++) {
         const GemvOp& o = ops[i];
-        if (o.plan.path != kPathI8 || o.cols != ops[0].cols || o.batch != ops[0].batch || o.type != ops[0].type)
+        if ((o.plan.path != kPathI8 && o.plan.path != kPathMma) || !o.tma || o.plan.path != path ||
+            o.cols != ops[0].cols || o.batch != ops[0].batch || o.type != ops[0].type)
             return set_error(CN_ERR_UNSUPPORTED, "GEMVs cannot share a launch");
         g->ops[i] = o;
         rows += (o.rows + 127) / 128 * 128;
     }
     g->n = n;
+    if (path == kPathMma) {
+        // the fp16 kernel's stream-K plan over the concatenated row tiles
+        int rc = gemv_plan(ctx, ops[0].type, rows, ops[0].cols, ops[0].batch, true, &g->plan);
+        if (rc) return rc;
+        CN_CHECK(g->plan.path == kPathMma, CN_ERR_UNSUPPORTED, "GEMVs cannot share a launch");
+        return CN_OK;
+    }
     GemvPlan p = ops[0].plan;
     p.tiles = (int)(rows / 128);
     p.ctas = gemv_i8_ctas(ctx->sms, p.tiles, p.units, ops[0].batch);
@@ -1462,6 +1537,9 @@ int gemv_group_make(cn_ctx* ctx, const GemvOp* ops, int n, GemvGroup* g) {
 }
 
 int gemv_group_run(cn_ctx* ctx, cudaStream_t st, const GemvGroup& g, const GemvBufs& b, float* const* y) {
+    for (int i = 0; i < g.n; i++)
+        CN_CHECK((reinterpret_cast<uintptr_t>(y[i]) & 3) == 0, CN_ERR_INVALID_ARG, "y must be aligned");
+    if (g.plan.path == kPathMma) return gemv_mma_launch(ctx, st, g.ops, g.n, g.plan, b, y);
     const CUtensorMap* maps[3];
     int64_t rows[3];
     for (int i = 0; i < g.n; i++) {
