@@ -1276,13 +1276,30 @@ int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool
     // Stream-K grid: every resident CTA gets an equal share of the
     // (tile, unit) space, but at least 2 units each.
     const int64_t total = (int64_t)p->tiles * p->units;
-    int64_t want = total / 2 > 0 ? total / 2 : 1;
+    int min_units = 2;
+#ifdef CHATNET_TUNING
+    if (const char* e = getenv("CHATNET_MMA_MIN_UNITS")) min_units = atoi(e) > 0 ? atoi(e) : 2;
+#endif
+    int64_t want = total / min_units > 0 ? total / min_units : 1;
     // at most 8 CTAs may share a tile (the fix-up sums up to 8 partials):
     // ranges of at least units/7 units guarantee that
     const int64_t cap = (int64_t)p->tiles * 7 > 0 ? (int64_t)p->tiles * 7 : 1;
     if (want > cap) want = cap;
     int ctas = ctx->sms * occ;
     if (want < ctas) ctas = (int)want;
+    // Whole tiles for short rows when there are enough tiles: one CTA per
+    // 128-row tile of at most 16 units, none shared (a shared tile's fix-up --
+    // partials, fence, counter, the last CTA's sum -- costs more there than
+    // the extra CTAs gain).  Measured on B200 (prep + GEMV replayed from a
+    // graph): Q4_0 5632 x 2048 (44 tiles) 11.9 -> 10.9 us, Q6_K 32000 x 4096
+    // 35.0 -> 29.9 us, Q4_K 11008 x 4096 at batch 32 53.5 -> 42.2 us,
+    // TinyLlama decode 621 -> 651 tok/s; long rows (Llama-2-70B's O and down
+    // at batch 32) lose with whole tiles (611 -> 504 tok/s) and keep the split.
+    int whole = 40;
+#ifdef CHATNET_TUNING
+    if (const char* e = getenv("CHATNET_MMA_WHOLE_TILES")) whole = atoi(e);
+#endif
+    if (whole > 0 && p->tiles >= whole && p->units <= 16 && p->tiles <= ctx->sms * occ) ctas = p->tiles;
     p->ctas = ctas;
     const int chunks = p->units * 8;
     p->xfrag_bytes = (size_t)chunks * p->nt * 32 * sizeof(uint4);
