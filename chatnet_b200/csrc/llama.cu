@@ -279,31 +279,6 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
             if ((rc = gemv(m, s, ops[2], m->xn, m->v, pc))) return rc;
         }
         if ((rc = mark(s, P_QKV))) return rc;
-        RopeKvArgs ra;
-        ra.q = m->q;
-        ra.k = m->k;
-        ra.v = m->v;
-        ra.rope = m->rope;
-        ra.pos_dev = m->pos;
-        ra.pos_host = 0;
-        ra.batch = B;
-        ra.n_heads = m->nh;
-        ra.n_kv = m->nkv;
-        ra.hd = c.head_dim;
-        ra.q_stride = qdim;
-        ra.kv_stride = kvd;
-        ra.kcache = m->kc;
-        ra.vcache = m->vc;
-        ra.cache_seq_stride = m->seq_stride;
-        ra.cache_layer_off = (int64_t)l * c.ctx_len * kvd;
-        ra.kv_f16 = c.kv_dtype == CN_KV_F16;
-        ra.ctx_len = c.ctx_len;
-        ra.err = m->ctx->dev_err;
-        ra.neox = c.rope_neox;
-        // the tensor-core attention (fp16 cache) rotates q and stores the new
-        // k/v rows itself; otherwise RoPE and the cache store run first
-        const bool fuse_rope = st.ap.mma;
-        if (!fuse_rope && ((rc = launch_rope_kv(ra, s)) || (rc = mark(s, P_ROPE)))) return rc;
         AttnArgs aa;
         aa.q = m->q;
         aa.kcache = m->kc;
@@ -316,22 +291,22 @@ static int enqueue_step(cn_llama* m, int B, cudaStream_t s) {
         aa.hd = c.head_dim;
         aa.q_stride = qdim;
         aa.cache_seq_stride = m->seq_stride;
-        aa.cache_layer_off = ra.cache_layer_off;
-        aa.kv_f16 = ra.kv_f16;
+        aa.cache_layer_off = (int64_t)l * c.ctx_len * kvd;
+        aa.kv_f16 = c.kv_dtype == CN_KV_F16;
         aa.ctx_len = c.ctx_len;
         aa.part = m->part;
         aa.counters = m->attn_ctr;
         aa.out = m->att;
         aa.out_stride = qdim;
         aa.prep = prep_target(&ops[3], m->gb);
-        if (fuse_rope) {
-            aa.rope.k = m->k;
-            aa.rope.v = m->v;
-            aa.rope.rope = m->rope;
-            aa.rope.kv_stride = kvd;
-            aa.rope.on = 1;
-            aa.rope.neox = c.rope_neox;
-        }
+        // TensorMath.ApplyRoPE of q and the new k row, and the new k/v rows'
+        // cache store, run inside the attention kernel
+        aa.rope.k = m->k;
+        aa.rope.v = m->v;
+        aa.rope.rope = m->rope;
+        aa.rope.kv_stride = kvd;
+        aa.rope.on = 1;
+        aa.rope.neox = c.rope_neox;
         if ((m->nh / m->nkv) * c.head_dim % 256 != 0) aa.prep.kind = -1;
         if ((rc = launch_attention(aa, st.ap, s)) || (rc = mark(s, P_ATTN))) return rc;
         pc = PrepCache();

@@ -1,12 +1,13 @@
 // ops.cu -- the decode-step kernels around the GEMVs.
 //
 //   rmsnorm_kernel     TensorMath.RmsNorm            (Tensors/TensorMath.cs:97-165)
-//   rope_kv_kernel     TensorMath.ApplyRoPE + the KV-cache store
-//                      (TensorMath.cs:408-458, Models/Llama/LlamaModel.cs:146-153)
 //   attn_split_kernel  LlamaModel.ComputeAttention + TensorMath.Softmax
 //                      (LlamaModel.cs:241-346, TensorMath.cs:177-241), split over
 //                      the context (flash-decoding); the last split CTA of each
-//                      (sequence, kv head) merges the splits
+//                      (sequence, kv head) merges the splits.  Both attention
+//                      kernels also apply TensorMath.ApplyRoPE to q and the
+//                      new k row and store the new k/v rows in the cache
+//                      (TensorMath.cs:408-458, Models/Llama/LlamaModel.cs:146-153)
 //   silu_mul_kernel    TensorMath.SiluElementwiseMul (TensorMath.cs:253-286)
 //   add_kernel         TensorMath.Add                (TensorMath.cs:712-733)
 //   embed_kernel       LlamaModel.LoadEmbedding      (LlamaModel.cs:365-394)
@@ -81,62 +82,6 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
 // ApplyRoPE does (theta = pos * exp(i * (1/hd) * -ln(base)), libm cos/sin),
 // so the rotation factors are bit-identical to the reference's.
 
-__global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ k,
-                               const float* __restrict__ v, const float2* __restrict__ rope,
-                               const int* __restrict__ pos_dev, int pos_host, int n_heads,
-                               int n_kv, int hd, int q_stride, int kv_stride, void* kcache,
-                               void* vcache, int64_t cache_seq_stride, int64_t cache_layer_off,
-                               int kv_f16, int ctx_len, uint32_t* err, int neox) {
-    pdl_trigger();
-    pdl_wait();
-    const int b = blockIdx.y;
-    const int pos = pos_dev ? pos_dev[b] : pos_host;
-    if (pos < 0 || pos >= ctx_len) {
-        if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(err, kErrBadArg);
-        return;
-    }
-    const int half = hd / 2;
-    const float2* tab = rope + (size_t)pos * half;
-    const int total = (n_heads + n_kv) * half + n_kv * hd;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-        const int64_t base = (int64_t)b * cache_seq_stride + cache_layer_off + (int64_t)pos * n_kv * hd;
-        // pair p: elements (2p, 2p + 1), or (p, p + half) for split-half RoPE
-        // (ApplyRoPENeox); the table is the same, since 2p * (1/hd) and
-        // p * (2/hd) are the same fp32 value
-        if (i < n_heads * half) {
-            int h = i / half, p = i % half;
-            const int ia = neox ? p : 2 * p, ib = neox ? p + half : 2 * p + 1;
-            float* vec = q + (size_t)b * q_stride + h * hd;
-            float2 cs = tab[p];
-            float x0 = vec[ia], x1 = vec[ib];
-            vec[ia] = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
-            vec[ib] = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
-        } else if (i < (n_heads + n_kv) * half) {
-            int j = i - n_heads * half;
-            int h = j / half, p = j % half;
-            const int ia = neox ? p : 2 * p, ib = neox ? p + half : 2 * p + 1;
-            const float* vec = k + (size_t)b * kv_stride + h * hd;
-            float2 cs = tab[p];
-            float x0 = vec[ia], x1 = vec[ib];
-            float r0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
-            float r1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
-            int64_t off = base + h * hd;
-            if (kv_f16) {
-                reinterpret_cast<__half*>(kcache)[off + ia] = __float2half_rn(r0);
-                reinterpret_cast<__half*>(kcache)[off + ib] = __float2half_rn(r1);
-            } else {
-                reinterpret_cast<float*>(kcache)[off + ia] = r0;
-                reinterpret_cast<float*>(kcache)[off + ib] = r1;
-            }
-        } else {
-            int d = i - (n_heads + n_kv) * half;
-            float val = v[(size_t)b * kv_stride + d];
-            if (kv_f16) reinterpret_cast<__half*>(vcache)[base + d] = __float2half_rn(val);
-            else reinterpret_cast<float*>(vcache)[base + d] = val;
-        }
-    }
-}
-
 // ---- attention: split-K over positions, then combine ----------------------------
 //
 // CTA (split s, kv head kh, sequence b) handles positions [p0, p1) of
@@ -148,6 +93,13 @@ __global__ void rope_kv_kernel(float* __restrict__ q, const float* __restrict__ 
 // This equals Softmax followed by the weighted V sum up to fp32 rounding.
 
 constexpr int kAttnThreads = 256;
+
+// 16 bytes global -> shared; src_bytes 0 writes zeros
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+
 constexpr int kMaxKvMul = 16;
 constexpr int kMaxHd = 256;
 
@@ -157,6 +109,7 @@ struct KvVec;
 template <>
 struct KvVec<float> {
     static constexpr int kPer16 = 4;
+    __device__ static float from_float(float v) { return v; }
     __device__ static void to_float(const uint4& v, float* out) {
         out[0] = __uint_as_float(v.x);
         out[1] = __uint_as_float(v.y);
@@ -167,6 +120,7 @@ struct KvVec<float> {
 template <>
 struct KvVec<__half> {
     static constexpr int kPer16 = 8;
+    __device__ static __half from_float(float v) { return __float2half_rn(v); }
     __device__ static void to_float(const uint4& v, float* out) {
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -303,9 +257,12 @@ __global__ void __launch_bounds__(kAttnThreads)
                       int n_heads, int n_kv, int hd, int q_stride, int64_t cache_seq_stride,
                       int64_t cache_layer_off, int ctx_len, int splits, int chunk, float scale,
                       float* __restrict__ part /* [b][head][split][hd + 4] */, int* __restrict__ counters,
-                      float* __restrict__ out, int out_stride, PrepTarget pt) {
+                      float* __restrict__ out, int out_stride, PrepTarget pt, RopeIn ri) {
     pdl_trigger();
-    pdl_wait();
+    // Cache rows below the current position were written by earlier steps:
+    // their copies start before the wait for the q/k/v kernel; the row at the
+    // current position (this step's k/v, rotated and stored here when ri.on)
+    // and q come after it.
     extern __shared__ __align__(16) float sm[];
     __shared__ int s_last;
     const int s = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
@@ -328,24 +285,76 @@ __global__ void __launch_bounds__(kAttnThreads)
     float* pr_base = part + ((size_t)b * n_heads + kh * kv_mul) * splits * prow;
 
     if (L == 0) {  // nothing of this split is inside 0..pos: an empty partial
+        pdl_wait();
         for (int e = tid; e < kv_mul * prow; e += blockDim.x) {
             const int g = e / prow, d = e % prow;
             pr_base[((size_t)g * splits + s) * prow + d] = d == hd ? -FLT_MAX : 0.f;
         }
     } else {
-        // stage q (fp32) and the K / V rows of the chunk (16-byte loads)
-        for (int i = tid; i < kv_mul * hd; i += blockDim.x)
-            qs[(i / hd) * qrow + i % hd] = q[(size_t)b * q_stride + (kh * kv_mul) * hd + i];
+        // the K / V rows of the chunk (16-byte copies); the current row last
         constexpr int P16 = KvVec<KV>::kPer16;
         const int vec_per_row = hd / P16;
-        const KV* kbase = kcache + (int64_t)b * cache_seq_stride + cache_layer_off + kh * hd;
-        const KV* vbase = vcache + (int64_t)b * cache_seq_stride + cache_layer_off + kh * hd;
+        KV* kbase = const_cast<KV*>(kcache) + (int64_t)b * cache_seq_stride + cache_layer_off + kh * hd;
+        KV* vbase = const_cast<KV*>(vcache) + (int64_t)b * cache_seq_stride + cache_layer_off + kh * hd;
+        const int r_new = pos - p0;
         for (int i = tid; i < L * vec_per_row; i += blockDim.x) {
             const int r = i / vec_per_row, c = i % vec_per_row;
+            if (r == r_new) continue;
             const int64_t g = (int64_t)(p0 + r) * kvdim + c * P16;
-            *reinterpret_cast<uint4*>(ks + r * krow + c * P16) = __ldg(reinterpret_cast<const uint4*>(kbase + g));
-            *reinterpret_cast<uint4*>(vs + r * hd + c * P16) = __ldg(reinterpret_cast<const uint4*>(vbase + g));
+            cp_async16(smem_u32(ks + r * krow + c * P16), kbase + g, 16);
+            cp_async16(smem_u32(vs + r * hd + c * P16), vbase + g, 16);
         }
+        pdl_wait();
+        if (!ri.on && r_new >= 0 && r_new < L) {
+            for (int c = tid; c < vec_per_row; c += blockDim.x) {
+                const int64_t g = (int64_t)pos * kvdim + c * P16;
+                cp_async16(smem_u32(ks + r_new * krow + c * P16), kbase + g, 16);
+                cp_async16(smem_u32(vs + r_new * hd + c * P16), vbase + g, 16);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        const float2* tab = ri.on ? ri.rope + (size_t)pos * (hd / 2) : nullptr;
+        if (ri.on && r_new >= 0 && r_new < L) {
+            // TensorMath.ApplyRoPE on the new k row, then k and v into the
+            // cache (rotation with explicit _rn products, pairs per ri.neox)
+            const float* kr = ri.k + (size_t)b * ri.kv_stride + kh * hd;
+            const float* vr = ri.v + (size_t)b * ri.kv_stride + kh * hd;
+            KV* kw = kbase + (int64_t)pos * kvdim;
+            KV* vw = vbase + (int64_t)pos * kvdim;
+            for (int p = tid; p < hd / 2; p += blockDim.x) {
+                const float2 cs = tab[p];
+                const int ia = ri.neox ? p : 2 * p, ib = ri.neox ? p + hd / 2 : 2 * p + 1;
+                const float x0 = kr[ia], x1 = kr[ib];
+                const KV k0 = KvVec<KV>::from_float(__fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y)));
+                const KV k1 = KvVec<KV>::from_float(__fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x)));
+                ks[r_new * krow + ia] = k0;
+                ks[r_new * krow + ib] = k1;
+                kw[ia] = k0;
+                kw[ib] = k1;
+                const KV v0 = KvVec<KV>::from_float(vr[2 * p]), v1 = KvVec<KV>::from_float(vr[2 * p + 1]);
+                vs[r_new * hd + 2 * p] = v0;
+                vs[r_new * hd + 2 * p + 1] = v1;
+                vw[2 * p] = v0;
+                vw[2 * p + 1] = v1;
+            }
+        }
+        // q of the group's heads (fp32), rotated here when ri.on
+        for (int i = tid; i < kv_mul * (hd / 2); i += blockDim.x) {
+            const int gi = i / (hd / 2), p = i % (hd / 2);
+            const int ia = ri.on && ri.neox ? p : 2 * p, ib = ri.on && ri.neox ? p + hd / 2 : 2 * p + 1;
+            const float* qr = q + (size_t)b * q_stride + (kh * kv_mul + gi) * hd;
+            float v0 = qr[ia], v1 = qr[ib];
+            if (ri.on) {
+                const float2 cs = tab[p];
+                const float r0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
+                const float r1 = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
+                v0 = r0;
+                v1 = r1;
+            }
+            qs[gi * qrow + ia] = v0;
+            qs[gi * qrow + ib] = v1;
+        }
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
         __syncthreads();
         // scores: one (position, head) dot product per thread-iteration
         for (int e = tid; e < L * kv_mul; e += blockDim.x) {
@@ -439,11 +448,6 @@ __device__ __forceinline__ void ldsm4_trans(uint32_t addr, uint32_t (&r)[4]) {
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                  : "r"(addr));
 }
-// 16 bytes global -> shared; src_bytes 0 writes zeros
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
-                 : "memory");
-}
 __device__ __forceinline__ uint32_t half2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
 template <int HD, int CHUNK>
@@ -511,7 +515,7 @@ __global__ void __launch_bounds__(2 * CHUNK)
         asm volatile("cp.async.commit_group;" ::: "memory");
         if (ri.on && r_new >= 0 && r_new < L) {
             // TensorMath.ApplyRoPE on the new k row, then k and v into the cache
-            // (the rope_kv_kernel arithmetic, bit for bit)
+            // (the same arithmetic as attn_split_kernel's)
             const float2* tab = ri.rope + (size_t)pos * (HD / 2);
             const float* kr = ri.k + (size_t)b * ri.kv_stride + kh * HD;
             const float* vr = ri.v + (size_t)b * ri.kv_stride + kh * HD;
@@ -535,7 +539,7 @@ __global__ void __launch_bounds__(2 * CHUNK)
             }
         }
         // query heads: fp16 hi in rows 0-7, the fp16 remainder in rows 8-15
-        // (rotated here when ri.on, as rope_kv_kernel would have)
+        // (rotated here when ri.on)
         for (int i = tid; i < 8 * HD / 2; i += NT) {
             const int gi = i / (HD / 2), p = i % (HD / 2);
             // the pair's elements: (2p, 2p + 1), or (p, p + HD/2) for split-half RoPE
@@ -825,16 +829,6 @@ int launch_rmsnorm(const float* x, const float* w, float* y, int n, int rows, fl
     return CN_OK;
 }
 
-int launch_rope_kv(const RopeKvArgs& a, cudaStream_t s) {
-    const int total = (a.n_heads + a.n_kv) * (a.hd / 2) + a.n_kv * a.hd;
-    dim3 grid(grid_1d(total, 256, 64), a.batch);
-    CN_CUDA(launch_k(true, rope_kv_kernel, grid, dim3(256), 0, s, a.q, a.k, a.v, a.rope, a.pos_dev, a.pos_host,
-                     a.n_heads, a.n_kv, a.hd, a.q_stride, a.kv_stride, a.kcache, a.vcache, a.cache_seq_stride,
-                     a.cache_layer_off, a.kv_f16, a.ctx_len, a.err, a.neox));
-    CN_CUDA(cudaGetLastError());
-    return CN_OK;
-}
-
 static bool attn_use_mma(int n_heads, int n_kv, int hd, bool kv_f16) {
     return kv_f16 && n_heads / n_kv <= 8 && (hd == 64 || hd == 128);
 }
@@ -912,8 +906,8 @@ int attention_prepare(const AttnPlan& p) {
 
 int launch_attention(const AttnArgs& a, const AttnPlan& p, cudaStream_t s) {
     dim3 grid(p.splits, a.n_kv, a.batch);
-    CN_CHECK(!a.rope.on || (p.mma && a.rope.k && a.rope.v && a.rope.rope), CN_ERR_INVALID_ARG,
-             "attention: RoPE fusion needs the tensor-core kernel");
+    CN_CHECK(!a.rope.on || (a.rope.k && a.rope.v && a.rope.rope), CN_ERR_INVALID_ARG,
+             "attention: RoPE fusion needs the new k/v rows and the table");
     const float scale = 1.0f / sqrtf((float)a.hd);
     CN_CHECK(a.out_stride % 4 == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 &&
                  (reinterpret_cast<uintptr_t>(a.part) & 15) == 0,
@@ -931,12 +925,12 @@ int launch_attention(const AttnArgs& a, const AttnPlan& p, cudaStream_t s) {
         CN_CUDA(launch_k(true, attn_split_kernel<__half>, grid, dim3(kAttnThreads), p.smem, s,
             a.q, (const __half*)a.kcache, (const __half*)a.vcache, a.pos_dev, a.pos_host, a.n_heads,
             a.n_kv, a.hd, a.q_stride, a.cache_seq_stride, a.cache_layer_off, a.ctx_len, p.splits,
-            p.chunk, scale, a.part, a.counters, a.out, a.out_stride, pt));
+            p.chunk, scale, a.part, a.counters, a.out, a.out_stride, pt, a.rope));
     } else {
         CN_CUDA(launch_k(true, attn_split_kernel<float>, grid, dim3(kAttnThreads), p.smem, s,
             a.q, (const float*)a.kcache, (const float*)a.vcache, a.pos_dev, a.pos_host, a.n_heads,
             a.n_kv, a.hd, a.q_stride, a.cache_seq_stride, a.cache_layer_off, a.ctx_len, p.splits,
-            p.chunk, scale, a.part, a.counters, a.out, a.out_stride, pt));
+            p.chunk, scale, a.part, a.counters, a.out, a.out_stride, pt, a.rope));
     }
     CN_CUDA(cudaGetLastError());
     return CN_OK;

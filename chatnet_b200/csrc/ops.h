@@ -8,23 +8,6 @@
 
 namespace cn {
 
-struct RopeKvArgs {
-    float* q;             // [batch][q_stride], rotated in place
-    const float* k;       // [batch][kv_stride]
-    const float* v;       // [batch][kv_stride]
-    const float2* rope;   // [ctx][hd/2] (cos, sin)
-    const int* pos_dev;   // [batch] positions on the device, or null
-    int pos_host;         // used when pos_dev is null
-    int batch, n_heads, n_kv, hd, q_stride, kv_stride;
-    void* kcache;         // [batch][layers][ctx][n_kv*hd], fp32 or fp16
-    void* vcache;
-    int64_t cache_seq_stride;  // elements between sequences
-    int64_t cache_layer_off;   // elements to this layer
-    int kv_f16, ctx_len;
-    uint32_t* err;
-    int neox = 0;         // split-half pairs (ApplyRoPENeox) instead of interleaved ones
-};
-
 struct AttnPlan {
     int splits = 0, chunk = 0;
     bool mma = false;  // tensor-core kernel (fp16 cache, kv_mul <= 8, head_dim 64 or 128)
@@ -62,7 +45,6 @@ struct AttnArgs {
 
 int launch_rmsnorm(const float* x, const float* w, float* y, int n, int rows, float eps,
                    cudaStream_t s);
-int launch_rope_kv(const RopeKvArgs& a, cudaStream_t s);
 int attention_plan(int n_heads, int n_kv, int hd, int max_seq, int batch, int sms, bool kv_f16, AttnPlan* p);
 // Sets the kernels' shared-memory limit for plan p (call before any capture).
 int attention_prepare(const AttnPlan& p);

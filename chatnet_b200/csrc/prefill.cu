@@ -156,7 +156,7 @@ __global__ void half_rows_kernel(const float* __restrict__ x, __half* __restrict
 
 // TensorMath.ApplyRoPE (interleaved pairs) on the q and k rows of the n prompt
 // tokens (token t at position pos0 + t), then k and v into the cache, with
-// rope_kv_kernel's arithmetic.  Also leaves fp16 copies of the new k and v
+// the decode attention kernels' arithmetic.  Also leaves fp16 copies of the new k and v
 // rows in kh/vh [n][kvdim] for the attention kernel.  One CTA per token, four
 // values per thread.
 __global__ void rope_prefill_kernel(float* __restrict__ q, const float* __restrict__ k,
