@@ -252,6 +252,52 @@ def test_config4_full_depth_b16_and_b1(ctx, oracle):
     assert int(am1[0]) == int(np.argmax(ref[0]))
 
 
+@pytest.mark.parametrize("kinds", [
+    # every projection Q8_0: the tiled fp16 GEMV, q/k/v and gate/up as one launch each
+    {"attn_q": "q8_0", "attn_k": "q8_0", "attn_v": "q8_0", "attn_output": "q8_0", "ffn_gate": "q8_0",
+     "ffn_up": "q8_0", "ffn_down": "q8_0", "token_embd": "q8_0", "output": "q8_0"},
+    # the reference's simplified importance-quant decodes, one per tensor kind
+    {"attn_q": "iq3_s", "attn_k": "iq3_xxs", "attn_v": "iq2_xs", "attn_output": "iq2_xxs", "ffn_gate": "iq2_s",
+     "ffn_up": "iq1_s", "ffn_down": "iq1_m", "token_embd": "iq3_s", "output": "iq2_s"},
+], ids=["q8_0", "iq"])
+@pytest.mark.parametrize("batch", [1, 3])
+def test_codec_family_models(ctx, oracle, kinds, batch):
+    """Whole decoders on Q8_0 (tiled GEMV, grouped launches) and on the IQ
+    codecs (generic kernel) match the oracle's Forward at batch 1 and 3."""
+    from tests.test_gpu_quant import _rand_b32, _rand_sb
+    dc = cf.replace(small_dc(max_batch=3), kv_filled=0, decode_pos=0)
+    m = dc.model
+    host = cf.host_tensors(dc)
+    names = tensor_names(m.n_layers)
+    types = []
+    for i, n in enumerate(names):
+        rows, cols = tensor_shape(m, n)
+        kind = n.split(".")[2] if n.startswith("blk.") else n.split(".")[0]
+        codec = kinds.get(kind)
+        if codec is None:  # norms stay fp32
+            types.append(cf.tensor_type(dc, n))
+            continue
+        t, blocks = (_rand_b32 if codec == "q8_0" else _rand_sb)(codec, rows, cols, 300 + i)
+        host[n] = blocks
+        types.append(t)
+    tensors = [ctx.upload(host[n], t, *tensor_shape(m, n)) for n, t in zip(names, types)]
+    g = CudaLlamaModel(ctx, m, tensors)
+    orcs = []
+    for _ in range(batch):
+        k = np.zeros((m.n_layers * m.ctx_len, m.kv_dim), np.float32)
+        orcs.append(_oracle.OracleLlama(oracle, m, host, types, names, k, k.copy()))
+    for step in range(2):
+        toks = [cf.token(dc, b, step) for b in range(batch)]
+        lg, am = g.decode(toks, [step] * batch)
+        for b in range(batch):
+            ref = orcs[b].forward([toks[b]], step)
+            assert rel_err(lg[b], ref) <= REL_TOL, (step, b)
+            assert am[b] == int(np.argmax(lg[b]))
+    g.close()
+    for t in tensors:
+        t.free()
+
+
 def test_mixed_codec_model(ctx, oracle):
     """A decoder whose projections, embedding and lm_head use the generic
     codecs (every K-quant and IQ4 type the reference decodes besides Q4_K /
