@@ -436,12 +436,16 @@ def gemv_mode(a) -> int:
     name, shape, batch = a.gemv.split(":")
     rows, cols = (int(v) for v in shape.split("x"))
     batch = int(batch)
-    t = {"q4_0": cn.TYPE_Q4_0, "q4_k": cn.TYPE_Q4_K, "q6_k": cn.TYPE_Q6_K, "q8_0": cn.TYPE_Q8_0}[name]
+    t = {"q4_0": cn.TYPE_Q4_0, "q4_k": cn.TYPE_Q4_K, "q6_k": cn.TYPE_Q6_K, "q8_0": cn.TYPE_Q8_0,
+         "q5_k": cn.TYPE_Q5_K}[name]
     ctx = cn.Context(0)
-    if t == cn.TYPE_Q8_0:  # no seeded generator: seeded random blocks, fp16 scale 0.01
+    if t in (cn.TYPE_Q8_0, cn.TYPE_Q5_K):  # no seeded generator: seeded random blocks, fp16 scales 0.01
+        blk, bpb = (32, 34) if t == cn.TYPE_Q8_0 else (256, 176)
         raw = np.random.default_rng(cn.synth_seed(2, f"gemv.{name}.{rows}x{cols}")).integers(
-            0, 256, size=(rows * cols // 32, 34), dtype=np.uint8)
+            0, 256, size=(rows * cols // blk, bpb), dtype=np.uint8)
         raw[:, 0:2] = np.frombuffer(np.float16(0.01).tobytes(), np.uint8)
+        if t == cn.TYPE_Q5_K:
+            raw[:, 2:4] = np.frombuffer(np.float16(0.01).tobytes(), np.uint8)
         W = ctx.upload(raw.ravel(), t, rows, cols)
     else:
         W = ctx.synth(t, rows, cols, cn.synth_seed(2, f"gemv.{name}.{rows}x{cols}"))

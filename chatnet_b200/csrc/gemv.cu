@@ -59,6 +59,12 @@ struct Fmt<CN_TYPE_Q8_0> {
     __device__ static int offset(int) { return 0; }
 };
 template <>
+struct Fmt<CN_TYPE_Q5_K> {
+    static constexpr int kBox = 176;  // one 176-byte super-block (qh@16, qs@48)
+    __device__ static int box_x(int u) { return 22 * u; }
+    __device__ static int offset(int) { return 0; }
+};
+template <>
 struct Fmt<CN_TYPE_Q4_K> {
     static constexpr int kBox = 144;  // one 144-byte super-block
     __device__ static int box_x(int u) { return 18 * u; }
@@ -78,12 +84,13 @@ template <int TYPE, int NT>
 struct Geo {
     static constexpr int kW = Fmt<TYPE>::kBox * kTileRows;             // raw blocks
     static constexpr int kXF = 8 * NT * 32 * 16;                        // B fragments
-    static constexpr int kXS = TYPE == CN_TYPE_Q4_K ? 8 * NT * 4 * 4 : 0;  // chunk sums
+    static constexpr bool kKQ = TYPE == CN_TYPE_Q4_K || TYPE == CN_TYPE_Q5_K;  // scales and mins
+    static constexpr int kXS = kKQ ? 8 * NT * 4 * 4 : 0;  // chunk sums
     static constexpr int kXI = NT * 4 * 4;                              // unit 2^-e per column
     static constexpr int kXIpad = (kXI + 127) / 128 * 128;
     static constexpr int kBytes = kW + kXF + kXS + kXI;                 // bytes landing per stage
     static constexpr int kStage = kW + kXF + kXS + kXIpad;              // multiple of 128
-    static constexpr int kTable = TYPE == CN_TYPE_Q4_K ? kCons * 16 * 8 * 8 : 0;
+    static constexpr int kTable = kKQ ? kCons * 16 * 8 * 8 : 0;
     static constexpr int kFixed = kTable + 64 * 16;                     // table + barriers
     // Two CTAs per SM when three or more stages fit in half the SM's shared
     // memory; otherwise one CTA with up to six stages.
@@ -271,15 +278,22 @@ __device__ __forceinline__ void unit_q8_0(const uint8_t* stw, const uint4* xf, i
 // value q * 2^-24, exact), so decode is a mask per half2; 2^24 is folded
 // into d*sc.  The per-(row, sub-block) scales d*sc*2^24 and dmin*m are
 // decoded once per unit by the whole warp into a shared table.
-template <int NT>
+// Q5_K (Q5 = true; DequantQ5K.cs:36-90): the same scales and mins at bytes
+// 4..15, the 32 high bits of a sub-block at qh bytes 4j..4j+3 (bit e % 8 of
+// byte e / 8 for element e) and its nibbles at 48 + 16j; each high bit goes
+// into the fp16 subnormal at bit 4 (low k-step, value (q + 16 h) 2^-24) or
+// bit 8 (high k-step, 16 (q + 16 h) 2^-24, the x fragments pre-scaled by 1/16).
+template <int NT, bool Q5 = false>
 __device__ __forceinline__ void unit_q4_k(const uint8_t* stw, const uint4* xf, const float* xs,
                                           float2* table, int row0, int g, int t, int lane,
                                           const bool* live, float (&acc)[NT][4]) {
+    constexpr int RB = Q5 ? 176 : 144;  // bytes per row of a unit
+    constexpr int QW = Q5 ? 12 : 4;     // first quant word of a row
     {
         // DecodeScales (DequantQ4K.cs:218-241) for row lane/2, sub-blocks
         // 4*(lane&1) .. +3, four 6-bit fields at a time
         const int r = lane >> 1, jh = lane & 1;
-        const uint8_t* rp = stw + (row0 + r) * 144;
+        const uint8_t* rp = stw + (row0 + r) * RB;
         const uint32_t* W = reinterpret_cast<const uint32_t*>(rp);
         float d = half_bits_to_float(lds_u16(rp)) * 16777216.0f;
         float dmin = half_bits_to_float(lds_u16(rp + 2));
@@ -293,14 +307,14 @@ __device__ __forceinline__ void unit_q4_k(const uint8_t* stw, const uint4* xf, c
             table[r * 8 + 4 * jh + k] = make_float2(d * ubyte_f(sc, k), dmin * ubyte_f(m, k));
     }
     __syncwarp();
-    const uint8_t* rg = stw + (row0 + g) * 144;
-    const uint8_t* rh = rg + 8 * 144;
+    const uint8_t* rg = stw + (row0 + g) * RB;
+    const uint8_t* rh = rg + 8 * RB;
     const uint32_t* Wg = reinterpret_cast<const uint32_t*>(rg);
     const uint32_t* Wh = reinterpret_cast<const uint32_t*>(rh);
     const uint32_t M = 0x000F000Fu, MH = 0x00F000F0u;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-        uint32_t wg = Wg[4 + 4 * j + t], wh = Wh[4 + 4 * j + t];
+        uint32_t wg = Wg[QW + 4 * j + t], wh = Wh[QW + 4 * j + t];
         // low nibbles at bits 0-3 (value q * 2^-24), high nibbles left at
         // bits 4-7 (value 16 q * 2^-24); the high k-step's x fragments are
         // pre-scaled by 1/16, so both k-steps accumulate q * x * 2^-24.
@@ -314,6 +328,20 @@ __device__ __forceinline__ void unit_q4_k(const uint8_t* stw, const uint4* xf, c
         a1[1] = wh & MH;
         a1[2] = wg8 & MH;
         a1[3] = wh8 & MH;
+        if constexpr (Q5) {
+            // high bits of positions 4t..4t+3 (low k-step) and 16+4t..16+4t+3
+            const int sh4 = 4 * (t & 1);
+            const uint32_t hg0 = (rg[16 + 4 * j + (t >> 1)] >> sh4) & 15u, hh0 = (rh[16 + 4 * j + (t >> 1)] >> sh4) & 15u;
+            const uint32_t hg1 = (rg[18 + 4 * j + (t >> 1)] >> sh4) & 15u, hh1 = (rh[18 + 4 * j + (t >> 1)] >> sh4) & 15u;
+            a0[0] |= ((hg0 & 1u) << 4) | ((hg0 & 4u) << 18);
+            a0[1] |= ((hh0 & 1u) << 4) | ((hh0 & 4u) << 18);
+            a0[2] |= ((hg0 & 2u) << 3) | ((hg0 & 8u) << 17);
+            a0[3] |= ((hh0 & 2u) << 3) | ((hh0 & 8u) << 17);
+            a1[0] |= ((hg1 & 1u) << 8) | ((hg1 & 4u) << 22);
+            a1[1] |= ((hh1 & 1u) << 8) | ((hh1 & 4u) << 22);
+            a1[2] |= ((hg1 & 2u) << 7) | ((hg1 & 8u) << 21);
+            a1[3] |= ((hh1 & 2u) << 7) | ((hh1 & 8u) << 21);
+        }
         const float2 sg = table[g * 8 + j], sh = table[(g + 8) * 8 + j];
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
@@ -627,9 +655,9 @@ __global__ void __launch_bounds__(kThreads, Geo<TYPE, NT>::kMinCtas)
             unit_q4_0<NT>(st, xf, warp * 16, g, t, lane, live, au);
         } else if constexpr (TYPE == CN_TYPE_Q8_0) {
             unit_q8_0<NT>(st, xf, warp * 16, g, t, lane, live, au);
-        } else if constexpr (TYPE == CN_TYPE_Q4_K) {
+        } else if constexpr (TYPE == CN_TYPE_Q4_K || TYPE == CN_TYPE_Q5_K) {
             const float* xs = reinterpret_cast<const float*>(st + G::kW + G::kXF);
-            unit_q4_k<NT>(st, xf, xs, table + warp * 128, warp * 16, g, t, lane, live, au);
+            unit_q4_k<NT, TYPE == CN_TYPE_Q5_K>(st, xf, xs, table + warp * 128, warp * 16, g, t, lane, live, au);
         } else {
             if (u & 1) unit_q6_k<NT, 2>(st, xf, u, warp * 16, g, t, lane, live, au);
             else unit_q6_k<NT, 0>(st, xf, u, warp * 16, g, t, lane, live, au);
@@ -1167,6 +1195,7 @@ static int box_bytes(int type) {
         case CN_TYPE_Q4_0: return Fmt<CN_TYPE_Q4_0>::kBox;
         case CN_TYPE_Q8_0: return Fmt<CN_TYPE_Q8_0>::kBox;
         case CN_TYPE_Q4_K: return Fmt<CN_TYPE_Q4_K>::kBox;
+        case CN_TYPE_Q5_K: return Fmt<CN_TYPE_Q5_K>::kBox;
         case CN_TYPE_Q6_K: return Fmt<CN_TYPE_Q6_K>::kBox;
         default: return 0;
     }
@@ -1270,6 +1299,7 @@ int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool
     if (type == CN_TYPE_Q4_0) { CN_OCC(CN_TYPE_Q4_0) }
     else if (type == CN_TYPE_Q8_0) { CN_OCC(CN_TYPE_Q8_0) }
     else if (type == CN_TYPE_Q4_K) { CN_OCC(CN_TYPE_Q4_K) }
+    else if (type == CN_TYPE_Q5_K) { CN_OCC(CN_TYPE_Q5_K) }
     else { CN_OCC(CN_TYPE_Q6_K) }
 #undef CN_OCC
     if (occ < 0) return occ;  // error code from the occupancy query
@@ -1303,7 +1333,7 @@ int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool
     p->ctas = ctas;
     const int chunks = p->units * 8;
     p->xfrag_bytes = (size_t)chunks * p->nt * 32 * sizeof(uint4);
-    p->xsum_bytes = type == CN_TYPE_Q4_K ? (size_t)chunks * p->nt * 4 * sizeof(float) : 0;
+    p->xsum_bytes = (type == CN_TYPE_Q4_K || type == CN_TYPE_Q5_K) ? (size_t)chunks * p->nt * 4 * sizeof(float) : 0;
     p->xinv_bytes = (size_t)p->units * p->nt * 4 * sizeof(float);
     p->partial_bytes = (size_t)2 * ctas * kTileRows * p->nt * 4 * sizeof(float);
     p->counters = (size_t)p->tiles * kCons;
@@ -1349,12 +1379,12 @@ int gemv_make(cn_ctx* ctx, int type, const void* d_w, int64_t rows, int64_t cols
     return gemv_plan(ctx, type, rows, cols, batch, op->tma, &op->plan);
 }
 
-float gemv_step1_scale(int type) { return type == CN_TYPE_Q4_K ? 0.0625f : 1.0f; }
+float gemv_step1_scale(int type) { return type == CN_TYPE_Q4_K || type == CN_TYPE_Q5_K ? 0.0625f : 1.0f; }
 
 int gemv_prep_kind(const GemvOp& op) {
     if (op.plan.path == kPathI8) return 3;
     if (op.plan.path == kPathTc) return 2;
-    return op.type == CN_TYPE_Q4_K ? 1 : 0;
+    return op.type == CN_TYPE_Q4_K || op.type == CN_TYPE_Q5_K ? 1 : 0;
 }
 
 bool pdl_enabled() {
@@ -1384,7 +1414,7 @@ PrepTarget prep_target(const GemvOp* op, const GemvBufs& b) {
     pt.nt_count = op->plan.nt;
     pt.step1 = gemv_step1_scale(op->type);
     pt.xfrag = b.xfrag;
-    pt.xsum = op->type == CN_TYPE_Q4_K ? b.xsum : nullptr;
+    pt.xsum = op->type == CN_TYPE_Q4_K || op->type == CN_TYPE_Q5_K ? b.xsum : nullptr;
     pt.xinv = b.xinv;
     return pt;
 }
@@ -1520,6 +1550,7 @@ static int gemv_mma_launch(cn_ctx* ctx, cudaStream_t st, const GemvOp* ops, int 
     if (type == CN_TYPE_Q4_0) { CN_DISPATCH(CN_TYPE_Q4_0) }
     if (type == CN_TYPE_Q8_0) { CN_DISPATCH(CN_TYPE_Q8_0) }
     if (type == CN_TYPE_Q4_K) { CN_DISPATCH(CN_TYPE_Q4_K) }
+    if (type == CN_TYPE_Q5_K) { CN_DISPATCH(CN_TYPE_Q5_K) }
     CN_DISPATCH(CN_TYPE_Q6_K)
 #undef CN_DISPATCH
 }

@@ -255,6 +255,16 @@ def _rand_sb(name, rows, cols, seed):
     return t, blocks.ravel()
 
 
+@pytest.mark.parametrize("rows,cols,batch", [(4096, 4096, 1), (300, 2048, 5), (1000, 4096, 16), (129, 768, 32)])
+def test_q5_k_matvec_parity(ctx, oracle, rows, cols, batch):
+    """Q5_K on the tiled fp16 GEMV (high bits into the fp16 subnormals):
+    every n-tile count and a partial row tile."""
+    t, blocks = _rand_sb("q5_k", rows, cols, 41 + batch)
+    W = ctx.upload(blocks, t, rows, cols)
+    x = _x(batch, cols, f"q5k.x.{rows}.{cols}.{batch}")
+    assert rel_err(ctx.matvec(W, x), oracle.matvec(t, blocks, x, rows)) <= REL_TOL
+
+
 @pytest.mark.parametrize("name", list(SB))
 def test_superblock_dequantize_bit_exact(ctx, oracle, name):
     t, blocks = _rand_sb(name, 37, 768, 21)

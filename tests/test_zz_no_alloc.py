@@ -41,9 +41,9 @@ def _noalloc(t, W, rows, cols, x, batch):
     return y.cpu().numpy()
 
 
-# Q4_0 300x2080, Q8_0 130x1056 and Q5_K take the untiled (warp-per-row) path:
-# an inner dimension that is not a multiple of 256, or a codec without a
-# tiled kernel; Q8_0 257x1024 the tiled fp16 GEMV
+# Q4_0 300x2080 and Q8_0 130x1056 take the untiled (warp-per-row) path (an
+# inner dimension that is not a multiple of 256); Q8_0 257x1024 and Q5_K
+# 129x768 the tiled fp16 GEMV
 CASES = [(cn.TYPE_Q4_K, 11008, 4096, 1), (cn.TYPE_Q4_0, 5632, 2048, 3),
          (cn.TYPE_Q6_K, 4096, 4096, 4), (cn.TYPE_Q4_K, 37, 512, 2),
          (cn.TYPE_Q4_0, 300, 2080, 2), (cn.TYPE_Q8_0, 257, 1024, 1), (cn.TYPE_Q8_0, 130, 1056, 2),
