@@ -89,13 +89,6 @@ struct Cursor {
         pos += n;
         return s;
     }
-    void skip(uint64_t n) {
-        if (bad || n > size - pos) {
-            bad = true;
-            return;
-        }
-        pos += n;
-    }
 };
 
 bool read_scalar(Cursor& c, uint32_t type, Value& v) {
