@@ -535,12 +535,34 @@ __device__ void finish_shared(const GemvArgs& a, int tile, int warp, int cta, in
     int64_t rows;
     float* y;
     tile_mat(a, tile, local, rows, y);
-    for (int e = lane; e < 16 * BW; e += 32) {
-        float s = 0.f;
-        for (int k = 0; k < ns; k++) s += __ldcg(src[k] + e);
+    // each lane sums kE elements of the sub-tile; the loads of kBatchC
+    // contributors are issued together (about 32 in flight per lane) rather
+    // than one L2 round trip after another, and the sums run in CTA order
+    constexpr int kE = 16 * BW / 32;
+    constexpr int kBatchC = 32 / kE < 1 ? 1 : (32 / kE > 8 ? 8 : 32 / kE);
+    float s[kE];
+#pragma unroll
+    for (int i = 0; i < kE; i++) s[i] = 0.f;
+#pragma unroll
+    for (int k0 = 0; k0 < 8; k0 += kBatchC) {
+        if (k0 >= ns) break;
+        float v[kBatchC][kE];
+#pragma unroll
+        for (int k = 0; k < kBatchC; k++)
+#pragma unroll
+            for (int i = 0; i < kE; i++) v[k][i] = k0 + k < ns ? __ldcg(src[k0 + k] + lane + 32 * i) : 0.f;
+#pragma unroll
+        for (int k = 0; k < kBatchC; k++)
+#pragma unroll
+            for (int i = 0; i < kE; i++)
+                if (k0 + k < ns) s[i] += v[k][i];
+    }
+#pragma unroll
+    for (int i = 0; i < kE; i++) {
+        const int e = lane + 32 * i;
         const int row = e / BW, b = e % BW;
         const int64_t r = (int64_t)local * kTileRows + warp * 16 + row;
-        if (b < a.batch && r < rows) y[(size_t)b * rows + r] = s;
+        if (b < a.batch && r < rows) y[(size_t)b * rows + r] = s[i];
     }
     if (lane == 0) atomicExch(ctr, 0);
 }

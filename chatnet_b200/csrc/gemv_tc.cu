@@ -203,12 +203,24 @@ __device__ void finish_tile(const Args& a, int r, int tile, int cta, int C, int6
     float s[NB];
 #pragma unroll
     for (int b = 0; b < NB; b++) s[b] = 0.f;
-    for (int c = c_first; c <= c_last; c++) {
-        const int first_tile = (int)(range_start(total, c, C) / a.units);
-        const int slot = 2 * c + (tile == first_tile ? 0 : 1);
-        const float* q = a.partials + ((size_t)slot * kRows + r) * 8;
+    // contributor c's partial sits in slot 2c, c_first's in 2c + 1 when its
+    // range began in an earlier tile; four contributors' loads go out
+    // together, the sums run in CTA order
+    const int first_slot = 2 * c_first + (range_start(total, c_first, C) < (int64_t)tile * a.units ? 1 : 0);
+    for (int c0 = c_first; c0 <= c_last; c0 += 4) {
+        float v[4][NB];
 #pragma unroll
-        for (int b = 0; b < NB; b++) s[b] += __ldcg(q + b);
+        for (int k = 0; k < 4; k++) {
+            const int slot = c0 + k == c_first ? first_slot : 2 * (c0 + k);
+            const float* q = a.partials + ((size_t)slot * kRows + r) * 8;
+#pragma unroll
+            for (int b = 0; b < NB; b++) v[k][b] = c0 + k <= c_last ? __ldcg(q + b) : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+#pragma unroll
+            for (int b = 0; b < NB; b++)
+                if (c0 + k <= c_last) s[b] += v[k][b];
     }
     if (row < a.rows) {
 #pragma unroll
