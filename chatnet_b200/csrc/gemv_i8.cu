@@ -63,7 +63,11 @@ struct Geo {
     static constexpr int kThreads = (kGroups * kCons + 1) * 32;
     static constexpr int kStages = (DEEP ? 200 * 1024 : NT == 1 ? 72 * 1024 : 110 * 1024) / kStage;
     static constexpr int kXchg = DEEP == 2 ? 2 * kCons * 32 * NT * 4 : 0;  // group partials, two buffers
-    static constexpr int kSmem = kStages * kStage + 256 + kXchg;
+    // the cluster-pair form (batch 1-2): the partner CTA's sums of the shared tile
+    static constexpr int kPair = DEEP && NB <= 2 ? kRows * NB * 4 : 0;
+    static constexpr int kSmem = kStages * kStage + 256 + kXchg + kPair;
+    // full[kStages], empty[kStages] and the pair barrier fit the 256-byte slot
+    static_assert(16 * kStages + 8 <= 256, "barrier slot");
 };
 static_assert(Geo<1>::kStages >= 3 && Geo<3>::kStages >= 4 && Geo<8>::kStages >= 4 && Geo<16>::kStages >= 3,
               "pipeline depth");
@@ -89,6 +93,7 @@ struct Args {
     int* counters;        // [tiles][kCons], zero on entry, left zero
     uint32_t* err;
     XchgOut xo;           // size > 1: outputs go to every rank (one matrix only)
+    int pair;             // 1: CTAs 2k, 2k+1 (one cluster) split tile k's units (see pair_finish)
 };
 
 // Stores output value (b, row) of matrix m: locally, or, in an exchange, into
@@ -263,6 +268,81 @@ __device__ void finish_subtile(const Args& a, int r, int t, int warp, int tile, 
     if ((threadIdx.x & 31) == 0) atomicExch(ctr, 0);
 }
 
+// ---- cluster pairs ------------------------------------------------------------
+//
+// When a launch gives every 128-row tile exactly two CTAs (rows of 49-74
+// tiles at batch 1-2: Llama-2-70B's O and down), the pair runs as one
+// two-CTA cluster and meets in the leader's shared memory instead of the
+// global fix-up above, whose release-acquire counter and L2 partials add
+// ~3 us to the end of every CTA.  CTA 2k (cluster rank 0) holds units
+// [0, units/2) of tile k, CTA 2k+1 the rest; the partner stores each owned
+// sum into the leader's buffer (st.shared::cluster), and each of its warps
+// then arrives, with release semantics at cluster scope, on the leader's pair
+// barrier; the leader waits for all eight (bounded), adds the partner's sum
+// to its own -- the stream-K order, CTA 2k then 2k+1 -- and stores.  Every
+// thread of both CTAs arrives on the cluster barrier at entry, and a partner
+// warp waits on it before its first remote store, so the leader's shared
+// memory is live; the leader stays resident until its barrier completes, so
+// no remote store can land after it exits.
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+// address of the same shared-memory offset in cluster CTA `rank`
+__device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+// bounded wait on a local barrier whose arrivals come from the other CTA
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t addr, uint32_t parity) {
+    uint32_t done;
+    uint64_t t0 = 0;
+    for (;;) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(addr), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if (!t0) t0 = globaltimer_ns();
+        else if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    }
+}
+
+template <int NB>
+__device__ void pair_finish(const Args& a, int r, int t, int tile, const float (&acc)[Geo<NB>::NT], uint32_t seq,
+                            uint32_t pbar, uint32_t pbuf) {
+    static_assert(Geo<NB>::NT == 1, "cluster pairs run batch 1-2");
+    const int b = owned_seq<NB>(0, t, a.batch);
+    const uint32_t slot = pbuf + (uint32_t)(r * NB + (b < 0 ? 0 : b)) * 4u;
+    cluster_wait();
+    if (cluster_rank() != 0) {
+        if (b >= 0)
+            asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(map_rank(slot, 0)), "f"(acc[0]) : "memory");
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0)
+            asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(map_rank(pbar, 0))
+                         : "memory");
+        return;
+    }
+    if (!mbar_wait_cluster(pbar, 0)) {
+        atomicOr(a.err, kErrTimeout);
+        return;
+    }
+    const int m = mat_of(a, tile);
+    const int64_t rows = pick64(a.rows, m);
+    const int64_t row = (int64_t)(tile - (m == 2 ? a.toff[2] : m == 1 ? a.toff[1] : 0)) * kRows + r;
+    if (b >= 0 && row < rows) store_out(a, pickp(a.y, m), rows, b, row, acc[0] + lds_f32(slot), seq);
+}
+
 }  // namespace i8
 
 template <int NB, int DEEP>
@@ -277,6 +357,10 @@ __global__ void __launch_bounds__(i8::Geo<NB, DEEP>::kThreads, i8::Geo<NB, DEEP>
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStage);
     uint64_t* empty = full + kStages;
     float* xg = reinterpret_cast<float*>(smem + kStages * kStage + 256);  // [2][kCons][32][NT]
+    // cluster pairs: the leader's barrier and its buffer of the partner's sums
+    uint64_t* pbar_p = empty + kStages;
+    const uint32_t pbar = smem_u32(pbar_p), pbuf = smem_u32(smem + kStages * kStage + 256 + G::kXchg);
+    const bool pair = G::kPair != 0 && a.pair;
     constexpr int kGroups = G::kGroups;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -285,9 +369,11 @@ __global__ void __launch_bounds__(i8::Geo<NB, DEEP>::kThreads, i8::Geo<NB, DEEP>
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kCons);
         }
+        if (pair) mbar_init(pbar_p, kCons);
         fence_mbar_init();
     }
     __syncthreads();
+    if (pair) cluster_arrive_relaxed();
     pdl_trigger();
 
     const int64_t total = (int64_t)a.tiles * a.units;
@@ -508,6 +594,15 @@ __global__ void __launch_bounds__(i8::Geo<NB, DEEP>::kThreads, i8::Geo<NB, DEEP>
         }
         const bool head_cut = (et == tile0) && (u0 != 0);
         const bool tail_cut = eu + seg != a.units;
+        if constexpr (G::kPair != 0) {
+            if (pair) {
+                pair_finish<NB>(a, r_own, t, et, acc, seq, pbar, pbuf);
+                et++;
+                eu = 0;
+                segi++;
+                continue;
+            }
+        }
         finish_subtile<NB>(a, r_own, t, cw, et, cta, C, total, head_cut || tail_cut, et == tile0 ? 0 : 1,
                            acc, seq);
         et++;
@@ -642,6 +737,57 @@ size_t gemv_i8_partial_bytes(int ctas) { return (size_t)2 * ctas * i8::kRows * i
 
 static int g_sms[64] = {0};
 
+// Launch as two-CTA clusters (the cluster-pair form), with programmatic
+// dependent launch like launch_k.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pair(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                               Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// How many two-CTA clusters of a deep batch-1/2 instantiation fit on the
+// device at once (0 if the query fails); read once per device and form.
+template <int NB, int DEEP>
+static int pair_clusters(int dev) {
+    static int n[64];
+    static bool have[64] = {false};
+    if (have[dev & 63]) return n[dev & 63];
+    using G = i8::Geo<NB, DEEP>;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * g_sms[dev & 63]);
+    cfg.blockDim = dim3(G::kThreads);
+    cfg.dynamicSmemBytes = G::kSmem;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int c = 0;
+    if (cudaOccupancyMaxActiveClusters(&c, gemv_i8_q4k_kernel<NB, DEEP>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        c = 0;
+    }
+    n[dev & 63] = c;
+    have[dev & 63] = true;
+    return c;
+}
+
 int gemv_i8_prepare() {
     static std::mutex mu;  // callers may be several host threads (the no-alloc entry point has no context)
     static bool done[64] = {false};
@@ -701,6 +847,29 @@ int gemv_i8_run_group(cudaStream_t st, uint32_t* err, int nmat, const CUtensorMa
     const bool deep = ctas <= g_sms[dev & 63];  // one CTA per SM: the deep pipeline
     // batch 1-2, up to grouped_units() units per CTA: the deep pipeline with two consumer groups
     const bool grouped = deep && batch <= 2 && (int64_t)tiles * a.units <= (int64_t)grouped_units() * ctas;
+    // two CTAs per tile at batch 1-2, every pair resident at once: cluster pairs
+    a.pair = 0;
+    if (deep && batch <= 2 && ctas == 2 * tiles && (!xo || xo->size <= 1 || xo->ll)) {
+        const int fit = grouped ? (batch == 1 ? pair_clusters<1, 2>(dev) : pair_clusters<2, 2>(dev))
+                                : (batch == 1 ? pair_clusters<1, 1>(dev) : pair_clusters<2, 1>(dev));
+        a.pair = fit >= tiles ? 1 : 0;
+    }
+    if (a.pair) {
+        if (grouped && batch == 1)
+            CN_CUDA(launch_pair(gemv_i8_q4k_kernel<1, 2>, dim3(ctas), dim3(i8::Geo<1, 2>::kThreads),
+                                (size_t)i8::Geo<1, 2>::kSmem, st, mp, a));
+        else if (grouped)
+            CN_CUDA(launch_pair(gemv_i8_q4k_kernel<2, 2>, dim3(ctas), dim3(i8::Geo<2, 2>::kThreads),
+                                (size_t)i8::Geo<2, 2>::kSmem, st, mp, a));
+        else if (batch == 1)
+            CN_CUDA(launch_pair(gemv_i8_q4k_kernel<1, 1>, dim3(ctas), dim3(i8::Geo<1, 1>::kThreads),
+                                (size_t)i8::Geo<1, 1>::kSmem, st, mp, a));
+        else
+            CN_CUDA(launch_pair(gemv_i8_q4k_kernel<2, 1>, dim3(ctas), dim3(i8::Geo<2, 1>::kThreads),
+                                (size_t)i8::Geo<2, 1>::kSmem, st, mp, a));
+        CN_CUDA(cudaGetLastError());
+        return CN_OK;
+    }
     if (grouped) {
         if (batch == 1)
             CN_CUDA(launch_k(true, gemv_i8_q4k_kernel<1, 2>, dim3(ctas), dim3(i8::Geo<1, 2>::kThreads),

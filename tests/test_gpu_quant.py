@@ -122,6 +122,7 @@ TC_CASES = [
     (7, 4096),      # one tile shared by 7 CTAs
     (1024, 8192),   # Llama-2-70B k/v projection: 56 CTAs, up to 7 per tile
     (2048, 5632),   # inner dimension not a power of two
+    (8000, 8192),   # 63 tiles, ragged last: two CTAs per tile, cluster pairs at batch 1-2
 ]
 
 
@@ -138,12 +139,13 @@ def test_matvec_q4_k_decode(ctx, oracle, rows, cols, batch):
     assert rel_err(y, ref) <= REL_TOL
 
 
-def test_matvec_repeatable(ctx):
-    """Stream-K partials are combined in a fixed order: results are bitwise stable."""
-    rows, cols = 4096, 11008
+@pytest.mark.parametrize("rows,cols,batch", [(4096, 11008, 4), (8192, 8192, 1)])
+def test_matvec_repeatable(ctx, rows, cols, batch):
+    """Stream-K partials (and cluster pairs) are combined in a fixed order:
+    results are bitwise stable."""
     blocks = cn.synth_fill(cn.TYPE_Q4_K, rows, cols, seed=5)
     W = ctx.upload(blocks, cn.TYPE_Q4_K, rows, cols)
-    x = _x(4, cols, "rep")
+    x = _x(batch, cols, "rep")
     y0 = ctx.matvec(W, x)
     for _ in range(3):
         assert bits_equal(ctx.matvec(W, x), y0)
