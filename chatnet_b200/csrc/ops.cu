@@ -175,6 +175,18 @@ __device__ __forceinline__ void attn_finish(float* __restrict__ pr_base, int spl
     float* obuf = linv + ((kv_mul + 3) & ~3);           // [kv_mul * hd], 16-byte aligned
     for (int g = warp; g < kv_mul; g += nwarp) {
         const float* pr = pr_base + (size_t)g * splits * prow;
+        if (splits <= 32) {
+            // one split per lane: its m and l in one L2 round trip
+            const bool has = lane < splits;
+            const float m = has ? __ldcg(pr + (size_t)lane * prow + hd) : -FLT_MAX;
+            const float l = has ? __ldcg(pr + (size_t)lane * prow + hd + 1) : 0.f;
+            const float M = warp_max(m);
+            const float w = m > -FLT_MAX ? expf(m - M) : 0.f;
+            if (has) wsm[g * splits + lane] = w;
+            const float lsum = warp_sum(w * l);
+            if (lane == 0) linv[g] = 1.0f / lsum;
+            continue;
+        }
         float M = -FLT_MAX;
         for (int t = lane; t < splits; t += 32) M = fmaxf(M, __ldcg(pr + (size_t)t * prow + hd));
         M = warp_max(M);
