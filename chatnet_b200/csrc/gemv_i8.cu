@@ -40,6 +40,7 @@ namespace i8 {
 constexpr int kRows = 128;
 constexpr int kRaw = 144 * kRows;  // raw Q4_K bytes per unit per tile
 constexpr int kCons = 8;           // consumer warps, 16 rows each
+constexpr int kMaxCluster = 8;     // most CTAs of one tile that meet in a cluster (portable size)
 
 // Three CTAs per SM with three stages each when one n-tile of activation
 // digits suffices (batch 1, 2), else two CTAs with four stages.  DEEP: one
@@ -63,10 +64,10 @@ struct Geo {
     static constexpr int kThreads = (kGroups * kCons + 1) * 32;
     static constexpr int kStages = (DEEP ? 200 * 1024 : NT == 1 ? 72 * 1024 : 110 * 1024) / kStage;
     static constexpr int kXchg = DEEP == 2 ? 2 * kCons * 32 * NT * 4 : 0;  // group partials, two buffers
-    // the cluster-pair form (batch 1-2): the partner CTA's sums of the shared tile
-    static constexpr int kPair = DEEP && NB <= 2 ? kRows * NB * 4 : 0;
+    // the cluster form (batch 1-2): the other CTAs' sums of the shared tile
+    static constexpr int kPair = DEEP && NB <= 2 ? (kMaxCluster - 1) * kRows * NB * 4 : 0;
     static constexpr int kSmem = kStages * kStage + 256 + kXchg + kPair;
-    // full[kStages], empty[kStages] and the pair barrier fit the 256-byte slot
+    // full[kStages], empty[kStages] and the cluster barrier fit the 256-byte slot
     static_assert(16 * kStages + 8 <= 256, "barrier slot");
 };
 static_assert(Geo<1>::kStages >= 3 && Geo<3>::kStages >= 4 && Geo<8>::kStages >= 4 && Geo<16>::kStages >= 3,
@@ -93,7 +94,7 @@ struct Args {
     int* counters;        // [tiles][kCons], zero on entry, left zero
     uint32_t* err;
     XchgOut xo;           // size > 1: outputs go to every rank (one matrix only)
-    int pair;             // 1: CTAs 2k, 2k+1 (one cluster) split tile k's units (see pair_finish)
+    int csize;            // > 1: CTAs csize*k .. csize*k + csize-1 (one cluster) split tile k's units (cluster_finish)
 };
 
 // Stores output value (b, row) of matrix m: locally, or, in an exchange, into
@@ -268,22 +269,23 @@ __device__ void finish_subtile(const Args& a, int r, int t, int warp, int tile, 
     if ((threadIdx.x & 31) == 0) atomicExch(ctr, 0);
 }
 
-// ---- cluster pairs ------------------------------------------------------------
+// ---- cluster splits -----------------------------------------------------------
 //
-// When a launch gives every 128-row tile exactly two CTAs (rows of 49-74
-// tiles at batch 1-2: Llama-2-70B's O and down), the pair runs as one
-// two-CTA cluster and meets in the leader's shared memory instead of the
+// When a launch gives every 128-row tile the same number s (2..8) of CTAs
+// (batch 1-2 grids of fewer tiles than SMs: Llama-2-70B's O and down with
+// s = 2, tensor-parallel q/k/v shards with s up to 7), the s CTAs of a tile
+// run as one cluster and meet in the leader's shared memory instead of the
 // global fix-up above, whose release-acquire counter and L2 partials add
-// ~3 us to the end of every CTA.  CTA 2k (cluster rank 0) holds units
-// [0, units/2) of tile k, CTA 2k+1 the rest; the partner stores each owned
-// sum into the leader's buffer (st.shared::cluster), and each of its warps
-// then arrives, with release semantics at cluster scope, on the leader's pair
-// barrier; the leader waits for all eight (bounded), adds the partner's sum
-// to its own -- the stream-K order, CTA 2k then 2k+1 -- and stores.  Every
-// thread of both CTAs arrives on the cluster barrier at entry, and a partner
-// warp waits on it before its first remote store, so the leader's shared
-// memory is live; the leader stays resident until its barrier completes, so
-// no remote store can land after it exits.
+// ~3 us to the end of every CTA.  CTA s*k + j (cluster rank j) holds the
+// j-th of s equal parts of tile k's units; each other CTA stores its owned
+// sums into the leader's buffer slot j-1 (st.shared::cluster), and each of
+// its warps then arrives, with release semantics at cluster scope, on the
+// leader's barrier; the leader waits for all 8 (s - 1) arrivals (bounded),
+// adds the slots to its own sums in rank order -- the stream-K order -- and
+// stores.  Every thread of the cluster arrives on the cluster barrier at
+// entry, and a warp waits on it before its first remote store, so the
+// leader's shared memory is live; the leader stays resident until its
+// barrier completes, so no remote store can land after it exits.
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -318,15 +320,19 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t addr, uint32_t parity
 }
 
 template <int NB>
-__device__ void pair_finish(const Args& a, int r, int t, int tile, const float (&acc)[Geo<NB>::NT], uint32_t seq,
-                            uint32_t pbar, uint32_t pbuf) {
-    static_assert(Geo<NB>::NT == 1, "cluster pairs run batch 1-2");
+__device__ void cluster_finish(const Args& a, int r, int t, int tile, const float (&acc)[Geo<NB>::NT],
+                               uint32_t seq, uint32_t pbar, uint32_t pbuf) {
+    static_assert(Geo<NB>::NT == 1, "cluster splits run batch 1-2");
+    constexpr uint32_t kSlot = kRows * NB * 4;  // bytes of one CTA's sums
     const int b = owned_seq<NB>(0, t, a.batch);
-    const uint32_t slot = pbuf + (uint32_t)(r * NB + (b < 0 ? 0 : b)) * 4u;
+    const uint32_t own = (uint32_t)(r * NB + (b < 0 ? 0 : b)) * 4u;
     cluster_wait();
-    if (cluster_rank() != 0) {
+    const uint32_t rank = cluster_rank();
+    if (rank != 0) {
         if (b >= 0)
-            asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(map_rank(slot, 0)), "f"(acc[0]) : "memory");
+            asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(map_rank(pbuf + (rank - 1) * kSlot + own, 0)),
+                         "f"(acc[0])
+                         : "memory");
         __syncwarp();
         if ((threadIdx.x & 31) == 0)
             asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(map_rank(pbar, 0))
@@ -340,7 +346,12 @@ __device__ void pair_finish(const Args& a, int r, int t, int tile, const float (
     const int m = mat_of(a, tile);
     const int64_t rows = pick64(a.rows, m);
     const int64_t row = (int64_t)(tile - (m == 2 ? a.toff[2] : m == 1 ? a.toff[1] : 0)) * kRows + r;
-    if (b >= 0 && row < rows) store_out(a, pickp(a.y, m), rows, b, row, acc[0] + lds_f32(slot), seq);
+    if (b < 0 || row >= rows) return;
+    float v = acc[0];
+    uint32_t p = pbuf + own;
+#pragma unroll 1
+    for (int j = 1; j < a.csize; j++, p += kSlot) v += lds_f32(p);
+    store_out(a, pickp(a.y, m), rows, b, row, v, seq);
 }
 
 }  // namespace i8
@@ -360,7 +371,7 @@ __global__ void __launch_bounds__(i8::Geo<NB, DEEP>::kThreads, i8::Geo<NB, DEEP>
     // cluster pairs: the leader's barrier and its buffer of the partner's sums
     uint64_t* pbar_p = empty + kStages;
     const uint32_t pbar = smem_u32(pbar_p), pbuf = smem_u32(smem + kStages * kStage + 256 + G::kXchg);
-    const bool pair = G::kPair != 0 && a.pair;
+    const bool pair = G::kPair != 0 && a.csize > 1;
     constexpr int kGroups = G::kGroups;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -369,7 +380,7 @@ __global__ void __launch_bounds__(i8::Geo<NB, DEEP>::kThreads, i8::Geo<NB, DEEP>
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kCons);
         }
-        if (pair) mbar_init(pbar_p, kCons);
+        if (pair) mbar_init(pbar_p, kCons * (a.csize - 1));
         fence_mbar_init();
     }
     __syncthreads();
@@ -596,7 +607,7 @@ __global__ void __launch_bounds__(i8::Geo<NB, DEEP>::kThreads, i8::Geo<NB, DEEP>
         const bool tail_cut = eu + seg != a.units;
         if constexpr (G::kPair != 0) {
             if (pair) {
-                pair_finish<NB>(a, r_own, t, et, acc, seq, pbar, pbuf);
+                cluster_finish<NB>(a, r_own, t, et, acc, seq, pbar, pbuf);
                 et++;
                 eu = 0;
                 segi++;
@@ -737,11 +748,11 @@ size_t gemv_i8_partial_bytes(int ctas) { return (size_t)2 * ctas * i8::kRows * i
 
 static int g_sms[64] = {0};
 
-// Launch as two-CTA clusters (the cluster-pair form), with programmatic
+// Launch as clusters of `cs` CTAs (the cluster-split form), with programmatic
 // dependent launch like launch_k.
 template <typename... KArgs, typename... Args>
-static cudaError_t launch_pair(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                               Args... args) {
+static cudaError_t launch_cluster(int cs, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                  cudaStream_t st, Args... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -749,7 +760,7 @@ static cudaError_t launch_pair(void (*kernel)(KArgs...), dim3 grid, dim3 block, 
     cfg.stream = st;
     cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.x = (unsigned)cs;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
     at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -759,21 +770,24 @@ static cudaError_t launch_pair(void (*kernel)(KArgs...), dim3 grid, dim3 block, 
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
-// How many two-CTA clusters of a deep batch-1/2 instantiation fit on the
-// device at once (0 if the query fails); read once per device and form.
+// How many clusters of `cs` CTAs of a deep batch-1/2 instantiation fit on
+// the device at once (0 if the query fails); read once per device, form and
+// size.
 template <int NB, int DEEP>
-static int pair_clusters(int dev) {
-    static int n[64];
-    static bool have[64] = {false};
-    if (have[dev & 63]) return n[dev & 63];
+static int cluster_fit(int dev, int cs) {
+    static std::mutex mu;
+    static int n[64][i8::kMaxCluster + 1];
+    static bool have[64][i8::kMaxCluster + 1] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (have[dev & 63][cs]) return n[dev & 63][cs];
     using G = i8::Geo<NB, DEEP>;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * g_sms[dev & 63]);
+    cfg.gridDim = dim3(cs * g_sms[dev & 63]);
     cfg.blockDim = dim3(G::kThreads);
     cfg.dynamicSmemBytes = G::kSmem;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.x = (unsigned)cs;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
@@ -783,8 +797,8 @@ static int pair_clusters(int dev) {
         cudaGetLastError();
         c = 0;
     }
-    n[dev & 63] = c;
-    have[dev & 63] = true;
+    n[dev & 63][cs] = c;
+    have[dev & 63][cs] = true;
     return c;
 }
 
@@ -847,26 +861,29 @@ int gemv_i8_run_group(cudaStream_t st, uint32_t* err, int nmat, const CUtensorMa
     const bool deep = ctas <= g_sms[dev & 63];  // one CTA per SM: the deep pipeline
     // batch 1-2, up to grouped_units() units per CTA: the deep pipeline with two consumer groups
     const bool grouped = deep && batch <= 2 && (int64_t)tiles * a.units <= (int64_t)grouped_units() * ctas;
-    // two CTAs per tile at batch 1-2, every pair resident at once: cluster pairs
-    a.pair = 0;
-    if (deep && batch <= 2 && ctas == 2 * tiles && (!xo || xo->size <= 1 || xo->ll)) {
-        const int fit = grouped ? (batch == 1 ? pair_clusters<1, 2>(dev) : pair_clusters<2, 2>(dev))
-                                : (batch == 1 ? pair_clusters<1, 1>(dev) : pair_clusters<2, 1>(dev));
-        a.pair = fit >= tiles ? 1 : 0;
+    // the same number (2..8) of CTAs on every tile at batch 1-2, every
+    // cluster resident at once: cluster splits
+    a.csize = 0;
+    const int cs = ctas % tiles == 0 ? ctas / tiles : 0;
+    if (deep && batch <= 2 && cs >= 2 && cs <= i8::kMaxCluster && cs <= a.units &&
+        (!xo || xo->size <= 1 || xo->ll)) {
+        const int fit = grouped ? (batch == 1 ? cluster_fit<1, 2>(dev, cs) : cluster_fit<2, 2>(dev, cs))
+                                : (batch == 1 ? cluster_fit<1, 1>(dev, cs) : cluster_fit<2, 1>(dev, cs));
+        a.csize = fit >= tiles ? cs : 0;
     }
-    if (a.pair) {
+    if (a.csize) {
         if (grouped && batch == 1)
-            CN_CUDA(launch_pair(gemv_i8_q4k_kernel<1, 2>, dim3(ctas), dim3(i8::Geo<1, 2>::kThreads),
-                                (size_t)i8::Geo<1, 2>::kSmem, st, mp, a));
+            CN_CUDA(launch_cluster(cs, gemv_i8_q4k_kernel<1, 2>, dim3(ctas), dim3(i8::Geo<1, 2>::kThreads),
+                                   (size_t)i8::Geo<1, 2>::kSmem, st, mp, a));
         else if (grouped)
-            CN_CUDA(launch_pair(gemv_i8_q4k_kernel<2, 2>, dim3(ctas), dim3(i8::Geo<2, 2>::kThreads),
-                                (size_t)i8::Geo<2, 2>::kSmem, st, mp, a));
+            CN_CUDA(launch_cluster(cs, gemv_i8_q4k_kernel<2, 2>, dim3(ctas), dim3(i8::Geo<2, 2>::kThreads),
+                                   (size_t)i8::Geo<2, 2>::kSmem, st, mp, a));
         else if (batch == 1)
-            CN_CUDA(launch_pair(gemv_i8_q4k_kernel<1, 1>, dim3(ctas), dim3(i8::Geo<1, 1>::kThreads),
-                                (size_t)i8::Geo<1, 1>::kSmem, st, mp, a));
+            CN_CUDA(launch_cluster(cs, gemv_i8_q4k_kernel<1, 1>, dim3(ctas), dim3(i8::Geo<1, 1>::kThreads),
+                                   (size_t)i8::Geo<1, 1>::kSmem, st, mp, a));
         else
-            CN_CUDA(launch_pair(gemv_i8_q4k_kernel<2, 1>, dim3(ctas), dim3(i8::Geo<2, 1>::kThreads),
-                                (size_t)i8::Geo<2, 1>::kSmem, st, mp, a));
+            CN_CUDA(launch_cluster(cs, gemv_i8_q4k_kernel<2, 1>, dim3(ctas), dim3(i8::Geo<2, 1>::kThreads),
+                                   (size_t)i8::Geo<2, 1>::kSmem, st, mp, a));
         CN_CUDA(cudaGetLastError());
         return CN_OK;
     }

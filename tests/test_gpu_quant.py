@@ -120,9 +120,9 @@ TC_CASES = [
     (300, 768),     # ragged last tile
     (1, 256),       # one row, one unit
     (7, 4096),      # one tile shared by 7 CTAs
-    (1024, 8192),   # Llama-2-70B k/v projection: 56 CTAs, up to 7 per tile
+    (1024, 8192),   # Llama-2-70B k/v projection: 7 CTAs per tile (clusters of 7 at batch 1-2)
     (2048, 5632),   # inner dimension not a power of two
-    (8000, 8192),   # 63 tiles, ragged last: two CTAs per tile, cluster pairs at batch 1-2
+    (8000, 8192),   # 63 tiles, ragged last: two CTAs per tile, clusters of 2 at batch 1-2
 ]
 
 
@@ -139,10 +139,10 @@ def test_matvec_q4_k_decode(ctx, oracle, rows, cols, batch):
     assert rel_err(y, ref) <= REL_TOL
 
 
-@pytest.mark.parametrize("rows,cols,batch", [(4096, 11008, 4), (8192, 8192, 1)])
+@pytest.mark.parametrize("rows,cols,batch", [(4096, 11008, 4), (8192, 8192, 1), (1024, 8192, 2)])
 def test_matvec_repeatable(ctx, rows, cols, batch):
-    """Stream-K partials (and cluster pairs) are combined in a fixed order:
-    results are bitwise stable."""
+    """Stream-K partials (and cluster splits of 2 and 7 CTAs per tile) are
+    combined in a fixed order: results are bitwise stable."""
     blocks = cn.synth_fill(cn.TYPE_Q4_K, rows, cols, seed=5)
     W = ctx.upload(blocks, cn.TYPE_Q4_K, rows, cols)
     x = _x(batch, cols, "rep")
