@@ -133,6 +133,37 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity) 
     }
 }
 
+// Thread-block clusters (more below): the relaxed arrival on the cluster
+// barrier (every thread of the cluster arrives once; a wait returns once all
+// have), the address of a shared-memory offset in another CTA of the
+// cluster, and a bounded wait on a local mbarrier that other CTAs arrive on.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+// address of the same shared-memory offset in cluster CTA `rank`
+__device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+// bounded wait on a local barrier whose arrivals come from other CTAs of the cluster
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t addr, uint32_t parity) {
+    uint32_t done;
+    uint64_t t0 = 0;
+    for (;;) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(addr), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if (!t0) t0 = globaltimer_ns();
+        else if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    }
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
                                             uint64_t* bar) {
     asm volatile(

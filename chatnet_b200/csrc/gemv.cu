@@ -27,6 +27,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <mutex>
 #include <vector>
 
 #include "cn_common.cuh"
@@ -101,6 +102,11 @@ struct Geo {
                                             : ((kFull - kFixed) / kStage > 6 ? 6 : (kFull - kFixed) / kStage);
     static constexpr int kMinCtas = kS2 >= 3 ? 2 : 1;
     static constexpr int kSmem = kFixed + kStages * kStage;
+    // cluster split (batch 1-8): one slot of a CTA's sums, and the most
+    // slots the leader can add past kSmem within the 227 KB a CTA may use
+    static constexpr int kSlotB = kTileRows * NT * 4 * 4;
+    static constexpr int kClusMax =
+        NT > 2 ? 0 : ((227 * 1024 - kSmem) / kSlotB > 7 ? 7 : (227 * 1024 - kSmem) / kSlotB);
 };
 
 // Up to three matrices with the same input run as one launch (q/k/v,
@@ -127,6 +133,7 @@ struct GemvArgs {
     float* partials;     // [2 * ctas][128 rows][nt*4] stream-K partial slots
     int* counters;       // [tiles * kCons]
     uint32_t* err;
+    int csize;           // > 1: CTAs csize*k .. csize*k + csize-1 (one cluster) split tile k (cluster_finish_mma)
 };
 
 // 32-bit word at byte offset `off` of a 4-byte aligned shared row, where
@@ -567,6 +574,62 @@ __device__ void finish_shared(const GemvArgs& a, int tile, int warp, int cta, in
     if (lane == 0) atomicExch(ctr, 0);
 }
 
+// Cluster split (batch 1-8, the same number s = 2..8 of CTAs on every
+// tile): the s CTAs of tile k form one cluster; rank j > 0 stores its sums
+// into the leader's slot j - 1 (dynamic shared memory past the kernel's own
+// layout) and each of its warps arrives on the leader's barrier with release
+// semantics at cluster scope; the leader waits for all kCons (s - 1)
+// arrivals (bounded) and adds the slots after its own sums in rank order --
+// the stream-K order of finish_shared, without its L2 partials and counter.
+template <int NT>
+__device__ void cluster_finish_mma(const GemvArgs& a, int tile, int warp, int g, int t, int lane,
+                                   float (&acc)[NT][4], uint32_t pbar, uint32_t pbuf, const float* slots) {
+    constexpr int BW = NT * 4;
+    constexpr uint32_t kSlot = kTileRows * BW * 4;  // bytes of one CTA's sums
+    const int r0 = warp * 16 + g, r1 = r0 + 8;
+    cluster_wait();
+    const uint32_t rank = cluster_rank();
+    if (rank != 0) {
+        const uint32_t dst = map_rank(pbuf + (rank - 1) * kSlot, 0);
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            const uint32_t c = (uint32_t)(nt * 4 + t) * 4u;
+            asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(dst + (uint32_t)r0 * BW * 4 + c),
+                         "f"(acc[nt][0] + acc[nt][1])
+                         : "memory");
+            asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(dst + (uint32_t)r1 * BW * 4 + c),
+                         "f"(acc[nt][2] + acc[nt][3])
+                         : "memory");
+        }
+        __syncwarp();
+        if (lane == 0)
+            asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(map_rank(pbar, 0))
+                         : "memory");
+        return;
+    }
+    if (!mbar_wait_cluster(pbar, 0)) {
+        if (lane == 0) atomicOr(a.err, kErrTimeout);
+        return;
+    }
+    int local;
+    int64_t rows;
+    float* y;
+    tile_mat(a, tile, local, rows, y);
+    const int64_t g0 = (int64_t)local * kTileRows + r0, g1 = g0 + 8;
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+        const int b = nt * 4 + t;
+        if (b >= a.batch) continue;
+        float v0 = acc[nt][0] + acc[nt][1], v1 = acc[nt][2] + acc[nt][3];
+#pragma unroll 1
+        for (int j = 1; j < a.csize; j++) {
+            v0 += slots[(j - 1) * kTileRows * BW + r0 * BW + b];
+            v1 += slots[(j - 1) * kTileRows * BW + r1 * BW + b];
+        }
+        if (g0 < rows) y[(size_t)b * rows + g0] = v0;
+        if (g1 < rows) y[(size_t)b * rows + g1] = v1;
+    }
+}
 
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile(
@@ -591,6 +654,10 @@ __global__ void __launch_bounds__(kThreads, Geo<TYPE, NT>::kMinCtas)
     float2* table = reinterpret_cast<float2*>(smem + S * G::kStage);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * G::kStage + G::kTable);
     uint64_t* empty = full + S;
+    // cluster split: the leader's barrier, and its slots past the layout above
+    uint64_t* pbar_p = empty + S;
+    static_assert(16 * G::kStages + 8 <= 64 * 16, "barrier slot");
+    const bool clus = NT <= 2 && a.csize > 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
@@ -598,22 +665,52 @@ __global__ void __launch_bounds__(kThreads, Geo<TYPE, NT>::kMinCtas)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kCons);
         }
+        if (clus) mbar_init(pbar_p, kCons * (a.csize - 1));
         fence_mbar_init();
     }
     __syncthreads();
+    if (clus) cluster_arrive_relaxed();
     pdl_trigger();
-    pdl_wait();
 
     const int64_t total = (int64_t)a.tiles * a.units;
     const int C = (int)(total < (int64_t)gridDim.x ? total : (int64_t)gridDim.x);
     const int cta = blockIdx.x;
-    if (cta >= C) return;
+    if (cta >= C) {
+        pdl_wait();
+        return;
+    }
     const int64_t v0 = range_start(total, cta, C), v1 = range_start(total, cta + 1, C);
 
     if (warp == kCons) {
         // producer: one lane streams raw blocks + activation fragments
-        if (lane != 0) return;
+        if (lane != 0) {
+            pdl_wait();
+            return;
+        }
         const int nunits = (int)(v1 - v0);
+        auto load_w = [&](uint8_t* st, int tile, int u, uint64_t* bar) {
+            int local;
+            int64_t rows;
+            float* y;
+            const int m = tile_mat(a, tile, local, rows, y);
+            tma_load_2d(st, &maps.m[m], Fmt<TYPE>::box_x(u), local * kTileRows, bar);
+        };
+        // the weights depend on no earlier kernel: the first stages' weight
+        // loads start before the wait for the kernel that writes the
+        // activation fragments
+        const int pre = nunits < S ? nunits : S;
+        {
+            int tile = (int)(v0 / a.units), u = (int)(v0 % a.units);
+            for (int k = 0; k < pre; k++) {
+                mbar_expect_tx(&full[k], G::kBytes);
+                load_w(stages + k * G::kStage, tile, u, &full[k]);
+                if (++u == a.units) {
+                    u = 0;
+                    tile++;
+                }
+            }
+        }
+        pdl_wait();
         int tile = (int)(v0 / a.units), u = (int)(v0 % a.units);
         int s = 0;
         uint32_t n = 0, phase = 0;
@@ -624,13 +721,9 @@ __global__ void __launch_bounds__(kThreads, Geo<TYPE, NT>::kMinCtas)
                 return;
             }
             uint8_t* st = stages + s * G::kStage;
-            mbar_expect_tx(&full[s], G::kBytes);
-            {
-                int local;
-                int64_t rows;
-                float* y;
-                const int m = tile_mat(a, tile, local, rows, y);
-                tma_load_2d(st, &maps.m[m], Fmt<TYPE>::box_x(u), local * kTileRows, &full[s]);
+            if (n >= (uint32_t)S) {
+                mbar_expect_tx(&full[s], G::kBytes);
+                load_w(st, tile, u, &full[s]);
             }
             bulk_g2s(st + G::kW, a.xfrag + (size_t)u * 8 * NT * 32, G::kXF, &full[s]);
             if constexpr (G::kXS > 0)
@@ -650,6 +743,7 @@ __global__ void __launch_bounds__(kThreads, Geo<TYPE, NT>::kMinCtas)
         return;
     }
 
+    pdl_wait();
     const int g = lane >> 2, t = lane & 3;
     bool live[NT];
 #pragma unroll
@@ -698,6 +792,13 @@ __global__ void __launch_bounds__(kThreads, Geo<TYPE, NT>::kMinCtas)
             // only the first and the last tile of the range can be shared
             const bool head_cut = (tile == tile0) && (u0 != 0);
             const bool tail_cut = (n == nunits - 1) && (u != a.units - 1);
+            if constexpr (NT <= 2) {
+                if (clus) {  // the range lies in one tile: this is its last unit
+                    cluster_finish_mma<NT>(a, tile, warp, g, t, lane, acc, smem_u32(pbar_p), smem_u32(smem + G::kSmem),
+                                           reinterpret_cast<const float*>(smem + G::kSmem));
+                    break;
+                }
+            }
             if (head_cut || tail_cut)
                 finish_shared<NT>(a, tile, warp, cta, tile == tile0 ? 0 : 1, total, C, g, t, lane, acc);
             else
@@ -1260,7 +1361,7 @@ static int occupancy_ctas(cn_ctx* ctx) {
     if (cached[dev] <= 0) {
         auto k = gemv_kernel<TYPE, NT>;
         CN_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     Geo<TYPE, NT>::kSmem));
+                                     Geo<TYPE, NT>::kSmem + Geo<TYPE, NT>::kClusMax * Geo<TYPE, NT>::kSlotB));
         int n = 0;
         CN_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kThreads, Geo<TYPE, NT>::kSmem));
         cached[dev] = n > 0 ? n : 1;
@@ -1362,10 +1463,54 @@ int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool
     return CN_OK;
 }
 
+// How many clusters of `cs` CTAs of gemv_kernel<TYPE, NT> fit on the device
+// at once with cs - 1 slots (0 if the query fails); read once per device and
+// size.
 template <int TYPE, int NT>
-static int launch_tma(cn_ctx* ctx, const GemvMaps* maps, const GemvPlan& p, const GemvArgs& a) {
-    CN_CUDA(launch_k(true, gemv_kernel<TYPE, NT>, dim3(p.ctas), dim3(kThreads), (size_t)Geo<TYPE, NT>::kSmem,
-                     ctx->stream, *maps, a));
+static int cluster_fit_mma(int dev, int cs) {
+    static std::mutex mu;
+    static int n[64][9];
+    static bool have[64][9] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (have[dev & 63][cs]) return n[dev & 63][cs];
+    using G = Geo<TYPE, NT>;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cs * 64);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = (size_t)G::kSmem + (size_t)(cs - 1) * G::kSlotB;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = (unsigned)cs;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int c = 0;
+    if (cudaOccupancyMaxActiveClusters(&c, gemv_kernel<TYPE, NT>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        c = 0;
+    }
+    n[dev & 63][cs] = c;
+    have[dev & 63][cs] = true;
+    return c;
+}
+
+template <int TYPE, int NT>
+static int launch_tma(cn_ctx* ctx, const GemvMaps* maps, const GemvPlan& p, GemvArgs a) {
+    using G = Geo<TYPE, NT>;
+    // the same number (2..8) of CTAs on every tile at batch 1-8, every
+    // cluster resident at once: cluster split
+    a.csize = 0;
+    const int cs = p.ctas % p.tiles == 0 ? p.ctas / p.tiles : 0;
+    if (NT <= 2 && cs >= 2 && cs - 1 <= G::kClusMax && cs <= p.units &&
+        cluster_fit_mma<TYPE, NT>(ctx->device, cs) >= p.tiles) {
+        a.csize = cs;
+        CN_CUDA(launch_cluster_k(true, cs, gemv_kernel<TYPE, NT>, dim3(p.ctas), dim3(kThreads),
+                                 (size_t)G::kSmem + (size_t)(cs - 1) * G::kSlotB, ctx->stream, *maps, a));
+    } else {
+        CN_CUDA(launch_k(true, gemv_kernel<TYPE, NT>, dim3(p.ctas), dim3(kThreads), (size_t)G::kSmem, ctx->stream,
+                         *maps, a));
+    }
     CN_CUDA(cudaGetLastError());
     return CN_OK;
 }

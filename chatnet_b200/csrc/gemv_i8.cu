@@ -286,39 +286,6 @@ __device__ void finish_subtile(const Args& a, int r, int t, int warp, int tile, 
 // entry, and a warp waits on it before its first remote store, so the
 // leader's shared memory is live; the leader stays resident until its
 // barrier completes, so no remote store can land after it exits.
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ void cluster_arrive_relaxed() {
-    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
-// address of the same shared-memory offset in cluster CTA `rank`
-__device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-    return r;
-}
-// bounded wait on a local barrier whose arrivals come from the other CTA
-__device__ __forceinline__ bool mbar_wait_cluster(uint32_t addr, uint32_t parity) {
-    uint32_t done;
-    uint64_t t0 = 0;
-    for (;;) {
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(done)
-            : "r"(addr), "r"(parity)
-            : "memory");
-        if (done) return true;
-        if (!t0) t0 = globaltimer_ns();
-        else if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
-    }
-}
-
 template <int NB>
 __device__ void cluster_finish(const Args& a, int r, int t, int tile, const float (&acc)[Geo<NB>::NT],
                                uint32_t seq, uint32_t pbar, uint32_t pbuf) {
@@ -748,28 +715,6 @@ size_t gemv_i8_partial_bytes(int ctas) { return (size_t)2 * ctas * i8::kRows * i
 
 static int g_sms[64] = {0};
 
-// Launch as clusters of `cs` CTAs (the cluster-split form), with programmatic
-// dependent launch like launch_k.
-template <typename... KArgs, typename... Args>
-static cudaError_t launch_cluster(int cs, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                                  cudaStream_t st, Args... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute at[2];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = (unsigned)cs;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
-    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = pdl_enabled() ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
-}
-
 // How many clusters of `cs` CTAs of a deep batch-1/2 instantiation fit on
 // the device at once (0 if the query fails); read once per device, form and
 // size.
@@ -873,17 +818,17 @@ int gemv_i8_run_group(cudaStream_t st, uint32_t* err, int nmat, const CUtensorMa
     }
     if (a.csize) {
         if (grouped && batch == 1)
-            CN_CUDA(launch_cluster(cs, gemv_i8_q4k_kernel<1, 2>, dim3(ctas), dim3(i8::Geo<1, 2>::kThreads),
-                                   (size_t)i8::Geo<1, 2>::kSmem, st, mp, a));
+            CN_CUDA(launch_cluster_k(true, cs, gemv_i8_q4k_kernel<1, 2>, dim3(ctas),
+                                     dim3(i8::Geo<1, 2>::kThreads), (size_t)i8::Geo<1, 2>::kSmem, st, mp, a));
         else if (grouped)
-            CN_CUDA(launch_cluster(cs, gemv_i8_q4k_kernel<2, 2>, dim3(ctas), dim3(i8::Geo<2, 2>::kThreads),
-                                   (size_t)i8::Geo<2, 2>::kSmem, st, mp, a));
+            CN_CUDA(launch_cluster_k(true, cs, gemv_i8_q4k_kernel<2, 2>, dim3(ctas),
+                                     dim3(i8::Geo<2, 2>::kThreads), (size_t)i8::Geo<2, 2>::kSmem, st, mp, a));
         else if (batch == 1)
-            CN_CUDA(launch_cluster(cs, gemv_i8_q4k_kernel<1, 1>, dim3(ctas), dim3(i8::Geo<1, 1>::kThreads),
-                                   (size_t)i8::Geo<1, 1>::kSmem, st, mp, a));
+            CN_CUDA(launch_cluster_k(true, cs, gemv_i8_q4k_kernel<1, 1>, dim3(ctas),
+                                     dim3(i8::Geo<1, 1>::kThreads), (size_t)i8::Geo<1, 1>::kSmem, st, mp, a));
         else
-            CN_CUDA(launch_cluster(cs, gemv_i8_q4k_kernel<2, 1>, dim3(ctas), dim3(i8::Geo<2, 1>::kThreads),
-                                   (size_t)i8::Geo<2, 1>::kSmem, st, mp, a));
+            CN_CUDA(launch_cluster_k(true, cs, gemv_i8_q4k_kernel<2, 1>, dim3(ctas),
+                                     dim3(i8::Geo<2, 1>::kThreads), (size_t)i8::Geo<2, 1>::kSmem, st, mp, a));
         CN_CUDA(cudaGetLastError());
         return CN_OK;
     }
