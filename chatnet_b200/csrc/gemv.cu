@@ -1452,7 +1452,20 @@ int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool
 #ifdef CHATNET_TUNING
     if (const char* e = getenv("CHATNET_MMA_WHOLE_TILES")) whole = atoi(e);
 #endif
-    if (whole > 0 && p->tiles >= whole && p->units <= 16 && p->tiles <= ctx->sms * occ) ctas = p->tiles;
+    if (whole > 0 && p->tiles >= whole && p->units <= 16 && p->tiles <= ctx->sms * occ) {
+        ctas = p->tiles;
+        // at batch 1-8, s = 2..4 CTAs per tile when all of them are resident
+        // together, at least two units each: a cluster split (launch_tma),
+        // whose fix-up costs little.  Measured on B200 (prep + GEMV, us):
+        // Q4_0 5632 x 2048 10.7 -> 8.3 / 7.5 / 6.7 at s = 2 / 3 / 4 (7.7 at
+        // s = 6), Q6_K 11008 x 4096 26.6 -> 17.9 / 17.8 at s = 2 / 3, and
+        // TinyLlama decode 911 -> 987 / 1005 tok/s at s = 2 / 3 for its
+        // 88-tile gate/up.
+        int sp = (ctx->sms * occ) / p->tiles;
+        if (sp > p->units / 2) sp = p->units / 2;
+        if (sp > 4) sp = 4;
+        if (p->nt <= 2 && sp >= 2) ctas = sp * p->tiles;
+    }
     p->ctas = ctas;
     const int chunks = p->units * 8;
     p->xfrag_bytes = (size_t)chunks * p->nt * 32 * sizeof(uint4);
