@@ -680,15 +680,20 @@ int gemv_i8_ctas(int sms, int tiles, int units, int batch) {
     // One n-tile of activation digits (batch 1, 2): at most one CTA per SM,
     // which then runs the deep pipeline (gemv_i8_run_group).  With at least
     // as many tiles as SMs, one CTA per SM splits the units evenly; with
-    // fewer, s CTAs per tile: 1 for rows of at most 16 units (the split's
-    // fix-up costs more than it saves there), else the largest s <= 7 with
-    // tiles * s <= sms.  Measured on B200 (prep + GEMV replayed from a graph,
-    // batch 1, us), this grid against 444 three-stage CTAs: 57344x8192 50.6
-    // vs 54.5, 10240x8192 15.6 vs 20.8, 8192x28672 29.3 vs 39.6, 8192x3584
-    // 9.2 vs 19.7, 8192x1024 5.4 vs 9.0.
+    // fewer, s CTAs per tile: the largest s <= 7 with tiles * s <= sms, and
+    // for rows of at most 16 units also s <= 4 with at least two units per
+    // CTA (such a grid runs as cluster splits, whose fix-up is cheap; the
+    // global one cost more than the split saved there).  Measured on B200
+    // (prep + GEMV replayed from a graph, batch 1, us), this grid against 444
+    // three-stage CTAs: 57344x8192 50.6 vs 54.5, 10240x8192 15.6 vs 20.8,
+    // 8192x28672 29.3 vs 39.6, 8192x3584 9.2 vs 19.7, 8192x1024 5.4 vs 9.0.
     if (i8::n_tiles(batch) == 1 && tile_cap_env() < 0) {
         if (tiles >= sms) return sms;
-        int sh = units <= 16 ? 1 : sms / tiles;
+        int sh = sms / tiles;
+        if (units <= 16) {
+            if (sh > units / 2) sh = units / 2;
+            if (sh > 4) sh = 4;
+        }
         sh = sh < 1 ? 1 : sh > 7 ? 7 : sh;
         if (sh > units) sh = units;
         return tiles * sh;
