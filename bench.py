@@ -437,14 +437,18 @@ def gemv_mode(a) -> int:
     rows, cols = (int(v) for v in shape.split("x"))
     batch = int(batch)
     t = {"q4_0": cn.TYPE_Q4_0, "q4_k": cn.TYPE_Q4_K, "q6_k": cn.TYPE_Q6_K, "q8_0": cn.TYPE_Q8_0,
-         "q5_k": cn.TYPE_Q5_K}[name]
+         "q5_k": cn.TYPE_Q5_K, "q4_1": cn.TYPE_Q4_1, "q5_0": cn.TYPE_Q5_0, "q5_1": cn.TYPE_Q5_1}[name]
     ctx = cn.Context(0)
-    if t in (cn.TYPE_Q8_0, cn.TYPE_Q5_K):  # no seeded generator: seeded random blocks, fp16 scales 0.01
-        blk, bpb = (32, 34) if t == cn.TYPE_Q8_0 else (256, 176)
+    # no seeded generator: seeded random blocks (block elements, bytes, has a
+    # second fp16 field), fp16 scales (and minima) 0.01
+    raw_fmt = {cn.TYPE_Q8_0: (32, 34, False), cn.TYPE_Q5_K: (256, 176, True), cn.TYPE_Q4_1: (32, 20, True),
+               cn.TYPE_Q5_0: (32, 22, False), cn.TYPE_Q5_1: (32, 24, True)}
+    if t in raw_fmt:
+        blk, bpb, second = raw_fmt[t]
         raw = np.random.default_rng(cn.synth_seed(2, f"gemv.{name}.{rows}x{cols}")).integers(
             0, 256, size=(rows * cols // blk, bpb), dtype=np.uint8)
         raw[:, 0:2] = np.frombuffer(np.float16(0.01).tobytes(), np.uint8)
-        if t == cn.TYPE_Q5_K:
+        if second:
             raw[:, 2:4] = np.frombuffer(np.float16(0.01).tobytes(), np.uint8)
         W = ctx.upload(raw.ravel(), t, rows, cols)
     else:

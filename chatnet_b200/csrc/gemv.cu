@@ -53,6 +53,25 @@ struct Fmt<CN_TYPE_Q4_0> {
     __device__ static int box_x(int u) { return 18 * u; }  // uint64 elements
     __device__ static int offset(int) { return 0; }
 };
+// Q4_1 / Q5_0 / Q5_1: eight 20 / 22 / 24-byte blocks per row and unit
+template <>
+struct Fmt<CN_TYPE_Q4_1> {
+    static constexpr int kBox = 160;
+    __device__ static int box_x(int u) { return 20 * u; }
+    __device__ static int offset(int) { return 0; }
+};
+template <>
+struct Fmt<CN_TYPE_Q5_0> {
+    static constexpr int kBox = 176;
+    __device__ static int box_x(int u) { return 22 * u; }
+    __device__ static int offset(int) { return 0; }
+};
+template <>
+struct Fmt<CN_TYPE_Q5_1> {
+    static constexpr int kBox = 192;
+    __device__ static int box_x(int u) { return 24 * u; }
+    __device__ static int offset(int) { return 0; }
+};
 template <>
 struct Fmt<CN_TYPE_Q8_0> {
     static constexpr int kBox = 272;  // bytes per row per unit (8 blocks of 34)
@@ -86,7 +105,9 @@ struct Geo {
     static constexpr int kW = Fmt<TYPE>::kBox * kTileRows;             // raw blocks
     static constexpr int kXF = 8 * NT * 32 * 16;                        // B fragments
     static constexpr bool kKQ = TYPE == CN_TYPE_Q4_K || TYPE == CN_TYPE_Q5_K;  // scales and mins
-    static constexpr int kXS = kKQ ? 8 * NT * 4 * 4 : 0;  // chunk sums
+    // chunk sums of x: the min terms of Q4_K / Q5_K and of Q4_1 / Q5_1
+    static constexpr bool kMin = kKQ || TYPE == CN_TYPE_Q4_1 || TYPE == CN_TYPE_Q5_1;
+    static constexpr int kXS = kMin ? 8 * NT * 4 * 4 : 0;
     static constexpr int kXI = NT * 4 * 4;                              // unit 2^-e per column
     static constexpr int kXIpad = (kXI + 127) / 128 * 128;
     static constexpr int kBytes = kW + kXF + kXS + kXI;                 // bytes landing per stage
@@ -227,6 +248,104 @@ __device__ __forceinline__ void unit_q4_0(const uint8_t* stw, const uint4* xf, i
             fma2(acc[nt][2], acc[nt][3], tmp[2], tmp[3], dh);
         }
     }
+}
+
+// Q4_1 (DequantQ4_1.cs:24-56, 134-171; d@0, m@2, qs@4), Q5_0
+// (DequantQ5_0.cs:29-68, 77-114; d@0, qh@2, qs@6) and Q5_1 (DequantQ5_1.cs:
+// 30-69, 78-119; d@0, m@2, qh@4, qs@8): Q4_0's nibble layout (byte i: low
+// nibble = element i, high nibble = element 16 + i), Q5's fifth bit of
+// element j at bit j of qh.  Each element enters the A fragment as the exact
+// fp16 1024 + q (low nibbles) or 1024 + 16 q (high nibbles), the fifth bit
+// ORed in at mantissa bit 4 or 8; one subtraction or FMA takes it to q (Q4_1,
+// Q5_1) or q - 16 (Q5_0).  d scales the block's fp32 partial sums and m times
+// the block's x sum (the chunk sums) joins the row, as the reference's
+// blockSum * d + inputSum * m.
+template <int TYPE>
+struct B32 {
+    static constexpr int kBpb = TYPE == CN_TYPE_Q4_1 ? 20 : TYPE == CN_TYPE_Q5_0 ? 22 : 24;
+    static constexpr int kQs = TYPE == CN_TYPE_Q4_1 ? 4 : TYPE == CN_TYPE_Q5_0 ? 6 : 8;
+    static constexpr int kQh = TYPE == CN_TYPE_Q5_0 ? 2 : 4;
+    static constexpr bool kQ5 = TYPE != CN_TYPE_Q4_1, kM = TYPE != CN_TYPE_Q5_0;
+};
+
+// the fifth bits of elements e, e + 2 (of qh) at bits 0 and 16
+__device__ __forceinline__ uint32_t qh_pair(uint32_t qh, int e) {
+    return ((qh >> e) & 1u) | (((qh >> (e + 2)) & 1u) << 16);
+}
+
+template <int TYPE, int NT, int B>
+__device__ __forceinline__ void block_b32(const uint8_t* rg, const uint8_t* rh, const uint4* xf, const float* xs,
+                                          int t, int lane, const bool* live, float (&acc)[NT][4]) {
+    using F = B32<TYPE>;
+    constexpr int o = F::kBpb * B;
+    constexpr uint32_t kLo = F::kM ? 0x64006400u : 0x64106410u;  // half2(1024) or half2(1040)
+    constexpr uint32_t kHi = F::kM ? 0xD400D400u : 0xD500D500u;  // half2(-64) or half2(-80)
+    const uint32_t k1_16 = 0x2C002C00u;                          // half2(1/16)
+    const float dg = half_bits_to_float(lds_u16(rg + o)), dh = half_bits_to_float(lds_u16(rh + o));
+    float mg = 0.f, mh = 0.f;
+    if constexpr (F::kM) {
+        mg = half_bits_to_float(lds_u16(rg + o + 2));
+        mh = half_bits_to_float(lds_u16(rh + o + 2));
+    }
+    constexpr int qmis = (o + F::kQs) & 3;
+    const uint32_t wg = word_at<qmis>(rg, o + F::kQs + 4 * t), wh = word_at<qmis>(rh, o + F::kQs + 4 * t);
+    uint32_t a0[4], a1[4], p, q;
+    nib_lo(wg, p, q);
+    a0[0] = p;
+    a0[2] = q;
+    nib_lo(wh, p, q);
+    a0[1] = p;
+    a0[3] = q;
+    nib_hi(wg, p, q);
+    a1[0] = p;
+    a1[2] = q;
+    nib_hi(wh, p, q);
+    a1[1] = p;
+    a1[3] = q;
+    if constexpr (F::kQ5) {
+        constexpr int hmis = (o + F::kQh) & 3;
+        const uint32_t qg = word_at<hmis>(rg, o + F::kQh), qhh = word_at<hmis>(rh, o + F::kQh);
+        // low nibbles: elements 4t + {0, 2} in a0[0], 4t + {1, 3} in a0[2]
+        a0[0] |= qh_pair(qg, 4 * t) << 4;
+        a0[2] |= qh_pair(qg, 4 * t + 1) << 4;
+        a0[1] |= qh_pair(qhh, 4 * t) << 4;
+        a0[3] |= qh_pair(qhh, 4 * t + 1) << 4;
+        // high nibbles: elements 16 + 4t + ...
+        a1[0] |= qh_pair(qg, 16 + 4 * t) << 8;
+        a1[2] |= qh_pair(qg, 16 + 4 * t + 1) << 8;
+        a1[1] |= qh_pair(qhh, 16 + 4 * t) << 8;
+        a1[3] |= qh_pair(qhh, 16 + 4 * t + 1) << 8;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        a0[k] = h2_sub(a0[k], kLo);
+        a1[k] = h2_fma(a1[k], k1_16, kHi);
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+        uint4 bx = bfrag<NT>(xf, B, nt, lane, live[nt]);
+        float tmp[4];
+        const float z[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t b0[2] = {bx.x, bx.y}, b1[2] = {bx.z, bx.w};
+        mma_16816(tmp, a0, b0, z);
+        mma_16816(tmp, a1, b1, tmp);
+        if constexpr (F::kM) {
+            const float X = xs[B * NT * 4 + nt * 4 + t];
+            acc[nt][0] = fmaf(mg, X, acc[nt][0]);
+            acc[nt][2] = fmaf(mh, X, acc[nt][2]);
+        }
+        fma2(acc[nt][0], acc[nt][1], tmp[0], tmp[1], dg);
+        fma2(acc[nt][2], acc[nt][3], tmp[2], tmp[3], dh);
+    }
+}
+
+template <int TYPE, int NT, int B = 0>
+__device__ __forceinline__ void unit_b32(const uint8_t* stw, const uint4* xf, const float* xs, int row0, int g,
+                                         int t, int lane, const bool* live, float (&acc)[NT][4]) {
+    constexpr int RB = Fmt<TYPE>::kBox;
+    const uint8_t* rg = stw + (row0 + g) * RB;
+    block_b32<TYPE, NT, B>(rg, rg + 8 * RB, xf, xs, t, lane, live, acc);
+    if constexpr (B < 7) unit_b32<TYPE, NT, B + 1>(stw, xf, xs, row0, g, t, lane, live, acc);
 }
 
 // Q8_0 (DequantQ8_0.cs:19-41; d@0, 32 int8 quants @2): each byte goes into
@@ -771,6 +890,9 @@ __global__ void __launch_bounds__(kThreads, Geo<TYPE, NT>::kMinCtas)
             unit_q4_0<NT>(st, xf, warp * 16, g, t, lane, live, au);
         } else if constexpr (TYPE == CN_TYPE_Q8_0) {
             unit_q8_0<NT>(st, xf, warp * 16, g, t, lane, live, au);
+        } else if constexpr (TYPE == CN_TYPE_Q4_1 || TYPE == CN_TYPE_Q5_0 || TYPE == CN_TYPE_Q5_1) {
+            const float* xs = reinterpret_cast<const float*>(st + G::kW + G::kXF);
+            unit_b32<TYPE, NT>(st, xf, xs, warp * 16, g, t, lane, live, au);
         } else if constexpr (TYPE == CN_TYPE_Q4_K || TYPE == CN_TYPE_Q5_K) {
             const float* xs = reinterpret_cast<const float*>(st + G::kW + G::kXF);
             unit_q4_k<NT, TYPE == CN_TYPE_Q5_K>(st, xf, xs, table + warp * 128, warp * 16, g, t, lane, live, au);
@@ -1313,12 +1435,20 @@ static EncodeTiledFn get_encode() {
     return fn;
 }
 
+// Types whose tiled GEMV reads the chunk sums of x (their min terms).
+static bool type_needs_xsum(int type) {
+    return type == CN_TYPE_Q4_K || type == CN_TYPE_Q5_K || type == CN_TYPE_Q4_1 || type == CN_TYPE_Q5_1;
+}
+
 static int box_bytes(int type) {
     switch (type) {
         case CN_TYPE_Q4_0: return Fmt<CN_TYPE_Q4_0>::kBox;
         case CN_TYPE_Q8_0: return Fmt<CN_TYPE_Q8_0>::kBox;
         case CN_TYPE_Q4_K: return Fmt<CN_TYPE_Q4_K>::kBox;
         case CN_TYPE_Q5_K: return Fmt<CN_TYPE_Q5_K>::kBox;
+        case CN_TYPE_Q4_1: return Fmt<CN_TYPE_Q4_1>::kBox;
+        case CN_TYPE_Q5_0: return Fmt<CN_TYPE_Q5_0>::kBox;
+        case CN_TYPE_Q5_1: return Fmt<CN_TYPE_Q5_1>::kBox;
         case CN_TYPE_Q6_K: return Fmt<CN_TYPE_Q6_K>::kBox;
         default: return 0;
     }
@@ -1423,6 +1553,9 @@ int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool
     else if (type == CN_TYPE_Q8_0) { CN_OCC(CN_TYPE_Q8_0) }
     else if (type == CN_TYPE_Q4_K) { CN_OCC(CN_TYPE_Q4_K) }
     else if (type == CN_TYPE_Q5_K) { CN_OCC(CN_TYPE_Q5_K) }
+    else if (type == CN_TYPE_Q4_1) { CN_OCC(CN_TYPE_Q4_1) }
+    else if (type == CN_TYPE_Q5_0) { CN_OCC(CN_TYPE_Q5_0) }
+    else if (type == CN_TYPE_Q5_1) { CN_OCC(CN_TYPE_Q5_1) }
     else { CN_OCC(CN_TYPE_Q6_K) }
 #undef CN_OCC
     if (occ < 0) return occ;  // error code from the occupancy query
@@ -1469,7 +1602,7 @@ int gemv_plan(cn_ctx* ctx, int type, int64_t rows, int64_t cols, int batch, bool
     p->ctas = ctas;
     const int chunks = p->units * 8;
     p->xfrag_bytes = (size_t)chunks * p->nt * 32 * sizeof(uint4);
-    p->xsum_bytes = (type == CN_TYPE_Q4_K || type == CN_TYPE_Q5_K) ? (size_t)chunks * p->nt * 4 * sizeof(float) : 0;
+    p->xsum_bytes = type_needs_xsum(type) ? (size_t)chunks * p->nt * 4 * sizeof(float) : 0;
     p->xinv_bytes = (size_t)p->units * p->nt * 4 * sizeof(float);
     p->partial_bytes = (size_t)2 * ctas * kTileRows * p->nt * 4 * sizeof(float);
     p->counters = (size_t)p->tiles * kCons;
@@ -1564,7 +1697,7 @@ float gemv_step1_scale(int type) { return type == CN_TYPE_Q4_K || type == CN_TYP
 int gemv_prep_kind(const GemvOp& op) {
     if (op.plan.path == kPathI8) return 3;
     if (op.plan.path == kPathTc) return 2;
-    return op.type == CN_TYPE_Q4_K || op.type == CN_TYPE_Q5_K ? 1 : 0;
+    return type_needs_xsum(op.type) ? 1 : 0;
 }
 
 bool pdl_enabled() {
@@ -1594,7 +1727,7 @@ PrepTarget prep_target(const GemvOp* op, const GemvBufs& b) {
     pt.nt_count = op->plan.nt;
     pt.step1 = gemv_step1_scale(op->type);
     pt.xfrag = b.xfrag;
-    pt.xsum = op->type == CN_TYPE_Q4_K || op->type == CN_TYPE_Q5_K ? b.xsum : nullptr;
+    pt.xsum = type_needs_xsum(op->type) ? b.xsum : nullptr;
     pt.xinv = b.xinv;
     return pt;
 }
@@ -1731,6 +1864,9 @@ static int gemv_mma_launch(cn_ctx* ctx, cudaStream_t st, const GemvOp* ops, int 
     if (type == CN_TYPE_Q8_0) { CN_DISPATCH(CN_TYPE_Q8_0) }
     if (type == CN_TYPE_Q4_K) { CN_DISPATCH(CN_TYPE_Q4_K) }
     if (type == CN_TYPE_Q5_K) { CN_DISPATCH(CN_TYPE_Q5_K) }
+    if (type == CN_TYPE_Q4_1) { CN_DISPATCH(CN_TYPE_Q4_1) }
+    if (type == CN_TYPE_Q5_0) { CN_DISPATCH(CN_TYPE_Q5_0) }
+    if (type == CN_TYPE_Q5_1) { CN_DISPATCH(CN_TYPE_Q5_1) }
     CN_DISPATCH(CN_TYPE_Q6_K)
 #undef CN_DISPATCH
 }

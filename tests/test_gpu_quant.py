@@ -218,6 +218,19 @@ def test_block32_matvec_parity(ctx, oracle, name, batch):
     assert rel_err(ctx.matvec(W, x), oracle.matvec(t, blocks, x, rows)) <= REL_TOL
 
 
+@pytest.mark.parametrize("name", ["q4_1", "q5_0", "q5_1"])
+@pytest.mark.parametrize("rows,cols,batch", [(4096, 4096, 1), (300, 2048, 3), (1000, 4096, 8), (129, 768, 16),
+                                            (257, 1024, 32), (96, 1056, 2)])
+def test_b32_tiled_matvec_parity(ctx, oracle, name, rows, cols, batch):
+    """Q4_1 / Q5_0 / Q5_1 on the tiled fp16 GEMV (whole 256-column units:
+    every n-tile count, partial row tiles, the cluster split at batch 1-8)
+    and, at 1056 columns, on the generic kernel."""
+    t, blocks = _rand_b32(name, rows, cols, 51 + batch)
+    W = ctx.upload(blocks, t, rows, cols)
+    x = _x(batch, cols, f"b32t.x.{name}.{rows}.{cols}.{batch}")
+    assert rel_err(ctx.matvec(W, x), oracle.matvec(t, blocks, x, rows)) <= REL_TOL
+
+
 @pytest.mark.parametrize("rows,cols,batch", [(4096, 4096, 1), (300, 2048, 5), (1000, 4096, 16), (129, 768, 32),
                                             (96, 1056, 2)])
 def test_q8_0_matvec_parity(ctx, oracle, rows, cols, batch):
